@@ -1,0 +1,17 @@
+#!/bin/bash
+# Builds the reference's GPU kernels (stbl/kernels.cu + kernels.h, compiled directly from the
+# reference tree, no copy) for sm_100a into oracle/_ref/libstbl_ref_kernels.so.  The library is the
+# second oracle for the kernels.h compatibility entry points: the GPU tests run both builds on the
+# same inputs and compare them bit for bit, as stbl/cmp_kernels.py does.  Needs the reference tree
+# (present where the repository is developed, absent on GPU boxes, which use the prebuilt file).
+set -euo pipefail
+REF=${STBL_REFERENCE:-/root/reference}
+HERE=$(cd "$(dirname "$0")" && pwd)
+if [ ! -f "$REF/stbl/kernels.cu" ]; then
+    echo "reference tree not found at $REF; keeping the prebuilt _ref/ (if any)" >&2
+    exit 0
+fi
+mkdir -p "$HERE/_ref"
+nvcc -O2 -std=c++17 -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC -shared \
+    "$REF/stbl/kernels.cu" -o "$HERE/_ref/libstbl_ref_kernels.so"
+echo "built $HERE/_ref/libstbl_ref_kernels.so"

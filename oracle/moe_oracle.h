@@ -1,0 +1,102 @@
+/* CPU oracle for the MoE decode hot path.  TEST INFRASTRUCTURE ONLY.
+ *
+ * This is a plain-C restatement of the reference's MoE layer (stbl/model.cu:426-594) and of the
+ * numerics of its torch stand-ins (ref/kernel.py) and GPU kernels (stbl/kernels.cu).  It is used
+ * by tests/, by __graft_entry__.smoke() and by bench.py's cpu_baseline / --impl reference legs as
+ * the checker and the CPU baseline.  The product (stblarge_b200/) never links or calls it.
+ *
+ * Every function names the reference lines it restates.  Parity of this oracle against the
+ * reference itself is pinned by tests/test_oracle_golden.py (golden vectors produced by importing
+ * ref/kernel.py, script tests/golden/make_golden.py) and, on a GPU box, by bitwise A/B against
+ * the reference's own kernels built from stbl/kernels.cu (oracle/build_ref.sh).
+ */
+#pragma once
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* weight storage formats (same ids as include/stbl_moe.h) */
+enum {
+    ORC_FMT_NONE = 0,
+    ORC_FMT_FP8_B128 = 1,    /* e4m3 codes [rows][k], fp32 scales [ceil(rows/128)][ceil(k/128)] */
+    ORC_FMT_MXFP4 = 2,       /* e2m1 codes [rows][k/2] low nibble first, e8m0 scales [rows][k/32] */
+};
+
+enum { ORC_SCORE_SIGMOID = 0, ORC_SCORE_SQRT_SOFTPLUS = 1 };
+
+/* ---- scalar formats --------------------------------------------------------------------------- */
+float orc_bf16_round(float x);               /* RNE to bf16, kernels.cu:13 */
+float orc_pow2_ceil(float t);                /* ref/kernel.py:22-26, kernels.cu:26-30 */
+float orc_e4m3_value(uint8_t code);          /* tools/convert_official.py:40-48 */
+uint8_t orc_e4m3_encode(float v);            /* RNE, saturating to +-448 (torch .to(float8_e4m3fn) after clamp) */
+float orc_e2m1_value(uint8_t nibble);        /* ref/kernel.py:14-16 */
+uint8_t orc_e2m1_encode(float v);            /* ref/kernel.py:48-52 + 75-77, v already within [-6, 6] */
+/* array forms of the above, for the Python tests */
+void orc_bf16_round_n(const float *x, int n, float *out);
+void orc_pow2_ceil_n(const float *x, int n, float *out);
+void orc_e4m3_encode_n(const float *x, int n, uint8_t *out);
+void orc_e2m1_encode_n(const float *x, int n, uint8_t *out);
+
+/* ---- quantizers ------------------------------------------------------------------------------- */
+/* act_quant(x, block, scale_fmt=pow2 ? "ue8m0" : None): ref/kernel.py:35-45, per row of k values. */
+void orc_act_quant(const float *x, int rows, int k, int block, int pow2, uint8_t *codes, float *scales);
+/* FP8 weight quantization with 128x128 fp32 block scales (act_quant's rule on 2-D blocks). */
+void orc_quant_fp8_b128(const float *w, int rows, int k, uint8_t *codes, float *scales);
+/* MXFP4 weight quantization, fp4_act_quant E8M0 branch: ref/kernel.py:55-72. */
+void orc_quant_mxfp4(const float *w, int rows, int k, uint8_t *packed, uint8_t *scales);
+
+/* ---- GEMVs over several tokens (fp8_gemm / fp4_gemm numerics, ref/kernel.py:85-102) ----------- */
+/* y[t][r] = sum_k (code_x*sx) * (code_w*sw), fp32, no output rounding. xs: per-(token, act block). */
+void orc_gemv_fp8_b128(const uint8_t *w, const float *ws, int rows, int k, const uint8_t *xc, const float *xs,
+                       int act_block, int n_tok, float *y);
+void orc_gemv_mxfp4(const uint8_t *w, const uint8_t *ws, int rows, int k, const uint8_t *xc, const float *xs,
+                    int act_block, int n_tok, float *y);
+
+/* ---- router (model.cu:430-452 composition, V3 group-limited or V4 flat selection) ------------- */
+/* logits[t][e] = W[e] . x[t]; fp32 with the reduction order of the GPU router kernel: lane l of 32
+ * takes k = 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, then an xor butterfly
+ * over the 32 lane sums (16, 8, 4, 2, 1).  Needs h % 128 == 0. */
+void orc_router_logits(const float *W, const uint16_t *x_bf16, int T, int E, int H, float *logits);
+/* scores, top-k ids in selection order (biased score descending, lower id first on ties) and
+ * routing weights score / (sum + 1e-20) * route_scale (model.cu:444-451, 527-530). */
+int orc_router_select(const float *logits, const float *bias, int T, int E, int topk, int n_groups, int topk_groups,
+                      int score_fn, float route_scale, float *scores, int *idx, float *weights);
+/* bucketed dispatch: counts[E], offsets[E+1], perm[T*topk] (expert-major, token then slot order);
+ * perm holds t * topk + slot. */
+void orc_dispatch(const int *idx, int T, int E, int topk, int *counts, int *offsets, int *perm);
+
+/* ---- whole MoE layer -------------------------------------------------------------------------- */
+typedef struct orc_moe_desc {
+    int hidden, inter, n_experts, topk, n_groups, topk_groups, score_fn;
+    float route_scale, swiglu_limit;
+    int routed_fmt, shared_fmt;
+    const float *router_w, *router_bias;
+    /* routed expert e, matrix m (0 gate [inter][hidden], 1 up, 2 down [hidden][inter]) */
+    const uint8_t *const *routed_w; /* [3 * n_experts], index m * n_experts + e; NULL = absent */
+    const void *const *routed_s;    /* [3 * n_experts] */
+    const uint8_t *shared_w[3];
+    const void *shared_s[3];
+} orc_moe_desc;
+
+/* y = bf16(sum over top-k slots in order of the routed outputs, then + shared output).  Writes
+ * idx / weights [T][topk] when non-NULL.  Returns 0, or -1 when a routed expert is absent. */
+int orc_moe_forward(const orc_moe_desc *d, const uint16_t *x, int T, uint16_t *y, int *idx, float *weights,
+                    int nthreads);
+
+/* ---- the reference's own kernel semantics (stbl/kernels.cu), exact summation orders ----------- */
+void orc_ref_act_quant_fp8(float *x, int n);                                              /* :56-63 */
+void orc_ref_round_bf16(float *x, int n);                                                 /* :86-89 */
+void orc_ref_gemv_fp8(float *y, const uint8_t *w, const uint8_t *scale, const float *x, int rows, int k,
+                      int round_out);                                                     /* :98-132 */
+void orc_ref_gemv_mxfp4(float *y, const uint8_t *w, const float *x, int rows, int k);     /* :142-191 */
+void orc_ref_gemv_f32(float *y, const float *w, const float *x, int rows, int k, int round_out); /* :206-214 */
+void orc_ref_sqrt_softplus(float *s, int n);                                              /* :437-442 */
+void orc_ref_swiglu(float *out, const float *g, const float *u, const float *weights, int count, float limit,
+                    int n);                                                               /* :445-459 */
+void orc_ref_axpy(float *y, const float *x, float a, int n);                              /* :461-464 */
+
+#ifdef __cplusplus
+}
+#endif

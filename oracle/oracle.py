@@ -1,0 +1,283 @@
+"""ctypes front end of the CPU oracle (liboracle.so).  TEST INFRASTRUCTURE ONLY.
+
+Used by tests/, __graft_entry__.smoke() and bench.py's CPU legs as the checker and the CPU baseline;
+the product package never imports it.  See moe_oracle.h for what each function restates.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+FMT_NONE, FMT_FP8_B128, FMT_MXFP4 = 0, 1, 2
+SCORE_SIGMOID, SCORE_SQRT_SOFTPLUS = 0, 1
+
+_lib = None
+P = ctypes.c_void_p
+I = ctypes.c_int
+F = ctypes.c_float
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(LIB_PATH)
+        for name in ("orc_bf16_round", "orc_pow2_ceil", "orc_e4m3_value"):
+            getattr(_lib, name).restype = ctypes.c_float
+        _lib.orc_bf16_round.argtypes = [F]
+        _lib.orc_pow2_ceil.argtypes = [F]
+        _lib.orc_e4m3_value.argtypes = [ctypes.c_uint8]
+        _lib.orc_e4m3_encode.restype = ctypes.c_uint8
+        _lib.orc_e4m3_encode.argtypes = [F]
+    return _lib
+
+
+def ptr(a):
+    return P(a.ctypes.data) if a is not None else P(0)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---- scalar formats, vectorised ---------------------------------------------------------------
+
+def bf16_round(x):
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().orc_bf16_round_n(ptr(x), I(x.size), ptr(out))
+    return out
+
+
+def pow2_ceil(x):
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().orc_pow2_ceil_n(ptr(x), I(x.size), ptr(out))
+    return out
+
+
+def e4m3_encode(x):
+    x = _f32(x)
+    out = np.empty(x.shape, np.uint8)
+    lib().orc_e4m3_encode_n(ptr(x), I(x.size), ptr(out))
+    return out
+
+
+def e2m1_encode(x):
+    x = _f32(x)
+    out = np.empty(x.shape, np.uint8)
+    lib().orc_e2m1_encode_n(ptr(x), I(x.size), ptr(out))
+    return out
+
+
+def e4m3_values():
+    return np.array([lib().orc_e4m3_value(c) for c in range(256)], np.float32)
+
+
+FP4_TABLE = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], np.float32)
+
+
+def bf16_bits_to_f32(b):
+    return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x):
+    return (bf16_round(x).view(np.uint32) >> 16).astype(np.uint16)
+
+
+# ---- quantizers ---------------------------------------------------------------------------------
+
+def act_quant(x, block, pow2):
+    x = _f32(x)
+    rows, k = x.reshape(-1, x.shape[-1]).shape
+    codes = np.empty((rows, k), np.uint8)
+    scales = np.empty((rows, k // block), np.float32)
+    lib().orc_act_quant(ptr(x), I(rows), I(k), I(block), I(int(pow2)), ptr(codes), ptr(scales))
+    return codes, scales
+
+
+def quant_fp8_b128(w):
+    w = _f32(w)
+    rows, k = w.shape
+    codes = np.empty((rows, k), np.uint8)
+    scales = np.empty(((rows + 127) // 128, (k + 127) // 128), np.float32)
+    lib().orc_quant_fp8_b128(ptr(w), I(rows), I(k), ptr(codes), ptr(scales))
+    return codes, scales
+
+
+def quant_mxfp4(w):
+    w = _f32(w)
+    rows, k = w.shape
+    packed = np.empty((rows, k // 2), np.uint8)
+    scales = np.empty((rows, k // 32), np.uint8)
+    lib().orc_quant_mxfp4(ptr(w), I(rows), I(k), ptr(packed), ptr(scales))
+    return packed, scales
+
+
+def gemv_fp8_b128(w, ws, xc, xs, act_block):
+    rows, k = w.shape
+    n = xc.shape[0]
+    y = np.empty((n, rows), np.float32)
+    lib().orc_gemv_fp8_b128(ptr(np.ascontiguousarray(w)), ptr(_f32(ws)), I(rows), I(k), ptr(np.ascontiguousarray(xc)),
+                            ptr(_f32(xs)), I(act_block), I(n), ptr(y))
+    return y
+
+
+def gemv_mxfp4(w, ws, xc, xs, act_block):
+    rows = w.shape[0]
+    k = w.shape[1] * 2
+    n = xc.shape[0]
+    y = np.empty((n, rows), np.float32)
+    lib().orc_gemv_mxfp4(ptr(np.ascontiguousarray(w)), ptr(np.ascontiguousarray(ws)), I(rows), I(k),
+                         ptr(np.ascontiguousarray(xc)), ptr(_f32(xs)), I(act_block), I(n), ptr(y))
+    return y
+
+
+# ---- router / dispatch ----------------------------------------------------------------------------
+
+def router_logits(W, x_bits):
+    W = _f32(W)
+    x_bits = np.ascontiguousarray(x_bits, np.uint16)
+    E, H = W.shape
+    T = x_bits.shape[0]
+    out = np.empty((T, E), np.float32)
+    lib().orc_router_logits(ptr(W), ptr(x_bits), I(T), I(E), I(H), ptr(out))
+    return out
+
+
+def router_select(logits, bias, topk, n_groups, topk_groups, score_fn, route_scale):
+    logits = _f32(logits)
+    T, E = logits.shape
+    scores = np.empty((T, E), np.float32)
+    idx = np.empty((T, topk), np.int32)
+    w = np.empty((T, topk), np.float32)
+    rc = lib().orc_router_select(ptr(logits), ptr(_f32(bias)), I(T), I(E), I(topk), I(n_groups), I(topk_groups),
+                                 I(score_fn), F(route_scale), ptr(scores), ptr(idx), ptr(w))
+    if rc:
+        raise ValueError("router_select: bad group configuration")
+    return scores, idx, w
+
+
+def dispatch(idx, E):
+    idx = np.ascontiguousarray(idx, np.int32)
+    T, k = idx.shape
+    counts = np.empty(E, np.int32)
+    offsets = np.empty(E + 1, np.int32)
+    perm = np.empty(T * k, np.int32)
+    lib().orc_dispatch(ptr(idx), I(T), I(E), I(k), ptr(counts), ptr(offsets), ptr(perm))
+    return counts, offsets, perm
+
+
+# ---- whole layer ----------------------------------------------------------------------------------
+
+class _Desc(ctypes.Structure):
+    _fields_ = [
+        ("hidden", I), ("inter", I), ("n_experts", I), ("topk", I), ("n_groups", I), ("topk_groups", I),
+        ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
+        ("router_w", P), ("router_bias", P), ("routed_w", P), ("routed_s", P),
+        ("shared_w", P * 3), ("shared_s", P * 3),
+    ]
+
+
+def moe_forward(cfg, weights, x_bits, nthreads=0):
+    """cfg: dict of layer shapes / routing (see stblarge_b200.config.MoEConfig.as_dict); weights: host
+    numpy weights as produced by stblarge_b200.synth (routed[m][e] = (codes, scales) or None,
+    shared[m] = (codes, scales) or None).  Returns (y_bits [T][H] uint16, idx, weights)."""
+    E = cfg["n_experts"]
+    keep = []
+
+    def p(a):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    rw = (P * (3 * E))()
+    rs = (P * (3 * E))()
+    for m in range(3):
+        for e in range(E):
+            item = weights["routed"][m][e]
+            if item is not None:
+                rw[m * E + e] = p(item[0])
+                rs[m * E + e] = p(item[1])
+    d = _Desc()
+    d.hidden, d.inter, d.n_experts, d.topk = cfg["hidden"], cfg["inter"], E, cfg["topk"]
+    d.n_groups, d.topk_groups, d.score_fn = cfg["n_groups"], cfg["topk_groups"], cfg["score_fn"]
+    d.route_scale, d.swiglu_limit = cfg["route_scale"], cfg["swiglu_limit"]
+    d.routed_fmt, d.shared_fmt = cfg["routed_fmt"], cfg["shared_fmt"]
+    d.router_w = p(_f32(weights["router_w"]))
+    d.router_bias = p(_f32(weights["router_bias"]))
+    d.routed_w = ctypes.cast(rw, P)
+    d.routed_s = ctypes.cast(rs, P)
+    if cfg["shared_fmt"] != FMT_NONE:
+        for m in range(3):
+            d.shared_w[m] = p(weights["shared"][m][0])
+            d.shared_s[m] = p(weights["shared"][m][1])
+    x_bits = np.ascontiguousarray(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    y = np.empty((T, cfg["hidden"]), np.uint16)
+    idx = np.empty((T, cfg["topk"]), np.int32)
+    w = np.empty((T, cfg["topk"]), np.float32)
+    rc = lib().orc_moe_forward(ctypes.byref(d), ptr(x_bits), I(T), ptr(y), ptr(idx), ptr(w), I(nthreads))
+    if rc:
+        raise ValueError("oracle moe_forward: a routed expert's weights are absent")
+    return y, idx, w
+
+
+# ---- the reference's kernels (stbl/kernels.cu semantics) -------------------------------------------
+
+def ref_act_quant_fp8(x):
+    x = _f32(x).copy()
+    lib().orc_ref_act_quant_fp8(ptr(x), I(x.size))
+    return x
+
+
+def ref_gemv_fp8(w, scale, x, round_out):
+    rows, k = w.shape
+    y = np.empty(rows, np.float32)
+    lib().orc_ref_gemv_fp8(ptr(y), ptr(np.ascontiguousarray(w)), ptr(np.ascontiguousarray(scale)), ptr(_f32(x)),
+                           I(rows), I(k), I(int(round_out)))
+    return y
+
+
+def ref_gemv_mxfp4(w17, x, rows, k):
+    y = np.empty(rows, np.float32)
+    lib().orc_ref_gemv_mxfp4(ptr(y), ptr(np.ascontiguousarray(w17)), ptr(_f32(x)), I(rows), I(k))
+    return y
+
+
+def ref_gemv_f32(w, x, round_out):
+    rows, k = w.shape
+    y = np.empty(rows, np.float32)
+    lib().orc_ref_gemv_f32(ptr(y), ptr(_f32(w)), ptr(_f32(x)), I(rows), I(k), I(int(round_out)))
+    return y
+
+
+def ref_sqrt_softplus(s):
+    s = _f32(s).copy()
+    lib().orc_ref_sqrt_softplus(ptr(s), I(s.size))
+    return s
+
+
+def ref_swiglu(g, u, weights, limit, n):
+    g, u, weights = _f32(g), _f32(u), _f32(weights)
+    out = np.empty(len(weights) * n, np.float32)
+    lib().orc_ref_swiglu(ptr(out), ptr(g), ptr(u), ptr(weights), I(len(weights)), F(limit), I(n))
+    return out
+
+
+def ref_axpy(y, x, a):
+    y = _f32(y).copy()
+    lib().orc_ref_axpy(ptr(y), ptr(_f32(x)), F(a), I(y.size))
+    return y
