@@ -1,0 +1,331 @@
+"""MoE-layer decode benchmark (BASELINE.json metric: decode tokens/s and achieved HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl b200|reference]
+
+A step is one call of the full-size DeepSeek-V3-shaped MoE layer (configs[1]: hidden 7168,
+moe_intermediate 2048, 256 routed experts + 1 shared, top-8 of 8 groups keeping 4, FP8 128x128
+block-scaled weights) on T decode tokens (default 16), with weights resident in HBM.  Every step
+gets fresh tokens (different routing), and L2 is flushed before each step; each step is timed with
+CUDA events on the launching stream.  `e2e` is the same metric through the host-buffer entry point
+(stbl_moe_forward_host: H2D of x, layer, D2H of y, inside the timed region).
+
+N > 1: one process per GPU; each rank runs an independent full layer replica on its own tokens
+(weak scaling; expert parallelism is not built yet), time = max over ranks.
+
+--impl reference: the reference's CPU path (the CPU oracle restating stbl/model.cu:426-594 on the
+numerics of ref/kernel.py) on the host cores, same workload and metric; rank 0 only.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from stblarge_b200 import synth  # noqa: E402
+from stblarge_b200.config import CFG2  # noqa: E402
+
+METRIC = "MoE-layer decode tokens/s (full-size FP8 layer)"
+UNIT = "tokens/s"
+HBM_NOMINAL_GBS = 8000.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def layer_bytes(cfg, n_distinct, T):
+    """Algorithmic bytes of one layer call: distinct routed experts + shared expert (codes and scales),
+    router weights + bias, x in, y out (per-token intermediates excluded)."""
+    return (n_distinct * cfg.bytes_per_expert() + cfg.bytes_per_expert(cfg.shared_fmt) + cfg.n_experts * cfg.hidden * 4
+            + cfg.n_experts * 4 + 2 * T * cfg.hidden * 2)
+
+
+def up_bytes(cfg, n_distinct):
+    """Algorithmic bytes of one expert-up launch: gate + up codes and scales of the distinct experts and
+    the shared expert (activations in and h out are under 0.1% and left out)."""
+    H, I = cfg.hidden, cfg.inter
+
+    def mat(fmt):
+        return I * H + 4 * ((I + 127) // 128) * ((H + 127) // 128)
+    return 2 * (n_distinct * mat(cfg.routed_fmt) + mat(cfg.shared_fmt))
+
+
+class ClockSampler:
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def cpu_oracle_layer(cfg, W_host, x_bits, nthreads):
+    from oracle import oracle as O
+    t0 = time.perf_counter()
+    O.moe_forward(cfg.as_dict(), W_host, x_bits, nthreads=nthreads)
+    return time.perf_counter() - t0
+
+
+def run_reference(args, rank):
+    """The reference's CPU path on this host's cores, on the b200 arm's workload."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle as O
+    cfg, T = CFG2, args.tokens
+    cores = os.cpu_count()
+    torch.set_num_threads(cores)
+    # routing uses the real router; expert weights come from a pool of 8 generated experts aliased
+    # behind the 256 ids (the oracle's work does not depend on the weight values)
+    g = torch.Generator().manual_seed(1000)
+    pool = []
+    for _ in range(8):
+        ws = []
+        for (r, k) in synth.mat_shapes(cfg):
+            c, s = synth.quant_fp8_b128(torch.randn(r, k, generator=g) * cfg.weight_std)
+            ws.append((c.numpy(), s.numpy()))
+        pool.append(ws)
+    W = {"router_w": synth.router_w(cfg), "router_bias": synth.router_bias(cfg),
+         "routed": [[pool[e % 8][m] for e in range(cfg.n_experts)] for m in range(3)], "shared": pool[0]}
+    xs = [synth.make_x(cfg.hidden, T, seed=10_000 + i) for i in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        cpu_oracle_layer(cfg, W, xs[i], cores)
+    total = 0.0
+    for i in range(args.steps):
+        total += cpu_oracle_layer(cfg, W, xs[args.warmup + i], cores)
+    value = T * args.steps / total
+    sample = f"{args.steps} full layer calls of the T={T} workload on the CPU oracle, {cores} threads"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 x fp32-accumulate",
+            "data": "synthetic", "config": {"workload": f"cfg2 full-size FP8 MoE layer, T={T} decode tokens",
+                                            "tokens": T, "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=16)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from stblarge_b200.moe import MoELayer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    cfg, T = CFG2, args.tokens
+    weights = synth.device_layer(cfg, device=dev)
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 16))
+    n_steps = args.warmup + args.steps
+    xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
+                      for i in range(n_steps)]).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def distinct_now():
+        r = layer.last_route()
+        return len(np.unique(r["idx"]))
+
+    for i in range(args.warmup):
+        layer(xs[i])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    sampler.start()
+    layer.set_timing(True)
+    distinct = []
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        layer(xs[args.warmup + i])
+        ev[i][1].record()
+        distinct.append(distinct_now())
+    torch.cuda.synchronize()
+    layer.set_timing(False)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_s = sum(step_ms) / 1e3
+    kt = layer.timing()
+    t = torch.tensor([total_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_max = float(t.item())
+    value = world * T * args.steps / total_max
+    bytes_steps = [layer_bytes(cfg, d, T) for d in distinct]
+    hbm_gbs = sum(bytes_steps) / total_s / 1e9
+    peak, peak_kind = peaks()
+    up_alg = sum(up_bytes(cfg, d) for d in distinct) / args.steps
+    up_ms = kt["up"] / max(kt["calls"], 1) * 1e3
+    up_gbs = up_alg / (up_ms / 1e3) / 1e9
+    launches = layer.stats()["launches_per_call"]
+
+    # end to end through the host-buffer entry point (pinned host memory)
+    xh = [xs[args.warmup + i].cpu().pin_memory() for i in range(args.steps)]
+    yh = torch.empty_like(xh[0]).pin_memory()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    stream = torch.cuda.current_stream()
+    for i in range(2):
+        layer.forward_host(xh[i], yh)
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_ev[i][0].record(stream)
+        layer.forward_host(xh[i], yh)
+        e2e_ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_s = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
+    t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * args.steps / float(t.item())
+
+    # batch-size sweep of configs[1] (1, 4, 16 tokens), device time, rank 0 report
+    sweep = []
+    if not args.no_sweep:
+        for Ts in (1, 4, 16):
+            lay = layer if Ts <= layer.max_tokens else None
+            xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
+                   for i in range(23)]
+            for i in range(3):
+                lay(xs2[i])
+            ms, dd = [], []
+            for i in range(3, 23):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                lay(xs2[i])
+                b.record()
+                dd.append(distinct_now())
+                ms.append(a.elapsed_time(b))
+            mean_ms = float(np.mean(ms))
+            gbs = np.mean([layer_bytes(cfg, d, Ts) for d in dd]) / (mean_ms / 1e3) / 1e9
+            sweep.append({"tokens": Ts, "tokens_per_s": Ts / (mean_ms / 1e3), "ms_per_call": mean_ms,
+                          "distinct_experts": float(np.mean(dd)), "hbm_gbs": gbs, "hbm_frac_of_measured": gbs / peak})
+    status = layer.status()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O  # noqa: F401  (the CPU baseline is the oracle)
+        xb = xs[args.warmup].cpu().numpy().view(np.uint16)
+        layer(xs[args.warmup])
+        r = layer.last_route()
+        W = {"router_w": weights["router_w"].cpu().numpy(), "router_bias": weights["router_bias"].cpu().numpy(),
+             "routed": [[None] * cfg.n_experts for _ in range(3)],
+             "shared": [(weights["shared_w"][m].cpu().numpy(), weights["shared_s"][m].cpu().numpy()) for m in range(3)]}
+        for e in np.unique(r["idx"]):
+            for m in range(3):
+                W["routed"][m][int(e)] = (weights["routed_w"][m][e].cpu().numpy(), weights["routed_s"][m][e].cpu().numpy())
+        cores = os.cpu_count()
+        dt = cpu_oracle_layer(cfg, W, xb, cores)
+        cpu = {"value": T / dt, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"1 layer call of the T={T} workload (the first timed step's tokens) on the CPU oracle"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 weights and activations, fp32 accumulate, bf16 io",
+            "data": "synthetic (seeded ~N(0,0.02) weights quantized to FP8 128x128; bf16 ~N(0,1) tokens)",
+            "config": {"workload": f"cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4), "
+                                   f"T={T} decode tokens per rank", "tokens_per_rank": T,
+                       "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                       "l2": "flushed (256 MB write) before every timed step; fresh tokens each step"},
+            "hbm_gbs": hbm_gbs, "hbm_frac_of_measured": hbm_gbs / peak, "hbm_frac_of_8tbs": hbm_gbs / HBM_NOMINAL_GBS,
+            "distinct_experts_per_step": float(np.mean(distinct)),
+            "kernel_ms_per_step": {"router": kt["router"] / max(kt["calls"], 1) * 1e3, "up": up_ms,
+                                   "down": kt["down"] / max(kt["calls"], 1) * 1e3},
+            "roofline": {"bound": "hbm", "kernel": "expert_kernel<FP8,up> (gate+up+SwiGLU)", "achieved": up_gbs,
+                         "peak": peak, "unit": "GB/s", "frac": up_gbs / peak, "peak_kind": peak_kind,
+                         "traffic": traffic_from_profile()},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * cfg.hidden * 2,
+                    "d2h_bytes_per_step": T * cfg.hidden * 2},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks, "sweep": sweep, "device_status": status,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the up kernel from the committed ncu summary, when there is one."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get("expert_up_fp8_bytes_per_launch")
+    except Exception:
+        return None
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,111 @@
+/* B200-native MoE decode layer: layer-level C ABI (libstbl_moe.so).
+ *
+ * Drop-in for the reference's MoE layer, stbl/model.cu:426-594 (moe(), the body of
+ * stbl_block_test stage 4, stbl/stbl.h:75-81), in the reference's C-ABI style: plain pointers and
+ * sizes, int status (0 ok, -1 error, message from stbl_moe_error), caller-owned device buffers,
+ * work ordered on the caller's cudaStream_t.  Routing, dispatch, the expert products and the
+ * combine all stay on the GPU: there is no device->host copy inside a layer call.
+ *
+ * Numerics (checked against the CPU oracle, oracle/moe_oracle.c):
+ *   logits = W_g x (fp32), score = sigmoid (DeepSeek-V3) or sqrt(softplus) (the reference engine),
+ *   selection over score + bias (group-limited when n_groups > 1 and topk_groups < n_groups; ties go
+ *   to the lower expert id), weights = score / (sum + 1e-20) * route_scale (stbl/model.cu:444-451,
+ *   527-530); per expert g, u = bf16(W1 q(x)), bf16(W3 q(x)), h = bf16(silu(g) u w) (clamped when
+ *   swiglu_limit > 0, stbl/kernels.cu:445-459), out = bf16(W2 q(h)); y = bf16(sum of outputs in top-k
+ *   order + shared expert) (stbl/model.cu:589-592).  q() is act_quant (ref/kernel.py:35-45): per-128
+ *   fp32 scales for STBL_FMT_FP8_B128 weights, per-32 power-of-two scales for STBL_FMT_MXFP4.
+ */
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* weight formats */
+enum {
+    STBL_FMT_NONE = 0,
+    STBL_FMT_FP8_B128 = 1, /* e4m3 codes [rows][k]; fp32 scales [ceil(rows/128)][ceil(k/128)] */
+    STBL_FMT_MXFP4 = 2     /* e2m1 codes [rows][k/2], even k in the low nibble; e8m0 scales [rows][k/32] */
+};
+
+/* router score functions */
+enum { STBL_SCORE_SIGMOID = 0, STBL_SCORE_SQRT_SOFTPLUS = 1 };
+
+typedef struct stbl_moe stbl_moe;
+
+typedef struct stbl_moe_desc {
+    int hidden;        /* H: multiple of 512 */
+    int inter;         /* I: moe_intermediate, multiple of 512 */
+    int n_experts;     /* E routed experts, <= 512, multiple of n_groups */
+    int topk;          /* <= 16 */
+    int n_groups;      /* expert groups for group-limited routing (1: none), <= 32 */
+    int topk_groups;   /* groups kept */
+    int score_fn;      /* STBL_SCORE_* */
+    float route_scale; /* routed scaling factor */
+    float swiglu_limit;/* 0: no SwiGLU clamps */
+    int routed_fmt;    /* STBL_FMT_FP8_B128 or STBL_FMT_MXFP4 */
+    int shared_fmt;    /* STBL_FMT_FP8_B128 or STBL_FMT_NONE */
+    int max_tokens;    /* largest T passed to stbl_moe_forward, <= 256 */
+    const float *router_w;    /* device fp32 [E][H] */
+    const float *router_bias; /* device fp32 [E] (score-correction bias) */
+    /* routed experts, device: expert e of matrix m (0 gate [I][H], 1 up [I][H], 2 down [H][I]) starts
+       at routed_w[m] + e * routed_w_stride[m] bytes (stride 0: the packed size of one matrix) */
+    const void *routed_w[3];
+    const void *routed_s[3];
+    long long routed_w_stride[3];
+    long long routed_s_stride[3];
+    /* shared expert, device */
+    const void *shared_w[3];
+    const void *shared_s[3];
+} stbl_moe_desc;
+
+/* Validate the description, allocate the layer's workspace on the current device and build its
+ * expert table.  Weight pointers must be 16-byte aligned.  Returns 0, or -1 with err filled. */
+int stbl_moe_create(const stbl_moe_desc *desc, stbl_moe **out, char *err, int errlen);
+
+/* y = MoE(x) for T decode tokens: x and y are device bf16 [T][H].  Enqueued on `stream`; returns
+ * without waiting.  Returns -1 (see stbl_moe_error) for a bad argument. */
+int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaStream_t stream);
+
+/* The same with host buffers (pinned or pageable): copies x in, runs the layer, copies y out and
+ * waits for the stream.  The reference's stbl_block_test(stage 4) contract (stbl/model.cu:1065-1071). */
+int stbl_moe_forward_host(stbl_moe *m, const void *x_bf16_host, int T, void *y_bf16_host, cudaStream_t stream);
+
+/* Routing of the last call, copied to host (waits for the stream): idx [T][topk] in selection order
+ * (stbl_last_route, stbl/stbl.h:85-86), weights [T][topk], counts [E], offsets [E+1] and the
+ * bucketed dispatch permutation perm [T*topk] (perm[p] = token * topk + slot, expert-major, token
+ * order inside an expert).  Any pointer may be NULL.  Returns T of that call, or -1. */
+int stbl_moe_last_route(stbl_moe *m, int *idx, float *weights, int *counts, int *offsets, int *perm);
+
+/* Router scores of the last call (fp32 [T][E]), for parity checks.  Returns T, or -1. */
+int stbl_moe_last_scores(stbl_moe *m, float *scores);
+
+/* Point routed expert e at other device memory (an expert cache slot).  Takes effect for calls
+ * enqueued on `stream` after this one. */
+int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream);
+
+/* Device status bits raised by kernels since the last call of this function (waits for the
+ * device): 1 a wait timed out, 2 a dispatch entry was out of range, 4 copies were still in flight
+ * when a CTA gave up.  0 when every call so far ran cleanly. */
+int stbl_moe_status(stbl_moe *m, uint32_t *status);
+
+/* Per-kernel device timing, the counterpart of the reference's STBL_TIMING / stbl_timing
+ * (stbl/model.cu:13-15, 250-258; stbl/stbl.h:82-84), without its stream synchronisations: while
+ * enabled, every call records CUDA events on its stream around the router, expert-up and
+ * expert-down launches.  stbl_moe_timing waits for the recorded events, adds their durations to
+ * per-section totals in seconds (order: router, expert up, expert down; sec[3] = number of calls
+ * timed) and returns the number of entries written (4). */
+int stbl_moe_set_timing(stbl_moe *m, int enable);
+int stbl_moe_timing(stbl_moe *m, double *sec, int n);
+
+/* Kernel launches per forward call and layer counters. */
+void stbl_moe_stats(const stbl_moe *m, uint64_t *calls, uint64_t *tokens, int *launches_per_call);
+
+const char *stbl_moe_error(const stbl_moe *m);
+void stbl_moe_destroy(stbl_moe *m);
+
+#ifdef __cplusplus
+}
+#endif

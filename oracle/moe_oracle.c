@@ -229,24 +229,31 @@ static void butterfly32(float *v) {
     }
 }
 
+int orc_router_ksplit(int H) { return (H % 512 == 0) ? 4 : 1; }
+
 void orc_router_logits(const float *W, const uint16_t *x_bf16, int T, int E, int H, float *logits) {
+    const int ks_n = orc_router_ksplit(H), slice = H / ks_n;
 #pragma omp parallel for schedule(static)
     for (int e = 0; e < E; e++) {
-        const float *w = W + (size_t)e * H;
         for (int t = 0; t < T; t++) {
-            const uint16_t *x = x_bf16 + (size_t)t * H;
-            float lane[32];
-            for (int l = 0; l < 32; l++) {
-                float acc = 0.f;
-                for (int i = 0; i < H / 128; i++)
-                    for (int j = 0; j < 4; j++) {
-                        const int c = 128 * i + 4 * l + j;
-                        acc = fmaf(w[c], bf16_to_f32(x[c]), acc);
-                    }
-                lane[l] = acc;
+            float total = 0.f;
+            for (int ks = 0; ks < ks_n; ks++) {
+                const float *w = W + (size_t)e * H + (size_t)ks * slice;
+                const uint16_t *x = x_bf16 + (size_t)t * H + (size_t)ks * slice;
+                float lane[32];
+                for (int l = 0; l < 32; l++) {
+                    float acc = 0.f;
+                    for (int i = 0; i < slice / 128; i++)
+                        for (int j = 0; j < 4; j++) {
+                            const int c = 128 * i + 4 * l + j;
+                            acc = fmaf(w[c], bf16_to_f32(x[c]), acc);
+                        }
+                    lane[l] = acc;
+                }
+                butterfly32(lane);
+                total = ks == 0 ? lane[0] : total + lane[0];
             }
-            butterfly32(lane);
-            logits[(size_t)t * E + e] = lane[0];
+            logits[(size_t)t * E + e] = total;
         }
     }
 }

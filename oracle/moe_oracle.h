@@ -55,9 +55,12 @@ void orc_gemv_mxfp4(const uint8_t *w, const uint8_t *ws, int rows, int k, const 
                     int act_block, int n_tok, float *y);
 
 /* ---- router (model.cu:430-452 composition, V3 group-limited or V4 flat selection) ------------- */
-/* logits[t][e] = W[e] . x[t]; fp32 with the reduction order of the GPU router kernel: lane l of 32
- * takes k = 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, then an xor butterfly
- * over the 32 lane sums (16, 8, 4, 2, 1).  Needs h % 128 == 0. */
+/* logits[t][e] = W[e] . x[t]; fp32 with the reduction order of the GPU router kernel: the hidden
+ * dimension is cut into orc_router_ksplit(H) equal slices (4 when H % 512 == 0, else 1); in each, lane
+ * l of 32 takes k = 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, then an xor
+ * butterfly adds the 32 lane sums (16, 8, 4, 2, 1); the slice sums are added in slice order.
+ * Needs H % 128 == 0. */
+int orc_router_ksplit(int H);
 void orc_router_logits(const float *W, const uint16_t *x_bf16, int T, int E, int H, float *logits);
 /* scores, top-k ids in selection order (biased score descending, lower id first on ties) and
  * routing weights score / (sum + 1e-20) * route_scale (model.cu:444-451, 527-530). */

@@ -1,0 +1,491 @@
+// Layer object and C ABI of the MoE decode path (include/stbl_moe.h).
+//
+// One layer call is three kernel launches on the caller's stream (four or five when the routed and
+// shared experts have different formats): router (+ selection + dispatch), expert up (+ SwiGLU +
+// h re-quantization), expert down (+ ordered combine).  No host synchronisation inside a call.
+#include <stdio.h>
+#include <string.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/stbl_moe.h"
+#include "layer.cuh"
+
+namespace stbl {
+__global__ void router_kernel(RouterParams p);
+const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
+}  // namespace stbl
+
+using namespace stbl;
+
+#define CK(x)                                                                                        \
+    do {                                                                                             \
+        cudaError_t e_ = (x);                                                                        \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+namespace {
+
+constexpr int kRPG = 2;  // rows per row group per work item (the instantiation in experts.cu)
+
+// events of one timed call: before the router, after it, after the up launches, after the downs
+struct TimedCall {
+    cudaEvent_t ev[4];
+};
+
+struct KernelCfg {
+    const void *fn = nullptr;
+    int stage_bytes = 0, nst = 0, smem = 0;
+};
+
+int act_blk_of(int fmt) { return fmt == STBL_FMT_FP8_B128 ? 128 : 32; }
+int act_pow2_of(int fmt) { return fmt == STBL_FMT_FP8_B128 ? 0 : 1; }
+
+long long mat_bytes(int fmt, int rows, int k, bool scales) {
+    if (fmt == STBL_FMT_FP8_B128)
+        return scales ? 4LL * ((rows + 127) / 128) * ((k + 127) / 128) : (long long)rows * k;
+    return scales ? (long long)rows * (k / 32) : (long long)rows * (k / 2);
+}
+
+bool lanes_ok(int K) {
+    if (K % 32) return false;
+    const int lk = K / 32;
+    if (lk >= 32) return lk % 32 == 0 && lk <= kConsumerThreads;
+    return lk >= 8 && 32 % lk == 0;
+}
+
+const void *expert_fn(int fmt, bool up) { return expert_kernel_ptr(fmt, up); }
+
+}  // namespace
+
+struct stbl_moe {
+    stbl_moe_desc d{};
+    int E = 0, H = 0, I = 0, K = 0, Tmax = 0, ksplit = 1, sms = 0, has_shared = 0;
+    int nG_H = 0, nG_I = 0;
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    float *partial = nullptr, *scores = nullptr, *wts = nullptr, *xs_a = nullptr, *xs_b = nullptr, *hs = nullptr;
+    int *idx = nullptr, *counts = nullptr, *offsets = nullptr, *perm = nullptr, *n_chunks = nullptr;
+    int *hcnt = nullptr, *ccnt = nullptr;
+    Chunk *chunks = nullptr;
+    uint8_t *xq_a = nullptr, *xq_b = nullptr, *hq = nullptr;
+    uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
+    unsigned int *done = nullptr;
+    uint32_t *status = nullptr;
+    ExpertPtrs *experts = nullptr;
+    std::vector<ExpertPtrs> host_experts;
+    int n_zero = 0;
+    int router_grid = 0, router_smem = 0;
+    KernelCfg up_r, up_s, down_r, down_s;
+    int last_T = 0;
+    uint64_t calls = 0, tokens = 0;
+    int launches = 0;
+    std::string err;
+    // timing (stbl_moe_set_timing)
+    int timing = 0;
+    std::vector<TimedCall> pending, event_pool;
+    double tsum[3] = {0, 0, 0};
+    uint64_t tcalls = 0;
+};
+
+namespace {
+
+template <typename T>
+T *carve(char *&p, size_t n) {
+    T *r = reinterpret_cast<T *>(p);
+    p += (n * sizeof(T) + 255) & ~(size_t)255;
+    return r;
+}
+
+KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
+    KernelCfg c;
+    c.fn = expert_fn(fmt, up);
+    const int nmat = up ? 2 : 1;
+    const int K = up ? H : I;
+    const int lk = K / 32, n_rg = kConsumerThreads / lk, RI = n_rg * kRPG;
+    const int rb = fmt == STBL_FMT_FP8_B128 ? K : K / 2;
+    int stage = nmat * RI * rb + (fmt == STBL_FMT_MXFP4 ? nmat * RI * (K / 32) : 0);
+    stage = (stage + 127) & ~127;
+    const int extra = 2 * 8 * 8 + 64 * 32 * 4 + 64 * 4 + 128;
+    int nst = (max_smem - extra) / stage;
+    if (nst > 8) nst = 8;
+    if (nst < 2) throw std::runtime_error("expert weight tile does not fit twice in shared memory");
+    c.stage_bytes = stage;
+    c.nst = nst;
+    c.smem = nst * stage + 2 * nst * 8 + 64 * 32 * 4 + 64 * 4;
+    CK(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
+    return c;
+}
+
+void create(stbl_moe *m, const stbl_moe_desc *d) {
+    if (!d) throw std::runtime_error("null description");
+    m->d = *d;
+    const int H = d->hidden, I = d->inter, E = d->n_experts, K = d->topk;
+    if (H <= 0 || I <= 0 || H % 512 || I % 512 || !lanes_ok(H) || !lanes_ok(I))
+        throw std::runtime_error("hidden and inter must be multiples of 512 with K/32 lanes a multiple or divisor of 32 (<= 448)");
+    if (E < 1 || E > kMaxExperts) throw std::runtime_error("n_experts must be in 1..512");
+    if (K < 1 || K > kMaxTopk || K > E) throw std::runtime_error("topk must be in 1..16 and <= n_experts");
+    if (d->n_groups < 1 || d->n_groups > 32 || E % d->n_groups) throw std::runtime_error("n_groups must divide n_experts and be <= 32");
+    if (d->topk_groups < 1 || d->topk_groups > d->n_groups) throw std::runtime_error("topk_groups must be in 1..n_groups");
+    const int gsz = E / d->n_groups;
+    const bool grouped = d->n_groups > 1 && d->topk_groups < d->n_groups;
+    if (grouped && (gsz < 2 || d->topk_groups * gsz < K)) throw std::runtime_error("kept groups hold fewer than topk experts");
+    if (d->score_fn != STBL_SCORE_SIGMOID && d->score_fn != STBL_SCORE_SQRT_SOFTPLUS) throw std::runtime_error("bad score_fn");
+    if (d->routed_fmt != STBL_FMT_FP8_B128 && d->routed_fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad routed_fmt");
+    if (d->shared_fmt != STBL_FMT_FP8_B128 && d->shared_fmt != STBL_FMT_NONE) throw std::runtime_error("bad shared_fmt");
+    if (d->max_tokens < 1 || d->max_tokens > 256) throw std::runtime_error("max_tokens must be in 1..256");
+    if (!d->router_w || !d->router_bias) throw std::runtime_error("router weights missing");
+    m->E = E, m->H = H, m->I = I, m->K = K, m->Tmax = d->max_tokens;
+    m->ksplit = router_ksplit(H);
+    m->has_shared = d->shared_fmt != STBL_FMT_NONE;
+    m->nG_H = (H + 127) / 128, m->nG_I = (I + 127) / 128;
+
+    // expert table (entry E: shared expert)
+    m->host_experts.assign(E + 1, ExpertPtrs{});
+    const int rows[3] = {I, I, H}, ks[3] = {H, H, I};
+    for (int mt = 0; mt < 3; mt++) {
+        if (!d->routed_w[mt] || !d->routed_s[mt]) throw std::runtime_error("routed expert weights missing");
+        const long long wst = d->routed_w_stride[mt] ? d->routed_w_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], false);
+        const long long sst = d->routed_s_stride[mt] ? d->routed_s_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], true);
+        for (int e = 0; e < E; e++) {
+            const uint8_t *w = static_cast<const uint8_t *>(d->routed_w[mt]) + (size_t)e * wst;
+            const uint8_t *s = static_cast<const uint8_t *>(d->routed_s[mt]) + (size_t)e * sst;
+            if (((uintptr_t)w & 15) || ((uintptr_t)s & 15)) throw std::runtime_error("expert weights must be 16-byte aligned");
+            m->host_experts[e].w[mt] = w;
+            m->host_experts[e].s[mt] = s;
+        }
+        if (m->has_shared) {
+            if (!d->shared_w[mt] || !d->shared_s[mt]) throw std::runtime_error("shared expert weights missing");
+            if (((uintptr_t)d->shared_w[mt] & 15) || ((uintptr_t)d->shared_s[mt] & 15))
+                throw std::runtime_error("shared expert weights must be 16-byte aligned");
+            m->host_experts[E].w[mt] = static_cast<const uint8_t *>(d->shared_w[mt]);
+            m->host_experts[E].s[mt] = d->shared_s[mt];
+        }
+    }
+
+    // workspace
+    const int T = m->Tmax, npos = T * K + T;
+    auto layout = [&](char *base) {
+        char *p = base;
+        m->experts = carve<ExpertPtrs>(p, E + 1);
+        m->partial = carve<float>(p, (size_t)m->ksplit * T * E);
+        m->scores = carve<float>(p, (size_t)T * E);
+        m->idx = carve<int>(p, (size_t)T * K);
+        m->wts = carve<float>(p, (size_t)T * K);
+        m->counts = carve<int>(p, E);
+        m->offsets = carve<int>(p, E + 1);
+        m->perm = carve<int>(p, (size_t)T * K);
+        m->chunks = carve<Chunk>(p, npos);
+        m->n_chunks = carve<int>(p, 4);
+        m->xq_a = carve<uint8_t>(p, (size_t)T * H);
+        m->xs_a = carve<float>(p, (size_t)T * (H / 32));
+        m->xq_b = carve<uint8_t>(p, (size_t)T * H);
+        m->xs_b = carve<float>(p, (size_t)T * (H / 32));
+        m->h = carve<uint16_t>(p, (size_t)npos * I);
+        m->hq = carve<uint8_t>(p, (size_t)npos * I);
+        m->hs = carve<float>(p, (size_t)npos * (I / 32));
+        m->hcnt = carve<int>(p, (size_t)npos * m->nG_I + (size_t)T * m->nG_H);  // hcnt then ccnt: one zeroed range
+        m->ccnt = m->hcnt + (size_t)npos * m->nG_I;
+        m->eo = carve<uint16_t>(p, (size_t)T * K * H);
+        m->sh = carve<uint16_t>(p, (size_t)T * H);
+        m->xin = carve<uint16_t>(p, (size_t)T * H);
+        m->yout = carve<uint16_t>(p, (size_t)T * H);
+        m->done = carve<unsigned int>(p, 4);
+        m->status = carve<uint32_t>(p, 4);
+        return (size_t)(p - base);
+    };
+    m->ws_bytes = layout(nullptr);
+    CK(cudaMalloc(&m->ws, m->ws_bytes));
+    CK(cudaMemset(m->ws, 0, m->ws_bytes));
+    layout(static_cast<char *>(m->ws));
+    m->n_zero = npos * m->nG_I + T * m->nG_H;
+    CK(cudaMemcpy(m->experts, m->host_experts.data(), sizeof(ExpertPtrs) * (E + 1), cudaMemcpyHostToDevice));
+
+    int dev = 0, max_smem = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    m->router_grid = (E * m->ksplit + kRouterThreads / 32 - 1) / (kRouterThreads / 32);
+    const int TW = (T + 31) / 32;
+    m->router_smem = 2 * (kRouterThreads / 32) * E * 4 + T * K * 4 + 4 * E * 4 + E * TW * 4;
+    CK(cudaFuncSetAttribute((const void *)router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m->router_smem));
+    m->up_r = make_cfg(d->routed_fmt, true, H, I, max_smem);
+    m->down_r = make_cfg(d->routed_fmt, false, H, I, max_smem);
+    if (m->has_shared && d->shared_fmt != d->routed_fmt) {
+        m->up_s = make_cfg(d->shared_fmt, true, H, I, max_smem);
+        m->down_s = make_cfg(d->shared_fmt, false, H, I, max_smem);
+    }
+}
+
+ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
+    ExpertParams p{};
+    p.experts = m->experts;
+    p.chunks = m->chunks;
+    p.n_chunks = m->n_chunks;
+    p.T = T, p.topk = m->K, p.E = m->E, p.H = m->H, p.I = m->I;
+    p.perm = m->perm;
+    p.wts = m->wts;
+    const bool routed_buf = fmt == m->d.routed_fmt;
+    if (up) {
+        p.xq = routed_buf ? m->xq_a : m->xq_b;
+        p.xs = routed_buf ? m->xs_a : m->xs_b;
+        p.xs_stride = m->H / 32;
+    } else {
+        p.xq = m->hq;
+        p.xs = m->hs;
+        p.xs_stride = m->I / 32;
+    }
+    p.act_blk = act_blk_of(fmt);
+    p.act_pow2 = act_pow2_of(fmt);
+    p.hs_stride = m->I / 32;
+    p.swiglu_limit = m->d.swiglu_limit;
+    p.h = m->h, p.hq = m->hq, p.hs = m->hs, p.hcnt = m->hcnt;
+    p.eo = m->eo, p.sh = m->sh, p.ccnt = m->ccnt;
+    p.has_shared = m->has_shared;
+    p.status = m->status;
+    return p;
+}
+
+void launch_expert(const KernelCfg &c, ExpertParams p, int grid, cudaStream_t st) {
+    void *args[] = {&p, const_cast<int *>(&c.stage_bytes), const_cast<int *>(&c.nst)};
+    CK(cudaLaunchKernel(c.fn, dim3(grid), dim3(kExpertThreads), args, c.smem, st));
+}
+
+TimedCall take_events(stbl_moe *m);
+void collect_timing(stbl_moe *m, size_t keep);
+
+void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
+    if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
+    if (!x || !y) throw std::runtime_error("null x or y");
+    TimedCall tc{};
+    if (m->timing) {
+        if (m->pending.size() >= 256) collect_timing(m, 0);
+        tc = take_events(m);
+        CK(cudaEventRecord(tc.ev[0], st));
+    }
+    RouterParams r{};
+    r.W = m->d.router_w, r.bias = m->d.router_bias, r.x = static_cast<const uint16_t *>(x);
+    r.T = T, r.E = m->E, r.H = m->H, r.topk = m->K, r.n_groups = m->d.n_groups, r.topk_groups = m->d.topk_groups;
+    r.score_fn = m->d.score_fn, r.route_scale = m->d.route_scale, r.ksplit = m->ksplit, r.has_shared = m->has_shared;
+    r.partial = m->partial, r.scores = m->scores, r.idx = m->idx, r.wts = m->wts;
+    r.counts = m->counts, r.offsets = m->offsets, r.perm = m->perm, r.chunks = m->chunks, r.n_chunks = m->n_chunks;
+    const int fr = m->d.routed_fmt, fs = m->has_shared ? m->d.shared_fmt : fr;
+    r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
+    if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
+    else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
+    r.zero = m->hcnt, r.n_zero = m->n_zero, r.done = m->done, r.status = m->status;
+    void *rargs[] = {&r};
+    CK(cudaLaunchKernel((const void *)router_kernel, dim3(m->router_grid), dim3(kRouterThreads), rargs, m->router_smem, st));
+    if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
+    int launches = 1;
+
+    const int grid = m->sms;
+    ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
+    pd.y = pu.y = static_cast<uint16_t *>(y);
+    if (m->has_shared && fs != fr) {
+        const int ns = (T + kNT - 1) / kNT;
+        ExpertParams su = expert_params(m, T, fs, true), sd = expert_params(m, T, fs, false);
+        su.y = sd.y = static_cast<uint16_t *>(y);
+        su.chunk_begin = 0, su.chunk_end = ns;
+        sd.chunk_begin = 0, sd.chunk_end = ns;
+        pu.chunk_begin = ns, pu.chunk_end = -1;
+        pd.chunk_begin = ns, pd.chunk_end = -1;
+        launch_expert(m->up_s, su, grid, st);
+        launch_expert(m->up_r, pu, grid, st);
+        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launch_expert(m->down_s, sd, grid, st);
+        launch_expert(m->down_r, pd, grid, st);
+        launches += 4;
+    } else {
+        pu.chunk_begin = pd.chunk_begin = 0;
+        pu.chunk_end = pd.chunk_end = -1;
+        launch_expert(m->up_r, pu, grid, st);
+        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launch_expert(m->down_r, pd, grid, st);
+        launches += 2;
+    }
+    if (m->timing) {
+        CK(cudaEventRecord(tc.ev[3], st));
+        m->pending.push_back(tc);
+    }
+    m->launches = launches;
+    m->last_T = T;
+    m->calls++;
+    m->tokens += T;
+}
+
+TimedCall take_events(stbl_moe *m) {
+    if (!m->event_pool.empty()) {
+        TimedCall t = m->event_pool.back();
+        m->event_pool.pop_back();
+        return t;
+    }
+    TimedCall t{};
+    for (auto &e : t.ev) CK(cudaEventCreate(&e));
+    return t;
+}
+
+// wait for the pending timed calls (all but the newest `keep`) and add their durations
+void collect_timing(stbl_moe *m, size_t keep) {
+    while (m->pending.size() > keep) {
+        TimedCall t = m->pending.front();
+        m->pending.erase(m->pending.begin());
+        CK(cudaEventSynchronize(t.ev[3]));
+        for (int i = 0; i < 3; i++) {
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, t.ev[i], t.ev[i + 1]));
+            m->tsum[i] += ms * 1e-3;
+        }
+        m->tcalls++;
+        m->event_pool.push_back(t);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int stbl_moe_create(const stbl_moe_desc *desc, stbl_moe **out, char *err, int errlen) {
+    stbl_moe *m = new stbl_moe();
+    try {
+        create(m, desc);
+        *out = m;
+        return 0;
+    } catch (const std::exception &e) {
+        if (err && errlen > 0) snprintf(err, errlen, "%s", e.what());
+        if (m->ws) cudaFree(m->ws);
+        delete m;
+        *out = nullptr;
+        return -1;
+    }
+}
+
+int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaStream_t stream) {
+    try {
+        forward(m, x_bf16, T, y_bf16, stream);
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_forward_host(stbl_moe *m, const void *x_bf16_host, int T, void *y_bf16_host, cudaStream_t stream) {
+    try {
+        if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
+        const size_t bytes = (size_t)T * m->H * 2;
+        CK(cudaMemcpyAsync(m->xin, x_bf16_host, bytes, cudaMemcpyHostToDevice, stream));
+        forward(m, m->xin, T, m->yout, stream);
+        CK(cudaMemcpyAsync(y_bf16_host, m->yout, bytes, cudaMemcpyDeviceToHost, stream));
+        CK(cudaStreamSynchronize(stream));
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_last_route(stbl_moe *m, int *idx, float *weights, int *counts, int *offsets, int *perm) {
+    try {
+        const int T = m->last_T;
+        CK(cudaDeviceSynchronize());
+        if (idx) CK(cudaMemcpy(idx, m->idx, sizeof(int) * T * m->K, cudaMemcpyDeviceToHost));
+        if (weights) CK(cudaMemcpy(weights, m->wts, sizeof(float) * T * m->K, cudaMemcpyDeviceToHost));
+        if (counts) CK(cudaMemcpy(counts, m->counts, sizeof(int) * m->E, cudaMemcpyDeviceToHost));
+        if (offsets) CK(cudaMemcpy(offsets, m->offsets, sizeof(int) * (m->E + 1), cudaMemcpyDeviceToHost));
+        if (perm) CK(cudaMemcpy(perm, m->perm, sizeof(int) * T * m->K, cudaMemcpyDeviceToHost));
+        return T;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_last_scores(stbl_moe *m, float *scores) {
+    try {
+        CK(cudaDeviceSynchronize());
+        CK(cudaMemcpy(scores, m->scores, sizeof(float) * m->last_T * m->E, cudaMemcpyDeviceToHost));
+        return m->last_T;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream) {
+    try {
+        if (e < 0 || e >= m->E) throw std::runtime_error("expert id out of range");
+        ExpertPtrs p{};
+        for (int i = 0; i < 3; i++) {
+            if (!w[i] || !s[i] || ((uintptr_t)w[i] & 15) || ((uintptr_t)s[i] & 15))
+                throw std::runtime_error("expert pointers must be non-null and 16-byte aligned");
+            p.w[i] = static_cast<const uint8_t *>(w[i]);
+            p.s[i] = s[i];
+        }
+        m->host_experts[e] = p;
+        CK(cudaMemcpyAsync(m->experts + e, &m->host_experts[e], sizeof(ExpertPtrs), cudaMemcpyHostToDevice, stream));
+        return 0;
+    } catch (const std::exception &e2) {
+        m->err = e2.what();
+        return -1;
+    }
+}
+
+int stbl_moe_status(stbl_moe *m, uint32_t *status) {
+    try {
+        CK(cudaDeviceSynchronize());
+        uint32_t s = 0;
+        CK(cudaMemcpy(&s, m->status, 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemset(m->status, 0, 4));
+        if (s) CK(cudaMemset(m->hcnt, 0, sizeof(int) * m->n_zero));
+        *status = s;
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_set_timing(stbl_moe *m, int enable) {
+    try {
+        if (!enable) collect_timing(m, 0);
+        m->timing = enable != 0;
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_timing(stbl_moe *m, double *sec, int n) {
+    try {
+        collect_timing(m, 0);
+        for (int i = 0; i < n && i < 3; i++) sec[i] = m->tsum[i];
+        if (n > 3) sec[3] = (double)m->tcalls;
+        return 4;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+void stbl_moe_stats(const stbl_moe *m, uint64_t *calls, uint64_t *tokens, int *launches_per_call) {
+    if (calls) *calls = m->calls;
+    if (tokens) *tokens = m->tokens;
+    if (launches_per_call) *launches_per_call = m->launches;
+}
+
+const char *stbl_moe_error(const stbl_moe *m) { return m ? m->err.c_str() : "null layer"; }
+
+void stbl_moe_destroy(stbl_moe *m) {
+    if (!m) return;
+    for (auto &t : m->pending) cudaEventSynchronize(t.ev[3]), m->event_pool.push_back(t);
+    for (auto &t : m->event_pool)
+        for (auto e : t.ev) cudaEventDestroy(e);
+    if (m->ws) cudaFree(m->ws);
+    delete m;
+}
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+"""ctypes binding of libstbl_moe.so (include/stbl_moe.h, include/stbl_kernels.h).
+
+The reference drives its engine from Python through ctypes (stbl/run.py:37-47, stbl/test_kernels.py:25);
+this module does the same for the B200 library.  There is no fallback: if the library is missing
+the import of a layer fails with an error that says how to build it.
+"""
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libstbl_moe.so")
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+F = ctypes.c_float
+LL = ctypes.c_longlong
+U32 = ctypes.c_uint32
+U64 = ctypes.c_uint64
+
+
+class MoEDesc(ctypes.Structure):
+    _fields_ = [
+        ("hidden", I), ("inter", I), ("n_experts", I), ("topk", I), ("n_groups", I), ("topk_groups", I),
+        ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
+        ("max_tokens", I), ("router_w", P), ("router_bias", P), ("routed_w", P * 3), ("routed_s", P * 3),
+        ("routed_w_stride", LL * 3), ("routed_s_stride", LL * 3), ("shared_w", P * 3), ("shared_s", P * 3),
+    ]
+
+
+# every symbol the headers declare, with its C signature
+SIGNATURES = {
+    # include/stbl_moe.h
+    "stbl_moe_create": (I, [ctypes.POINTER(MoEDesc), ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_moe_forward": (I, [P, P, I, P, P]),
+    "stbl_moe_forward_host": (I, [P, P, I, P, P]),
+    "stbl_moe_last_route": (I, [P, P, P, P, P, P]),
+    "stbl_moe_last_scores": (I, [P, P]),
+    "stbl_moe_set_expert": (I, [P, I, P, P, P]),
+    "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),
+    "stbl_moe_set_timing": (I, [P, I]),
+    "stbl_moe_timing": (I, [P, P, I]),
+    "stbl_moe_stats": (None, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(I)]),
+    "stbl_moe_error": (ctypes.c_char_p, [P]),
+    "stbl_moe_destroy": (None, [P]),
+    # include/stbl_kernels.h
+    "stbl_act_quant_fp8": (None, [P, I, P]),
+    "stbl_round_bf16": (None, [P, I, P]),
+    "stbl_gemv_fp8": (None, [P, P, P, P, I, I, I, P]),
+    "stbl_gemv_mxfp4": (None, [P, P, P, I, I, P]),
+    "stbl_gemv_mxfp4_batch": (None, [P, P, P, I, I, I, P]),
+    "stbl_gemv_f32": (None, [P, P, P, I, I, I, P]),
+    "stbl_sqrt_softplus": (None, [P, I, P]),
+    "stbl_swiglu": (None, [P, P, P, F, F, I, P]),
+    "stbl_swiglu_batch": (None, [P, P, P, P, I, F, I, P]),
+    "stbl_axpy": (None, [P, P, F, I, P]),
+}
+
+_lib = None
+
+
+def load():
+    """The library, with argument types set.  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m stblarge_b200.build` "
+                               "(the MoE path has no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib

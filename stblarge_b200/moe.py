@@ -1,0 +1,155 @@
+"""Host-side mirror of the MoE layer: a thin Python object over the stbl_moe C ABI.
+
+    layer = MoELayer(cfg, weights, max_tokens=16)   # weights: device tensors (see synth.device_layer)
+    y = layer(x)                                     # x: cuda bf16 [T, hidden] -> y: cuda bf16 [T, hidden]
+    route = layer.last_route()                       # expert ids, weights, dispatch permutation
+
+The layer call enqueues three kernels on the current torch stream (router + dispatch, expert
+up + SwiGLU, expert down + combine) and never synchronises.  `forward_host` is the end-to-end form
+(host buffers in and out, as the reference's stbl_block_test stage 4).
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import lib as L
+from .config import FMT_NONE, MoEConfig
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+class MoELayer:
+    def __init__(self, cfg: MoEConfig, weights: dict, max_tokens: int = 16):
+        self.lib = L.load()
+        self.cfg = cfg
+        self.weights = weights  # keeps the device tensors alive
+        self.max_tokens = max_tokens
+        d = L.MoEDesc()
+        d.hidden, d.inter, d.n_experts, d.topk = cfg.hidden, cfg.inter, cfg.n_experts, cfg.topk
+        d.n_groups, d.topk_groups, d.score_fn = cfg.n_groups, cfg.topk_groups, cfg.score_fn
+        d.route_scale, d.swiglu_limit = cfg.route_scale, cfg.swiglu_limit
+        d.routed_fmt, d.shared_fmt, d.max_tokens = cfg.routed_fmt, cfg.shared_fmt, max_tokens
+        d.router_w = weights["router_w"].data_ptr()
+        d.router_bias = weights["router_bias"].data_ptr()
+        for m in range(3):
+            w, s = weights["routed_w"][m], weights["routed_s"][m]
+            d.routed_w[m], d.routed_s[m] = w.data_ptr(), s.data_ptr()
+            d.routed_w_stride[m] = w.stride(0) * w.element_size()
+            d.routed_s_stride[m] = s.stride(0) * s.element_size()
+            if cfg.shared_fmt != FMT_NONE:
+                d.shared_w[m] = weights["shared_w"][m].data_ptr()
+                d.shared_s[m] = weights["shared_s"][m].data_ptr()
+        err = ctypes.create_string_buffer(512)
+        h = ctypes.c_void_p()
+        if self.lib.stbl_moe_create(ctypes.byref(d), ctypes.byref(h), err, 512) != 0:
+            raise RuntimeError("stbl_moe_create: " + err.value.decode())
+        self.handle = h
+        self._desc = d
+
+    def _check(self, rc, what):
+        if rc < 0:
+            raise RuntimeError(f"{what}: {self.lib.stbl_moe_error(self.handle).decode()}")
+        return rc
+
+    def __call__(self, x, out=None, stream=None):
+        return self.forward(x, out, stream)
+
+    def forward(self, x, out=None, stream=None):
+        """x: cuda [T, hidden] bfloat16 (or int16/uint16 bf16 bits)."""
+        assert x.is_cuda and x.dim() == 2 and x.shape[1] == self.cfg.hidden and x.element_size() == 2
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self._check(self.lib.stbl_moe_forward(self.handle, _ptr(x), x.shape[0], _ptr(out), ctypes.c_void_p(st.cuda_stream)),
+                    "stbl_moe_forward")
+        return out
+
+    def forward_host(self, x_bits, y_bits=None, stream=None):
+        """End to end with host buffers: x_bits uint16 [T, hidden] (numpy or pinned torch)."""
+        if isinstance(x_bits, np.ndarray):
+            x_bits = np.ascontiguousarray(x_bits, np.uint16)
+            T = x_bits.shape[0]
+            y = np.empty_like(x_bits) if y_bits is None else y_bits
+            xp, yp = x_bits.ctypes.data, y.ctypes.data
+        else:
+            T = x_bits.shape[0]
+            y = torch.empty_like(x_bits) if y_bits is None else y_bits
+            xp, yp = x_bits.data_ptr(), y.data_ptr()
+        st = stream if stream is not None else torch.cuda.current_stream()
+        self._check(self.lib.stbl_moe_forward_host(self.handle, ctypes.c_void_p(xp), T, ctypes.c_void_p(yp),
+                                                   ctypes.c_void_p(st.cuda_stream)), "stbl_moe_forward_host")
+        return y
+
+    def last_route(self):
+        cfg = self.cfg
+        T = self.max_tokens
+        idx = np.empty((T, cfg.topk), np.int32)
+        w = np.empty((T, cfg.topk), np.float32)
+        counts = np.empty(cfg.n_experts, np.int32)
+        offsets = np.empty(cfg.n_experts + 1, np.int32)
+        perm = np.empty(T * cfg.topk, np.int32)
+        T = self._check(self.lib.stbl_moe_last_route(self.handle, idx.ctypes.data, w.ctypes.data, counts.ctypes.data,
+                                                     offsets.ctypes.data, perm.ctypes.data), "stbl_moe_last_route")
+        return {"idx": idx[:T], "weights": w[:T], "counts": counts, "offsets": offsets, "perm": perm[:T * cfg.topk]}
+
+    def last_scores(self):
+        s = np.empty((self.max_tokens, self.cfg.n_experts), np.float32)
+        T = self._check(self.lib.stbl_moe_last_scores(self.handle, s.ctypes.data), "stbl_moe_last_scores")
+        return s[:T]
+
+    def set_expert(self, e, w, s, stream=None):
+        """Point routed expert e at other device tensors (three codes, three scales)."""
+        wp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in w])
+        sp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in s])
+        st = stream if stream is not None else torch.cuda.current_stream()
+        self._check(self.lib.stbl_moe_set_expert(self.handle, e, wp, sp, ctypes.c_void_p(st.cuda_stream)),
+                    "stbl_moe_set_expert")
+
+    def status(self):
+        s = ctypes.c_uint32()
+        self._check(self.lib.stbl_moe_status(self.handle, ctypes.byref(s)), "stbl_moe_status")
+        return s.value
+
+    def set_timing(self, enable=True):
+        self._check(self.lib.stbl_moe_set_timing(self.handle, int(enable)), "stbl_moe_set_timing")
+
+    def timing(self):
+        """Per-kernel device seconds summed over the timed calls: router, up, down, calls."""
+        sec = np.zeros(4, np.float64)
+        self._check(self.lib.stbl_moe_timing(self.handle, sec.ctypes.data, 4), "stbl_moe_timing")
+        return {"router": sec[0], "up": sec[1], "down": sec[2], "calls": int(sec[3])}
+
+    def stats(self):
+        calls, tokens, launches = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_int()
+        self.lib.stbl_moe_stats(self.handle, ctypes.byref(calls), ctypes.byref(tokens), ctypes.byref(launches))
+        return {"calls": calls.value, "tokens": tokens.value, "launches_per_call": launches.value}
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.stbl_moe_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def host_weights_to_device(cfg, W, device="cuda"):
+    """Upload numpy weights made by synth.host_layer into the expert-major device layout."""
+    out = {"router_w": torch.from_numpy(W["router_w"]).to(device),
+           "router_bias": torch.from_numpy(W["router_bias"]).to(device),
+           "routed_w": [], "routed_s": [], "shared_w": None, "shared_s": None}
+    for m in range(3):
+        out["routed_w"].append(torch.from_numpy(np.stack([W["routed"][m][e][0] for e in range(cfg.n_experts)])).to(device))
+        out["routed_s"].append(torch.from_numpy(np.stack([W["routed"][m][e][1] for e in range(cfg.n_experts)])).to(device))
+    if cfg.shared_fmt != FMT_NONE:
+        out["shared_w"] = [torch.from_numpy(W["shared"][m][0]).to(device) for m in range(3)]
+        out["shared_s"] = [torch.from_numpy(W["shared"][m][1]).to(device) for m in range(3)]
+    return out

@@ -1,0 +1,180 @@
+"""Parity of the B200 MoE layer (libstbl_moe.so through its C ABI) with the CPU oracle.
+
+Bar: router logits, scores, expert ids, routing weights and the dispatch permutation bit-exact;
+layer output within max-abs 1e-2 of max |reference| in bf16 (BASELINE tolerance), reported in bf16
+ulps as well.  Small layers run the oracle on every expert; full-size layers hand the oracle only
+the experts the GPU chose (it fails if it would route elsewhere)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from stblarge_b200 import synth
+from stblarge_b200.config import CFG1, CFG1_FP4, CFG2, CFG3, FMT_NONE
+from stblarge_b200.moe import MoELayer, host_weights_to_device
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def compare_y(y_bits, ref_bits):
+    y, ref = O.bf16_bits_to_f32(y_bits), O.bf16_bits_to_f32(ref_bits)
+    err = np.abs(y - ref).max()
+    scale = np.abs(ref).max()
+    ulps = np.abs(y - ref) / np.maximum(np.abs(ref) * 2.0 ** -8, 1e-30)
+    return err / scale, float(np.mean(y_bits == ref_bits)), float(ulps.max())
+
+
+def oracle_weights_from_device(cfg, dev, experts):
+    W = {"router_w": dev["router_w"].cpu().numpy(), "router_bias": dev["router_bias"].cpu().numpy(),
+         "routed": [[None] * cfg.n_experts for _ in range(3)], "shared": None}
+    for e in sorted(set(int(v) for v in experts)):
+        for m in range(3):
+            W["routed"][m][e] = (dev["routed_w"][m][e].cpu().numpy(), dev["routed_s"][m][e].cpu().numpy())
+    if cfg.shared_fmt != FMT_NONE:
+        W["shared"] = [(dev["shared_w"][m].cpu().numpy(), dev["shared_s"][m].cpu().numpy()) for m in range(3)]
+    return W
+
+
+def run_and_check(cfg, layer, dev_w, host_W, x_bits):
+    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+    y = layer(x)
+    torch.cuda.synchronize()
+    y_bits = y.view(torch.int16).cpu().numpy().view(np.uint16)
+    route = layer.last_route()
+    scores = layer.last_scores()
+    if host_W is None:
+        host_W = oracle_weights_from_device(cfg, dev_w, route["idx"].reshape(-1))
+    # router: logits order restated exactly in the oracle -> scores, ids, weights, dispatch bit-exact
+    lg = O.router_logits(host_W["router_w"], x_bits)
+    s_ref, idx_ref, w_ref = O.router_select(lg, host_W["router_bias"], cfg.topk, cfg.n_groups, cfg.topk_groups,
+                                            cfg.score_fn, cfg.route_scale)
+    assert np.array_equal(scores.view(np.uint32), s_ref.view(np.uint32)), "router scores differ"
+    assert np.array_equal(route["idx"], idx_ref), "expert ids differ"
+    assert np.array_equal(route["weights"].view(np.uint32), w_ref.view(np.uint32)), "routing weights differ"
+    counts, offsets, perm = O.dispatch(idx_ref, cfg.n_experts)
+    assert np.array_equal(route["counts"], counts)
+    assert np.array_equal(route["offsets"], offsets)
+    assert np.array_equal(route["perm"], perm), "dispatch permutation differs"
+    y_ref, idx2, _ = O.moe_forward(cfg.as_dict(), host_W, x_bits)
+    assert np.array_equal(idx2, idx_ref)
+    rel, same, ulps = compare_y(y_bits, y_ref)
+    assert rel <= TOL, f"max-abs-rel {rel:.3e} (bit-identical fraction {same:.4f}, max {ulps:.1f} bf16 ulps)"
+    assert layer.status() == 0
+    return rel, same
+
+
+@pytest.fixture(scope="module")
+def small_layers():
+    out = {}
+    for cfg in (CFG1, CFG1_FP4):
+        W = synth.host_layer(cfg)
+        dev = host_weights_to_device(cfg, W)
+        out[cfg.name] = (W, dev, MoELayer(cfg, dev, max_tokens=64))
+    return out
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_fp4"])
+@pytest.mark.parametrize("T", [1, 4, 5, 16, 64])
+def test_small_layer_parity(small_layers, name, T):
+    W, dev, layer = small_layers[name]
+    cfg = layer.cfg
+    run_and_check(cfg, layer, dev, W, synth.make_x(cfg.hidden, T, seed=100 + T))
+
+
+@pytest.mark.parametrize("name,golden_name", [("cfg1", "layer_cfg1"), ("cfg1_fp4", "layer_cfg1_fp4")])
+def test_small_layer_matches_reference_golden(small_layers, golden, name, golden_name):
+    """The GPU layer against the reference's own torch composition (fixture from ref/kernel.py)."""
+    W, dev, layer = small_layers[name]
+    g = golden(golden_name)
+    x = torch.from_numpy(g["x"].view(np.int16)).cuda()
+    y = layer(x)
+    torch.cuda.synchronize()
+    route = layer.last_route()
+    assert np.array_equal(route["idx"], g["idx"])
+    np.testing.assert_allclose(route["weights"], g["w"], rtol=1e-6)
+    rel, _, _ = compare_y(y.view(torch.int16).cpu().numpy().view(np.uint16), g["y"])
+    assert rel <= TOL
+
+
+def test_repeat_is_bitwise_deterministic(small_layers):
+    W, dev, layer = small_layers["cfg1"]
+    x = torch.from_numpy(synth.make_x(1024, 16, seed=7).view(np.int16)).cuda()
+    a = layer(x).clone()
+    b = layer(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_forward_host_matches_device(small_layers):
+    W, dev, layer = small_layers["cfg1"]
+    xb = synth.make_x(1024, 8, seed=9)
+    y_host = layer.forward_host(xb)
+    y_dev = layer(torch.from_numpy(xb.view(np.int16)).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(y_host, y_dev.view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def test_planted_router_ties(small_layers):
+    """Identical router rows give identical logits: ties must go to the lower expert id, as in the
+    reference's partial_sort comparator (stbl/model.cu:444-449)."""
+    W, dev, _ = small_layers["cfg1"]
+    cfg = CFG1
+    W2 = dict(W)
+    rw = W["router_w"].copy()
+    rw[5] = rw[2]
+    rw[9] = rw[2]
+    rw[13] = rw[1]
+    W2["router_w"] = rw
+    W2["router_bias"] = np.zeros_like(W["router_bias"])
+    dev2 = dict(dev)
+    dev2["router_w"] = torch.from_numpy(rw).cuda()
+    dev2["router_bias"] = torch.zeros_like(dev["router_bias"])
+    layer = MoELayer(cfg, dev2, max_tokens=16)
+    run_and_check(cfg, layer, dev2, W2, synth.make_x(1024, 16, seed=11))
+    layer.close()
+
+
+@pytest.fixture(scope="module")
+def cfg2_layer():
+    dev = synth.device_layer(CFG2)
+    layer = MoELayer(CFG2, dev, max_tokens=16)
+    yield dev, layer
+    layer.close()
+    del dev
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("T", [1, 4, 16])
+def test_full_size_fp8_layer(cfg2_layer, T):
+    dev, layer = cfg2_layer
+    run_and_check(CFG2, layer, dev, None, synth.make_x(CFG2.hidden, T, seed=200 + T))
+
+
+def test_full_size_fp8_device_quantization_matches_oracle(cfg2_layer):
+    """The GPU-side synthetic quantizer (torch on the device) agrees byte for byte with the oracle's."""
+    dev, _ = cfg2_layer
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234)
+    w = torch.randn(256, 1024, generator=g, device="cuda") * 0.02
+    c, s = synth.quant_fp8_b128(w)
+    oc, os_ = O.quant_fp8_b128(w.cpu().numpy())
+    assert np.array_equal(c.cpu().numpy(), oc) and np.array_equal(s.cpu().numpy(), os_)
+
+
+@pytest.fixture(scope="module")
+def cfg3_layer():
+    dev = synth.device_layer(CFG3)
+    layer = MoELayer(CFG3, dev, max_tokens=64)
+    yield dev, layer
+    layer.close()
+    del dev
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_full_size_fp4_layer(cfg3_layer, T):
+    dev, layer = cfg3_layer
+    run_and_check(CFG3, layer, dev, None, synth.make_x(CFG3.hidden, T, seed=300 + T))
