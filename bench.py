@@ -184,11 +184,23 @@ def main():
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
                       for i in range(n_steps)]).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
-    def distinct_now():
-        r = layer.last_route()
-        return len(np.unique(r["idx"]))
+    def distinct_of(x):
+        """Distinct experts the layer routes x to (untimed pass; reads the routing back)."""
+        layer(x)
+        return len(np.unique(layer.last_route()["idx"]))
+
+    def timed_steps(inputs):
+        """Device time of each call, L2 flushed before each; nothing synchronises inside the loop, so
+        the host runs ahead and the GPU executes flush, layer, flush, layer ... back to back."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in inputs]
+        for x, (a, b) in zip(inputs, evs):
+            flush.zero_()
+            a.record()
+            layer(x)
+            b.record()
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
 
     for i in range(args.warmup):
         layer(xs[i])
@@ -196,25 +208,19 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    sampler = ClockSampler(local)
     sampler.start()
+    layer.timing()
     layer.set_timing(True)
-    distinct = []
-    for i in range(args.steps):
-        flush.zero_()
-        ev[i][0].record()
-        layer(xs[args.warmup + i])
-        ev[i][1].record()
-        distinct.append(distinct_now())
-    torch.cuda.synchronize()
+    step_ms = timed_steps([xs[args.warmup + i] for i in range(args.steps)])
     layer.set_timing(False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    total_s = sum(step_ms) / 1e3
     kt = layer.timing()
+    distinct = [distinct_of(xs[args.warmup + i]) for i in range(args.steps)]
+    total_s = sum(step_ms) / 1e3
     t = torch.tensor([total_s], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -247,28 +253,28 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = world * T * args.steps / float(t.item())
 
-    # batch-size sweep of configs[1] (1, 4, 16 tokens), device time, rank 0 report
+    # batch-size sweep of configs[1] (1, 4, 16 tokens): device time per call and per kernel
     sweep = []
     if not args.no_sweep:
         for Ts in (1, 4, 16):
-            lay = layer if Ts <= layer.max_tokens else None
             xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
                    for i in range(23)]
             for i in range(3):
-                lay(xs2[i])
-            ms, dd = [], []
-            for i in range(3, 23):
-                flush.zero_()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record()
-                lay(xs2[i])
-                b.record()
-                dd.append(distinct_now())
-                ms.append(a.elapsed_time(b))
+                layer(xs2[i])
+            torch.cuda.synchronize()
+            layer.timing()
+            base = layer.timing()
+            layer.set_timing(True)
+            ms = timed_steps(xs2[3:])
+            layer.set_timing(False)
+            k2 = layer.timing()
+            n2 = max(k2["calls"] - base["calls"], 1)
+            dd = [distinct_of(x) for x in xs2[3:]]
             mean_ms = float(np.mean(ms))
             gbs = np.mean([layer_bytes(cfg, d, Ts) for d in dd]) / (mean_ms / 1e3) / 1e9
             sweep.append({"tokens": Ts, "tokens_per_s": Ts / (mean_ms / 1e3), "ms_per_call": mean_ms,
-                          "distinct_experts": float(np.mean(dd)), "hbm_gbs": gbs, "hbm_frac_of_measured": gbs / peak})
+                          "distinct_experts": float(np.mean(dd)), "hbm_gbs": gbs, "hbm_frac_of_measured": gbs / peak,
+                          "kernel_ms": {k: (k2[k] - base[k]) / n2 * 1e3 for k in ("router", "up", "down")}})
     status = layer.status()
 
     cpu = None

@@ -49,7 +49,6 @@ struct RouterParams {
     float route_scale;
     int ksplit;
     int has_shared;
-    float *partial;          // [ksplit][T][E]
     float *scores;           // [T][E]
     int *idx;                // [T][topk]
     float *wts;              // [T][topk]
@@ -66,14 +65,14 @@ struct RouterParams {
     uint8_t *xq_b;
     float *xs_b;
     int blk_b, pow2_b;
-    int *zero;               // counters cleared each call
-    int n_zero;
     unsigned int *done;      // last-CTA ticket
     uint32_t *status;
 };
 
 // One launch of the expert kernels covers chunks [chunk_begin, chunk_end); chunk_end < 0 means
-// "up to n_chunks[0]" (known only on the device).
+// "up to n_chunks[0]" (known only on the device).  Each CTA takes one contiguous range of the
+// launch's work items (chunk-major, tile-minor), so a CTA streams long contiguous runs of one
+// expert's rows and reloads its activations only when the chunk changes.
 struct ExpertParams {
     const ExpertPtrs *experts;
     const Chunk *chunks;
@@ -82,25 +81,27 @@ struct ExpertParams {
     int T, topk, E, H, I;
     const int *perm;
     const float *wts;
-    // up: input x codes [T][H] + scales [T][xs_stride]; down: hq [pos][I] + hs [pos][xs_stride]
+    // up: x codes [T][H] + scales [T][xs_stride] from the router kernel
     const uint8_t *xq;
     const float *xs;
-    int act_blk, act_pow2;
-    int xs_stride;           // scale floats per activation row (K / 32: room for per-32 scales)
-    int hs_stride;           // scale floats per hs row (I / 32)
+    int xs_stride;           // scale floats per x row (H / 32: room for per-32 scales)
+    int act_blk, act_pow2;   // act_quant rule of this launch's weight format
     float swiglu_limit;
-    // up outputs
-    uint16_t *h;             // [pos][I] bf16
-    uint8_t *hq;             // [pos][I]
-    float *hs;               // [pos][I / 32]
-    int *hcnt;               // [chunk][ceil(I / 128)] rows done
-    // down outputs
+    uint16_t *h;             // [pos][I] bf16: written by up, read (and re-quantized in registers) by down
     uint16_t *eo;            // [T * topk][H] bf16, routed outputs in (token, slot) order
     uint16_t *sh;            // [T][H] bf16, shared-expert outputs
-    uint16_t *y;             // [T][H] bf16, the layer output
-    int *ccnt;               // [T][ceil(H / 128)] rows done
     int has_shared;
     uint32_t *status;
 };
+
+struct CombineParams {
+    const uint16_t *eo;
+    const uint16_t *sh;
+    uint16_t *y;
+    int T, topk, H, has_shared;
+};
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace stbl

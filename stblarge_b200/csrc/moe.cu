@@ -1,8 +1,9 @@
 // Layer object and C ABI of the MoE decode path (include/stbl_moe.h).
 //
-// One layer call is three kernel launches on the caller's stream (four or five when the routed and
-// shared experts have different formats): router (+ selection + dispatch), expert up (+ SwiGLU +
-// h re-quantization), expert down (+ ordered combine).  No host synchronisation inside a call.
+// One layer call is four kernel launches on the caller's stream (six when the routed and shared
+// experts have different formats): router (+ selection + dispatch), expert up (+ SwiGLU), expert
+// down (+ act_quant of h), combine.  They are chained with programmatic dependent launch, so each
+// kernel's CTAs start while the previous kernel drains.  No host synchronisation inside a call.
 #include <stdio.h>
 #include <string.h>
 
@@ -16,6 +17,7 @@
 namespace stbl {
 __global__ void router_kernel(RouterParams p);
 const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
+const void *combine_kernel_ptr();                 // experts.cu
 }  // namespace stbl
 
 using namespace stbl;
@@ -63,20 +65,17 @@ const void *expert_fn(int fmt, bool up) { return expert_kernel_ptr(fmt, up); }
 struct stbl_moe {
     stbl_moe_desc d{};
     int E = 0, H = 0, I = 0, K = 0, Tmax = 0, ksplit = 1, sms = 0, has_shared = 0;
-    int nG_H = 0, nG_I = 0;
     void *ws = nullptr;
     size_t ws_bytes = 0;
-    float *partial = nullptr, *scores = nullptr, *wts = nullptr, *xs_a = nullptr, *xs_b = nullptr, *hs = nullptr;
+    float *scores = nullptr, *wts = nullptr, *xs_a = nullptr, *xs_b = nullptr;
     int *idx = nullptr, *counts = nullptr, *offsets = nullptr, *perm = nullptr, *n_chunks = nullptr;
-    int *hcnt = nullptr, *ccnt = nullptr;
     Chunk *chunks = nullptr;
-    uint8_t *xq_a = nullptr, *xq_b = nullptr, *hq = nullptr;
+    uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     unsigned int *done = nullptr;
     uint32_t *status = nullptr;
     ExpertPtrs *experts = nullptr;
     std::vector<ExpertPtrs> host_experts;
-    int n_zero = 0;
     int router_grid = 0, router_smem = 0;
     KernelCfg up_r, up_s, down_r, down_s;
     int last_T = 0;
@@ -108,13 +107,13 @@ KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
     const int rb = fmt == STBL_FMT_FP8_B128 ? K : K / 2;
     int stage = nmat * RI * rb + (fmt == STBL_FMT_MXFP4 ? nmat * RI * (K / 32) : 0);
     stage = (stage + 127) & ~127;
-    const int extra = 2 * 8 * 8 + 64 * 32 * 4 + 64 * 4 + 128;
+    const int extra = 2 * 8 * 8 + 2 * 1024 * 4 + 128;
     int nst = (max_smem - extra) / stage;
     if (nst > 8) nst = 8;
     if (nst < 2) throw std::runtime_error("expert weight tile does not fit twice in shared memory");
     c.stage_bytes = stage;
     c.nst = nst;
-    c.smem = nst * stage + 2 * nst * 8 + 64 * 32 * 4 + 64 * 4;
+    c.smem = nst * stage + 2 * nst * 8 + 2 * 1024 * 4;
     CK(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
     return c;
 }
@@ -140,7 +139,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     m->E = E, m->H = H, m->I = I, m->K = K, m->Tmax = d->max_tokens;
     m->ksplit = router_ksplit(H);
     m->has_shared = d->shared_fmt != STBL_FMT_NONE;
-    m->nG_H = (H + 127) / 128, m->nG_I = (I + 127) / 128;
 
     // expert table (entry E: shared expert)
     m->host_experts.assign(E + 1, ExpertPtrs{});
@@ -170,7 +168,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     auto layout = [&](char *base) {
         char *p = base;
         m->experts = carve<ExpertPtrs>(p, E + 1);
-        m->partial = carve<float>(p, (size_t)m->ksplit * T * E);
         m->scores = carve<float>(p, (size_t)T * E);
         m->idx = carve<int>(p, (size_t)T * K);
         m->wts = carve<float>(p, (size_t)T * K);
@@ -184,10 +181,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->xq_b = carve<uint8_t>(p, (size_t)T * H);
         m->xs_b = carve<float>(p, (size_t)T * (H / 32));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
-        m->hq = carve<uint8_t>(p, (size_t)npos * I);
-        m->hs = carve<float>(p, (size_t)npos * (I / 32));
-        m->hcnt = carve<int>(p, (size_t)npos * m->nG_I + (size_t)T * m->nG_H);  // hcnt then ccnt: one zeroed range
-        m->ccnt = m->hcnt + (size_t)npos * m->nG_I;
         m->eo = carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
@@ -200,14 +193,14 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     CK(cudaMalloc(&m->ws, m->ws_bytes));
     CK(cudaMemset(m->ws, 0, m->ws_bytes));
     layout(static_cast<char *>(m->ws));
-    m->n_zero = npos * m->nG_I + T * m->nG_H;
     CK(cudaMemcpy(m->experts, m->host_experts.data(), sizeof(ExpertPtrs) * (E + 1), cudaMemcpyHostToDevice));
 
     int dev = 0, max_smem = 0;
     CK(cudaGetDevice(&dev));
     CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    m->router_grid = (E * m->ksplit + kRouterThreads / 32 - 1) / (kRouterThreads / 32);
+    const int epc = (kRouterThreads / 32) / m->ksplit;  // experts per router CTA
+    m->router_grid = (E + epc - 1) / epc;
     const int TW = (T + 31) / 32;
     m->router_smem = 2 * (kRouterThreads / 32) * E * 4 + T * K * 4 + 4 * E * 4 + E * TW * 4;
     CK(cudaFuncSetAttribute((const void *)router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m->router_smem));
@@ -228,29 +221,39 @@ ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
     p.perm = m->perm;
     p.wts = m->wts;
     const bool routed_buf = fmt == m->d.routed_fmt;
-    if (up) {
-        p.xq = routed_buf ? m->xq_a : m->xq_b;
-        p.xs = routed_buf ? m->xs_a : m->xs_b;
-        p.xs_stride = m->H / 32;
-    } else {
-        p.xq = m->hq;
-        p.xs = m->hs;
-        p.xs_stride = m->I / 32;
-    }
+    (void)up;
+    p.xq = routed_buf ? m->xq_a : m->xq_b;
+    p.xs = routed_buf ? m->xs_a : m->xs_b;
+    p.xs_stride = m->H / 32;
     p.act_blk = act_blk_of(fmt);
     p.act_pow2 = act_pow2_of(fmt);
-    p.hs_stride = m->I / 32;
     p.swiglu_limit = m->d.swiglu_limit;
-    p.h = m->h, p.hq = m->hq, p.hs = m->hs, p.hcnt = m->hcnt;
-    p.eo = m->eo, p.sh = m->sh, p.ccnt = m->ccnt;
+    p.h = m->h;
+    p.eo = m->eo, p.sh = m->sh;
     p.has_shared = m->has_shared;
     p.status = m->status;
     return p;
 }
 
+// Launch with programmatic dependent launch: the kernel may start while the previous one in the
+// stream drains (its CTAs block in griddepcontrol.wait until that grid has completed).
+void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelExC(&cfg, fn, args));
+}
+
 void launch_expert(const KernelCfg &c, ExpertParams p, int grid, cudaStream_t st) {
     void *args[] = {&p, const_cast<int *>(&c.stage_bytes), const_cast<int *>(&c.nst)};
-    CK(cudaLaunchKernel(c.fn, dim3(grid), dim3(kExpertThreads), args, c.smem, st));
+    launch_pdl(c.fn, dim3(grid), dim3(kExpertThreads), args, c.smem, st);
 }
 
 TimedCall take_events(stbl_moe *m);
@@ -269,25 +272,23 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     r.W = m->d.router_w, r.bias = m->d.router_bias, r.x = static_cast<const uint16_t *>(x);
     r.T = T, r.E = m->E, r.H = m->H, r.topk = m->K, r.n_groups = m->d.n_groups, r.topk_groups = m->d.topk_groups;
     r.score_fn = m->d.score_fn, r.route_scale = m->d.route_scale, r.ksplit = m->ksplit, r.has_shared = m->has_shared;
-    r.partial = m->partial, r.scores = m->scores, r.idx = m->idx, r.wts = m->wts;
+    r.scores = m->scores, r.idx = m->idx, r.wts = m->wts;
     r.counts = m->counts, r.offsets = m->offsets, r.perm = m->perm, r.chunks = m->chunks, r.n_chunks = m->n_chunks;
     const int fr = m->d.routed_fmt, fs = m->has_shared ? m->d.shared_fmt : fr;
     r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
     if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
-    r.zero = m->hcnt, r.n_zero = m->n_zero, r.done = m->done, r.status = m->status;
+    r.done = m->done, r.status = m->status;
     void *rargs[] = {&r};
-    CK(cudaLaunchKernel((const void *)router_kernel, dim3(m->router_grid), dim3(kRouterThreads), rargs, m->router_smem, st));
+    launch_pdl((const void *)router_kernel, dim3(m->router_grid), dim3(kRouterThreads), rargs, m->router_smem, st);
     if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
     int launches = 1;
 
     const int grid = m->sms;
     ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
-    pd.y = pu.y = static_cast<uint16_t *>(y);
     if (m->has_shared && fs != fr) {
         const int ns = (T + kNT - 1) / kNT;
         ExpertParams su = expert_params(m, T, fs, true), sd = expert_params(m, T, fs, false);
-        su.y = sd.y = static_cast<uint16_t *>(y);
         su.chunk_begin = 0, su.chunk_end = ns;
         sd.chunk_begin = 0, sd.chunk_end = ns;
         pu.chunk_begin = ns, pu.chunk_end = -1;
@@ -306,6 +307,11 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         launch_expert(m->down_r, pd, grid, st);
         launches += 2;
     }
+    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
+    void *cargs[] = {&cp};
+    const int cthreads = T * (m->H / 8);
+    launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
+    launches += 1;
     if (m->timing) {
         CK(cudaEventRecord(tc.ev[3], st));
         m->pending.push_back(tc);
@@ -439,7 +445,6 @@ int stbl_moe_status(stbl_moe *m, uint32_t *status) {
         uint32_t s = 0;
         CK(cudaMemcpy(&s, m->status, 4, cudaMemcpyDeviceToHost));
         CK(cudaMemset(m->status, 0, 4));
-        if (s) CK(cudaMemset(m->hcnt, 0, sizeof(int) * m->n_zero));
         *status = s;
         return 0;
     } catch (const std::exception &e) {

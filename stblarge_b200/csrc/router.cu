@@ -1,9 +1,9 @@
 // Router, top-k selection and bucketed dispatch of the MoE layer: one launch.
 //
-// Phase A (every CTA): router logits as ksplit partial sums per (expert, hidden slice), one warp per
-// unit, all tokens at once; FP8 activation quantization of x for the expert kernels; clearing of the
-// per-call completion counters.  Phase B (the last CTA to finish phase A, by an atomic ticket):
-// scores, group-limited top-k, routing weights, and the bucketed permutation + chunk table.
+// Phase A (every CTA): router logits of a few experts (one warp per hidden slice, the slices combined
+// in slice order in shared memory) and their scores, for all tokens at once; FP8 activation
+// quantization of x for the expert kernels.  Phase B (the last CTA to finish phase A, by an atomic
+// ticket): group-limited top-k, routing weights, and the bucketed permutation + chunk table.
 //
 // Replaces the reference's router GEMV, score kernel, blocking device->host copy and host
 // partial_sort (stbl/model.cu:430-452, stbl/kernels.cu:206-214, 437-442): nothing leaves the GPU.
@@ -13,41 +13,60 @@
 
 namespace stbl {
 
+// ---- phase B helpers ------------------------------------------------------------------------------
+
+__device__ __forceinline__ float router_score(float logit, int fn) {
+    // double evaluation, one rounding to fp32: bit-identical to the CPU oracle's
+    if (fn == kScoreSigmoid) return (float)(1.0 / (1.0 + exp(-(double)logit)));
+    const double sp = logit > 20.f ? (double)logit : log1p(exp((double)logit));
+    return (float)sqrt(sp);
+}
+
+__device__ __forceinline__ bool beats(float va, int a, float vb, int b) { return va > vb || (va == vb && a < b); }
+
 // ---- phase A --------------------------------------------------------------------------------------
 
-// Lane l of the warp takes hidden positions base + 128 i + 4 l + j (i ascending, j = 0..3), by fused
-// multiply-add, then the 32 lane sums are added by an xor butterfly.  oracle/moe_oracle.c restates
-// exactly this order, so the logits agree bit for bit.
-__device__ void logits_unit(const RouterParams &p, int e, int ks, int lane) {
+// One warp computes the slice ks of expert e's logits for tokens t0 .. t0+nt-1: lane l takes hidden
+// positions base + 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, then the 32 lane
+// sums are added by an xor butterfly.  oracle/moe_oracle.c restates exactly this order, so the logits
+// agree bit for bit.  The weight loads of a slice are issued before any use (7 per lane in flight).
+__device__ __forceinline__ void logits_slice(const RouterParams &p, int e, int ks, int t0, int nt, int lane,
+                                             float *out /* [8] per token, lane 0 */) {
     const int slice = p.H / p.ksplit;
     const float *w = p.W + (size_t)e * p.H + (size_t)ks * slice;
     const uint16_t *x = p.x + (size_t)ks * slice;
-    for (int t0 = 0; t0 < p.T; t0 += 8) {
-        const int nt = min(8, p.T - t0);
-        float acc[8];
+    float acc[8];
 #pragma unroll
-        for (int t = 0; t < 8; t++) acc[t] = 0.f;
-        for (int i = 0; i < slice / 128; i++) {
-            const int k = 128 * i + 4 * lane;
-            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(w + k));
+    for (int t = 0; t < 8; t++) acc[t] = 0.f;
+    const int n_it = slice / 128;
+    for (int i0 = 0; i0 < n_it; i0 += 7) {
+        float4 w4[7];
 #pragma unroll
-            for (int t = 0; t < 8; t++) {
-                if (t < nt) {
-                    const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)(t0 + t) * p.H + k));
-                    acc[t] = fmaf(w4.x, __uint_as_float(xv.x << 16), acc[t]);
-                    acc[t] = fmaf(w4.y, __uint_as_float(xv.x & 0xffff0000u), acc[t]);
-                    acc[t] = fmaf(w4.z, __uint_as_float(xv.y << 16), acc[t]);
-                    acc[t] = fmaf(w4.w, __uint_as_float(xv.y & 0xffff0000u), acc[t]);
+        for (int u = 0; u < 7; u++)
+            if (i0 + u < n_it) w4[u] = __ldg(reinterpret_cast<const float4 *>(w + 128 * (i0 + u) + 4 * lane));
+#pragma unroll
+        for (int u = 0; u < 7; u++) {
+            if (i0 + u < n_it) {
+                const int k = 128 * (i0 + u) + 4 * lane;
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    if (t < nt) {
+                        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)(t0 + t) * p.H + k));
+                        acc[t] = fmaf(w4[u].x, __uint_as_float(xv.x << 16), acc[t]);
+                        acc[t] = fmaf(w4[u].y, __uint_as_float(xv.x & 0xffff0000u), acc[t]);
+                        acc[t] = fmaf(w4[u].z, __uint_as_float(xv.y << 16), acc[t]);
+                        acc[t] = fmaf(w4[u].w, __uint_as_float(xv.y & 0xffff0000u), acc[t]);
+                    }
                 }
             }
         }
+    }
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            float v = acc[t];
+    for (int t = 0; t < 8; t++) {
+        float v = acc[t];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && t < nt) p.partial[((size_t)ks * p.T + t0 + t) * p.E + e] = v;
-        }
+        for (int o = 16; o > 0; o >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, o);
+        out[t] = v;
     }
 }
 
@@ -72,17 +91,6 @@ __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq,
     *reinterpret_cast<uint32_t *>(xq + (size_t)t * H + k) = codes;
     if ((k % blk) == 0) xs[(size_t)t * (H / 32) + k / blk] = s;
 }
-
-// ---- phase B helpers ------------------------------------------------------------------------------
-
-__device__ __forceinline__ float router_score(float logit, int fn) {
-    // double evaluation, one rounding to fp32: bit-identical to the CPU oracle's
-    if (fn == kScoreSigmoid) return (float)(1.0 / (1.0 + exp(-(double)logit)));
-    const double sp = logit > 20.f ? (double)logit : log1p(exp((double)logit));
-    return (float)sqrt(sp);
-}
-
-__device__ __forceinline__ bool beats(float va, int a, float vb, int b) { return va > vb || (va == vb && a < b); }
 
 // exclusive scan over n <= 2 * kRouterThreads values in smem (in place); returns the total
 __device__ int block_exclusive_scan(int *v, int n, int *warp_tot) {
@@ -123,15 +131,39 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
     const int nwarps_grid = gridDim.x * (kRouterThreads / 32);
     const int gwarp = blockIdx.x * (kRouterThreads / 32) + warp;
 
-    // phase A: logits partials, activation quantization, counter clearing
-    for (int u = gwarp; u < p.E * p.ksplit; u += nwarps_grid) logits_unit(p, u / p.ksplit, u % p.ksplit, lane);
+    pdl_wait();  // x may come from the kernel before this one
+    pdl_launch_dependents();
+
+    // phase A: logits of experts_per_cta experts (ksplit warps each, slices combined in slice order
+    // through shared memory), their scores, activation quantization of x
+    __shared__ float part[kRouterThreads / 32][8];
+    const int epc = (kRouterThreads / 32) / p.ksplit;  // experts per CTA
+    const int e_loc = warp / p.ksplit, ks = warp % p.ksplit;
+    const int e = blockIdx.x * epc + e_loc;
+    for (int t0 = 0; t0 < p.T; t0 += 8) {
+        const int nt = min(8, p.T - t0);
+        float o[8];
+        if (e < p.E) logits_slice(p, e, ks, t0, nt, lane, o);
+        if (lane == 0 && e < p.E)
+#pragma unroll
+            for (int t = 0; t < 8; t++) part[warp][t] = o[t];
+        __syncthreads();
+        if (tid < epc * nt) {
+            const int el = tid / nt, t = tid % nt, ee = blockIdx.x * epc + el;
+            if (ee < p.E) {
+                float logit = part[el * p.ksplit][t];
+                for (int k2 = 1; k2 < p.ksplit; k2++) logit = logit + part[el * p.ksplit + k2][t];
+                p.scores[(size_t)(t0 + t) * p.E + ee] = router_score(logit, p.score_fn);
+            }
+        }
+        __syncthreads();
+    }
     const int groups = p.T * (p.H / 128);
     for (int u = gwarp; u < groups; u += nwarps_grid) {
         quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane);
         if (p.xq_b != p.xq_a)
             quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane);
     }
-    for (int i = blockIdx.x * kRouterThreads + tid; i < p.n_zero; i += gridDim.x * kRouterThreads) p.zero[i] = 0;
 
     // last-CTA ticket
     __shared__ int is_last;
@@ -169,13 +201,10 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
             const int e = lane + 32 * j;
             bv[j] = 0.f;
             if (j < EJ && e < E) {
-                float logit = __ldcg(p.partial + (size_t)t * E + e);
-                for (int ks = 1; ks < p.ksplit; ks++) logit = logit + __ldcg(p.partial + ((size_t)ks * T + t) * E + e);
-                const float s = router_score(logit, p.score_fn);
-                const float b = s + p.bias[e];
+                const float s = __ldcg(p.scores + (size_t)t * E + e);
+                const float b = s + __ldg(p.bias + e);
                 wb[e] = b;
                 ws[e] = s;
-                p.scores[(size_t)t * E + e] = s;
                 bv[j] = b;
                 has |= 1u << j;
             }
