@@ -49,6 +49,7 @@ struct RouterParams {
     float route_scale;
     int ksplit;
     int has_shared;
+    int nt_routed, nt_shared;  // tokens per chunk of a routed / the shared expert
     float *scores;           // [T][E]
     int *idx;                // [T][topk]
     float *wts;              // [T][topk]

@@ -13,11 +13,14 @@
 
 #include "../../include/stbl_moe.h"
 #include "layer.cuh"
+#include "tc_params.cuh"
 
 namespace stbl {
 __global__ void router_kernel(RouterParams p);
 const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
 const void *combine_kernel_ptr();                 // experts.cu
+const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
+int expert_tc_smem_bytes(bool up, int H, int I, int nst);
 }  // namespace stbl
 
 using namespace stbl;
@@ -77,7 +80,15 @@ struct stbl_moe {
     ExpertPtrs *experts = nullptr;
     std::vector<ExpertPtrs> host_experts;
     int router_grid = 0, router_smem = 0;
-    KernelCfg up_r, up_s, down_r, down_s;
+    KernelCfg up_r, down_r;           // CUDA-core kernels (MXFP4 routed experts)
+    // tensor-core kernels (FP8 experts): tensor maps, launch shape
+    TcMaps tc_up{}, tc_down{};
+    int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
+    bool routed_tc = false;           // routed experts on the tensor-core kernels
+    uint8_t *hq = nullptr;
+    float *hs = nullptr;
+    int *hcnt = nullptr, *ccnt = nullptr;
+    size_t cnt_bytes = 0;
     int last_T = 0;
     uint64_t calls = 0, tokens = 0;
     int launches = 0;
@@ -97,6 +108,39 @@ T *carve(char *&p, size_t n) {
     p += (n * sizeof(T) + 255) & ~(size_t)255;
     return r;
 }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !ptr) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 3-D tensor map over `experts` matrices of [rows][K] e4m3 codes (expert stride in bytes), read in
+// tiles of 128 bytes x box_rows rows with the 128-byte swizzle the MMA descriptors expect
+CUtensorMap weight_map(const void *base, int K, int rows, int experts, long long estride, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)experts};
+    const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)estride};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an expert weight tensor");
+    return m;
+}
+
+void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st);
 
 KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
     KernelCfg c;
@@ -181,6 +225,10 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->xq_b = carve<uint8_t>(p, (size_t)T * H);
         m->xs_b = carve<float>(p, (size_t)T * (H / 32));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
+        m->hq = carve<uint8_t>(p, (size_t)npos * I);
+        m->hs = carve<float>(p, (size_t)npos * (I / 128));
+        m->hcnt = carve<int>(p, (size_t)npos * (I / 128) + (size_t)T * (H / 128));  // hcnt then ccnt
+        m->ccnt = m->hcnt + (size_t)npos * (I / 128);
         m->eo = carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
@@ -189,6 +237,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->status = carve<uint32_t>(p, 4);
         return (size_t)(p - base);
     };
+    m->cnt_bytes = sizeof(int) * ((size_t)npos * (I / 128) + (size_t)T * (H / 128));
     m->ws_bytes = layout(nullptr);
     CK(cudaMalloc(&m->ws, m->ws_bytes));
     CK(cudaMemset(m->ws, 0, m->ws_bytes));
@@ -204,12 +253,84 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     const int TW = (T + 31) / 32;
     m->router_smem = 2 * (kRouterThreads / 32) * E * 4 + T * K * 4 + 4 * E * 4 + E * TW * 4;
     CK(cudaFuncSetAttribute((const void *)router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m->router_smem));
-    m->up_r = make_cfg(d->routed_fmt, true, H, I, max_smem);
-    m->down_r = make_cfg(d->routed_fmt, false, H, I, max_smem);
-    if (m->has_shared && d->shared_fmt != d->routed_fmt) {
-        m->up_s = make_cfg(d->shared_fmt, true, H, I, max_smem);
-        m->down_s = make_cfg(d->shared_fmt, false, H, I, max_smem);
+    m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
+    if (!m->routed_tc) {
+        m->up_r = make_cfg(d->routed_fmt, true, H, I, max_smem);
+        m->down_r = make_cfg(d->routed_fmt, false, H, I, max_smem);
     }
+    if (m->routed_tc || m->has_shared) {
+        if (H % 128 || I % 128) throw std::runtime_error("FP8 experts need hidden and inter multiples of 128");
+        // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
+        const long long wst[3] = {
+            d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H,
+            d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H,
+            d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I};
+        if (m->routed_tc) {
+            m->tc_up.w[0] = weight_map(d->routed_w[0], H, I, E, wst[0], 64);
+            m->tc_up.w[1] = weight_map(d->routed_w[1], H, I, E, wst[1], 64);
+            m->tc_down.w[0] = weight_map(d->routed_w[2], I, H, E, wst[2], 128);
+            m->tc_down.w[1] = m->tc_down.w[0];
+        }
+        if (m->has_shared) {
+            m->tc_up.s[0] = weight_map(d->shared_w[0], H, I, 1, (long long)I * H, 64);
+            m->tc_up.s[1] = weight_map(d->shared_w[1], H, I, 1, (long long)I * H, 64);
+            m->tc_down.s[0] = weight_map(d->shared_w[2], I, H, 1, (long long)H * I, 128);
+            m->tc_down.s[1] = m->tc_down.s[0];
+        }
+        if (!m->routed_tc) m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
+        if (!m->has_shared) m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
+        auto pick = [&](bool up, int &nst, int &smem) {
+            for (nst = 8; nst >= 2; nst--)
+                if (expert_tc_smem_bytes(up, H, I, nst) + 256 <= max_smem) break;
+            if (nst < 2) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
+            smem = expert_tc_smem_bytes(up, H, I, nst);
+            CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        };
+        pick(true, m->tc_nst_up, m->tc_smem_up);
+        pick(false, m->tc_nst_down, m->tc_smem_down);
+    }
+}
+
+TcParams tc_params(stbl_moe *m, int T, bool up) {
+    TcParams p{};
+    p.chunks = m->chunks;
+    p.n_chunks = m->n_chunks;
+    p.T = T, p.topk = m->K, p.E = m->E, p.H = m->H, p.I = m->I;
+    p.perm = m->perm;
+    p.wts = m->wts;
+    const stbl_moe_desc &d = m->d;
+    if (up) {
+        // x codes for the FP8 (per-128) rule: the routed buffer when the routed experts are FP8, else
+        // the shared expert's
+        p.act_q = m->routed_tc ? m->xq_a : m->xq_b;
+        p.act_s = m->routed_tc ? m->xs_a : m->xs_b;
+        p.act_s_stride = m->H / 32;
+    } else {
+        p.act_q = m->hq;
+        p.act_s = m->hs;
+        p.act_s_stride = m->I / 128;
+    }
+    const int I = m->I, H = m->H;
+    const int mats[2] = {up ? 0 : 2, up ? 1 : 2};
+    for (int i = 0; i < 2; i++) {
+        const int mt = mats[i];
+        p.w_scale[i] = m->routed_tc ? static_cast<const float *>(d.routed_s[mt]) : nullptr;
+        p.s_scale[i] = m->has_shared ? static_cast<const float *>(d.shared_s[mt]) : nullptr;
+    }
+    const int rows = up ? I : H, K = up ? H : I;
+    const long long sst = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]]
+                                                       : 4LL * ((rows + 127) / 128) * ((K + 127) / 128);
+    p.w_scale_stride = sst / 4;
+    p.h = m->h, p.hq = m->hq, p.hs = m->hs, p.hcnt = m->hcnt;
+    p.eo = m->eo, p.sh = m->sh, p.ccnt = m->ccnt;
+    p.has_shared = m->has_shared;
+    p.status = m->status;
+    return p;
+}
+
+void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
+    void *args[] = {up ? &m->tc_up : &m->tc_down, &p, up ? &m->tc_nst_up : &m->tc_nst_down};
+    launch_pdl(expert_tc_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc_smem_up : m->tc_smem_down, st);
 }
 
 ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
@@ -278,6 +399,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
     if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
+    r.nt_routed = m->routed_tc ? 16 : kNT;
+    r.nt_shared = 16;
     r.done = m->done, r.status = m->status;
     void *rargs[] = {&r};
     launch_pdl((const void *)router_kernel, dim3(m->router_grid), dim3(kRouterThreads), rargs, m->router_smem, st);
@@ -285,33 +408,46 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     int launches = 1;
 
     const int grid = m->sms;
-    ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
-    if (m->has_shared && fs != fr) {
-        const int ns = (T + kNT - 1) / kNT;
-        ExpertParams su = expert_params(m, T, fs, true), sd = expert_params(m, T, fs, false);
-        su.chunk_begin = 0, su.chunk_end = ns;
-        sd.chunk_begin = 0, sd.chunk_end = ns;
-        pu.chunk_begin = ns, pu.chunk_end = -1;
-        pd.chunk_begin = ns, pd.chunk_end = -1;
-        launch_expert(m->up_s, su, grid, st);
-        launch_expert(m->up_r, pu, grid, st);
-        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
-        launch_expert(m->down_s, sd, grid, st);
-        launch_expert(m->down_r, pd, grid, st);
-        launches += 4;
-    } else {
+    if (m->routed_tc) {
+        // every expert on the tensor cores; the down kernel also writes y (ordered combine)
+        TcParams pu = tc_params(m, T, true), pd = tc_params(m, T, false);
         pu.chunk_begin = pd.chunk_begin = 0;
         pu.chunk_end = pd.chunk_end = -1;
+        pd.y = static_cast<uint16_t *>(y);
+        pd.fuse_combine = 1;
+        launch_tc(m, true, pu, st);
+        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launch_tc(m, false, pd, st);
+        launches += 2;
+    } else {
+        // MXFP4 routed experts on the CUDA-core kernels, the FP8 shared expert on the tensor cores,
+        // then the combine kernel
+        const int ns = m->has_shared ? (T + 15) / 16 : 0;
+        ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
+        pu.chunk_begin = pd.chunk_begin = ns;
+        pu.chunk_end = pd.chunk_end = -1;
+        if (ns) {
+            TcParams su = tc_params(m, T, true);
+            su.chunk_begin = 0, su.chunk_end = ns;
+            launch_tc(m, true, su, st);
+            launches++;
+        }
         launch_expert(m->up_r, pu, grid, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        if (ns) {
+            TcParams sd = tc_params(m, T, false);
+            sd.chunk_begin = 0, sd.chunk_end = ns;
+            launch_tc(m, false, sd, st);
+            launches++;
+        }
         launch_expert(m->down_r, pd, grid, st);
         launches += 2;
+        CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
+        void *cargs[] = {&cp};
+        const int cthreads = T * (m->H / 8);
+        launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
+        launches += 1;
     }
-    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
-    void *cargs[] = {&cp};
-    const int cthreads = T * (m->H / 8);
-    launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
-    launches += 1;
     if (m->timing) {
         CK(cudaEventRecord(tc.ev[3], st));
         m->pending.push_back(tc);
@@ -445,6 +581,7 @@ int stbl_moe_status(stbl_moe *m, uint32_t *status) {
         uint32_t s = 0;
         CK(cudaMemcpy(&s, m->status, 4, cudaMemcpyDeviceToHost));
         CK(cudaMemset(m->status, 0, 4));
+        if (s) CK(cudaMemset(m->hcnt, 0, m->cnt_bytes));
         *status = s;
         return 0;
     } catch (const std::exception &e) {

@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
     __syncthreads();
     for (int e = tid; e < E; e += kRouterThreads) {
         off[e] = cnt[e];
-        nch[e] = (cnt[e] + kNT - 1) / kNT;
+        nch[e] = (cnt[e] + p.nt_routed - 1) / p.nt_routed;
         choff[e] = nch[e];
     }
     __syncthreads();
@@ -292,13 +292,14 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
         for (int w = 0; w < (t >> 5); w++) rank += __popc(bm[e * TW + w]);
         p.perm[off[e] + rank] = a;
     }
-    const int ns = p.has_shared ? (T + kNT - 1) / kNT : 0;
-    for (int i = tid; i < ns; i += kRouterThreads) p.chunks[i] = Chunk{E, T * K + i * kNT, min(kNT, T - i * kNT), 0};
+    const int ns = p.has_shared ? (T + p.nt_shared - 1) / p.nt_shared : 0;
+    for (int i = tid; i < ns; i += kRouterThreads)
+        p.chunks[i] = Chunk{E, T * K + i * p.nt_shared, min(p.nt_shared, T - i * p.nt_shared), 0};
     for (int e = tid; e < E; e += kRouterThreads) {
         p.counts[e] = cnt[e];
         p.offsets[e] = off[e];
         for (int c = 0; c < nch[e]; c++)
-            p.chunks[ns + choff[e] + c] = Chunk{e, off[e] + c * kNT, min(kNT, cnt[e] - c * kNT), 0};
+            p.chunks[ns + choff[e] + c] = Chunk{e, off[e] + c * p.nt_routed, min(p.nt_routed, cnt[e] - c * p.nt_routed), 0};
     }
     if (tid == 0) {
         p.offsets[E] = T * K;

@@ -1,0 +1,39 @@
+// Host/device parameter blocks of the tensor-core expert kernels (experts_tc.cu).
+#pragma once
+
+#include <cuda.h>
+
+#include "layer.cuh"
+
+namespace stbl {
+
+struct TcMaps {
+    CUtensorMap w[2];  // up: routed gate, routed up; down: routed down (twice)
+    CUtensorMap s[2];  // up: shared gate, shared up; down: shared down (twice)
+};
+
+struct TcParams {
+    const Chunk *chunks;
+    const int *n_chunks;
+    int chunk_begin, chunk_end;
+    int T, topk, E, H, I;
+    const int *perm;
+    const float *wts;
+    const uint8_t *act_q;      // up: x codes [T][H]; down: h codes [pos][I]
+    const float *act_s;        // per-128 activation scales, row stride act_s_stride
+    int act_s_stride;
+    const float *w_scale[2];   // routed block scales of the two matrices (up) / one (down), [E][rb][kb]
+    long long w_scale_stride;  // floats per expert
+    const float *s_scale[2];   // shared expert block scales
+    uint16_t *h;               // up out: [pos][I] bf16
+    uint8_t *hq;               // up finisher out: [pos][I] e4m3 codes
+    float *hs;                 // up finisher out: [pos][I / 128]
+    int *hcnt;                 // [chunk][I / 128] rows landed
+    uint16_t *eo, *sh, *y;     // down outputs
+    int *ccnt;                 // [T][H / 128] tiles landed
+    int fuse_combine;          // down: write y through the completion counters
+    int has_shared;
+    uint32_t *status;
+};
+
+}  // namespace stbl
