@@ -1,20 +1,20 @@
 // Grouped expert products on the 5th-generation tensor cores (FP8 128x128-block experts).
 //
-// Work item: (chunk of <= 16 tokens of one expert, 128-row output tile).  One persistent CTA per SM
-// takes a contiguous range of items; six warps:
-//   warp 0     TMA producer: 128 x 128-byte weight tiles (128B swizzle) into a ring of stages;
+// Work item: (chunk of <= 16 tokens of one expert, output tile).  One persistent CTA per SM takes a
+// contiguous range of items; six warps:
+//   warp 0     TMA producer: per 128-K block one stage = a 128-row x 128-byte weight tile and a
+//              16-row x 128-byte activation tile, both in the 128-byte swizzle layout;
 //   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 token columns,
-//              K = 32 per instruction, four per 128-K block into one of four TMEM accumulators;
-//   warps 2-5  epilogue: builds the chunk's activation operand (e4m3 codes, 16 rows x K) in shared
-//              memory, reads each 128-K block's partials from TMEM, applies the fp32 block scales
-//              (weight block x activation block, the promotion of ref/kernel.py:85-91) and
-//              accumulates in registers; then writes the outputs.
+//              K = 32 per instruction, four per 128-K block into one of eight TMEM accumulators;
+//   warps 2-5  epilogue: read each block's partials from TMEM, apply the fp32 block scales (weight
+//              block x activation block: the promotion of ref/kernel.py:85-91) and accumulate in
+//              registers; then write the outputs.
 // up: the tile is [64 gate rows; 64 up rows]; h = bf16(silu(bf16 g) * bf16 u * w) (stbl/kernels.cu:
 //   445-459).  When both 64-row halves of a 128-row group of a chunk have landed, that CTA
 //   re-quantizes the group (act_quant per 128, ref/kernel.py:35-45) for the down kernel.
-// down: eo = bf16(W2 q(h)); when the top-k routed experts and the shared expert of a token have all
-//   landed on a 128-row tile, that CTA writes y = bf16(sum of eo in top-k order + shared)
-//   (stbl/model.cu:589-592).
+// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); when the top-k routed experts and the shared
+//   expert of a token have all landed on a tile, that CTA writes y = bf16(sum of eo in top-k order +
+//   shared) for the tile (stbl/model.cu:589-592).
 // Every wait is bounded; a CTA that gives up raises a status bit, drains its copies and MMAs, frees
 // its TMEM and returns.
 #include "layer.cuh"
@@ -24,10 +24,12 @@
 namespace stbl {
 
 constexpr int kTcThreads = 192;
-constexpr int kTcN = 16;         // token columns per MMA (chunk size)
-constexpr int kTcAcc = 4;        // TMEM accumulators (16 columns each)
-constexpr int kTcTmemCols = 64;
-constexpr int kTileBytes = 128 * 128;
+constexpr int kTcN = 16;          // token columns per MMA (chunk size)
+constexpr int kTcAcc = 8;         // TMEM accumulators (16 columns each)
+constexpr int kTcTmemCols = 128;
+constexpr int kATile = 128 * 128;
+constexpr int kBTile = kTcN * 128;
+constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
 
 struct TcChunk {
     int e, pos0, n, ok;
@@ -45,33 +47,37 @@ __device__ __forceinline__ TcChunk tc_chunk(const TcParams &p, int c) {
     return r;
 }
 
-// token (UP: row of x) and weight of slot j of a chunk
 __device__ __forceinline__ int tc_token(const TcParams &p, const TcChunk &c, int j) {
     const int pos = c.pos0 + j;
     return c.e < p.E ? p.perm[pos] / p.topk : pos - p.T * p.topk;
+}
+
+// first row of the chunk's B tiles: b_direct (x by token): routed chunks (T <= 16) read tokens 0..15
+// and use column = token; shared chunks read their own 16 consecutive tokens, column = slot.
+// Otherwise (rows by position) the chunk's first position, column = slot.
+__device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
+    if (!p.b_direct) return ch.pos0;
+    return ch.e == p.E ? ch.pos0 - p.T * p.topk : 0;
 }
 
 template <bool UP>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p,
                                                                   int nst) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // 1024-align the dynamic region for the 128B-swizzle atoms
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;            // reduction length
     const int rows = UP ? p.I : p.H;         // output rows per matrix
     const int nkb = K / 128;
     const int tiles = UP ? rows / 64 : rows / 128;
-    unsigned char *Bs = smem;                               // [nkb][16 rows][128 B], swizzled
-    unsigned char *As = Bs + (size_t)nkb * kTcN * 128;      // [nst][128 rows][128 B], swizzled
-    float *sx = reinterpret_cast<float *>(As + (size_t)nst * kTileBytes);  // [16][nkb] activation scales
-    float *sw = sx + kTcN * nkb;                            // [2][nkb] weight scales of the item
-    float *xch = sw + 2 * nkb;                              // [64][17] up: u exchange
-    uint64_t *full = reinterpret_cast<uint64_t *>(xch + 64 * 17 + 2);
+    unsigned char *stages = smem;                                         // [nst][A tile | B tile]
+    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * kStage);  // [16][nkb] activation scales
+    float *sw = sx + kTcN * nkb;                                          // [2][nkb] weight scales
+    float *xacc = sw + 2 * nkb;                                           // [128][17] item sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(xacc + 128 * 17 + 2);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
     uint64_t *acc_empty = acc_full + kTcAcc;
-    uint64_t *b_ready = acc_empty + kTcAcc;
-    uint64_t *mma_done = b_ready + 1;
+    uint64_t *mma_done = acc_empty + kTcAcc;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     __shared__ int fin_flag[kTcN + 1];
@@ -81,7 +87,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         abort_flag = 0;
         for (int s = 0; s < nst; s++) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
         for (int a = 0; a < kTcAcc; a++) mbar_init(&acc_full[a], 1), mbar_init(&acc_empty[a], 128);
-        mbar_init(b_ready, 128);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -101,6 +106,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]), tma_prefetch_map(&maps.s[m]);
+            tma_prefetch_map(&maps.b);
             int q = 0;  // running stage counter
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {
@@ -108,6 +114,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 const TcChunk ch = tc_chunk(p, c);
                 const bool shared = ch.e == p.E;
                 const int z = shared ? 0 : ch.e;
+                const int brow = b_row(p, ch);
                 for (int kb = 0; kb < nkb; kb++, q++) {
                     const int s = q % nst;
                     if (!mbar_wait(&empty[s], ((q / nst) & 1) ^ 1, &abort_flag)) {
@@ -116,14 +123,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                         stop = true;
                         break;
                     }
-                    unsigned char *a = As + (size_t)s * kTileBytes;
-                    mbar_arrive_expect_tx(&full[s], kTileBytes);
+                    unsigned char *a = stages + (size_t)s * kStage;
+                    mbar_arrive_expect_tx(&full[s], kStage);
                     if (UP) {
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 64, z, &full[s]);
-                        tma_load_3d(a + kTileBytes / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
+                        tma_load_3d(a + kATile / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
                     } else {
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 128, z, &full[s]);
                     }
+                    tma_load_2d(a + kATile, &maps.b, kb * 128, brow, &full[s]);
                 }
             }
             // drain: every issued tile must land before the CTA may exit
@@ -140,40 +148,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f8_f32(128, kTcN);
-            int q = 0, acc_i = 0, cur = -1, builds = 0;
-            bool stop = false;
-            for (int it = lo; it < hi && !stop; it++) {
-                const int c = p.chunk_begin + it / tiles;
-                if (c != cur) {
-                    cur = c;
-                    if (!mbar_wait(b_ready, builds & 1, &abort_flag)) {
-                        abort_flag = 1;
-                        atomicOr(p.status, kErrWaitTimeout);
-                        break;
-                    }
-                    builds++;
-                    tc_fence_after();
+            const int total = (hi - lo) * nkb;
+            for (int q = 0; q < total; q++) {
+                const int s = q % nst, b = q % kTcAcc;
+                if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag) ||
+                    !mbar_wait(&acc_empty[b], ((q / kTcAcc) & 1) ^ 1, &abort_flag)) {
+                    abort_flag = 1;
+                    atomicOr(p.status, kErrWaitTimeout);
+                    break;
                 }
-                for (int kb = 0; kb < nkb; kb++, q++, acc_i++) {
-                    const int s = q % nst, b = acc_i % kTcAcc;
-                    if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag) ||
-                        !mbar_wait(&acc_empty[b], ((acc_i / kTcAcc) & 1) ^ 1, &abort_flag)) {
-                        abort_flag = 1;
-                        atomicOr(p.status, kErrWaitTimeout);
-                        stop = true;
-                        break;
-                    }
-                    tc_fence_after();
-                    const unsigned char *a = As + (size_t)s * kTileBytes;
-                    const unsigned char *bb = Bs + (size_t)kb * kTcN * 128;
+                tc_fence_after();
+                const unsigned char *a = stages + (size_t)s * kStage;
 #pragma unroll
-                    for (int k = 0; k < 4; k++)
-                        umma_f8(tmem + b * kTcN, sw128_desc(a + 32 * k), sw128_desc(bb + 32 * k), idesc, k > 0);
-                    umma_commit(&empty[s]);
-                    umma_commit(&acc_full[b]);
-                }
+                for (int k = 0; k < 4; k++)
+                    umma_f8(tmem + b * kTcN, sw128_desc(a + 32 * k), sw128_desc(a + kATile + 32 * k), idesc, k > 0);
+                umma_commit(&empty[s]);
+                umma_commit(&acc_full[b]);
             }
-            // all issued MMAs complete before TMEM is freed
+            // every issued MMA completes before TMEM is freed
             umma_commit(mma_done);
             const uint64_t t0 = global_ns();
             while (!mbar_try_wait(mma_done, 0))
@@ -187,59 +179,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         const int et = tid - 64;                   // 0..127
         const int row = 32 * (warp & 3) + lane;    // TMEM lane = tile row
         const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        int acc_i = 0, cur = -1, builds = 0;
-        TcChunk ch{0, 0, 0, 0};
-        int tok[kTcN];
-        float wt[kTcN];
+        int q = 0;
         for (int it = lo; it < hi; it++) {
             const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-            if (c != cur) {
-                // the previous chunk's MMAs have all been consumed (its last accumulator was read), so the
-                // operand buffer can be rebuilt: 16 rows of e4m3 codes in the 128B-swizzle layout
-                cur = c;
-                ch = tc_chunk(p, c);
-                if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
-#pragma unroll
-                for (int j = 0; j < kTcN; j++) {
-                    tok[j] = 0, wt[j] = 0.f;
-                    if (j < ch.n) {
-                        const int pos = ch.pos0 + j;
-                        tok[j] = tc_token(p, ch, j);
-                        wt[j] = ch.e < p.E ? p.wts[p.perm[pos]] : 1.f;
-                    }
-                }
-                const int chunks16 = nkb * 8;  // 16-byte chunks per row
-                for (int q = et; q < kTcN * chunks16; q += 128) {
-                    const int j = q / chunks16, cc = q % chunks16, kb = cc >> 3, c16 = cc & 7;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (j < ch.n) {
-                        const int src_row = UP ? tc_token(p, ch, j) : ch.pos0 + j;
-                        v = __ldg(reinterpret_cast<const uint4 *>(p.act_q + (size_t)src_row * K + kb * 128 + c16 * 16));
-                    }
-                    *reinterpret_cast<uint4 *>(Bs + (size_t)kb * kTcN * 128 + j * 128 + ((c16 ^ (j & 7)) * 16)) = v;
-                }
-                for (int q = et; q < kTcN * nkb; q += 128) {
-                    const int j = q / nkb, kb = q % nkb;
-                    float s = 0.f;
-                    if (j < ch.n) {
-                        const int src_row = UP ? tc_token(p, ch, j) : ch.pos0 + j;
-                        s = __ldg(p.act_s + (size_t)src_row * p.act_s_stride + kb);
-                    }
-                    sx[j * nkb + kb] = s;
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(b_ready);
-                builds++;
-            }
-            // the item's weight block scales (one per 128-K block; up: gate and up of the same row block)
+            const TcChunk ch = tc_chunk(p, c);
+            if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
+            const bool shared = ch.e == p.E;
+            // the item's scales: activation blocks of the 16 B rows, weight blocks of the tile
             bar_sync(2, 128);
+            const int brow = b_row(p, ch);
+            const int bvalid = p.b_direct && !shared ? p.T : ch.n;  // B rows holding real activations
+            for (int u = et; u < kTcN * nkb; u += 128) {
+                const int j = u / nkb, kb = u % nkb;
+                sx[u] = j < bvalid ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
+            }
             {
-                const bool shared = ch.e == p.E;
                 const int rblk = UP ? (tile * 64) / 128 : tile;
-                for (int q = et; q < (UP ? 2 : 1) * nkb; q += 128) {
-                    const int m = q / nkb, kb = q % nkb;
+                for (int u = et; u < (UP ? 2 : 1) * nkb; u += 128) {
+                    const int m = u / nkb, kb = u % nkb;
                     const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)ch.e * p.w_scale_stride;
-                    sw[m * nkb + kb] = __ldg(base + (size_t)rblk * nkb + kb);
+                    sw[u] = __ldg(base + (size_t)rblk * nkb + kb);
                 }
             }
             bar_sync(2, 128);
@@ -248,9 +207,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 #pragma unroll
             for (int j = 0; j < kTcN; j++) acc[j] = 0.f;
             bool ok = true;
-            for (int kb = 0; kb < nkb; kb++, acc_i++) {
-                const int b = acc_i % kTcAcc;
-                if (!mbar_wait(&acc_full[b], (acc_i / kTcAcc) & 1, &abort_flag)) {
+            for (int kb = 0; kb < nkb; kb++, q++) {
+                const int b = q % kTcAcc;
+                if (!mbar_wait(&acc_full[b], (q / kTcAcc) & 1, &abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -271,21 +230,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 break;
             }
             if (UP) {
-                // u rows hand their sums to the matching gate rows
-                if (row >= 64)
+                // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
 #pragma unroll
-                    for (int j = 0; j < kTcN; j++) xch[(row - 64) * 17 + j] = acc[j];
+                for (int j = 0; j < kTcN; j++) xacc[row * 17 + j] = acc[j];
                 bar_sync(2, 128);
-                if (row < 64) {
-                    const int r = tile * 64 + row;
-#pragma unroll
-                    for (int j = 0; j < kTcN; j++) {
-                        if (j < ch.n) {
-                            const float gv = bf16r(acc[j]), uv = bf16r(xch[row * 17 + j]);
-                            const float hv = gv / (1.f + expf(-gv)) * uv * wt[j];
-                            p.h[(size_t)(ch.pos0 + j) * p.I + r] = f32_to_bf16_bits(hv);
-                        }
-                    }
+                const int i = et & 63, r = tile * 64 + i;
+                for (int j = et >> 6; j < ch.n; j += 2) {
+                    const int pos = ch.pos0 + j;
+                    const int col = p.b_direct && ch.e < p.E ? tc_token(p, ch, j) : j;
+                    const float wt = ch.e < p.E ? p.wts[p.perm[pos]] : 1.f;
+                    const float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
+                    const float hv = gv / (1.f + expf(-gv)) * uv * wt;
+                    p.h[(size_t)pos * p.I + r] = f32_to_bf16_bits(hv);
                 }
                 bar_sync(2, 128);
                 // completion count of the 128-row group; the second half to land re-quantizes it
@@ -316,7 +272,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                         const float s = amax * (1.0f / 448.0f);
                         uint32_t codes = 0;
 #pragma unroll
-                        for (int q = 0; q < 4; q++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[q] / s, -448.f), 448.f)) << (8 * q);
+                        for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
                         *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
                         if (lane == 0) p.hs[(size_t)pos * (p.I / 128) + g] = s;
                     }
@@ -326,38 +282,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 #pragma unroll
                 for (int j = 0; j < kTcN; j++) {
                     if (j < ch.n) {
+                        const int pos = ch.pos0 + j;
                         const uint16_t o = f32_to_bf16_bits(acc[j]);
-                        if (ch.e < p.E) p.eo[(size_t)p.perm[ch.pos0 + j] * p.H + r] = o;
-                        else p.sh[(size_t)tok[j] * p.H + r] = o;
+                        if (ch.e < p.E) p.eo[(size_t)p.perm[pos] * p.H + r] = o;
+                        else p.sh[(size_t)(pos - p.T * p.topk) * p.H + r] = o;
                     }
                 }
-                bar_sync(2, 128);
-                // combine when the last of the token's top-k experts and the shared expert lands here
-                if (p.fuse_combine && et < kTcN) {
-                    int f = 0;
-                    if (et < ch.n) {
-                        __threadfence();
-                        int *cnt = p.ccnt + (size_t)tc_token(p, ch, et) * (p.H / 128) + tile;
-                        if (atomicAdd(cnt, 1) + 1 == p.topk + p.has_shared) {
-                            *cnt = 0;
+                if (p.fuse_combine) {
+                    bar_sync(2, 128);
+                    // combine when the last of a token's top-k experts and the shared expert lands here
+                    if (et < kTcN) {
+                        int f = 0;
+                        if (et < ch.n) {
                             __threadfence();
-                            f = 1;
+                            int *cnt = p.ccnt + (size_t)tc_token(p, ch, et) * (p.H / 128) + tile;
+                            if (atomicAdd(cnt, 1) + 1 == p.topk + p.has_shared) {
+                                *cnt = 0;
+                                __threadfence();
+                                f = 1;
+                            }
                         }
+                        fin_flag[et] = f;
                     }
-                    fin_flag[et] = f;
-                }
-                bar_sync(2, 128);
-                for (int j = 0; j < ch.n && p.fuse_combine; j++) {
-                    if (!fin_flag[j]) continue;
-                    const int tk = tc_token(p, ch, j);
-                    float a = 0.f;
-                    for (int sl = 0; sl < p.topk; sl++)
-                        a = a + bf16_bits_to_f32(__ldcg(p.eo + ((size_t)tk * p.topk + sl) * p.H + r));
-                    if (p.has_shared) a = a + bf16_bits_to_f32(__ldcg(p.sh + (size_t)tk * p.H + r));
-                    p.y[(size_t)tk * p.H + r] = f32_to_bf16_bits(a);
+                    bar_sync(2, 128);
+                    for (int j = 0; j < ch.n; j++) {
+                        if (!fin_flag[j]) continue;
+                        const int tk = tc_token(p, ch, j);
+                        float a = 0.f;
+                        for (int sl = 0; sl < p.topk; sl++)
+                            a = a + bf16_bits_to_f32(__ldcg(p.eo + ((size_t)tk * p.topk + sl) * p.H + r));
+                        if (p.has_shared) a = a + bf16_bits_to_f32(__ldcg(p.sh + (size_t)tk * p.H + r));
+                        p.y[(size_t)tk * p.H + r] = f32_to_bf16_bits(a);
+                    }
                 }
             }
-            bar_sync(2, 128);
         }
     }
     tc_fence_before();
@@ -368,6 +326,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
     }
 }
 
+// x codes and scales of every position (routed assignments in dispatch order, then the shared
+// expert's tokens), for the up kernel's activation tiles when T > 16
+__global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int pos = blockIdx.x;
+    const int nrouted = p.T * p.topk;
+    const int tok = pos < nrouted ? p.perm[pos] / p.topk : pos - nrouted;
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.xq + (size_t)tok * p.H);
+    uint4 *dst = reinterpret_cast<uint4 *>(p.xq_pos + (size_t)pos * p.H);
+    for (int i = threadIdx.x; i < p.H / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x)
+        p.xs_pos[(size_t)pos * (p.H / 128) + i] = __ldg(p.xs + (size_t)tok * p.xs_stride + i);
+}
+
 template __global__ void expert_tc_kernel<true>(const __grid_constant__ TcMaps, TcParams, int);
 template __global__ void expert_tc_kernel<false>(const __grid_constant__ TcMaps, TcParams, int);
 
@@ -375,11 +348,12 @@ const void *expert_tc_kernel_ptr(bool up) {
     return up ? (const void *)expert_tc_kernel<true> : (const void *)expert_tc_kernel<false>;
 }
 
-// shared-memory bytes of one launch (the host adds 1 KB for the alignment of the dynamic region)
+const void *gather_kernel_ptr() { return (const void *)gather_kernel; }
+
+// dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
 int expert_tc_smem_bytes(bool up, int H, int I, int nst) {
     const int K = up ? H : I, nkb = K / 128;
-    return nkb * kTcN * 128 + nst * kTileBytes + 4 * (kTcN * nkb + 2 * nkb + 64 * 17 + 2) +
-           8 * (2 * nst + 2 * kTcAcc + 2) + 1024;
+    return nst * kStage + 4 * (kTcN * nkb + 2 * nkb + 128 * 17 + 2) + 8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
 }
 
 }  // namespace stbl

@@ -20,6 +20,7 @@ __global__ void router_kernel(RouterParams p);
 const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
 const void *combine_kernel_ptr();                 // experts.cu
 const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
+const void *gather_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
 }  // namespace stbl
 
@@ -85,8 +86,9 @@ struct stbl_moe {
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
     bool routed_tc = false;           // routed experts on the tensor-core kernels
-    uint8_t *hq = nullptr;
-    float *hs = nullptr;
+    uint8_t *hq = nullptr, *xq_pos = nullptr;
+    float *hs = nullptr, *xs_pos = nullptr;
+    CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
     int *hcnt = nullptr, *ccnt = nullptr;
     size_t cnt_bytes = 0;
     int last_T = 0;
@@ -141,6 +143,20 @@ CUtensorMap weight_map(const void *base, int K, int rows, int experts, long long
 }
 
 void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st);
+
+// 2-D tensor map over [rows][K] e4m3 activation codes, read in 16-row x 128-byte tiles (128B swizzle)
+CUtensorMap act_map(const void *base, int K, int rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {128, 16};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an activation tensor");
+    return m;
+}
 
 KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
     KernelCfg c;
@@ -208,7 +224,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     }
 
     // workspace
-    const int T = m->Tmax, npos = T * K + T;
+    const int T = m->Tmax, npos = T * K + T, Tpad = (T + 15) / 16 * 16;
     auto layout = [&](char *base) {
         char *p = base;
         m->experts = carve<ExpertPtrs>(p, E + 1);
@@ -220,13 +236,15 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->perm = carve<int>(p, (size_t)T * K);
         m->chunks = carve<Chunk>(p, npos);
         m->n_chunks = carve<int>(p, 4);
-        m->xq_a = carve<uint8_t>(p, (size_t)T * H);
-        m->xs_a = carve<float>(p, (size_t)T * (H / 32));
-        m->xq_b = carve<uint8_t>(p, (size_t)T * H);
-        m->xs_b = carve<float>(p, (size_t)T * (H / 32));
+        m->xq_a = carve<uint8_t>(p, (size_t)Tpad * H);
+        m->xs_a = carve<float>(p, (size_t)Tpad * (H / 32));
+        m->xq_b = carve<uint8_t>(p, (size_t)Tpad * H);
+        m->xs_b = carve<float>(p, (size_t)Tpad * (H / 32));
+        m->xq_pos = carve<uint8_t>(p, (size_t)(npos + 16) * H);
+        m->xs_pos = carve<float>(p, (size_t)(npos + 16) * (H / 128));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
-        m->hq = carve<uint8_t>(p, (size_t)npos * I);
-        m->hs = carve<float>(p, (size_t)npos * (I / 128));
+        m->hq = carve<uint8_t>(p, (size_t)(npos + 16) * I);
+        m->hs = carve<float>(p, (size_t)(npos + 16) * (I / 128));
         m->hcnt = carve<int>(p, (size_t)npos * (I / 128) + (size_t)T * (H / 128));  // hcnt then ccnt
         m->ccnt = m->hcnt + (size_t)npos * (I / 128);
         m->eo = carve<uint16_t>(p, (size_t)T * K * H);
@@ -279,9 +297,15 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         }
         if (!m->routed_tc) m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
         if (!m->has_shared) m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
+        m->bmap_xa = act_map(m->xq_a, H, Tpad);
+        m->bmap_xb = act_map(m->xq_b, H, Tpad);
+        m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
+        m->bmap_hq = act_map(m->hq, I, npos + 16);
         auto pick = [&](bool up, int &nst, int &smem) {
-            for (nst = 8; nst >= 2; nst--)
-                if (expert_tc_smem_bytes(up, H, I, nst) + 256 <= max_smem) break;
+            cudaFuncAttributes fa{};
+            CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up)));
+            for (nst = 16; nst >= 2; nst--)
+                if (expert_tc_smem_bytes(up, H, I, nst) + (int)fa.sharedSizeBytes <= max_smem) break;
             if (nst < 2) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
             smem = expert_tc_smem_bytes(up, H, I, nst);
             CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -291,7 +315,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     }
 }
 
-TcParams tc_params(stbl_moe *m, int T, bool up) {
+TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     TcParams p{};
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
@@ -300,13 +324,18 @@ TcParams tc_params(stbl_moe *m, int T, bool up) {
     p.wts = m->wts;
     const stbl_moe_desc &d = m->d;
     if (up) {
-        // x codes for the FP8 (per-128) rule: the routed buffer when the routed experts are FP8, else
-        // the shared expert's
-        p.act_q = m->routed_tc ? m->xq_a : m->xq_b;
-        p.act_s = m->routed_tc ? m->xs_a : m->xs_b;
-        p.act_s_stride = m->H / 32;
+        // direct: x codes by token for the FP8 (per-128) rule (the routed buffer when the routed experts
+        // are FP8, else the shared expert's); gathered: codes by position (gather_kernel)
+        p.b_direct = direct;
+        if (direct) {
+            p.act_s = m->routed_tc ? m->xs_a : m->xs_b;
+            p.act_s_stride = m->H / 32;
+        } else {
+            p.act_s = m->xs_pos;
+            p.act_s_stride = m->H / 128;
+        }
     } else {
-        p.act_q = m->hq;
+        p.b_direct = 0;
         p.act_s = m->hs;
         p.act_s_stride = m->I / 128;
     }
@@ -329,8 +358,17 @@ TcParams tc_params(stbl_moe *m, int T, bool up) {
 }
 
 void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
-    void *args[] = {up ? &m->tc_up : &m->tc_down, &p, up ? &m->tc_nst_up : &m->tc_nst_down};
+    TcMaps maps = up ? m->tc_up : m->tc_down;
+    if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
+    else maps.b = m->bmap_hq;
+    void *args[] = {&maps, &p, up ? &m->tc_nst_up : &m->tc_nst_down};
     launch_pdl(expert_tc_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc_smem_up : m->tc_smem_down, st);
+}
+
+void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
+    GatherParams g{m->perm, T, m->K, m->H, m->has_shared, m->xq_a, m->xs_a, m->H / 32, m->xq_pos, m->xs_pos};
+    void *args[] = {&g};
+    launch_pdl(gather_kernel_ptr(), dim3(T * m->K + (m->has_shared ? T : 0)), dim3(256), args, 0, st);
 }
 
 ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
@@ -410,7 +448,12 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     const int grid = m->sms;
     if (m->routed_tc) {
         // every expert on the tensor cores; the down kernel also writes y (ordered combine)
-        TcParams pu = tc_params(m, T, true), pd = tc_params(m, T, false);
+        const bool direct = T <= 16;
+        if (!direct) {
+            launch_gather(m, T, st);
+            launches++;
+        }
+        TcParams pu = tc_params(m, T, true, direct), pd = tc_params(m, T, false);
         pu.chunk_begin = pd.chunk_begin = 0;
         pu.chunk_end = pd.chunk_end = -1;
         pd.y = static_cast<uint16_t *>(y);

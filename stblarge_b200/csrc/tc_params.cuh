@@ -10,6 +10,7 @@ namespace stbl {
 struct TcMaps {
     CUtensorMap w[2];  // up: routed gate, routed up; down: routed down (twice)
     CUtensorMap s[2];  // up: shared gate, shared up; down: shared down (twice)
+    CUtensorMap b;     // activation operand: 16-row x 128-byte tiles of e4m3 codes
 };
 
 struct TcParams {
@@ -19,8 +20,11 @@ struct TcParams {
     int T, topk, E, H, I;
     const int *perm;
     const float *wts;
-    const uint8_t *act_q;      // up: x codes [T][H]; down: h codes [pos][I]
-    const float *act_s;        // per-128 activation scales, row stride act_s_stride
+    // B tiles: 16 rows of the activation map.  b_direct: the map holds x by token; a routed chunk
+    // (T <= 16) reads tokens 0..15 and finds token t in column t, a shared-expert chunk reads its 16
+    // consecutive tokens.  Otherwise the map holds rows by position and a chunk reads its own.
+    int b_direct;
+    const float *act_s;        // per-128 activation scales of the map's rows, row stride act_s_stride
     int act_s_stride;
     const float *w_scale[2];   // routed block scales of the two matrices (up) / one (down), [E][rb][kb]
     long long w_scale_stride;  // floats per expert
@@ -34,6 +38,18 @@ struct TcParams {
     int fuse_combine;          // down: write y through the completion counters
     int has_shared;
     uint32_t *status;
+};
+
+// gathers x codes and scales into position order for the up kernel when T > 16
+struct GatherParams {
+    const int *perm;
+    int T, topk, H;
+    int has_shared;
+    const uint8_t *xq;
+    const float *xs;
+    int xs_stride;
+    uint8_t *xq_pos;
+    float *xs_pos;             // [pos][H / 128]
 };
 
 }  // namespace stbl
