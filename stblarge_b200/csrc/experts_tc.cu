@@ -5,16 +5,14 @@
 //   warp 0     TMA producer: per 128-K block one stage = a 128-row x 128-byte weight tile and a
 //              16-row x 128-byte activation tile, both in the 128-byte swizzle layout;
 //   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 token columns,
-//              K = 32 per instruction, four per 128-K block into one of eight TMEM accumulators;
-//   warps 2-5  epilogue: read each block's partials from TMEM, apply the fp32 block scales (weight
-//              block x activation block: the promotion of ref/kernel.py:85-91) and accumulate in
-//              registers; then write the outputs.
+//              K = 32 per instruction, four per 128-K block, each block into its own 16 TMEM columns;
+//              blocks are grouped by four (one completion signal per group), four groups in flight;
+//   warps 2-5  epilogue: read a group's four blocks of partials from TMEM in one load, apply the
+//              fp32 block scales (weight block x activation block: the promotion of
+//              ref/kernel.py:85-91) and accumulate in registers; then write the outputs.
 // up: the tile is [64 gate rows; 64 up rows]; h = bf16(silu(bf16 g) * bf16 u * w) (stbl/kernels.cu:
-//   445-459).  When both 64-row halves of a 128-row group of a chunk have landed, that CTA
-//   re-quantizes the group (act_quant per 128, ref/kernel.py:35-45) for the down kernel.
-// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); when the top-k routed experts and the shared
-//   expert of a token have all landed on a tile, that CTA writes y = bf16(sum of eo in top-k order +
-//   shared) for the tile (stbl/model.cu:589-592).
+//   445-459).  hquant_kernel then re-quantizes h (act_quant per 128, ref/kernel.py:35-45).
+// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); combine_kernel (experts.cu) adds them.
 // Every wait is bounded; a CTA that gives up raises a status bit, drains its copies and MMAs, frees
 // its TMEM and returns.
 #include "layer.cuh"
@@ -25,18 +23,21 @@ namespace stbl {
 
 constexpr int kTcThreads = 192;
 constexpr int kTcN = 16;          // token columns per MMA (chunk size)
-constexpr int kTcAcc = 8;         // TMEM accumulators (16 columns each)
-constexpr int kTcTmemCols = 128;
+constexpr int kTcG = 4;           // 128-K blocks per accumulator group (one TMEM read per group)
+constexpr int kTcGroups = 4;      // accumulator groups in TMEM (4 x 4 x 16 columns)
+constexpr int kTcAcc = kTcGroups;
+constexpr int kTcTmemCols = kTcGroups * kTcG * kTcN;
 constexpr int kATile = 128 * 128;
 constexpr int kBTile = kTcN * 128;
 constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
+constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
+constexpr int kTcChunks = 32;     // chunk entries of a CTA's item range kept in shared memory
 
 struct TcChunk {
     int e, pos0, n, ok;
 };
 
-__device__ __forceinline__ TcChunk tc_chunk(const TcParams &p, int c) {
-    const Chunk ch = p.chunks[c];
+__device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
     TcChunk r{ch.e, ch.pos0, ch.n, 1};
     const int nrouted = p.T * p.topk;
     const bool shared = ch.e == p.E;
@@ -45,11 +46,6 @@ __device__ __forceinline__ TcChunk tc_chunk(const TcParams &p, int c) {
                              : (ch.pos0 < 0 || ch.pos0 + ch.n > nrouted));
     if (bad) r = TcChunk{0, 0, 0, 0};
     return r;
-}
-
-__device__ __forceinline__ int tc_token(const TcParams &p, const TcChunk &c, int j) {
-    const int pos = c.pos0 + j;
-    return c.e < p.E ? p.perm[pos] / p.topk : pos - p.T * p.topk;
 }
 
 // first row of the chunk's B tiles: b_direct (x by token): routed chunks (T <= 16) read tokens 0..15
@@ -70,17 +66,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
     const int nkb = K / 128;
     const int tiles = UP ? rows / 64 : rows / 128;
     unsigned char *stages = smem;                                         // [nst][A tile | B tile]
-    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * kStage);  // [16][nkb] activation scales
-    float *sw = sx + kTcN * nkb;                                          // [2][nkb] weight scales
-    float *xacc = sw + 2 * nkb;                                           // [128][17] item sums
-    uint64_t *full = reinterpret_cast<uint64_t *>(xacc + 128 * 17 + 2);
+    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * kStage);  // [2][16][nkb] activation scales
+    float *sw = sx + 2 * kTcN * nkb;                                      // [2][2][nkb] weight scales
+    float *xacc = sw + 4 * nkb;                                           // [128][17] item sums
+    float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
+    int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);           // [2][16] B column of a slot
+    int *slot_dst = slot_col + 2 * kTcN;                                  // [2][16] output row of a slot
+    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);         // [kTcChunks] this CTA's chunks
+    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kTcChunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
     uint64_t *acc_empty = acc_full + kTcAcc;
     uint64_t *mma_done = acc_empty + kTcAcc;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
-    __shared__ int fin_flag[kTcN + 1];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -101,6 +100,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
     const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
     const int lo = (int)(n_items * blockIdx.x / gridDim.x), hi = (int)(n_items * (blockIdx.x + 1) / gridDim.x);
+    // the chunks this CTA's items touch, in shared memory (items beyond the table read global memory)
+    const int c_lo = p.chunk_begin + lo / tiles;
+    for (int i = tid; i < kTcChunks; i += kTcThreads)
+        if (lo < hi && c_lo + i <= p.chunk_begin + (hi - 1) / tiles) ctab[i] = p.chunks[c_lo + i];
+    __syncthreads();
+    auto chunk_of = [&](int c) -> TcChunk {
+        const Chunk ch = (c - c_lo < kTcChunks) ? ctab[c - c_lo] : p.chunks[c];
+        return tc_check(p, ch);
+    };
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {
                 const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-                const TcChunk ch = tc_chunk(p, c);
+                const TcChunk ch = chunk_of(c);
                 const bool shared = ch.e == p.E;
                 const int z = shared ? 0 : ch.e;
                 const int brow = b_row(p, ch);
@@ -148,22 +156,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f8_f32(128, kTcN);
-            const int total = (hi - lo) * nkb;
-            for (int q = 0; q < total; q++) {
-                const int s = q % nst, b = q % kTcAcc;
-                if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag) ||
-                    !mbar_wait(&acc_empty[b], ((q / kTcAcc) & 1) ^ 1, &abort_flag)) {
-                    abort_flag = 1;
-                    atomicOr(p.status, kErrWaitTimeout);
-                    break;
-                }
-                tc_fence_after();
-                const unsigned char *a = stages + (size_t)s * kStage;
+            const int ng = (nkb + kTcG - 1) / kTcG;  // groups per item
+            int q = 0, gq = 0;
+            bool stop = false;
+            for (int it = lo; it < hi && !stop; it++) {
+                for (int gi = 0; gi < ng && !stop; gi++, gq++) {
+                    const int g = gq % kTcGroups;
+                    if (!mbar_wait(&acc_empty[g], ((gq / kTcGroups) & 1) ^ 1, &abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    const int nb = min(kTcG, nkb - gi * kTcG);
+                    for (int u = 0; u < nb; u++, q++) {
+                        const int s = q % nst;
+                        if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag)) {
+                            stop = true;
+                            break;
+                        }
+                        tc_fence_after();
+                        const unsigned char *a = stages + (size_t)s * kStage;
+                        const uint32_t d = tmem + (uint32_t)((g * kTcG + u) * kTcN);
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    umma_f8(tmem + b * kTcN, sw128_desc(a + 32 * k), sw128_desc(a + kATile + 32 * k), idesc, k > 0);
-                umma_commit(&empty[s]);
-                umma_commit(&acc_full[b]);
+                        for (int k = 0; k < 4; k++)
+                            umma_f8(d, sw128_desc(a + 32 * k), sw128_desc(a + kATile + 32 * k), idesc, k > 0);
+                        umma_commit(&empty[s]);
+                    }
+                    if (!stop) umma_commit(&acc_full[g]);
+                }
+            }
+            if (stop) {
+                abort_flag = 1;
+                atomicOr(p.status, kErrWaitTimeout);
             }
             // every issued MMA completes before TMEM is freed
             umma_commit(mma_done);
@@ -176,51 +199,102 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         }
     } else {
         // ---------------- epilogue warpgroup (warps 2..5) ----------------
+        // Per item: scales and slot metadata of the NEXT item are loaded into registers before this
+        // item's accumulators are drained (their latency hides behind the MMAs) and parked in the other
+        // half of double-buffered shared arrays afterwards; nothing in the loop waits on global memory.
         const int et = tid - 64;                   // 0..127
         const int row = 32 * (warp & 3) + lane;    // TMEM lane = tile row
         const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        int q = 0;
-        for (int it = lo; it < hi; it++) {
+        const int nsw = (UP ? 2 : 1) * nkb;
+        float px[kTcPre];
+        float pw = 0.f;
+        int pcol = 0, pdst = 0;
+        float pwt = 0.f;
+        // loads of item `it` into registers (thread et takes sx entries et, et + 128, ..., one weight scale
+        // and, for et < 16, slot et's column, output row and routing weight)
+        auto prefetch = [&](int it) {
             const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-            const TcChunk ch = tc_chunk(p, c);
-            if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
+            const TcChunk ch = chunk_of(c);
             const bool shared = ch.e == p.E;
-            // the item's scales: activation blocks of the 16 B rows, weight blocks of the tile
-            bar_sync(2, 128);
             const int brow = b_row(p, ch);
-            const int bvalid = p.b_direct && !shared ? p.T : ch.n;  // B rows holding real activations
-            for (int u = et; u < kTcN * nkb; u += 128) {
+            const int bvalid = p.b_direct && !shared ? p.T : ch.n;
+#pragma unroll
+            for (int k = 0; k < kTcPre; k++) {
+                const int u = et + 128 * k;
                 const int j = u / nkb, kb = u % nkb;
-                sx[u] = j < bvalid ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
+                px[k] = (u < kTcN * nkb && j < bvalid) ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
             }
-            {
+            if (et < nsw) {
+                const int m = et / nkb, kb = et % nkb;
                 const int rblk = UP ? (tile * 64) / 128 : tile;
-                for (int u = et; u < (UP ? 2 : 1) * nkb; u += 128) {
-                    const int m = u / nkb, kb = u % nkb;
-                    const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)ch.e * p.w_scale_stride;
-                    sw[u] = __ldg(base + (size_t)rblk * nkb + kb);
+                const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)ch.e * p.w_scale_stride;
+                pw = __ldg(base + (size_t)rblk * nkb + kb);
+            }
+            if (et < kTcN) {
+                const int pos = ch.pos0 + et;
+                pcol = et, pdst = pos, pwt = 1.f;
+                if (et < ch.n) {
+                    if (!shared) {
+                        const int a = __ldg(p.perm + pos);
+                        if (UP) {
+                            pwt = __ldg(p.wts + a);
+                            if (p.b_direct) pcol = a / p.topk;
+                        } else {
+                            pdst = a;  // eo row
+                        }
+                    } else if (!UP) {
+                        pdst = pos - p.T * p.topk;  // sh row
+                    }
                 }
             }
-            bar_sync(2, 128);
+        };
+        auto park = [&](int buf) {
+#pragma unroll
+            for (int k = 0; k < kTcPre; k++) {
+                const int u = et + 128 * k;
+                if (u < kTcN * nkb) sx[buf * kTcN * nkb + u] = px[k];
+            }
+            if (et < nsw) sw[buf * 2 * nkb + et] = pw;
+            if (et < kTcN) slot_col[buf * kTcN + et] = pcol, slot_dst[buf * kTcN + et] = pdst, slot_w[buf * kTcN + et] = pwt;
+        };
+        int gq = 0;
+        if (lo < hi) {
+            prefetch(lo);
+            park(0);
+        }
+        bar_sync(2, 128);
+        for (int it = lo; it < hi; it++) {
+            const int buf = (it - lo) & 1;
+            const int c = p.chunk_begin + it / tiles, tile = it % tiles;
+            const TcChunk ch = chunk_of(c);
+            if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
+            if (it + 1 < hi) prefetch(it + 1);
+            const float *sxb = sx + buf * kTcN * nkb, *swb = sw + buf * 2 * nkb;
             const int mrow = UP ? (row >> 6) : 0;  // up: rows 64..127 are the up matrix
             float acc[kTcN];
 #pragma unroll
             for (int j = 0; j < kTcN; j++) acc[j] = 0.f;
             bool ok = true;
-            for (int kb = 0; kb < nkb; kb++, q++) {
-                const int b = q % kTcAcc;
-                if (!mbar_wait(&acc_full[b], (q / kTcAcc) & 1, &abort_flag)) {
+            for (int kb0 = 0; kb0 < nkb; kb0 += kTcG, gq++) {
+                const int g = gq % kTcGroups;
+                if (!mbar_wait(&acc_full[g], (gq / kTcGroups) & 1, &abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                float d[16];
-                tmem_ld16(tl + b * kTcN, d);
+                float d[kTcG * kTcN];
+                tmem_ld64(tl + (uint32_t)(g * kTcG * kTcN), d);
                 tc_fence_before();
-                mbar_arrive(&acc_empty[b]);
-                const float wsc = sw[mrow * nkb + kb];
+                mbar_arrive(&acc_empty[g]);
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) acc[j] = fmaf(d[j], wsc * sx[j * nkb + kb], acc[j]);
+                for (int u = 0; u < kTcG; u++) {
+                    const int kb = kb0 + u;
+                    if (kb < nkb) {
+                        const float wsc = swb[mrow * nkb + kb];
+#pragma unroll
+                        for (int j = 0; j < kTcN; j++) acc[j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc[j]);
+                    }
+                }
             }
             if (bar_sync_or(2, 128, !ok)) {
                 if (et == 0) {
@@ -229,6 +303,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 }
                 break;
             }
+            const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
+            const float *swt = slot_w + buf * kTcN;
             if (UP) {
                 // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
 #pragma unroll
@@ -236,86 +312,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 bar_sync(2, 128);
                 const int i = et & 63, r = tile * 64 + i;
                 for (int j = et >> 6; j < ch.n; j += 2) {
-                    const int pos = ch.pos0 + j;
-                    const int col = p.b_direct && ch.e < p.E ? tc_token(p, ch, j) : j;
-                    const float wt = ch.e < p.E ? p.wts[p.perm[pos]] : 1.f;
+                    const int col = scol[j];
                     const float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
-                    const float hv = gv / (1.f + expf(-gv)) * uv * wt;
-                    p.h[(size_t)pos * p.I + r] = f32_to_bf16_bits(hv);
-                }
-                bar_sync(2, 128);
-                // completion count of the 128-row group; the second half to land re-quantizes it
-                if (et == 0) {
-                    int f = 0;
-                    if (ch.n > 0) {
-                        __threadfence();
-                        int *cnt = p.hcnt + (size_t)c * (p.I / 128) + tile / 2;
-                        if (atomicAdd(cnt, 64) + 64 == 128) {
-                            *cnt = 0;
-                            __threadfence();
-                            f = 1;
-                        }
-                    }
-                    fin_flag[0] = f;
-                }
-                bar_sync(2, 128);
-                if (fin_flag[0]) {
-                    const int g = tile / 2;
-                    for (int j = warp - 2; j < ch.n; j += 4) {
-                        const int pos = ch.pos0 + j;
-                        const uint16_t *src = p.h + (size_t)pos * p.I + g * 128;
-                        const uint2 xv = __ldcg(reinterpret_cast<const uint2 *>(src + 4 * lane));
-                        const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u),
-                                            __uint_as_float(xv.y << 16), __uint_as_float(xv.y & 0xffff0000u)};
-                        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-                        amax = fmaxf(warp_max(amax), 1e-4f);
-                        const float s = amax * (1.0f / 448.0f);
-                        uint32_t codes = 0;
-#pragma unroll
-                        for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
-                        *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
-                        if (lane == 0) p.hs[(size_t)pos * (p.I / 128) + g] = s;
-                    }
+                    const float hv = gv / (1.f + expf(-gv)) * uv * swt[j];
+                    p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
                 }
             } else {
                 const int r = tile * 128 + row;
+                uint16_t *out = ch.e < p.E ? p.eo : p.sh;
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) {
-                    if (j < ch.n) {
-                        const int pos = ch.pos0 + j;
-                        const uint16_t o = f32_to_bf16_bits(acc[j]);
-                        if (ch.e < p.E) p.eo[(size_t)p.perm[pos] * p.H + r] = o;
-                        else p.sh[(size_t)(pos - p.T * p.topk) * p.H + r] = o;
-                    }
-                }
-                if (p.fuse_combine) {
-                    bar_sync(2, 128);
-                    // combine when the last of a token's top-k experts and the shared expert lands here
-                    if (et < kTcN) {
-                        int f = 0;
-                        if (et < ch.n) {
-                            __threadfence();
-                            int *cnt = p.ccnt + (size_t)tc_token(p, ch, et) * (p.H / 128) + tile;
-                            if (atomicAdd(cnt, 1) + 1 == p.topk + p.has_shared) {
-                                *cnt = 0;
-                                __threadfence();
-                                f = 1;
-                            }
-                        }
-                        fin_flag[et] = f;
-                    }
-                    bar_sync(2, 128);
-                    for (int j = 0; j < ch.n; j++) {
-                        if (!fin_flag[j]) continue;
-                        const int tk = tc_token(p, ch, j);
-                        float a = 0.f;
-                        for (int sl = 0; sl < p.topk; sl++)
-                            a = a + bf16_bits_to_f32(__ldcg(p.eo + ((size_t)tk * p.topk + sl) * p.H + r));
-                        if (p.has_shared) a = a + bf16_bits_to_f32(__ldcg(p.sh + (size_t)tk * p.H + r));
-                        p.y[(size_t)tk * p.H + r] = f32_to_bf16_bits(a);
-                    }
-                }
+                for (int j = 0; j < kTcN; j++)
+                    if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
             }
+            if (it + 1 < hi) park(buf ^ 1);
+            bar_sync(2, 128);
         }
     }
     tc_fence_before();
@@ -341,6 +351,31 @@ __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
         p.xs_pos[(size_t)pos * (p.H / 128) + i] = __ldg(p.xs + (size_t)tok * p.xs_stride + i);
 }
 
+// act_quant per 128 (ref/kernel.py:35-45, fp32 scale amax/448) of h for the down kernel: one warp per
+// (position, 128-value block), four values a lane.
+__global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const int per_row = p.I / 128;
+    if (w >= p.n_pos * per_row) return;
+    const int pos = w / per_row, g = w % per_row;
+    const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(p.h + (size_t)pos * p.I + g * 128 + 4 * lane));
+    const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
+                        __uint_as_float(xv.y & 0xffff0000u)};
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    amax = fmaxf(warp_max(amax), 1e-4f);
+    const float s = amax * (1.0f / 448.0f);
+    uint32_t codes = 0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
+    *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
+    if (lane == 0) p.hs[(size_t)pos * per_row + g] = s;
+}
+
+const void *hquant_kernel_ptr() { return (const void *)hquant_kernel; }
+
 template __global__ void expert_tc_kernel<true>(const __grid_constant__ TcMaps, TcParams, int);
 template __global__ void expert_tc_kernel<false>(const __grid_constant__ TcMaps, TcParams, int);
 
@@ -353,7 +388,8 @@ const void *gather_kernel_ptr() { return (const void *)gather_kernel; }
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
 int expert_tc_smem_bytes(bool up, int H, int I, int nst) {
     const int K = up ? H : I, nkb = K / 128;
-    return nst * kStage + 4 * (kTcN * nkb + 2 * nkb + 128 * 17 + 2) + 8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
+    return nst * kStage + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 6 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
+           8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
 }
 
 }  // namespace stbl

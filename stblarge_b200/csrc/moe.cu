@@ -21,6 +21,7 @@ const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
 const void *combine_kernel_ptr();                 // experts.cu
 const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
 const void *gather_kernel_ptr();                  // experts_tc.cu
+const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
 }  // namespace stbl
 
@@ -89,8 +90,7 @@ struct stbl_moe {
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
-    int *hcnt = nullptr, *ccnt = nullptr;
-    size_t cnt_bytes = 0;
+
     int last_T = 0;
     uint64_t calls = 0, tokens = 0;
     int launches = 0;
@@ -245,8 +245,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->h = carve<uint16_t>(p, (size_t)npos * I);
         m->hq = carve<uint8_t>(p, (size_t)(npos + 16) * I);
         m->hs = carve<float>(p, (size_t)(npos + 16) * (I / 128));
-        m->hcnt = carve<int>(p, (size_t)npos * (I / 128) + (size_t)T * (H / 128));  // hcnt then ccnt
-        m->ccnt = m->hcnt + (size_t)npos * (I / 128);
         m->eo = carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
@@ -255,7 +253,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->status = carve<uint32_t>(p, 4);
         return (size_t)(p - base);
     };
-    m->cnt_bytes = sizeof(int) * ((size_t)npos * (I / 128) + (size_t)T * (H / 128));
     m->ws_bytes = layout(nullptr);
     CK(cudaMalloc(&m->ws, m->ws_bytes));
     CK(cudaMemset(m->ws, 0, m->ws_bytes));
@@ -277,7 +274,8 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->down_r = make_cfg(d->routed_fmt, false, H, I, max_smem);
     }
     if (m->routed_tc || m->has_shared) {
-        if (H % 128 || I % 128) throw std::runtime_error("FP8 experts need hidden and inter multiples of 128");
+        if (H % 128 || I % 128 || H > 8192 || I > 8192)
+            throw std::runtime_error("FP8 experts need hidden and inter multiples of 128, at most 8192");
         // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
         const long long wst[3] = {
             d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H,
@@ -350,11 +348,21 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     const long long sst = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]]
                                                        : 4LL * ((rows + 127) / 128) * ((K + 127) / 128);
     p.w_scale_stride = sst / 4;
-    p.h = m->h, p.hq = m->hq, p.hs = m->hs, p.hcnt = m->hcnt;
-    p.eo = m->eo, p.sh = m->sh, p.ccnt = m->ccnt;
+    p.h = m->h;
+    p.eo = m->eo, p.sh = m->sh;
     p.has_shared = m->has_shared;
     p.status = m->status;
     return p;
+}
+
+// act_quant of h for the positions of [pos_begin, pos_end) (the down kernel's B operand)
+void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
+    if (pos_end <= pos_begin) return;
+    HquantParams hp{m->h + (size_t)pos_begin * m->I, m->hq + (size_t)pos_begin * m->I, m->hs + (size_t)pos_begin * (m->I / 128),
+                    pos_end - pos_begin, m->I};
+    void *args[] = {&hp};
+    const int warps = hp.n_pos * (m->I / 128);
+    launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
 }
 
 void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
@@ -446,8 +454,9 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     int launches = 1;
 
     const int grid = m->sms;
+    const int npos = T * m->K + (m->has_shared ? T : 0);
     if (m->routed_tc) {
-        // every expert on the tensor cores; the down kernel also writes y (ordered combine)
+        // every expert on the tensor cores: [gather] -> up -> hquant -> down -> combine
         const bool direct = T <= 16;
         if (!direct) {
             launch_gather(m, T, st);
@@ -456,15 +465,14 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         TcParams pu = tc_params(m, T, true, direct), pd = tc_params(m, T, false);
         pu.chunk_begin = pd.chunk_begin = 0;
         pu.chunk_end = pd.chunk_end = -1;
-        pd.y = static_cast<uint16_t *>(y);
-        pd.fuse_combine = 1;
         launch_tc(m, true, pu, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launch_hquant(m, 0, npos, st);
         launch_tc(m, false, pd, st);
-        launches += 2;
+        launches += 3;
     } else {
-        // MXFP4 routed experts on the CUDA-core kernels, the FP8 shared expert on the tensor cores,
-        // then the combine kernel
+        // MXFP4 routed experts on the CUDA-core kernels (they re-quantize h themselves), the FP8 shared
+        // expert on the tensor cores
         const int ns = m->has_shared ? (T + 15) / 16 : 0;
         ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
         pu.chunk_begin = pd.chunk_begin = ns;
@@ -478,19 +486,20 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         launch_expert(m->up_r, pu, grid, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         if (ns) {
+            launch_hquant(m, T * m->K, npos, st);
             TcParams sd = tc_params(m, T, false);
             sd.chunk_begin = 0, sd.chunk_end = ns;
             launch_tc(m, false, sd, st);
-            launches++;
+            launches += 2;
         }
         launch_expert(m->down_r, pd, grid, st);
         launches += 2;
-        CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
-        void *cargs[] = {&cp};
-        const int cthreads = T * (m->H / 8);
-        launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
-        launches += 1;
     }
+    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
+    void *cargs[] = {&cp};
+    const int cthreads = T * (m->H / 8);
+    launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
+    launches += 1;
     if (m->timing) {
         CK(cudaEventRecord(tc.ev[3], st));
         m->pending.push_back(tc);
@@ -624,7 +633,6 @@ int stbl_moe_status(stbl_moe *m, uint32_t *status) {
         uint32_t s = 0;
         CK(cudaMemcpy(&s, m->status, 4, cudaMemcpyDeviceToHost));
         CK(cudaMemset(m->status, 0, 4));
-        if (s) CK(cudaMemset(m->hcnt, 0, m->cnt_bytes));
         *status = s;
         return 0;
     } catch (const std::exception &e) {

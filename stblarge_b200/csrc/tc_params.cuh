@@ -30,14 +30,17 @@ struct TcParams {
     long long w_scale_stride;  // floats per expert
     const float *s_scale[2];   // shared expert block scales
     uint16_t *h;               // up out: [pos][I] bf16
-    uint8_t *hq;               // up finisher out: [pos][I] e4m3 codes
-    float *hs;                 // up finisher out: [pos][I / 128]
-    int *hcnt;                 // [chunk][I / 128] rows landed
-    uint16_t *eo, *sh, *y;     // down outputs
-    int *ccnt;                 // [T][H / 128] tiles landed
-    int fuse_combine;          // down: write y through the completion counters
+    uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
     uint32_t *status;
+};
+
+// act_quant of h (positions x I) into e4m3 codes and per-128 scales for the down kernel
+struct HquantParams {
+    const uint16_t *h;
+    uint8_t *hq;
+    float *hs;
+    int n_pos, I;
 };
 
 // gathers x codes and scales into position order for the up kernel when T > 16
