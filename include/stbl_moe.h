@@ -106,6 +106,23 @@ void stbl_moe_stats(const stbl_moe *m, uint64_t *calls, uint64_t *tokens, int *l
 const char *stbl_moe_error(const stbl_moe *m);
 void stbl_moe_destroy(stbl_moe *m);
 
+/* Routing without allocating.  This entry point has no counterpart in the reference; it exists for
+ * callers that cannot allocate device memory: code running while a CUDA graph is being captured,
+ * engines that own a fixed memory pool and allow no allocation outside it, embedded runtimes without
+ * an allocator.  It runs the layer's router (logits, scores, group-limited top-k, routing weights,
+ * bucketed dispatch; the same kernel and results as stbl_moe_forward's routing) for T tokens with all
+ * of its working memory in one fixed array inside the library (about 660 KB, held by every GPU that
+ * loads the library until the process exits).  Limits: T <= 64, n_experts <= 256, hidden a multiple
+ * of 128 up to 8192, topk <= 16; larger sizes are rejected with a message in err.  Inputs and outputs
+ * are device buffers owned by the caller: idx, weights [T][topk], counts [E], offsets [E+1],
+ * perm [T*topk] (as stbl_moe_last_route).  Every call shares the array, so calls that overlap on the
+ * GPU race: serialise them.  The first call on each device looks the array up
+ * (cudaGetSymbolAddress); make it before any stream capture.  Returns 0, or -1 with err filled. */
+int stbl_route_noalloc(const float *router_w, const float *router_bias, const void *x_bf16, int T, int n_experts,
+                       int hidden, int topk, int n_groups, int topk_groups, int score_fn, float route_scale, int *idx,
+                       float *weights, int *counts, int *offsets, int *perm, cudaStream_t stream, char *err,
+                       int errlen);
+
 #ifdef __cplusplus
 }
 #endif

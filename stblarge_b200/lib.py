@@ -43,6 +43,7 @@ SIGNATURES = {
     "stbl_moe_stats": (None, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(I)]),
     "stbl_moe_error": (ctypes.c_char_p, [P]),
     "stbl_moe_destroy": (None, [P]),
+    "stbl_route_noalloc": (I, [P, P, P, I, I, I, I, I, I, I, F, P, P, P, P, P, P, ctypes.c_char_p, I]),
     # include/stbl_kernels.h
     "stbl_act_quant_fp8": (None, [P, I, P]),
     "stbl_round_bf16": (None, [P, I, P]),
