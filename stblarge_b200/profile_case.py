@@ -3,19 +3,55 @@ moe_intermediate 2048, FP8 128x128 or MXFP4) but only a few routed experts resid
 capture under ncu holds under 2 GB of device memory and ends in seconds.
 
     python -m stblarge_b200.profile_case [--experts 16] [--tokens 1] [--calls 3] [--fmt fp8|fp4]
+    python -m stblarge_b200.profile_case --router-only [--experts 256] [--tokens 16]
 
 Each call is preceded by a 256 MB write that flushes L2.  Prints the per-kernel device times.
+--router-only runs just the router kernel (through stbl_route_noalloc) on the full-size router
+(7168 x E fp32), holding about 10 MB of device memory.
 """
 
 import argparse
+import ctypes
 import dataclasses
 
 import numpy as np
 import torch
 
+from . import lib as L
 from . import synth
 from .config import CFG2, CFG3
 from .moe import MoELayer
+
+
+def router_only(a):
+    cfg = dataclasses.replace(CFG2, n_experts=a.experts, n_groups=8 if a.experts % 8 == 0 and a.experts >= 16 else 1,
+                              topk_groups=4 if a.experts % 8 == 0 and a.experts >= 16 else 1)
+    lib = L.load()
+    w = torch.from_numpy(synth.router_w(cfg)).cuda()
+    b = torch.from_numpy(synth.router_bias(cfg)).cuda()
+    T = a.tokens
+    idx = torch.empty(T * cfg.topk, dtype=torch.int32, device="cuda")
+    wt = torch.empty(T * cfg.topk, dtype=torch.float32, device="cuda")
+    counts = torch.empty(cfg.n_experts + 1, dtype=torch.int32, device="cuda")
+    offsets = torch.empty(cfg.n_experts + 1, dtype=torch.int32, device="cuda")
+    perm = torch.empty(T * cfg.topk, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    err = ctypes.create_string_buffer(256)
+    xs = [torch.from_numpy(synth.make_x(cfg.hidden, T, seed=90 + i).view(np.int16)).cuda()
+          for i in range(a.warmup + a.calls)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in xs]
+    st = torch.cuda.current_stream().cuda_stream
+    for x, (e0, e1) in zip(xs, ev):
+        flush.zero_()
+        e0.record()
+        rc = lib.stbl_route_noalloc(w.data_ptr(), b.data_ptr(), x.data_ptr(), T, cfg.n_experts, cfg.hidden, cfg.topk,
+                                    cfg.n_groups, cfg.topk_groups, cfg.score_fn, cfg.route_scale, idx.data_ptr(),
+                                    wt.data_ptr(), counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(), st, err, 256)
+        e1.record()
+        assert rc == 0, err.value.decode()
+    torch.cuda.synchronize()
+    ms = [e0.elapsed_time(e1) for e0, e1 in ev[a.warmup:]]
+    print(f"router E={cfg.n_experts} T={T}: {np.mean(ms) * 1e3:.1f} us per call (event-timed, L2 flushed)")
 
 
 def main():
@@ -25,7 +61,11 @@ def main():
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--fmt", default="fp8", choices=["fp8", "fp4"])
+    ap.add_argument("--router-only", action="store_true")
     a = ap.parse_args()
+    if a.router_only:
+        router_only(a)
+        return
     base = CFG2 if a.fmt == "fp8" else CFG3
     E = a.experts
     groups = 8 if E % 8 == 0 and E // 8 >= 2 else 1
