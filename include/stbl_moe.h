@@ -36,7 +36,7 @@ enum { STBL_SCORE_SIGMOID = 0, STBL_SCORE_SQRT_SOFTPLUS = 1 };
 typedef struct stbl_moe stbl_moe;
 
 typedef struct stbl_moe_desc {
-    int hidden;        /* H: multiple of 512 */
+    int hidden;        /* H: multiple of 512, at most 8192 */
     int inter;         /* I: moe_intermediate, multiple of 512 */
     int n_experts;     /* E routed experts, <= 512, multiple of n_groups */
     int topk;          /* <= 16 */
@@ -48,7 +48,7 @@ typedef struct stbl_moe_desc {
     int routed_fmt;    /* STBL_FMT_FP8_B128 or STBL_FMT_MXFP4 */
     int shared_fmt;    /* STBL_FMT_FP8_B128 or STBL_FMT_NONE */
     int max_tokens;    /* largest T passed to stbl_moe_forward, <= 256 */
-    const float *router_w;    /* device fp32 [E][H] */
+    const float *router_w;    /* device fp32 [E][H], 16-byte aligned */
     const float *router_bias; /* device fp32 [E] (score-correction bias) */
     /* routed experts, device: expert e of matrix m (0 gate [I][H], 1 up [I][H], 2 down [H][I]) starts
        at routed_w[m] + e * routed_w_stride[m] bytes (stride 0: the packed size of one matrix) */
@@ -65,8 +65,8 @@ typedef struct stbl_moe_desc {
  * expert table.  Weight pointers must be 16-byte aligned.  Returns 0, or -1 with err filled. */
 int stbl_moe_create(const stbl_moe_desc *desc, stbl_moe **out, char *err, int errlen);
 
-/* y = MoE(x) for T decode tokens: x and y are device bf16 [T][H].  Enqueued on `stream`; returns
- * without waiting.  Returns -1 (see stbl_moe_error) for a bad argument. */
+/* y = MoE(x) for T decode tokens: x and y are device bf16 [T][H], x 16-byte aligned.  Enqueued on
+ * `stream`; returns without waiting.  Returns -1 (see stbl_moe_error) for a bad argument. */
 int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaStream_t stream);
 
 /* The same with host buffers (pinned or pageable): copies x in, runs the layer, copies y out and
@@ -110,10 +110,11 @@ void stbl_moe_destroy(stbl_moe *m);
  * callers that cannot allocate device memory: code running while a CUDA graph is being captured,
  * engines that own a fixed memory pool and allow no allocation outside it, embedded runtimes without
  * an allocator.  It runs the layer's router (logits, scores, group-limited top-k, routing weights,
- * bucketed dispatch; the same kernel and results as stbl_moe_forward's routing) for T tokens with all
- * of its working memory in one fixed array inside the library (about 660 KB, held by every GPU that
- * loads the library until the process exits).  Limits: T <= 64, n_experts <= 256, hidden a multiple
- * of 128 up to 8192, topk <= 16; larger sizes are rejected with a message in err.  Inputs and outputs
+ * bucketed dispatch; the same kernels and results as stbl_moe_forward's routing) for T tokens with
+ * all of its working memory in one fixed array inside the library (about 660 KB, held by every GPU
+ * that loads the library until the process exits).  Limits: T <= 64, n_experts <= 256, hidden a
+ * multiple of 128 up to 8192 (up to 2048 when it is not a multiple of 512), topk <= 16; larger sizes
+ * are rejected with a message in err.  router_w and x must be 16-byte aligned.  Inputs and outputs
  * are device buffers owned by the caller: idx, weights [T][topk], counts [E], offsets [E+1],
  * perm [T*topk] (as stbl_moe_last_route).  Every call shares the array, so calls that overlap on the
  * GPU race: serialise them.  The first call on each device looks the array up

@@ -13,7 +13,12 @@ enum : int { kScoreSigmoid = 0, kScoreSqrtSoftplus = 1 };
 
 constexpr int kMaxExperts = 512;    // router: a lane holds experts l, l+32, ... (16 per lane)
 constexpr int kMaxTopk = 16;
-constexpr int kRouterThreads = 256;
+constexpr int kRouterMaxTokens = 256;
+constexpr int kLgThreads = 256;     // router logits kernel: 8 warps
+constexpr int kLgExperts = 8;       // experts per logits CTA (two quads of 4)
+constexpr int kLgRound = 32;        // tokens staged in shared memory at a time
+constexpr int kLgMaxSlice = 2048;   // longest hidden slice (H / ksplit) the logits kernel stages
+constexpr int kSelThreads = 512;    // router selection kernel: one CTA, a warp per token
 constexpr int kExpertWarps = 15;    // warp 0 streams weights, warps 1..14 compute
 constexpr int kConsumerWarps = kExpertWarps - 1;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;  // 448
@@ -66,9 +71,16 @@ struct RouterParams {
     uint8_t *xq_b;
     float *xs_b;
     int blk_b, pow2_b;
-    unsigned int *done;      // last-CTA ticket
     uint32_t *status;
 };
+
+// Sets the logits kernel's shared-memory limit on the current device (once per device, before any
+// stream capture).
+cudaError_t router_setup();
+// Enqueues the router's two kernels (logits + scores, then selection + dispatch).  pdl_first lets
+// the logits kernel start while the previous kernel on the stream drains.  H / router_ksplit(H)
+// must be at most kLgMaxSlice and T at most kRouterMaxTokens.
+cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first);
 
 // One launch of the expert kernels covers chunks [chunk_begin, chunk_end); chunk_end < 0 means
 // "up to n_chunks[0]" (known only on the device).  Each CTA takes one contiguous range of the

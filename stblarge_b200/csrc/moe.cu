@@ -1,9 +1,10 @@
 // Layer object and C ABI of the MoE decode path (include/stbl_moe.h).
 //
-// One layer call is four kernel launches on the caller's stream (six when the routed and shared
-// experts have different formats): router (+ selection + dispatch), expert up (+ SwiGLU), expert
-// down (+ act_quant of h), combine.  They are chained with programmatic dependent launch, so each
-// kernel's CTAs start while the previous kernel drains.  No host synchronisation inside a call.
+// One layer call is six kernel launches on the caller's stream for FP8 experts (seven above 16
+// tokens, eight when the routed experts are MXFP4): router logits, router selection + dispatch,
+// expert up (+ SwiGLU), act_quant of h, expert down, combine.  They are chained with programmatic
+// dependent launch, so each kernel's CTAs start while the previous kernel drains.  No host
+// synchronisation inside a call.
 #include <stdio.h>
 #include <string.h>
 
@@ -16,7 +17,6 @@
 #include "tc_params.cuh"
 
 namespace stbl {
-__global__ void router_kernel(RouterParams p);
 const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
 const void *combine_kernel_ptr();                 // experts.cu
 const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
@@ -77,11 +77,9 @@ struct stbl_moe {
     Chunk *chunks = nullptr;
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
-    unsigned int *done = nullptr;
     uint32_t *status = nullptr;
     ExpertPtrs *experts = nullptr;
     std::vector<ExpertPtrs> host_experts;
-    int router_grid = 0, router_smem = 0;
     KernelCfg up_r, down_r;           // CUDA-core kernels (MXFP4 routed experts)
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
@@ -194,8 +192,10 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     if (d->score_fn != STBL_SCORE_SIGMOID && d->score_fn != STBL_SCORE_SQRT_SOFTPLUS) throw std::runtime_error("bad score_fn");
     if (d->routed_fmt != STBL_FMT_FP8_B128 && d->routed_fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad routed_fmt");
     if (d->shared_fmt != STBL_FMT_FP8_B128 && d->shared_fmt != STBL_FMT_NONE) throw std::runtime_error("bad shared_fmt");
-    if (d->max_tokens < 1 || d->max_tokens > 256) throw std::runtime_error("max_tokens must be in 1..256");
+    if (d->max_tokens < 1 || d->max_tokens > kRouterMaxTokens) throw std::runtime_error("max_tokens must be in 1..256");
+    if (H / router_ksplit(H) > kLgMaxSlice) throw std::runtime_error("hidden must be at most 8192");
     if (!d->router_w || !d->router_bias) throw std::runtime_error("router weights missing");
+    if ((uintptr_t)d->router_w & 15) throw std::runtime_error("router weights must be 16-byte aligned");
     m->E = E, m->H = H, m->I = I, m->K = K, m->Tmax = d->max_tokens;
     m->ksplit = router_ksplit(H);
     m->has_shared = d->shared_fmt != STBL_FMT_NONE;
@@ -249,7 +249,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
-        m->done = carve<unsigned int>(p, 4);
         m->status = carve<uint32_t>(p, 4);
         return (size_t)(p - base);
     };
@@ -263,11 +262,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     CK(cudaGetDevice(&dev));
     CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    const int epc = (kRouterThreads / 32) / m->ksplit;  // experts per router CTA
-    m->router_grid = (E + epc - 1) / epc;
-    const int TW = (T + 31) / 32;
-    m->router_smem = 2 * (kRouterThreads / 32) * E * 4 + T * K * 4 + 4 * E * 4 + E * TW * 4;
-    CK(cudaFuncSetAttribute((const void *)router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m->router_smem));
+    CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
     if (!m->routed_tc) {
         m->up_r = make_cfg(d->routed_fmt, true, H, I, max_smem);
@@ -429,6 +424,7 @@ void collect_timing(stbl_moe *m, size_t keep);
 void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
     if (!x || !y) throw std::runtime_error("null x or y");
+    if ((uintptr_t)x & 15) throw std::runtime_error("x must be 16-byte aligned");
     TimedCall tc{};
     if (m->timing) {
         if (m->pending.size() >= 256) collect_timing(m, 0);
@@ -447,11 +443,10 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
     r.nt_routed = m->routed_tc ? 16 : kNT;
     r.nt_shared = 16;
-    r.done = m->done, r.status = m->status;
-    void *rargs[] = {&r};
-    launch_pdl((const void *)router_kernel, dim3(m->router_grid), dim3(kRouterThreads), rargs, m->router_smem, st);
+    r.status = m->status;
+    CK(launch_router(r, st, true));
     if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
-    int launches = 1;
+    int launches = 2;
 
     const int grid = m->sms;
     const int npos = T * m->K + (m->has_shared ? T : 0);

@@ -3,10 +3,12 @@
 // Some callers cannot allocate device memory: code that runs while a CUDA graph is being captured
 // (cudaMalloc is not capturable), engines that own a fixed memory pool and forbid allocations outside
 // it, and embedded runtimes that never link an allocator.  For them this entry point runs the router
-// kernel (router.cu, unchanged) with all of its working memory in one fixed-size array that the
-// library declares at file scope; the caller passes only its inputs and output buffers.
+// kernels (router.cu, the same launches as the layer's) with all of their working memory in one
+// fixed-size array that the library declares at file scope; the caller passes only its inputs and
+// output buffers.
 //
-// Limits: T <= kNaMaxTokens tokens, E <= kNaMaxExperts experts, H <= kNaMaxHidden, topk <= 16.
+// Limits: T <= kNaMaxTokens tokens, E <= kNaMaxExperts experts, H <= kNaMaxHidden (and at most
+// 2048 when H is not a multiple of 512: the router's hidden slice), topk <= 16.
 // The array (about 660 KB) is part of the library image: every GPU that loads the library holds it
 // until the process exits.  All calls share it, so calls that overlap on the GPU (two streams, two
 // threads) race; serialise them.  The first call on each device looks up the array's device
@@ -16,10 +18,6 @@
 
 #include "../../include/stbl_moe.h"
 #include "layer.cuh"
-
-namespace stbl {
-__global__ void router_kernel(RouterParams p);
-}  // namespace stbl
 
 using namespace stbl;
 
@@ -36,8 +34,8 @@ constexpr size_t kNaXq = kNaScores + sizeof(float) * kNaMaxTokens * kNaMaxExpert
 constexpr size_t kNaXs = kNaXq + (size_t)kNaMaxTokens * kNaMaxHidden;                   // f32 [T][H / 32]
 constexpr size_t kNaChunks = kNaXs + sizeof(float) * kNaMaxTokens * (kNaMaxHidden / 32);  // Chunk [T * (topk + 1)]
 constexpr size_t kNaNChunks = kNaChunks + sizeof(Chunk) * kNaMaxTokens * (kNaMaxTopk + 1);  // int [4]
-constexpr size_t kNaDone = kNaNChunks + 256;                                           // u32 ticket
-constexpr size_t kNaBytes = kNaDone + 256;
+constexpr size_t kNaStatus = kNaNChunks + 256;                                         // u32 status
+constexpr size_t kNaBytes = kNaStatus + 256;
 
 static __device__ __align__(256) unsigned char g_route_scratch[kNaBytes];
 
@@ -59,6 +57,10 @@ extern "C" int stbl_route_noalloc(const float *router_w, const float *router_bia
     if (T < 1 || T > kNaMaxTokens) return fail(err, errlen, "stbl_route_noalloc: T must be in 1..64");
     if (E < 1 || E > kNaMaxExperts) return fail(err, errlen, "stbl_route_noalloc: n_experts must be in 1..256");
     if (H < 128 || H > kNaMaxHidden || H % 128) return fail(err, errlen, "stbl_route_noalloc: hidden must be a multiple of 128, at most 8192");
+    if (H / router_ksplit(H) > kLgMaxSlice)
+        return fail(err, errlen, "stbl_route_noalloc: hidden must be at most 2048 when it is not a multiple of 512");
+    if ((uintptr_t)router_w & 15 || (uintptr_t)x_bf16 & 15)
+        return fail(err, errlen, "stbl_route_noalloc: router_w and x must be 16-byte aligned");
     if (topk < 1 || topk > kNaMaxTopk || topk > E) return fail(err, errlen, "stbl_route_noalloc: topk must be in 1..16 and <= n_experts");
     if (n_groups < 1 || n_groups > 32 || E % n_groups || topk_groups < 1 || topk_groups > n_groups)
         return fail(err, errlen, "stbl_route_noalloc: bad expert groups");
@@ -82,6 +84,11 @@ extern "C" int stbl_route_noalloc(const float *router_w, const float *router_bia
                 if (err && errlen > 0) snprintf(err, errlen, "stbl_route_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
                 return -1;
             }
+            const cudaError_t e2 = router_setup();
+            if (e2 != cudaSuccess) {
+                if (err && errlen > 0) snprintf(err, errlen, "stbl_route_noalloc: %s", cudaGetErrorString(e2));
+                return -1;
+            }
             g_na_addr[dev] = static_cast<unsigned char *>(ptr);
         }
         base = g_na_addr[dev];
@@ -99,18 +106,8 @@ extern "C" int stbl_route_noalloc(const float *router_w, const float *router_bia
     r.xq_a = r.xq_b = base + kNaXq;
     r.xs_a = r.xs_b = reinterpret_cast<float *>(base + kNaXs);
     r.blk_a = r.blk_b = 128, r.pow2_a = r.pow2_b = 0;
-    r.done = reinterpret_cast<unsigned int *>(base + kNaDone);
-    r.status = reinterpret_cast<uint32_t *>(base + kNaDone + 4);
-    // the last-CTA ticket must start at zero (a call cut short could have left it set)
-    cudaError_t e = cudaMemsetAsync(base + kNaDone, 0, 8, stream);
-    if (e == cudaSuccess) {
-        const int epc = (kRouterThreads / 32) / r.ksplit;
-        const int grid = (E + epc - 1) / epc;
-        const int TW = (T + 31) / 32;
-        const int smem = 2 * (kRouterThreads / 32) * E * 4 + T * topk * 4 + 4 * E * 4 + E * TW * 4;
-        void *args[] = {&r};
-        e = cudaLaunchKernel((const void *)router_kernel, dim3(grid), dim3(kRouterThreads), args, smem, stream);
-    }
+    r.status = reinterpret_cast<uint32_t *>(base + kNaStatus);
+    const cudaError_t e = launch_router(r, stream, false);
     if (e != cudaSuccess) {
         if (err && errlen > 0) snprintf(err, errlen, "stbl_route_noalloc: %s", cudaGetErrorString(e));
         return -1;

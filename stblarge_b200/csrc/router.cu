@@ -1,19 +1,26 @@
-// Router, top-k selection and bucketed dispatch of the MoE layer: one launch.
+// Router, top-k selection and bucketed dispatch of the MoE layer: two launches.
 //
-// Phase A (every CTA): router logits of a few experts (one warp per hidden slice, the slices combined
-// in slice order in shared memory) and their scores, for all tokens at once; FP8 activation
-// quantization of x for the expert kernels.  Phase B (the last CTA to finish phase A, by an atomic
-// ticket): group-limited top-k, routing weights, and the bucketed permutation + chunk table.
+// router_logits_kernel (many CTAs, clusters of ksplit): router logits and scores.  A CTA owns 8
+// experts and one hidden slice; it streams its 8 weight rows and the tokens' x slices into shared
+// memory with bulk copies (the weight copies start before the programmatic-launch wait, since the
+// router weights never change), computes the slice partials of 4 experts x 8 tokens per warp from
+// registers, and the ksplit CTAs of a cluster add their partials in slice order through distributed
+// shared memory.  It also does the activation quantization of x for the expert kernels.
+// router_select_kernel (one CTA of 512 threads): group-limited top-k per token (a warp per token),
+// routing weights, and the bucketed permutation + chunk table.
 //
 // Replaces the reference's router GEMV, score kernel, blocking device->host copy and host
 // partial_sort (stbl/model.cu:430-452, stbl/kernels.cu:206-214, 437-442): nothing leaves the GPU.
+#include <cooperative_groups.h>
 #include <limits.h>
 
 #include "layer.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace stbl {
 
-// ---- phase B helpers ------------------------------------------------------------------------------
+// ---- selection helpers -----------------------------------------------------------------------------
 
 __device__ __forceinline__ float router_score(float logit, int fn) {
     // double evaluation, one rounding to fp32: bit-identical to the CPU oracle's
@@ -24,50 +31,15 @@ __device__ __forceinline__ float router_score(float logit, int fn) {
 
 __device__ __forceinline__ bool beats(float va, int a, float vb, int b) { return va > vb || (va == vb && a < b); }
 
-// ---- phase A --------------------------------------------------------------------------------------
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
-// One warp computes the slice ks of expert e's logits for tokens t0 .. t0+nt-1: lane l takes hidden
-// positions base + 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, then the 32 lane
-// sums are added by an xor butterfly.  oracle/moe_oracle.c restates exactly this order, so the logits
-// agree bit for bit.  The weight loads of a slice are issued before any use (7 per lane in flight).
-__device__ __forceinline__ void logits_slice(const RouterParams &p, int e, int ks, int t0, int nt, int lane,
-                                             float *out /* [8] per token, lane 0 */) {
-    const int slice = p.H / p.ksplit;
-    const float *w = p.W + (size_t)e * p.H + (size_t)ks * slice;
-    const uint16_t *x = p.x + (size_t)ks * slice;
-    float acc[8];
-#pragma unroll
-    for (int t = 0; t < 8; t++) acc[t] = 0.f;
-    const int n_it = slice / 128;
-    for (int i0 = 0; i0 < n_it; i0 += 7) {
-        float4 w4[7];
-#pragma unroll
-        for (int u = 0; u < 7; u++)
-            if (i0 + u < n_it) w4[u] = __ldg(reinterpret_cast<const float4 *>(w + 128 * (i0 + u) + 4 * lane));
-#pragma unroll
-        for (int u = 0; u < 7; u++) {
-            if (i0 + u < n_it) {
-                const int k = 128 * (i0 + u) + 4 * lane;
-#pragma unroll
-                for (int t = 0; t < 8; t++) {
-                    if (t < nt) {
-                        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)(t0 + t) * p.H + k));
-                        acc[t] = fmaf(w4[u].x, __uint_as_float(xv.x << 16), acc[t]);
-                        acc[t] = fmaf(w4[u].y, __uint_as_float(xv.x & 0xffff0000u), acc[t]);
-                        acc[t] = fmaf(w4[u].z, __uint_as_float(xv.y << 16), acc[t]);
-                        acc[t] = fmaf(w4[u].w, __uint_as_float(xv.y & 0xffff0000u), acc[t]);
-                    }
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < 8; t++) {
-        float v = acc[t];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, o);
-        out[t] = v;
-    }
+// merge two (first, second) key pairs of disjoint sets into the pair of their union
+__device__ __forceinline__ void top2_merge(uint32_t &a1, uint32_t &a2, uint32_t b1, uint32_t b2) {
+    const uint32_t lo = min(a1, b1);
+    a1 = max(a1, b1);
+    a2 = max(lo, max(a2, b2));
 }
 
 // act_quant (ref/kernel.py:35-45) of 128 consecutive values of one token: lane l takes 4 of them.
@@ -92,8 +64,10 @@ __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq,
     if ((k % blk) == 0) xs[(size_t)t * (H / 32) + k / blk] = s;
 }
 
-// exclusive scan over n <= 2 * kRouterThreads values in smem (in place); returns the total
+// exclusive scan over n <= 2 * NTHREADS values in smem (in place); returns the total
+template <int NTHREADS>
 __device__ int block_exclusive_scan(int *v, int n, int *warp_tot) {
+    constexpr int NW = NTHREADS / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int a = 2 * tid < n ? v[2 * tid] : 0, b = 2 * tid + 1 < n ? v[2 * tid + 1] : 0;
     int incl = a + b;
@@ -105,17 +79,17 @@ __device__ int block_exclusive_scan(int *v, int n, int *warp_tot) {
     if (lane == 31) warp_tot[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-        int w = lane < kRouterThreads / 32 ? warp_tot[lane] : 0;
+        int w = lane < NW ? warp_tot[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, w, o);
             if (lane >= o) w += y;
         }
-        if (lane < kRouterThreads / 32) warp_tot[lane] = w;  // inclusive per warp
+        if (lane < NW) warp_tot[lane] = w;  // inclusive per warp
     }
     __syncthreads();
     const int base = (warp ? warp_tot[warp - 1] : 0) + incl - (a + b);
-    const int total = warp_tot[kRouterThreads / 32 - 1];
+    const int total = warp_tot[NW - 1];
     __syncthreads();
     if (2 * tid < n) v[2 * tid] = base;
     if (2 * tid + 1 < n) v[2 * tid + 1] = base + a;
@@ -123,103 +97,236 @@ __device__ int block_exclusive_scan(int *v, int n, int *warp_tot) {
     return total;
 }
 
-// ---- the kernel -----------------------------------------------------------------------------------
+// ---- logits kernel -----------------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
+// Shared memory of router_logits_kernel: weight rows [8][slice] f32 | x rows [min(T, 32)][slice] bf16 |
+// slice partials [8][T] f32 | two mbarriers.
+__host__ __device__ inline size_t router_logits_smem(int H, int T) {
+    const int slice = H / router_ksplit(H), xr = T < kLgRound ? T : kLgRound;
+    return (size_t)kLgExperts * slice * 4 + (size_t)xr * slice * 2 + (size_t)kLgExperts * T * 4 + 16;
+}
+
+// Logits of experts e0 .. e0+7 over hidden slice ks (= the CTA's rank in its cluster of ksplit).
+// Warp w takes experts e0 + 4 (w & 1) .. +3 and a quarter of the staged tokens; lane l of it
+// accumulates, for each (expert, token), the products at hidden positions base + 128 i + 4 l + j
+// (i ascending, j = 0..3) by fused multiply-add, and the 32 lane sums of a (expert, token) are added
+// by the xor-butterfly tree (computed as a reduce-scatter, which adds the same pairs).  The cluster's
+// CTAs then add their slice sums in slice order.  oracle/moe_oracle.c restates exactly this order,
+// so the logits agree bit for bit.
+__global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int abort_flag;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nwarps_grid = gridDim.x * (kRouterThreads / 32);
-    const int gwarp = blockIdx.x * (kRouterThreads / 32) + warp;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ks = (int)cluster.block_rank();
+    const int eb = blockIdx.x / p.ksplit;
+    const int slice = p.H / p.ksplit, n_it = slice / 128;
+    const int e0 = eb * kLgExperts, ne = min(kLgExperts, p.E - e0);
+    const int xr = min(p.T, kLgRound);
+    float *w_s = reinterpret_cast<float *>(smem);
+    uint16_t *x_s = reinterpret_cast<uint16_t *>(w_s + kLgExperts * slice);
+    float *part = reinterpret_cast<float *>(x_s + (size_t)xr * slice);  // [8][T]
+    uint64_t *bar_w = reinterpret_cast<uint64_t *>(part + kLgExperts * p.T);
+    uint64_t *bar_x = bar_w + 1;
 
+    if (tid == 0) {
+        abort_flag = 0;
+        mbar_init(bar_w, 1);
+        mbar_init(bar_x, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // the router weights are never written by a kernel: stream them before the programmatic wait
+    if (warp == 0) {
+        if (lane == 0) mbar_arrive_expect_tx(bar_w, (uint32_t)(ne * slice * 4));
+        __syncwarp();
+        if (lane < ne) bulk_g2s(w_s + lane * slice, p.W + (size_t)(e0 + lane) * p.H + (size_t)ks * slice, slice * 4, bar_w);
+    }
     pdl_wait();  // x may come from the kernel before this one
+    auto stage_x = [&](int r0, int nr) {
+        if (warp == 0) {
+            if (lane == 0) mbar_arrive_expect_tx(bar_x, (uint32_t)(nr * slice * 2));
+            __syncwarp();
+            for (int t = lane; t < nr; t += 32)
+                bulk_g2s(x_s + (size_t)t * slice, p.x + (size_t)(r0 + t) * p.H + (size_t)ks * slice, slice * 2, bar_x);
+        }
+    };
+    stage_x(0, xr);
     pdl_launch_dependents();
 
-    // phase A: logits of experts_per_cta experts (ksplit warps each, slices combined in slice order
-    // through shared memory), their scores, activation quantization of x
-    __shared__ float part[kRouterThreads / 32][8];
-    const int epc = (kRouterThreads / 32) / p.ksplit;  // experts per CTA
-    const int e_loc = warp / p.ksplit, ks = warp % p.ksplit;
-    const int e = blockIdx.x * epc + e_loc;
-    for (int t0 = 0; t0 < p.T; t0 += 8) {
-        const int nt = min(8, p.T - t0);
-        float o[8];
-        if (e < p.E) logits_slice(p, e, ks, t0, nt, lane, o);
-        if (lane == 0 && e < p.E)
-#pragma unroll
-            for (int t = 0; t < 8; t++) part[warp][t] = o[t];
-        __syncthreads();
-        if (tid < epc * nt) {
-            const int el = tid / nt, t = tid % nt, ee = blockIdx.x * epc + el;
-            if (ee < p.E) {
-                float logit = part[el * p.ksplit][t];
-                for (int k2 = 1; k2 < p.ksplit; k2++) logit = logit + part[el * p.ksplit + k2][t];
-                p.scores[(size_t)(t0 + t) * p.E + ee] = router_score(logit, p.score_fn);
-            }
+    // activation quantization of x for the expert kernels, spread over every warp of the grid
+    {
+        const int nwarps_grid = gridDim.x * (kLgThreads / 32), gwarp = blockIdx.x * (kLgThreads / 32) + warp;
+        const int groups = p.T * (p.H / 128);
+        for (int u = gwarp; u < groups; u += nwarps_grid) {
+            quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane);
+            if (p.xq_b != p.xq_a)
+                quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane);
         }
-        __syncthreads();
-    }
-    const int groups = p.T * (p.H / 128);
-    for (int u = gwarp; u < groups; u += nwarps_grid) {
-        quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane);
-        if (p.xq_b != p.xq_a)
-            quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane);
     }
 
-    // last-CTA ticket
-    __shared__ int is_last;
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        is_last = atomicAdd(p.done, 1u) == gridDim.x - 1;
+    bool ok = mbar_wait(bar_w, 0, &abort_flag);
+    const int q = warp & 1, tg = warp >> 1;
+    int last_round = 0;  // the last round whose rows were requested
+    for (int r0 = 0, round = 0; r0 < p.T; r0 += kLgRound, round++) {
+        const int nr = min(kLgRound, p.T - r0);
+        if (round > 0) {
+            __syncthreads();  // every warp is done with the previous round's rows
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            stage_x(r0, nr);
+            last_round = round;
+        }
+        ok = mbar_wait(bar_x, round & 1, &abort_flag) && ok;
+        ok = __syncthreads_and(ok ? 1 : 0) != 0;  // uniform: every warp stops if one gave up
+        if (!ok) break;
+        const int tpg = (nr + 3) / 4, tb = tg * tpg, nt = min(tpg, nr - tb);
+        if (nt > 0 && 4 * q < ne) {
+            float acc[32];
+#pragma unroll
+            for (int v = 0; v < 32; v++) acc[v] = 0.f;
+            const float *wq = w_s + (size_t)(4 * q) * slice + 4 * lane;
+            const uint16_t *xq = x_s + (size_t)tb * slice + 4 * lane;
+            for (int i = 0; i < n_it; i++) {
+                float4 w4[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) w4[e] = *reinterpret_cast<const float4 *>(wq + (size_t)e * slice + 128 * i);
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    if (t < nt) {
+                        const uint2 xv = *reinterpret_cast<const uint2 *>(xq + (size_t)t * slice + 128 * i);
+                        const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xffff0000u);
+                        const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xffff0000u);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            float a = acc[e * 8 + t];
+                            a = fmaf(w4[e].x, x0, a);
+                            a = fmaf(w4[e].y, x1, a);
+                            a = fmaf(w4[e].z, x2, a);
+                            a = fmaf(w4[e].w, x3, a);
+                            acc[e * 8 + t] = a;
+                        }
+                    }
+                }
+            }
+            const float sum = warp_reduce_scatter<32>(acc, lane);  // lane l: expert l >> 3, token l & 7
+            const int e = 4 * q + (lane >> 3), t = lane & 7;
+            if (t < nt && e < ne) part[e * p.T + r0 + tb + t] = sum;
+        }
     }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
+    if (!ok && tid == 0) {
+        atomicOr(p.status, kErrWaitTimeout);
+        abort_flag = 1;
+    }
 
-    // phase B
+    // slice partials of the cluster, added in slice order; scores
+    cluster.sync();
+    for (int u = ks + p.ksplit * tid; u < kLgExperts * p.T; u += p.ksplit * kLgThreads) {
+        const int el = u / p.T, t = u % p.T;
+        if (el < ne) {
+            float logit = cluster.map_shared_rank(part, 0)[u];
+            for (int k2 = 1; k2 < p.ksplit; k2++) logit = logit + cluster.map_shared_rank(part, k2)[u];
+            p.scores[(size_t)t * p.E + e0 + el] = router_score(logit, p.score_fn);
+        }
+    }
+    cluster.sync();  // the other CTAs have read this CTA's partials
+
+    // a CTA that gave up waits (bounded) for its own copies before its shared memory is released
+    if (abort_flag && tid == 0) {
+        int dummy = 0;
+        if (!mbar_wait(bar_w, 0, &dummy) || !mbar_wait(bar_x, last_round & 1, &dummy)) atomicOr(p.status, kErrCopyTimeout);
+    }
+}
+
+// ---- selection + dispatch kernel ---------------------------------------------------------------------
+
+__host__ __device__ inline size_t router_select_smem(int T, int E, int K) {
+    const int TW = (T + 31) / 32;
+    return (size_t)T * K * 4 + 4 * (size_t)E * 4 + (size_t)E * TW * 4;
+}
+
+__global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int warp_tot[kSelThreads / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();  // scores and quantized x of the logits kernel
+    pdl_launch_dependents();
+
     const int E = p.E, T = p.T, K = p.topk;
     const int TW = (T + 31) / 32;
-    float *sb = reinterpret_cast<float *>(smem);                    // [8][E] biased scores
-    float *sc = sb + (kRouterThreads / 32) * E;                      // [8][E] scores
-    int *sidx = reinterpret_cast<int *>(sc + (kRouterThreads / 32) * E);  // [T][K]
-    int *cnt = sidx + T * K;                                         // [E]
-    int *off = cnt + E;                                              // [E]
-    int *nch = off + E;                                              // [E]
-    int *choff = nch + E;                                            // [E]
-    uint32_t *bm = reinterpret_cast<uint32_t *>(choff + E);          // [E][TW]
-    __shared__ int warp_tot[kRouterThreads / 32];
+    int *sidx = reinterpret_cast<int *>(smem);  // [T][K]
+    int *cnt = sidx + T * K;                    // [E]
+    int *off = cnt + E;                         // [E]
+    int *nch = off + E;                         // [E]
+    int *choff = nch + E;                       // [E]
+    uint32_t *bm = reinterpret_cast<uint32_t *>(choff + E);  // [E][TW]
 
     const int EJ = (E + 31) / 32;
     const int gsz = E / p.n_groups;
     const bool grouped = p.n_groups > 1 && p.topk_groups < p.n_groups;
-    for (int t = warp; t < T; t += kRouterThreads / 32) {
-        float *wb = sb + warp * E, *ws = sc + warp * E;
-        float bv[kMaxExperts / 32];
+    // group sizes with a register-level top-2: a power of two up to 32 (segments of lanes within a
+    // register) or a multiple of 32 (whole registers); others scan sequentially
+    const bool g_pow2 = gsz <= 32 && (gsz & (gsz - 1)) == 0;
+    const bool g_mult = gsz % 32 == 0;
+    for (int t = warp; t < T; t += kSelThreads / 32) {
+        // lane l holds expert l + 32 j: key of the biased score (selection) and the score (weights)
+        uint32_t key[kMaxExperts / 32];
+        float sv[kMaxExperts / 32];
         uint32_t has = 0;
 #pragma unroll
         for (int j = 0; j < kMaxExperts / 32; j++) {
             const int e = lane + 32 * j;
-            bv[j] = 0.f;
+            key[j] = 0u;
+            sv[j] = 0.f;
             if (j < EJ && e < E) {
                 const float s = __ldcg(p.scores + (size_t)t * E + e);
-                const float b = s + __ldg(p.bias + e);
-                wb[e] = b;
-                ws[e] = s;
-                bv[j] = b;
+                sv[j] = s;
+                key[j] = float_key(s + __ldg(p.bias + e) + 0.0f);
                 has |= 1u << j;
             }
         }
-        __syncwarp();
         uint32_t keepg = 0xffffffffu;
         if (grouped) {
+            // group score = top-1 + top-2 of the biased scores in the group (values only); lane g
+            // ends with group g's score
             float gs = 0.f;
-            if (lane < p.n_groups) {
-                int b1 = -1, b2 = -1;
-                for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
-                    if (b1 < 0 || beats(wb[e], e, wb[b1], b1)) b2 = b1, b1 = e;
-                    else if (b2 < 0 || beats(wb[e], e, wb[b2], b2)) b2 = e;
+            if (g_mult) {
+                const int m = gsz / 32;
+                for (int g = 0; g < p.n_groups; g++) {
+                    uint32_t l1 = 0u, l2 = 0u;
+#pragma unroll
+                    for (int j = 0; j < kMaxExperts / 32; j++)
+                        if (j >= g * m && j < (g + 1) * m) top2_merge(l1, l2, key[j], 0u);
+                    const uint32_t m1 = __reduce_max_sync(0xffffffffu, l1);
+                    const uint32_t tie = __ballot_sync(0xffffffffu, l1 == m1);
+                    const uint32_t m2 = __popc(tie) > 1 ? m1 : __reduce_max_sync(0xffffffffu, l1 == m1 ? l2 : l1);
+                    if (lane == g) gs = key_float(m1) + key_float(m2);
                 }
-                gs = gsz > 1 ? wb[b1] + wb[b2] : wb[b1];
+            } else if (g_pow2) {
+                const int segs = 32 / gsz;  // groups per register
+#pragma unroll
+                for (int j = 0; j < kMaxExperts / 32; j++) {
+                    if (j < EJ) {
+                        uint32_t a1 = key[j], a2 = 0u;
+                        for (int o = gsz / 2; o > 0; o >>= 1) {
+                            const uint32_t b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+                            const uint32_t b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+                            top2_merge(a1, a2, b1, b2);
+                        }
+                        const float v = key_float(a1) + key_float(a2);
+                        // group j * segs + s is held by lanes s * gsz ..; lane g takes its group's score
+                        const float got = __shfl_sync(0xffffffffu, v, (lane % segs) * gsz);
+                        if (lane / segs == j) gs = got;
+                    }
+                }
+            } else if (lane < p.n_groups) {
+                int b1 = -1, b2 = -1;
+                float v1 = 0.f, v2 = 0.f;
+                for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
+                    const float b = __ldcg(p.scores + (size_t)t * E + e) + __ldg(p.bias + e);
+                    if (b1 < 0 || beats(b, e, v1, b1)) b2 = b1, v2 = v1, b1 = e, v1 = b;
+                    else if (b2 < 0 || beats(b, e, v2, b2)) b2 = e, v2 = b;
+                }
+                gs = v1 + v2;
             }
             int rank = 0;
             for (int h = 0; h < p.n_groups; h++) {
@@ -235,25 +342,26 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
             if (((has >> j) & 1u) && ((keepg >> (e / gsz)) & 1u)) avail |= 1u << j;
         }
         int mine = -1;
+        float s_mine = 0.f;
         for (int i = 0; i < K; i++) {
+            uint32_t bk = 0u;
             int bj = -1;
-            float bvv = 0.f;
+            float bs = 0.f;
 #pragma unroll
             for (int j = 0; j < kMaxExperts / 32; j++)
-                if (((avail >> j) & 1u) && (bj < 0 || bv[j] > bvv)) bj = j, bvv = bv[j];
-            const uint32_t key = bj >= 0 ? float_key(bvv + 0.0f) : 0u;
-            const uint32_t mk = __reduce_max_sync(0xffffffffu, key);
-            const int cand = (bj >= 0 && key == mk) ? lane + 32 * bj : INT_MAX;
+                if (((avail >> j) & 1u) && (bj < 0 || key[j] > bk)) bj = j, bk = key[j], bs = sv[j];
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
+            const int cand = (bj >= 0 && bk == mk) ? lane + 32 * bj : INT_MAX;
             int win = __reduce_min_sync(0xffffffffu, cand);
             if (win == INT_MAX) {  // fewer candidates than topk: cannot happen for a validated layer
                 if (lane == 0) atomicOr(p.status, kErrBadTable);
                 win = 0;
             }
             if (lane == (win & 31)) avail &= ~(1u << (win >> 5));
-            if (lane == i) mine = win;
+            const float s_win = __shfl_sync(0xffffffffu, bs, win & 31);
+            if (lane == i) mine = win, s_mine = s_win;
         }
         // weights: unbiased scores normalised in top-k order (stbl/model.cu:450-451, 527-530)
-        const float s_mine = (lane < K) ? ws[mine] : 0.f;
         float sum = 0.f;
         for (int i = 0; i < K; i++) sum += __shfl_sync(0xffffffffu, s_mine, i);
         if (lane < K) {
@@ -264,38 +372,37 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
             p.wts[t * K + lane] = wt;
             sidx[t * K + lane] = mine;
         }
-        __syncwarp();
     }
     __syncthreads();
 
     // bucketed dispatch: counts, offsets, stable rank by token through a per-expert token bitmap
-    for (int e = tid; e < E; e += kRouterThreads) cnt[e] = 0;
-    for (int i = tid; i < E * TW; i += kRouterThreads) bm[i] = 0;
+    for (int e = tid; e < E; e += kSelThreads) cnt[e] = 0;
+    for (int i = tid; i < E * TW; i += kSelThreads) bm[i] = 0;
     __syncthreads();
-    for (int a = tid; a < T * K; a += kRouterThreads) {
+    for (int a = tid; a < T * K; a += kSelThreads) {
         const int e = sidx[a], t = a / K;
         atomicAdd(&cnt[e], 1);
         atomicOr(&bm[e * TW + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
-    for (int e = tid; e < E; e += kRouterThreads) {
+    for (int e = tid; e < E; e += kSelThreads) {
         off[e] = cnt[e];
         nch[e] = (cnt[e] + p.nt_routed - 1) / p.nt_routed;
         choff[e] = nch[e];
     }
     __syncthreads();
-    block_exclusive_scan(off, E, warp_tot);
-    const int routed_chunks = block_exclusive_scan(choff, E, warp_tot);
-    for (int a = tid; a < T * K; a += kRouterThreads) {
+    block_exclusive_scan<kSelThreads>(off, E, warp_tot);
+    const int routed_chunks = block_exclusive_scan<kSelThreads>(choff, E, warp_tot);
+    for (int a = tid; a < T * K; a += kSelThreads) {
         const int e = sidx[a], t = a / K;
         int rank = __popc(bm[e * TW + (t >> 5)] & ((1u << (t & 31)) - 1u));
         for (int w = 0; w < (t >> 5); w++) rank += __popc(bm[e * TW + w]);
         p.perm[off[e] + rank] = a;
     }
     const int ns = p.has_shared ? (T + p.nt_shared - 1) / p.nt_shared : 0;
-    for (int i = tid; i < ns; i += kRouterThreads)
+    for (int i = tid; i < ns; i += kSelThreads)
         p.chunks[i] = Chunk{E, T * K + i * p.nt_shared, min(p.nt_shared, T - i * p.nt_shared), 0};
-    for (int e = tid; e < E; e += kRouterThreads) {
+    for (int e = tid; e < E; e += kSelThreads) {
         p.counts[e] = cnt[e];
         p.offsets[e] = off[e];
         for (int c = 0; c < nch[e]; c++)
@@ -305,8 +412,40 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(RouterParams p) 
         p.offsets[E] = T * K;
         p.n_chunks[0] = ns + routed_chunks;
         p.n_chunks[1] = ns;
-        *p.done = 0;
     }
+}
+
+// ---- host side ---------------------------------------------------------------------------------------
+
+cudaError_t router_setup() {
+    return cudaFuncSetAttribute((const void *)router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)router_logits_smem(4 * kLgMaxSlice, kRouterMaxTokens));
+}
+
+cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first) {
+    void *args[] = {&r};
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(r.ksplit * ((r.E + kLgExperts - 1) / kLgExperts));
+    cfg.blockDim = dim3(kLgThreads);
+    cfg.dynamicSmemBytes = router_logits_smem(r.H, r.T);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = r.ksplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_first ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelExC(&cfg, (const void *)router_logits_kernel, args);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kSelThreads);
+    cfg.dynamicSmemBytes = router_select_smem(r.T, r.E, r.topk);
+    cfg.attrs = attr + 1;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, (const void *)router_select_kernel, args);
 }
 
 }  // namespace stbl
