@@ -64,39 +64,6 @@ __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq,
     if ((k % blk) == 0) xs[(size_t)t * (H / 32) + k / blk] = s;
 }
 
-// exclusive scan over n <= 2 * NTHREADS values in smem (in place); returns the total
-template <int NTHREADS>
-__device__ int block_exclusive_scan(int *v, int n, int *warp_tot) {
-    constexpr int NW = NTHREADS / 32;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int a = 2 * tid < n ? v[2 * tid] : 0, b = 2 * tid + 1 < n ? v[2 * tid + 1] : 0;
-    int incl = a + b;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < NW ? warp_tot[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += y;
-        }
-        if (lane < NW) warp_tot[lane] = w;  // inclusive per warp
-    }
-    __syncthreads();
-    const int base = (warp ? warp_tot[warp - 1] : 0) + incl - (a + b);
-    const int total = warp_tot[NW - 1];
-    __syncthreads();
-    if (2 * tid < n) v[2 * tid] = base;
-    if (2 * tid + 1 < n) v[2 * tid + 1] = base + a;
-    __syncthreads();
-    return total;
-}
-
 // ---- logits kernel -----------------------------------------------------------------------------------
 
 // Shared memory of router_logits_kernel: weight rows [8][slice] f32 | x rows [min(T, 32)][slice] bf16 |
@@ -106,12 +73,55 @@ __host__ __device__ inline size_t router_logits_smem(int H, int T) {
     return (size_t)kLgExperts * slice * 4 + (size_t)xr * slice * 2 + (size_t)kLgExperts * T * 4 + 16;
 }
 
+// Slice partials of EPW experts x up to NT tokens by one warp, in the order router_logits_kernel
+// states: lane l accumulates the products at positions 128 i + 4 l + j (i ascending, j = 0..3) by
+// fused multiply-add, then the lane sums of each (expert, token) are added by the xor-butterfly tree
+// (a reduce-scatter adds the same pairs).  w: the first expert's row of the slice in shared memory
+// (rows slice floats apart); x: the first token's row (slice bf16 apart); the sums go to
+// part[e * T + t0 + t] for e < ne, t < nt.
+template <int EPW, int NT>
+__device__ __forceinline__ void logits_tile(const float *w, const uint16_t *x, int slice, int n_it, int nt, int ne,
+                                            int lane, float *part, int T, int t0) {
+    constexpr int V = EPW * NT;
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; v++) acc[v] = 0.f;
+    const float *wl = w + 4 * lane;
+    const uint16_t *xl = x + 4 * lane;
+    for (int i = 0; i < n_it; i++) {
+        float4 w4[EPW];
+#pragma unroll
+        for (int e = 0; e < EPW; e++) w4[e] = *reinterpret_cast<const float4 *>(wl + (size_t)e * slice + 128 * i);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            if (t < nt) {
+                const uint2 xv = *reinterpret_cast<const uint2 *>(xl + (size_t)t * slice + 128 * i);
+                const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xffff0000u);
+                const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xffff0000u);
+#pragma unroll
+                for (int e = 0; e < EPW; e++) {
+                    float a = acc[e * NT + t];
+                    a = fmaf(w4[e].x, x0, a);
+                    a = fmaf(w4[e].y, x1, a);
+                    a = fmaf(w4[e].z, x2, a);
+                    a = fmaf(w4[e].w, x3, a);
+                    acc[e * NT + t] = a;
+                }
+            }
+        }
+    }
+    const float sum = warp_reduce_scatter<V>(acc, lane);  // lane l: value l / (32 / V)
+    constexpr int LPV = 32 / V;
+    const int v = lane / LPV, e = v / NT, t = v % NT;
+    if (lane % LPV == 0 && t < nt && e < ne) part[e * T + t0 + t] = sum;
+}
+
 // Logits of experts e0 .. e0+7 over hidden slice ks (= the CTA's rank in its cluster of ksplit).
-// Warp w takes experts e0 + 4 (w & 1) .. +3 and a quarter of the staged tokens; lane l of it
-// accumulates, for each (expert, token), the products at hidden positions base + 128 i + 4 l + j
-// (i ascending, j = 0..3) by fused multiply-add, and the 32 lane sums of a (expert, token) are added
-// by the xor-butterfly tree (computed as a reduce-scatter, which adds the same pairs).  The cluster's
-// CTAs then add their slice sums in slice order.  oracle/moe_oracle.c restates exactly this order,
+// The 8 warps split the (expert, staged token) pairs by the number of tokens (logits_tile); lane l
+// of a warp accumulates, for each of its (expert, token) pairs, the products at hidden positions
+// base + 128 i + 4 l + j (i ascending, j = 0..3) by fused multiply-add, and the 32 lane sums of a
+// pair are added by the xor-butterfly tree.  The cluster's CTAs then add their slice sums in slice
+// order.  oracle/moe_oracle.c restates exactly this order,
 // so the logits agree bit for bit.
 __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -166,7 +176,6 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
     }
 
     bool ok = mbar_wait(bar_w, 0, &abort_flag);
-    const int q = warp & 1, tg = warp >> 1;
     int last_round = 0;  // the last round whose rows were requested
     for (int r0 = 0, round = 0; r0 < p.T; r0 += kLgRound, round++) {
         const int nr = min(kLgRound, p.T - r0);
@@ -179,38 +188,27 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
         ok = mbar_wait(bar_x, round & 1, &abort_flag) && ok;
         ok = __syncthreads_and(ok ? 1 : 0) != 0;  // uniform: every warp stops if one gave up
         if (!ok) break;
-        const int tpg = (nr + 3) / 4, tb = tg * tpg, nt = min(tpg, nr - tb);
-        if (nt > 0 && 4 * q < ne) {
-            float acc[32];
-#pragma unroll
-            for (int v = 0; v < 32; v++) acc[v] = 0.f;
-            const float *wq = w_s + (size_t)(4 * q) * slice + 4 * lane;
-            const uint16_t *xq = x_s + (size_t)tb * slice + 4 * lane;
-            for (int i = 0; i < n_it; i++) {
-                float4 w4[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) w4[e] = *reinterpret_cast<const float4 *>(wq + (size_t)e * slice + 128 * i);
-#pragma unroll
-                for (int t = 0; t < 8; t++) {
-                    if (t < nt) {
-                        const uint2 xv = *reinterpret_cast<const uint2 *>(xq + (size_t)t * slice + 128 * i);
-                        const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xffff0000u);
-                        const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xffff0000u);
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            float a = acc[e * 8 + t];
-                            a = fmaf(w4[e].x, x0, a);
-                            a = fmaf(w4[e].y, x1, a);
-                            a = fmaf(w4[e].z, x2, a);
-                            a = fmaf(w4[e].w, x3, a);
-                            acc[e * 8 + t] = a;
-                        }
-                    }
-                }
+        // work split of the round by its token count: (experts, tokens) per warp
+        if (nr <= 4) {  // a warp per expert
+            if (warp < ne) {
+                if (nr <= 2) logits_tile<1, 2>(w_s + (size_t)warp * slice, x_s, slice, n_it, nr, ne - warp, lane, part + warp * p.T, p.T, r0);
+                else logits_tile<1, 4>(w_s + (size_t)warp * slice, x_s, slice, n_it, nr, ne - warp, lane, part + warp * p.T, p.T, r0);
             }
-            const float sum = warp_reduce_scatter<32>(acc, lane);  // lane l: expert l >> 3, token l & 7
-            const int e = 4 * q + (lane >> 3), t = lane & 7;
-            if (t < nt && e < ne) part[e * p.T + r0 + tb + t] = sum;
+        } else if (nr <= 8) {  // 2 experts x half of the tokens
+            const int e_lo = 2 * (warp & 3), tpg = (nr + 1) / 2, tb = (warp >> 2) * tpg, nt = min(tpg, nr - tb);
+            if (e_lo < ne && nt > 0)
+                logits_tile<2, 4>(w_s + (size_t)e_lo * slice, x_s + (size_t)tb * slice, slice, n_it, nt, ne - e_lo, lane,
+                                  part + e_lo * p.T, p.T, r0 + tb);
+        } else {  // 4 experts x a quarter of the tokens
+            const int e_lo = 4 * (warp & 1), tpg = (nr + 3) / 4, tb = (warp >> 1) * tpg, nt = min(tpg, nr - tb);
+            if (e_lo < ne && nt > 0) {
+                if (nr <= 16)
+                    logits_tile<4, 4>(w_s + (size_t)e_lo * slice, x_s + (size_t)tb * slice, slice, n_it, nt, ne - e_lo, lane,
+                                      part + e_lo * p.T, p.T, r0 + tb);
+                else
+                    logits_tile<4, 8>(w_s + (size_t)e_lo * slice, x_s + (size_t)tb * slice, slice, n_it, nt, ne - e_lo, lane,
+                                      part + e_lo * p.T, p.T, r0 + tb);
+            }
         }
     }
     if (!ok && tid == 0) {
@@ -239,179 +237,245 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
 
 // ---- selection + dispatch kernel ---------------------------------------------------------------------
 
+
+// Group-limited top-k of token t by one warp (stbl/model.cu:444-452 with the DeepSeek-V3 group limit):
+// lane l holds experts l + 32 j (j < EJ) as keys of their biased scores (float_key order) and their
+// unbiased scores.  The group score is the sum of the group's two largest biased scores; the
+// topk_groups best groups are kept (ties to the lower group id), then the topk best experts of the
+// kept groups are taken in order (ties to the lower expert id), and their unbiased scores,
+// normalised in that order, times route_scale are the weights.  Written for latency: one token is
+// a chain of warp collectives (about 25 cycles each), so independent collectives are issued
+// unconditionally and the per-lane argmax is a tree.
+template <int EJ>
+__device__ __forceinline__ void select_token(const RouterParams &p, int t, int lane, int *sidx, int *cnt, uint32_t *bm,
+                                             int TW, bool live) {
+    const int E = p.E, K = p.topk;
+    const uint32_t lane_bit = 1u << lane;
+    uint32_t key[EJ];
+    float sv[EJ];
+#pragma unroll
+    for (int j = 0; j < EJ; j++) {
+        const int e = lane + 32 * j;
+        key[j] = 0u;  // below every float's key: not selectable
+        sv[j] = 0.f;
+        if (e < E) {
+            const float s = __ldcg(p.scores + (size_t)t * E + e);
+            sv[j] = s;
+            key[j] = float_key(s + __ldg(p.bias + e) + 0.0f);
+        }
+    }
+    if (p.n_groups > 1 && p.topk_groups < p.n_groups) {
+        const int gsz = E / p.n_groups;
+        const bool pow2 = (gsz & (gsz - 1)) == 0;
+        // group score = top-1 + top-2 of the group's biased scores (values only); lane g ends with
+        // group g's score
+        float gs = 0.f;
+        if (pow2 && gsz >= 32) {
+            // a group is m whole registers: a tree of top-2 merges over them, then over the lanes
+            const int m = gsz >> 5;
+            uint32_t a1[EJ], a2[EJ];
+#pragma unroll
+            for (int j = 0; j < EJ; j++) a1[j] = key[j], a2[j] = 0u;
+#pragma unroll
+            for (int s = 1; s < EJ; s *= 2)
+                if (s < m)
+#pragma unroll
+                    for (int j = 0; j + s < EJ; j += 2 * s) top2_merge(a1[j], a2[j], a1[j + s], a2[j + s]);
+            // every register's lane-wide top-2 (only group leaders j = g m are used): second largest =
+            // the largest after the lowest lane holding the maximum swaps in its own second
+#pragma unroll
+            for (int j = 0; j < EJ; j++) {
+                const uint32_t m1 = __reduce_max_sync(0xffffffffu, a1[j]);
+                const uint32_t bal = __ballot_sync(0xffffffffu, a1[j] == m1);
+                const uint32_t m2 = __reduce_max_sync(0xffffffffu, (bal & (0u - bal)) == lane_bit ? a2[j] : a1[j]);
+                if (lane * m == j) gs = key_float(m1) + key_float(m2);
+            }
+        } else if (pow2) {
+            // a group is a segment of gsz lanes of one register: top-2 merges across the segment
+            const int segs = 32 / gsz, seg_shift = __ffs(segs) - 1;
+#pragma unroll
+            for (int j = 0; j < EJ; j++) {
+                uint32_t a1 = key[j], a2 = 0u;
+                for (int o = gsz / 2; o > 0; o >>= 1) {
+                    const uint32_t b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+                    const uint32_t b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+                    top2_merge(a1, a2, b1, b2);
+                }
+                const float v = key_float(a1) + key_float(a2);
+                // group j * segs + s is held by lanes s * gsz ..; lane g takes its group's score
+                const float got = __shfl_sync(0xffffffffu, v, (lane & (segs - 1)) * gsz);
+                if ((lane >> seg_shift) == j) gs = got;
+            }
+        } else if (lane < p.n_groups) {
+            // other group sizes: lane g scans its group
+            int b1 = -1, b2 = -1;
+            float v1 = 0.f, v2 = 0.f;
+            for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
+                const float b = __ldcg(p.scores + (size_t)t * E + e) + __ldg(p.bias + e);
+                if (b1 < 0 || beats(b, e, v1, b1)) b2 = b1, v2 = v1, b1 = e, v1 = b;
+                else if (b2 < 0 || beats(b, e, v2, b2)) b2 = e, v2 = b;
+            }
+            gs = v1 + v2;
+        }
+        int rank = 0;
+        for (int h = 0; h < p.n_groups; h++) {
+            const float gh = __shfl_sync(0xffffffffu, gs, h);
+            rank += beats(gh, h, gs, lane);
+        }
+        const uint32_t keepg = __ballot_sync(0xffffffffu, lane < p.n_groups && rank < p.topk_groups);
+        // experts of the groups not kept become unselectable
+        if (pow2) {
+            const int gshift = __ffs(gsz) - 1;
+#pragma unroll
+            for (int j = 0; j < EJ; j++)
+                if (!((keepg >> (((lane + 32 * j) >> gshift) & 31)) & 1u)) key[j] = 0u;
+        } else {
+#pragma unroll
+            for (int j = 0; j < EJ; j++)
+                if (!((keepg >> (((lane + 32 * j) / gsz) & 31)) & 1u)) key[j] = 0u;
+        }
+    }
+    int mine = -1;
+    float s_mine = 0.f;
+    for (int i = 0; i < K; i++) {
+        // lane argmax by a tree (ties to the lower register)
+        uint32_t bk[EJ];
+        int bj[EJ];
+#pragma unroll
+        for (int j = 0; j < EJ; j++) bk[j] = key[j], bj[j] = j;
+#pragma unroll
+        for (int s = 1; s < EJ; s *= 2)
+#pragma unroll
+            for (int j = 0; j + s < EJ; j += 2 * s)
+                if (bk[j + s] > bk[j]) bk[j] = bk[j + s], bj[j] = bj[j + s];
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk[0]);
+        const int cand = (mk != 0u && bk[0] == mk) ? lane + 32 * bj[0] : INT_MAX;
+        int win = __reduce_min_sync(0xffffffffu, cand);
+        if (win == INT_MAX) {  // fewer candidates than topk: cannot happen for a validated layer
+            if (lane == 0 && live) atomicOr(p.status, kErrBadTable);
+            win = 0;
+        }
+        const int wj = lane == (win & 31) ? (win >> 5) : -1;
+        float s_own = 0.f;
+#pragma unroll
+        for (int j = 0; j < EJ; j++)
+            if (j == wj) key[j] = 0u, s_own = sv[j];
+        const float s_win = __shfl_sync(0xffffffffu, s_own, win & 31);
+        if (lane == i) mine = win, s_mine = s_win;
+    }
+    // weights: unbiased scores normalised in top-k order (stbl/model.cu:450-451, 527-530)
+    float sum = 0.f;
+    for (int i = 0; i < K; i++) sum += __shfl_sync(0xffffffffu, s_mine, i);
+    if (lane < K) {
+        float wt = s_mine;
+        wt /= sum + 1e-20f;
+        wt *= p.route_scale;
+        if (live) {
+            p.idx[t * K + lane] = mine;
+            p.wts[t * K + lane] = wt;
+        }
+        sidx[t * K + lane] = mine;
+        // dispatch counts and the expert's token bitmap (a token picks an expert at most once)
+        atomicAdd(&cnt[mine], 1);
+        atomicOr(&bm[mine * TW + (t >> 5)], 1u << (t & 31));
+    }
+}
+
 __host__ __device__ inline size_t router_select_smem(int T, int E, int K) {
     const int TW = (T + 31) / 32;
-    return (size_t)T * K * 4 + 4 * (size_t)E * 4 + (size_t)E * TW * 4;
+    return (size_t)T * K * 4 + 2 * (size_t)E * 4 + (size_t)E * TW * 4;
 }
 
 __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ int warp_tot[kSelThreads / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    pdl_wait();  // scores and quantized x of the logits kernel
-    pdl_launch_dependents();
-
     const int E = p.E, T = p.T, K = p.topk;
     const int TW = (T + 31) / 32;
+    const int sh_r = __ffs(p.nt_routed) - 1, sh_s = __ffs(p.nt_shared) - 1;  // chunk sizes: powers of two
     int *sidx = reinterpret_cast<int *>(smem);  // [T][K]
-    int *cnt = sidx + T * K;                    // [E]
-    int *off = cnt + E;                         // [E]
-    int *nch = off + E;                         // [E]
-    int *choff = nch + E;                       // [E]
-    uint32_t *bm = reinterpret_cast<uint32_t *>(choff + E);  // [E][TW]
+    int *cnt = sidx + T * K;                    // [E] assignments per expert
+    int *pk = cnt + E;                          // [E] exclusive scan of assignments | chunks << 16
+    uint32_t *bm = reinterpret_cast<uint32_t *>(pk + E);  // [E][TW] tokens of each expert
+    // registers per lane for E experts, rounded up to a power of two
+    const int ej = E <= 32 ? 1 : E <= 64 ? 2 : E <= 128 ? 4 : E <= 256 ? 8 : 16;
 
-    const int EJ = (E + 31) / 32;
-    const int gsz = E / p.n_groups;
-    const bool grouped = p.n_groups > 1 && p.topk_groups < p.n_groups;
-    // group sizes with a register-level top-2: a power of two up to 32 (segments of lanes within a
-    // register) or a multiple of 32 (whole registers); others scan sequentially
-    const bool g_pow2 = gsz <= 32 && (gsz & (gsz - 1)) == 0;
-    const bool g_mult = gsz % 32 == 0;
-    for (int t = warp; t < T; t += kSelThreads / 32) {
-        // lane l holds expert l + 32 j: key of the biased score (selection) and the score (weights)
-        uint32_t key[kMaxExperts / 32];
-        float sv[kMaxExperts / 32];
-        uint32_t has = 0;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; j++) {
-            const int e = lane + 32 * j;
-            key[j] = 0u;
-            sv[j] = 0.f;
-            if (j < EJ && e < E) {
-                const float s = __ldcg(p.scores + (size_t)t * E + e);
-                sv[j] = s;
-                key[j] = float_key(s + __ldg(p.bias + e) + 0.0f);
-                has |= 1u << j;
+    // Two passes over one copy of the code.  The first runs before the programmatic-launch wait,
+    // while the logits kernel is still computing, on at most one token per warp: it reads whatever
+    // the scores buffer holds and stores nothing to global memory; it only brings this kernel's
+    // instructions into the SM's instruction caches, so that the second, real pass does not stall
+    // on instruction fetches.
+#pragma unroll 1
+    for (int pass = 0; pass < 2; pass++) {
+        const bool live = pass == 1;
+        for (int e = tid; e < E; e += kSelThreads) cnt[e] = 0;
+        for (int i = tid; i < E * TW; i += kSelThreads) bm[i] = 0;
+        if (live) {
+            pdl_wait();  // scores and quantized x of the logits kernel
+            pdl_launch_dependents();
+        }
+        __syncthreads();
+        const int t_end = live ? T : min(T, kSelThreads / 32);
+        for (int t = warp; t < t_end; t += kSelThreads / 32) {
+            switch (ej) {
+                case 1: select_token<1>(p, t, lane, sidx, cnt, bm, TW, live); break;
+                case 2: select_token<2>(p, t, lane, sidx, cnt, bm, TW, live); break;
+                case 4: select_token<4>(p, t, lane, sidx, cnt, bm, TW, live); break;
+                case 8: select_token<8>(p, t, lane, sidx, cnt, bm, TW, live); break;
+                default: select_token<16>(p, t, lane, sidx, cnt, bm, TW, live); break;
             }
         }
-        uint32_t keepg = 0xffffffffu;
-        if (grouped) {
-            // group score = top-1 + top-2 of the biased scores in the group (values only); lane g
-            // ends with group g's score
-            float gs = 0.f;
-            if (g_mult) {
-                const int m = gsz / 32;
-                for (int g = 0; g < p.n_groups; g++) {
-                    uint32_t l1 = 0u, l2 = 0u;
-#pragma unroll
-                    for (int j = 0; j < kMaxExperts / 32; j++)
-                        if (j >= g * m && j < (g + 1) * m) top2_merge(l1, l2, key[j], 0u);
-                    const uint32_t m1 = __reduce_max_sync(0xffffffffu, l1);
-                    const uint32_t tie = __ballot_sync(0xffffffffu, l1 == m1);
-                    const uint32_t m2 = __popc(tie) > 1 ? m1 : __reduce_max_sync(0xffffffffu, l1 == m1 ? l2 : l1);
-                    if (lane == g) gs = key_float(m1) + key_float(m2);
-                }
-            } else if (g_pow2) {
-                const int segs = 32 / gsz;  // groups per register
-#pragma unroll
-                for (int j = 0; j < kMaxExperts / 32; j++) {
-                    if (j < EJ) {
-                        uint32_t a1 = key[j], a2 = 0u;
-                        for (int o = gsz / 2; o > 0; o >>= 1) {
-                            const uint32_t b1 = __shfl_xor_sync(0xffffffffu, a1, o);
-                            const uint32_t b2 = __shfl_xor_sync(0xffffffffu, a2, o);
-                            top2_merge(a1, a2, b1, b2);
-                        }
-                        const float v = key_float(a1) + key_float(a2);
-                        // group j * segs + s is held by lanes s * gsz ..; lane g takes its group's score
-                        const float got = __shfl_sync(0xffffffffu, v, (lane % segs) * gsz);
-                        if (lane / segs == j) gs = got;
-                    }
-                }
-            } else if (lane < p.n_groups) {
-                int b1 = -1, b2 = -1;
-                float v1 = 0.f, v2 = 0.f;
-                for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
-                    const float b = __ldcg(p.scores + (size_t)t * E + e) + __ldg(p.bias + e);
-                    if (b1 < 0 || beats(b, e, v1, b1)) b2 = b1, v2 = v1, b1 = e, v1 = b;
-                    else if (b2 < 0 || beats(b, e, v2, b2)) b2 = e, v2 = b;
-                }
-                gs = v1 + v2;
-            }
-            int rank = 0;
-            for (int h = 0; h < p.n_groups; h++) {
-                const float gh = __shfl_sync(0xffffffffu, gs, h);
-                rank += beats(gh, h, gs, lane);
-            }
-            keepg = __ballot_sync(0xffffffffu, lane < p.n_groups && rank < p.topk_groups);
-        }
-        uint32_t avail = 0;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; j++) {
-            const int e = lane + 32 * j;
-            if (((has >> j) & 1u) && ((keepg >> (e / gsz)) & 1u)) avail |= 1u << j;
-        }
-        int mine = -1;
-        float s_mine = 0.f;
-        for (int i = 0; i < K; i++) {
-            uint32_t bk = 0u;
-            int bj = -1;
-            float bs = 0.f;
-#pragma unroll
-            for (int j = 0; j < kMaxExperts / 32; j++)
-                if (((avail >> j) & 1u) && (bj < 0 || key[j] > bk)) bj = j, bk = key[j], bs = sv[j];
-            const uint32_t mk = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
-            const int cand = (bj >= 0 && bk == mk) ? lane + 32 * bj : INT_MAX;
-            int win = __reduce_min_sync(0xffffffffu, cand);
-            if (win == INT_MAX) {  // fewer candidates than topk: cannot happen for a validated layer
-                if (lane == 0) atomicOr(p.status, kErrBadTable);
-                win = 0;
-            }
-            if (lane == (win & 31)) avail &= ~(1u << (win >> 5));
-            const float s_win = __shfl_sync(0xffffffffu, bs, win & 31);
-            if (lane == i) mine = win, s_mine = s_win;
-        }
-        // weights: unbiased scores normalised in top-k order (stbl/model.cu:450-451, 527-530)
-        float sum = 0.f;
-        for (int i = 0; i < K; i++) sum += __shfl_sync(0xffffffffu, s_mine, i);
-        if (lane < K) {
-            float wt = s_mine;
-            wt /= sum + 1e-20f;
-            wt *= p.route_scale;
-            p.idx[t * K + lane] = mine;
-            p.wts[t * K + lane] = wt;
-            sidx[t * K + lane] = mine;
-        }
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // bucketed dispatch: counts, offsets, stable rank by token through a per-expert token bitmap
-    for (int e = tid; e < E; e += kSelThreads) cnt[e] = 0;
-    for (int i = tid; i < E * TW; i += kSelThreads) bm[i] = 0;
-    __syncthreads();
-    for (int a = tid; a < T * K; a += kSelThreads) {
-        const int e = sidx[a], t = a / K;
-        atomicAdd(&cnt[e], 1);
-        atomicOr(&bm[e * TW + (t >> 5)], 1u << (t & 31));
-    }
-    __syncthreads();
-    for (int e = tid; e < E; e += kSelThreads) {
-        off[e] = cnt[e];
-        nch[e] = (cnt[e] + p.nt_routed - 1) / p.nt_routed;
-        choff[e] = nch[e];
-    }
-    __syncthreads();
-    block_exclusive_scan<kSelThreads>(off, E, warp_tot);
-    const int routed_chunks = block_exclusive_scan<kSelThreads>(choff, E, warp_tot);
-    for (int a = tid; a < T * K; a += kSelThreads) {
-        const int e = sidx[a], t = a / K;
-        int rank = __popc(bm[e * TW + (t >> 5)] & ((1u << (t & 31)) - 1u));
-        for (int w = 0; w < (t >> 5); w++) rank += __popc(bm[e * TW + w]);
-        p.perm[off[e] + rank] = a;
-    }
-    const int ns = p.has_shared ? (T + p.nt_shared - 1) / p.nt_shared : 0;
-    for (int i = tid; i < ns; i += kSelThreads)
-        p.chunks[i] = Chunk{E, T * K + i * p.nt_shared, min(p.nt_shared, T - i * p.nt_shared), 0};
-    for (int e = tid; e < E; e += kSelThreads) {
-        p.counts[e] = cnt[e];
-        p.offsets[e] = off[e];
-        for (int c = 0; c < nch[e]; c++)
-            p.chunks[ns + choff[e] + c] = Chunk{e, off[e] + c * p.nt_routed, min(p.nt_routed, cnt[e] - c * p.nt_routed), 0};
-    }
-    if (tid == 0) {
-        p.offsets[E] = T * K;
-        p.n_chunks[0] = ns + routed_chunks;
-        p.n_chunks[1] = ns;
+        // bucketed dispatch.  Warp 0 scans (assignments | chunks << 16) over the experts, lane l
+        // owning experts l * epl .. (l + 1) * epl - 1; every thread then places its assignments by
+        // their stable rank among the expert's tokens (the expert's token bitmap).
+        if (warp == 0) {
+            const int epl = (E + 31) / 32, e0 = lane * epl;
+            int run = 0;
+            for (int i = 0; i < epl; i++) {
+                const int e = e0 + i;
+                if (e < E) run += cnt[e] | (((cnt[e] + p.nt_routed - 1) >> sh_r) << 16);
+            }
+            int incl = run;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int acc = incl - run;
+            for (int i = 0; i < epl; i++) {
+                const int e = e0 + i;
+                if (e < E) {
+                    pk[e] = acc;
+                    acc += cnt[e] | (((cnt[e] + p.nt_routed - 1) >> sh_r) << 16);
+                }
+            }
+        }
+        __syncthreads();
+        for (int a = tid; a < t_end * K; a += kSelThreads) {
+            const int e = sidx[a], t = a / K;
+            int rank = __popc(bm[e * TW + (t >> 5)] & ((1u << (t & 31)) - 1u));
+            for (int w = 0; w < (t >> 5); w++) rank += __popc(bm[e * TW + w]);
+            if (live) p.perm[(pk[e] & 0xffff) + rank] = a;
+        }
+        const int ns = p.has_shared ? (T + p.nt_shared - 1) >> sh_s : 0;
+        if (live) {
+            for (int i = tid; i < ns; i += kSelThreads)
+                p.chunks[i] = Chunk{E, T * K + (i << sh_s), min(p.nt_shared, T - (i << sh_s)), 0};
+            for (int e = tid; e < E; e += kSelThreads) {
+                const int c_e = cnt[e], off = pk[e] & 0xffff, ch = pk[e] >> 16;
+                p.counts[e] = c_e;
+                p.offsets[e] = off;
+                for (int c = 0; (c << sh_r) < c_e; c++)
+                    p.chunks[ns + ch + c] = Chunk{e, off + (c << sh_r), min(p.nt_routed, c_e - (c << sh_r)), 0};
+                if (e == E - 1) {
+                    p.offsets[E] = T * K;
+                    p.n_chunks[0] = ns + ch + ((c_e + p.nt_routed - 1) >> sh_r);
+                    p.n_chunks[1] = ns;
+                }
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -423,6 +487,8 @@ cudaError_t router_setup() {
 }
 
 cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first) {
+    if ((r.nt_routed & (r.nt_routed - 1)) || (r.nt_shared & (r.nt_shared - 1)) || r.nt_routed < 1 || r.nt_shared < 1)
+        return cudaErrorInvalidValue;  // chunk sizes must be powers of two
     void *args[] = {&r};
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attr[2];
