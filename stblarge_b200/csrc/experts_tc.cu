@@ -1,7 +1,11 @@
 // Grouped expert products on the 5th-generation tensor cores (FP8 128x128-block experts).
 //
-// Work item: (chunk of <= 16 tokens of one expert, output tile).  One persistent CTA per SM takes a
-// contiguous range of items; six warps:
+// Work item: (chunk of <= 16 tokens of one expert, output tile), nkb = K / 128 blocks of K each.
+// One persistent CTA per SM takes an equal contiguous range of the (item, K block) units, so no SM
+// idles while others finish a last item.  An item cut by a range boundary is finished by the CTA
+// holding its first K block (which reaches it last, at the end of its range): the CTAs whose ranges
+// start inside the item publish their partial sums first thing and raise a flag; the finishing CTA
+// adds them in CTA order.  Publishers never wait, so the waits cannot form a cycle.  Six warps:
 //   warp 0     TMA producer: per 128-K block one stage = a 128-row x 128-byte weight tile and a
 //              16-row x 128-byte activation tile, both in the 128-byte swizzle layout;
 //   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 token columns,
@@ -32,6 +36,7 @@ constexpr int kBTile = kTcN * 128;
 constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
 constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
 constexpr int kTcChunks = 32;     // chunk entries of a CTA's item range kept in shared memory
+constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
 
 struct TcChunk {
     int e, pos0, n, ok;
@@ -54,6 +59,21 @@ __device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
 __device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
     if (!p.b_direct) return ch.pos0;
     return ch.e == p.E ? ch.pos0 - p.T * p.topk : 0;
+}
+
+__device__ __forceinline__ void flag_release(unsigned int *f, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// wait until *f == v; gives up when *abort is raised or after kWaitLimitNs
+__device__ __forceinline__ bool flag_wait(const unsigned int *f, unsigned int v, volatile int *abort) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        unsigned int x;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(x) : "l"(f) : "memory");
+        if (x == v) return true;
+        if (*abort || global_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 
 template <bool UP>
@@ -99,7 +119,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
     pdl_launch_dependents();
     const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
-    const int lo = (int)(n_items * blockIdx.x / gridDim.x), hi = (int)(n_items * (blockIdx.x + 1) / gridDim.x);
+    const long long n_units = n_items * nkb;
+    const long long u_lo = n_units * blockIdx.x / gridDim.x, u_hi = n_units * (blockIdx.x + 1) / gridDim.x;
+    // items [lo, hi) touched by this CTA; item it covers K blocks [ka, kz) of it
+    const int lo = (int)(u_lo / nkb), hi = u_hi > u_lo ? (int)((u_hi - 1) / nkb) + 1 : lo;
+    auto k_range = [&](int it, int &ka, int &kz) {
+        ka = (int)max(u_lo - (long long)it * nkb, 0LL);
+        kz = (int)min(u_hi - (long long)it * nkb, (long long)nkb);
+    };
     // the chunks this CTA's items touch, in shared memory (items beyond the table read global memory)
     const int c_lo = p.chunk_begin + lo / tiles;
     for (int i = tid; i < kTcChunks; i += kTcThreads)
@@ -123,14 +150,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 const bool shared = ch.e == p.E;
                 const int z = shared ? 0 : ch.e;
                 const int brow = b_row(p, ch);
-                for (int kb = 0; kb < nkb; kb++, q++) {
-                    const int s = q % nst;
-                    if (!mbar_wait(&empty[s], ((q / nst) & 1) ^ 1, &abort_flag)) {
+                int ka, kz;
+                k_range(it, ka, kz);
+                // K blocks are requested kTcBatch at a time, once as many stages are free, so that
+                // DRAM sees consecutive 128-byte pieces of each weight row together
+                for (int kb0 = ka; kb0 < kz && !stop; kb0 += kTcBatch) {
+                  const int nb = min(kTcBatch, kz - kb0);
+                  for (int u = 0; u < nb; u++) {
+                    const int qq = q + u;
+                    if (!mbar_wait(&empty[qq % nst], ((qq / nst) & 1) ^ 1, &abort_flag)) {
                         abort_flag = 1;
                         atomicOr(p.status, kErrWaitTimeout);
                         stop = true;
                         break;
                     }
+                  }
+                  for (int u = 0; u < nb && !stop; u++, q++) {
+                    const int s = q % nst, kb = kb0 + u;
                     unsigned char *a = stages + (size_t)s * kStage;
                     mbar_arrive_expect_tx(&full[s], kStage);
                     if (UP) {
@@ -140,6 +176,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 128, z, &full[s]);
                     }
                     tma_load_2d(a + kATile, &maps.b, kb * 128, brow, &full[s]);
+                  }
                 }
             }
             // drain: every issued tile must land before the CTA may exit
@@ -156,17 +193,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f8_f32(128, kTcN);
-            const int ng = (nkb + kTcG - 1) / kTcG;  // groups per item
             int q = 0, gq = 0;
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {
-                for (int gi = 0; gi < ng && !stop; gi++, gq++) {
+                int ka, kz;
+                k_range(it, ka, kz);
+                for (int kb0 = ka; kb0 < kz && !stop; kb0 += kTcG, gq++) {
                     const int g = gq % kTcGroups;
                     if (!mbar_wait(&acc_empty[g], ((gq / kTcGroups) & 1) ^ 1, &abort_flag)) {
                         stop = true;
                         break;
                     }
-                    const int nb = min(kTcG, nkb - gi * kTcG);
+                    const int nb = min(kTcG, kz - kb0);
                     for (int u = 0; u < nb; u++, q++) {
                         const int s = q % nst;
                         if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag)) {
@@ -275,7 +313,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 #pragma unroll
             for (int j = 0; j < kTcN; j++) acc[j] = 0.f;
             bool ok = true;
-            for (int kb0 = 0; kb0 < nkb; kb0 += kTcG, gq++) {
+            int ka, kz;
+            k_range(it, ka, kz);
+            for (int kb0 = ka; kb0 < kz; kb0 += kTcG, gq++) {
                 const int g = gq % kTcGroups;
                 if (!mbar_wait(&acc_full[g], (gq / kTcGroups) & 1, &abort_flag)) {
                     ok = false;
@@ -289,7 +329,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 #pragma unroll
                 for (int u = 0; u < kTcG; u++) {
                     const int kb = kb0 + u;
-                    if (kb < nkb) {
+                    if (kb < kz) {
                         const float wsc = swb[mrow * nkb + kb];
 #pragma unroll
                         for (int j = 0; j < kTcN; j++) acc[j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc[j]);
@@ -302,6 +342,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                     atomicOr(p.status, kErrWaitTimeout);
                 }
                 break;
+            }
+            if (ka > 0) {
+                // the range starts inside this item: publish the partial sums for the CTA that finishes it
+                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)blockIdx.x * 128 + row) * kTcN);
+#pragma unroll
+                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+                __threadfence();
+                bar_sync(2, 128);
+                if (et == 0) flag_release(p.flags + blockIdx.x, p.seq);
+                if (it + 1 < hi) park(buf ^ 1);
+                bar_sync(2, 128);
+                continue;
+            }
+            // this CTA holds the item's first K block: add the partials of the CTAs whose ranges start
+            // inside the item, in CTA order
+            bool got = true;
+            for (int c = blockIdx.x + 1; c < (int)gridDim.x; c++) {
+                const long long uc = n_units * c / gridDim.x;
+                if (uc >= (long long)(it + 1) * nkb) break;
+                if (n_units * (c + 1) / gridDim.x == uc) continue;  // empty range
+                if (et == 0) got = flag_wait(p.flags + c, p.seq, &abort_flag) && got;
+                bar_sync(2, 128);
+                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * kTcN);
+#pragma unroll
+                for (int j = 0; j < kTcN / 4; j++) {
+                    const float4 v = __ldcg(src + j);
+                    acc[4 * j] += v.x, acc[4 * j + 1] += v.y, acc[4 * j + 2] += v.z, acc[4 * j + 3] += v.w;
+                }
+            }
+            if (!got) {
+                abort_flag = 1;
+                atomicOr(p.status, kErrWaitTimeout);
             }
             const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
             const float *swt = slot_w + buf * kTcN;

@@ -78,6 +78,9 @@ struct stbl_moe {
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     uint32_t *status = nullptr;
+    float *tc_partial = nullptr;      // split-item partial sums of the tensor-core kernels, [sms][128][16]
+    unsigned int *tc_flags = nullptr; // [sms] launch number whose partial a CTA slot holds
+    unsigned int tc_seq = 0;
     ExpertPtrs *experts = nullptr;
     std::vector<ExpertPtrs> host_experts;
     KernelCfg up_r, down_r;           // CUDA-core kernels (MXFP4 routed experts)
@@ -223,6 +226,11 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         }
     }
 
+    int dev = 0, max_smem = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+
     // workspace
     const int T = m->Tmax, npos = T * K + T, Tpad = (T + 15) / 16 * 16;
     auto layout = [&](char *base) {
@@ -250,6 +258,8 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 16);
+        m->tc_flags = carve<unsigned int>(p, m->sms);
         return (size_t)(p - base);
     };
     m->ws_bytes = layout(nullptr);
@@ -258,10 +268,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     layout(static_cast<char *>(m->ws));
     CK(cudaMemcpy(m->experts, m->host_experts.data(), sizeof(ExpertPtrs) * (E + 1), cudaMemcpyHostToDevice));
 
-    int dev = 0, max_smem = 0;
-    CK(cudaGetDevice(&dev));
-    CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
-    CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
     if (!m->routed_tc) {
@@ -297,9 +303,11 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         auto pick = [&](bool up, int &nst, int &smem) {
             cudaFuncAttributes fa{};
             CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up)));
-            for (nst = 16; nst >= 2; nst--)
+            // at most 8 stages (two batches of 4 K blocks in flight): measured best on B200, more
+            // outstanding requests only lengthen the DRAM queues
+            for (nst = 8; nst >= 4; nst--)
                 if (expert_tc_smem_bytes(up, H, I, nst) + (int)fa.sharedSizeBytes <= max_smem) break;
-            if (nst < 2) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
+            if (nst < 4) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
             smem = expert_tc_smem_bytes(up, H, I, nst);
             CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         };
@@ -346,6 +354,10 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     p.h = m->h;
     p.eo = m->eo, p.sh = m->sh;
     p.has_shared = m->has_shared;
+    p.partial = m->tc_partial;
+    p.flags = m->tc_flags;
+    if (++m->tc_seq == 0) m->tc_seq = 1;
+    p.seq = m->tc_seq;
     p.status = m->status;
     return p;
 }

@@ -32,6 +32,11 @@ struct TcParams {
     uint16_t *h;               // up out: [pos][I] bf16
     uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
+    // split items: CTA b publishes the partial sums of the item its range starts inside in
+    // partial[b] ([128 rows][16 columns] fp32) and then sets flags[b] = seq
+    float *partial;
+    unsigned int *flags;
+    unsigned int seq;          // this launch's number, never 0
     uint32_t *status;
 };
 
