@@ -308,9 +308,11 @@ def main():
             "distinct_experts_per_step": float(np.mean(distinct)),
             "kernel_ms_per_step": {"router": kt["router"] / max(kt["calls"], 1) * 1e3, "up": up_ms,
                                    "down": kt["down"] / max(kt["calls"], 1) * 1e3},
-            "roofline": {"bound": "hbm", "kernel": "expert_kernel<FP8,up> (gate+up+SwiGLU)", "achieved": up_gbs,
+            "roofline": {"bound": "hbm", "kernel": "expert_tc_kernel<up> (tcgen05 FP8 gate+up, SwiGLU)", "achieved": up_gbs,
                          "peak": peak, "unit": "GB/s", "frac": up_gbs / peak, "peak_kind": peak_kind,
-                         "traffic": traffic_from_profile()},
+                         "traffic": traffic_from_profile(float(np.mean(distinct)) + 1.0),
+                         "traffic_note": "ncu DRAM read+write bytes per expert of one up launch (profiles/traffic.json) "
+                                         "x the step's mean distinct routed experts + the shared expert"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * cfg.hidden * 2,
                     "d2h_bytes_per_step": T * cfg.hidden * 2},
             "gpu_launches": launches * args.steps,
@@ -324,13 +326,16 @@ def main():
         dist.destroy_process_group()
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the up kernel from the committed ncu summary, when there is one."""
+def traffic_from_profile(experts_per_launch):
+    """DRAM bytes per launch of the up kernel: the committed ncu figure per expert (a capture of a
+    smaller case, where traffic grows in proportion to the experts streamed) times the experts one
+    launch of this workload streams.  None when there is no committed figure."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f).get("expert_up_fp8_bytes_per_launch")
+            per_expert = json.load(f).get("expert_up_fp8_dram_bytes_per_expert")
     except Exception:
         return None
+    return None if per_expert is None else per_expert * experts_per_launch
 
 
 if __name__ == "__main__":

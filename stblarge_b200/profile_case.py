@@ -88,8 +88,10 @@ def main():
     torch.cuda.synchronize()
     t = layer.timing()
     n = max(t["calls"], 1)
+    distinct = len(np.unique(layer.last_route()["idx"]))
     print(f"{cfg.name} T={a.tokens}: router {t['router'] / n * 1e3:.4f} ms, up {t['up'] / n * 1e3:.4f} ms, "
-          f"down {t['down'] / n * 1e3:.4f} ms per call, status {layer.status()}")
+          f"down {t['down'] / n * 1e3:.4f} ms per call, status {layer.status()}, "
+          f"distinct routed experts in the last call {distinct} (+ the shared expert)")
     layer.close()
 
 
