@@ -106,6 +106,23 @@ void stbl_moe_stats(const stbl_moe *m, uint64_t *calls, uint64_t *tokens, int *l
 const char *stbl_moe_error(const stbl_moe *m);
 void stbl_moe_destroy(stbl_moe *m);
 
+/* Expert parallelism over the GPUs of one node (NVLink / NVSwitch).  Rank `rank` of `n_ranks` (<= 8,
+ * dividing n_experts) holds routed experts [rank E/n, (rank+1) E/n): desc->routed_w/routed_s point at
+ * the first of them (desc->n_experts stays the global count; the router and its weights are global,
+ * the shared expert is replicated).  Each rank routes its own tokens; dispatch and combine are done by
+ * the layer's kernels with stores into peer GPUs' memory through one exchange region per rank (no
+ * host synchronisation, no collective library in the data path).  Needs FP8 routed experts.
+ * Bring-up: every rank creates its layer, exports its region with stbl_moe_ep_handle, the host
+ * side gathers the n_ranks handles in rank order (any transport: the Python mirror uses
+ * torch.distributed all_gather_object) and passes them to stbl_moe_ep_connect.  After that every
+ * rank must call stbl_moe_forward the same number of times, in the same order across layers (each
+ * call exchanges with every rank); device waits on other ranks time out after 1 s and raise status
+ * bit 1.  This replaces the reference design's NCCL all-to-all pair (dispatch, combine). */
+#define STBL_EP_HANDLE_BYTES 64
+int stbl_moe_create_ep(const stbl_moe_desc *desc, int rank, int n_ranks, stbl_moe **out, char *err, int errlen);
+int stbl_moe_ep_handle(stbl_moe *m, void *handle /* STBL_EP_HANDLE_BYTES */);
+int stbl_moe_ep_connect(stbl_moe *m, const void *handles /* n_ranks x STBL_EP_HANDLE_BYTES, rank order */);
+
 /* Routing without allocating.  This entry point has no counterpart in the reference; it exists for
  * callers that cannot allocate device memory: code running while a CUDA graph is being captured,
  * engines that own a fixed memory pool and allow no allocation outside it, embedded runtimes without

@@ -409,6 +409,18 @@ __global__ void __launch_bounds__(kExpertThreads, 1)
 __global__ void __launch_bounds__(256) combine_kernel(CombineParams p) {
     pdl_wait();
     pdl_launch_dependents();
+    if (p.ep.n_ranks > 1) {
+        // expert parallelism: this rank's down kernel (before this one) has finished writing into
+        // every source rank's eo rows: say so everywhere, then wait until every rank has said so
+        __shared__ int ok;
+        if (threadIdx.x == 0) {
+            if (blockIdx.x == 0) signal_all(p.ep, p.ep.L.done_flag);
+            ok = wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.done_flag),
+                                p.ep.n_ranks, p.ep.epoch);
+            if (!ok) atomicOr(p.status, kErrWaitTimeout);
+        }
+        __syncthreads();
+    }
     const int per_row = p.H / 8;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= p.T * per_row) return;
@@ -417,7 +429,8 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineParams p) {
 #pragma unroll
     for (int q = 0; q < 8; q++) acc[q] = 0.f;
     for (int s = 0; s < p.topk; s++) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p.eo + ((size_t)t * p.topk + s) * p.H + c));
+        // L2 loads: under expert parallelism the rows were written by other GPUs during this call
+        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.eo + ((size_t)t * p.topk + s) * p.H + c));
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int q = 0; q < 4; q++) {

@@ -44,7 +44,7 @@ struct TcChunk {
 
 __device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
     TcChunk r{ch.e, ch.pos0, ch.n, 1};
-    const int nrouted = p.T * p.topk;
+    const int nrouted = p.n_routed;
     const bool shared = ch.e == p.E;
     const bool bad = ch.e < 0 || ch.e > p.E || (shared && !p.has_shared) || ch.n < 1 || ch.n > kTcN ||
                      (shared ? (ch.pos0 < nrouted || ch.pos0 + ch.n > nrouted + p.T)
@@ -58,7 +58,7 @@ __device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
 // Otherwise (rows by position) the chunk's first position, column = slot.
 __device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
     if (!p.b_direct) return ch.pos0;
-    return ch.e == p.E ? ch.pos0 - p.T * p.topk : 0;
+    return ch.e == p.E ? ch.pos0 - p.n_routed : 0;
 }
 
 __device__ __forceinline__ void flag_release(unsigned int *f, unsigned int v) {
@@ -117,6 +117,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 
     pdl_wait();
     pdl_launch_dependents();
+    if (UP && p.ep.n_ranks > 1) {
+        // every rank's payload rows must have landed in this rank's receive rows: the payload
+        // kernel before this one has finished, so raise this rank's flag everywhere, then wait for all
+        if (blockIdx.x == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
+        if (tid == 0) {
+            if (!wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.pay_flag),
+                                p.ep.n_ranks, p.ep.epoch)) {
+                abort_flag = 1;
+                atomicOr(p.status, kErrWaitTimeout);
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // the rows are read by TMA
+        }
+        __syncthreads();
+    }
     const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
     const long long n_units = n_items * nkb;
@@ -272,7 +286,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 const int pos = ch.pos0 + et;
                 pcol = et, pdst = pos, pwt = 1.f;
                 if (et < ch.n) {
-                    if (!shared) {
+                    if (!shared && p.pos_w) {
+                        // expert parallelism: weight and origin of the receive row
+                        if (UP) pwt = __ldcg(p.pos_w + pos);
+                        else pdst = __ldcg(p.pos_meta + pos);  // source rank << 16 | assignment
+                    } else if (!shared) {
                         const int a = __ldg(p.perm + pos);
                         if (UP) {
                             pwt = __ldg(p.wts + a);
@@ -281,7 +299,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                             pdst = a;  // eo row
                         }
                     } else if (!UP) {
-                        pdst = pos - p.T * p.topk;  // sh row
+                        pdst = pos - p.n_routed;  // sh row
                     }
                 }
             }
@@ -391,10 +409,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 }
             } else {
                 const int r = tile * 128 + row;
-                uint16_t *out = ch.e < p.E ? p.eo : p.sh;
+                if (ch.e < p.E && p.pos_w) {
+                    // expert parallelism: straight into the source rank's eo row, over NVLink
 #pragma unroll
-                for (int j = 0; j < kTcN; j++)
-                    if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
+                    for (int j = 0; j < kTcN; j++)
+                        if (j < ch.n) {
+                            const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
+                            if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
+                                if (row == 0) atomicOr(p.status, kErrBadTable);
+                                continue;
+                            }
+                            uint16_t *out = reinterpret_cast<uint16_t *>(p.ep.region[src] + p.ep.L.eo);
+                            out[(size_t)a * p.H + r] = f32_to_bf16_bits(acc[j]);
+                        }
+                } else {
+                    uint16_t *out = ch.e < p.E ? p.eo : p.sh;
+#pragma unroll
+                    for (int j = 0; j < kTcN; j++)
+                        if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
+                }
             }
             if (it + 1 < hi) park(buf ^ 1);
             bar_sync(2, 128);
@@ -429,21 +462,27 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
     pdl_wait();
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
-    const int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const int per_row = p.I / 128;
-    if (w >= p.n_pos * per_row) return;
-    const int pos = w / per_row, g = w % per_row;
-    const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(p.h + (size_t)pos * p.I + g * 128 + 4 * lane));
-    const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
-                        __uint_as_float(xv.y & 0xffff0000u)};
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    amax = fmaxf(warp_max(amax), 1e-4f);
-    const float s = amax * (1.0f / 448.0f);
-    uint32_t codes = 0;
+    const int nw = gridDim.x * (blockDim.x / 32);
+    // rows: [0, n_pos), or under expert parallelism [0, routed rows received) and the shared rows
+    const int n_head = p.n_routed_dev ? min(*p.n_routed_dev, p.n_pos) : p.n_pos;
+    const int rows = n_head + (p.n_routed_dev ? p.n_tail : 0);
+    for (int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w < rows * per_row; w += nw) {
+        int pos = w / per_row;
+        const int g = w % per_row;
+        if (pos >= n_head) pos = p.n_pos + (pos - n_head);
+        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(p.h + (size_t)pos * p.I + g * 128 + 4 * lane));
+        const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
+                            __uint_as_float(xv.y & 0xffff0000u)};
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(warp_max(amax), 1e-4f);
+        const float s = amax * (1.0f / 448.0f);
+        uint32_t codes = 0;
 #pragma unroll
-    for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
-    *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
-    if (lane == 0) p.hs[(size_t)pos * per_row + g] = s;
+        for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
+        *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
+        if (lane == 0) p.hs[(size_t)pos * per_row + g] = s;
+    }
 }
 
 const void *hquant_kernel_ptr() { return (const void *)hquant_kernel; }

@@ -107,11 +107,79 @@ struct ExpertParams {
     uint32_t *status;
 };
 
+// ---- expert parallelism ------------------------------------------------------------------------
+//
+// Rank r of n holds routed experts [r E/n, (r+1) E/n).  Every rank owns one exchange region, mapped
+// into every other rank's address space (CUDA IPC over NVLink); the regions have the same layout on
+// every rank.  Per layer call (epoch = the call's number, the same on every rank):
+//   counts  each rank writes its per-expert assignment counts into every rank's inbox[r] and raises
+//           cnt_flag[r] there; every rank waits for all n cnt_flags, then knows where each of its
+//           assignments lands in its owner's receive rows (expert-major, then source rank, then the
+//           source's token order)
+//   payload each rank writes the FP8 codes + scales of each assignment's token, its routing weight
+//           and (source rank, assignment) into the owner's receive rows; the owner's up kernel, once
+//           the payload kernel before it has finished, raises pay_flag[r] on every rank and waits for
+//           all n pay_flags
+//   outputs the owner's down kernel stores each assignment's bf16 output row straight into the source
+//           rank's eo rows; the combine kernel raises done_flag[r] on every rank and waits for all n
+// Every wait is bounded.  A rank never waits for a later step of another rank, so the waits cannot
+// form a cycle; the count exchange of call c+1 cannot start on any rank before every rank has
+// finished call c's combine, which protects every buffer that peers write.
+constexpr int kEpMaxRanks = 8;
+
+struct EpLayout {            // byte offsets inside an exchange region
+    long long inbox;         // int [n][E]: assignment counts per expert, by source rank
+    long long cnt_flag;      // u32 [n]
+    long long pay_flag;      // u32 [n]
+    long long done_flag;     // u32 [n]
+    long long xq_pos;        // u8 [rows][H]: receive rows (routed, capacity n Tmax topk), then the shared rows
+    long long xs_pos;        // f32 [rows][H / 128]
+    long long pos_meta;      // int [routed capacity]: source rank << 16 | assignment (token * topk + slot)
+    long long pos_w;         // f32 [routed capacity]: routing weight of the row
+    long long eo;            // bf16 [Tmax topk][H]: this rank's routed outputs, written by the owners
+    long long bytes;
+};
+
+struct EpView {
+    char *region[kEpMaxRanks];  // every rank's exchange region (this rank's own at [rank])
+    EpLayout L;
+    int rank, n_ranks;
+    unsigned int epoch;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned int *f, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// wait until flags[s] == v for every s < n (flags written by other GPUs); false after kWaitLimitNs
+__device__ __forceinline__ bool wait_flags_sys(const unsigned int *flags, int n, unsigned int v) {
+    const uint64_t t0 = global_ns();
+    for (int s = 0; s < n; s++) {
+        for (;;) {
+            unsigned int x;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(x) : "l"(flags + s) : "memory");
+            if (x == v) break;
+            if (global_ns() - t0 > kWaitLimitNs) return false;
+        }
+    }
+    return true;
+}
+
+// raise flag `which` (a byte offset of the layout) at index rank on every rank's region
+__device__ __forceinline__ void signal_all(const EpView &v, long long which) {
+    __threadfence_system();
+    for (int d = 0; d < v.n_ranks; d++)
+        st_release_sys(reinterpret_cast<unsigned int *>(v.region[d] + which) + v.rank, v.epoch);
+}
+
 struct CombineParams {
     const uint16_t *eo;
     const uint16_t *sh;
     uint16_t *y;
     int T, topk, H, has_shared;
+    // expert parallelism (ep.n_ranks > 1): raise done_flag on every rank, wait for all of them
+    EpView ep;
+    uint32_t *status;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -15,6 +15,7 @@
 #include "../../include/stbl_moe.h"
 #include "layer.cuh"
 #include "tc_params.cuh"
+#include "ep.cuh"
 
 namespace stbl {
 const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
@@ -70,6 +71,15 @@ const void *expert_fn(int fmt, bool up) { return expert_kernel_ptr(fmt, up); }
 struct stbl_moe {
     stbl_moe_desc d{};
     int E = 0, H = 0, I = 0, K = 0, Tmax = 0, ksplit = 1, sms = 0, has_shared = 0;
+    // expert parallelism: this rank holds routed experts [ep_rank E_loc, (ep_rank + 1) E_loc)
+    int ep_rank = 0, ep_n = 1, E_loc = 0;
+    int routed_cap = 0;               // routed rows of the position-ordered buffers
+    char *ep_region = nullptr;        // exchange region (expert parallelism), exported by CUDA IPC
+    EpLayout ep_L{};
+    char *ep_peer[kEpMaxRanks] = {};
+    bool ep_connected = false;
+    unsigned int ep_epoch = 0;
+    int *a_dst = nullptr, *n_rows = nullptr;
     void *ws = nullptr;
     size_t ws_bytes = 0;
     float *scores = nullptr, *wts = nullptr, *xs_a = nullptr, *xs_b = nullptr;
@@ -179,17 +189,45 @@ KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
     return c;
 }
 
-void create(stbl_moe *m, const stbl_moe_desc *d) {
+// exchange-region layout (expert parallelism); the same on every rank
+EpLayout ep_layout(int E, int n, int routed_cap, int Tmax, int K, int H) {
+    EpLayout L{};
+    long long o = 0;
+    auto take = [&](long long bytes) {
+        const long long r = o;
+        o += (bytes + 255) & ~255LL;
+        return r;
+    };
+    L.inbox = take(4LL * n * E);
+    L.cnt_flag = take(4LL * kEpMaxRanks);
+    L.pay_flag = take(4LL * kEpMaxRanks);
+    L.done_flag = take(4LL * kEpMaxRanks);
+    L.xq_pos = take((long long)(routed_cap + Tmax + 16) * H);
+    L.xs_pos = take(4LL * (routed_cap + Tmax + 16) * (H / 128));
+    L.pos_meta = take(4LL * routed_cap);
+    L.pos_w = take(4LL * routed_cap);
+    L.eo = take(2LL * Tmax * K * H);
+    L.bytes = o;
+    return L;
+}
+
+void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) {
     if (!d) throw std::runtime_error("null description");
     m->d = *d;
-    const int H = d->hidden, I = d->inter, E = d->n_experts, K = d->topk;
+    const int H = d->hidden, I = d->inter, Eg = d->n_experts, K = d->topk;
+    if (ep_n < 1 || ep_n > kEpMaxRanks || ep_rank < 0 || ep_rank >= ep_n) throw std::runtime_error("bad rank / n_ranks (n_ranks <= 8)");
+    if (Eg % ep_n) throw std::runtime_error("n_experts must be a multiple of n_ranks");
+    if (ep_n > 1 && d->routed_fmt != STBL_FMT_FP8_B128) throw std::runtime_error("expert parallelism needs FP8 routed experts");
+    m->ep_rank = ep_rank, m->ep_n = ep_n;
+    // the router sees every expert; the expert kernels see this rank's E / n_ranks
+    const int E = Eg / ep_n;
     if (H <= 0 || I <= 0 || H % 512 || I % 512 || !lanes_ok(H) || !lanes_ok(I))
         throw std::runtime_error("hidden and inter must be multiples of 512 with K/32 lanes a multiple or divisor of 32 (<= 448)");
-    if (E < 1 || E > kMaxExperts) throw std::runtime_error("n_experts must be in 1..512");
-    if (K < 1 || K > kMaxTopk || K > E) throw std::runtime_error("topk must be in 1..16 and <= n_experts");
-    if (d->n_groups < 1 || d->n_groups > 32 || E % d->n_groups) throw std::runtime_error("n_groups must divide n_experts and be <= 32");
+    if (Eg < 1 || Eg > kMaxExperts) throw std::runtime_error("n_experts must be in 1..512");
+    if (K < 1 || K > kMaxTopk || K > Eg) throw std::runtime_error("topk must be in 1..16 and <= n_experts");
+    if (d->n_groups < 1 || d->n_groups > 32 || Eg % d->n_groups) throw std::runtime_error("n_groups must divide n_experts and be <= 32");
     if (d->topk_groups < 1 || d->topk_groups > d->n_groups) throw std::runtime_error("topk_groups must be in 1..n_groups");
-    const int gsz = E / d->n_groups;
+    const int gsz = Eg / d->n_groups;
     const bool grouped = d->n_groups > 1 && d->topk_groups < d->n_groups;
     if (grouped && (gsz < 2 || d->topk_groups * gsz < K)) throw std::runtime_error("kept groups hold fewer than topk experts");
     if (d->score_fn != STBL_SCORE_SIGMOID && d->score_fn != STBL_SCORE_SQRT_SOFTPLUS) throw std::runtime_error("bad score_fn");
@@ -199,7 +237,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     if (H / router_ksplit(H) > kLgMaxSlice) throw std::runtime_error("hidden must be at most 8192");
     if (!d->router_w || !d->router_bias) throw std::runtime_error("router weights missing");
     if ((uintptr_t)d->router_w & 15) throw std::runtime_error("router weights must be 16-byte aligned");
-    m->E = E, m->H = H, m->I = I, m->K = K, m->Tmax = d->max_tokens;
+    m->E = Eg, m->E_loc = E, m->H = H, m->I = I, m->K = K, m->Tmax = d->max_tokens;
     m->ksplit = router_ksplit(H);
     m->has_shared = d->shared_fmt != STBL_FMT_NONE;
 
@@ -231,16 +269,24 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
 
-    // workspace
-    const int T = m->Tmax, npos = T * K + T, Tpad = (T + 15) / 16 * 16;
+    // workspace (+ the exchange region under expert parallelism)
+    const int T = m->Tmax, Tpad = (T + 15) / 16 * 16;
+    m->routed_cap = ep_n * T * K;
+    const int npos = m->routed_cap + T;
+    if (ep_n > 1) {
+        m->ep_L = ep_layout(Eg, ep_n, m->routed_cap, T, K, H);
+        CK(cudaMalloc(&m->ep_region, m->ep_L.bytes));
+        CK(cudaMemset(m->ep_region, 0, m->ep_L.bytes));
+        m->ep_peer[ep_rank] = m->ep_region;
+    }
     auto layout = [&](char *base) {
         char *p = base;
         m->experts = carve<ExpertPtrs>(p, E + 1);
-        m->scores = carve<float>(p, (size_t)T * E);
+        m->scores = carve<float>(p, (size_t)T * Eg);
         m->idx = carve<int>(p, (size_t)T * K);
         m->wts = carve<float>(p, (size_t)T * K);
-        m->counts = carve<int>(p, E);
-        m->offsets = carve<int>(p, E + 1);
+        m->counts = carve<int>(p, Eg);
+        m->offsets = carve<int>(p, Eg + 1);
         m->perm = carve<int>(p, (size_t)T * K);
         m->chunks = carve<Chunk>(p, npos);
         m->n_chunks = carve<int>(p, 4);
@@ -248,24 +294,31 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
         m->xs_a = carve<float>(p, (size_t)Tpad * (H / 32));
         m->xq_b = carve<uint8_t>(p, (size_t)Tpad * H);
         m->xs_b = carve<float>(p, (size_t)Tpad * (H / 32));
-        m->xq_pos = carve<uint8_t>(p, (size_t)(npos + 16) * H);
-        m->xs_pos = carve<float>(p, (size_t)(npos + 16) * (H / 128));
+        m->xq_pos = ep_n > 1 ? nullptr : carve<uint8_t>(p, (size_t)(npos + 16) * H);
+        m->xs_pos = ep_n > 1 ? nullptr : carve<float>(p, (size_t)(npos + 16) * (H / 128));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
         m->hq = carve<uint8_t>(p, (size_t)(npos + 16) * I);
         m->hs = carve<float>(p, (size_t)(npos + 16) * (I / 128));
-        m->eo = carve<uint16_t>(p, (size_t)T * K * H);
+        m->eo = ep_n > 1 ? nullptr : carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
         m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 16);
         m->tc_flags = carve<unsigned int>(p, m->sms);
+        m->a_dst = carve<int>(p, (size_t)T * K);
+        m->n_rows = carve<int>(p, 4);
         return (size_t)(p - base);
     };
     m->ws_bytes = layout(nullptr);
     CK(cudaMalloc(&m->ws, m->ws_bytes));
     CK(cudaMemset(m->ws, 0, m->ws_bytes));
     layout(static_cast<char *>(m->ws));
+    if (ep_n > 1) {
+        m->xq_pos = reinterpret_cast<uint8_t *>(m->ep_region + m->ep_L.xq_pos);
+        m->xs_pos = reinterpret_cast<float *>(m->ep_region + m->ep_L.xs_pos);
+        m->eo = reinterpret_cast<uint16_t *>(m->ep_region + m->ep_L.eo);
+    }
     CK(cudaMemcpy(m->experts, m->host_experts.data(), sizeof(ExpertPtrs) * (E + 1), cudaMemcpyHostToDevice));
 
     CK(router_setup());
@@ -316,11 +369,30 @@ void create(stbl_moe *m, const stbl_moe_desc *d) {
     }
 }
 
+EpView ep_view(const stbl_moe *m) {
+    EpView v{};
+    v.n_ranks = m->ep_n;
+    v.rank = m->ep_rank;
+    v.epoch = m->ep_epoch;
+    v.L = m->ep_L;
+    for (int d = 0; d < m->ep_n; d++) v.region[d] = m->ep_peer[d];
+    return v;
+}
+
 TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     TcParams p{};
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
-    p.T = T, p.topk = m->K, p.E = m->E, p.H = m->H, p.I = m->I;
+    p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
+    p.ep = ep_view(m);
+    if (m->ep_n > 1) {
+        p.n_routed = m->routed_cap;
+        p.pos_w = reinterpret_cast<const float *>(m->ep_region + m->ep_L.pos_w);
+        p.pos_meta = reinterpret_cast<const int *>(m->ep_region + m->ep_L.pos_meta);
+        p.T_max_assign = m->Tmax * m->K;
+    } else {
+        p.n_routed = T * m->K;
+    }
     p.perm = m->perm;
     p.wts = m->wts;
     const stbl_moe_desc &d = m->d;
@@ -391,7 +463,7 @@ ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
     p.experts = m->experts;
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
-    p.T = T, p.topk = m->K, p.E = m->E, p.H = m->H, p.I = m->I;
+    p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
     p.perm = m->perm;
     p.wts = m->wts;
     const bool routed_buf = fmt == m->d.routed_fmt;
@@ -436,6 +508,8 @@ void collect_timing(stbl_moe *m, size_t keep);
 void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
     if (!x || !y) throw std::runtime_error("null x or y");
+    if (m->ep_n > 1 && !m->ep_connected) throw std::runtime_error("expert-parallel layer not connected (stbl_moe_ep_connect)");
+    if (m->ep_n > 1 && ++m->ep_epoch == 0) m->ep_epoch = 1;
     if ((uintptr_t)x & 15) throw std::runtime_error("x must be 16-byte aligned");
     TimedCall tc{};
     if (m->timing) {
@@ -462,7 +536,34 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
 
     const int grid = m->sms;
     const int npos = T * m->K + (m->has_shared ? T : 0);
-    if (m->routed_tc) {
+    if (m->ep_n > 1) {
+        // expert parallelism: counts exchange -> payload into the owners' receive rows -> up (waits
+        // for every rank's payload) -> hquant -> down (outputs into the source ranks' eo rows)
+        EpCountsParams cpp{};
+        cpp.ep = ep_view(m);
+        cpp.counts = m->counts, cpp.offsets = m->offsets, cpp.perm = m->perm, cpp.idx = m->idx;
+        cpp.T = T, cpp.topk = m->K, cpp.E = m->E, cpp.E_loc = m->E_loc;
+        cpp.nt_routed = 16, cpp.nt_shared = 16, cpp.has_shared = m->has_shared, cpp.routed_cap = m->routed_cap;
+        cpp.a_dst = m->a_dst, cpp.chunks = m->chunks, cpp.n_chunks = m->n_chunks, cpp.n_rows = m->n_rows;
+        cpp.status = m->status;
+        EpPayloadParams ppp{};
+        ppp.ep = cpp.ep;
+        ppp.idx = m->idx, ppp.wts = m->wts, ppp.a_dst = m->a_dst;
+        ppp.xq = m->xq_a, ppp.xs = m->xs_a, ppp.xs_stride = m->H / 32;
+        ppp.T = T, ppp.topk = m->K, ppp.H = m->H, ppp.E_loc = m->E_loc, ppp.routed_cap = m->routed_cap;
+        ppp.has_shared = m->has_shared;
+        CK(launch_ep(cpp, ppp, m->sms, st));
+        TcParams pu = tc_params(m, T, true, false), pd = tc_params(m, T, false);
+        pu.chunk_begin = pd.chunk_begin = 0;
+        pu.chunk_end = pd.chunk_end = -1;
+        launch_tc(m, true, pu, st);
+        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        HquantParams hp{m->h, m->hq, m->hs, m->routed_cap, m->I, m->n_rows, m->has_shared ? T : 0};
+        void *hargs[] = {&hp};
+        launch_pdl(hquant_kernel_ptr(), dim3(m->sms), dim3(256), hargs, 0, st);
+        launch_tc(m, false, pd, st);
+        launches += 5;
+    } else if (m->routed_tc) {
         // every expert on the tensor cores: [gather] -> up -> hquant -> down -> combine
         const bool direct = T <= 16;
         if (!direct) {
@@ -502,7 +603,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         launch_expert(m->down_r, pd, grid, st);
         launches += 2;
     }
-    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared};
+    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};
     void *cargs[] = {&cp};
     const int cthreads = T * (m->H / 8);
     launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
@@ -549,16 +650,57 @@ void collect_timing(stbl_moe *m, size_t keep) {
 extern "C" {
 
 int stbl_moe_create(const stbl_moe_desc *desc, stbl_moe **out, char *err, int errlen) {
+    return stbl_moe_create_ep(desc, 0, 1, out, err, errlen);
+}
+
+int stbl_moe_create_ep(const stbl_moe_desc *desc, int rank, int n_ranks, stbl_moe **out, char *err, int errlen) {
     stbl_moe *m = new stbl_moe();
     try {
-        create(m, desc);
+        create(m, desc, rank, n_ranks);
         *out = m;
         return 0;
     } catch (const std::exception &e) {
         if (err && errlen > 0) snprintf(err, errlen, "%s", e.what());
         if (m->ws) cudaFree(m->ws);
+        if (m->ep_region) cudaFree(m->ep_region);
         delete m;
         *out = nullptr;
+        return -1;
+    }
+}
+
+int stbl_moe_ep_handle(stbl_moe *m, void *handle) {
+    try {
+        if (m->ep_n < 2) throw std::runtime_error("not an expert-parallel layer");
+        static_assert(sizeof(cudaIpcMemHandle_t) == STBL_EP_HANDLE_BYTES, "IPC handle size");
+        cudaIpcMemHandle_t h;
+        CK(cudaIpcGetMemHandle(&h, m->ep_region));
+        memcpy(handle, &h, sizeof h);
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_ep_connect(stbl_moe *m, const void *handles) {
+    try {
+        if (m->ep_n < 2) throw std::runtime_error("not an expert-parallel layer");
+        if (m->ep_connected) throw std::runtime_error("already connected");
+        for (int d = 0; d < m->ep_n; d++) {
+            if (d == m->ep_rank) continue;
+            cudaIpcMemHandle_t h;
+            memcpy(&h, static_cast<const char *>(handles) + (size_t)d * STBL_EP_HANDLE_BYTES, sizeof h);
+            void *ptr = nullptr;
+            CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+            m->ep_peer[d] = static_cast<char *>(ptr);
+        }
+        m->ep_connected = true;
+        return 0;
+    } catch (const std::exception &e) {
+        for (int d = 0; d < m->ep_n; d++)
+            if (d != m->ep_rank && m->ep_peer[d]) cudaIpcCloseMemHandle(m->ep_peer[d]), m->ep_peer[d] = nullptr;
+        m->err = e.what();
         return -1;
     }
 }
@@ -617,7 +759,7 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores) {
 
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream) {
     try {
-        if (e < 0 || e >= m->E) throw std::runtime_error("expert id out of range");
+        if (e < 0 || e >= m->E_loc) throw std::runtime_error("expert id out of range (local experts of this rank)");
         ExpertPtrs p{};
         for (int i = 0; i < 3; i++) {
             if (!w[i] || !s[i] || ((uintptr_t)w[i] & 15) || ((uintptr_t)s[i] & 15))
@@ -685,6 +827,9 @@ void stbl_moe_destroy(stbl_moe *m) {
     for (auto &t : m->event_pool)
         for (auto e : t.ev) cudaEventDestroy(e);
     if (m->ws) cudaFree(m->ws);
+    for (int d = 0; d < m->ep_n; d++)
+        if (d != m->ep_rank && m->ep_peer[d]) cudaIpcCloseMemHandle(m->ep_peer[d]);
+    if (m->ep_region) cudaFree(m->ep_region);
     delete m;
 }
 

@@ -32,6 +32,16 @@ struct TcParams {
     uint16_t *h;               // up out: [pos][I] bf16
     uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
+    // rows [0, n_routed) are routed assignments, the shared expert's rows follow (row n_routed + token)
+    int n_routed;
+    // expert parallelism (ep.n_ranks > 1): the rows are this rank's receive rows; pos_w / pos_meta give
+    // each routed row's routing weight and origin (source rank << 16 | assignment); the up kernel
+    // raises pay_flag on every rank and waits for all of them first; the down kernel stores routed
+    // outputs into the source rank's eo rows
+    const float *pos_w;
+    const int *pos_meta;
+    int T_max_assign;          // rows of a source rank's eo (max_tokens x topk)
+    EpView ep;
     // split items: CTA b publishes the partial sums of the item its range starts inside in
     // partial[b] ([128 rows][16 columns] fp32) and then sets flags[b] = seq
     float *partial;
@@ -46,6 +56,9 @@ struct HquantParams {
     uint8_t *hq;
     float *hs;
     int n_pos, I;
+    // expert parallelism: rows [0, *n_routed_dev) (known on the device) and [n_pos, n_pos + n_tail)
+    const int *n_routed_dev;
+    int n_tail;
 };
 
 // gathers x codes and scales into position order for the up kernel when T > 16

@@ -32,6 +32,9 @@ class MoEDesc(ctypes.Structure):
 SIGNATURES = {
     # include/stbl_moe.h
     "stbl_moe_create": (I, [ctypes.POINTER(MoEDesc), ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_moe_create_ep": (I, [ctypes.POINTER(MoEDesc), I, I, ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_moe_ep_handle": (I, [P, P]),
+    "stbl_moe_ep_connect": (I, [P, P]),
     "stbl_moe_forward": (I, [P, P, I, P, P]),
     "stbl_moe_forward_host": (I, [P, P, I, P, P]),
     "stbl_moe_last_route": (I, [P, P, P, P, P, P]),

@@ -22,8 +22,16 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
 
 
+EP_HANDLE_BYTES = 64
+
+
 class MoELayer:
-    def __init__(self, cfg: MoEConfig, weights: dict, max_tokens: int = 16):
+    """ep: (rank, n_ranks, process_group) for expert parallelism: `weights` then holds this rank's
+    routed experts [rank E/n, (rank+1) E/n) (synth.device_layer(cfg, experts=range(...))) and the
+    full router; the layers of all ranks connect through their exchange regions (handles gathered
+    with torch.distributed over the group), and every rank must then call forward in lockstep."""
+
+    def __init__(self, cfg: MoEConfig, weights: dict, max_tokens: int = 16, ep=None):
         self.lib = L.load()
         self.cfg = cfg
         self.weights = weights  # keeps the device tensors alive
@@ -45,10 +53,20 @@ class MoELayer:
                 d.shared_s[m] = weights["shared_s"][m].data_ptr()
         err = ctypes.create_string_buffer(512)
         h = ctypes.c_void_p()
-        if self.lib.stbl_moe_create(ctypes.byref(d), ctypes.byref(h), err, 512) != 0:
-            raise RuntimeError("stbl_moe_create: " + err.value.decode())
+        rank, n_ranks, group = ep if ep is not None else (0, 1, None)
+        if self.lib.stbl_moe_create_ep(ctypes.byref(d), rank, n_ranks, ctypes.byref(h), err, 512) != 0:
+            raise RuntimeError("stbl_moe_create_ep: " + err.value.decode())
         self.handle = h
         self._desc = d
+        self.ep = (rank, n_ranks)
+        if n_ranks > 1:
+            import torch.distributed as dist
+            mine = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+            self._check(self.lib.stbl_moe_ep_handle(self.handle, mine), "stbl_moe_ep_handle")
+            allh = [None] * n_ranks
+            dist.all_gather_object(allh, bytes(mine.raw), group=group)
+            blob = ctypes.create_string_buffer(b"".join(allh), EP_HANDLE_BYTES * n_ranks)
+            self._check(self.lib.stbl_moe_ep_connect(self.handle, blob), "stbl_moe_ep_connect")
 
     def _check(self, rc, what):
         if rc < 0:
@@ -141,14 +159,16 @@ class MoELayer:
             pass
 
 
-def host_weights_to_device(cfg, W, device="cuda"):
-    """Upload numpy weights made by synth.host_layer into the expert-major device layout."""
+def host_weights_to_device(cfg, W, device="cuda", experts=None):
+    """Upload numpy weights made by synth.host_layer into the expert-major device layout (the routed
+    experts in `experts`, e.g. an expert-parallel rank's shard; all by default)."""
+    experts = range(cfg.n_experts) if experts is None else experts
     out = {"router_w": torch.from_numpy(W["router_w"]).to(device),
            "router_bias": torch.from_numpy(W["router_bias"]).to(device),
            "routed_w": [], "routed_s": [], "shared_w": None, "shared_s": None}
     for m in range(3):
-        out["routed_w"].append(torch.from_numpy(np.stack([W["routed"][m][e][0] for e in range(cfg.n_experts)])).to(device))
-        out["routed_s"].append(torch.from_numpy(np.stack([W["routed"][m][e][1] for e in range(cfg.n_experts)])).to(device))
+        out["routed_w"].append(torch.from_numpy(np.stack([W["routed"][m][e][0] for e in experts])).to(device))
+        out["routed_s"].append(torch.from_numpy(np.stack([W["routed"][m][e][1] for e in experts])).to(device))
     if cfg.shared_fmt != FMT_NONE:
         out["shared_w"] = [torch.from_numpy(W["shared"][m][0]).to(device) for m in range(3)]
         out["shared_s"] = [torch.from_numpy(W["shared"][m][1]).to(device) for m in range(3)]

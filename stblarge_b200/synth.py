@@ -143,12 +143,14 @@ def mat_shapes(cfg):
     return ((I, H), (I, H), (H, I))
 
 
-def device_layer(cfg, device="cuda"):
+def device_layer(cfg, device="cuda", experts=None):
     """Quantized device tensors in the expert-major layout the C ABI takes:
     'routed_w'[m]: uint8 [E, rows, codes per row]; 'routed_s'[m]: scales [E, ...];
     'shared_w'[m], 'shared_s'[m] likewise without the expert axis; 'router_w' fp32 [E, H];
-    'router_bias' fp32 [E]."""
-    E = cfg.n_experts
+    'router_bias' fp32 [E].  experts: the routed experts to build (a range: an expert-parallel
+    rank's shard; expert e keeps seed 1000 + e), all by default."""
+    experts = range(cfg.n_experts) if experts is None else experts
+    E = len(experts)
     shapes = mat_shapes(cfg)
     routed_w, routed_s = [], []
     for m, (r, k) in enumerate(shapes):
@@ -158,14 +160,14 @@ def device_layer(cfg, device="cuda"):
         else:
             routed_w.append(torch.empty(E, r, k // 2, dtype=torch.uint8, device=device))
             routed_s.append(torch.empty(E, r, k // 32, dtype=torch.uint8, device=device))
-    for e in range(E):
+    for i, e in enumerate(experts):
         g = torch.Generator(device=device)
         g.manual_seed(1000 + e)
         for m, (r, k) in enumerate(shapes):
             w = torch.randn(r, k, generator=g, device=device, dtype=torch.float32) * cfg.weight_std
             c, s = quantize(w, cfg.routed_fmt)
-            routed_w[m][e].copy_(c)
-            routed_s[m][e].copy_(s)
+            routed_w[m][i].copy_(c)
+            routed_s[m][i].copy_(s)
     out = {"routed_w": routed_w, "routed_s": routed_s, "shared_w": None, "shared_s": None}
     if cfg.shared_fmt != FMT_NONE:
         g = torch.Generator(device=device)

@@ -1,0 +1,56 @@
+"""Expert parallelism on 2 GPUs of one node (skipped with fewer): routed experts sharded over the
+ranks, dispatch and combine by the layer's own kernels through peer memory.  Bar: on every rank,
+expert ids and routing weights bit-exact and outputs within max-abs-rel 1e-2 of the oracle's
+single-device layer; a rank that skips a call makes the others' bounded device waits run out with
+a status bit, without a fault."""
+
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests import ep_worker
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(fn, n):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=fn, args=(r, n, port, q)) for r in range(n)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in ps:
+        rank, out, err = q.get(timeout=300)
+        res[rank] = (out, err)
+    for p in ps:
+        p.join(timeout=120)
+    return res
+
+
+def test_ep_two_ranks_match_oracle():
+    res = _run(ep_worker.parity, 2)
+    for rank, (out, err) in sorted(res.items()):
+        assert err is None, f"rank {rank}:\n{err}"
+        for r in out:
+            assert r["idx"] and r["w"], (rank, r)
+            assert r["rel"] <= ep_worker.TOL, (rank, r)
+            assert r["status"] == 0, (rank, r)
+
+
+def test_ep_skipped_call_times_out_with_status():
+    res = _run(ep_worker.skipped_call, 2)
+    for rank, (out, err) in sorted(res.items()):
+        assert err is None, f"rank {rank}:\n{err}"
+        assert out["first"] == 0
+    assert res[0][0]["second"] & 1, res[0]
