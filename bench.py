@@ -9,8 +9,12 @@ gets fresh tokens (different routing), and L2 is flushed before each step; each 
 CUDA events on the launching stream.  `e2e` is the same metric through the host-buffer entry point
 (stbl_moe_forward_host: H2D of x, layer, D2H of y, inside the timed region).
 
-N > 1: one process per GPU; each rank runs an independent full layer replica on its own tokens
-(weak scaling; expert parallelism is not built yet), time = max over ranks.
+N > 1: one process per GPU, expert parallelism: rank r holds routed experts [r 256/N, (r+1) 256/N)
+(the router and the shared expert are replicated); every rank routes its own tokens, and the
+layer's kernels dispatch them to the owning ranks and bring the outputs back through NVLink peer
+memory.  --workload cfg2 (default): T tokens per rank (weak scaling, the N=1 line is configs[1]);
+--workload cfg4: configs[3], 256 tokens in all split over the ranks (strong scaling), uniform
+routing (bias 0) or Zipf(1.2) with --zipf.  Time = max over ranks of the device time.
 
 --impl reference: the reference's CPU path (the CPU oracle restating stbl/model.cu:426-594 on the
 numerics of ref/kernel.py) on the host cores, same workload and metric; rank 0 only.
@@ -156,6 +160,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"])
+    ap.add_argument("--zipf", action="store_true", help="cfg4: Zipf(1.2) expert popularity instead of uniform")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -177,18 +183,34 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    cfg, T = CFG2, args.tokens
-    weights = synth.device_layer(cfg, device=dev)
-    layer = MoELayer(cfg, weights, max_tokens=max(T, 16))
+    import dataclasses
+    if args.workload == "cfg4":
+        cfg = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=1.2 if args.zipf else 0.0)
+        if 256 % world:
+            raise SystemExit("cfg4 splits 256 tokens over the ranks: --gpus must divide 256")
+        T = 256 // world
+    else:
+        cfg, T = CFG2, args.tokens
+    E_loc = cfg.n_experts // world
+    shard = range(rank * E_loc, (rank + 1) * E_loc)
+    weights = synth.device_layer(cfg, device=dev, experts=shard)
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 16), ep=(rank, world, None) if world > 1 else None)
     n_steps = args.warmup + args.steps
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
                       for i in range(n_steps)]).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
 
     def distinct_of(x):
-        """Distinct experts the layer routes x to (untimed pass; reads the routing back)."""
+        """Distinct routed experts of this rank's shard that the step streams: the experts that any
+        rank's tokens are routed to (untimed pass, every rank in step; routes read back)."""
         layer(x)
-        return len(np.unique(layer.last_route()["idx"]))
+        ids = layer.last_route()["idx"]
+        if world > 1:
+            allids = [None] * world
+            dist.all_gather_object(allids, ids)
+            ids = np.concatenate([a.reshape(-1) for a in allids])
+        ids = np.unique(ids)
+        return int(np.sum((ids >= shard.start) & (ids < shard.stop)))
 
     def timed_steps(inputs):
         """Device time of each call, L2 flushed before each; nothing synchronises inside the loop, so
@@ -255,7 +277,7 @@ def main():
 
     # batch-size sweep of configs[1] (1, 4, 16 tokens): device time per call and per kernel
     sweep = []
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1 and args.workload == "cfg2":
         for Ts in (1, 4, 16):
             xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
                    for i in range(23)]
@@ -298,13 +320,19 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 weights and activations, fp32 accumulate, bf16 io",
+            "scaling": "strong" if args.workload == "cfg4" else "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 weights and activations, fp32 accumulate, bf16 io",
             "data": "synthetic (seeded ~N(0,0.02) weights quantized to FP8 128x128; bf16 ~N(0,1) tokens)",
-            "config": {"workload": f"cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4), "
-                                   f"T={T} decode tokens per rank", "tokens_per_rank": T,
-                       "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+            "config": {"workload": (f"cfg4 expert-parallel full-size FP8 MoE layer, 256 tokens split over {world} GPU(s), "
+                                    f"{'Zipf(1.2)' if args.zipf else 'uniform'} routing"
+                                    if args.workload == "cfg4" else
+                                    "cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4)")
+                                   + f", T={T} decode tokens per rank", "tokens_per_rank": T,
+                       "parallelism": "single GPU" if world == 1 else
+                       f"ep{world}: expert parallelism, {E_loc} routed experts per GPU, dispatch/combine through NVLink peer memory",
                        "l2": "flushed (256 MB write) before every timed step; fresh tokens each step"},
             "hbm_gbs": hbm_gbs, "hbm_frac_of_measured": hbm_gbs / peak, "hbm_frac_of_8tbs": hbm_gbs / HBM_NOMINAL_GBS,
+            "hbm_note": "per GPU (rank 0): its shard's distinct routed experts + shared expert + router + x/y, over its device time",
             "distinct_experts_per_step": float(np.mean(distinct)),
             "kernel_ms_per_step": {"router": kt["router"] / max(kt["calls"], 1) * 1e3, "up": up_ms,
                                    "down": kt["down"] / max(kt["calls"], 1) * 1e3},
