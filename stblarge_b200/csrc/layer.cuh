@@ -71,6 +71,11 @@ struct RouterParams {
     uint8_t *xq_b;
     float *xs_b;
     int blk_b, pow2_b;
+    // selection state shared by the select kernel's CTAs: [E] counts, [E][ceil(T/32)] token bitmaps,
+    // a ticket; zeroed by the logits kernel
+    int *sel_cnt;
+    uint32_t *sel_bm;
+    unsigned int *sel_ticket;
     uint32_t *status;
 };
 

@@ -80,6 +80,9 @@ struct stbl_moe {
     bool ep_connected = false;
     unsigned int ep_epoch = 0;
     int *a_dst = nullptr, *n_rows = nullptr;
+    int *sel_cnt = nullptr;
+    uint32_t *sel_bm = nullptr;
+    unsigned int *sel_ticket = nullptr;
     void *ws = nullptr;
     size_t ws_bytes = 0;
     float *scores = nullptr, *wts = nullptr, *xs_a = nullptr, *xs_b = nullptr;
@@ -308,6 +311,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->tc_flags = carve<unsigned int>(p, m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
+        m->sel_cnt = carve<int>(p, Eg);
+        m->sel_bm = carve<uint32_t>(p, (size_t)Eg * ((T + 31) / 32));
+        m->sel_ticket = carve<unsigned int>(p, 4);
         return (size_t)(p - base);
     };
     m->ws_bytes = layout(nullptr);
@@ -529,6 +535,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
     r.nt_routed = m->routed_tc ? 16 : kNT;
     r.nt_shared = 16;
+    r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
     CK(launch_router(r, st, true));
     if (m->timing) CK(cudaEventRecord(tc.ev[1], st));

@@ -35,7 +35,10 @@ constexpr size_t kNaXs = kNaXq + (size_t)kNaMaxTokens * kNaMaxHidden;           
 constexpr size_t kNaChunks = kNaXs + sizeof(float) * kNaMaxTokens * (kNaMaxHidden / 32);  // Chunk [T * (topk + 1)]
 constexpr size_t kNaNChunks = kNaChunks + sizeof(Chunk) * kNaMaxTokens * (kNaMaxTopk + 1);  // int [4]
 constexpr size_t kNaStatus = kNaNChunks + 256;                                         // u32 status
-constexpr size_t kNaBytes = kNaStatus + 256;
+constexpr size_t kNaSelCnt = kNaStatus + 256;                                          // int [E]
+constexpr size_t kNaSelBm = kNaSelCnt + sizeof(int) * kNaMaxExperts;                  // u32 [E][T / 32]
+constexpr size_t kNaSelTicket = kNaSelBm + sizeof(uint32_t) * kNaMaxExperts * (kNaMaxTokens / 32);  // u32
+constexpr size_t kNaBytes = kNaSelTicket + 256;
 
 static __device__ __align__(256) unsigned char g_route_scratch[kNaBytes];
 
@@ -107,6 +110,9 @@ extern "C" int stbl_route_noalloc(const float *router_w, const float *router_bia
     r.xs_a = r.xs_b = reinterpret_cast<float *>(base + kNaXs);
     r.blk_a = r.blk_b = 128, r.pow2_a = r.pow2_b = 0;
     r.status = reinterpret_cast<uint32_t *>(base + kNaStatus);
+    r.sel_cnt = reinterpret_cast<int *>(base + kNaSelCnt);
+    r.sel_bm = reinterpret_cast<uint32_t *>(base + kNaSelBm);
+    r.sel_ticket = reinterpret_cast<unsigned int *>(base + kNaSelTicket);
     const cudaError_t e = launch_router(r, stream, false);
     if (e != cudaSuccess) {
         if (err && errlen > 0) snprintf(err, errlen, "stbl_route_noalloc: %s", cudaGetErrorString(e));

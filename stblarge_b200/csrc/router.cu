@@ -6,8 +6,8 @@
 // router weights never change), computes the slice partials of 4 experts x 8 tokens per warp from
 // registers, and the ksplit CTAs of a cluster add their partials in slice order through distributed
 // shared memory.  It also does the activation quantization of x for the expert kernels.
-// router_select_kernel (one CTA of 512 threads): group-limited top-k per token (a warp per token),
-// routing weights, and the bucketed permutation + chunk table.
+// router_select_kernel (a CTA of 512 threads per 16 tokens): group-limited top-k per token (a warp
+// per token), routing weights; the last CTA builds the bucketed permutation + chunk table.
 //
 // Replaces the reference's router GEMV, score kernel, blocking device->host copy and host
 // partial_sort (stbl/model.cu:430-452, stbl/kernels.cu:206-214, 437-442): nothing leaves the GPU.
@@ -163,6 +163,12 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
     };
     stage_x(0, xr);
     pdl_launch_dependents();
+    if (blockIdx.x == 0) {  // the select kernel's global counts, token bitmaps and ticket start at zero
+        const int TW = (p.T + 31) / 32;
+        for (int i = tid; i < p.E; i += kLgThreads) p.sel_cnt[i] = 0;
+        for (int i = tid; i < p.E * TW; i += kLgThreads) p.sel_bm[i] = 0;
+        if (tid == 0) *p.sel_ticket = 0;
+    }
 
     // activation quantization of x for the expert kernels, spread over every warp of the grid
     {
@@ -247,8 +253,8 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
 // a chain of warp collectives (about 25 cycles each), so independent collectives are issued
 // unconditionally and the per-lane argmax is a tree.
 template <int EJ>
-__device__ __forceinline__ void select_token(const RouterParams &p, int t, int lane, int *sidx, int *cnt, uint32_t *bm,
-                                             int TW, bool live) {
+__device__ __forceinline__ void select_token(const RouterParams &p, int t, int lane, int *sel_row, int *cnt, uint32_t *bm,
+                                             int TW, int tb, bool live) {
     const int E = p.E, K = p.topk;
     const uint32_t lane_bit = 1u << lane;
     uint32_t key[EJ];
@@ -370,71 +376,104 @@ __device__ __forceinline__ void select_token(const RouterParams &p, int t, int l
         float wt = s_mine;
         wt /= sum + 1e-20f;
         wt *= p.route_scale;
-        if (live) {
-            p.idx[t * K + lane] = mine;
-            p.wts[t * K + lane] = wt;
-        }
-        sidx[t * K + lane] = mine;
-        // dispatch counts and the expert's token bitmap (a token picks an expert at most once)
+        if (live) p.wts[t * K + lane] = wt;
+        sel_row[lane] = mine;  // p.idx + t K in the live pass
+        // dispatch counts and the expert's token bitmap (a token picks an expert at most once); bit
+        // tb stands for the token
         atomicAdd(&cnt[mine], 1);
-        atomicOr(&bm[mine * TW + (t >> 5)], 1u << (t & 31));
+        atomicOr(&bm[mine * TW + (tb >> 5)], 1u << (tb & 31));
     }
 }
 
-__host__ __device__ inline size_t router_select_smem(int T, int E, int K) {
-    const int TW = (T + 31) / 32;
-    return (size_t)T * K * 4 + 2 * (size_t)E * 4 + (size_t)E * TW * 4;
+// tokens selected by one CTA of the select kernel (one per warp)
+constexpr int kSelTokensPerCta = kSelThreads / 32;
+
+__host__ __device__ inline size_t router_select_smem(int E, int K, int T) {
+    return (size_t)kSelTokensPerCta * K * 4 + 2 * (size_t)E * 4 + (size_t)E * ((T + 31) / 32) * 4;
 }
 
+// One CTA per 16 tokens (a warp per token).  Every CTA adds its tokens' choices to the global
+// per-expert counts and token bitmaps (zeroed by the logits kernel); the last CTA to finish (by an
+// atomic ticket) builds the bucketed dispatch for all T tokens.
 __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int is_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = p.E, T = p.T, K = p.topk;
-    const int TW = (T + 31) / 32;
     const int sh_r = __ffs(p.nt_routed) - 1, sh_s = __ffs(p.nt_shared) - 1;  // chunk sizes: powers of two
-    int *sidx = reinterpret_cast<int *>(smem);  // [T][K]
-    int *cnt = sidx + T * K;                    // [E] assignments per expert
-    int *pk = cnt + E;                          // [E] exclusive scan of assignments | chunks << 16
-    uint32_t *bm = reinterpret_cast<uint32_t *>(pk + E);  // [E][TW] tokens of each expert
+    const int t0 = blockIdx.x * kSelTokensPerCta, n_own = min(kSelTokensPerCta, T - t0);
+    int *s_idx = reinterpret_cast<int *>(smem);        // [16][K] (first pass)
+    int *s_cnt = s_idx + kSelTokensPerCta * K;         // [E] (first pass)
+    int *pk = s_cnt + E;                               // [E] exclusive scan of assignments | chunks << 16
+    uint32_t *s_bm = reinterpret_cast<uint32_t *>(pk + E);  // [E][TW] (first pass: 16 tokens, one word)
     // registers per lane for E experts, rounded up to a power of two
     const int ej = E <= 32 ? 1 : E <= 64 ? 2 : E <= 128 ? 4 : E <= 256 ? 8 : 16;
 
     // Two passes over one copy of the code.  The first runs before the programmatic-launch wait,
-    // while the logits kernel is still computing, on at most one token per warp: it reads whatever
-    // the scores buffer holds and stores nothing to global memory; it only brings this kernel's
-    // instructions into the SM's instruction caches, so that the second, real pass does not stall
-    // on instruction fetches.
+    // while the logits kernel is still computing, on this CTA's tokens and shared memory only: it
+    // reads whatever the scores buffer holds and stores nothing to global memory; it only brings this
+    // kernel's instructions into the SM's instruction caches, so that the second, real pass does not
+    // stall on instruction fetches.
 #pragma unroll 1
     for (int pass = 0; pass < 2; pass++) {
         const bool live = pass == 1;
-        for (int e = tid; e < E; e += kSelThreads) cnt[e] = 0;
-        for (int i = tid; i < E * TW; i += kSelThreads) bm[i] = 0;
+        // several CTAs (live pass): global counts and bitmaps of all T tokens; one CTA, or the first
+        // pass: shared memory
+        const bool global_state = live && gridDim.x > 1;
+        int *cnt = global_state ? p.sel_cnt : s_cnt;
+        uint32_t *bm = global_state ? p.sel_bm : s_bm;
+        const int TW = live ? (T + 31) / 32 : 1;
+        if (!global_state)
+            for (int e = tid; e < E * TW; e += kSelThreads) s_bm[e] = 0;
+        if (!global_state)
+            for (int e = tid; e < E; e += kSelThreads) s_cnt[e] = 0;
         if (live) {
-            pdl_wait();  // scores and quantized x of the logits kernel
+            pdl_wait();  // scores, quantized x and the zeroed global counts of the logits kernel
             pdl_launch_dependents();
         }
         __syncthreads();
-        const int t_end = live ? T : min(T, kSelThreads / 32);
-        for (int t = warp; t < t_end; t += kSelThreads / 32) {
+        if (warp < n_own) {
+            const int t = t0 + warp;
+            int *sel_row = live ? p.idx + (size_t)t * K : s_idx + warp * K;
+            const int tb = live ? t : warp;
             switch (ej) {
-                case 1: select_token<1>(p, t, lane, sidx, cnt, bm, TW, live); break;
-                case 2: select_token<2>(p, t, lane, sidx, cnt, bm, TW, live); break;
-                case 4: select_token<4>(p, t, lane, sidx, cnt, bm, TW, live); break;
-                case 8: select_token<8>(p, t, lane, sidx, cnt, bm, TW, live); break;
-                default: select_token<16>(p, t, lane, sidx, cnt, bm, TW, live); break;
+                case 1: select_token<1>(p, t, lane, sel_row, cnt, bm, TW, tb, live); break;
+                case 2: select_token<2>(p, t, lane, sel_row, cnt, bm, TW, tb, live); break;
+                case 4: select_token<4>(p, t, lane, sel_row, cnt, bm, TW, tb, live); break;
+                case 8: select_token<8>(p, t, lane, sel_row, cnt, bm, TW, tb, live); break;
+                default: select_token<16>(p, t, lane, sel_row, cnt, bm, TW, tb, live); break;
             }
+        }
+        if (global_state) {
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) is_last = atomicAdd(p.sel_ticket, 1u) == gridDim.x - 1;
+            __syncthreads();
+            if (!is_last) break;
+            __threadfence();
+            // every CTA's counts and bitmaps, into shared memory for the dispatch below
+            for (int e = tid; e < E; e += kSelThreads) s_cnt[e] = __ldcg(p.sel_cnt + e);
+            for (int i = tid; i < E * TW; i += kSelThreads) s_bm[i] = __ldcg(p.sel_bm + i);
+            cnt = s_cnt;
+            bm = s_bm;
         }
         __syncthreads();
 
-        // bucketed dispatch.  Warp 0 scans (assignments | chunks << 16) over the experts, lane l
-        // owning experts l * epl .. (l + 1) * epl - 1; every thread then places its assignments by
-        // their stable rank among the expert's tokens (the expert's token bitmap).
+        // bucketed dispatch over n tokens (live: all T; first pass: this CTA's), from shared memory.
+        // Warp 0 scans (assignments | chunks << 16) over the experts, lane l owning experts
+        // l * epl .. (l + 1) * epl - 1; every thread then places assignments by their stable rank among
+        // the expert's tokens (the expert's token bitmap).
+        const int n = live ? T : n_own;
+        const int *sel = live ? p.idx : s_idx;
         if (warp == 0) {
             const int epl = (E + 31) / 32, e0 = lane * epl;
             int run = 0;
             for (int i = 0; i < epl; i++) {
                 const int e = e0 + i;
-                if (e < E) run += cnt[e] | (((cnt[e] + p.nt_routed - 1) >> sh_r) << 16);
+                if (e < E) {
+                    const int c = cnt[e];
+                    run += c | (((c + p.nt_routed - 1) >> sh_r) << 16);
+                }
             }
             int incl = run;
 #pragma unroll
@@ -447,15 +486,17 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
                 const int e = e0 + i;
                 if (e < E) {
                     pk[e] = acc;
-                    acc += cnt[e] | (((cnt[e] + p.nt_routed - 1) >> sh_r) << 16);
+                    const int c = cnt[e];
+                    acc += c | (((c + p.nt_routed - 1) >> sh_r) << 16);
                 }
             }
         }
         __syncthreads();
-        for (int a = tid; a < t_end * K; a += kSelThreads) {
-            const int e = sidx[a], t = a / K;
-            int rank = __popc(bm[e * TW + (t >> 5)] & ((1u << (t & 31)) - 1u));
-            for (int w = 0; w < (t >> 5); w++) rank += __popc(bm[e * TW + w]);
+        for (int a = tid; a < n * K; a += kSelThreads) {
+            const int e = live ? __ldcg(sel + a) : sel[a], t = a / K;
+            const uint32_t *row = bm + (size_t)e * TW;
+            int rank = __popc(row[t >> 5] & ((1u << (t & 31)) - 1u));
+            for (int w = 0; w < (t >> 5); w++) rank += __popc(row[w]);
             if (live) p.perm[(pk[e] & 0xffff) + rank] = a;
         }
         const int ns = p.has_shared ? (T + p.nt_shared - 1) >> sh_s : 0;
@@ -506,9 +547,9 @@ cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first) {
     cfg.numAttrs = pdl_first ? 2 : 1;
     cudaError_t e = cudaLaunchKernelExC(&cfg, (const void *)router_logits_kernel, args);
     if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3(1);
+    cfg.gridDim = dim3((r.T + kSelTokensPerCta - 1) / kSelTokensPerCta);
     cfg.blockDim = dim3(kSelThreads);
-    cfg.dynamicSmemBytes = router_select_smem(r.T, r.E, r.topk);
+    cfg.dynamicSmemBytes = router_select_smem(r.E, r.topk, r.T);
     cfg.attrs = attr + 1;
     cfg.numAttrs = 1;
     return cudaLaunchKernelExC(&cfg, (const void *)router_select_kernel, args);
