@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from stblarge_b200 import synth  # noqa: E402
-from stblarge_b200.config import CFG2  # noqa: E402
+from stblarge_b200.config import CFG2, CFG3, FMT_MXFP4  # noqa: E402
 
 METRIC = "MoE-layer decode tokens/s (full-size FP8 layer)"
 UNIT = "tokens/s"
@@ -62,6 +62,8 @@ def up_bytes(cfg, n_distinct):
     H, I = cfg.hidden, cfg.inter
 
     def mat(fmt):
+        if fmt == FMT_MXFP4:
+            return I * H // 2 + I * (H // 32)
         return I * H + 4 * ((I + 127) // 128) * ((H + 127) // 128)
     return 2 * (n_distinct * mat(cfg.routed_fmt) + mat(cfg.shared_fmt))
 
@@ -160,7 +162,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"])
     ap.add_argument("--zipf", action="store_true", help="cfg4: Zipf(1.2) expert popularity instead of uniform")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -189,12 +191,15 @@ def main():
         if 256 % world:
             raise SystemExit("cfg4 splits 256 tokens over the ranks: --gpus must divide 256")
         T = 256 // world
+    elif args.workload == "cfg3":
+        cfg, T = CFG3, args.tokens
     else:
         cfg, T = CFG2, args.tokens
     E_loc = cfg.n_experts // world
     shard = range(rank * E_loc, (rank + 1) * E_loc)
     weights = synth.device_layer(cfg, device=dev, experts=shard)
-    layer = MoELayer(cfg, weights, max_tokens=max(T, 16), ep=(rank, world, None) if world > 1 else None)
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if args.workload == "cfg3" else 16),
+                     ep=(rank, world, None) if world > 1 else None)
     n_steps = args.warmup + args.steps
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
                       for i in range(n_steps)]).to(dev)
@@ -277,8 +282,8 @@ def main():
 
     # batch-size sweep of configs[1] (1, 4, 16 tokens): device time per call and per kernel
     sweep = []
-    if not args.no_sweep and world == 1 and args.workload == "cfg2":
-        for Ts in (1, 4, 16):
+    if not args.no_sweep and world == 1 and args.workload in ("cfg2", "cfg3"):
+        for Ts in ((1, 4, 16) if args.workload == "cfg2" else (1, 4, 16, 64)):
             xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
                    for i in range(23)]
             for i in range(3):
@@ -326,6 +331,8 @@ def main():
             "config": {"workload": (f"cfg4 expert-parallel full-size FP8 MoE layer, 256 tokens split over {world} GPU(s), "
                                     f"{'Zipf(1.2)' if args.zipf else 'uniform'} routing"
                                     if args.workload == "cfg4" else
+                                    "cfg3 full-size layer, MXFP4 routed experts (FP8 shared), Zipf(1.0) routing"
+                                    if args.workload == "cfg3" else
                                     "cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4)")
                                    + f", T={T} decode tokens per rank", "tokens_per_rank": T,
                        "parallelism": "single GPU" if world == 1 else

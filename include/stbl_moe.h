@@ -82,8 +82,10 @@ int stbl_moe_last_route(stbl_moe *m, int *idx, float *weights, int *counts, int 
 /* Router scores of the last call (fp32 [T][E]), for parity checks.  Returns T, or -1. */
 int stbl_moe_last_scores(stbl_moe *m, float *scores);
 
-/* Point routed expert e at other device memory (an expert cache slot).  Takes effect for calls
- * enqueued on `stream` after this one. */
+/* Point routed expert e at another slot of the layer's expert arrays (an expert cache: the arrays
+ * passed in the description are the slot pool, slot j at routed_w[m] + j * routed_w_stride[m]).  w and
+ * s must be the same slot j for all three matrices and their scales.  Takes effect for calls enqueued
+ * on `stream` after this one. */
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream);
 
 /* Device status bits raised by kernels since the last call of this function (waits for the

@@ -1,0 +1,58 @@
+// Ordered combine of the MoE layer: y = bf16(((0 + eo_0) + ... + eo_{k-1}) + shared), the sums in fp32
+// in top-k order (stbl/model.cu:589-592, the reference's k_axpy chain + k_round_bf16), one thread per
+// 8 outputs.  Under expert parallelism the routed rows were written by the owning GPUs; the kernel
+// first raises this rank's done flag everywhere and waits for every rank's.
+#include "layer.cuh"
+
+namespace stbl {
+
+__global__ void __launch_bounds__(256) combine_kernel(CombineParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (p.ep.n_ranks > 1) {
+        // expert parallelism: this rank's down kernel (before this one) has finished writing into
+        // every source rank's eo rows: say so everywhere, then wait until every rank has said so
+        __shared__ int ok;
+        if (threadIdx.x == 0) {
+            if (blockIdx.x == 0) signal_all(p.ep, p.ep.L.done_flag);
+            ok = wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.done_flag),
+                                p.ep.n_ranks, p.ep.epoch);
+            if (!ok) atomicOr(p.status, kErrWaitTimeout);
+        }
+        __syncthreads();
+    }
+    const int per_row = p.H / 8;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= p.T * per_row) return;
+    const int t = i / per_row, c = (i % per_row) * 8;
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc[q] = 0.f;
+    for (int s = 0; s < p.topk; s++) {
+        // L2 loads: under expert parallelism the rows were written by other GPUs during this call
+        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.eo + ((size_t)t * p.topk + s) * p.H + c));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            acc[2 * q] = acc[2 * q] + __uint_as_float(w[q] << 16);
+            acc[2 * q + 1] = acc[2 * q + 1] + __uint_as_float(w[q] & 0xffff0000u);
+        }
+    }
+    if (p.has_shared) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p.sh + (size_t)t * p.H + c));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            acc[2 * q] = acc[2 * q] + __uint_as_float(w[q] << 16);
+            acc[2 * q + 1] = acc[2 * q + 1] + __uint_as_float(w[q] & 0xffff0000u);
+        }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) o[q] = (uint32_t)f32_to_bf16_bits(acc[2 * q]) | ((uint32_t)f32_to_bf16_bits(acc[2 * q + 1]) << 16);
+    *reinterpret_cast<uint4 *>(p.y + (size_t)t * p.H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+const void *combine_kernel_ptr() { return (const void *)combine_kernel; }
+
+}  // namespace stbl

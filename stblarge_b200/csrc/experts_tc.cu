@@ -22,11 +22,11 @@
 #include "layer.cuh"
 #include "tc_params.cuh"
 #include "umma.cuh"
+#include "tc_common.cuh"
 
 namespace stbl {
 
 constexpr int kTcThreads = 192;
-constexpr int kTcN = 16;          // token columns per MMA (chunk size)
 constexpr int kTcG = 4;           // 128-K blocks per accumulator group (one TMEM read per group)
 constexpr int kTcGroups = 4;      // accumulator groups in TMEM (4 x 4 x 16 columns)
 constexpr int kTcAcc = kTcGroups;
@@ -37,44 +37,6 @@ constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzl
 constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
 constexpr int kTcChunks = 32;     // chunk entries of a CTA's item range kept in shared memory
 constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
-
-struct TcChunk {
-    int e, pos0, n, ok;
-};
-
-__device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
-    TcChunk r{ch.e, ch.pos0, ch.n, 1};
-    const int nrouted = p.n_routed;
-    const bool shared = ch.e == p.E;
-    const bool bad = ch.e < 0 || ch.e > p.E || (shared && !p.has_shared) || ch.n < 1 || ch.n > kTcN ||
-                     (shared ? (ch.pos0 < nrouted || ch.pos0 + ch.n > nrouted + p.T)
-                             : (ch.pos0 < 0 || ch.pos0 + ch.n > nrouted));
-    if (bad) r = TcChunk{0, 0, 0, 0};
-    return r;
-}
-
-// first row of the chunk's B tiles: b_direct (x by token): routed chunks (T <= 16) read tokens 0..15
-// and use column = token; shared chunks read their own 16 consecutive tokens, column = slot.
-// Otherwise (rows by position) the chunk's first position, column = slot.
-__device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
-    if (!p.b_direct) return ch.pos0;
-    return ch.e == p.E ? ch.pos0 - p.n_routed : 0;
-}
-
-__device__ __forceinline__ void flag_release(unsigned int *f, unsigned int v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
-}
-
-// wait until *f == v; gives up when *abort is raised or after kWaitLimitNs
-__device__ __forceinline__ bool flag_wait(const unsigned int *f, unsigned int v, volatile int *abort) {
-    const uint64_t t0 = global_ns();
-    for (;;) {
-        unsigned int x;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(x) : "l"(f) : "memory");
-        if (x == v) return true;
-        if (*abort || global_ns() - t0 > kWaitLimitNs) return false;
-    }
-}
 
 template <bool UP>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p,
@@ -162,7 +124,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 const int c = p.chunk_begin + it / tiles, tile = it % tiles;
                 const TcChunk ch = chunk_of(c);
                 const bool shared = ch.e == p.E;
-                const int z = shared ? 0 : ch.e;
+                const int z = shared ? 0 : expert_slot(p, ch.e);
                 const int brow = b_row(p, ch);
                 int ka, kz;
                 k_range(it, ka, kz);
@@ -279,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
             if (et < nsw) {
                 const int m = et / nkb, kb = et % nkb;
                 const int rblk = UP ? (tile * 64) / 128 : tile;
-                const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)ch.e * p.w_scale_stride;
+                const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
                 pw = __ldg(base + (size_t)rblk * nkb + kb);
             }
             if (et < kTcN) {
@@ -403,7 +365,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
                 const int i = et & 63, r = tile * 64 + i;
                 for (int j = et >> 6; j < ch.n; j += 2) {
                     const int col = scol[j];
-                    const float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
+                    float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
+                    if (p.swiglu_limit > 0.f) {
+                        gv = fminf(gv, p.swiglu_limit);
+                        uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
+                    }
                     const float hv = gv / (1.f + expf(-gv)) * uv * swt[j];
                     p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
                 }
@@ -452,8 +418,14 @@ __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
     const uint4 *src = reinterpret_cast<const uint4 *>(p.xq + (size_t)tok * p.H);
     uint4 *dst = reinterpret_cast<uint4 *>(p.xq_pos + (size_t)pos * p.H);
     for (int i = threadIdx.x; i < p.H / 16; i += blockDim.x) dst[i] = __ldg(src + i);
-    for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x)
-        p.xs_pos[(size_t)pos * (p.H / 128) + i] = __ldg(p.xs + (size_t)tok * p.xs_stride + i);
+    if (p.xe8) {
+        const uint32_t *se = reinterpret_cast<const uint32_t *>(p.xe8 + (size_t)tok * (p.H / 32));
+        uint32_t *de = reinterpret_cast<uint32_t *>(p.xe8_pos + (size_t)pos * (p.H / 32));
+        for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x) de[i] = __ldg(se + i);
+    } else {
+        for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x)
+            p.xs_pos[(size_t)pos * (p.H / 128) + i] = __ldg(p.xs + (size_t)tok * p.xs_stride + i);
+    }
 }
 
 // act_quant per 128 (ref/kernel.py:35-45, fp32 scale amax/448) of h for the down kernel: one warp per
@@ -475,13 +447,20 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
         const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
                             __uint_as_float(xv.y & 0xffff0000u)};
         float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-        amax = fmaxf(warp_max(amax), 1e-4f);
-        const float s = amax * (1.0f / 448.0f);
+        // per-128: fp32 amax / 448 over the warp; per-32: power-of-two ceiling over 8 lanes
+        for (int o = p.he8 ? 4 : 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        amax = fmaxf(amax, 1e-4f);
+        const float tq = amax * (1.0f / 448.0f);
+        const float s = p.he8 ? pow2_ceil(tq) : tq;
         uint32_t codes = 0;
 #pragma unroll
         for (int u = 0; u < 4; u++) codes |= (uint32_t)e4m3_code(fminf(fmaxf(v[u] / s, -448.f), 448.f)) << (8 * u);
         *reinterpret_cast<uint32_t *>(p.hq + (size_t)pos * p.I + g * 128 + 4 * lane) = codes;
-        if (lane == 0) p.hs[(size_t)pos * per_row + g] = s;
+        if (p.he8) {
+            if ((lane & 7) == 0) p.he8[(size_t)pos * (p.I / 32) + g * 4 + (lane >> 3)] = (uint8_t)(__float_as_uint(s) >> 23);
+        } else if (lane == 0) {
+            p.hs[(size_t)pos * per_row + g] = s;
+        }
     }
 }
 

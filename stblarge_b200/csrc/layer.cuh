@@ -1,5 +1,5 @@
 // Device-side structures of the MoE layer: the expert pointer table, the dispatch chunks and the
-// parameter blocks of the three kernels that make up one layer call (router, expert up, expert down).
+// parameter blocks of the router and combine kernels.
 #pragma once
 
 #include <stdint.h>
@@ -19,20 +19,8 @@ constexpr int kLgExperts = 8;       // experts per logits CTA (two quads of 4)
 constexpr int kLgRound = 32;        // tokens staged in shared memory at a time
 constexpr int kLgMaxSlice = 2048;   // longest hidden slice (H / ksplit) the logits kernel stages
 constexpr int kSelThreads = 512;    // router selection kernel: one CTA, a warp per token
-constexpr int kExpertWarps = 15;    // warp 0 streams weights, warps 1..14 compute
-constexpr int kConsumerWarps = kExpertWarps - 1;
-constexpr int kConsumerThreads = 32 * kConsumerWarps;  // 448
-constexpr int kExpertThreads = 32 * kExpertWarps;      // 480
-constexpr int kNT = 4;              // tokens of one expert handled per pass over its weights
 
-// Device addresses of one expert's three matrices (0 gate [I][H], 1 up [I][H], 2 down [H][I]) and
-// their scales.  Entry E of the table is the shared expert.  The expert cache re-points entries.
-struct ExpertPtrs {
-    const uint8_t *w[3];
-    const void *s[3];
-};
-
-// Up to kNT tokens of one expert.  Rows pos0 .. pos0+n-1 of the position-ordered buffers (h, hq)
+// Up to 16 tokens of one expert.  Rows pos0 .. pos0+n-1 of the position-ordered buffers (h, hq)
 // belong to it.  Routed positions are the bucketed dispatch order; position p < T*topk is assignment
 // perm[p] = token * topk + slot.  Shared-expert positions are T*topk + token.
 struct Chunk {
@@ -68,6 +56,7 @@ struct RouterParams {
     uint8_t *xq_a;
     float *xs_a;
     int blk_a, pow2_a;
+    uint8_t *xe8_a;          // optional: scales of a as e8m0 bytes [T][H / 32] (per-32 power-of-two rule)
     uint8_t *xq_b;
     float *xs_b;
     int blk_b, pow2_b;
@@ -86,31 +75,6 @@ cudaError_t router_setup();
 // the logits kernel start while the previous kernel on the stream drains.  H / router_ksplit(H)
 // must be at most kLgMaxSlice and T at most kRouterMaxTokens.
 cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first);
-
-// One launch of the expert kernels covers chunks [chunk_begin, chunk_end); chunk_end < 0 means
-// "up to n_chunks[0]" (known only on the device).  Each CTA takes one contiguous range of the
-// launch's work items (chunk-major, tile-minor), so a CTA streams long contiguous runs of one
-// expert's rows and reloads its activations only when the chunk changes.
-struct ExpertParams {
-    const ExpertPtrs *experts;
-    const Chunk *chunks;
-    const int *n_chunks;
-    int chunk_begin, chunk_end;
-    int T, topk, E, H, I;
-    const int *perm;
-    const float *wts;
-    // up: x codes [T][H] + scales [T][xs_stride] from the router kernel
-    const uint8_t *xq;
-    const float *xs;
-    int xs_stride;           // scale floats per x row (H / 32: room for per-32 scales)
-    int act_blk, act_pow2;   // act_quant rule of this launch's weight format
-    float swiglu_limit;
-    uint16_t *h;             // [pos][I] bf16: written by up, read (and re-quantized in registers) by down
-    uint16_t *eo;            // [T * topk][H] bf16, routed outputs in (token, slot) order
-    uint16_t *sh;            // [T][H] bf16, shared-expert outputs
-    int has_shared;
-    uint32_t *status;
-};
 
 // ---- expert parallelism ------------------------------------------------------------------------
 //

@@ -18,9 +18,10 @@
 #include "ep.cuh"
 
 namespace stbl {
-const void *expert_kernel_ptr(int fmt, bool up);  // experts.cu
-const void *combine_kernel_ptr();                 // experts.cu
+const void *combine_kernel_ptr();                 // combine.cu
 const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
+const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
+int expert_tc4_smem_bytes(int nst);
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
@@ -36,16 +37,9 @@ using namespace stbl;
 
 namespace {
 
-constexpr int kRPG = 2;  // rows per row group per work item (the instantiation in experts.cu)
-
 // events of one timed call: before the router, after it, after the up launches, after the downs
 struct TimedCall {
     cudaEvent_t ev[4];
-};
-
-struct KernelCfg {
-    const void *fn = nullptr;
-    int stage_bytes = 0, nst = 0, smem = 0;
 };
 
 int act_blk_of(int fmt) { return fmt == STBL_FMT_FP8_B128 ? 128 : 32; }
@@ -57,14 +51,7 @@ long long mat_bytes(int fmt, int rows, int k, bool scales) {
     return scales ? (long long)rows * (k / 32) : (long long)rows * (k / 2);
 }
 
-bool lanes_ok(int K) {
-    if (K % 32) return false;
-    const int lk = K / 32;
-    if (lk >= 32) return lk % 32 == 0 && lk <= kConsumerThreads;
-    return lk >= 8 && 32 % lk == 0;
-}
 
-const void *expert_fn(int fmt, bool up) { return expert_kernel_ptr(fmt, up); }
 
 }  // namespace
 
@@ -94,13 +81,19 @@ struct stbl_moe {
     float *tc_partial = nullptr;      // split-item partial sums of the tensor-core kernels, [sms][128][16]
     unsigned int *tc_flags = nullptr; // [sms] launch number whose partial a CTA slot holds
     unsigned int tc_seq = 0;
-    ExpertPtrs *experts = nullptr;
-    std::vector<ExpertPtrs> host_experts;
-    KernelCfg up_r, down_r;           // CUDA-core kernels (MXFP4 routed experts)
+    // expert slots: routed expert e reads slot slot[e] of the strided weight arrays (an expert cache
+    // re-points experts at other slots, stbl_moe_set_expert)
+    int *slot = nullptr;
+    std::vector<int> host_slot;
+    long long w_stride[3] = {0, 0, 0}, s_stride[3] = {0, 0, 0};  // bytes between slots
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
-    bool routed_tc = false;           // routed experts on the tensor-core kernels
+    bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
+    bool routed_fp4 = false;          // routed experts MXFP4, on the block-scaled tensor-core kernels
+    TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
+    int tc4_nst = 0, tc4_smem = 0;
+    uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32)
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
@@ -156,6 +149,24 @@ CUtensorMap weight_map(const void *base, int K, int rows, int experts, long long
     return m;
 }
 
+// The same over MXFP4 codes (two per byte): the map's data type unpacks each 16 codes to 16 bytes in
+// shared memory, the layout kind::mxf8f6f4 reads e2m1 operands in; the transaction count of a box is
+// its packed size.  Needs 32-byte aligned base and strides.
+CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long long estride, int box_rows) {
+    CUtensorMap m;
+    if (((uintptr_t)base & 31) || (estride & 31) || ((K / 2) & 31))
+        throw std::runtime_error("MXFP4 expert weights must be 32-byte aligned (base, row and expert strides)");
+    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)experts};
+    const cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)estride};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void *>(base), dims, strides, box,
+                                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an MXFP4 expert weight tensor");
+    return m;
+}
+
 void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st);
 
 // 2-D tensor map over [rows][K] e4m3 activation codes, read in 16-row x 128-byte tiles (128B swizzle)
@@ -170,26 +181,6 @@ CUtensorMap act_map(const void *base, int K, int rows) {
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an activation tensor");
     return m;
-}
-
-KernelCfg make_cfg(int fmt, bool up, int H, int I, int max_smem) {
-    KernelCfg c;
-    c.fn = expert_fn(fmt, up);
-    const int nmat = up ? 2 : 1;
-    const int K = up ? H : I;
-    const int lk = K / 32, n_rg = kConsumerThreads / lk, RI = n_rg * kRPG;
-    const int rb = fmt == STBL_FMT_FP8_B128 ? K : K / 2;
-    int stage = nmat * RI * rb + (fmt == STBL_FMT_MXFP4 ? nmat * RI * (K / 32) : 0);
-    stage = (stage + 127) & ~127;
-    const int extra = 2 * 8 * 8 + 2 * 1024 * 4 + 128;
-    int nst = (max_smem - extra) / stage;
-    if (nst > 8) nst = 8;
-    if (nst < 2) throw std::runtime_error("expert weight tile does not fit twice in shared memory");
-    c.stage_bytes = stage;
-    c.nst = nst;
-    c.smem = nst * stage + 2 * nst * 8 + 2 * 1024 * 4;
-    CK(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
-    return c;
 }
 
 // exchange-region layout (expert parallelism); the same on every rank
@@ -224,8 +215,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     m->ep_rank = ep_rank, m->ep_n = ep_n;
     // the router sees every expert; the expert kernels see this rank's E / n_ranks
     const int E = Eg / ep_n;
-    if (H <= 0 || I <= 0 || H % 512 || I % 512 || !lanes_ok(H) || !lanes_ok(I))
-        throw std::runtime_error("hidden and inter must be multiples of 512 with K/32 lanes a multiple or divisor of 32 (<= 448)");
+    if (H <= 0 || I <= 0 || H % 512 || I % 512) throw std::runtime_error("hidden and inter must be multiples of 512");
     if (Eg < 1 || Eg > kMaxExperts) throw std::runtime_error("n_experts must be in 1..512");
     if (K < 1 || K > kMaxTopk || K > Eg) throw std::runtime_error("topk must be in 1..16 and <= n_experts");
     if (d->n_groups < 1 || d->n_groups > 32 || Eg % d->n_groups) throw std::runtime_error("n_groups must divide n_experts and be <= 32");
@@ -244,26 +234,20 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     m->ksplit = router_ksplit(H);
     m->has_shared = d->shared_fmt != STBL_FMT_NONE;
 
-    // expert table (entry E: shared expert)
-    m->host_experts.assign(E + 1, ExpertPtrs{});
+    // routed experts: slots of strided arrays (slot e = expert e until an expert cache re-points it)
+    m->host_slot.resize(E);
+    for (int e = 0; e < E; e++) m->host_slot[e] = e;
     const int rows[3] = {I, I, H}, ks[3] = {H, H, I};
     for (int mt = 0; mt < 3; mt++) {
         if (!d->routed_w[mt] || !d->routed_s[mt]) throw std::runtime_error("routed expert weights missing");
-        const long long wst = d->routed_w_stride[mt] ? d->routed_w_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], false);
-        const long long sst = d->routed_s_stride[mt] ? d->routed_s_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], true);
-        for (int e = 0; e < E; e++) {
-            const uint8_t *w = static_cast<const uint8_t *>(d->routed_w[mt]) + (size_t)e * wst;
-            const uint8_t *s = static_cast<const uint8_t *>(d->routed_s[mt]) + (size_t)e * sst;
-            if (((uintptr_t)w & 15) || ((uintptr_t)s & 15)) throw std::runtime_error("expert weights must be 16-byte aligned");
-            m->host_experts[e].w[mt] = w;
-            m->host_experts[e].s[mt] = s;
-        }
+        m->w_stride[mt] = d->routed_w_stride[mt] ? d->routed_w_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], false);
+        m->s_stride[mt] = d->routed_s_stride[mt] ? d->routed_s_stride[mt] : mat_bytes(d->routed_fmt, rows[mt], ks[mt], true);
+        if (((uintptr_t)d->routed_w[mt] & 15) || ((uintptr_t)d->routed_s[mt] & 15) || (m->w_stride[mt] & 15) || (m->s_stride[mt] & 3))
+            throw std::runtime_error("expert weights must be 16-byte aligned");
         if (m->has_shared) {
             if (!d->shared_w[mt] || !d->shared_s[mt]) throw std::runtime_error("shared expert weights missing");
             if (((uintptr_t)d->shared_w[mt] & 15) || ((uintptr_t)d->shared_s[mt] & 15))
                 throw std::runtime_error("shared expert weights must be 16-byte aligned");
-            m->host_experts[E].w[mt] = static_cast<const uint8_t *>(d->shared_w[mt]);
-            m->host_experts[E].s[mt] = d->shared_s[mt];
         }
     }
 
@@ -284,7 +268,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     }
     auto layout = [&](char *base) {
         char *p = base;
-        m->experts = carve<ExpertPtrs>(p, E + 1);
+        m->slot = carve<int>(p, E);
         m->scores = carve<float>(p, (size_t)T * Eg);
         m->idx = carve<int>(p, (size_t)T * K);
         m->wts = carve<float>(p, (size_t)T * K);
@@ -297,6 +281,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xs_a = carve<float>(p, (size_t)Tpad * (H / 32));
         m->xq_b = carve<uint8_t>(p, (size_t)Tpad * H);
         m->xs_b = carve<float>(p, (size_t)Tpad * (H / 32));
+        m->xe8_a = carve<uint8_t>(p, (size_t)Tpad * (H / 32));
+        m->xe8_pos = carve<uint8_t>(p, (size_t)(npos + 16) * (H / 32));
+        m->he8 = carve<uint8_t>(p, (size_t)(npos + 16) * (I / 32));
         m->xq_pos = ep_n > 1 ? nullptr : carve<uint8_t>(p, (size_t)(npos + 16) * H);
         m->xs_pos = ep_n > 1 ? nullptr : carve<float>(p, (size_t)(npos + 16) * (H / 128));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
@@ -325,17 +312,38 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xs_pos = reinterpret_cast<float *>(m->ep_region + m->ep_L.xs_pos);
         m->eo = reinterpret_cast<uint16_t *>(m->ep_region + m->ep_L.eo);
     }
-    CK(cudaMemcpy(m->experts, m->host_experts.data(), sizeof(ExpertPtrs) * (E + 1), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->slot, m->host_slot.data(), sizeof(int) * E, cudaMemcpyHostToDevice));
 
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
-    if (!m->routed_tc) {
-        m->up_r = make_cfg(d->routed_fmt, true, H, I, max_smem);
-        m->down_r = make_cfg(d->routed_fmt, false, H, I, max_smem);
+    m->routed_fp4 = d->routed_fmt == STBL_FMT_MXFP4;
+    if (H % 128 || I % 128 || H > 8192 || I > 8192)
+        throw std::runtime_error("experts need hidden and inter multiples of 128, at most 8192");
+    if (m->routed_fp4) {
+        const long long wst4[3] = {
+            d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H / 2,
+            d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H / 2,
+            d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I / 2};
+        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, E, wst4[0], 64);
+        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, E, wst4[1], 64);
+        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, E, wst4[2], 128);
+        m->tc4_up.s[0] = m->tc4_up.s[1] = m->tc4_up.w[0];
+        m->tc4_down.s[0] = m->tc4_down.s[1] = m->tc4_down.w[0];
+        for (int mt = 0; mt < 3; mt++)
+            if (((uintptr_t)d->routed_s[mt] & 15) || (m->s_stride[mt] & 15))
+                throw std::runtime_error("MXFP4 scales must be 16-byte aligned (base and expert stride)");
+        cudaFuncAttributes fa{};
+        CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(true)));
+        // as many stages as fit (up to 11): a stage holds 8 KB of packed codes (16 KB unpacked), so
+        // the FP8 kernel's 8 stages would keep only half its bytes in flight
+        for (m->tc4_nst = 11; m->tc4_nst >= 4; m->tc4_nst--)
+            if (expert_tc4_smem_bytes(m->tc4_nst) + (int)fa.sharedSizeBytes <= max_smem) break;
+        if (m->tc4_nst < 4) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
+        m->tc4_smem = expert_tc4_smem_bytes(m->tc4_nst);
+        CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(true), cudaFuncAttributeMaxDynamicSharedMemorySize, m->tc4_smem));
+        CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(false), cudaFuncAttributeMaxDynamicSharedMemorySize, m->tc4_smem));
     }
-    if (m->routed_tc || m->has_shared) {
-        if (H % 128 || I % 128 || H > 8192 || I > 8192)
-            throw std::runtime_error("FP8 experts need hidden and inter multiples of 128, at most 8192");
+    {
         // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
         const long long wst[3] = {
             d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H,
@@ -353,8 +361,11 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             m->tc_down.s[0] = weight_map(d->shared_w[2], I, H, 1, (long long)H * I, 128);
             m->tc_down.s[1] = m->tc_down.s[0];
         }
-        if (!m->routed_tc) m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
-        if (!m->has_shared) m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
+        if (!m->routed_tc && m->has_shared)
+            m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
+        if (!m->has_shared && m->routed_tc)
+            m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
+        if (!m->routed_tc && !m->has_shared) m->tc_up = m->tc4_up, m->tc_down = m->tc4_down;  // unused maps, valid
         m->bmap_xa = act_map(m->xq_a, H, Tpad);
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
         m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
@@ -387,6 +398,7 @@ EpView ep_view(const stbl_moe *m) {
 
 TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     TcParams p{};
+    p.slot = m->slot;
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
     p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
@@ -429,7 +441,14 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     const long long sst = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]]
                                                        : 4LL * ((rows + 127) / 128) * ((K + 127) / 128);
     p.w_scale_stride = sst / 4;
+    if (m->routed_fp4) {
+        p.w_e8[0] = static_cast<const uint8_t *>(d.routed_s[mats[0]]);
+        p.w_e8[1] = static_cast<const uint8_t *>(d.routed_s[mats[1]]);
+        p.w_e8_stride = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]] : (long long)rows * (K / 32);
+        p.act_e8 = up ? (direct ? m->xe8_a : m->xe8_pos) : m->he8;
+    }
     p.h = m->h;
+    p.swiglu_limit = m->d.swiglu_limit;
     p.eo = m->eo, p.sh = m->sh;
     p.has_shared = m->has_shared;
     p.partial = m->tc_partial;
@@ -458,33 +477,29 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     launch_pdl(expert_tc_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc_smem_up : m->tc_smem_down, st);
 }
 
-void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
-    GatherParams g{m->perm, T, m->K, m->H, m->has_shared, m->xq_a, m->xs_a, m->H / 32, m->xq_pos, m->xs_pos};
-    void *args[] = {&g};
-    launch_pdl(gather_kernel_ptr(), dim3(T * m->K + (m->has_shared ? T : 0)), dim3(256), args, 0, st);
+void launch_tc4(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
+    TcMaps maps = up ? m->tc4_up : m->tc4_down;
+    maps.b = up ? (p.b_direct ? m->bmap_xa : m->bmap_xpos) : m->bmap_hq;
+    void *args[] = {&maps, &p, &m->tc4_nst};
+    launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, m->tc4_smem, st);
 }
 
-ExpertParams expert_params(stbl_moe *m, int T, int fmt, bool up) {
-    ExpertParams p{};
-    p.experts = m->experts;
-    p.chunks = m->chunks;
-    p.n_chunks = m->n_chunks;
-    p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
-    p.perm = m->perm;
-    p.wts = m->wts;
-    const bool routed_buf = fmt == m->d.routed_fmt;
-    (void)up;
-    p.xq = routed_buf ? m->xq_a : m->xq_b;
-    p.xs = routed_buf ? m->xs_a : m->xs_b;
-    p.xs_stride = m->H / 32;
-    p.act_blk = act_blk_of(fmt);
-    p.act_pow2 = act_pow2_of(fmt);
-    p.swiglu_limit = m->d.swiglu_limit;
-    p.h = m->h;
-    p.eo = m->eo, p.sh = m->sh;
-    p.has_shared = m->has_shared;
-    p.status = m->status;
-    return p;
+void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
+    GatherParams g{m->perm, T, m->K, m->H, m->has_shared, m->xq_a, m->xs_a, m->H / 32, m->xq_pos, m->xs_pos, nullptr, nullptr};
+    if (m->routed_fp4) g.xe8 = m->xe8_a, g.xe8_pos = m->xe8_pos;  // routed positions only
+    void *args[] = {&g};
+    const int rows = T * m->K + (m->has_shared && !m->routed_fp4 ? T : 0);
+    launch_pdl(gather_kernel_ptr(), dim3(rows), dim3(256), args, 0, st);
+}
+
+// act_quant of h by the per-32 power-of-two rule (MXFP4 experts), e8m0 scales
+void launch_hquant32(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
+    if (pos_end <= pos_begin) return;
+    HquantParams hp{m->h + (size_t)pos_begin * m->I, m->hq + (size_t)pos_begin * m->I, nullptr, pos_end - pos_begin, m->I,
+                    nullptr, 0, m->he8 + (size_t)pos_begin * (m->I / 32)};
+    void *args[] = {&hp};
+    const int warps = hp.n_pos * (m->I / 128);
+    launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
 }
 
 // Launch with programmatic dependent launch: the kernel may start while the previous one in the
@@ -501,11 +516,6 @@ void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     CK(cudaLaunchKernelExC(&cfg, fn, args));
-}
-
-void launch_expert(const KernelCfg &c, ExpertParams p, int grid, cudaStream_t st) {
-    void *args[] = {&p, const_cast<int *>(&c.stage_bytes), const_cast<int *>(&c.nst)};
-    launch_pdl(c.fn, dim3(grid), dim3(kExpertThreads), args, c.smem, st);
 }
 
 TimedCall take_events(stbl_moe *m);
@@ -533,7 +543,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
     if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
-    r.nt_routed = m->routed_tc ? 16 : kNT;
+    r.xe8_a = m->routed_fp4 ? m->xe8_a : nullptr;
+    r.nt_routed = 16;
     r.nt_shared = 16;
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
@@ -541,7 +552,6 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
     int launches = 2;
 
-    const int grid = m->sms;
     const int npos = T * m->K + (m->has_shared ? T : 0);
     if (m->ep_n > 1) {
         // expert parallelism: counts exchange -> payload into the owners' receive rows -> up (waits
@@ -586,20 +596,28 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         launch_tc(m, false, pd, st);
         launches += 3;
     } else {
-        // MXFP4 routed experts on the CUDA-core kernels (they re-quantize h themselves), the FP8 shared
-        // expert on the tensor cores
+        // MXFP4 routed experts on the block-scaled tensor-core kernels, the FP8 shared expert on the FP8
+        // ones (its chunks read x by token, as 16 consecutive tokens, at any T):
+        // [gather] -> shared up, routed up -> hquant (per-32 routed, per-128 shared) -> shared down,
+        // routed down -> combine
+        const bool direct = T <= 16;
         const int ns = m->has_shared ? (T + 15) / 16 : 0;
-        ExpertParams pu = expert_params(m, T, fr, true), pd = expert_params(m, T, fr, false);
-        pu.chunk_begin = pd.chunk_begin = ns;
-        pu.chunk_end = pd.chunk_end = -1;
+        if (!direct) {
+            launch_gather(m, T, st);
+            launches++;
+        }
         if (ns) {
-            TcParams su = tc_params(m, T, true);
+            TcParams su = tc_params(m, T, true, true);
             su.chunk_begin = 0, su.chunk_end = ns;
             launch_tc(m, true, su, st);
             launches++;
         }
-        launch_expert(m->up_r, pu, grid, st);
+        TcParams pu = tc_params(m, T, true, direct);
+        pu.chunk_begin = ns, pu.chunk_end = -1;
+        launch_tc4(m, true, pu, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launch_hquant32(m, 0, T * m->K, st);
+        launches += 2;
         if (ns) {
             launch_hquant(m, T * m->K, npos, st);
             TcParams sd = tc_params(m, T, false);
@@ -607,8 +625,10 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
             launch_tc(m, false, sd, st);
             launches += 2;
         }
-        launch_expert(m->down_r, pd, grid, st);
-        launches += 2;
+        TcParams pd = tc_params(m, T, false);
+        pd.chunk_begin = ns, pd.chunk_end = -1;
+        launch_tc4(m, false, pd, st);
+        launches += 1;
     }
     CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};
     void *cargs[] = {&cp};
@@ -767,15 +787,18 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores) {
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream) {
     try {
         if (e < 0 || e >= m->E_loc) throw std::runtime_error("expert id out of range (local experts of this rank)");
-        ExpertPtrs p{};
-        for (int i = 0; i < 3; i++) {
-            if (!w[i] || !s[i] || ((uintptr_t)w[i] & 15) || ((uintptr_t)s[i] & 15))
-                throw std::runtime_error("expert pointers must be non-null and 16-byte aligned");
-            p.w[i] = static_cast<const uint8_t *>(w[i]);
-            p.s[i] = s[i];
-        }
-        m->host_experts[e] = p;
-        CK(cudaMemcpyAsync(m->experts + e, &m->host_experts[e], sizeof(ExpertPtrs), cudaMemcpyHostToDevice, stream));
+        // the new memory must be one slot of the layer's strided expert arrays, the same slot for all
+        // three matrices and their scales
+        const long long off = (long long)(static_cast<const char *>(w[0]) - static_cast<const char *>(m->d.routed_w[0]));
+        if (!w[0] || off < 0 || off % m->w_stride[0]) throw std::runtime_error("expert memory must be a slot of the layer's expert arrays");
+        const long long sl = off / m->w_stride[0];
+        if (sl >= m->E_loc) throw std::runtime_error("expert slot out of range");
+        for (int i = 0; i < 3; i++)
+            if (w[i] != static_cast<const char *>(m->d.routed_w[i]) + sl * m->w_stride[i] ||
+                s[i] != static_cast<const char *>(m->d.routed_s[i]) + sl * m->s_stride[i])
+                throw std::runtime_error("the three matrices and scales of an expert must share one slot");
+        m->host_slot[e] = (int)sl;
+        CK(cudaMemcpyAsync(m->slot + e, &m->host_slot[e], sizeof(int), cudaMemcpyHostToDevice, stream));
         return 0;
     } catch (const std::exception &e2) {
         m->err = e2.what();

@@ -14,6 +14,7 @@ struct TcMaps {
 };
 
 struct TcParams {
+    const int *slot;           // [E] storage slot of each routed expert in the weight arrays (null: e)
     const Chunk *chunks;
     const int *n_chunks;
     int chunk_begin, chunk_end;
@@ -28,7 +29,13 @@ struct TcParams {
     int act_s_stride;
     const float *w_scale[2];   // routed block scales of the two matrices (up) / one (down), [E][rb][kb]
     long long w_scale_stride;  // floats per expert
+    // MXFP4 routed experts (experts_tc4.cu): e8m0 weight scales [E][rows][K / 32] of the two
+    // matrices (up) / one (down), bytes per expert; e8m0 activation scales [rows][K / 32] of the B rows
+    const uint8_t *w_e8[2];
+    long long w_e8_stride;
+    const uint8_t *act_e8;
     const float *s_scale[2];   // shared expert block scales
+    float swiglu_limit;        // > 0: SwiGLU clamps (stbl/kernels.cu:445-459)
     uint16_t *h;               // up out: [pos][I] bf16
     uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
@@ -54,11 +61,13 @@ struct TcParams {
 struct HquantParams {
     const uint16_t *h;
     uint8_t *hq;
-    float *hs;
+    float *hs;                 // scales [pos][I / 128] (per-128 rule); unused for the per-32 rule
     int n_pos, I;
     // expert parallelism: rows [0, *n_routed_dev) (known on the device) and [n_pos, n_pos + n_tail)
     const int *n_routed_dev;
     int n_tail;
+    // per-32 power-of-two rule (MXFP4 experts) instead of per-128: scales as e8m0 bytes [pos][I / 32]
+    uint8_t *he8;
 };
 
 // gathers x codes and scales into position order for the up kernel when T > 16
@@ -71,6 +80,9 @@ struct GatherParams {
     int xs_stride;
     uint8_t *xq_pos;
     float *xs_pos;             // [pos][H / 128]
+    // MXFP4 routed experts: e8m0 scales [T][H / 32] -> [pos][H / 32]; then only routed positions
+    const uint8_t *xe8;
+    uint8_t *xe8_pos;
 };
 
 }  // namespace stbl

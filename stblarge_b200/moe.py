@@ -120,8 +120,16 @@ class MoELayer:
         T = self._check(self.lib.stbl_moe_last_scores(self.handle, s.ctypes.data), "stbl_moe_last_scores")
         return s[:T]
 
+    def set_expert_slot(self, e, slot, stream=None):
+        """Routed expert e reads slot `slot` of the layer's expert arrays from now on (an expert cache
+        that keeps experts in a pool of slots re-points them this way)."""
+        w = [self.weights["routed_w"][m][slot] for m in range(3)]
+        s = [self.weights["routed_s"][m][slot] for m in range(3)]
+        self.set_expert(e, w, s, stream)
+
     def set_expert(self, e, w, s, stream=None):
-        """Point routed expert e at other device tensors (three codes, three scales)."""
+        """Point routed expert e at another slot of the layer's expert arrays (three codes, three
+        scales, all of the same slot)."""
         wp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in w])
         sp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in s])
         st = stream if stream is not None else torch.cuda.current_stream()

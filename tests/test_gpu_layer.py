@@ -178,3 +178,19 @@ def cfg3_layer():
 def test_full_size_fp4_layer(cfg3_layer, T):
     dev, layer = cfg3_layer
     run_and_check(CFG3, layer, dev, None, synth.make_x(CFG3.hidden, T, seed=300 + T))
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_fp4"])
+def test_expert_slots_repoint_experts(small_layers, name):
+    """An expert cache re-points experts at other slots of the expert arrays: with experts 0..15
+    reading slots 15..0, the layer must equal the oracle whose expert e has slot 15 - e's weights."""
+    W, dev, _ = small_layers[name]
+    cfg = CFG1 if name == "cfg1" else CFG1_FP4
+    layer = MoELayer(cfg, dev, max_tokens=16)
+    E = cfg.n_experts
+    for e in range(E):
+        layer.set_expert_slot(e, E - 1 - e)
+    W2 = dict(W)
+    W2["routed"] = [[W["routed"][m][E - 1 - e] for e in range(E)] for m in range(3)]
+    run_and_check(cfg, layer, dev, W2, synth.make_x(cfg.hidden, 16, seed=77))
+    layer.close()
