@@ -8,16 +8,22 @@
 // accumulator once.  The numerics equal the reference's fp32 sum of dequantized products up to
 // summation order (ref/kernel.py:94-102 fp4_gemm).
 //
-// Work split and roles as in experts_tc.cu (stream-K over (item, 128-K block) units, one persistent
-// CTA per SM, six warps):
-//   warp 0     producer: lane 0 issues TMA for the weight tile (the packed codes land in the 128-byte
-//              swizzled layout the MMA reads, each 16 codes padded to 16 bytes: tensor-map type
-//              16U4_ALIGN16B) and the activation tile; all 32 lanes copy the K block's scale words
-//              (cp.async) into the stage, in the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM:
-//              byte (l * 16 + c * 4 + j) = scale of row 32 c + l for the K/32 sub-block j
-//   warp 1     MMA issuer: per K block, tcgen05.cp of the two scale blocks into a TMEM slot, then four
-//              block-scaled MMAs (K = 32 each, scale byte j selected in the instruction descriptor)
-//   warps 2-5  epilogue: one TMEM read per item, stream-K partials, SwiGLU (up) / outputs (down)
+// Items are 128 output rows x one chunk of up to 16 token columns; for the up product an item holds
+// 128 gate rows AND the matching 128 up rows (two accumulators), so SwiGLU reads both from TMEM.
+// Stream-K over (item, 256-K unit) pairs, one persistent CTA per SM.  A pipeline stage is one
+// 256-K unit: each weight matrix arrives as ONE 4-D TMA box of 128 rows x 2 K blocks (128 contiguous
+// bytes of packed codes per row and op; single-K-block boxes read 64-byte row pieces, which streams
+// about a third slower from HBM), the activations as one 16-row x 2-K-block box.  Six warps:
+//   warp 0     producer: lane 0 issues the TMA boxes (the packed codes land in the 128-byte swizzled
+//              layout the MMA reads, each 16 codes padded to 16 bytes: tensor-map type
+//              16U4_ALIGN16B); all 32 lanes copy the unit's scale words (cp.async) into the stage, in
+//              the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM: byte (l * 16 + c * 4 + j) =
+//              scale of row 32 c + l for the K/32 sub-block j
+//   warp 1     MMA issuer: per K block, tcgen05.cp of the scale blocks into a TMEM slot, then four
+//              block-scaled MMAs per weight matrix (K = 32 each, scale byte j selected in the
+//              instruction descriptor)
+//   warps 2-5  epilogue: TMEM reads of the item's accumulators, stream-K partials, SwiGLU (up) /
+//              outputs (down)
 #include "layer.cuh"
 #include "tc_common.cuh"
 #include "umma.cuh"
@@ -25,16 +31,27 @@
 namespace stbl {
 
 constexpr int kT4Threads = 192;
-constexpr int kT4Acc = 4;            // item accumulators in TMEM (16 columns each)
-constexpr int kT4SfSlots = 4;        // scale-factor slots in TMEM (4 columns A + 4 columns B each)
-constexpr int kT4SfBase = 64;        // first TMEM column of the scale slots
-constexpr int kT4TmemCols = 128;
-constexpr int kT4A = 128 * 128;      // weight tile in shared memory (unpacked codes)
-constexpr int kT4B = kTcN * 128;     // activation tile
-constexpr int kT4Stage = kT4A + kT4B + 512 + 512;  // + scale blocks A and B: 19 KB
-constexpr int kT4TxBytes = 128 * 64 + kT4B;          // TMA bytes per stage (packed codes + activations)
-constexpr int kT4Batch = 4;          // K blocks requested back to back
+constexpr int kT4Acc = 4;            // item accumulators in TMEM (32 columns each for up, 16 for down)
+constexpr int kT4Kb = 2;             // K blocks per stage (one 256-K unit)
+constexpr int kT4ATile = 128 * 128;  // one K block of one weight matrix in shared memory (unpacked codes)
+constexpr int kT4BTile = kTcN * 128; // one K block of activations
+constexpr int kT4SfSlots = 4;        // scale-factor slots in TMEM, 16 columns each (A0, A1, B)
+constexpr int kT4SfBase = 128;       // first TMEM column of the scale slots
+constexpr int kT4TmemCols = 256;
 constexpr int kT4Chunks = 32;
+constexpr int kT4PartialCols = 32;   // floats per row in the stream-K partial buffer
+
+template <bool UP>
+struct T4 {
+    static constexpr int nA = UP ? 2 : 1;                  // weight matrices per item
+    static constexpr int A = nA * kT4Kb * kT4ATile;        // [m][kb][128 rows][128 B]
+    static constexpr int B = kT4Kb * kT4BTile;             // [kb][16 rows][128 B]
+    static constexpr int SF = (nA + 1) * kT4Kb * 512;      // [m | B][kb][512 B]
+    static constexpr int stage = A + B + SF;               // up 71 KB, down 38 KB
+    static constexpr int tx = nA * kT4Kb * 128 * 64 + B;   // TMA bytes: packed codes + activations
+    static constexpr int NV = nA * kTcN;                   // accumulator columns per item
+};
+static_assert(T4<true>::stage % 1024 == 0 && T4<false>::stage % 1024 == 0, "stages must keep 1 KB alignment");
 
 __device__ __forceinline__ uint64_t plain_desc_32x16(const void *p) {
     // K-major, no swizzle: 8-row core matrices of 16-byte rows, 128 bytes apart (SBO), one along K
@@ -75,18 +92,17 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
 template <bool UP>
 __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_constant__ TcMaps maps, TcParams p,
                                                                    int nst) {
+    using S = T4<UP>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;     // reduction length
     const int rows = UP ? p.I : p.H;  // output rows per matrix
-    const int nkb = K / 128, kw = K / 32;  // K blocks; scale bytes per row
-    const int tiles = UP ? rows / 64 : rows / 128;
-    unsigned char *stages = smem;                                               // [nst][A | B | SFA | SFB]
-    float *xacc = reinterpret_cast<float *>(stages + (size_t)nst * kT4Stage);  // [128][17] item sums (up)
-    float *slot_w = xacc + 128 * 17;                                            // [2][16]
-    int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);                 // [2][16]
-    int *slot_dst = slot_col + 2 * kTcN;                                        // [2][16]
-    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);               // [kT4Chunks]
+    const int nu = K / 256, kw = K / 32;  // 256-K units per item; scale bytes per row
+    const int tiles = rows / 128;
+    unsigned char *stages = smem;                                                   // [nst][A | B | SF]
+    int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][16] by column
+    float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);                  // [2][16]
+    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);                      // [kT4Chunks]
     uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kT4Chunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
@@ -114,12 +130,12 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     pdl_launch_dependents();
     const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
-    const long long n_units = n_items * nkb;
+    const long long n_units = n_items * nu;
     const long long u_lo = n_units * blockIdx.x / gridDim.x, u_hi = n_units * (blockIdx.x + 1) / gridDim.x;
-    const int lo = (int)(u_lo / nkb), hi = u_hi > u_lo ? (int)((u_hi - 1) / nkb) + 1 : lo;
-    auto k_range = [&](int it, int &ka, int &kz) {
-        ka = (int)max(u_lo - (long long)it * nkb, 0LL);
-        kz = (int)min(u_hi - (long long)it * nkb, (long long)nkb);
+    const int lo = (int)(u_lo / nu), hi = u_hi > u_lo ? (int)((u_hi - 1) / nu) + 1 : lo;
+    auto u_range = [&](int it, int &ua, int &uz) {
+        ua = (int)max(u_lo - (long long)it * nu, 0LL);
+        uz = (int)min(u_hi - (long long)it * nu, (long long)nu);
     };
     const int c_lo = p.chunk_begin + lo / tiles;
     for (int i = tid; i < kT4Chunks; i += kT4Threads)
@@ -133,7 +149,7 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     if (warp == 0) {
         // ---------------- producer (lane 0: TMA; all lanes: scale words) ----------------
         if (lane == 0) {
-            for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]);
+            for (int m = 0; m < S::nA; m++) tma_prefetch_map(&maps.w[m]);
             tma_prefetch_map(&maps.b);
         }
         int q = 0;
@@ -143,54 +159,48 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
             const TcChunk ch = chunk_of(c);
             const int brow = b_row(p, ch);
             const int z = expert_slot(p, ch.e);
-            int ka, kz;
-            k_range(it, ka, kz);
-            // this lane's scale rows: A rows 32 cc + lane (cc = 0..3) of the tile, B row `lane` (< 16)
-            const uint8_t *sa[4];
+            int ua, uz;
+            u_range(it, ua, uz);
+            // this lane's scale rows: rows 32 cc + lane (cc = 0..3) of each weight tile, B row `lane` (< 16)
+            const uint8_t *sa[S::nA][4];
 #pragma unroll
-            for (int cc = 0; cc < 4; cc++) {
-                const int m = 32 * cc + lane;
-                const int mat = UP ? (m >> 6) : 0, r = UP ? tile * 64 + (m & 63) : tile * 128 + m;
-                sa[cc] = p.w_e8[mat] + (size_t)z * p.w_e8_stride + (size_t)r * kw;
-            }
+            for (int m = 0; m < S::nA; m++)
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++)
+                    sa[m][cc] = p.w_e8[m] + (size_t)z * p.w_e8_stride + (size_t)(tile * 128 + 32 * cc + lane) * kw;
             const uint8_t *sb = p.act_e8 + (size_t)(brow + (lane & 15)) * kw;
-            for (int kb0 = ka; kb0 < kz && !stop; kb0 += kT4Batch) {
-                const int nb = min(kT4Batch, kz - kb0);
-                for (int u = 0; u < nb; u++) {
-                    const int qq = q + u;
-                    if (!mbar_wait(&empty[qq % nst], ((qq / nst) & 1) ^ 1, &abort_flag)) {
-                        if (lane == 0) {
-                            abort_flag = 1;
-                            atomicOr(p.status, kErrWaitTimeout);
-                        }
-                        stop = true;
-                        break;
+            for (int u = ua; u < uz; u++, q++) {
+                const int s = q % nst;
+                if (!mbar_wait(&empty[s], ((q / nst) & 1) ^ 1, &abort_flag)) {
+                    if (lane == 0) {
+                        abort_flag = 1;
+                        atomicOr(p.status, kErrWaitTimeout);
                     }
+                    stop = true;
                 }
                 if (__any_sync(0xffffffffu, stop)) {
                     stop = true;
                     break;
                 }
-                for (int u = 0; u < nb; u++, q++) {
-                    const int s = q % nst, kb = kb0 + u;
-                    unsigned char *a = stages + (size_t)s * kT4Stage;
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&full[s], kT4TxBytes);
-                        if (UP) {
-                            tma_load_3d(a, &maps.w[0], kb * 128, tile * 64, z, &full[s]);
-                            tma_load_3d(a + kT4A / 2, &maps.w[1], kb * 128, tile * 64, z, &full[s]);
-                        } else {
-                            tma_load_3d(a, &maps.w[0], kb * 128, tile * 128, z, &full[s]);
-                        }
-                        tma_load_2d(a + kT4A, &maps.b, kb * 128, brow, &full[s]);
-                    }
-                    uint32_t *sfa = reinterpret_cast<uint32_t *>(a + kT4A + kT4B);
-                    uint32_t *sfb = sfa + 128;
+                unsigned char *a = stages + (size_t)s * S::stage;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], S::tx);
 #pragma unroll
-                    for (int cc = 0; cc < 4; cc++) cp_async4(sfa + lane * 4 + cc, sa[cc] + kb * 4);
-                    if (lane < 16) cp_async4(sfb + lane * 4, sb + kb * 4);
-                    cp_async_arrive(&full[s]);
+                    for (int m = 0; m < S::nA; m++)
+                        tma_load_4d(a + m * kT4Kb * kT4ATile, &maps.w[m], 0, tile * 128, kT4Kb * u, z, &full[s]);
+                    tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
                 }
+                uint32_t *sf = reinterpret_cast<uint32_t *>(a + S::A + S::B);
+#pragma unroll
+                for (int g = 0; g < kT4Kb; g++) {
+                    const int kb = kT4Kb * u + g;
+#pragma unroll
+                    for (int m = 0; m < S::nA; m++)
+#pragma unroll
+                        for (int cc = 0; cc < 4; cc++) cp_async4(sf + (m * kT4Kb + g) * 128 + lane * 4 + cc, sa[m][cc] + kb * 4);
+                    if (lane < 16) cp_async4(sf + (S::nA * kT4Kb + g) * 128 + lane * 4, sb + kb * 4);
+                }
+                cp_async_arrive(&full[s]);
             }
         }
         // drain: every issued copy must land before the CTA may exit
@@ -215,10 +225,10 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
                     stop = true;
                     break;
                 }
-                int ka, kz;
-                k_range(it, ka, kz);
-                const uint32_t d = tmem + (uint32_t)(acc * kTcN);
-                for (int kb = ka; kb < kz; kb++, q++) {
+                int ua, uz;
+                u_range(it, ua, uz);
+                const uint32_t d = tmem + (uint32_t)(acc * S::NV);
+                for (int u = ua; u < uz; u++, q++) {
                     const int s = q % nst;
                     if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag)) {
                         stop = true;
@@ -226,14 +236,22 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
                     }
                     fence_proxy_async_smem();  // scale words arrived through cp.async
                     tc_fence_after();
-                    const unsigned char *a = stages + (size_t)s * kT4Stage;
-                    const uint32_t sf = tmem + (uint32_t)(kT4SfBase + (q % kT4SfSlots) * 8);
-                    tmem_cp_sf(sf, a + kT4A + kT4B);
-                    tmem_cp_sf(sf + 4, a + kT4A + kT4B + 512);
+                    const unsigned char *a = stages + (size_t)s * S::stage;
+                    const unsigned char *sfs = a + S::A + S::B;
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        umma_mx(d, sw128_desc(a + 32 * j), sw128_desc(a + kT4A + 32 * j), idesc_mx(j), (kb > ka || j > 0),
-                                sf, sf + 4);
+                    for (int g = 0; g < kT4Kb; g++) {
+                        const uint32_t sf = tmem + (uint32_t)(kT4SfBase + ((kT4Kb * q + g) % kT4SfSlots) * 16);
+#pragma unroll
+                        for (int m = 0; m < S::nA; m++) tmem_cp_sf(sf + 4 * m, sfs + (m * kT4Kb + g) * 512);
+                        tmem_cp_sf(sf + 8, sfs + (S::nA * kT4Kb + g) * 512);
+#pragma unroll
+                        for (int m = 0; m < S::nA; m++)
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                umma_mx(d + m * kTcN, sw128_desc(a + (m * kT4Kb + g) * kT4ATile + 32 * j),
+                                        sw128_desc(a + S::A + g * kT4BTile + 32 * j), idesc_mx(j), (u > ua || g > 0 || j > 0),
+                                        sf + 4 * m, sf + 8);
+                    }
                     umma_commit(&empty[s]);
                 }
                 if (!stop) umma_commit(&acc_full[acc]);
@@ -255,33 +273,37 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
         const int et = tid - 64;                 // 0..127
         const int row = 32 * (warp & 3) + lane;  // TMEM lane = tile row
         const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        // the next item's columns: assignment et's column, destination row (h position / eo row), weight
         int pcol = 0, pdst = 0;
-        float pwt = 0.f;
+        float pwt = 1.f;
+        bool pval = false;
         auto prefetch = [&](int it) {
             const int c = p.chunk_begin + it / tiles;
             const TcChunk ch = chunk_of(c);
-            if (et < kTcN) {
+            pval = et < ch.n;
+            if (pval) {
                 const int pos = ch.pos0 + et;
+                const int a = __ldg(p.perm + pos);
                 pcol = et, pdst = pos, pwt = 1.f;
-                if (et < ch.n) {
-                    const int a = __ldg(p.perm + pos);
-                    if (UP) {
-                        pwt = __ldg(p.wts + a);
-                        if (p.b_direct) pcol = a / p.topk;
-                    } else {
-                        pdst = a;  // eo row
-                    }
+                if (UP) {
+                    pwt = __ldg(p.wts + a);
+                    if (p.b_direct) pcol = a / p.topk;  // x read by token: column = token
+                } else {
+                    pdst = a;  // eo row
                 }
             }
         };
+        // scatter into the column table of buffer buf (all 128 threads; two barriers)
         auto park = [&](int buf) {
-            if (et < kTcN) slot_col[buf * kTcN + et] = pcol, slot_dst[buf * kTcN + et] = pdst, slot_w[buf * kTcN + et] = pwt;
+            if (et < kTcN) col_dst[buf * kTcN + et] = -1;
+            bar_sync(2, 128);
+            if (pval) col_dst[buf * kTcN + pcol] = pdst, col_w[buf * kTcN + pcol] = pwt;
+            bar_sync(2, 128);
         };
         if (lo < hi) {
             prefetch(lo);
             park(0);
         }
-        bar_sync(2, 128);
         int ia = 0;
         for (int it = lo; it < hi; it++, ia++) {
             const int buf = (it - lo) & 1;
@@ -290,13 +312,14 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
             if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
             if (it + 1 < hi) prefetch(it + 1);
             const int acc_i = ia % kT4Acc;
-            int ka, kz;
-            k_range(it, ka, kz);
+            int ua, uz;
+            u_range(it, ua, uz);
             bool ok = mbar_wait(&acc_full[acc_i], (ia / kT4Acc) & 1, &abort_flag);
-            float acc[kTcN];
+            float va[kTcN], vb[kTcN];
             if (ok) {
                 tc_fence_after();
-                tmem_ld16(tl + (uint32_t)(acc_i * kTcN), acc);
+                tmem_ld16(tl + (uint32_t)(acc_i * S::NV), va);
+                if (UP) tmem_ld16(tl + (uint32_t)(acc_i * S::NV + kTcN), vb);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc_i]);
             }
@@ -307,62 +330,69 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
                 }
                 break;
             }
-            if (ka > 0) {
+            float *prow = p.partial + ((size_t)blockIdx.x * 128 + row) * kT4PartialCols;
+            if (ua > 0) {
                 // the range starts inside this item: publish the partial sums for the CTA that finishes it
-                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)blockIdx.x * 128 + row) * kTcN);
+                float4 *dst = reinterpret_cast<float4 *>(prow);
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]);
+                if (UP)
+#pragma unroll
+                    for (int j = 0; j < kTcN / 4; j++)
+                        dst[kTcN / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
                 if (et == 0) flag_release(p.flags + blockIdx.x, p.seq);
                 if (it + 1 < hi) park(buf ^ 1);
-                bar_sync(2, 128);
                 continue;
             }
             bool got = true;
             for (int cb = blockIdx.x + 1; cb < (int)gridDim.x; cb++) {
                 const long long uc = n_units * cb / gridDim.x;
-                if (uc >= (long long)(it + 1) * nkb) break;
+                if (uc >= (long long)(it + 1) * nu) break;
                 if (n_units * (cb + 1) / gridDim.x == uc) continue;  // empty range
                 if (et == 0) got = flag_wait(p.flags + cb, p.seq, &abort_flag) && got;
                 bar_sync(2, 128);
-                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)cb * 128 + row) * kTcN);
+                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)cb * 128 + row) * kT4PartialCols);
 #pragma unroll
                 for (int j = 0; j < kTcN / 4; j++) {
                     const float4 v = __ldcg(src + j);
-                    acc[4 * j] += v.x, acc[4 * j + 1] += v.y, acc[4 * j + 2] += v.z, acc[4 * j + 3] += v.w;
+                    va[4 * j] += v.x, va[4 * j + 1] += v.y, va[4 * j + 2] += v.z, va[4 * j + 3] += v.w;
                 }
+                if (UP)
+#pragma unroll
+                    for (int j = 0; j < kTcN / 4; j++) {
+                        const float4 v = __ldcg(src + kTcN / 4 + j);
+                        vb[4 * j] += v.x, vb[4 * j + 1] += v.y, vb[4 * j + 2] += v.z, vb[4 * j + 3] += v.w;
+                    }
             }
             if (!got) {
                 abort_flag = 1;
                 atomicOr(p.status, kErrWaitTimeout);
             }
-            const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
-            const float *swt = slot_w + buf * kTcN;
+            const int *cdst = col_dst + buf * kTcN;
+            const float *cw = col_w + buf * kTcN;
+            const int r = tile * 128 + row;
             if (UP) {
-                // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
+                // SwiGLU per column straight from the two accumulators (gate: va, up: vb)
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) xacc[row * 17 + j] = acc[j];
-                bar_sync(2, 128);
-                const int i = et & 63, r = tile * 64 + i;
-                for (int j = et >> 6; j < ch.n; j += 2) {
-                    const int col = scol[j];
-                    float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
+                for (int j = 0; j < kTcN; j++) {
+                    const int dst = cdst[j];
+                    if (dst < 0) continue;
+                    float gv = bf16r(va[j]), uv = bf16r(vb[j]);
                     if (p.swiglu_limit > 0.f) {
                         gv = fminf(gv, p.swiglu_limit);
                         uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
                     }
-                    const float hv = gv / (1.f + expf(-gv)) * uv * swt[j];
-                    p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
+                    const float hv = gv / (1.f + expf(-gv)) * uv * cw[j];
+                    p.h[(size_t)dst * p.I + r] = f32_to_bf16_bits(hv);
                 }
             } else {
-                const int r = tile * 128 + row;
 #pragma unroll
                 for (int j = 0; j < kTcN; j++)
-                    if (j < ch.n) p.eo[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
+                    if (j < ch.n) p.eo[(size_t)cdst[j] * p.H + r] = f32_to_bf16_bits(va[j]);
             }
             if (it + 1 < hi) park(buf ^ 1);
-            bar_sync(2, 128);
         }
     }
     tc_fence_before();
@@ -381,8 +411,12 @@ const void *expert_tc4_kernel_ptr(bool up) {
 }
 
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
-int expert_tc4_smem_bytes(int nst) {
-    return nst * kT4Stage + 4 * (128 * 17 + 6 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
+int expert_tc4_smem_bytes(bool up, int nst) {
+    const int stage = up ? T4<true>::stage : T4<false>::stage;
+    return nst * stage + 4 * (4 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
 }
+
+// floats per row of the stream-K partial buffer this kernel needs
+int expert_tc4_partial_cols() { return kT4PartialCols; }
 
 }  // namespace stbl

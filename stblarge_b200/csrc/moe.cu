@@ -21,7 +21,8 @@ namespace stbl {
 const void *combine_kernel_ptr();                 // combine.cu
 const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
 const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
-int expert_tc4_smem_bytes(int nst);
+int expert_tc4_smem_bytes(bool up, int nst);
+int expert_tc4_partial_cols();
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
@@ -78,7 +79,7 @@ struct stbl_moe {
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     uint32_t *status = nullptr;
-    float *tc_partial = nullptr;      // split-item partial sums of the tensor-core kernels, [sms][128][16]
+    float *tc_partial = nullptr;      // split-item partial sums of the tensor-core kernels, [sms][128][32]
     unsigned int *tc_flags = nullptr; // [sms] launch number whose partial a CTA slot holds
     unsigned int tc_seq = 0;
     // expert slots: routed expert e reads slot slot[e] of the strided weight arrays (an expert cache
@@ -92,11 +93,12 @@ struct stbl_moe {
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_fp4 = false;          // routed experts MXFP4, on the block-scaled tensor-core kernels
     TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
-    int tc4_nst = 0, tc4_smem = 0;
+    int tc4_nst_up = 0, tc4_nst_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
     uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32)
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
+    CUtensorMap bmap4_xa{}, bmap4_xpos{}, bmap4_hq{};         // the same, two K blocks per box (MXFP4 kernels)
 
     int last_T = 0;
     uint64_t calls = 0, tokens = 0;
@@ -149,18 +151,20 @@ CUtensorMap weight_map(const void *base, int K, int rows, int experts, long long
     return m;
 }
 
-// The same over MXFP4 codes (two per byte): the map's data type unpacks each 16 codes to 16 bytes in
-// shared memory, the layout kind::mxf8f6f4 reads e2m1 operands in; the transaction count of a box is
-// its packed size.  Needs 32-byte aligned base and strides.
-CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long long estride, int box_rows) {
+// The same over MXFP4 codes (two per byte), as a 4-D view {128 codes, rows, K blocks, experts} whose
+// K-block dimension (64 bytes apart) comes after the rows: one box is 128 rows x 2 K blocks, 128
+// contiguous bytes of each row, landing as two [128 rows][128 B] tiles.  The map's data type unpacks
+// each 16 codes to 16 bytes in shared memory, the layout kind::mxf8f6f4 reads e2m1 operands in; the
+// transaction count of a box is its packed size.  Needs 32-byte aligned base and strides.
+CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long long estride) {
     CUtensorMap m;
     if (((uintptr_t)base & 31) || (estride & 31) || ((K / 2) & 31))
         throw std::runtime_error("MXFP4 expert weights must be 32-byte aligned (base, row and expert strides)");
-    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)experts};
-    const cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)estride};
-    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, 1};
-    const cuuint32_t es[3] = {1, 1, 1};
-    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void *>(base), dims, strides, box,
+    const cuuint64_t dims[4] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128), (cuuint64_t)experts};
+    const cuuint64_t strides[3] = {(cuuint64_t)(K / 2), 64, (cuuint64_t)estride};
+    const cuuint32_t box[4] = {128, 128, 2, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, const_cast<void *>(base), dims, strides, box,
                                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an MXFP4 expert weight tensor");
@@ -168,6 +172,21 @@ CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long lon
 }
 
 void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st);
+
+// 3-D view {128 codes, rows, K blocks} of [rows][K] e4m3 activation codes: one box is 16 rows x 2 K
+// blocks, landing as two [16 rows][128 B] tiles (128B swizzle); the MXFP4 kernels' B operand
+CUtensorMap act_map2(const void *base, int K, int rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K, 128};
+    const cuuint32_t box[3] = {128, 16, 2};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an activation tensor");
+    return m;
+}
 
 // 2-D tensor map over [rows][K] e4m3 activation codes, read in 16-row x 128-byte tiles (128B swizzle)
 CUtensorMap act_map(const void *base, int K, int rows) {
@@ -294,7 +313,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
-        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 16);
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 32);
         m->tc_flags = carve<unsigned int>(p, m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
@@ -324,24 +343,26 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H / 2,
             d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H / 2,
             d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I / 2};
-        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, E, wst4[0], 64);
-        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, E, wst4[1], 64);
-        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, E, wst4[2], 128);
+        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, E, wst4[0]);
+        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, E, wst4[1]);
+        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, E, wst4[2]);
         m->tc4_up.s[0] = m->tc4_up.s[1] = m->tc4_up.w[0];
         m->tc4_down.s[0] = m->tc4_down.s[1] = m->tc4_down.w[0];
         for (int mt = 0; mt < 3; mt++)
             if (((uintptr_t)d->routed_s[mt] & 15) || (m->s_stride[mt] & 15))
                 throw std::runtime_error("MXFP4 scales must be 16-byte aligned (base and expert stride)");
-        cudaFuncAttributes fa{};
-        CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(true)));
-        // as many stages as fit (up to 11): a stage holds 8 KB of packed codes (16 KB unpacked), so
-        // the FP8 kernel's 8 stages would keep only half its bytes in flight
-        for (m->tc4_nst = 11; m->tc4_nst >= 4; m->tc4_nst--)
-            if (expert_tc4_smem_bytes(m->tc4_nst) + (int)fa.sharedSizeBytes <= max_smem) break;
-        if (m->tc4_nst < 4) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-        m->tc4_smem = expert_tc4_smem_bytes(m->tc4_nst);
-        CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(true), cudaFuncAttributeMaxDynamicSharedMemorySize, m->tc4_smem));
-        CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(false), cudaFuncAttributeMaxDynamicSharedMemorySize, m->tc4_smem));
+        // as many stages as fit: a stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
+        for (int up = 1; up >= 0; up--) {
+            cudaFuncAttributes fa{};
+            CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
+            int nst = 6;
+            while (nst >= 2 && expert_tc4_smem_bytes(up, nst) + (int)fa.sharedSizeBytes > max_smem) nst--;
+            if (nst < 2) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
+            const int smem = expert_tc4_smem_bytes(up, nst);
+            CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            (up ? m->tc4_nst_up : m->tc4_nst_down) = nst;
+            (up ? m->tc4_smem_up : m->tc4_smem_down) = smem;
+        }
     }
     {
         // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
@@ -370,6 +391,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
         m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
         m->bmap_hq = act_map(m->hq, I, npos + 16);
+        m->bmap4_xa = act_map2(m->xq_a, H, Tpad);
+        m->bmap4_xpos = act_map2(m->xq_pos, H, npos + 16);
+        m->bmap4_hq = act_map2(m->hq, I, npos + 16);
         auto pick = [&](bool up, int &nst, int &smem) {
             cudaFuncAttributes fa{};
             CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up)));
@@ -479,9 +503,9 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
 
 void launch_tc4(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     TcMaps maps = up ? m->tc4_up : m->tc4_down;
-    maps.b = up ? (p.b_direct ? m->bmap_xa : m->bmap_xpos) : m->bmap_hq;
-    void *args[] = {&maps, &p, &m->tc4_nst};
-    launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, m->tc4_smem, st);
+    maps.b = up ? (p.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
+    void *args[] = {&maps, &p, up ? &m->tc4_nst_up : &m->tc4_nst_down};
+    launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc4_smem_up : m->tc4_smem_down, st);
 }
 
 void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
