@@ -1,410 +1,13 @@
-// Grouped expert products on the 5th-generation tensor cores (FP8 128x128-block experts).
-//
-// Work item: (chunk of <= 16 tokens of one expert, output tile), nkb = K / 128 blocks of K each.
-// One persistent CTA per SM takes an equal contiguous range of the (item, K block) units, so no SM
-// idles while others finish a last item.  An item cut by a range boundary is finished by the CTA
-// holding its first K block (which reaches it last, at the end of its range): the CTAs whose ranges
-// start inside the item publish their partial sums first thing and raise a flag; the finishing CTA
-// adds them in CTA order.  Publishers never wait, so the waits cannot form a cycle.  Six warps:
-//   warp 0     TMA producer: per 128-K block one stage = a 128-row x 128-byte weight tile and a
-//              16-row x 128-byte activation tile, both in the 128-byte swizzle layout;
-//   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 token columns,
-//              K = 32 per instruction, four per 128-K block, each block into its own 16 TMEM columns;
-//              blocks are grouped by four (one completion signal per group), four groups in flight;
-//   warps 2-5  epilogue: read a group's four blocks of partials from TMEM in one load, apply the
-//              fp32 block scales (weight block x activation block: the promotion of
-//              ref/kernel.py:85-91) and accumulate in registers; then write the outputs.
-// up: the tile is [64 gate rows; 64 up rows]; h = bf16(silu(bf16 g) * bf16 u * w) (stbl/kernels.cu:
-//   445-459).  hquant_kernel then re-quantizes h (act_quant per 128, ref/kernel.py:35-45).
-// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); combine_kernel (experts.cu) adds them.
-// Every wait is bounded; a CTA that gives up raises a status bit, drains its copies and MMAs, frees
-// its TMEM and returns.
-#include "layer.cuh"
-#include "tc_params.cuh"
-#include "umma.cuh"
-#include "tc_common.cuh"
+// FP8 128x128-block expert kernels (the body is tc8_body.cuh), the gather of x rows by position and
+// the re-quantization of h between the up and down products.
+#include "tc8_body.cuh"
 
 namespace stbl {
-
-constexpr int kTcThreads = 192;
-constexpr int kTcG = 4;           // 128-K blocks per accumulator group (one TMEM read per group)
-constexpr int kTcGroups = 4;      // accumulator groups in TMEM (4 x 4 x 16 columns)
-constexpr int kTcAcc = kTcGroups;
-constexpr int kTcTmemCols = kTcGroups * kTcG * kTcN;
-constexpr int kATile = 128 * 128;
-constexpr int kBTile = kTcN * 128;
-constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
-constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
-constexpr int kTcChunks = 32;     // chunk entries of a CTA's item range kept in shared memory
-constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
 
 template <bool UP>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p,
                                                                   int nst) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    const int K = UP ? p.H : p.I;            // reduction length
-    const int rows = UP ? p.I : p.H;         // output rows per matrix
-    const int nkb = K / 128;
-    const int tiles = UP ? rows / 64 : rows / 128;
-    unsigned char *stages = smem;                                         // [nst][A tile | B tile]
-    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * kStage);  // [2][16][nkb] activation scales
-    float *sw = sx + 2 * kTcN * nkb;                                      // [2][2][nkb] weight scales
-    float *xacc = sw + 4 * nkb;                                           // [128][17] item sums
-    float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
-    int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);           // [2][16] B column of a slot
-    int *slot_dst = slot_col + 2 * kTcN;                                  // [2][16] output row of a slot
-    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);         // [kTcChunks] this CTA's chunks
-    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kTcChunks);
-    uint64_t *empty = full + nst;
-    uint64_t *acc_full = empty + nst;
-    uint64_t *acc_empty = acc_full + kTcAcc;
-    uint64_t *mma_done = acc_empty + kTcAcc;
-    __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag;
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        abort_flag = 0;
-        for (int s = 0; s < nst; s++) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
-        for (int a = 0; a < kTcAcc; a++) mbar_init(&acc_full[a], 1), mbar_init(&acc_empty[a], 128);
-        mbar_init(mma_done, 1);
-        fence_barrier_init();
-    }
-    if (warp == 1) tmem_alloc(&tmem_base, kTcTmemCols);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_base;
-
-    pdl_wait();
-    pdl_launch_dependents();
-    if (UP && p.ep.n_ranks > 1) {
-        // every rank's payload rows must have landed in this rank's receive rows: the payload
-        // kernel before this one has finished, so raise this rank's flag everywhere, then wait for all
-        if (blockIdx.x == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
-        if (tid == 0) {
-            if (!wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.pay_flag),
-                                p.ep.n_ranks, p.ep.epoch)) {
-                abort_flag = 1;
-                atomicOr(p.status, kErrWaitTimeout);
-            }
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // the rows are read by TMA
-        }
-        __syncthreads();
-    }
-    const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
-    const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
-    const long long n_units = n_items * nkb;
-    const long long u_lo = n_units * blockIdx.x / gridDim.x, u_hi = n_units * (blockIdx.x + 1) / gridDim.x;
-    // items [lo, hi) touched by this CTA; item it covers K blocks [ka, kz) of it
-    const int lo = (int)(u_lo / nkb), hi = u_hi > u_lo ? (int)((u_hi - 1) / nkb) + 1 : lo;
-    auto k_range = [&](int it, int &ka, int &kz) {
-        ka = (int)max(u_lo - (long long)it * nkb, 0LL);
-        kz = (int)min(u_hi - (long long)it * nkb, (long long)nkb);
-    };
-    // the chunks this CTA's items touch, in shared memory (items beyond the table read global memory)
-    const int c_lo = p.chunk_begin + lo / tiles;
-    for (int i = tid; i < kTcChunks; i += kTcThreads)
-        if (lo < hi && c_lo + i <= p.chunk_begin + (hi - 1) / tiles) ctab[i] = p.chunks[c_lo + i];
-    __syncthreads();
-    auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - c_lo < kTcChunks) ? ctab[c - c_lo] : p.chunks[c];
-        return tc_check(p, ch);
-    };
-
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]), tma_prefetch_map(&maps.s[m]);
-            tma_prefetch_map(&maps.b);
-            int q = 0;  // running stage counter
-            bool stop = false;
-            for (int it = lo; it < hi && !stop; it++) {
-                const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-                const TcChunk ch = chunk_of(c);
-                const bool shared = ch.e == p.E;
-                const int z = shared ? 0 : expert_slot(p, ch.e);
-                const int brow = b_row(p, ch);
-                int ka, kz;
-                k_range(it, ka, kz);
-                // K blocks are requested kTcBatch at a time, once as many stages are free, so that
-                // DRAM sees consecutive 128-byte pieces of each weight row together
-                for (int kb0 = ka; kb0 < kz && !stop; kb0 += kTcBatch) {
-                  const int nb = min(kTcBatch, kz - kb0);
-                  for (int u = 0; u < nb; u++) {
-                    const int qq = q + u;
-                    if (!mbar_wait(&empty[qq % nst], ((qq / nst) & 1) ^ 1, &abort_flag)) {
-                        abort_flag = 1;
-                        atomicOr(p.status, kErrWaitTimeout);
-                        stop = true;
-                        break;
-                    }
-                  }
-                  for (int u = 0; u < nb && !stop; u++, q++) {
-                    const int s = q % nst, kb = kb0 + u;
-                    unsigned char *a = stages + (size_t)s * kStage;
-                    mbar_arrive_expect_tx(&full[s], kStage);
-                    if (UP) {
-                        tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 64, z, &full[s]);
-                        tma_load_3d(a + kATile / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
-                    } else {
-                        tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 128, z, &full[s]);
-                    }
-                    tma_load_2d(a + kATile, &maps.b, kb * 128, brow, &full[s]);
-                  }
-                }
-            }
-            // drain: every issued tile must land before the CTA may exit
-            for (int j = max(0, q - nst); j < q; j++) {
-                const uint64_t t0 = global_ns();
-                while (!mbar_try_wait(&full[j % nst], (j / nst) & 1))
-                    if (global_ns() - t0 > kWaitLimitNs) {
-                        atomicOr(p.status, kErrCopyTimeout);
-                        break;
-                    }
-            }
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f8_f32(128, kTcN);
-            int q = 0, gq = 0;
-            bool stop = false;
-            for (int it = lo; it < hi && !stop; it++) {
-                int ka, kz;
-                k_range(it, ka, kz);
-                for (int kb0 = ka; kb0 < kz && !stop; kb0 += kTcG, gq++) {
-                    const int g = gq % kTcGroups;
-                    if (!mbar_wait(&acc_empty[g], ((gq / kTcGroups) & 1) ^ 1, &abort_flag)) {
-                        stop = true;
-                        break;
-                    }
-                    const int nb = min(kTcG, kz - kb0);
-                    for (int u = 0; u < nb; u++, q++) {
-                        const int s = q % nst;
-                        if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag)) {
-                            stop = true;
-                            break;
-                        }
-                        tc_fence_after();
-                        const unsigned char *a = stages + (size_t)s * kStage;
-                        const uint32_t d = tmem + (uint32_t)((g * kTcG + u) * kTcN);
-#pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            umma_f8(d, sw128_desc(a + 32 * k), sw128_desc(a + kATile + 32 * k), idesc, k > 0);
-                        umma_commit(&empty[s]);
-                    }
-                    if (!stop) umma_commit(&acc_full[g]);
-                }
-            }
-            if (stop) {
-                abort_flag = 1;
-                atomicOr(p.status, kErrWaitTimeout);
-            }
-            // every issued MMA completes before TMEM is freed
-            umma_commit(mma_done);
-            const uint64_t t0 = global_ns();
-            while (!mbar_try_wait(mma_done, 0))
-                if (global_ns() - t0 > kWaitLimitNs) {
-                    atomicOr(p.status, kErrCopyTimeout);
-                    break;
-                }
-        }
-    } else {
-        // ---------------- epilogue warpgroup (warps 2..5) ----------------
-        // Per item: scales and slot metadata of the NEXT item are loaded into registers before this
-        // item's accumulators are drained (their latency hides behind the MMAs) and parked in the other
-        // half of double-buffered shared arrays afterwards; nothing in the loop waits on global memory.
-        const int et = tid - 64;                   // 0..127
-        const int row = 32 * (warp & 3) + lane;    // TMEM lane = tile row
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        const int nsw = (UP ? 2 : 1) * nkb;
-        float px[kTcPre];
-        float pw = 0.f;
-        int pcol = 0, pdst = 0;
-        float pwt = 0.f;
-        // loads of item `it` into registers (thread et takes sx entries et, et + 128, ..., one weight scale
-        // and, for et < 16, slot et's column, output row and routing weight)
-        auto prefetch = [&](int it) {
-            const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-            const TcChunk ch = chunk_of(c);
-            const bool shared = ch.e == p.E;
-            const int brow = b_row(p, ch);
-            const int bvalid = p.b_direct && !shared ? p.T : ch.n;
-#pragma unroll
-            for (int k = 0; k < kTcPre; k++) {
-                const int u = et + 128 * k;
-                const int j = u / nkb, kb = u % nkb;
-                px[k] = (u < kTcN * nkb && j < bvalid) ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
-            }
-            if (et < nsw) {
-                const int m = et / nkb, kb = et % nkb;
-                const int rblk = UP ? (tile * 64) / 128 : tile;
-                const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
-                pw = __ldg(base + (size_t)rblk * nkb + kb);
-            }
-            if (et < kTcN) {
-                const int pos = ch.pos0 + et;
-                pcol = et, pdst = pos, pwt = 1.f;
-                if (et < ch.n) {
-                    if (!shared && p.pos_w) {
-                        // expert parallelism: weight and origin of the receive row
-                        if (UP) pwt = __ldcg(p.pos_w + pos);
-                        else pdst = __ldcg(p.pos_meta + pos);  // source rank << 16 | assignment
-                    } else if (!shared) {
-                        const int a = __ldg(p.perm + pos);
-                        if (UP) {
-                            pwt = __ldg(p.wts + a);
-                            if (p.b_direct) pcol = a / p.topk;
-                        } else {
-                            pdst = a;  // eo row
-                        }
-                    } else if (!UP) {
-                        pdst = pos - p.n_routed;  // sh row
-                    }
-                }
-            }
-        };
-        auto park = [&](int buf) {
-#pragma unroll
-            for (int k = 0; k < kTcPre; k++) {
-                const int u = et + 128 * k;
-                if (u < kTcN * nkb) sx[buf * kTcN * nkb + u] = px[k];
-            }
-            if (et < nsw) sw[buf * 2 * nkb + et] = pw;
-            if (et < kTcN) slot_col[buf * kTcN + et] = pcol, slot_dst[buf * kTcN + et] = pdst, slot_w[buf * kTcN + et] = pwt;
-        };
-        int gq = 0;
-        if (lo < hi) {
-            prefetch(lo);
-            park(0);
-        }
-        bar_sync(2, 128);
-        for (int it = lo; it < hi; it++) {
-            const int buf = (it - lo) & 1;
-            const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-            const TcChunk ch = chunk_of(c);
-            if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
-            if (it + 1 < hi) prefetch(it + 1);
-            const float *sxb = sx + buf * kTcN * nkb, *swb = sw + buf * 2 * nkb;
-            const int mrow = UP ? (row >> 6) : 0;  // up: rows 64..127 are the up matrix
-            float acc[kTcN];
-#pragma unroll
-            for (int j = 0; j < kTcN; j++) acc[j] = 0.f;
-            bool ok = true;
-            int ka, kz;
-            k_range(it, ka, kz);
-            for (int kb0 = ka; kb0 < kz; kb0 += kTcG, gq++) {
-                const int g = gq % kTcGroups;
-                if (!mbar_wait(&acc_full[g], (gq / kTcGroups) & 1, &abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                float d[kTcG * kTcN];
-                tmem_ld64(tl + (uint32_t)(g * kTcG * kTcN), d);
-                tc_fence_before();
-                mbar_arrive(&acc_empty[g]);
-#pragma unroll
-                for (int u = 0; u < kTcG; u++) {
-                    const int kb = kb0 + u;
-                    if (kb < kz) {
-                        const float wsc = swb[mrow * nkb + kb];
-#pragma unroll
-                        for (int j = 0; j < kTcN; j++) acc[j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc[j]);
-                    }
-                }
-            }
-            if (bar_sync_or(2, 128, !ok)) {
-                if (et == 0) {
-                    abort_flag = 1;
-                    atomicOr(p.status, kErrWaitTimeout);
-                }
-                break;
-            }
-            if (ka > 0) {
-                // the range starts inside this item: publish the partial sums for the CTA that finishes it
-                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)blockIdx.x * 128 + row) * kTcN);
-#pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-                __threadfence();
-                bar_sync(2, 128);
-                if (et == 0) flag_release(p.flags + blockIdx.x, p.seq);
-                if (it + 1 < hi) park(buf ^ 1);
-                bar_sync(2, 128);
-                continue;
-            }
-            // this CTA holds the item's first K block: add the partials of the CTAs whose ranges start
-            // inside the item, in CTA order
-            bool got = true;
-            for (int c = blockIdx.x + 1; c < (int)gridDim.x; c++) {
-                const long long uc = n_units * c / gridDim.x;
-                if (uc >= (long long)(it + 1) * nkb) break;
-                if (n_units * (c + 1) / gridDim.x == uc) continue;  // empty range
-                if (et == 0) got = flag_wait(p.flags + c, p.seq, &abort_flag) && got;
-                bar_sync(2, 128);
-                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * kTcN);
-#pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) {
-                    const float4 v = __ldcg(src + j);
-                    acc[4 * j] += v.x, acc[4 * j + 1] += v.y, acc[4 * j + 2] += v.z, acc[4 * j + 3] += v.w;
-                }
-            }
-            if (!got) {
-                abort_flag = 1;
-                atomicOr(p.status, kErrWaitTimeout);
-            }
-            const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
-            const float *swt = slot_w + buf * kTcN;
-            if (UP) {
-                // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
-#pragma unroll
-                for (int j = 0; j < kTcN; j++) xacc[row * 17 + j] = acc[j];
-                bar_sync(2, 128);
-                const int i = et & 63, r = tile * 64 + i;
-                for (int j = et >> 6; j < ch.n; j += 2) {
-                    const int col = scol[j];
-                    float gv = bf16r(xacc[i * 17 + col]), uv = bf16r(xacc[(64 + i) * 17 + col]);
-                    if (p.swiglu_limit > 0.f) {
-                        gv = fminf(gv, p.swiglu_limit);
-                        uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
-                    }
-                    const float hv = gv / (1.f + expf(-gv)) * uv * swt[j];
-                    p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
-                }
-            } else {
-                const int r = tile * 128 + row;
-                if (ch.e < p.E && p.pos_w) {
-                    // expert parallelism: straight into the source rank's eo row, over NVLink
-#pragma unroll
-                    for (int j = 0; j < kTcN; j++)
-                        if (j < ch.n) {
-                            const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
-                            if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
-                                if (row == 0) atomicOr(p.status, kErrBadTable);
-                                continue;
-                            }
-                            uint16_t *out = reinterpret_cast<uint16_t *>(p.ep.region[src] + p.ep.L.eo);
-                            out[(size_t)a * p.H + r] = f32_to_bf16_bits(acc[j]);
-                        }
-                } else {
-                    uint16_t *out = ch.e < p.E ? p.eo : p.sh;
-#pragma unroll
-                    for (int j = 0; j < kTcN; j++)
-                        if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
-                }
-            }
-            if (it + 1 < hi) park(buf ^ 1);
-            bar_sync(2, 128);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, kTcTmemCols);
-    }
+    tc8_body<UP>(maps, p, nst, blockIdx.x, gridDim.x);
 }
 
 // x codes and scales of every position (routed assignments in dispatch order, then the shared

@@ -24,9 +24,7 @@
 //              instruction descriptor)
 //   warps 2-5  epilogue: TMEM reads of the item's accumulators, stream-K partials, SwiGLU (up) /
 //              outputs (down)
-#include "layer.cuh"
-#include "tc_common.cuh"
-#include "umma.cuh"
+#include "tc8_body.cuh"
 
 namespace stbl {
 
@@ -89,9 +87,9 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One CTA's share of the MXFP4 products: CTA `cta` of the `ncta` that run this body.
 template <bool UP>
-__global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_constant__ TcMaps maps, TcParams p,
-                                                                   int nst) {
+__device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
     using S = T4<UP>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -131,7 +129,7 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
     const long long n_units = n_items * nu;
-    const long long u_lo = n_units * blockIdx.x / gridDim.x, u_hi = n_units * (blockIdx.x + 1) / gridDim.x;
+    const long long u_lo = n_units * cta / ncta, u_hi = n_units * (cta + 1) / ncta;
     const int lo = (int)(u_lo / nu), hi = u_hi > u_lo ? (int)((u_hi - 1) / nu) + 1 : lo;
     auto u_range = [&](int it, int &ua, int &uz) {
         ua = (int)max(u_lo - (long long)it * nu, 0LL);
@@ -330,7 +328,7 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
                 }
                 break;
             }
-            float *prow = p.partial + ((size_t)blockIdx.x * 128 + row) * kT4PartialCols;
+            float *prow = p.partial + ((size_t)cta * 128 + row) * kT4PartialCols;
             if (ua > 0) {
                 // the range starts inside this item: publish the partial sums for the CTA that finishes it
                 float4 *dst = reinterpret_cast<float4 *>(prow);
@@ -342,15 +340,15 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
                         dst[kTcN / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
-                if (et == 0) flag_release(p.flags + blockIdx.x, p.seq);
+                if (et == 0) flag_release(p.flags + cta, p.seq);
                 if (it + 1 < hi) park(buf ^ 1);
                 continue;
             }
             bool got = true;
-            for (int cb = blockIdx.x + 1; cb < (int)gridDim.x; cb++) {
-                const long long uc = n_units * cb / gridDim.x;
+            for (int cb = cta + 1; cb < ncta; cb++) {
+                const long long uc = n_units * cb / ncta;
                 if (uc >= (long long)(it + 1) * nu) break;
-                if (n_units * (cb + 1) / gridDim.x == uc) continue;  // empty range
+                if (n_units * (cb + 1) / ncta == uc) continue;  // empty range
                 if (et == 0) got = flag_wait(p.flags + cb, p.seq, &abort_flag) && got;
                 bar_sync(2, 128);
                 const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)cb * 128 + row) * kT4PartialCols);
@@ -403,8 +401,31 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     }
 }
 
-template __global__ void expert_tc4_kernel<true>(const __grid_constant__ TcMaps, TcParams, int);
-template __global__ void expert_tc4_kernel<false>(const __grid_constant__ TcMaps, TcParams, int);
+// The MXFP4 launch: the routed experts' MXFP4 products and, on a share of the CTAs, the FP8 shared
+// expert's (tc8_body), in one persistent grid, so the shared expert's 44 MB stream alongside the
+// routed weights instead of in launches of their own.  The split follows the bytes each side streams
+// (known only on the device: the routed chunk count comes from the router); p8 may hold no chunks.
+template <bool UP>
+__global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_constant__ TcMaps maps8, TcParams p8,
+                                                                   int nst8, const __grid_constant__ TcMaps maps4,
+                                                                   TcParams p4, int nst4) {
+    pdl_wait();
+    const int n4c = max(0, (p4.chunk_end >= 0 ? p4.chunk_end : *(volatile const int *)p4.n_chunks) - p4.chunk_begin);
+    const int n8c = max(0, p8.chunk_end - p8.chunk_begin);
+    // streamed bytes: MXFP4 up 128 x 2 rows x K/2, down 128 x K/2 per tile; FP8 128 x K per tile
+    const double b4 = (double)n4c * (UP ? p4.I / 128 : p4.H / 128) * (UP ? 256.0 : 128.0) * (UP ? p4.H : p4.I) / 2;
+    const double b8 = (double)n8c * (UP ? p8.I / 64 : p8.H / 128) * 128.0 * (UP ? p8.H : p8.I);
+    const int ncta = gridDim.x;
+    int c8 = 0;
+    if (n8c > 0) c8 = n4c > 0 ? min(ncta - 1, max(1, (int)(ncta * b8 / (b8 + b4) + 0.5))) : ncta;
+    if ((int)blockIdx.x < c8) tc8_body<UP>(maps8, p8, nst8, blockIdx.x, c8);
+    else tc4_body<UP>(maps4, p4, nst4, blockIdx.x - c8, ncta - c8);
+}
+
+template __global__ void expert_tc4_kernel<true>(const __grid_constant__ TcMaps, TcParams, int, const __grid_constant__ TcMaps,
+                                                 TcParams, int);
+template __global__ void expert_tc4_kernel<false>(const __grid_constant__ TcMaps, TcParams, int, const __grid_constant__ TcMaps,
+                                                  TcParams, int);
 
 const void *expert_tc4_kernel_ptr(bool up) {
     return up ? (const void *)expert_tc4_kernel<true> : (const void *)expert_tc4_kernel<false>;

@@ -79,8 +79,8 @@ struct stbl_moe {
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     uint32_t *status = nullptr;
-    float *tc_partial = nullptr;      // split-item partial sums of the tensor-core kernels, [sms][128][32]
-    unsigned int *tc_flags = nullptr; // [sms] launch number whose partial a CTA slot holds
+    float *tc_partial = nullptr;      // split-item partial sums: FP8 body [sms][128][16], then MXFP4 [sms][128][32]
+    unsigned int *tc_flags = nullptr; // [2][sms] launch number whose partial a CTA slot holds (FP8, MXFP4 bodies)
     unsigned int tc_seq = 0;
     // expert slots: routed expert e reads slot slot[e] of the strided weight arrays (an expert cache
     // re-points experts at other slots, stbl_moe_set_expert)
@@ -93,7 +93,7 @@ struct stbl_moe {
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_fp4 = false;          // routed experts MXFP4, on the block-scaled tensor-core kernels
     TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
-    int tc4_nst_up = 0, tc4_nst_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
+    int tc4_nst_up = 0, tc4_nst_down = 0, tc4_nst8_up = 0, tc4_nst8_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
     uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32)
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
@@ -313,8 +313,8 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
-        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 32);
-        m->tc_flags = carve<unsigned int>(p, m->sms);
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 48);
+        m->tc_flags = carve<unsigned int>(p, 2 * m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
         m->sel_cnt = carve<int>(p, Eg);
@@ -351,18 +351,6 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         for (int mt = 0; mt < 3; mt++)
             if (((uintptr_t)d->routed_s[mt] & 15) || (m->s_stride[mt] & 15))
                 throw std::runtime_error("MXFP4 scales must be 16-byte aligned (base and expert stride)");
-        // as many stages as fit: a stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
-        for (int up = 1; up >= 0; up--) {
-            cudaFuncAttributes fa{};
-            CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
-            int nst = 6;
-            while (nst >= 2 && expert_tc4_smem_bytes(up, nst) + (int)fa.sharedSizeBytes > max_smem) nst--;
-            if (nst < 2) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-            const int smem = expert_tc4_smem_bytes(up, nst);
-            CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            (up ? m->tc4_nst_up : m->tc4_nst_down) = nst;
-            (up ? m->tc4_smem_up : m->tc4_smem_down) = smem;
-        }
     }
     {
         // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
@@ -407,6 +395,24 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         };
         pick(true, m->tc_nst_up, m->tc_smem_up);
         pick(false, m->tc_nst_down, m->tc_smem_down);
+        if (m->routed_fp4) {
+            // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
+            // fit; a MXFP4 stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
+            for (int up = 1; up >= 0; up--) {
+                cudaFuncAttributes fa{};
+                CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
+                const int room = max_smem - (int)fa.sharedSizeBytes;
+                int n4 = 6, n8 = 8;
+                while (n4 >= 2 && expert_tc4_smem_bytes(up, n4) > room) n4--;
+                while (n8 >= 4 && expert_tc_smem_bytes(up, H, I, n8) > room) n8--;
+                if (n4 < 2 || n8 < 4) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
+                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8));
+                CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+                (up ? m->tc4_nst_up : m->tc4_nst_down) = n4;
+                (up ? m->tc4_nst8_up : m->tc4_nst8_down) = n8;
+                (up ? m->tc4_smem_up : m->tc4_smem_down) = smem;
+            }
+        }
     }
 }
 
@@ -501,10 +507,16 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     launch_pdl(expert_tc_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc_smem_up : m->tc_smem_down, st);
 }
 
-void launch_tc4(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
-    TcMaps maps = up ? m->tc4_up : m->tc4_down;
-    maps.b = up ? (p.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
-    void *args[] = {&maps, &p, up ? &m->tc4_nst_up : &m->tc4_nst_down};
+// the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range)
+void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st) {
+    TcMaps maps8 = up ? m->tc_up : m->tc_down;
+    maps8.b = up ? m->bmap_xb : m->bmap_hq;
+    TcMaps maps4 = up ? m->tc4_up : m->tc4_down;
+    maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
+    p4.flags = m->tc_flags + m->sms;
+    p4.partial = m->tc_partial + (size_t)m->sms * 128 * 16;
+    int *n8 = up ? &m->tc4_nst8_up : &m->tc4_nst8_down, *n4 = up ? &m->tc4_nst_up : &m->tc4_nst_down;
+    void *args[] = {&maps8, &p8, n8, &maps4, &p4, n4};
     launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc4_smem_up : m->tc4_smem_down, st);
 }
 
@@ -620,38 +632,30 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
         launch_tc(m, false, pd, st);
         launches += 3;
     } else {
-        // MXFP4 routed experts on the block-scaled tensor-core kernels, the FP8 shared expert on the FP8
-        // ones (its chunks read x by token, as 16 consecutive tokens, at any T):
-        // [gather] -> shared up, routed up -> hquant (per-32 routed, per-128 shared) -> shared down,
-        // routed down -> combine
+        // MXFP4 routed experts on the block-scaled tensor cores; the FP8 shared expert (its chunks read
+        // x by token, as 16 consecutive tokens, at any T) on a share of the same launches' CTAs:
+        // [gather] -> up (routed + shared) -> hquant (per-32 routed, per-128 shared) -> down -> combine
         const bool direct = T <= 16;
         const int ns = m->has_shared ? (T + 15) / 16 : 0;
         if (!direct) {
             launch_gather(m, T, st);
             launches++;
         }
-        if (ns) {
-            TcParams su = tc_params(m, T, true, true);
-            su.chunk_begin = 0, su.chunk_end = ns;
-            launch_tc(m, true, su, st);
-            launches++;
-        }
-        TcParams pu = tc_params(m, T, true, direct);
+        TcParams su = tc_params(m, T, true, true), pu = tc_params(m, T, true, direct);
+        su.chunk_begin = 0, su.chunk_end = ns;
         pu.chunk_begin = ns, pu.chunk_end = -1;
-        launch_tc4(m, true, pu, st);
+        launch_tc4(m, true, su, pu, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         launch_hquant32(m, 0, T * m->K, st);
         launches += 2;
         if (ns) {
             launch_hquant(m, T * m->K, npos, st);
-            TcParams sd = tc_params(m, T, false);
-            sd.chunk_begin = 0, sd.chunk_end = ns;
-            launch_tc(m, false, sd, st);
-            launches += 2;
+            launches++;
         }
-        TcParams pd = tc_params(m, T, false);
+        TcParams sd = tc_params(m, T, false), pd = tc_params(m, T, false);
+        sd.chunk_begin = 0, sd.chunk_end = ns;
         pd.chunk_begin = ns, pd.chunk_end = -1;
-        launch_tc4(m, false, pd, st);
+        launch_tc4(m, false, sd, pd, st);
         launches += 1;
     }
     CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};
