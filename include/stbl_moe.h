@@ -59,6 +59,10 @@ typedef struct stbl_moe_desc {
     /* shared expert, device */
     const void *shared_w[3];
     const void *shared_s[3];
+    /* slots in the routed arrays (0: n_experts); an expert cache's pool may hold fewer or more
+       slots than a layer has experts (stbl_cache_layer_desc fills this and the routed pointers; a
+       layer with fewer slots than experts runs only once its cache is attached) */
+    int n_slots;
 } stbl_moe_desc;
 
 /* Validate the description, allocate the layer's workspace on the current device and build its
@@ -87,6 +91,51 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores);
  * s must be the same slot j for all three matrices and their scales.  Takes effect for calls enqueued
  * on `stream` after this one. */
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream);
+
+/* y = MoE(x) with the routed experts given instead of selected: idx is device int [T][topk], the
+ * expert ids of each token in the order their outputs are added (distinct within a token, in
+ * 0..n_experts-1; a token that breaks this is routed to experts 0..topk-1 and status bit 2 is
+ * raised).  Weights are the router's, for the given experts: score / (sum + 1e-20) * route_scale in
+ * the given order.  The reference's forced-route replay of a recorded route trace. */
+int stbl_moe_forward_routed(stbl_moe *m, const void *x_bf16, int T, const int *idx, void *y_bf16, cudaStream_t stream);
+
+/* GPU expert cache over a host expert store: the reference's expert cache and demand reads
+ * (stbl/model.cu:99-106, 269-296, 347-422; stbl_stats, stbl/stbl.h:20), with the planning and the
+ * copies done on the GPU.  The store holds every expert of n_layers layers in page-locked host memory
+ * (cudaHostAlloc / cudaMallocHost / cudaHostRegister): piece q of expert e of layer l at
+ * host_w[q] (codes, q = 0 gate [I][H], 1 up, 2 down [H][I]) or host_s[q] (scales) + (l * n_experts +
+ * e) * stride (stride 0: the packed size), 16-byte aligned.  The cache is `slots` expert slots in
+ * device memory shared by all attached layers.  A layer created from stbl_cache_layer_desc and
+ * attached with stbl_moe_attach_cache brings the experts each call selects into the cache before its
+ * expert kernels run: right after the router one CTA replays the reference's LRU order (the call's
+ * cached experts touched first, then its experts in token-major top-k order: a hit is touched again,
+ * a miss takes a never-used slot in order or else the least recently used slot) and one grid copies
+ * the missing experts from the store (the GPU reads the page-locked memory directly).  No host
+ * synchronisation; the copies are ordered on the layer call's stream.  Calls of attached layers on
+ * different streams must not overlap (they share the cache state). */
+typedef struct stbl_cache stbl_cache;
+typedef struct stbl_cache_desc {
+    int n_layers, n_experts, slots;
+    int fmt;                 /* STBL_FMT_FP8_B128 or STBL_FMT_MXFP4 */
+    int hidden, inter;       /* multiples of 512 */
+    const void *host_w[3];
+    const void *host_s[3];
+    long long host_w_stride[3];
+    long long host_s_stride[3];
+} stbl_cache_desc;
+int stbl_cache_create(const stbl_cache_desc *desc, stbl_cache **out, char *err, int errlen);
+/* Points desc's routed weights at the cache's slot pool (routed_w/routed_s, strides, n_slots,
+ * routed_fmt); the caller fills the rest and creates the layer with stbl_moe_create. */
+int stbl_cache_layer_desc(const stbl_cache *c, stbl_moe_desc *desc);
+/* Layer m (made from stbl_cache_layer_desc, single GPU) becomes layer `layer` of the cache.  Needs
+ * slots >= max_tokens * topk (a call's experts must fit at once). */
+int stbl_moe_attach_cache(stbl_moe *m, stbl_cache *c, int layer);
+/* Counters since creation (waits for the device): routed experts found in the cache, experts copied
+ * in, bytes copied.  The reference's stbl_stats(hits, misses). */
+int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint64_t *bytes);
+/* Residency (waits for the device): map [n_layers][n_experts] slot or -1; owner [slots] l * E + e or -1. */
+int stbl_cache_state(const stbl_cache *c, int *map, int *owner);
+void stbl_cache_destroy(stbl_cache *c);
 
 /* Device status bits raised by kernels since the last call of this function (waits for the
  * device): 1 a wait timed out, 2 a dispatch entry was out of range, 4 copies were still in flight

@@ -380,8 +380,24 @@ static void expert_ffn(const orc_moe_desc *d, int fmt, const uint8_t *const w[3]
     free(xc), free(xs), free(g), free(u);
 }
 
+/* The layer with the routed experts given (forced routes): forced [T][topk], weights = unbiased
+ * scores of the given experts normalised in the given order, times route_scale (the selection's
+ * weight rule, model.cu:450-451, 527-530).  forced == NULL: the router selects. */
+static int moe_forward_impl(const orc_moe_desc *d, const uint16_t *x, int T, const int *forced, uint16_t *y, int *idx_out,
+                            float *w_out, int nthreads);
+
 int orc_moe_forward(const orc_moe_desc *d, const uint16_t *x, int T, uint16_t *y, int *idx_out, float *w_out,
                     int nthreads) {
+    return moe_forward_impl(d, x, T, NULL, y, idx_out, w_out, nthreads);
+}
+
+int orc_moe_forward_routed(const orc_moe_desc *d, const uint16_t *x, int T, const int *forced, uint16_t *y, int *idx_out,
+                           float *w_out, int nthreads) {
+    return moe_forward_impl(d, x, T, forced, y, idx_out, w_out, nthreads);
+}
+
+static int moe_forward_impl(const orc_moe_desc *d, const uint16_t *x, int T, const int *forced, uint16_t *y, int *idx_out,
+                            float *w_out, int nthreads) {
 #ifdef _OPENMP
     if (nthreads > 0) omp_set_num_threads(nthreads);
 #else
@@ -392,11 +408,33 @@ int orc_moe_forward(const orc_moe_desc *d, const uint16_t *x, int T, uint16_t *y
     int *idx = (int *)malloc(sizeof(int) * (size_t)T * K);
     float *wts = (float *)malloc(sizeof(float) * (size_t)T * K);
     orc_router_logits(d->router_w, x, T, E, H, logits);
+    float *scores = (float *)malloc(sizeof(float) * (size_t)T * E);
     if (orc_router_select(logits, d->router_bias, T, E, K, d->n_groups, d->topk_groups, d->score_fn, d->route_scale,
-                          NULL, idx, wts)) {
-        free(logits), free(idx), free(wts);
+                          scores, idx, wts)) {
+        free(logits), free(idx), free(wts), free(scores);
         return -1;
     }
+    if (forced) {
+        for (int t = 0; t < T; t++) {
+            float sum = 0.f;
+            for (int i = 0; i < K; i++) {
+                const int e = forced[t * K + i];
+                if (e < 0 || e >= E) {
+                    free(logits), free(idx), free(wts), free(scores);
+                    return -1;
+                }
+                idx[t * K + i] = e;
+                sum += scores[(size_t)t * E + e];
+            }
+            for (int i = 0; i < K; i++) {
+                float wt = scores[(size_t)t * E + idx[t * K + i]];
+                wt /= sum + 1e-20f;
+                wt *= d->route_scale;
+                wts[t * K + i] = wt;
+            }
+        }
+    }
+    free(scores);
     float *xf = (float *)malloc(sizeof(float) * (size_t)T * H);
     for (size_t i = 0; i < (size_t)T * H; i++) xf[i] = bf16_to_f32(x[i]);
     float *eo = (float *)calloc((size_t)T * K * H, sizeof(float));

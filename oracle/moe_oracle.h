@@ -87,6 +87,8 @@ typedef struct orc_moe_desc {
  * idx / weights [T][topk] when non-NULL.  Returns 0, or -1 when a routed expert is absent. */
 int orc_moe_forward(const orc_moe_desc *d, const uint16_t *x, int T, uint16_t *y, int *idx, float *weights,
                     int nthreads);
+int orc_moe_forward_routed(const orc_moe_desc *d, const uint16_t *x, int T, const int *forced, uint16_t *y, int *idx,
+                           float *weights, int nthreads);
 
 /* ---- the reference's own kernel semantics (stbl/kernels.cu), exact summation orders ----------- */
 void orc_ref_act_quant_fp8(float *x, int n);                                              /* :56-63 */

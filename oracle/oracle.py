@@ -189,10 +189,12 @@ class _Desc(ctypes.Structure):
     ]
 
 
-def moe_forward(cfg, weights, x_bits, nthreads=0):
+def moe_forward(cfg, weights, x_bits, nthreads=0, forced=None):
     """cfg: dict of layer shapes / routing (see stblarge_b200.config.MoEConfig.as_dict); weights: host
     numpy weights as produced by stblarge_b200.synth (routed[m][e] = (codes, scales) or None,
-    shared[m] = (codes, scales) or None).  Returns (y_bits [T][H] uint16, idx, weights)."""
+    shared[m] = (codes, scales) or None).  forced: int [T][topk] routed experts given instead of
+    selected (weights from the router's scores of those experts).  Returns (y_bits [T][H] uint16,
+    idx, weights)."""
     E = cfg["n_experts"]
     keep = []
 
@@ -229,7 +231,11 @@ def moe_forward(cfg, weights, x_bits, nthreads=0):
     y = np.empty((T, cfg["hidden"]), np.uint16)
     idx = np.empty((T, cfg["topk"]), np.int32)
     w = np.empty((T, cfg["topk"]), np.float32)
-    rc = lib().orc_moe_forward(ctypes.byref(d), ptr(x_bits), I(T), ptr(y), ptr(idx), ptr(w), I(nthreads))
+    if forced is None:
+        rc = lib().orc_moe_forward(ctypes.byref(d), ptr(x_bits), I(T), ptr(y), ptr(idx), ptr(w), I(nthreads))
+    else:
+        f = np.ascontiguousarray(forced, np.int32).reshape(T, cfg["topk"])
+        rc = lib().orc_moe_forward_routed(ctypes.byref(d), ptr(x_bits), I(T), ptr(f), ptr(y), ptr(idx), ptr(w), I(nthreads))
     if rc:
         raise ValueError("oracle moe_forward: a routed expert's weights are absent")
     return y, idx, w
@@ -281,3 +287,63 @@ def ref_axpy(y, x, a):
     y = _f32(y).copy()
     lib().orc_ref_axpy(ptr(y), ptr(_f32(x)), F(a), I(y.size))
     return y
+
+
+# ---- expert cache bookkeeping ---------------------------------------------------------------------
+
+class LruExpertCache:
+    """The reference's expert cache decisions without prefetch (stbl/model.cu:99-106 ExpertCache,
+    371-393 take_slot, 397-422 expert(), 503-520 the touch order in moe()): an LRU list of (layer,
+    expert) keys, most recent first.  A call first moves its cached experts to the front in order, then
+    walks its experts in order: a hit moves to the front again, a miss takes the next never-used slot
+    (slots are used in order) or else the slot of the list's last key, and goes to the front.  A call
+    with several tokens walks its distinct experts in order of first appearance (token-major, top-k
+    order), the single-token rule applied to the token batch.  Test infrastructure only."""
+
+    def __init__(self, slots):
+        self.slots = slots
+        self.where = {}      # (layer, expert) -> slot
+        self.lru = []        # keys, most recent first
+        self.next_slot = 0
+        self.hits = self.misses = 0
+
+    def _front(self, key):
+        self.lru.remove(key)
+        self.lru.insert(0, key)
+
+    def _take_slot(self):
+        if self.next_slot < self.slots:
+            self.next_slot += 1
+            return self.next_slot - 1
+        key = self.lru.pop()
+        return self.where.pop(key)
+
+    def call(self, layer, ids):
+        """ids: the call's routed expert ids, token-major.  Returns the misses as (slot, expert) in
+        the order they were placed."""
+        order = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))
+        for e in order:
+            if (layer, e) in self.where:
+                self._front((layer, e))
+        placed = []
+        for e in order:
+            key = (layer, e)
+            if key in self.where:
+                self._front(key)
+                self.hits += 1
+            else:
+                self.misses += 1
+                s = self._take_slot()
+                self.where[key] = s
+                self.lru.insert(0, key)
+                placed.append((s, e))
+        return placed
+
+    def state(self, n_layers, n_experts):
+        """(map [n_layers][n_experts] slot or -1, owner [slots] layer * n_experts + expert or -1)"""
+        m = np.full((n_layers, n_experts), -1, np.int32)
+        owner = np.full(self.slots, -1, np.int32)
+        for (l, e), s in self.where.items():
+            m[l, e] = s
+            owner[s] = l * n_experts + e
+        return m, owner

@@ -1,0 +1,94 @@
+"""Host-side mirror of the GPU expert cache (stbl_cache_* C ABI, the reference's expert cache,
+stbl/model.cu:99-106, 347-422).
+
+    store = host_store(cfg, n_layers)                  # pinned host tensors, every expert of every layer
+    cache = ExpertCache(cfg, n_layers, slots, store)   # `slots` experts in device memory
+    layer = MoELayer(cfg, resident_weights, max_tokens=1, cache=(cache, l))
+    y = layer(x)                                       # the call brings its experts into the cache
+    cache.stats()                                      # hits, misses, bytes copied
+
+The planning (hits, LRU victims) and the copies of missing experts run on the GPU inside the layer
+call, ordered on its stream; nothing here synchronises except stats() / state().
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import lib as L
+from . import synth
+from .config import MoEConfig
+
+
+def host_store(cfg: MoEConfig, n_layers: int, seed_of=None, physical=None):
+    """Pinned host tensors holding the routed experts of n_layers layers, expert-major:
+    'w'[m]: uint8 [n_layers * E, ...], 's'[m]: scales [n_layers * E, ...] (the layout of
+    synth.device_layer's routed tensors, one layer after another).  Layer l's expert e gets the
+    synthetic weights of seed seed_of(l, e) (default 1000 + l * E + e).  physical: hold only that many
+    distinct experts and repeat them (store row r = physical row r % physical); the bytes each expert
+    moves are the same, the host memory is smaller."""
+    E = cfg.n_experts
+    n = n_layers * E
+    seed_of = seed_of or (lambda l, e: 1000 + l * E + e)
+    rows = n if physical is None else min(physical, n)
+    w0, s0 = synth.routed_expert(cfg, 0)
+    w = [torch.empty((rows,) + tuple(t.shape), dtype=t.dtype, pin_memory=True) for t in w0]
+    s = [torch.empty((rows,) + tuple(t.shape), dtype=t.dtype, pin_memory=True) for t in s0]
+    for r in range(rows):
+        l, e = divmod(r, E)
+        ws, ss = synth.routed_expert(cfg, seed_of(l, e))
+        for m in range(3):
+            w[m][r].copy_(ws[m])
+            s[m][r].copy_(ss[m])
+    return {"w": w, "s": s, "rows": rows, "n": n}
+
+
+class ExpertCache:
+    def __init__(self, cfg: MoEConfig, n_layers: int, slots: int, store: dict):
+        self.lib = L.load()
+        self.cfg, self.n_layers, self.slots = cfg, n_layers, slots
+        self.store = store  # keeps the pinned tensors alive
+        d = L.CacheDesc()
+        d.n_layers, d.n_experts, d.slots, d.fmt = n_layers, cfg.n_experts, slots, cfg.routed_fmt
+        d.hidden, d.inter = cfg.hidden, cfg.inter
+        for m in range(3):
+            w, s = store["w"][m], store["s"][m]
+            d.host_w[m], d.host_s[m] = w.data_ptr(), s.data_ptr()
+            d.host_w_stride[m] = w.stride(0) * w.element_size()
+            d.host_s_stride[m] = s.stride(0) * s.element_size()
+        if store["rows"] < store["n"]:
+            raise ValueError("a repeated store (physical < experts) needs stbl_cache_desc strides of its own")
+        err = ctypes.create_string_buffer(512)
+        h = ctypes.c_void_p()
+        if self.lib.stbl_cache_create(ctypes.byref(d), ctypes.byref(h), err, 512) != 0:
+            raise RuntimeError("stbl_cache_create: " + err.value.decode())
+        self.handle = h
+
+    def layer_desc(self, desc):
+        if self.lib.stbl_cache_layer_desc(self.handle, ctypes.byref(desc)) != 0:
+            raise RuntimeError("stbl_cache_layer_desc failed")
+
+    def stats(self):
+        h, m, b = L.U64(), L.U64(), L.U64()
+        if self.lib.stbl_cache_stats(self.handle, ctypes.byref(h), ctypes.byref(m), ctypes.byref(b)) != 0:
+            raise RuntimeError("stbl_cache_stats failed")
+        return {"hits": h.value, "misses": m.value, "bytes": b.value}
+
+    def state(self):
+        mp = np.empty((self.n_layers, self.cfg.n_experts), np.int32)
+        owner = np.empty(self.slots, np.int32)
+        if self.lib.stbl_cache_state(self.handle, mp.ctypes.data, owner.ctypes.data) != 0:
+            raise RuntimeError("stbl_cache_state failed")
+        return mp, owner
+
+    def close(self):
+        if self.handle:
+            self.lib.stbl_cache_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

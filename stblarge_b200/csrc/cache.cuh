@@ -1,0 +1,32 @@
+// GPU expert cache (include/stbl_moe.h: stbl_cache_*): declarations shared by cache.cu and moe.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+struct stbl_cache {
+    int L = 0, E = 0, S = 0, fmt = 0, H = 0, I = 0, dev = 0;
+    // one expert = six pieces: codes of gate, up, down, then their scales; slot s holds piece p at
+    // pool + s * slot_bytes + piece_off[p]
+    long long piece_bytes[6] = {}, piece_off[6] = {}, slot_bytes = 0, expert_bytes = 0;
+    const uint8_t *host[6] = {};      // device-visible addresses of the host store (pinned memory)
+    long long host_stride[6] = {};    // bytes between experts (l * E + e) of a piece
+    uint8_t *pool = nullptr;          // [S][slot_bytes]
+    int *map = nullptr;               // [L][E] slot of (layer, expert), -1 when not resident
+    int *owner = nullptr;             // [S] l * E + e held by the slot, -1 when free
+    unsigned long long *ts = nullptr; // [S] last use (a logical clock), 0 never used
+    unsigned long long *ctr = nullptr;// [0] clock, [1] hits, [2] misses, [3] bytes copied
+    int2 *jobs = nullptr;             // [S] (slot, l * E + e) to fill in the current call
+    int *n_jobs = nullptr;
+    int copy_ctas = 0;
+    std::string err;
+};
+
+namespace stbl {
+// Enqueues the cache step of one layer call: the planner (hits, LRU victims, the layer's slot table
+// = map row `layer`) and the copy of the missing experts from the host store into their slots.
+// idx: device [n] routed expert ids of the call (token-major, top-k order).
+void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *status, cudaStream_t st);
+}  // namespace stbl

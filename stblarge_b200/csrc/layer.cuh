@@ -66,6 +66,7 @@ struct RouterParams {
     uint32_t *sel_bm;
     unsigned int *sel_ticket;
     uint32_t *status;
+    const int *forced_idx;   // optional: [T][topk] experts given instead of selected (forced routes)
 };
 
 // Sets the logits kernel's shared-memory limit on the current device (once per device, before any

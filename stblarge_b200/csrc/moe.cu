@@ -16,6 +16,7 @@
 #include "layer.cuh"
 #include "tc_params.cuh"
 #include "ep.cuh"
+#include "cache.cuh"
 
 namespace stbl {
 const void *combine_kernel_ptr();                 // combine.cu
@@ -86,6 +87,9 @@ struct stbl_moe {
     // re-points experts at other slots, stbl_moe_set_expert)
     int *slot = nullptr;
     std::vector<int> host_slot;
+    int n_slots = 0;                  // slots in the routed arrays (>= E_loc)
+    stbl_cache *cache = nullptr;      // attached expert cache (stbl_moe_attach_cache), layer cache_layer
+    int cache_layer = 0;
     long long w_stride[3] = {0, 0, 0}, s_stride[3] = {0, 0, 0};  // bytes between slots
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
@@ -254,8 +258,11 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     m->has_shared = d->shared_fmt != STBL_FMT_NONE;
 
     // routed experts: slots of strided arrays (slot e = expert e until an expert cache re-points it)
+    if (d->n_slots < 0 || d->n_slots > (1 << 20)) throw std::runtime_error("n_slots must be in 0..2^20");
+    if (ep_n > 1 && d->n_slots > 0 && d->n_slots != E) throw std::runtime_error("expert parallelism takes no extra slots");
+    m->n_slots = d->n_slots > 0 ? d->n_slots : E;
     m->host_slot.resize(E);
-    for (int e = 0; e < E; e++) m->host_slot[e] = e;
+    for (int e = 0; e < E; e++) m->host_slot[e] = e < m->n_slots ? e : 0;  // fewer slots: an expert cache places them
     const int rows[3] = {I, I, H}, ks[3] = {H, H, I};
     for (int mt = 0; mt < 3; mt++) {
         if (!d->routed_w[mt] || !d->routed_s[mt]) throw std::runtime_error("routed expert weights missing");
@@ -343,9 +350,10 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H / 2,
             d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H / 2,
             d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I / 2};
-        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, E, wst4[0]);
-        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, E, wst4[1]);
-        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, E, wst4[2]);
+        const int ns = m->n_slots;
+        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, ns, wst4[0]);
+        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, ns, wst4[1]);
+        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, ns, wst4[2]);
         m->tc4_up.s[0] = m->tc4_up.s[1] = m->tc4_up.w[0];
         m->tc4_down.s[0] = m->tc4_down.s[1] = m->tc4_down.w[0];
         for (int mt = 0; mt < 3; mt++)
@@ -359,9 +367,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H,
             d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I};
         if (m->routed_tc) {
-            m->tc_up.w[0] = weight_map(d->routed_w[0], H, I, E, wst[0], 64);
-            m->tc_up.w[1] = weight_map(d->routed_w[1], H, I, E, wst[1], 64);
-            m->tc_down.w[0] = weight_map(d->routed_w[2], I, H, E, wst[2], 128);
+            m->tc_up.w[0] = weight_map(d->routed_w[0], H, I, m->n_slots, wst[0], 64);
+            m->tc_up.w[1] = weight_map(d->routed_w[1], H, I, m->n_slots, wst[1], 64);
+            m->tc_down.w[0] = weight_map(d->routed_w[2], I, H, m->n_slots, wst[2], 128);
             m->tc_down.w[1] = m->tc_down.w[0];
         }
         if (m->has_shared) {
@@ -428,7 +436,7 @@ EpView ep_view(const stbl_moe *m) {
 
 TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     TcParams p{};
-    p.slot = m->slot;
+    p.slot = m->cache ? m->cache->map + (size_t)m->cache_layer * m->E : m->slot;
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
     p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
@@ -557,12 +565,13 @@ void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem,
 TimedCall take_events(stbl_moe *m);
 void collect_timing(stbl_moe *m, size_t keep);
 
-void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
+void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const int *forced = nullptr) {
     if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
     if (!x || !y) throw std::runtime_error("null x or y");
     if (m->ep_n > 1 && !m->ep_connected) throw std::runtime_error("expert-parallel layer not connected (stbl_moe_ep_connect)");
     if (m->ep_n > 1 && ++m->ep_epoch == 0) m->ep_epoch = 1;
     if ((uintptr_t)x & 15) throw std::runtime_error("x must be 16-byte aligned");
+    if (m->n_slots < m->E_loc && !m->cache) throw std::runtime_error("the layer has fewer slots than experts: attach its expert cache first");
     TimedCall tc{};
     if (m->timing) {
         if (m->pending.size() >= 256) collect_timing(m, 0);
@@ -584,9 +593,15 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st) {
     r.nt_shared = 16;
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
+    r.forced_idx = forced;
     CK(launch_router(r, st, true));
-    if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
     int launches = 2;
+    if (m->cache) {
+        // bring the call's routed experts into the cache: plan (hits, LRU victims), copy the misses
+        launch_cache(m->cache, m->cache_layer, m->idx, T * m->K, m->status, st);
+        launches += 2;
+    }
+    if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
 
     const int npos = T * m->K + (m->has_shared ? T : 0);
     if (m->ep_n > 1) {
@@ -770,6 +785,44 @@ int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaS
     }
 }
 
+int stbl_moe_forward_routed(stbl_moe *m, const void *x_bf16, int T, const int *idx, void *y_bf16, cudaStream_t stream) {
+    try {
+        if (!idx) throw std::runtime_error("null idx");
+        if (m->ep_n > 1) throw std::runtime_error("forced routes are single-GPU");
+        forward(m, x_bf16, T, y_bf16, stream, idx);
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_attach_cache(stbl_moe *m, stbl_cache *c, int layer) {
+    try {
+        if (!c) throw std::runtime_error("null cache");
+        if (m->ep_n > 1) throw std::runtime_error("the expert cache is single-GPU");
+        if (layer < 0 || layer >= c->L) throw std::runtime_error("layer out of the cache's range");
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        if (dev != c->dev) throw std::runtime_error("the cache lives on another device");
+        if (c->E != m->E || c->H != m->H || c->I != m->I || c->fmt != m->d.routed_fmt)
+            throw std::runtime_error("cache and layer shapes or formats differ");
+        if (m->n_slots != c->S) throw std::runtime_error("layer not made from stbl_cache_layer_desc (n_slots)");
+        for (int q = 0; q < 3; q++)
+            if (m->d.routed_w[q] != c->pool + c->piece_off[q] || m->d.routed_s[q] != c->pool + c->piece_off[q + 3] ||
+                m->w_stride[q] != c->slot_bytes || m->s_stride[q] != c->slot_bytes)
+                throw std::runtime_error("layer not made from stbl_cache_layer_desc (routed pointers)");
+        if ((long long)c->S < std::min((long long)m->Tmax * m->K, (long long)m->E))
+            throw std::runtime_error("the cache needs at least min(max_tokens * topk, n_experts) slots");
+        m->cache = c;
+        m->cache_layer = layer;
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
 int stbl_moe_forward_host(stbl_moe *m, const void *x_bf16_host, int T, void *y_bf16_host, cudaStream_t stream) {
     try {
         if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
@@ -815,12 +868,13 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores) {
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream) {
     try {
         if (e < 0 || e >= m->E_loc) throw std::runtime_error("expert id out of range (local experts of this rank)");
+        if (m->cache) throw std::runtime_error("the layer's experts are placed by its expert cache");
         // the new memory must be one slot of the layer's strided expert arrays, the same slot for all
         // three matrices and their scales
         const long long off = (long long)(static_cast<const char *>(w[0]) - static_cast<const char *>(m->d.routed_w[0]));
         if (!w[0] || off < 0 || off % m->w_stride[0]) throw std::runtime_error("expert memory must be a slot of the layer's expert arrays");
         const long long sl = off / m->w_stride[0];
-        if (sl >= m->E_loc) throw std::runtime_error("expert slot out of range");
+        if (sl >= m->n_slots) throw std::runtime_error("expert slot out of range");
         for (int i = 0; i < 3; i++)
             if (w[i] != static_cast<const char *>(m->d.routed_w[i]) + sl * m->w_stride[i] ||
                 s[i] != static_cast<const char *>(m->d.routed_s[i]) + sl * m->s_stride[i])

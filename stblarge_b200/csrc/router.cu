@@ -263,117 +263,131 @@ __device__ __forceinline__ void select_token(const RouterParams &p, int t, int l
                                              int TW, int tb, bool live) {
     const int E = p.E, K = p.topk;
     const uint32_t lane_bit = 1u << lane;
-    uint32_t key[EJ];
-    float sv[EJ];
-#pragma unroll
-    for (int j = 0; j < EJ; j++) {
-        const int e = lane + 32 * j;
-        key[j] = 0u;  // below every float's key: not selectable
-        sv[j] = 0.f;
-        if (e < E) {
-            const float s = __ldcg(p.scores + (size_t)t * E + e);
-            sv[j] = s;
-            key[j] = float_key(s + __ldg(p.bias + e) + 0.0f);
-        }
-    }
-    if (p.n_groups > 1 && p.topk_groups < p.n_groups) {
-        const int gsz = E / p.n_groups;
-        const bool pow2 = (gsz & (gsz - 1)) == 0;
-        // group score = top-1 + top-2 of the group's biased scores (values only); lane g ends with
-        // group g's score
-        float gs = 0.f;
-        if (pow2 && gsz >= 32) {
-            // a group is m whole registers: a tree of top-2 merges over them, then over the lanes
-            const int m = gsz >> 5;
-            uint32_t a1[EJ], a2[EJ];
-#pragma unroll
-            for (int j = 0; j < EJ; j++) a1[j] = key[j], a2[j] = 0u;
-#pragma unroll
-            for (int s = 1; s < EJ; s *= 2)
-                if (s < m)
-#pragma unroll
-                    for (int j = 0; j + s < EJ; j += 2 * s) top2_merge(a1[j], a2[j], a1[j + s], a2[j + s]);
-            // every register's lane-wide top-2 (only group leaders j = g m are used): second largest =
-            // the largest after the lowest lane holding the maximum swaps in its own second
-#pragma unroll
-            for (int j = 0; j < EJ; j++) {
-                const uint32_t m1 = __reduce_max_sync(0xffffffffu, a1[j]);
-                const uint32_t bal = __ballot_sync(0xffffffffu, a1[j] == m1);
-                const uint32_t m2 = __reduce_max_sync(0xffffffffu, (bal & (0u - bal)) == lane_bit ? a2[j] : a1[j]);
-                if (lane * m == j) gs = key_float(m1) + key_float(m2);
-            }
-        } else if (pow2) {
-            // a group is a segment of gsz lanes of one register: top-2 merges across the segment
-            const int segs = 32 / gsz, seg_shift = __ffs(segs) - 1;
-#pragma unroll
-            for (int j = 0; j < EJ; j++) {
-                uint32_t a1 = key[j], a2 = 0u;
-                for (int o = gsz / 2; o > 0; o >>= 1) {
-                    const uint32_t b1 = __shfl_xor_sync(0xffffffffu, a1, o);
-                    const uint32_t b2 = __shfl_xor_sync(0xffffffffu, a2, o);
-                    top2_merge(a1, a2, b1, b2);
-                }
-                const float v = key_float(a1) + key_float(a2);
-                // group j * segs + s is held by lanes s * gsz ..; lane g takes its group's score
-                const float got = __shfl_sync(0xffffffffu, v, (lane & (segs - 1)) * gsz);
-                if ((lane >> seg_shift) == j) gs = got;
-            }
-        } else if (lane < p.n_groups) {
-            // other group sizes: lane g scans its group
-            int b1 = -1, b2 = -1;
-            float v1 = 0.f, v2 = 0.f;
-            for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
-                const float b = __ldcg(p.scores + (size_t)t * E + e) + __ldg(p.bias + e);
-                if (b1 < 0 || beats(b, e, v1, b1)) b2 = b1, v2 = v1, b1 = e, v1 = b;
-                else if (b2 < 0 || beats(b, e, v2, b2)) b2 = e, v2 = b;
-            }
-            gs = v1 + v2;
-        }
-        int rank = 0;
-        for (int h = 0; h < p.n_groups; h++) {
-            const float gh = __shfl_sync(0xffffffffu, gs, h);
-            rank += beats(gh, h, gs, lane);
-        }
-        const uint32_t keepg = __ballot_sync(0xffffffffu, lane < p.n_groups && rank < p.topk_groups);
-        // experts of the groups not kept become unselectable
-        if (pow2) {
-            const int gshift = __ffs(gsz) - 1;
-#pragma unroll
-            for (int j = 0; j < EJ; j++)
-                if (!((keepg >> (((lane + 32 * j) >> gshift) & 31)) & 1u)) key[j] = 0u;
-        } else {
-#pragma unroll
-            for (int j = 0; j < EJ; j++)
-                if (!((keepg >> (((lane + 32 * j) / gsz) & 31)) & 1u)) key[j] = 0u;
-        }
-    }
     int mine = -1;
     float s_mine = 0.f;
-    for (int i = 0; i < K; i++) {
-        // lane argmax by a tree (ties to the lower register)
-        uint32_t bk[EJ];
-        int bj[EJ];
-#pragma unroll
-        for (int j = 0; j < EJ; j++) bk[j] = key[j], bj[j] = j;
-#pragma unroll
-        for (int s = 1; s < EJ; s *= 2)
-#pragma unroll
-            for (int j = 0; j + s < EJ; j += 2 * s)
-                if (bk[j + s] > bk[j]) bk[j] = bk[j + s], bj[j] = bj[j + s];
-        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk[0]);
-        const int cand = (mk != 0u && bk[0] == mk) ? lane + 32 * bj[0] : INT_MAX;
-        int win = __reduce_min_sync(0xffffffffu, cand);
-        if (win == INT_MAX) {  // fewer candidates than topk: cannot happen for a validated layer
+    if (p.forced_idx) {
+        // forced routes: the token's experts are given; a row that is out of range or repeats an
+        // expert is replaced by experts 0..K-1 (and flagged), so the dispatch stays consistent
+        int f = -1 - lane;  // distinct placeholders on lanes >= K
+        if (lane < K) f = __ldg(p.forced_idx + (size_t)t * K + lane);
+        const uint32_t same = __match_any_sync(0xffffffffu, f);
+        const bool bad = lane < K && (f < 0 || f >= E || (same & (lane_bit - 1u)) != 0u);
+        if (__any_sync(0xffffffffu, bad)) {
             if (lane == 0 && live) atomicOr(p.status, kErrBadTable);
-            win = 0;
+            f = lane;
         }
-        const int wj = lane == (win & 31) ? (win >> 5) : -1;
-        float s_own = 0.f;
+        if (lane < K) mine = f, s_mine = __ldcg(p.scores + (size_t)t * E + f);
+    } else {
+        uint32_t key[EJ];
+        float sv[EJ];
 #pragma unroll
-        for (int j = 0; j < EJ; j++)
-            if (j == wj) key[j] = 0u, s_own = sv[j];
-        const float s_win = __shfl_sync(0xffffffffu, s_own, win & 31);
-        if (lane == i) mine = win, s_mine = s_win;
+        for (int j = 0; j < EJ; j++) {
+            const int e = lane + 32 * j;
+            key[j] = 0u;  // below every float's key: not selectable
+            sv[j] = 0.f;
+            if (e < E) {
+                const float s = __ldcg(p.scores + (size_t)t * E + e);
+                sv[j] = s;
+                key[j] = float_key(s + __ldg(p.bias + e) + 0.0f);
+            }
+        }
+        if (p.n_groups > 1 && p.topk_groups < p.n_groups) {
+            const int gsz = E / p.n_groups;
+            const bool pow2 = (gsz & (gsz - 1)) == 0;
+            // group score = top-1 + top-2 of the group's biased scores (values only); lane g ends with
+            // group g's score
+            float gs = 0.f;
+            if (pow2 && gsz >= 32) {
+                // a group is m whole registers: a tree of top-2 merges over them, then over the lanes
+                const int m = gsz >> 5;
+                uint32_t a1[EJ], a2[EJ];
+#pragma unroll
+                for (int j = 0; j < EJ; j++) a1[j] = key[j], a2[j] = 0u;
+#pragma unroll
+                for (int s = 1; s < EJ; s *= 2)
+                    if (s < m)
+#pragma unroll
+                        for (int j = 0; j + s < EJ; j += 2 * s) top2_merge(a1[j], a2[j], a1[j + s], a2[j + s]);
+                // every register's lane-wide top-2 (only group leaders j = g m are used): second largest =
+                // the largest after the lowest lane holding the maximum swaps in its own second
+#pragma unroll
+                for (int j = 0; j < EJ; j++) {
+                    const uint32_t m1 = __reduce_max_sync(0xffffffffu, a1[j]);
+                    const uint32_t bal = __ballot_sync(0xffffffffu, a1[j] == m1);
+                    const uint32_t m2 = __reduce_max_sync(0xffffffffu, (bal & (0u - bal)) == lane_bit ? a2[j] : a1[j]);
+                    if (lane * m == j) gs = key_float(m1) + key_float(m2);
+                }
+            } else if (pow2) {
+                // a group is a segment of gsz lanes of one register: top-2 merges across the segment
+                const int segs = 32 / gsz, seg_shift = __ffs(segs) - 1;
+#pragma unroll
+                for (int j = 0; j < EJ; j++) {
+                    uint32_t a1 = key[j], a2 = 0u;
+                    for (int o = gsz / 2; o > 0; o >>= 1) {
+                        const uint32_t b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+                        const uint32_t b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+                        top2_merge(a1, a2, b1, b2);
+                    }
+                    const float v = key_float(a1) + key_float(a2);
+                    // group j * segs + s is held by lanes s * gsz ..; lane g takes its group's score
+                    const float got = __shfl_sync(0xffffffffu, v, (lane & (segs - 1)) * gsz);
+                    if ((lane >> seg_shift) == j) gs = got;
+                }
+            } else if (lane < p.n_groups) {
+                // other group sizes: lane g scans its group
+                int b1 = -1, b2 = -1;
+                float v1 = 0.f, v2 = 0.f;
+                for (int e = lane * gsz; e < (lane + 1) * gsz; e++) {
+                    const float b = __ldcg(p.scores + (size_t)t * E + e) + __ldg(p.bias + e);
+                    if (b1 < 0 || beats(b, e, v1, b1)) b2 = b1, v2 = v1, b1 = e, v1 = b;
+                    else if (b2 < 0 || beats(b, e, v2, b2)) b2 = e, v2 = b;
+                }
+                gs = v1 + v2;
+            }
+            int rank = 0;
+            for (int h = 0; h < p.n_groups; h++) {
+                const float gh = __shfl_sync(0xffffffffu, gs, h);
+                rank += beats(gh, h, gs, lane);
+            }
+            const uint32_t keepg = __ballot_sync(0xffffffffu, lane < p.n_groups && rank < p.topk_groups);
+            // experts of the groups not kept become unselectable
+            if (pow2) {
+                const int gshift = __ffs(gsz) - 1;
+#pragma unroll
+                for (int j = 0; j < EJ; j++)
+                    if (!((keepg >> (((lane + 32 * j) >> gshift) & 31)) & 1u)) key[j] = 0u;
+            } else {
+#pragma unroll
+                for (int j = 0; j < EJ; j++)
+                    if (!((keepg >> (((lane + 32 * j) / gsz) & 31)) & 1u)) key[j] = 0u;
+            }
+        }
+        for (int i = 0; i < K; i++) {
+            // lane argmax by a tree (ties to the lower register)
+            uint32_t bk[EJ];
+            int bj[EJ];
+#pragma unroll
+            for (int j = 0; j < EJ; j++) bk[j] = key[j], bj[j] = j;
+#pragma unroll
+            for (int s = 1; s < EJ; s *= 2)
+#pragma unroll
+                for (int j = 0; j + s < EJ; j += 2 * s)
+                    if (bk[j + s] > bk[j]) bk[j] = bk[j + s], bj[j] = bj[j + s];
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, bk[0]);
+            const int cand = (mk != 0u && bk[0] == mk) ? lane + 32 * bj[0] : INT_MAX;
+            int win = __reduce_min_sync(0xffffffffu, cand);
+            if (win == INT_MAX) {  // fewer candidates than topk: cannot happen for a validated layer
+                if (lane == 0 && live) atomicOr(p.status, kErrBadTable);
+                win = 0;
+            }
+            const int wj = lane == (win & 31) ? (win >> 5) : -1;
+            float s_own = 0.f;
+#pragma unroll
+            for (int j = 0; j < EJ; j++)
+                if (j == wj) key[j] = 0u, s_own = sv[j];
+            const float s_win = __shfl_sync(0xffffffffu, s_own, win & 31);
+            if (lane == i) mine = win, s_mine = s_win;
+        }
     }
     // weights: unbiased scores normalised in top-k order (stbl/model.cu:450-451, 527-530)
     float sum = 0.f;

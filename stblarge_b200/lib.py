@@ -25,6 +25,14 @@ class MoEDesc(ctypes.Structure):
         ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
         ("max_tokens", I), ("router_w", P), ("router_bias", P), ("routed_w", P * 3), ("routed_s", P * 3),
         ("routed_w_stride", LL * 3), ("routed_s_stride", LL * 3), ("shared_w", P * 3), ("shared_s", P * 3),
+        ("n_slots", I),
+    ]
+
+
+class CacheDesc(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", I), ("n_experts", I), ("slots", I), ("fmt", I), ("hidden", I), ("inter", I),
+        ("host_w", P * 3), ("host_s", P * 3), ("host_w_stride", LL * 3), ("host_s_stride", LL * 3),
     ]
 
 
@@ -40,6 +48,13 @@ SIGNATURES = {
     "stbl_moe_last_route": (I, [P, P, P, P, P, P]),
     "stbl_moe_last_scores": (I, [P, P]),
     "stbl_moe_set_expert": (I, [P, I, P, P, P]),
+    "stbl_moe_forward_routed": (I, [P, P, I, P, P, P]),
+    "stbl_cache_create": (I, [ctypes.POINTER(CacheDesc), ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_cache_layer_desc": (I, [P, ctypes.POINTER(MoEDesc)]),
+    "stbl_moe_attach_cache": (I, [P, P, I]),
+    "stbl_cache_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "stbl_cache_state": (I, [P, P, P]),
+    "stbl_cache_destroy": (None, [P]),
     "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),
     "stbl_moe_set_timing": (I, [P, I]),
     "stbl_moe_timing": (I, [P, P, I]),

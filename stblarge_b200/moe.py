@@ -31,7 +31,9 @@ class MoELayer:
     full router; the layers of all ranks connect through their exchange regions (handles gathered
     with torch.distributed over the group), and every rank must then call forward in lockstep."""
 
-    def __init__(self, cfg: MoEConfig, weights: dict, max_tokens: int = 16, ep=None):
+    def __init__(self, cfg: MoEConfig, weights: dict, max_tokens: int = 16, ep=None, cache=None):
+        """cache: (ExpertCache, layer index): the routed experts live in the cache (weights then needs
+        only 'router_w', 'router_bias' and the shared expert)."""
         self.lib = L.load()
         self.cfg = cfg
         self.weights = weights  # keeps the device tensors alive
@@ -43,11 +45,14 @@ class MoELayer:
         d.routed_fmt, d.shared_fmt, d.max_tokens = cfg.routed_fmt, cfg.shared_fmt, max_tokens
         d.router_w = weights["router_w"].data_ptr()
         d.router_bias = weights["router_bias"].data_ptr()
+        if cache is not None:
+            cache[0].layer_desc(d)
         for m in range(3):
-            w, s = weights["routed_w"][m], weights["routed_s"][m]
-            d.routed_w[m], d.routed_s[m] = w.data_ptr(), s.data_ptr()
-            d.routed_w_stride[m] = w.stride(0) * w.element_size()
-            d.routed_s_stride[m] = s.stride(0) * s.element_size()
+            if cache is None:
+                w, s = weights["routed_w"][m], weights["routed_s"][m]
+                d.routed_w[m], d.routed_s[m] = w.data_ptr(), s.data_ptr()
+                d.routed_w_stride[m] = w.stride(0) * w.element_size()
+                d.routed_s_stride[m] = s.stride(0) * s.element_size()
             if cfg.shared_fmt != FMT_NONE:
                 d.shared_w[m] = weights["shared_w"][m].data_ptr()
                 d.shared_s[m] = weights["shared_s"][m].data_ptr()
@@ -59,6 +64,9 @@ class MoELayer:
         self.handle = h
         self._desc = d
         self.ep = (rank, n_ranks)
+        self.cache = cache
+        if cache is not None:
+            self._check(self.lib.stbl_moe_attach_cache(self.handle, cache[0].handle, cache[1]), "stbl_moe_attach_cache")
         if n_ranks > 1:
             import torch.distributed as dist
             mine = ctypes.create_string_buffer(EP_HANDLE_BYTES)
@@ -85,6 +93,18 @@ class MoELayer:
         st = stream if stream is not None else torch.cuda.current_stream(x.device)
         self._check(self.lib.stbl_moe_forward(self.handle, _ptr(x), x.shape[0], _ptr(out), ctypes.c_void_p(st.cuda_stream)),
                     "stbl_moe_forward")
+        return out
+
+    def forward_routed(self, x, idx, out=None, stream=None):
+        """The layer with its routed experts given: idx cuda int32 [T, topk] (distinct per token)."""
+        assert x.is_cuda and x.dim() == 2 and x.shape[1] == self.cfg.hidden and x.element_size() == 2
+        assert idx.is_cuda and idx.dtype == torch.int32 and tuple(idx.shape) == (x.shape[0], self.cfg.topk)
+        x, idx = x.contiguous(), idx.contiguous()
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self._check(self.lib.stbl_moe_forward_routed(self.handle, _ptr(x), x.shape[0], _ptr(idx), _ptr(out),
+                                                     ctypes.c_void_p(st.cuda_stream)), "stbl_moe_forward_routed")
         return out
 
     def forward_host(self, x_bits, y_bits=None, stream=None):

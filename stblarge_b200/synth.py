@@ -143,12 +143,25 @@ def mat_shapes(cfg):
     return ((I, H), (I, H), (H, I))
 
 
-def device_layer(cfg, device="cuda", experts=None):
+def routed_expert(cfg, seed, device="cuda"):
+    """One routed expert's quantized matrices (gate, up, down) and scales from seed `seed`."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    ws, ss = [], []
+    for (r, k) in mat_shapes(cfg):
+        w = torch.randn(r, k, generator=g, device=device, dtype=torch.float32) * cfg.weight_std
+        c, s = quantize(w, cfg.routed_fmt)
+        ws.append(c)
+        ss.append(s)
+    return ws, ss
+
+
+def device_layer(cfg, device="cuda", experts=None, seed_base=1000):
     """Quantized device tensors in the expert-major layout the C ABI takes:
     'routed_w'[m]: uint8 [E, rows, codes per row]; 'routed_s'[m]: scales [E, ...];
     'shared_w'[m], 'shared_s'[m] likewise without the expert axis; 'router_w' fp32 [E, H];
     'router_bias' fp32 [E].  experts: the routed experts to build (a range: an expert-parallel
-    rank's shard; expert e keeps seed 1000 + e), all by default."""
+    rank's shard; expert e keeps seed seed_base + e), all by default."""
     experts = range(cfg.n_experts) if experts is None else experts
     E = len(experts)
     shapes = mat_shapes(cfg)
@@ -161,13 +174,10 @@ def device_layer(cfg, device="cuda", experts=None):
             routed_w.append(torch.empty(E, r, k // 2, dtype=torch.uint8, device=device))
             routed_s.append(torch.empty(E, r, k // 32, dtype=torch.uint8, device=device))
     for i, e in enumerate(experts):
-        g = torch.Generator(device=device)
-        g.manual_seed(1000 + e)
-        for m, (r, k) in enumerate(shapes):
-            w = torch.randn(r, k, generator=g, device=device, dtype=torch.float32) * cfg.weight_std
-            c, s = quantize(w, cfg.routed_fmt)
-            routed_w[m][i].copy_(c)
-            routed_s[m][i].copy_(s)
+        ws, ss = routed_expert(cfg, seed_base + e, device)
+        for m in range(3):
+            routed_w[m][i].copy_(ws[m])
+            routed_s[m][i].copy_(ss[m])
     out = {"routed_w": routed_w, "routed_s": routed_s, "shared_w": None, "shared_s": None}
     if cfg.shared_fmt != FMT_NONE:
         g = torch.Generator(device=device)

@@ -1,0 +1,85 @@
+"""GPU expert cache (stbl_cache_*) and forced routes (stbl_moe_forward_routed), through the C ABI.
+
+Cached layers must give the same bits as layers holding every expert in device memory (same
+kernels, same weights, read from the cache's slots), and the cache's decisions (which slot holds
+which expert, hits, misses) must equal the reference's LRU bookkeeping restated in the oracle
+(oracle.LruExpertCache, stbl/model.cu:347-422, 503-520) after every call.  Forced routes are checked
+against the oracle layer with the same routes."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from stblarge_b200 import synth
+from stblarge_b200.cache import ExpertCache, host_store
+from stblarge_b200.config import CFG1, CFG1_FP4
+from stblarge_b200.moe import MoELayer
+from tests.test_gpu_layer import TOL, compare_y, oracle_weights_from_device
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(cfg, T, seed):
+    return torch.from_numpy(synth.make_x(cfg.hidden, T, seed=seed).view(np.int16)).cuda()
+
+
+@pytest.mark.parametrize("cfg", [CFG1, CFG1_FP4], ids=["fp8", "mxfp4"])
+def test_cached_layers_match_resident_layers_and_reference_lru(cfg):
+    L, S, Tmax, E = 3, 8, 2, cfg.n_experts
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, S, store)
+    resident = [synth.device_layer(cfg, seed_base=1000 + l * E) for l in range(L)]
+    plain = [MoELayer(cfg, resident[l], max_tokens=Tmax) for l in range(L)]
+    cached = [MoELayer(cfg, resident[l], max_tokens=Tmax, cache=(cache, l)) for l in range(L)]
+    lru = O.LruExpertCache(S)
+    rng = np.random.default_rng(11)
+    for call in range(16):
+        l, T = int(rng.integers(L)), int(rng.integers(1, Tmax + 1))
+        x = _x(cfg, T, 500 + call)
+        y_plain, y = plain[l](x), cached[l](x)
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), y_plain.view(torch.int16)), f"call {call}: cached layer differs"
+        lru.call(l, cached[l].last_route()["idx"])
+        mp, owner = cache.state()
+        emp, eowner = lru.state(L, E)
+        assert np.array_equal(mp, emp), f"call {call}: residency map differs"
+        assert np.array_equal(owner, eowner), f"call {call}: slot owners differ"
+        st = cache.stats()
+        assert (st["hits"], st["misses"]) == (lru.hits, lru.misses)
+    assert lru.misses > S and lru.hits > 0, "the sequence must both evict and hit"
+    assert cache.stats()["bytes"] == lru.misses * sum(
+        t[0].numel() * t.element_size() for t in store["w"] + store["s"])
+    for layer in cached + plain:
+        assert layer.status() == 0
+        layer.close()
+    cache.close()
+
+
+@pytest.mark.parametrize("cfg", [CFG1, CFG1_FP4], ids=["fp8", "mxfp4"])
+def test_forward_routed_matches_oracle(cfg):
+    dev = synth.device_layer(cfg)
+    layer = MoELayer(cfg, dev, max_tokens=8)
+    rng = np.random.default_rng(3)
+    for T in (1, 5):
+        x_bits = synth.make_x(cfg.hidden, T, seed=40 + T)
+        forced = np.stack([rng.permutation(cfg.n_experts)[:cfg.topk] for _ in range(T)]).astype(np.int32)
+        y = layer.forward_routed(torch.from_numpy(x_bits.view(np.int16)).cuda(), torch.from_numpy(forced).cuda())
+        torch.cuda.synchronize()
+        route = layer.last_route()
+        assert np.array_equal(route["idx"], forced)
+        W = oracle_weights_from_device(cfg, dev, forced.reshape(-1))
+        y_ref, idx_ref, w_ref = O.moe_forward(cfg.as_dict(), W, x_bits, forced=forced)
+        assert np.array_equal(route["weights"].view(np.uint32), w_ref.view(np.uint32)), "routing weights differ"
+        counts, offsets, perm = O.dispatch(forced, cfg.n_experts)
+        assert np.array_equal(route["perm"], perm)
+        rel, same, ulps = compare_y(y.view(torch.int16).cpu().numpy().view(np.uint16), y_ref)
+        assert rel <= TOL, f"max-abs-rel {rel:.3e} ({ulps:.1f} bf16 ulps)"
+    assert layer.status() == 0
+    # a row that repeats an expert is replaced by experts 0..topk-1 and flagged
+    bad = np.zeros((1, cfg.topk), np.int32)
+    layer.forward_routed(_x(cfg, 1, 9), torch.from_numpy(bad).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(layer.last_route()["idx"][0], np.arange(cfg.topk))
+    assert layer.status() == 2
+    layer.close()
