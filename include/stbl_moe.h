@@ -122,6 +122,10 @@ typedef struct stbl_cache_desc {
     const void *host_s[3];
     long long host_w_stride[3];
     long long host_s_stride[3];
+    /* experts held by the store (0: n_layers * n_experts); expert (l, e) reads store row
+       (l * n_experts + e) mod host_rows, so a store smaller than the model repeats its experts
+       (synthetic benchmarks: every miss still moves a whole expert) */
+    long long host_rows;
 } stbl_cache_desc;
 int stbl_cache_create(const stbl_cache_desc *desc, stbl_cache **out, char *err, int errlen);
 /* Points desc's routed weights at the cache's slot pool (routed_w/routed_s, strides, n_slots,

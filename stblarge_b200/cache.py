@@ -57,8 +57,7 @@ class ExpertCache:
             d.host_w[m], d.host_s[m] = w.data_ptr(), s.data_ptr()
             d.host_w_stride[m] = w.stride(0) * w.element_size()
             d.host_s_stride[m] = s.stride(0) * s.element_size()
-        if store["rows"] < store["n"]:
-            raise ValueError("a repeated store (physical < experts) needs stbl_cache_desc strides of its own")
+        d.host_rows = store["rows"]
         err = ctypes.create_string_buffer(512)
         h = ctypes.c_void_p()
         if self.lib.stbl_cache_create(ctypes.byref(d), ctypes.byref(h), err, 512) != 0:

@@ -50,6 +50,7 @@ struct CacheCopyParams {
     uint8_t *pool;
     long long slot_bytes;
     long long piece_bytes[6], piece_off[6], host_stride[6];
+    long long host_rows;
     const uint8_t *host[6];
     int chunks[6];  // kCopyChunk pieces of each matrix piece
 };
@@ -191,7 +192,8 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
         const int2 job = p.jobs[jb];
         const long long off = (long long)r * kCopyChunk;
         const long long bytes = min((long long)kCopyChunk, p.piece_bytes[q] - off);
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)job.y * p.host_stride[q] + off);
+        const long long hrow = (long long)job.y % p.host_rows;
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + off);
         uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + off);
         const int words = (int)(bytes >> 4);
         uint4 v[kCopyUnroll];
@@ -229,6 +231,7 @@ void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *sta
     launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
     CacheCopyParams cp{};
     cp.jobs = c->jobs, cp.n_jobs = c->n_jobs, cp.pool = c->pool, cp.slot_bytes = c->slot_bytes;
+    cp.host_rows = c->host_rows;
     for (int q = 0; q < 6; q++) {
         cp.piece_bytes[q] = c->piece_bytes[q], cp.piece_off[q] = c->piece_off[q], cp.host_stride[q] = c->host_stride[q];
         cp.host[q] = c->host[q];
@@ -275,6 +278,8 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
         if ((long long)d->n_layers * d->n_experts >= (1LL << 31)) throw std::runtime_error("store too large");
         c = new stbl_cache();
         c->L = d->n_layers, c->E = d->n_experts, c->S = d->slots, c->fmt = d->fmt, c->H = d->hidden, c->I = d->inter;
+        if (d->host_rows < 0 || d->host_rows > (long long)c->L * c->E) throw std::runtime_error("host_rows must be in 0..n_layers*n_experts");
+        c->host_rows = d->host_rows ? d->host_rows : (long long)c->L * c->E;
         CK(cudaGetDevice(&c->dev));
         const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
         long long off = 0;

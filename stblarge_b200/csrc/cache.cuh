@@ -12,7 +12,8 @@ struct stbl_cache {
     // pool + s * slot_bytes + piece_off[p]
     long long piece_bytes[6] = {}, piece_off[6] = {}, slot_bytes = 0, expert_bytes = 0;
     const uint8_t *host[6] = {};      // device-visible addresses of the host store (pinned memory)
-    long long host_stride[6] = {};    // bytes between experts (l * E + e) of a piece
+    long long host_stride[6] = {};    // bytes between store rows of a piece
+    long long host_rows = 0;          // store rows; expert (l, e) is row (l * E + e) mod host_rows
     uint8_t *pool = nullptr;          // [S][slot_bytes]
     int *map = nullptr;               // [L][E] slot of (layer, expert), -1 when not resident
     int *owner = nullptr;             // [S] l * E + e held by the slot, -1 when free

@@ -33,6 +33,7 @@ class CacheDesc(ctypes.Structure):
     _fields_ = [
         ("n_layers", I), ("n_experts", I), ("slots", I), ("fmt", I), ("hidden", I), ("inter", I),
         ("host_w", P * 3), ("host_s", P * 3), ("host_w_stride", LL * 3), ("host_s_stride", LL * 3),
+        ("host_rows", LL),
     ]
 
 
