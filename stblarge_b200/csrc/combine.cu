@@ -7,8 +7,8 @@
 namespace stbl {
 
 __global__ void __launch_bounds__(256) combine_kernel(CombineParams p) {
+    pdl_launch_dependents();  // the next kernel may start its prologue; it waits for this one's end
     pdl_wait();
-    pdl_launch_dependents();
     if (p.ep.n_ranks > 1) {
         // expert parallelism: this rank's down kernel (before this one) has finished writing into
         // every source rank's eo rows: say so everywhere, then wait until every rank has said so

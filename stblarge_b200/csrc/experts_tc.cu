@@ -13,8 +13,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_c
 // x codes and scales of every position (routed assignments in dispatch order, then the shared
 // expert's tokens), for the up kernel's activation tiles when T > 16
 __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
+    pdl_launch_dependents();  // the next kernel may start its prologue; it waits for this one's end
     pdl_wait();
-    pdl_launch_dependents();
     const int pos = blockIdx.x;
     const int nrouted = p.T * p.topk;
     const int tok = pos < nrouted ? p.perm[pos] / p.topk : pos - nrouted;
@@ -34,8 +34,8 @@ __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
 // act_quant per 128 (ref/kernel.py:35-45, fp32 scale amax/448) of h for the down kernel: one warp per
 // (position, 128-value block), four values a lane.
 __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
+    pdl_launch_dependents();  // the next kernel may start its prologue; it waits for this one's end
     pdl_wait();
-    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int per_row = p.I / 128;
     const int nw = gridDim.x * (blockDim.x / 32);

@@ -36,7 +36,7 @@ constexpr int kT4BTile = kTcN * 128; // one K block of activations
 constexpr int kT4SfSlots = 4;        // scale-factor slots in TMEM, 16 columns each (A0, A1, B)
 constexpr int kT4SfBase = 128;       // first TMEM column of the scale slots
 constexpr int kT4TmemCols = 256;
-constexpr int kT4Chunks = 32;
+constexpr int kT4Chunks = 192;       // chunk entries [chunk_begin, +192) kept in shared memory
 constexpr int kT4PartialCols = 32;   // floats per row in the stream-K partial buffer
 
 template <bool UP>
@@ -100,16 +100,21 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     unsigned char *stages = smem;                                                   // [nst][A | B | SF]
     int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][16] by column
     float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);                  // [2][16]
-    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);                      // [kT4Chunks]
+    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);                      // [kT4Chunks] from chunk_begin
     uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kT4Chunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
     uint64_t *acc_empty = acc_full + kT4Acc;
     uint64_t *mma_done = acc_empty + kT4Acc;
     __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, s_chunk_end;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 32) {
+        // the tensor maps are kernel parameters: fetch their descriptors while the previous kernel drains
+        for (int m = 0; m < S::nA; m++) tma_prefetch_map(&maps.w[m]);
+        tma_prefetch_map(&maps.b);
+    }
     if (tid == 0) {
         abort_flag = 0;
         // full: the producer lane's transaction arrival + one cp.async arrival per producer lane
@@ -126,7 +131,11 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
 
     pdl_wait();
     pdl_launch_dependents();
-    const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
+    // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
+    if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
+    if (p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    __syncthreads();
+    const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
     const long long n_units = n_items * nu;
     const long long u_lo = n_units * cta / ncta, u_hi = n_units * (cta + 1) / ncta;
@@ -135,21 +144,13 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
         ua = (int)max(u_lo - (long long)it * nu, 0LL);
         uz = (int)min(u_hi - (long long)it * nu, (long long)nu);
     };
-    const int c_lo = p.chunk_begin + lo / tiles;
-    for (int i = tid; i < kT4Chunks; i += kT4Threads)
-        if (lo < hi && c_lo + i <= p.chunk_begin + (hi - 1) / tiles) ctab[i] = p.chunks[c_lo + i];
-    __syncthreads();
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - c_lo < kT4Chunks) ? ctab[c - c_lo] : p.chunks[c];
+        const Chunk ch = (c - p.chunk_begin < kT4Chunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
         return tc_check(p, ch);
     };
 
     if (warp == 0) {
         // ---------------- producer (lane 0: TMA; all lanes: scale words) ----------------
-        if (lane == 0) {
-            for (int m = 0; m < S::nA; m++) tma_prefetch_map(&maps.w[m]);
-            tma_prefetch_map(&maps.b);
-        }
         int q = 0;
         bool stop = false;
         for (int it = lo; it < hi && !stop; it++) {

@@ -87,7 +87,8 @@ struct stbl_moe {
     // re-points experts at other slots, stbl_moe_set_expert)
     int *slot = nullptr;
     std::vector<int> host_slot;
-    int n_slots = 0;                  // slots in the routed arrays (>= E_loc)
+    int n_slots = 0;                  // slots in the routed arrays
+    bool slots_moved = false;         // some expert reads a slot other than its own id
     stbl_cache *cache = nullptr;      // attached expert cache (stbl_moe_attach_cache), layer cache_layer
     int cache_layer = 0;
     long long w_stride[3] = {0, 0, 0}, s_stride[3] = {0, 0, 0};  // bytes between slots
@@ -436,7 +437,10 @@ EpView ep_view(const stbl_moe *m) {
 
 TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     TcParams p{};
-    p.slot = m->cache ? m->cache->map + (size_t)m->cache_layer * m->E : m->slot;
+    // slot table: the cache's map row, the layer's own table once an expert was re-pointed, else none
+    // (slot = expert: the kernels skip the lookup)
+    p.slot = m->cache ? m->cache->map + (size_t)m->cache_layer * m->E : (m->slots_moved ? m->slot : nullptr);
+    p.chunk_cap = m->routed_cap + m->Tmax;
     p.chunks = m->chunks;
     p.n_chunks = m->n_chunks;
     p.T = T, p.topk = m->K, p.E = m->E_loc, p.H = m->H, p.I = m->I;
@@ -880,6 +884,7 @@ int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *
                 s[i] != static_cast<const char *>(m->d.routed_s[i]) + sl * m->s_stride[i])
                 throw std::runtime_error("the three matrices and scales of an expert must share one slot");
         m->host_slot[e] = (int)sl;
+        if (sl != e) m->slots_moved = true;
         CK(cudaMemcpyAsync(m->slot + e, &m->host_slot[e], sizeof(int), cudaMemcpyHostToDevice, stream));
         return 0;
     } catch (const std::exception &e2) {

@@ -38,7 +38,7 @@ constexpr int kATile = 128 * 128;
 constexpr int kBTile = kTcN * 128;
 constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
 constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
-constexpr int kTcChunks = 32;     // chunk entries of a CTA's item range kept in shared memory
+constexpr int kTcChunks = 192;    // chunk entries [chunk_begin, +192) kept in shared memory (one per thread)
 constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
 
 // One CTA's share of an FP8 expert launch: CTA `cta` of the `ncta` that run this body (in a mixed
@@ -58,16 +58,21 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
     int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);           // [2][16] B column of a slot
     int *slot_dst = slot_col + 2 * kTcN;                                  // [2][16] output row of a slot
-    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);         // [kTcChunks] this CTA's chunks
+    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);         // [kTcChunks] from chunk_begin
     uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kTcChunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
     uint64_t *acc_empty = acc_full + kTcAcc;
     uint64_t *mma_done = acc_empty + kTcAcc;
     __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, s_chunk_end;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 32) {
+        // the tensor maps are kernel parameters: fetch their descriptors while the previous kernel drains
+        for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]), tma_prefetch_map(&maps.s[m]);
+        tma_prefetch_map(&maps.b);
+    }
     if (tid == 0) {
         abort_flag = 0;
         for (int s = 0; s < nst; s++) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
@@ -97,7 +102,11 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         }
         __syncthreads();
     }
-    const int chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
+    // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
+    if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
+    if (p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    __syncthreads();
+    const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
     const long long n_units = n_items * nkb;
     const long long u_lo = n_units * cta / ncta, u_hi = n_units * (cta + 1) / ncta;
@@ -107,21 +116,15 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         ka = (int)max(u_lo - (long long)it * nkb, 0LL);
         kz = (int)min(u_hi - (long long)it * nkb, (long long)nkb);
     };
-    // the chunks this CTA's items touch, in shared memory (items beyond the table read global memory)
-    const int c_lo = p.chunk_begin + lo / tiles;
-    for (int i = tid; i < kTcChunks; i += kTcThreads)
-        if (lo < hi && c_lo + i <= p.chunk_begin + (hi - 1) / tiles) ctab[i] = p.chunks[c_lo + i];
-    __syncthreads();
+    // chunks beyond the shared-memory table are read from global memory
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - c_lo < kTcChunks) ? ctab[c - c_lo] : p.chunks[c];
+        const Chunk ch = (c - p.chunk_begin < kTcChunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
         return tc_check(p, ch);
     };
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]), tma_prefetch_map(&maps.s[m]);
-            tma_prefetch_map(&maps.b);
             int q = 0;  // running stage counter
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {

@@ -18,6 +18,7 @@ struct TcParams {
     const Chunk *chunks;
     const int *n_chunks;
     int chunk_begin, chunk_end;
+    int chunk_cap;             // entries of the chunks array (reads beyond the live count stay inside it)
     int T, topk, E, H, I;
     const int *perm;
     const float *wts;
