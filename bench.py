@@ -371,11 +371,16 @@ def main():
             "distinct_experts_per_step": float(np.mean(distinct)),
             "kernel_ms_per_step": {"router": kt["router"] / max(kt["calls"], 1) * 1e3, "up": up_ms,
                                    "down": kt["down"] / max(kt["calls"], 1) * 1e3},
-            "roofline": {"bound": "hbm", "kernel": "expert_tc_kernel<up> (tcgen05 FP8 gate+up, SwiGLU)", "achieved": up_gbs,
-                         "peak": peak, "unit": "GB/s", "frac": up_gbs / peak, "peak_kind": peak_kind,
-                         "traffic": traffic_from_profile(float(np.mean(distinct)) + 1.0),
-                         "traffic_note": "ncu DRAM read+write bytes per expert of one up launch (profiles/traffic.json) "
-                                         "x the step's mean distinct routed experts + the shared expert"},
+            "roofline": {"bound": "hbm", "kernel": ("expert_tc4_kernel<up> (tcgen05 MXFP4 routed + FP8 shared gate+up, SwiGLU)"
+                                                    if cfg.routed_fmt == FMT_MXFP4 else
+                                                    "expert_tc_kernel<up> (tcgen05 FP8 gate+up, SwiGLU)"),
+                         "achieved": up_gbs, "peak": peak, "unit": "GB/s", "frac": up_gbs / peak, "peak_kind": peak_kind,
+                         "traffic": traffic_from_profile(cfg, float(np.mean(distinct)) + 1.0, up_alg),
+                         "traffic_note": ("ncu DRAM read+write over algorithmic bytes of one MXFP4 up launch "
+                                          "(profiles/traffic.json) x this step's algorithmic up bytes"
+                                          if cfg.routed_fmt == FMT_MXFP4 else
+                                          "ncu DRAM read+write bytes per expert of one up launch (profiles/traffic.json) "
+                                          "x the step's mean distinct routed experts + the shared expert")},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * cfg.hidden * 2,
                     "d2h_bytes_per_step": T * cfg.hidden * 2},
             "gpu_launches": launches * args.steps,
@@ -389,15 +394,20 @@ def main():
         dist.destroy_process_group()
 
 
-def traffic_from_profile(experts_per_launch):
-    """DRAM bytes per launch of the up kernel: the committed ncu figure per expert (a capture of a
-    smaller case, where traffic grows in proportion to the experts streamed) times the experts one
-    launch of this workload streams.  None when there is no committed figure."""
+def traffic_from_profile(cfg, experts_per_launch, up_alg):
+    """DRAM bytes per launch of the up kernel from the committed ncu captures of smaller cases, where
+    traffic grows in proportion to the experts streamed: FP8, the figure per expert times the experts
+    one launch streams; MXFP4 (a mixed launch), the captured DRAM / algorithmic ratio times this
+    launch's algorithmic bytes.  None when there is no committed figure."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            per_expert = json.load(f).get("expert_up_fp8_dram_bytes_per_expert")
+            t = json.load(f)
     except Exception:
         return None
+    if cfg.routed_fmt == FMT_MXFP4:
+        r = t.get("expert_up_mxfp4_dram_over_algorithmic")
+        return None if r is None else r * up_alg
+    per_expert = t.get("expert_up_fp8_dram_bytes_per_expert")
     return None if per_expert is None else per_expert * experts_per_launch
 
 
