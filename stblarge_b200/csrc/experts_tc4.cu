@@ -373,18 +373,27 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
             const float *cw = col_w + buf * kTcN;
             const int r = tile * 128 + row;
             if (UP) {
-                // SwiGLU per column straight from the two accumulators (gate: va, up: vb)
+                // SwiGLU per column straight from the two accumulators (gate: va, up: vb); h is bf16
+                // (stbl/kernels.cu:445-459) and goes to the down product as act_quant per 32 with a
+                // power-of-two scale (stbl/kernels.cu:56-63): the 32 rows of this warp are one block,
+                // so the block's amax is a warp reduction and h never leaves the SM unquantized
 #pragma unroll
                 for (int j = 0; j < kTcN; j++) {
                     const int dst = cdst[j];
-                    if (dst < 0) continue;
+                    if (dst < 0) continue;  // the same for every thread of the warpgroup
                     float gv = bf16r(va[j]), uv = bf16r(vb[j]);
                     if (p.swiglu_limit > 0.f) {
                         gv = fminf(gv, p.swiglu_limit);
                         uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
                     }
-                    const float hv = gv / (1.f + expf(-gv)) * uv * cw[j];
-                    p.h[(size_t)dst * p.I + r] = f32_to_bf16_bits(hv);
+                    const float hv = bf16r(gv / (1.f + expf(-gv)) * uv * cw[j]);
+                    float amax = fabsf(hv);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                    amax = fmaxf(amax, 1e-4f);
+                    const float s = pow2_ceil(amax * (1.0f / 448.0f));
+                    p.hq[(size_t)dst * p.I + r] = e4m3_code(fminf(fmaxf(hv / s, -448.f), 448.f));
+                    if (lane == 0) p.he8[(size_t)dst * (p.I / 32) + r / 32] = (uint8_t)(__float_as_uint(s) >> 23);
                 }
             } else {
 #pragma unroll

@@ -490,6 +490,7 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
         p.act_e8 = up ? (direct ? m->xe8_a : m->xe8_pos) : m->he8;
     }
     p.h = m->h;
+    p.hq = m->hq, p.he8 = m->he8;
     p.swiglu_limit = m->d.swiglu_limit;
     p.eo = m->eo, p.sh = m->sh;
     p.has_shared = m->has_shared;
@@ -540,15 +541,6 @@ void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
     launch_pdl(gather_kernel_ptr(), dim3(rows), dim3(256), args, 0, st);
 }
 
-// act_quant of h by the per-32 power-of-two rule (MXFP4 experts), e8m0 scales
-void launch_hquant32(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
-    if (pos_end <= pos_begin) return;
-    HquantParams hp{m->h + (size_t)pos_begin * m->I, m->hq + (size_t)pos_begin * m->I, nullptr, pos_end - pos_begin, m->I,
-                    nullptr, 0, m->he8 + (size_t)pos_begin * (m->I / 32)};
-    void *args[] = {&hp};
-    const int warps = hp.n_pos * (m->I / 128);
-    launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
-}
 
 // Launch with programmatic dependent launch: the kernel may start while the previous one in the
 // stream drains (its CTAs block in griddepcontrol.wait until that grid has completed).
@@ -653,7 +645,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     } else {
         // MXFP4 routed experts on the block-scaled tensor cores; the FP8 shared expert (its chunks read
         // x by token, as 16 consecutive tokens, at any T) on a share of the same launches' CTAs:
-        // [gather] -> up (routed + shared) -> hquant (per-32 routed, per-128 shared) -> down -> combine
+        // [gather] -> up (routed + shared; the routed h rows quantized per 32 in its epilogue) ->
+        // hquant (per-128, shared rows) -> down -> combine
         const bool direct = T <= 16;
         const int ns = m->has_shared ? (T + 15) / 16 : 0;
         if (!direct) {
@@ -663,10 +656,9 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         TcParams su = tc_params(m, T, true, true), pu = tc_params(m, T, true, direct);
         su.chunk_begin = 0, su.chunk_end = ns;
         pu.chunk_begin = ns, pu.chunk_end = -1;
-        launch_tc4(m, true, su, pu, st);
+        launch_tc4(m, true, su, pu, st);  // the routed rows of h leave it already quantized (per 32)
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
-        launch_hquant32(m, 0, T * m->K, st);
-        launches += 2;
+        launches += 1;
         if (ns) {
             launch_hquant(m, T * m->K, npos, st);
             launches++;

@@ -38,6 +38,7 @@ struct TcParams {
     const float *s_scale[2];   // shared expert block scales
     float swiglu_limit;        // > 0: SwiGLU clamps (stbl/kernels.cu:445-459)
     uint16_t *h;               // up out: [pos][I] bf16
+    uint8_t *hq, *he8;         // MXFP4 up out: h quantized for the down product, e4m3 [pos][I] + e8m0 [pos][I/32]
     uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
     // rows [0, n_routed) are routed assignments, the shared expert's rows follow (row n_routed + token)
