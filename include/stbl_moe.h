@@ -63,6 +63,12 @@ typedef struct stbl_moe_desc {
        slots than a layer has experts (stbl_cache_layer_desc fills this and the routed pointers; a
        layer with fewer slots than experts runs only once its cache is attached) */
     int n_slots;
+    /* MXFP4 only: 1 when routed_s already holds the scales in the tensor cores' scale-block layout
+       (per slot and matrix [rows/128][k/128][512 B], byte l*16 + c*4 + j = scale of row 32c + l,
+       32-block j of the 128-k block; an expert cache's pool holds them so).  0: the natural
+       [rows][k/32] layout; the layer then keeps its own copy in the block layout, made at create for
+       every slot and again for a slot when stbl_moe_set_expert points an expert at it. */
+    int routed_s_blocked;
 } stbl_moe_desc;
 
 /* Validate the description, allocate the layer's workspace on the current device and build its

@@ -52,7 +52,11 @@ struct CacheCopyParams {
     long long piece_bytes[6], piece_off[6], host_stride[6];
     long long host_rows;
     const uint8_t *host[6];
-    int chunks[6];  // kCopyChunk pieces of each matrix piece
+    int chunks[6];  // work items of each piece: kCopyChunk bytes, or (blocked scales) one 128-row tile
+    // MXFP4 caches: the scale pieces (3..5) are written in the expert kernel's scale-block layout
+    // (per 128 rows x 128 K a 512-byte block, byte l*16 + c*4 + j = scale of row 32c + l, 32-block j)
+    int blocked;
+    int rows[3], K[3];
 };
 
 __device__ __forceinline__ unsigned long long min_u64_warp(unsigned long long v) {
@@ -190,6 +194,27 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
         int r = (int)(it % per_job), q = 0;
         while (q < 5 && r >= p.chunks[q]) r -= p.chunks[q++];
         const int2 job = p.jobs[jb];
+        if (p.blocked && q >= 3) {
+            // one 128-row tile of natural [rows][K/32] scales through shared memory into its blocks
+            extern __shared__ uint4 tile_s[];
+            const int mt = q - 3, kw = p.K[mt] / 32, nkb = p.K[mt] / 128;
+            const long long hrow = (long long)job.y % p.host_rows;
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + (size_t)r * 128 * kw);
+            const int words = 128 * kw / 16;
+            __syncthreads();  // the previous item's reads of tile_s are done
+            for (int w = threadIdx.x; w < words; w += kCopyThreads) tile_s[w] = src[w];
+            __syncthreads();
+            const uint8_t *ts = reinterpret_cast<const uint8_t *>(tile_s);
+            uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + (size_t)r * nkb * 512);
+            for (int w = threadIdx.x; w < nkb * 32; w += kCopyThreads) {  // 16 bytes = row group l of block kb
+                const int kb = w >> 5, l = w & 31;
+                uint32_t v[4];
+#pragma unroll
+                for (int c = 0; c < 4; c++) v[c] = *reinterpret_cast<const uint32_t *>(ts + (size_t)(32 * c + l) * kw + kb * 4);
+                dst[w] = make_uint4(v[0], v[1], v[2], v[3]);
+            }
+            continue;
+        }
         const long long off = (long long)r * kCopyChunk;
         const long long bytes = min((long long)kCopyChunk, p.piece_bytes[q] - off);
         const long long hrow = (long long)job.y % p.host_rows;
@@ -232,13 +257,21 @@ void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *sta
     CacheCopyParams cp{};
     cp.jobs = c->jobs, cp.n_jobs = c->n_jobs, cp.pool = c->pool, cp.slot_bytes = c->slot_bytes;
     cp.host_rows = c->host_rows;
+    cp.blocked = c->fmt == STBL_FMT_MXFP4;
+    const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
+    int smem = 0;
     for (int q = 0; q < 6; q++) {
         cp.piece_bytes[q] = c->piece_bytes[q], cp.piece_off[q] = c->piece_off[q], cp.host_stride[q] = c->host_stride[q];
         cp.host[q] = c->host[q];
         cp.chunks[q] = (int)((c->piece_bytes[q] + kCopyChunk - 1) / kCopyChunk);
+        if (cp.blocked && q >= 3) {
+            cp.rows[q - 3] = rows[q - 3], cp.K[q - 3] = ks[q - 3];
+            cp.chunks[q] = rows[q - 3] / 128;
+            smem = std::max(smem, 128 * (ks[q - 3] / 32));
+        }
     }
     void *a2[] = {&cp};
-    launch_pdl_k((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, 0, st);
+    launch_pdl_k((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, smem, st);
 }
 
 }  // namespace stbl
@@ -331,6 +364,7 @@ int stbl_cache_layer_desc(const stbl_cache *c, stbl_moe_desc *d) {
     if (!c || !d) return -1;
     d->routed_fmt = c->fmt;
     d->n_slots = c->S;
+    d->routed_s_blocked = c->fmt == STBL_FMT_MXFP4;  // the copy writes MXFP4 scales in the block layout
     for (int q = 0; q < 3; q++) {
         d->routed_w[q] = c->pool + c->piece_off[q];
         d->routed_s[q] = c->pool + c->piece_off[q + 3];

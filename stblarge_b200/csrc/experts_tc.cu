@@ -22,9 +22,9 @@ __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
     uint4 *dst = reinterpret_cast<uint4 *>(p.xq_pos + (size_t)pos * p.H);
     for (int i = threadIdx.x; i < p.H / 16; i += blockDim.x) dst[i] = __ldg(src + i);
     if (p.xe8) {
-        const uint32_t *se = reinterpret_cast<const uint32_t *>(p.xe8 + (size_t)tok * (p.H / 32));
-        uint32_t *de = reinterpret_cast<uint32_t *>(p.xe8_pos + (size_t)pos * (p.H / 32));
-        for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x) de[i] = __ldg(se + i);
+        for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x)
+            *reinterpret_cast<uint32_t *>(p.xe8_pos + ((size_t)i * p.xe8_pos_rows + pos) * 16) =
+                __ldg(reinterpret_cast<const uint32_t *>(p.xe8 + ((size_t)i * p.xe8_rows + tok) * 16));
     } else {
         for (int i = threadIdx.x; i < p.H / 128; i += blockDim.x)
             p.xs_pos[(size_t)pos * (p.H / 128) + i] = __ldg(p.xs + (size_t)tok * p.xs_stride + i);

@@ -14,17 +14,21 @@
 // 256-K unit: each weight matrix arrives as ONE 4-D TMA box of 128 rows x 2 K blocks (128 contiguous
 // bytes of packed codes per row and op; single-K-block boxes read 64-byte row pieces, which streams
 // about a third slower from HBM), the activations as one 16-row x 2-K-block box.  Six warps:
-//   warp 0     producer: lane 0 issues the TMA boxes (the packed codes land in the 128-byte swizzled
-//              layout the MMA reads, each 16 codes padded to 16 bytes: tensor-map type
-//              16U4_ALIGN16B); all 32 lanes copy the unit's scale words (cp.async) into the stage, in
-//              the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM: byte (l * 16 + c * 4 + j) =
-//              scale of row 32 c + l for the K/32 sub-block j
+//   warp 0     producer: lane 0 issues every copy of a stage on the copy engine: the TMA boxes (the
+//              packed codes land in the 128-byte swizzled layout the MMA reads, each 16 codes padded
+//              to 16 bytes: tensor-map type 16U4_ALIGN16B) and bulk copies of the scales, which are
+//              kept in HBM in the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM (weights: per
+//              128 rows x 128 K a 512-byte block, byte l * 16 + c * 4 + j = scale of row 32 c + l for
+//              the K/32 sub-block j; activations: 16 bytes per row and 128-K block), so one barrier
+//              with one transaction count covers the whole stage and no proxy fence is needed
 //   warp 1     MMA issuer: per K block, tcgen05.cp of the scale blocks into a TMEM slot, then four
 //              block-scaled MMAs per weight matrix (K = 32 each, scale byte j selected in the
 //              instruction descriptor)
 //   warps 2-5  epilogue: TMEM reads of the item's accumulators, stream-K partials, SwiGLU (up) /
 //              outputs (down)
 #include "tc8_body.cuh"
+
+#include <algorithm>
 
 namespace stbl {
 
@@ -79,14 +83,6 @@ __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, const void *smem) {
     asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(plain_desc_32x16(smem)) : "memory");
 }
 
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // One CTA's share of the MXFP4 products: CTA `cta` of the `ncta` that run this body.
 template <bool UP>
 __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
@@ -95,7 +91,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;     // reduction length
     const int rows = UP ? p.I : p.H;  // output rows per matrix
-    const int nu = K / 256, kw = K / 32;  // 256-K units per item; scale bytes per row
+    const int nu = K / 256;               // 256-K units per item
     const int tiles = rows / 128;
     unsigned char *stages = smem;                                                   // [nst][A | B | SF]
     int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][16] by column
@@ -117,8 +113,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     }
     if (tid == 0) {
         abort_flag = 0;
-        // full: the producer lane's transaction arrival + one cp.async arrival per producer lane
-        for (int s = 0; s < nst; s++) mbar_init(&full[s], 1 + 32), mbar_init(&empty[s], 1);
+        // full: the producer lane's arrival with the stage's transaction bytes
+        for (int s = 0; s < nst; s++) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
         for (int a = 0; a < kT4Acc; a++) mbar_init(&acc_full[a], 1), mbar_init(&acc_empty[a], 128);
         mbar_init(mma_done, 1);
         fence_barrier_init();
@@ -150,60 +146,47 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     };
 
     if (warp == 0) {
-        // ---------------- producer (lane 0: TMA; all lanes: scale words) ----------------
-        int q = 0;
-        bool stop = false;
-        for (int it = lo; it < hi && !stop; it++) {
-            const int c = p.chunk_begin + it / tiles, tile = it % tiles;
-            const TcChunk ch = chunk_of(c);
-            const int brow = b_row(p, ch);
-            const int z = expert_slot(p, ch.e);
-            int ua, uz;
-            u_range(it, ua, uz);
-            // this lane's scale rows: rows 32 cc + lane (cc = 0..3) of each weight tile, B row `lane` (< 16)
-            const uint8_t *sa[S::nA][4];
-#pragma unroll
-            for (int m = 0; m < S::nA; m++)
-#pragma unroll
-                for (int cc = 0; cc < 4; cc++)
-                    sa[m][cc] = p.w_e8[m] + (size_t)z * p.w_e8_stride + (size_t)(tile * 128 + 32 * cc + lane) * kw;
-            const uint8_t *sb = p.act_e8 + (size_t)(brow + (lane & 15)) * kw;
-            for (int u = ua; u < uz; u++, q++) {
-                const int s = q % nst;
-                if (!mbar_wait(&empty[s], ((q / nst) & 1) ^ 1, &abort_flag)) {
-                    if (lane == 0) {
+        // ---------------- producer (lane 0: every copy of a stage, on the copy engine) ----------------
+        if (lane == 0) {
+            const int nkb = K / 128;
+            int q = 0;
+            bool stop = false;
+            for (int it = lo; it < hi && !stop; it++) {
+                const int c = p.chunk_begin + it / tiles, tile = it % tiles;
+                const TcChunk ch = chunk_of(c);
+                const int brow = b_row(p, ch);
+                const int z = expert_slot(p, ch.e);
+                int ua, uz;
+                u_range(it, ua, uz);
+                for (int u = ua; u < uz; u++, q++) {
+                    const int s = q % nst;
+                    if (!mbar_wait(&empty[s], ((q / nst) & 1) ^ 1, &abort_flag)) {
                         abort_flag = 1;
                         atomicOr(p.status, kErrWaitTimeout);
+                        stop = true;
+                        break;
                     }
-                    stop = true;
-                }
-                if (__any_sync(0xffffffffu, stop)) {
-                    stop = true;
-                    break;
-                }
-                unsigned char *a = stages + (size_t)s * S::stage;
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], S::tx);
+                    unsigned char *a = stages + (size_t)s * S::stage;
+                    unsigned char *sf = a + S::A + S::B;
+                    mbar_arrive_expect_tx(&full[s], S::tx + S::nA * kT4Kb * 512 + kT4Kb * kTcN * 16);
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
                         tma_load_4d(a + m * kT4Kb * kT4ATile, &maps.w[m], 0, tile * 128, kT4Kb * u, z, &full[s]);
                     tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
-                }
-                uint32_t *sf = reinterpret_cast<uint32_t *>(a + S::A + S::B);
-#pragma unroll
-                for (int g = 0; g < kT4Kb; g++) {
-                    const int kb = kT4Kb * u + g;
+                    // scales: the unit's two 512-byte weight-scale blocks per matrix are adjacent; the
+                    // activation scales are the chunk's 16 rows of 16 bytes per K block
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
+                        bulk_g2s(sf + m * kT4Kb * 512,
+                                 p.sf_a[m] + (size_t)z * p.sf_a_stride + ((size_t)tile * nkb + kT4Kb * u) * 512, kT4Kb * 512,
+                                 &full[s]);
 #pragma unroll
-                        for (int cc = 0; cc < 4; cc++) cp_async4(sf + (m * kT4Kb + g) * 128 + lane * 4 + cc, sa[m][cc] + kb * 4);
-                    if (lane < 16) cp_async4(sf + (S::nA * kT4Kb + g) * 128 + lane * 4, sb + kb * 4);
+                    for (int g = 0; g < kT4Kb; g++)
+                        bulk_g2s(sf + (S::nA * kT4Kb + g) * 512,
+                                 p.act_e8 + ((size_t)(kT4Kb * u + g) * p.act_e8_rows + brow) * 16, kTcN * 16, &full[s]);
                 }
-                cp_async_arrive(&full[s]);
             }
-        }
-        // drain: every issued copy must land before the CTA may exit
-        if (lane == 0)
+            // drain: every issued copy must land before the CTA may exit
             for (int j = max(0, q - nst); j < q; j++) {
                 const uint64_t t0 = global_ns();
                 while (!mbar_try_wait(&full[j % nst], (j / nst) & 1))
@@ -212,7 +195,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                         break;
                     }
             }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
@@ -233,7 +216,6 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                         stop = true;
                         break;
                     }
-                    fence_proxy_async_smem();  // scale words arrived through cp.async
                     tc_fence_after();
                     const unsigned char *a = stages + (size_t)s * S::stage;
                     const unsigned char *sfs = a + S::A + S::B;
@@ -393,7 +375,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     amax = fmaxf(amax, 1e-4f);
                     const float s = pow2_ceil(amax * (1.0f / 448.0f));
                     p.hq[(size_t)dst * p.I + r] = e4m3_code(fminf(fmaxf(hv / s, -448.f), 448.f));
-                    if (lane == 0) p.he8[(size_t)dst * (p.I / 32) + r / 32] = (uint8_t)(__float_as_uint(s) >> 23);
+                    if (lane == 0) p.he8[((size_t)tile * p.he8_rows + dst) * 16 + (warp & 3)] = (uint8_t)(__float_as_uint(s) >> 23);
                 }
             } else {
 #pragma unroll
@@ -445,6 +427,33 @@ const void *expert_tc4_kernel_ptr(bool up) {
 int expert_tc4_smem_bytes(bool up, int nst) {
     const int stage = up ? T4<true>::stage : T4<false>::stage;
     return nst * stage + 4 * (4 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
+}
+
+// e8m0 weight scales [rows][K/32] of slots [z0, z0 + nz) (slot z at src + z * src_stride) into the
+// scale-block layout the expert kernel copies: per slot [rows/128][K/128][512 B], byte l*16 + c*4 + j =
+// scale of row 32c + l, 32-block j (slot z at dst + z * dst_stride).  One thread per 4-byte word.
+__global__ void __launch_bounds__(256) sf_repack_kernel(const uint8_t *src, long long src_stride, uint8_t *dst,
+                                                        long long dst_stride, int rows, int K, int z0, int nz) {
+    const int nkb = K / 128;
+    const long long per_slot = (long long)rows * nkb;  // words
+    const long long total = per_slot * nz;
+    for (long long w = (long long)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (long long)gridDim.x * blockDim.x) {
+        const int z = z0 + (int)(w / per_slot);
+        const long long r = w % per_slot;
+        const int blk = (int)(r >> 7), i = (int)(r & 127);
+        const int tile = blk / nkb, kb = blk % nkb, l = i >> 2, c = i & 3;
+        const int row = tile * 128 + 32 * c + l;
+        const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(src + (size_t)z * src_stride + (size_t)row * (K / 32) + kb * 4));
+        *reinterpret_cast<uint32_t *>(dst + (size_t)z * dst_stride + (size_t)r * 4) = v;
+    }
+}
+
+cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *dst, long long dst_stride, int rows, int K,
+                             int z0, int nz, cudaStream_t st) {
+    const long long total = (long long)rows * (K / 128) * nz;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+    sf_repack_kernel<<<blocks, 256, 0, st>>>(src, src_stride, dst, dst_stride, rows, K, z0, nz);
+    return cudaGetLastError();
 }
 
 // floats per row of the stream-K partial buffer this kernel needs

@@ -56,7 +56,10 @@ struct RouterParams {
     uint8_t *xq_a;
     float *xs_a;
     int blk_a, pow2_a;
-    uint8_t *xe8_a;          // optional: scales of a as e8m0 bytes [T][H / 32] (per-32 power-of-two rule)
+    uint8_t *xe8_a;          // optional: scales of a as e8m0 bytes (per-32 power-of-two rule) in the
+                             // tensor cores' activation-scale layout [H/128][xe8_rows][16 B]: row t's
+                             // bytes 0..3 = the scales of its four 32-blocks of one 128-K block
+    int xe8_rows;
     uint8_t *xq_b;
     float *xs_b;
     int blk_b, pow2_b;

@@ -24,6 +24,8 @@ const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
 const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
 int expert_tc4_smem_bytes(bool up, int nst);
 int expert_tc4_partial_cols();
+cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *dst, long long dst_stride, int rows, int K,
+                             int z0, int nz, cudaStream_t st);
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
@@ -99,7 +101,12 @@ struct stbl_moe {
     bool routed_fp4 = false;          // routed experts MXFP4, on the block-scaled tensor-core kernels
     TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
     int tc4_nst_up = 0, tc4_nst_down = 0, tc4_nst8_up = 0, tc4_nst8_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
-    uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32)
+    uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32), [K/128][rows][16 B]
+    int Tpad = 0, pos_rows = 0;       // rows of the token-ordered and position-ordered activation buffers
+    // MXFP4 weight scales in the scale-block layout: the layer's own copy (natural scales given), slot z
+    // of matrix m at sf_own + z * sf_own_stride + sf_own_off[m]
+    uint8_t *sf_own = nullptr;
+    long long sf_own_stride = 0, sf_own_off[3] = {0, 0, 0};
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
@@ -308,9 +315,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xs_a = carve<float>(p, (size_t)Tpad * (H / 32));
         m->xq_b = carve<uint8_t>(p, (size_t)Tpad * H);
         m->xs_b = carve<float>(p, (size_t)Tpad * (H / 32));
-        m->xe8_a = carve<uint8_t>(p, (size_t)Tpad * (H / 32));
-        m->xe8_pos = carve<uint8_t>(p, (size_t)(npos + 16) * (H / 32));
-        m->he8 = carve<uint8_t>(p, (size_t)(npos + 16) * (I / 32));
+        m->xe8_a = carve<uint8_t>(p, (size_t)(H / 128) * Tpad * 16);
+        m->xe8_pos = carve<uint8_t>(p, (size_t)(H / 128) * (npos + 16) * 16);
+        m->he8 = carve<uint8_t>(p, (size_t)(I / 128) * (npos + 16) * 16);
         m->xq_pos = ep_n > 1 ? nullptr : carve<uint8_t>(p, (size_t)(npos + 16) * H);
         m->xs_pos = ep_n > 1 ? nullptr : carve<float>(p, (size_t)(npos + 16) * (H / 128));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
@@ -340,6 +347,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->eo = reinterpret_cast<uint16_t *>(m->ep_region + m->ep_L.eo);
     }
     CK(cudaMemcpy(m->slot, m->host_slot.data(), sizeof(int) * E, cudaMemcpyHostToDevice));
+    m->Tpad = Tpad, m->pos_rows = npos + 16;
 
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
@@ -352,6 +360,23 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H / 2,
             d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I / 2};
         const int ns = m->n_slots;
+        if (!d->routed_s_blocked) {
+            // the layer's own copy of every slot's scales in the scale-block layout
+            long long off = 0;
+            for (int mt = 0; mt < 3; mt++) {
+                m->sf_own_off[mt] = off;
+                off += ((long long)rows[mt] * (ks[mt] / 32) + 1023) & ~1023LL;
+            }
+            m->sf_own_stride = off;
+            CK(cudaMalloc(&m->sf_own, (size_t)ns * off));
+            for (int mt = 0; mt < 3; mt++)
+                CK(launch_sf_repack(static_cast<const uint8_t *>(d->routed_s[mt]), m->s_stride[mt], m->sf_own + m->sf_own_off[mt],
+                                    m->sf_own_stride, rows[mt], ks[mt], 0, ns, 0));
+            CK(cudaDeviceSynchronize());
+        } else {
+            for (int mt = 0; mt < 3; mt++)
+                if (m->s_stride[mt] & 511) throw std::runtime_error("block-layout MXFP4 scales need a slot stride multiple of 512");
+        }
         m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, ns, wst4[0]);
         m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, ns, wst4[1]);
         m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, ns, wst4[2]);
@@ -484,10 +509,12 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
                                                        : 4LL * ((rows + 127) / 128) * ((K + 127) / 128);
     p.w_scale_stride = sst / 4;
     if (m->routed_fp4) {
-        p.w_e8[0] = static_cast<const uint8_t *>(d.routed_s[mats[0]]);
-        p.w_e8[1] = static_cast<const uint8_t *>(d.routed_s[mats[1]]);
-        p.w_e8_stride = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]] : (long long)rows * (K / 32);
+        for (int i = 0; i < 2; i++)
+            p.sf_a[i] = m->sf_own ? m->sf_own + m->sf_own_off[mats[i]] : static_cast<const uint8_t *>(d.routed_s[mats[i]]);
+        p.sf_a_stride = m->sf_own ? m->sf_own_stride : m->s_stride[mats[0]];
         p.act_e8 = up ? (direct ? m->xe8_a : m->xe8_pos) : m->he8;
+        p.act_e8_rows = up && direct ? m->Tpad : m->pos_rows;
+        p.he8_rows = m->pos_rows;
     }
     p.h = m->h;
     p.hq = m->hq, p.he8 = m->he8;
@@ -535,7 +562,7 @@ void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st)
 
 void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
     GatherParams g{m->perm, T, m->K, m->H, m->has_shared, m->xq_a, m->xs_a, m->H / 32, m->xq_pos, m->xs_pos, nullptr, nullptr};
-    if (m->routed_fp4) g.xe8 = m->xe8_a, g.xe8_pos = m->xe8_pos;  // routed positions only
+    if (m->routed_fp4) g.xe8 = m->xe8_a, g.xe8_pos = m->xe8_pos, g.xe8_rows = m->Tpad, g.xe8_pos_rows = m->pos_rows;  // routed positions only
     void *args[] = {&g};
     const int rows = T * m->K + (m->has_shared && !m->routed_fp4 ? T : 0);
     launch_pdl(gather_kernel_ptr(), dim3(rows), dim3(256), args, 0, st);
@@ -585,6 +612,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
     r.xe8_a = m->routed_fp4 ? m->xe8_a : nullptr;
+    r.xe8_rows = m->Tpad;
     r.nt_routed = 16;
     r.nt_shared = 16;
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
@@ -877,6 +905,13 @@ int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *
                 throw std::runtime_error("the three matrices and scales of an expert must share one slot");
         m->host_slot[e] = (int)sl;
         if (sl != e) m->slots_moved = true;
+        if (m->sf_own) {
+            // the slot's MXFP4 scales as they are now, into the layer's scale-block copy
+            const int rows[3] = {m->I, m->I, m->H}, ks[3] = {m->H, m->H, m->I};
+            for (int mt = 0; mt < 3; mt++)
+                CK(launch_sf_repack(static_cast<const uint8_t *>(m->d.routed_s[mt]), m->s_stride[mt], m->sf_own + m->sf_own_off[mt],
+                                    m->sf_own_stride, rows[mt], ks[mt], (int)sl, 1, stream));
+        }
         CK(cudaMemcpyAsync(m->slot + e, &m->host_slot[e], sizeof(int), cudaMemcpyHostToDevice, stream));
         return 0;
     } catch (const std::exception &e2) {
@@ -936,6 +971,7 @@ void stbl_moe_destroy(stbl_moe *m) {
     for (auto &t : m->event_pool)
         for (auto e : t.ev) cudaEventDestroy(e);
     if (m->ws) cudaFree(m->ws);
+    if (m->sf_own) cudaFree(m->sf_own);
     for (int d = 0; d < m->ep_n; d++)
         if (d != m->ep_rank && m->ep_peer[d]) cudaIpcCloseMemHandle(m->ep_peer[d]);
     if (m->ep_region) cudaFree(m->ep_region);

@@ -44,10 +44,10 @@ __device__ __forceinline__ void top2_merge(uint32_t &a1, uint32_t &a2, uint32_t 
 
 // act_quant (ref/kernel.py:35-45) of 128 consecutive values of one token: lane l takes 4 of them.
 // blk 128: fp32 scale amax/448; blk 32: power-of-two scale per 32 (pow2 selects the rounding).
-// xe8 (optional): the scales as e8m0 bytes [T][H / 32] (per-32 power-of-two rule: the MXFP4 experts'
-// tensor-core kernel takes its activation scales in that form).
+// xe8 (optional): the scales as e8m0 bytes (per-32 power-of-two rule), laid out as the MXFP4 experts'
+// tensor-core kernel copies them: [H/128][xe8_rows][16 B], row t's bytes 0..3 for the 128-K block.
 __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq, float *xs, int blk, int pow2, int lane,
-                            uint8_t *xe8) {
+                            uint8_t *xe8, int xe8_rows) {
     const int k = 128 * g + 4 * lane;
     const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)t * H + k));
     const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
@@ -66,7 +66,7 @@ __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq,
     *reinterpret_cast<uint32_t *>(xq + (size_t)t * H + k) = codes;
     if ((k % blk) == 0) {
         xs[(size_t)t * (H / 32) + k / blk] = s;
-        if (xe8) xe8[(size_t)t * (H / 32) + k / 32] = (uint8_t)(__float_as_uint(s) >> 23);
+        if (xe8) xe8[((size_t)(k / 128) * xe8_rows + t) * 16 + (k / 32) % 4] = (uint8_t)(__float_as_uint(s) >> 23);
     }
 }
 
@@ -181,9 +181,10 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
         const int nwarps_grid = gridDim.x * (kLgThreads / 32), gwarp = blockIdx.x * (kLgThreads / 32) + warp;
         const int groups = p.T * (p.H / 128);
         for (int u = gwarp; u < groups; u += nwarps_grid) {
-            quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane, p.xe8_a);
+            quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane, p.xe8_a,
+                        p.xe8_rows);
             if (p.xq_b != p.xq_a)
-                quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane, nullptr);
+                quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane, nullptr, 0);
         }
     }
 

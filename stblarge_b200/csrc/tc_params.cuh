@@ -32,13 +32,18 @@ struct TcParams {
     long long w_scale_stride;  // floats per expert
     // MXFP4 routed experts (experts_tc4.cu): e8m0 weight scales [E][rows][K / 32] of the two
     // matrices (up) / one (down), bytes per expert; e8m0 activation scales [rows][K / 32] of the B rows
-    const uint8_t *w_e8[2];
-    long long w_e8_stride;
+    // MXFP4: weight scales in the tensor cores' scale-block layout (per matrix [rows/128][K/128][512 B]:
+    // byte l*16 + c*4 + j = scale of row 32c + l, 32-block j), slot z at sf_a[m] + z * sf_a_stride; the
+    // activation scales [K/128][act_e8_rows][16 B]
+    const uint8_t *sf_a[2];
+    long long sf_a_stride;
     const uint8_t *act_e8;
+    int act_e8_rows;
     const float *s_scale[2];   // shared expert block scales
     float swiglu_limit;        // > 0: SwiGLU clamps (stbl/kernels.cu:445-459)
     uint16_t *h;               // up out: [pos][I] bf16
-    uint8_t *hq, *he8;         // MXFP4 up out: h quantized for the down product, e4m3 [pos][I] + e8m0 [pos][I/32]
+    uint8_t *hq, *he8;         // MXFP4 up out: h quantized for the down product: e4m3 [pos][I], e8m0
+    int he8_rows;              // scales in the activation-scale layout [I/128][he8_rows][16 B]
     uint16_t *eo, *sh;         // down outputs: routed [T * topk][H] in (token, slot) order, shared [T][H]
     int has_shared;
     // rows [0, n_routed) are routed assignments, the shared expert's rows follow (row n_routed + token)
@@ -82,9 +87,11 @@ struct GatherParams {
     int xs_stride;
     uint8_t *xq_pos;
     float *xs_pos;             // [pos][H / 128]
-    // MXFP4 routed experts: e8m0 scales [T][H / 32] -> [pos][H / 32]; then only routed positions
+    // MXFP4 routed experts: e8m0 scales in the activation-scale layout [H/128][rows][16 B], token rows
+    // (xe8_rows) -> position rows (xe8_pos_rows); then only routed positions
     const uint8_t *xe8;
     uint8_t *xe8_pos;
+    int xe8_rows, xe8_pos_rows;
 };
 
 }  // namespace stbl

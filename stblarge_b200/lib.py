@@ -25,7 +25,7 @@ class MoEDesc(ctypes.Structure):
         ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
         ("max_tokens", I), ("router_w", P), ("router_bias", P), ("routed_w", P * 3), ("routed_s", P * 3),
         ("routed_w_stride", LL * 3), ("routed_s_stride", LL * 3), ("shared_w", P * 3), ("shared_s", P * 3),
-        ("n_slots", I),
+        ("n_slots", I), ("routed_s_blocked", I),
     ]
 
 
