@@ -121,7 +121,9 @@ int stbl_moe_forward_routed(stbl_moe *m, const void *x_bf16, int T, const int *i
  * different streams must not overlap (they share the cache state). */
 typedef struct stbl_cache stbl_cache;
 typedef struct stbl_cache_desc {
-    int n_layers, n_experts, slots;
+    int n_layers, n_experts;
+    int slots;               /* device slots; 0: as many as the free device memory holds after a headroom of
+                                max(4 GiB, 5 %), at most n_layers * n_experts (stbl_cache_info reports it) */
     int fmt;                 /* STBL_FMT_FP8_B128 or STBL_FMT_MXFP4 */
     int hidden, inter;       /* multiples of 512 */
     const void *host_w[3];
@@ -140,6 +142,8 @@ int stbl_cache_layer_desc(const stbl_cache *c, stbl_moe_desc *desc);
 /* Layer m (made from stbl_cache_layer_desc, single GPU) becomes layer `layer` of the cache.  Needs
  * slots >= max_tokens * topk (a call's experts must fit at once). */
 int stbl_moe_attach_cache(stbl_moe *m, stbl_cache *c, int layer);
+/* Slots of the cache and bytes per slot (one expert: codes and scales of its three matrices). */
+int stbl_cache_info(const stbl_cache *c, int *slots, uint64_t *slot_bytes);
 /* Counters since creation (waits for the device): routed experts found in the cache, experts copied
  * in, bytes copied.  The reference's stbl_stats(hits, misses). */
 int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint64_t *bytes);

@@ -63,6 +63,10 @@ class ExpertCache:
         if self.lib.stbl_cache_create(ctypes.byref(d), ctypes.byref(h), err, 512) != 0:
             raise RuntimeError("stbl_cache_create: " + err.value.decode())
         self.handle = h
+        n, b = L.I(), L.U64()
+        if self.lib.stbl_cache_info(self.handle, ctypes.byref(n), ctypes.byref(b)) != 0:
+            raise RuntimeError("stbl_cache_info failed")
+        self.slots, self.slot_bytes = n.value, b.value  # slots=0 asks the library to size the cache
 
     def layer_desc(self, desc):
         if self.lib.stbl_cache_layer_desc(self.handle, ctypes.byref(desc)) != 0:

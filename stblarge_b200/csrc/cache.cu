@@ -304,7 +304,7 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
     try {
         if (!d || !out) throw std::runtime_error("null argument");
         if (d->n_layers < 1 || d->n_experts < 1 || d->n_experts > 512) throw std::runtime_error("n_layers >= 1, n_experts in 1..512");
-        if (d->slots < 1 || d->slots > (1 << 20) - 1) throw std::runtime_error("slots must be in 1..2^20-1");
+        if (d->slots < 0 || d->slots > (1 << 20) - 1) throw std::runtime_error("slots must be in 0..2^20-1");
         if (d->fmt != STBL_FMT_FP8_B128 && d->fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad fmt");
         if (d->hidden <= 0 || d->inter <= 0 || d->hidden % 512 || d->inter % 512)
             throw std::runtime_error("hidden and inter must be multiples of 512");
@@ -336,6 +336,17 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
             c->host[q] = static_cast<const uint8_t *>(pa.devicePointer);
         }
         c->slot_bytes = off;
+        if (c->S == 0) {
+            // sized from the device's free memory (the reference sizes its cache from the host's available
+            // memory, stbl/model.cu:960-977): all of it but a headroom of max(4 GiB, 5 %), at most one slot
+            // per expert of the store
+            size_t free_b = 0, total_b = 0;
+            CK(cudaMemGetInfo(&free_b, &total_b));
+            const long long headroom = std::max<long long>(4LL << 30, (long long)(total_b / 20));
+            const long long room = (long long)free_b - headroom;
+            c->S = (int)std::min<long long>({room > 0 ? room / c->slot_bytes : 0, (long long)c->L * c->E, (1 << 20) - 1});
+            if (c->S < 1) throw std::runtime_error("not enough device memory for an expert cache slot");
+        }
         int sms = 0;
         CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->dev));
         c->copy_ctas = 2 * sms;
@@ -371,6 +382,13 @@ int stbl_cache_layer_desc(const stbl_cache *c, stbl_moe_desc *d) {
         d->routed_w_stride[q] = c->slot_bytes;
         d->routed_s_stride[q] = c->slot_bytes;
     }
+    return 0;
+}
+
+int stbl_cache_info(const stbl_cache *c, int *slots, uint64_t *slot_bytes) {
+    if (!c) return -1;
+    if (slots) *slots = c->S;
+    if (slot_bytes) *slot_bytes = (uint64_t)c->slot_bytes;
     return 0;
 }
 

@@ -54,6 +54,7 @@ SIGNATURES = {
     "stbl_cache_layer_desc": (I, [P, ctypes.POINTER(MoEDesc)]),
     "stbl_moe_attach_cache": (I, [P, P, I]),
     "stbl_cache_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "stbl_cache_info": (I, [P, ctypes.POINTER(I), ctypes.POINTER(U64)]),
     "stbl_cache_state": (I, [P, P, P]),
     "stbl_cache_destroy": (None, [P]),
     "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),

@@ -83,3 +83,29 @@ def test_forward_routed_matches_oracle(cfg):
     assert np.array_equal(layer.last_route()["idx"][0], np.arange(cfg.topk))
     assert layer.status() == 2
     layer.close()
+
+
+def test_cache_sized_from_free_memory():
+    # slots = 0: the library sizes the cache; a small store fits entirely (one slot per expert)
+    cfg, L = CFG1_FP4, 2
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, 0, store)
+    assert cache.slots == L * cfg.n_experts
+    assert cache.slot_bytes >= sum(t[0].numel() * t.element_size() for t in store["w"] + store["s"])
+    resident = synth.device_layer(cfg, seed_base=1000 + cfg.n_experts)
+    plain = MoELayer(cfg, resident, max_tokens=2)
+    cached = MoELayer(cfg, resident, max_tokens=2, cache=(cache, 1))
+    seen, routed = set(), 0
+    for call in range(3):
+        x = _x(cfg, 2, 700 + call)
+        assert torch.equal(cached(x).view(torch.int16), plain(x).view(torch.int16))
+        ids = set(int(e) for e in cached.last_route()["idx"].reshape(-1))
+        routed += len(ids)
+        seen |= ids
+    st = cache.stats()
+    # every slot is free or holds its expert for good: each distinct expert misses exactly once
+    assert st["misses"] == len(seen) and st["hits"] == routed - len(seen)
+    for layer in (cached, plain):
+        assert layer.status() == 0
+        layer.close()
+    cache.close()
