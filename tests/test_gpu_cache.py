@@ -109,3 +109,29 @@ def test_cache_sized_from_free_memory():
         assert layer.status() == 0
         layer.close()
     cache.close()
+
+
+@pytest.mark.parametrize("cfg", [CFG1, CFG1_FP4], ids=["fp8", "mxfp4"])
+def test_cached_layer_with_forced_routes(cfg):
+    # the streamed-decode combination: routes given, experts brought in by the cache
+    L, S, E = 2, 6, cfg.n_experts
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, S, store)
+    resident = [synth.device_layer(cfg, seed_base=1000 + l * E) for l in range(L)]
+    plain = [MoELayer(cfg, resident[l], max_tokens=1) for l in range(L)]
+    cached = [MoELayer(cfg, resident[l], max_tokens=1, cache=(cache, l)) for l in range(L)]
+    lru = O.LruExpertCache(S)
+    rng = np.random.default_rng(21)
+    for call in range(12):
+        l = call % L
+        idx = torch.from_numpy(rng.permutation(E)[:cfg.topk].astype(np.int32).reshape(1, -1)).cuda()
+        x = _x(cfg, 1, 800 + call)
+        y_plain, y = plain[l].forward_routed(x, idx), cached[l].forward_routed(x, idx)
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), y_plain.view(torch.int16)), f"call {call}"
+        lru.call(l, idx.cpu().numpy())
+        assert (cache.stats()["hits"], cache.stats()["misses"]) == (lru.hits, lru.misses)
+    for layer in cached + plain:
+        assert layer.status() == 0
+        layer.close()
+    cache.close()

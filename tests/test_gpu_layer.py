@@ -140,14 +140,14 @@ def test_planted_router_ties(small_layers):
 @pytest.fixture(scope="module")
 def cfg2_layer():
     dev = synth.device_layer(CFG2)
-    layer = MoELayer(CFG2, dev, max_tokens=16)
+    layer = MoELayer(CFG2, dev, max_tokens=64)
     yield dev, layer
     layer.close()
     del dev
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("T", [1, 4, 16])
+@pytest.mark.parametrize("T", [1, 4, 16, 64])  # 64: gathered activations, experts with several chunks
 def test_full_size_fp8_layer(cfg2_layer, T):
     dev, layer = cfg2_layer
     run_and_check(CFG2, layer, dev, None, synth.make_x(CFG2.hidden, T, seed=200 + T))
