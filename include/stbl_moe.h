@@ -27,7 +27,12 @@ extern "C" {
 enum {
     STBL_FMT_NONE = 0,
     STBL_FMT_FP8_B128 = 1, /* e4m3 codes [rows][k]; fp32 scales [ceil(rows/128)][ceil(k/128)] */
-    STBL_FMT_MXFP4 = 2     /* e2m1 codes [rows][k/2], even k in the low nibble; e8m0 scales [rows][k/32] */
+    STBL_FMT_MXFP4 = 2,    /* e2m1 codes [rows][k/2], even k in the low nibble; e8m0 scales [rows][k/32] */
+    STBL_FMT_FP8_E8M0 = 3  /* e4m3 codes [rows][k]; e8m0 scales [ceil(rows/32)][k/32], one per 32x32 block: the
+                              reference engine's FP8 format (stbl/kernels.cu:98-132, tools/convert_official.py:74-81).
+                              Routed (with an FP8-e8m0 or no shared expert, or with MXFP4 routed experts) and
+                              shared (with MXFP4 or FP8-e8m0 routed experts); activations are quantized per 32
+                              with power-of-two scales (stbl/kernels.cu:56-63) */
 };
 
 /* router score functions */
@@ -150,6 +155,13 @@ int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint
 /* Residency (waits for the device): map [n_layers][n_experts] slot or -1; owner [slots] l * E + e or -1. */
 int stbl_cache_state(const stbl_cache *c, int *map, int *owner);
 void stbl_cache_destroy(stbl_cache *c);
+
+/* The reference engine's MXFP4 storage, GGUF blocks of 17 bytes per 32 values (the e8m0 scale, then 16
+ * bytes holding values 0..15 in the low nibbles and 16..31 in the high nibbles; stbl/kernels.cu:134-141,
+ * tools/convert_official.py:187-201), into the layer's STBL_FMT_MXFP4 layout: codes [rows][k/2] (even
+ * index in the low nibble) and scales [rows][k/32].  Device buffers, enqueued on `stream`; k a multiple of
+ * 32.  Lossless: the reference's weights load into a layer this way, once. */
+int stbl_mxfp4_from_gguf(const void *blocks, int rows, int k, void *codes, void *scales, cudaStream_t stream);
 
 /* Device status bits raised by kernels since the last call of this function (waits for the
  * device): 1 a wait timed out, 2 a dispatch entry was out of range, 4 copies were still in flight

@@ -169,7 +169,79 @@ void orc_quant_mxfp4(const float *w, int rows, int k, uint8_t *packed, uint8_t *
         }
 }
 
+/* FP8 weights with e8m0 scales per 32x32 block (the reference engine's format, kernels.cu:98-132,
+ * tools/convert_official.py:74-81).  Synthetic weights only: the reference copies the checkpoint's
+ * scales byte for byte; here a block's scale follows act_quant's power-of-two rule (ref/kernel.py:35-45
+ * with scale_fmt): amax clamp_min(1e-4), s = 2^ceil(log2(amax / 448)), q = e4m3(clamp(w / s, +-448)). */
+void orc_quant_fp8_e8m0(const float *w, int rows, int k, uint8_t *codes, uint8_t *scales) {
+    const int rb = (rows + 31) / 32, kb = k / 32;
+    for (int bi = 0; bi < rb; bi++)
+        for (int bj = 0; bj < kb; bj++) {
+            float amax = 0.f;
+            for (int r = bi * 32; r < rows && r < bi * 32 + 32; r++)
+                for (int c = bj * 32; c < bj * 32 + 32; c++) amax = fmaxf(amax, fabsf(w[(size_t)r * k + c]));
+            amax = fmaxf(amax, 1e-4f);
+            const float s = orc_pow2_ceil(amax * kInv448);
+            for (int r = bi * 32; r < rows && r < bi * 32 + 32; r++)
+                for (int c = bj * 32; c < bj * 32 + 32; c++) {
+                    float q = w[(size_t)r * k + c] / s;
+                    q = fminf(fmaxf(q, -448.f), 448.f);
+                    codes[(size_t)r * k + c] = orc_e4m3_encode(q);
+                }
+            scales[(size_t)bi * kb + bj] = (uint8_t)(f2u(s) >> 23);
+        }
+}
+
+/* GGUF MXFP4 block (kernels.cu:134-141, tools/convert_official.py:187-201): the scale byte, then 16
+ * bytes with values 0..15 of the block in the low nibbles and 16..31 in the high nibbles. */
+void orc_mxfp4_to_gguf(const uint8_t *codes, const uint8_t *scales, int rows, int k, uint8_t *blocks) {
+    for (int r = 0; r < rows; r++)
+        for (int b = 0; b < k / 32; b++) {
+            const uint8_t *src = codes + (size_t)r * (k / 2) + (size_t)b * 16;
+            uint8_t *dst = blocks + ((size_t)r * (k / 32) + b) * 17;
+            uint8_t v[32];
+            for (int i = 0; i < 16; i++) v[2 * i] = src[i] & 15, v[2 * i + 1] = src[i] >> 4;
+            dst[0] = scales[(size_t)r * (k / 32) + b];
+            for (int i = 0; i < 16; i++) dst[1 + i] = (uint8_t)(v[i] | (v[16 + i] << 4));
+        }
+}
+
+void orc_mxfp4_from_gguf(const uint8_t *blocks, int rows, int k, uint8_t *codes, uint8_t *scales) {
+    for (int r = 0; r < rows; r++)
+        for (int b = 0; b < k / 32; b++) {
+            const uint8_t *src = blocks + ((size_t)r * (k / 32) + b) * 17;
+            uint8_t v[32];
+            for (int i = 0; i < 16; i++) v[i] = src[1 + i] & 15, v[16 + i] = src[1 + i] >> 4;
+            scales[(size_t)r * (k / 32) + b] = src[0];
+            for (int i = 0; i < 16; i++) codes[(size_t)r * (k / 2) + (size_t)b * 16 + i] = (uint8_t)(v[2 * i] | (v[2 * i + 1] << 4));
+        }
+}
+
 /* ---- GEMVs ------------------------------------------------------------------------------------ */
+
+/* FP8 e4m3 with 32x32 e8m0 block scales: B = code * 2^(e8m0 - 127), dequantized products accumulated
+ * in fp32, k ascending (the 32-block e8m0 variant of fp8_gemm, ref/kernel.py:85-91). */
+void orc_gemv_fp8_e8m0(const uint8_t *w, const uint8_t *ws, int rows, int k, const uint8_t *xc, const float *xs,
+                       int act_block, int n_tok, float *y) {
+    e4m3_init();
+    const int na = k / act_block;
+    float *A = (float *)malloc(sizeof(float) * (size_t)n_tok * k);
+    for (int t = 0; t < n_tok; t++)
+        for (int c = 0; c < k; c++) A[(size_t)t * k + c] = g_e4m3[xc[(size_t)t * k + c]] * xs[(size_t)t * na + c / act_block];
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++) {
+        const uint8_t *wr = w + (size_t)r * k;
+        const uint8_t *sr = ws + (size_t)(r / 32) * (k / 32);
+        float acc[64];
+        for (int t = 0; t < n_tok; t++) acc[t] = 0.f;
+        for (int c = 0; c < k; c++) {
+            const float B = g_e4m3[wr[c]] * u2f((uint32_t)sr[c / 32] << 23);
+            for (int t = 0; t < n_tok; t++) acc[t] = acc[t] + A[(size_t)t * k + c] * B;
+        }
+        for (int t = 0; t < n_tok; t++) y[(size_t)t * rows + r] = acc[t];
+    }
+    free(A);
+}
 
 /* fp8_gemm (ref/kernel.py:85-91): A = code * a_s and B = code * b_s are each one fp32 product; the
  * dot product is accumulated in fp32, k ascending. */
@@ -348,6 +420,8 @@ static void gemv_fmt(int fmt, const uint8_t *w, const void *s, int rows, int k, 
                      int n_tok, float *y) {
     if (fmt == ORC_FMT_FP8_B128)
         orc_gemv_fp8_b128(w, (const float *)s, rows, k, xc, xs, act_block_of(fmt), n_tok, y);
+    else if (fmt == ORC_FMT_FP8_E8M0)
+        orc_gemv_fp8_e8m0(w, (const uint8_t *)s, rows, k, xc, xs, act_block_of(fmt), n_tok, y);
     else
         orc_gemv_mxfp4(w, (const uint8_t *)s, rows, k, xc, xs, act_block_of(fmt), n_tok, y);
 }

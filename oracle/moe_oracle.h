@@ -22,6 +22,7 @@ enum {
     ORC_FMT_NONE = 0,
     ORC_FMT_FP8_B128 = 1,    /* e4m3 codes [rows][k], fp32 scales [ceil(rows/128)][ceil(k/128)] */
     ORC_FMT_MXFP4 = 2,       /* e2m1 codes [rows][k/2] low nibble first, e8m0 scales [rows][k/32] */
+    ORC_FMT_FP8_E8M0 = 3,    /* e4m3 codes [rows][k], e8m0 scales [ceil(rows/32)][k/32] (32x32 blocks) */
 };
 
 enum { ORC_SCORE_SIGMOID = 0, ORC_SCORE_SQRT_SOFTPLUS = 1 };
@@ -46,6 +47,12 @@ void orc_act_quant(const float *x, int rows, int k, int block, int pow2, uint8_t
 void orc_quant_fp8_b128(const float *w, int rows, int k, uint8_t *codes, float *scales);
 /* MXFP4 weight quantization, fp4_act_quant E8M0 branch: ref/kernel.py:55-72. */
 void orc_quant_mxfp4(const float *w, int rows, int k, uint8_t *packed, uint8_t *scales);
+void orc_quant_fp8_e8m0(const float *w, int rows, int k, uint8_t *codes, uint8_t *scales);
+void orc_gemv_fp8_e8m0(const uint8_t *w, const uint8_t *ws, int rows, int k, const uint8_t *xc, const float *xs,
+                       int act_block, int n_tok, float *y);
+/* MXFP4 in the official layout -> the reference engine's GGUF 17-byte blocks, and back */
+void orc_mxfp4_to_gguf(const uint8_t *codes, const uint8_t *scales, int rows, int k, uint8_t *blocks);
+void orc_mxfp4_from_gguf(const uint8_t *blocks, int rows, int k, uint8_t *codes, uint8_t *scales);
 
 /* ---- GEMVs over several tokens (fp8_gemm / fp4_gemm numerics, ref/kernel.py:85-102) ----------- */
 /* y[t][r] = sum_k (code_x*sx) * (code_w*sw), fp32, no output rounding. xs: per-(token, act block). */

@@ -124,12 +124,48 @@ def quant_mxfp4(w):
     return packed, scales
 
 
+def quant_fp8_e8m0(w):
+    w = _f32(w)
+    rows, k = w.shape
+    codes = np.empty((rows, k), np.uint8)
+    scales = np.empty(((rows + 31) // 32, k // 32), np.uint8)
+    lib().orc_quant_fp8_e8m0(ptr(w), I(rows), I(k), ptr(codes), ptr(scales))
+    return codes, scales
+
+
+def mxfp4_to_gguf(codes, scales):
+    """Official MXFP4 (codes [rows][k/2], e8m0 [rows][k/32]) -> GGUF 17-byte blocks [rows][k/32][17]."""
+    codes, scales = np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint8)
+    rows, k = codes.shape[0], codes.shape[1] * 2
+    blocks = np.empty((rows, k // 32, 17), np.uint8)
+    lib().orc_mxfp4_to_gguf(ptr(codes), ptr(scales), I(rows), I(k), ptr(blocks))
+    return blocks
+
+
+def mxfp4_from_gguf(blocks):
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    rows, k = blocks.shape[0], blocks.shape[1] * 32
+    codes = np.empty((rows, k // 2), np.uint8)
+    scales = np.empty((rows, k // 32), np.uint8)
+    lib().orc_mxfp4_from_gguf(ptr(blocks), I(rows), I(k), ptr(codes), ptr(scales))
+    return codes, scales
+
+
 def gemv_fp8_b128(w, ws, xc, xs, act_block):
     rows, k = w.shape
     n = xc.shape[0]
     y = np.empty((n, rows), np.float32)
     lib().orc_gemv_fp8_b128(ptr(np.ascontiguousarray(w)), ptr(_f32(ws)), I(rows), I(k), ptr(np.ascontiguousarray(xc)),
                             ptr(_f32(xs)), I(act_block), I(n), ptr(y))
+    return y
+
+
+def gemv_fp8_e8m0(w, ws, xc, xs, act_block):
+    rows, k = w.shape
+    n = xc.shape[0]
+    y = np.empty((n, rows), np.float32)
+    lib().orc_gemv_fp8_e8m0(ptr(np.ascontiguousarray(w)), ptr(np.ascontiguousarray(ws)), I(rows), I(k),
+                            ptr(np.ascontiguousarray(xc)), ptr(_f32(xs)), I(act_block), I(n), ptr(y))
     return y
 
 

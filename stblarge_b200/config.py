@@ -12,6 +12,7 @@ from dataclasses import asdict, dataclass, replace
 FMT_NONE = 0
 FMT_FP8_B128 = 1  # e4m3 codes [rows][k], fp32 scales [ceil(rows/128)][ceil(k/128)]
 FMT_MXFP4 = 2     # e2m1 codes [rows][k/2] (even index in the low nibble), e8m0 scales [rows][k/32]
+FMT_FP8_E8M0 = 3  # e4m3 codes [rows][k], e8m0 scales [ceil(rows/32)][k/32]: the reference engine's FP8
 
 # router score functions
 SCORE_SIGMOID = 0          # DeepSeek-V3: sigmoid, group-limited top-k
@@ -51,6 +52,9 @@ class MoEConfig:
         elif fmt == FMT_MXFP4:
             def mat(r, k):
                 return r * k // 2 + r * (k // 32)
+        elif fmt == FMT_FP8_E8M0:
+            def mat(r, k):
+                return r * k + ((r + 31) // 32) * (k // 32)
         else:
             return 0
         return 2 * mat(I, H) + mat(H, I)
@@ -60,5 +64,12 @@ CFG1 = MoEConfig("cfg1", hidden=1024, inter=512, n_experts=16, topk=4, n_groups=
 CFG1_FP4 = replace(CFG1, name="cfg1_fp4", routed_fmt=FMT_MXFP4)
 CFG2 = MoEConfig("cfg2", hidden=7168, inter=2048, n_experts=256, topk=8, n_groups=8, topk_groups=4)
 CFG3 = replace(CFG2, name="cfg3", routed_fmt=FMT_MXFP4, zipf_s=1.0)
+# the reference engine's own formats and routing: MXFP4 routed experts, FP8 shared expert with e8m0
+# 32x32 block scales, per-32 power-of-two activation scales, sqrt(softplus) scores without group limit
+CFG1_REF = replace(CFG1, name="cfg1_ref", routed_fmt=FMT_MXFP4, shared_fmt=FMT_FP8_E8M0, score_fn=SCORE_SQRT_SOFTPLUS,
+                   n_groups=1, topk_groups=1)
+CFG1_E8 = replace(CFG1, name="cfg1_e8", routed_fmt=FMT_FP8_E8M0, shared_fmt=FMT_FP8_E8M0)
+CFG3_REF = replace(CFG2, name="cfg3_ref", routed_fmt=FMT_MXFP4, shared_fmt=FMT_FP8_E8M0, score_fn=SCORE_SQRT_SOFTPLUS,
+                   n_groups=1, topk_groups=1)
 
-PRESETS = {c.name: c for c in (CFG1, CFG1_FP4, CFG2, CFG3)}
+PRESETS = {c.name: c for c in (CFG1, CFG1_FP4, CFG2, CFG3, CFG1_REF, CFG1_E8, CFG3_REF)}

@@ -50,7 +50,6 @@ struct T4 {
     static constexpr int B = kT4Kb * kT4BTile;             // [kb][16 rows][128 B]
     static constexpr int SF = (nA + 1) * kT4Kb * 512;      // [m | B][kb][512 B]
     static constexpr int stage = A + B + SF;               // up 71 KB, down 38 KB
-    static constexpr int tx = nA * kT4Kb * 128 * 64 + B;   // TMA bytes: packed codes + activations
     static constexpr int NV = nA * kTcN;                   // accumulator columns per item
 };
 static_assert(T4<true>::stage % 1024 == 0 && T4<false>::stage % 1024 == 0, "stages must keep 1 KB alignment");
@@ -61,11 +60,11 @@ __device__ __forceinline__ uint64_t plain_desc_32x16(const void *p) {
     return ((a & 0x3FFFFull) >> 4) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (7-9 = 5), B e4m3 (10-12 = 0),
-// K-major, N >> 3 at 17-22, scale type ue8m0 (bit 23), M >> 4 at 24-28; the scale byte of the K/32
+// Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (7-9 = 5) or e4m3 (0), B e4m3 (10-12 =
+// 0), K-major, N >> 3 at 17-22, scale type ue8m0 (bit 23), M >> 4 at 24-28; the scale byte of the K/32
 // sub-block j for B at bits 4-5 and for A at bits 29-30.
-__device__ __forceinline__ uint32_t idesc_mx(int j) {
-    return ((uint32_t)j << 4) | (5u << 7) | ((uint32_t)(kTcN >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+__device__ __forceinline__ uint32_t idesc_mx(int j, bool a8) {
+    return ((uint32_t)j << 4) | ((a8 ? 0u : 5u) << 7) | ((uint32_t)(kTcN >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
            ((uint32_t)j << 29);
 }
 
@@ -155,7 +154,12 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 const int c = p.chunk_begin + it / tiles, tile = it % tiles;
                 const TcChunk ch = chunk_of(c);
                 const int brow = b_row(p, ch);
-                const int z = expert_slot(p, ch.e);
+                // routed experts from their slots; the shared expert (its own maps and scale blocks) when the
+                // layer's shared expert is in a block-scaled format too
+                const bool shared = ch.e == p.E;
+                const int z = shared ? 0 : expert_slot(p, ch.e);
+                const bool a8 = shared ? p.s_a8 : p.w_a8;
+                const uint32_t a_bytes = S::nA * kT4Kb * 128 * (a8 ? 128 : 64);
                 int ua, uz;
                 u_range(it, ua, uz);
                 for (int u = ua; u < uz; u++, q++) {
@@ -168,17 +172,20 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     }
                     unsigned char *a = stages + (size_t)s * S::stage;
                     unsigned char *sf = a + S::A + S::B;
-                    mbar_arrive_expect_tx(&full[s], S::tx + S::nA * kT4Kb * 512 + kT4Kb * kTcN * 16);
+                    mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * kTcN * 16);
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
-                        tma_load_4d(a + m * kT4Kb * kT4ATile, &maps.w[m], 0, tile * 128, kT4Kb * u, z, &full[s]);
+                        tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile * 128, kT4Kb * u, z,
+                                    &full[s]);
                     tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
                     // scales: the unit's two 512-byte weight-scale blocks per matrix are adjacent; the
                     // activation scales are the chunk's 16 rows of 16 bytes per K block
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
                         bulk_g2s(sf + m * kT4Kb * 512,
-                                 p.sf_a[m] + (size_t)z * p.sf_a_stride + ((size_t)tile * nkb + kT4Kb * u) * 512, kT4Kb * 512,
+                                 (shared ? p.sf_s[m] : p.sf_a[m] + (size_t)z * p.sf_a_stride) +
+                                     ((size_t)tile * nkb + kT4Kb * u) * 512,
+                                 kT4Kb * 512,
                                  &full[s]);
 #pragma unroll
                     for (int g = 0; g < kT4Kb; g++)
@@ -210,6 +217,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 int ua, uz;
                 u_range(it, ua, uz);
                 const uint32_t d = tmem + (uint32_t)(acc * S::NV);
+                const TcChunk ch = chunk_of(p.chunk_begin + it / tiles);
+                const bool a8 = ch.e == p.E ? p.s_a8 : p.w_a8;
                 for (int u = ua; u < uz; u++, q++) {
                     const int s = q % nst;
                     if (!mbar_wait(&full[s], (q / nst) & 1, &abort_flag)) {
@@ -230,7 +239,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
 #pragma unroll
                             for (int j = 0; j < 4; j++)
                                 umma_mx(d + m * kTcN, sw128_desc(a + (m * kT4Kb + g) * kT4ATile + 32 * j),
-                                        sw128_desc(a + S::A + g * kT4BTile + 32 * j), idesc_mx(j), (u > ua || g > 0 || j > 0),
+                                        sw128_desc(a + S::A + g * kT4BTile + 32 * j), idesc_mx(j, a8), (u > ua || g > 0 || j > 0),
                                         sf + 4 * m, sf + 8);
                     }
                     umma_commit(&empty[s]);
@@ -264,13 +273,17 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
             pval = et < ch.n;
             if (pval) {
                 const int pos = ch.pos0 + et;
-                const int a = __ldg(p.perm + pos);
                 pcol = et, pdst = pos, pwt = 1.f;
-                if (UP) {
-                    pwt = __ldg(p.wts + a);
-                    if (p.b_direct) pcol = a / p.topk;  // x read by token: column = token
+                if (ch.e == p.E) {
+                    if (!UP) pdst = pos - p.n_routed;  // shared expert: its output row is the token's
                 } else {
-                    pdst = a;  // eo row
+                    const int a = __ldg(p.perm + pos);
+                    if (UP) {
+                        pwt = __ldg(p.wts + a);
+                        if (p.b_direct) pcol = a / p.topk;  // x read by token: column = token
+                    } else {
+                        pdst = a;  // eo row
+                    }
                 }
             }
         };
@@ -380,7 +393,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
             } else {
 #pragma unroll
                 for (int j = 0; j < kTcN; j++)
-                    if (j < ch.n) p.eo[(size_t)cdst[j] * p.H + r] = f32_to_bf16_bits(va[j]);
+                    if (j < ch.n) (ch.e == p.E ? p.sh : p.eo)[(size_t)cdst[j] * p.H + r] = f32_to_bf16_bits(va[j]);
             }
             if (it + 1 < hi) park(buf ^ 1);
         }
@@ -429,11 +442,13 @@ int expert_tc4_smem_bytes(bool up, int nst) {
     return nst * stage + 4 * (4 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
 }
 
-// e8m0 weight scales [rows][K/32] of slots [z0, z0 + nz) (slot z at src + z * src_stride) into the
-// scale-block layout the expert kernel copies: per slot [rows/128][K/128][512 B], byte l*16 + c*4 + j =
-// scale of row 32c + l, 32-block j (slot z at dst + z * dst_stride).  One thread per 4-byte word.
+// e8m0 weight scales of slots [z0, z0 + nz) (slot z at src + z * src_stride) into the scale-block
+// layout the expert kernel copies: per slot [rows/128][K/128][512 B], byte l*16 + c*4 + j = scale of
+// row 32c + l, 32-block j (slot z at dst + z * dst_stride).  Source rows hold K/32 bytes and cover
+// rps weight rows each: 1 for MXFP4 ([rows][K/32]), 32 for FP8 with 32x32 blocks ([rows/32][K/32]).
+// One thread per 4-byte word.
 __global__ void __launch_bounds__(256) sf_repack_kernel(const uint8_t *src, long long src_stride, uint8_t *dst,
-                                                        long long dst_stride, int rows, int K, int z0, int nz) {
+                                                        long long dst_stride, int rows, int K, int z0, int nz, int rps) {
     const int nkb = K / 128;
     const long long per_slot = (long long)rows * nkb;  // words
     const long long total = per_slot * nz;
@@ -443,16 +458,16 @@ __global__ void __launch_bounds__(256) sf_repack_kernel(const uint8_t *src, long
         const int blk = (int)(r >> 7), i = (int)(r & 127);
         const int tile = blk / nkb, kb = blk % nkb, l = i >> 2, c = i & 3;
         const int row = tile * 128 + 32 * c + l;
-        const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(src + (size_t)z * src_stride + (size_t)row * (K / 32) + kb * 4));
+        const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(src + (size_t)z * src_stride + (size_t)(row / rps) * (K / 32) + kb * 4));
         *reinterpret_cast<uint32_t *>(dst + (size_t)z * dst_stride + (size_t)r * 4) = v;
     }
 }
 
 cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *dst, long long dst_stride, int rows, int K,
-                             int z0, int nz, cudaStream_t st) {
+                             int z0, int nz, int rps, cudaStream_t st) {
     const long long total = (long long)rows * (K / 128) * nz;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
-    sf_repack_kernel<<<blocks, 256, 0, st>>>(src, src_stride, dst, dst_stride, rows, K, z0, nz);
+    sf_repack_kernel<<<blocks, 256, 0, st>>>(src, src_stride, dst, dst_stride, rows, K, z0, nz, rps);
     return cudaGetLastError();
 }
 

@@ -25,7 +25,7 @@ const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
 int expert_tc4_smem_bytes(bool up, int nst);
 int expert_tc4_partial_cols();
 cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *dst, long long dst_stride, int rows, int K,
-                             int z0, int nz, cudaStream_t st);
+                             int z0, int nz, int rps, cudaStream_t st);
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst);
@@ -52,8 +52,12 @@ int act_pow2_of(int fmt) { return fmt == STBL_FMT_FP8_B128 ? 0 : 1; }
 long long mat_bytes(int fmt, int rows, int k, bool scales) {
     if (fmt == STBL_FMT_FP8_B128)
         return scales ? 4LL * ((rows + 127) / 128) * ((k + 127) / 128) : (long long)rows * k;
+    if (fmt == STBL_FMT_FP8_E8M0) return scales ? (long long)((rows + 31) / 32) * (k / 32) : (long long)rows * k;
     return scales ? (long long)rows * (k / 32) : (long long)rows * (k / 2);
 }
+
+// weight rows that share one row of e8m0 scales: 32 for FP8 with 32x32 blocks, 1 for MXFP4
+int scale_rows_of(int fmt) { return fmt == STBL_FMT_FP8_E8M0 ? 32 : 1; }
 
 
 
@@ -98,7 +102,10 @@ struct stbl_moe {
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
-    bool routed_fp4 = false;          // routed experts MXFP4, on the block-scaled tensor-core kernels
+    bool routed_bs = false;           // routed experts MXFP4 or FP8-e8m0: the block-scaled tensor-core kernels
+    bool shared_bs = false;           // shared expert FP8-e8m0: handled by the block-scaled kernels too
+    uint8_t *sf_shared = nullptr;     // the shared expert's scales in the scale-block layout (3 matrices)
+    long long sf_shared_off[3] = {0, 0, 0};
     TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
     int tc4_nst_up = 0, tc4_nst_down = 0, tc4_nst8_up = 0, tc4_nst8_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
     uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32), [K/128][rows][16 B]
@@ -168,6 +175,23 @@ CUtensorMap weight_map(const void *base, int K, int rows, int experts, long long
 // contiguous bytes of each row, landing as two [128 rows][128 B] tiles.  The map's data type unpacks
 // each 16 codes to 16 bytes in shared memory, the layout kind::mxf8f6f4 reads e2m1 operands in; the
 // transaction count of a box is its packed size.  Needs 32-byte aligned base and strides.
+// The same view of e4m3 codes (FP8 with e8m0 32x32 block scales): one box is 128 rows x 2 K blocks of
+// 128 bytes, landing as two [128 rows][128 B] tiles, the operand layout of the block-scaled MMA.
+CUtensorMap weight_map8x2(const void *base, int K, int rows, int experts, long long estride) {
+    CUtensorMap m;
+    if (((uintptr_t)base & 15) || (estride & 15) || (K & 15))
+        throw std::runtime_error("FP8 expert weights must be 16-byte aligned (base, row and expert strides)");
+    const cuuint64_t dims[4] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128), (cuuint64_t)experts};
+    const cuuint64_t strides[3] = {(cuuint64_t)K, 128, (cuuint64_t)(estride ? estride : (long long)rows * K)};
+    const cuuint32_t box[4] = {128, 128, 2, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for an FP8-e8m0 expert weight tensor");
+    return m;
+}
+
 CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long long estride) {
     CUtensorMap m;
     if (((uintptr_t)base & 31) || (estride & 31) || ((K / 2) & 31))
@@ -255,8 +279,12 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     const bool grouped = d->n_groups > 1 && d->topk_groups < d->n_groups;
     if (grouped && (gsz < 2 || d->topk_groups * gsz < K)) throw std::runtime_error("kept groups hold fewer than topk experts");
     if (d->score_fn != STBL_SCORE_SIGMOID && d->score_fn != STBL_SCORE_SQRT_SOFTPLUS) throw std::runtime_error("bad score_fn");
-    if (d->routed_fmt != STBL_FMT_FP8_B128 && d->routed_fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad routed_fmt");
-    if (d->shared_fmt != STBL_FMT_FP8_B128 && d->shared_fmt != STBL_FMT_NONE) throw std::runtime_error("bad shared_fmt");
+    if (d->routed_fmt != STBL_FMT_FP8_B128 && d->routed_fmt != STBL_FMT_MXFP4 && d->routed_fmt != STBL_FMT_FP8_E8M0)
+        throw std::runtime_error("bad routed_fmt");
+    if (d->shared_fmt != STBL_FMT_FP8_B128 && d->shared_fmt != STBL_FMT_FP8_E8M0 && d->shared_fmt != STBL_FMT_NONE)
+        throw std::runtime_error("bad shared_fmt");
+    if (d->routed_fmt == STBL_FMT_FP8_B128 && d->shared_fmt == STBL_FMT_FP8_E8M0)
+        throw std::runtime_error("an FP8-e8m0 shared expert needs block-scaled routed experts (MXFP4 or FP8-e8m0)");
     if (d->max_tokens < 1 || d->max_tokens > kRouterMaxTokens) throw std::runtime_error("max_tokens must be in 1..256");
     if (H / router_ksplit(H) > kLgMaxSlice) throw std::runtime_error("hidden must be at most 8192");
     if (!d->router_w || !d->router_bias) throw std::runtime_error("router weights missing");
@@ -351,15 +379,14 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
 
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
-    m->routed_fp4 = d->routed_fmt == STBL_FMT_MXFP4;
+    m->routed_bs = !m->routed_tc;
+    m->shared_bs = d->shared_fmt == STBL_FMT_FP8_E8M0;
     if (H % 128 || I % 128 || H > 8192 || I > 8192)
         throw std::runtime_error("experts need hidden and inter multiples of 128, at most 8192");
-    if (m->routed_fp4) {
-        const long long wst4[3] = {
-            d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H / 2,
-            d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H / 2,
-            d->routed_w_stride[2] ? d->routed_w_stride[2] : (long long)H * I / 2};
-        const int ns = m->n_slots;
+    if (m->routed_bs) {
+        const bool e8 = d->routed_fmt == STBL_FMT_FP8_E8M0;
+        const long long wst4[3] = {m->w_stride[0], m->w_stride[1], m->w_stride[2]};
+        const int ns = m->n_slots, rps = scale_rows_of(d->routed_fmt);
         if (!d->routed_s_blocked) {
             // the layer's own copy of every slot's scales in the scale-block layout
             long long off = 0;
@@ -371,20 +398,39 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             CK(cudaMalloc(&m->sf_own, (size_t)ns * off));
             for (int mt = 0; mt < 3; mt++)
                 CK(launch_sf_repack(static_cast<const uint8_t *>(d->routed_s[mt]), m->s_stride[mt], m->sf_own + m->sf_own_off[mt],
-                                    m->sf_own_stride, rows[mt], ks[mt], 0, ns, 0));
+                                    m->sf_own_stride, rows[mt], ks[mt], 0, ns, rps, 0));
             CK(cudaDeviceSynchronize());
         } else {
             for (int mt = 0; mt < 3; mt++)
                 if (m->s_stride[mt] & 511) throw std::runtime_error("block-layout MXFP4 scales need a slot stride multiple of 512");
         }
-        m->tc4_up.w[0] = weight_map4(d->routed_w[0], H, I, ns, wst4[0]);
-        m->tc4_up.w[1] = weight_map4(d->routed_w[1], H, I, ns, wst4[1]);
-        m->tc4_down.w[0] = m->tc4_down.w[1] = weight_map4(d->routed_w[2], I, H, ns, wst4[2]);
+        auto wmap = [&](const void *base, int K, int R, int n, long long st) {
+            return e8 ? weight_map8x2(base, K, R, n, st) : weight_map4(base, K, R, n, st);
+        };
+        m->tc4_up.w[0] = wmap(d->routed_w[0], H, I, ns, wst4[0]);
+        m->tc4_up.w[1] = wmap(d->routed_w[1], H, I, ns, wst4[1]);
+        m->tc4_down.w[0] = m->tc4_down.w[1] = wmap(d->routed_w[2], I, H, ns, wst4[2]);
         m->tc4_up.s[0] = m->tc4_up.s[1] = m->tc4_up.w[0];
         m->tc4_down.s[0] = m->tc4_down.s[1] = m->tc4_down.w[0];
+        if (m->shared_bs) {
+            // FP8-e8m0 shared expert on the same kernels: its own maps and scale blocks
+            m->tc4_up.s[0] = weight_map8x2(d->shared_w[0], H, I, 1, (long long)I * H);
+            m->tc4_up.s[1] = weight_map8x2(d->shared_w[1], H, I, 1, (long long)I * H);
+            m->tc4_down.s[0] = m->tc4_down.s[1] = weight_map8x2(d->shared_w[2], I, H, 1, (long long)H * I);
+            long long off = 0;
+            for (int mt = 0; mt < 3; mt++) {
+                m->sf_shared_off[mt] = off;
+                off += ((long long)rows[mt] * (ks[mt] / 32) + 1023) & ~1023LL;
+            }
+            CK(cudaMalloc(&m->sf_shared, (size_t)off));
+            for (int mt = 0; mt < 3; mt++)
+                CK(launch_sf_repack(static_cast<const uint8_t *>(d->shared_s[mt]), 0, m->sf_shared + m->sf_shared_off[mt], 0,
+                                    rows[mt], ks[mt], 0, 1, 32, 0));
+            CK(cudaDeviceSynchronize());
+        }
         for (int mt = 0; mt < 3; mt++)
             if (((uintptr_t)d->routed_s[mt] & 15) || (m->s_stride[mt] & 15))
-                throw std::runtime_error("MXFP4 scales must be 16-byte aligned (base and expert stride)");
+                throw std::runtime_error("block-scaled expert scales must be 16-byte aligned (base and expert stride)");
     }
     {
         // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
@@ -398,17 +444,17 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             m->tc_down.w[0] = weight_map(d->routed_w[2], I, H, m->n_slots, wst[2], 128);
             m->tc_down.w[1] = m->tc_down.w[0];
         }
-        if (m->has_shared) {
+        if (m->has_shared && !m->shared_bs) {
             m->tc_up.s[0] = weight_map(d->shared_w[0], H, I, 1, (long long)I * H, 64);
             m->tc_up.s[1] = weight_map(d->shared_w[1], H, I, 1, (long long)I * H, 64);
             m->tc_down.s[0] = weight_map(d->shared_w[2], I, H, 1, (long long)H * I, 128);
             m->tc_down.s[1] = m->tc_down.s[0];
         }
-        if (!m->routed_tc && m->has_shared)
+        if (!m->routed_tc && m->has_shared && !m->shared_bs)
             m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
         if (!m->has_shared && m->routed_tc)
             m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
-        if (!m->routed_tc && !m->has_shared) m->tc_up = m->tc4_up, m->tc_down = m->tc4_down;  // unused maps, valid
+        if (!m->routed_tc && (!m->has_shared || m->shared_bs)) m->tc_up = m->tc4_up, m->tc_down = m->tc4_down;  // unused, valid
         m->bmap_xa = act_map(m->xq_a, H, Tpad);
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
         m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
@@ -429,7 +475,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         };
         pick(true, m->tc_nst_up, m->tc_smem_up);
         pick(false, m->tc_nst_down, m->tc_smem_down);
-        if (m->routed_fp4) {
+        if (m->routed_bs) {
             // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
             // fit; a MXFP4 stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
             for (int up = 1; up >= 0; up--) {
@@ -508,13 +554,16 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     const long long sst = d.routed_s_stride[mats[0]] ? d.routed_s_stride[mats[0]]
                                                        : 4LL * ((rows + 127) / 128) * ((K + 127) / 128);
     p.w_scale_stride = sst / 4;
-    if (m->routed_fp4) {
+    if (m->routed_bs) {
         for (int i = 0; i < 2; i++)
             p.sf_a[i] = m->sf_own ? m->sf_own + m->sf_own_off[mats[i]] : static_cast<const uint8_t *>(d.routed_s[mats[i]]);
         p.sf_a_stride = m->sf_own ? m->sf_own_stride : m->s_stride[mats[0]];
         p.act_e8 = up ? (direct ? m->xe8_a : m->xe8_pos) : m->he8;
         p.act_e8_rows = up && direct ? m->Tpad : m->pos_rows;
         p.he8_rows = m->pos_rows;
+        p.w_a8 = d.routed_fmt == STBL_FMT_FP8_E8M0;
+        p.s_a8 = m->shared_bs;
+        for (int i = 0; i < 2; i++) p.sf_s[i] = m->sf_shared ? m->sf_shared + m->sf_shared_off[mats[i]] : nullptr;
     }
     p.h = m->h;
     p.hq = m->hq, p.he8 = m->he8;
@@ -562,9 +611,10 @@ void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st)
 
 void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
     GatherParams g{m->perm, T, m->K, m->H, m->has_shared, m->xq_a, m->xs_a, m->H / 32, m->xq_pos, m->xs_pos, nullptr, nullptr};
-    if (m->routed_fp4) g.xe8 = m->xe8_a, g.xe8_pos = m->xe8_pos, g.xe8_rows = m->Tpad, g.xe8_pos_rows = m->pos_rows;  // routed positions only
+    if (m->routed_bs) g.xe8 = m->xe8_a, g.xe8_pos = m->xe8_pos, g.xe8_rows = m->Tpad, g.xe8_pos_rows = m->pos_rows;
     void *args[] = {&g};
-    const int rows = T * m->K + (m->has_shared && !m->routed_fp4 ? T : 0);
+    // the shared expert's rows too when it reads by position (not when the FP8 body reads x by token)
+    const int rows = T * m->K + (m->has_shared && (!m->routed_bs || m->shared_bs) ? T : 0);
     launch_pdl(gather_kernel_ptr(), dim3(rows), dim3(256), args, 0, st);
 }
 
@@ -609,9 +659,10 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     r.counts = m->counts, r.offsets = m->offsets, r.perm = m->perm, r.chunks = m->chunks, r.n_chunks = m->n_chunks;
     const int fr = m->d.routed_fmt, fs = m->has_shared ? m->d.shared_fmt : fr;
     r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
-    if (fs == fr) r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
+    if (act_blk_of(fs) == act_blk_of(fr) && act_pow2_of(fs) == act_pow2_of(fr))  // one quantization serves both
+        r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
-    r.xe8_a = m->routed_fp4 ? m->xe8_a : nullptr;
+    r.xe8_a = m->routed_bs ? m->xe8_a : nullptr;
     r.xe8_rows = m->Tpad;
     r.nt_routed = 16;
     r.nt_shared = 16;
@@ -671,29 +722,31 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         launch_tc(m, false, pd, st);
         launches += 3;
     } else {
-        // MXFP4 routed experts on the block-scaled tensor cores; the FP8 shared expert (its chunks read
-        // x by token, as 16 consecutive tokens, at any T) on a share of the same launches' CTAs:
-        // [gather] -> up (routed + shared; the routed h rows quantized per 32 in its epilogue) ->
-        // hquant (per-128, shared rows) -> down -> combine
+        // routed experts MXFP4 or FP8-e8m0 on the block-scaled tensor cores.  An FP8 128x128 shared
+        // expert (its chunks read x by token, as 16 consecutive tokens, at any T) runs on a share of the
+        // same launches' CTAs; an FP8-e8m0 shared expert is one more set of chunks of the block-scaled
+        // body.  [gather] -> up (h quantized per 32 in its epilogue for every block-scaled row) ->
+        // [hquant per 128 of the FP8 128x128 shared rows] -> down -> combine
         const bool direct = T <= 16;
         const int ns = m->has_shared ? (T + 15) / 16 : 0;
+        const int n8 = m->shared_bs ? 0 : ns;  // chunks of the FP8 128x128 body (the shared expert's, first)
         if (!direct) {
             launch_gather(m, T, st);
             launches++;
         }
         TcParams su = tc_params(m, T, true, true), pu = tc_params(m, T, true, direct);
-        su.chunk_begin = 0, su.chunk_end = ns;
-        pu.chunk_begin = ns, pu.chunk_end = -1;
-        launch_tc4(m, true, su, pu, st);  // the routed rows of h leave it already quantized (per 32)
+        su.chunk_begin = 0, su.chunk_end = n8;
+        pu.chunk_begin = n8, pu.chunk_end = -1;
+        launch_tc4(m, true, su, pu, st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         launches += 1;
-        if (ns) {
+        if (n8) {
             launch_hquant(m, T * m->K, npos, st);
             launches++;
         }
         TcParams sd = tc_params(m, T, false), pd = tc_params(m, T, false);
-        sd.chunk_begin = 0, sd.chunk_end = ns;
-        pd.chunk_begin = ns, pd.chunk_end = -1;
+        sd.chunk_begin = 0, sd.chunk_end = n8;
+        pd.chunk_begin = n8, pd.chunk_end = -1;
         launch_tc4(m, false, sd, pd, st);
         launches += 1;
     }
@@ -910,7 +963,7 @@ int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *
             const int rows[3] = {m->I, m->I, m->H}, ks[3] = {m->H, m->H, m->I};
             for (int mt = 0; mt < 3; mt++)
                 CK(launch_sf_repack(static_cast<const uint8_t *>(m->d.routed_s[mt]), m->s_stride[mt], m->sf_own + m->sf_own_off[mt],
-                                    m->sf_own_stride, rows[mt], ks[mt], (int)sl, 1, stream));
+                                    m->sf_own_stride, rows[mt], ks[mt], (int)sl, 1, scale_rows_of(m->d.routed_fmt), stream));
         }
         CK(cudaMemcpyAsync(m->slot + e, &m->host_slot[e], sizeof(int), cudaMemcpyHostToDevice, stream));
         return 0;
@@ -972,6 +1025,7 @@ void stbl_moe_destroy(stbl_moe *m) {
         for (auto e : t.ev) cudaEventDestroy(e);
     if (m->ws) cudaFree(m->ws);
     if (m->sf_own) cudaFree(m->sf_own);
+    if (m->sf_shared) cudaFree(m->sf_shared);
     for (int d = 0; d < m->ep_n; d++)
         if (d != m->ep_rank && m->ep_peer[d]) cudaIpcCloseMemHandle(m->ep_peer[d]);
     if (m->ep_region) cudaFree(m->ep_region);

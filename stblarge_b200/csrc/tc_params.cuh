@@ -37,6 +37,10 @@ struct TcParams {
     // activation scales [K/128][act_e8_rows][16 B]
     const uint8_t *sf_a[2];
     long long sf_a_stride;
+    // weights of the block-scaled kernel in e4m3 (FP8 with e8m0 32x32 block scales) instead of e2m1:
+    // routed (w_a8) and shared expert (s_a8); the shared expert's scale blocks (one copy per matrix)
+    int w_a8, s_a8;
+    const uint8_t *sf_s[2];
     const uint8_t *act_e8;
     int act_e8_rows;
     const float *s_scale[2];   // shared expert block scales

@@ -57,6 +57,7 @@ SIGNATURES = {
     "stbl_cache_info": (I, [P, ctypes.POINTER(I), ctypes.POINTER(U64)]),
     "stbl_cache_state": (I, [P, P, P]),
     "stbl_cache_destroy": (None, [P]),
+    "stbl_mxfp4_from_gguf": (I, [P, I, I, P, P, P]),
     "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),
     "stbl_moe_set_timing": (I, [P, I]),
     "stbl_moe_timing": (I, [P, P, I]),

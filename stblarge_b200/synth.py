@@ -15,7 +15,7 @@ Two generators:
 import numpy as np
 import torch
 
-from .config import FMT_FP8_B128, FMT_MXFP4, FMT_NONE
+from .config import FMT_FP8_B128, FMT_FP8_E8M0, FMT_MXFP4, FMT_NONE
 
 FP4_GRID = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=torch.float32)
 
@@ -59,9 +59,27 @@ def quant_mxfp4(w):
     return packed, scales
 
 
+def quant_fp8_e8m0(w):
+    """float [rows, k] -> (e4m3 codes uint8 [rows, k], e8m0 scale bytes [ceil(rows/32), k/32]): per 32x32
+    block a power-of-two scale by act_quant's rule (amax clamp 1e-4, 2^ceil(log2(amax / 448)))."""
+    rows, k = w.shape
+    rb = (rows + 31) // 32
+    wp = torch.zeros(rb * 32, k, dtype=torch.float32, device=w.device)
+    wp[:rows] = w.float()
+    blk = wp.view(rb, 32, k // 32, 32)
+    amax = blk.abs().amax(dim=(1, 3)).clamp_min(1e-4)
+    s = pow2_ceil(amax * torch.tensor(1.0 / 448.0, dtype=torch.float32, device=w.device))
+    q = (blk / s[:, None, :, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    codes = q.view(torch.uint8).view(rb * 32, k)[:rows].contiguous()
+    scales = ((s.view(torch.int32) >> 23) & 0xFF).to(torch.uint8).contiguous()
+    return codes, scales
+
+
 def quantize(w, fmt):
     if fmt == FMT_FP8_B128:
         return quant_fp8_b128(w)
+    if fmt == FMT_FP8_E8M0:
+        return quant_fp8_e8m0(w)
     if fmt == FMT_MXFP4:
         return quant_mxfp4(w)
     raise ValueError(f"unknown weight format {fmt}")
@@ -170,6 +188,9 @@ def device_layer(cfg, device="cuda", experts=None, seed_base=1000):
         if cfg.routed_fmt == FMT_FP8_B128:
             routed_w.append(torch.empty(E, r, k, dtype=torch.uint8, device=device))
             routed_s.append(torch.empty(E, (r + 127) // 128, (k + 127) // 128, dtype=torch.float32, device=device))
+        elif cfg.routed_fmt == FMT_FP8_E8M0:
+            routed_w.append(torch.empty(E, r, k, dtype=torch.uint8, device=device))
+            routed_s.append(torch.empty(E, (r + 31) // 32, k // 32, dtype=torch.uint8, device=device))
         else:
             routed_w.append(torch.empty(E, r, k // 2, dtype=torch.uint8, device=device))
             routed_s.append(torch.empty(E, r, k // 32, dtype=torch.uint8, device=device))
