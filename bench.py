@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from stblarge_b200 import synth  # noqa: E402
-from stblarge_b200.config import CFG2, CFG3, FMT_MXFP4  # noqa: E402
+from stblarge_b200.config import CFG2, CFG3, CFG3_REF, FMT_FP8_E8M0, FMT_MXFP4  # noqa: E402
 
 METRIC = "MoE-layer decode tokens/s (full-size FP8 layer)"
 UNIT = "tokens/s"
@@ -64,6 +64,8 @@ def up_bytes(cfg, n_distinct):
     def mat(fmt):
         if fmt == FMT_MXFP4:
             return I * H // 2 + I * (H // 32)
+        if fmt == FMT_FP8_E8M0:
+            return I * H + ((I + 31) // 32) * (H // 32)
         return I * H + 4 * ((I + 127) // 128) * ((H + 127) // 128)
     return 2 * (n_distinct * mat(cfg.routed_fmt) + mat(cfg.shared_fmt))
 
@@ -187,7 +189,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg3ref", "cfg4", "cfg5"])
     ap.add_argument("--zipf", action="store_true", help="cfg4: Zipf(1.2) expert popularity instead of uniform")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -221,12 +223,14 @@ def main():
         T = 256 // world
     elif args.workload == "cfg3":
         cfg, T = CFG3, args.tokens
+    elif args.workload == "cfg3ref":
+        cfg, T = CFG3_REF, args.tokens
     else:
         cfg, T = CFG2, args.tokens
     E_loc = cfg.n_experts // world
     shard = range(rank * E_loc, (rank + 1) * E_loc)
     weights = synth.device_layer(cfg, device=dev, experts=shard)
-    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if args.workload == "cfg3" else 16),
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if args.workload in ("cfg3", "cfg3ref") else 16),
                      ep=(rank, world, None) if world > 1 else None)
     n_steps = args.warmup + args.steps
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
@@ -310,7 +314,7 @@ def main():
 
     # batch-size sweep of configs[1] (1, 4, 16 tokens): device time per call and per kernel
     sweep = []
-    if not args.no_sweep and world == 1 and args.workload in ("cfg2", "cfg3"):
+    if not args.no_sweep and world == 1 and args.workload in ("cfg2", "cfg3", "cfg3ref"):
         for Ts in ((1, 4, 16) if args.workload == "cfg2" else (1, 4, 16, 64)):
             xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
                    for i in range(23)]
@@ -354,13 +358,20 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if args.workload == "cfg4" else "weak", "vs_baseline": None,
-            "dtype": "fp8-e4m3 weights and activations, fp32 accumulate, bf16 io",
-            "data": "synthetic (seeded ~N(0,0.02) weights quantized to FP8 128x128; bf16 ~N(0,1) tokens)",
+            "dtype": ("fp8-e4m3 weights and activations, fp32 accumulate, bf16 io" if cfg.routed_fmt != FMT_MXFP4 else
+                      "e2m1 routed / e4m3 shared weights, e4m3 activations, fp32 accumulate, bf16 io"),
+            "data": ("synthetic (seeded ~N(0,0.02) weights quantized to "
+                     + {"cfg3": "MXFP4 routed / FP8 128x128 shared",
+                        "cfg3ref": "MXFP4 routed / FP8 e8m0-32x32 shared"}.get(args.workload, "FP8 128x128")
+                     + "; bf16 ~N(0,1) tokens)"),
             "config": {"workload": (f"cfg4 expert-parallel full-size FP8 MoE layer, 256 tokens split over {world} GPU(s), "
                                     f"{'Zipf(1.2)' if args.zipf else 'uniform'} routing"
                                     if args.workload == "cfg4" else
                                     "cfg3 full-size layer, MXFP4 routed experts (FP8 shared), Zipf(1.0) routing"
                                     if args.workload == "cfg3" else
+                                    "cfg3ref full-size layer in the reference engine's formats and routing: MXFP4 routed "
+                                    "experts, FP8 shared expert with e8m0 32x32 block scales, sqrt(softplus) top-8 of 256"
+                                    if args.workload == "cfg3ref" else
                                     "cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4)")
                                    + f", T={T} decode tokens per rank", "tokens_per_rank": T,
                        "parallelism": "single GPU" if world == 1 else

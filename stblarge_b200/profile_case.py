@@ -1,8 +1,9 @@
 """A small, profiler-friendly case of the MoE layer: full-size expert shapes (hidden 7168,
-moe_intermediate 2048, FP8 128x128 or MXFP4) but only a few routed experts resident, so that a
+moe_intermediate 2048, FP8 128x128, MXFP4, or the reference engine's formats: MXFP4 routed and
+FP8-e8m0 shared, sqrt(softplus) scores) but only a few routed experts resident, so that a
 capture under ncu holds under 2 GB of device memory and ends in seconds.
 
-    python -m stblarge_b200.profile_case [--experts 16] [--tokens 1] [--calls 3] [--fmt fp8|fp4]
+    python -m stblarge_b200.profile_case [--experts 16] [--tokens 1] [--calls 3] [--fmt fp8|fp4|ref]
     python -m stblarge_b200.profile_case --router-only [--experts 256] [--tokens 16]
 
 Each call is preceded by a 256 MB write that flushes L2.  Prints the per-kernel device times.
@@ -19,7 +20,7 @@ import torch
 
 from . import lib as L
 from . import synth
-from .config import CFG2, CFG3
+from .config import CFG2, CFG3, CFG3_REF
 from .moe import MoELayer
 
 
@@ -60,15 +61,15 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
-    ap.add_argument("--fmt", default="fp8", choices=["fp8", "fp4"])
+    ap.add_argument("--fmt", default="fp8", choices=["fp8", "fp4", "ref"])
     ap.add_argument("--router-only", action="store_true")
     a = ap.parse_args()
     if a.router_only:
         router_only(a)
         return
-    base = CFG2 if a.fmt == "fp8" else CFG3
+    base = {"fp8": CFG2, "fp4": CFG3, "ref": CFG3_REF}[a.fmt]
     E = a.experts
-    groups = 8 if E % 8 == 0 and E // 8 >= 2 else 1
+    groups = 8 if E % 8 == 0 and E // 8 >= 2 and base.n_groups > 1 else 1
     cfg = dataclasses.replace(base, name=f"{base.name}_E{E}", n_experts=E, n_groups=groups,
                               topk_groups=min(4, groups) if groups > 1 else 1)
     dev = synth.device_layer(cfg)
