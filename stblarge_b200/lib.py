@@ -1,4 +1,4 @@
-"""ctypes binding of libstbl_moe.so (include/stbl_moe.h, include/stbl_kernels.h).
+"""ctypes binding of libstbl_moe.so (include/stbl_moe.h, include/stbl_kernels.h, include/stbl_gguf.h).
 
 The reference drives its engine from Python through ctypes (stbl/run.py:37-47, stbl/test_kernels.py:25);
 this module does the same for the B200 library.  There is no fallback: if the library is missing
@@ -27,6 +27,11 @@ class MoEDesc(ctypes.Structure):
         ("routed_w_stride", LL * 3), ("routed_s_stride", LL * 3), ("shared_w", P * 3), ("shared_s", P * 3),
         ("n_slots", I), ("routed_s_blocked", I),
     ]
+
+
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", U32), ("n_dims", U32), ("dims", U64 * 4), ("offset", U64),
+                ("nbytes", U64), ("data", P)]
 
 
 class CacheDesc(ctypes.Structure):
@@ -65,6 +70,17 @@ SIGNATURES = {
     "stbl_moe_error": (ctypes.c_char_p, [P]),
     "stbl_moe_destroy": (None, [P]),
     "stbl_route_noalloc": (I, [P, P, P, I, I, I, I, I, I, I, F, P, P, P, P, P, P, ctypes.c_char_p, I]),
+    # include/stbl_gguf.h
+    "stbl_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_gguf_close": (None, [P]),
+    "stbl_gguf_info": (I, [P, ctypes.POINTER(U32), ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "stbl_gguf_tensor_at": (I, [P, U64, ctypes.POINTER(GgufTensor)]),
+    "stbl_gguf_find": (I, [P, ctypes.c_char_p, ctypes.POINTER(GgufTensor)]),
+    "stbl_gguf_kv_at": (I, [P, U64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U32)]),
+    "stbl_gguf_u32": (I, [P, ctypes.c_char_p, ctypes.POINTER(U32)]),
+    "stbl_gguf_f32": (I, [P, ctypes.c_char_p, ctypes.POINTER(F)]),
+    "stbl_gguf_uints": (ctypes.c_int64, [P, ctypes.c_char_p, ctypes.POINTER(U64), ctypes.c_int64]),
+    "stbl_gguf_str": (ctypes.c_int64, [P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int64]),
     # include/stbl_kernels.h
     "stbl_act_quant_fp8": (None, [P, I, P]),
     "stbl_round_bf16": (None, [P, I, P]),

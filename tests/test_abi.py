@@ -14,7 +14,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_symbols():
     names = set()
-    for h in ("stbl_moe.h", "stbl_kernels.h"):
+    for h in ("stbl_moe.h", "stbl_kernels.h", "stbl_gguf.h"):
         text = open(os.path.join(ROOT, "include", h)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         names |= set(re.findall(r"\b(stbl_\w+)\s*\(", text))
@@ -30,7 +30,8 @@ def test_headers_declare_the_expected_api():
     names = declared_symbols()
     for required in ("stbl_moe_create", "stbl_moe_forward", "stbl_moe_forward_host", "stbl_moe_last_route",
                      "stbl_moe_destroy", "stbl_gemv_fp8", "stbl_gemv_mxfp4_batch", "stbl_act_quant_fp8",
-                     "stbl_gemv_f32", "stbl_swiglu_batch", "stbl_axpy", "stbl_round_bf16", "stbl_sqrt_softplus"):
+                     "stbl_gemv_f32", "stbl_swiglu_batch", "stbl_axpy", "stbl_round_bf16", "stbl_sqrt_softplus",
+                     "stbl_gguf_open", "stbl_gguf_find", "stbl_gguf_u32"):
         assert required in names
 
 
