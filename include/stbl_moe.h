@@ -163,6 +163,20 @@ void stbl_cache_destroy(stbl_cache *c);
  * 32.  Lossless: the reference's weights load into a layer this way, once. */
 int stbl_mxfp4_from_gguf(const void *blocks, int rows, int k, void *codes, void *scales, cudaStream_t stream);
 
+/* The layer inside its transformer block, the reference's FFN sub-block (stbl/model.cu:803-805), in the
+ * layer's own launches:
+ *   x = bf16(norm_w * (x_pre * rsqrt(mean(x_pre^2) + eps)))   stbl_rms_norm (stbl/kernels.cu:217-236, 594-596),
+ *       fused into the router kernel, same operations and reduction order (bit-identical)
+ *   y = the layer's output for x                             moe() / stbl_moe_forward
+ *   h_out[t][j][d] = bf16(post[t][j] * y[t][d] + sum_a comb[t][a][j] * res[t][a][d]) for j < hc
+ *                                                            stbl_hc_post (stbl/kernels.cu:328-338, 609-612),
+ *       fused into the combine kernel, same rounding steps (bit-identical)
+ * x_pre fp32 [T][hidden] (the hc_pre output), norm_w fp32 [hidden], res fp32 [T][hc][hidden], post fp32
+ * [T][hc], comb fp32 [T][hc][hc], h_out fp32 [T][hc][hidden] (bf16 values); device pointers, x_pre,
+ * norm_w, res and h_out 16-byte aligned; hc <= 16; single-GPU layers. */
+int stbl_moe_forward_block(stbl_moe *m, const float *x_pre, const float *norm_w, float eps, const float *res,
+                           const float *post, const float *comb, int hc, int T, float *h_out, cudaStream_t stream);
+
 /* Device status bits raised by kernels since the last call of this function (waits for the
  * device): 1 a wait timed out, 2 a dispatch entry was out of range, 4 copies were still in flight
  * when a CTA gave up.  0 when every call so far ran cleanly. */

@@ -663,3 +663,50 @@ void orc_ref_swiglu(float *out, const float *g, const float *u, const float *wei
 void orc_ref_axpy(float *y, const float *x, float a, int n) {
     for (int i = 0; i < n; i++) y[i] = fmaf(a, x[i], y[i]);
 }
+
+/* k_rms_norm with its 256-thread launch (stbl/kernels.cu:217-236, 594-596), per row: the sum of squares
+ * in the kernel's order (thread i: x[i], x[i + 256], ... by fused multiply-add; each warp's 32 sums by
+ * the xor butterfly, lane 0's result; the 8 warp sums by the same butterfly), then
+ * out = bf16(w * (x * r)).  r: the kernel calls CUDA's rsqrtf; here 1/sqrt correctly rounded from
+ * double, which can differ from rsqrtf in the last bit of r (the GPU kernels are checked against the
+ * reference kernel itself, bit for bit). */
+static float warp_sum_xor32(const float *v32) {
+    float v[32];
+    for (int l = 0; l < 32; l++) v[l] = v32[l];
+    for (int o = 16; o > 0; o >>= 1) {
+        float n[32];
+        for (int l = 0; l < 32; l++) n[l] = v[l] + v[l ^ o];
+        for (int l = 0; l < 32; l++) v[l] = n[l];
+    }
+    return v[0];
+}
+
+void orc_ref_rms_norm(float *out, const float *x, const float *w, int rows, int dim, float eps) {
+    for (int r = 0; r < rows; r++) {
+        const float *xr = x + (size_t)r * dim;
+        float part[32] = {0};
+        for (int wp = 0; wp < 8; wp++) {
+            float lanes[32];
+            for (int l = 0; l < 32; l++) {
+                float s = 0.f;
+                for (int i = 32 * wp + l; i < dim; i += 256) s = fmaf(xr[i], xr[i], s);
+                lanes[l] = s;
+            }
+            part[wp] = warp_sum_xor32(lanes);
+        }
+        const float total = warp_sum_xor32(part);
+        const float rr = (float)(1.0 / sqrt((double)(total / (float)dim + eps)));
+        for (int i = 0; i < dim; i++) out[(size_t)r * dim + i] = orc_bf16_round(w[i] * (xr[i] * rr));
+    }
+}
+
+/* k_hc_post (stbl/kernels.cu:328-338): out[j][d] = bf16(post[j] * x[d] + sum_a comb[a][j] * res[a][d]),
+ * each product and sum rounded in a's order (exact restatement). */
+void orc_ref_hc_post(float *out, const float *x, const float *res, const float *post, const float *comb, int hc, int dim) {
+    for (int j = 0; j < hc; j++)
+        for (int d = 0; d < dim; d++) {
+            float s = 0.f;
+            for (int a = 0; a < hc; a++) s = s + comb[a * hc + j] * res[(size_t)a * dim + d];
+            out[(size_t)j * dim + d] = orc_bf16_round(post[j] * x[d] + s);
+        }
+}

@@ -108,6 +108,9 @@ void orc_ref_sqrt_softplus(float *s, int n);                                    
 void orc_ref_swiglu(float *out, const float *g, const float *u, const float *weights, int count, float limit,
                     int n);                                                               /* :445-459 */
 void orc_ref_axpy(float *y, const float *x, float a, int n);                              /* :461-464 */
+void orc_ref_rms_norm(float *out, const float *x, const float *w, int rows, int dim, float eps); /* :217-236 */
+void orc_ref_hc_post(float *out, const float *x, const float *res, const float *post, const float *comb, int hc,
+                     int dim);                                                            /* :328-338 */
 
 #ifdef __cplusplus
 }

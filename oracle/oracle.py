@@ -325,6 +325,24 @@ def ref_axpy(y, x, a):
     return y
 
 
+def ref_rms_norm(x, w, eps):
+    """k_rms_norm per row of x [rows][dim] (r from a correctly rounded 1/sqrt; see moe_oracle.c)."""
+    x, w = _f32(x), _f32(w)
+    rows, dim = x.shape
+    out = np.empty_like(x)
+    lib().orc_ref_rms_norm(ptr(out), ptr(x), ptr(w), I(rows), I(dim), F(eps))
+    return out
+
+
+def ref_hc_post(y, res, post, comb):
+    """k_hc_post of one token: y [dim], res [hc][dim], post [hc], comb [hc][hc] -> [hc][dim]."""
+    y, res, post, comb = _f32(y), _f32(res), _f32(post), _f32(comb)
+    hc, dim = res.shape
+    out = np.empty((hc, dim), np.float32)
+    lib().orc_ref_hc_post(ptr(out), ptr(y), ptr(res), ptr(post), ptr(comb), I(hc), I(dim))
+    return out
+
+
 # ---- expert cache bookkeeping ---------------------------------------------------------------------
 
 class LruExpertCache:

@@ -70,6 +70,12 @@ struct RouterParams {
     unsigned int *sel_ticket;
     uint32_t *status;
     const int *forced_idx;   // optional: [T][topk] experts given instead of selected (forced routes)
+    // optional fused RMSNorm (x_pre non-null; x is then not read): the layer input is
+    // bf16(norm_w * (x_pre * rsqrt(mean(x_pre^2) + norm_eps))), computed per token as the reference's
+    // k_rms_norm does (stbl/kernels.cu:217-236): 256 strided partial sums, two xor-butterfly warp sums
+    const float *x_pre;      // [T][H] fp32
+    const float *norm_w;     // [H]
+    float norm_eps;
 };
 
 // Sets the logits kernel's shared-memory limit on the current device (once per device, before any
@@ -148,11 +154,19 @@ __device__ __forceinline__ void signal_all(const EpView &v, long long which) {
 struct CombineParams {
     const uint16_t *eo;
     const uint16_t *sh;
-    uint16_t *y;
+    uint16_t *y;             // [T][H] bf16 (null: not written)
     int T, topk, H, has_shared;
     // expert parallelism (ep.n_ranks > 1): raise done_flag on every rank, wait for all of them
     EpView ep;
     uint32_t *status;
+    // optional fused hyper-connection post (hout non-null; the reference's k_hc_post,
+    // stbl/kernels.cu:328-338, per token): hout[t][j][d] = bf16(post[t][j] * y[t][d] +
+    // sum_a comb[t][a][j] * res[t][a][d]), products and sums rounded step by step in a's order
+    const float *res;        // [T][hc][H]
+    const float *post;       // [T][hc]
+    const float *comb;       // [T][hc][hc]
+    float *hout;             // [T][hc][H], bf16 values
+    int hc;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

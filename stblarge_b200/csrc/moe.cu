@@ -638,8 +638,19 @@ void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem,
 TimedCall take_events(stbl_moe *m);
 void collect_timing(stbl_moe *m, size_t keep);
 
-void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const int *forced = nullptr) {
+// the block around the layer (stbl_moe_forward_block): RMSNorm before it, hyper-connection post after
+struct BlockIO {
+    const float *x_pre, *norm_w;
+    float eps;
+    const float *res, *post, *comb;
+    int hc;
+    float *hout;
+};
+
+void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const int *forced = nullptr,
+             const BlockIO *io = nullptr) {
     if (T < 1 || T > m->Tmax) throw std::runtime_error("T must be in 1..max_tokens");
+    if (io) x = io->x_pre, y = io->hout;
     if (!x || !y) throw std::runtime_error("null x or y");
     if (m->ep_n > 1 && !m->ep_connected) throw std::runtime_error("expert-parallel layer not connected (stbl_moe_ep_connect)");
     if (m->ep_n > 1 && ++m->ep_epoch == 0) m->ep_epoch = 1;
@@ -652,7 +663,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         CK(cudaEventRecord(tc.ev[0], st));
     }
     RouterParams r{};
-    r.W = m->d.router_w, r.bias = m->d.router_bias, r.x = static_cast<const uint16_t *>(x);
+    r.W = m->d.router_w, r.bias = m->d.router_bias, r.x = io ? nullptr : static_cast<const uint16_t *>(x);
+    if (io) r.x_pre = io->x_pre, r.norm_w = io->norm_w, r.norm_eps = io->eps;
     r.T = T, r.E = m->E, r.H = m->H, r.topk = m->K, r.n_groups = m->d.n_groups, r.topk_groups = m->d.topk_groups;
     r.score_fn = m->d.score_fn, r.route_scale = m->d.route_scale, r.ksplit = m->ksplit, r.has_shared = m->has_shared;
     r.scores = m->scores, r.idx = m->idx, r.wts = m->wts;
@@ -750,7 +762,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         launch_tc4(m, false, sd, pd, st);
         launches += 1;
     }
-    CombineParams cp{m->eo, m->sh, static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};
+    CombineParams cp{m->eo, m->sh, io ? nullptr : static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};
+    if (io) cp.res = io->res, cp.post = io->post, cp.comb = io->comb, cp.hout = io->hout, cp.hc = io->hc;
     void *cargs[] = {&cp};
     const int cthreads = T * (m->H / 8);
     launch_pdl(combine_kernel_ptr(), dim3((cthreads + 255) / 256), dim3(256), cargs, 0, st);
@@ -855,6 +868,23 @@ int stbl_moe_ep_connect(stbl_moe *m, const void *handles) {
 int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaStream_t stream) {
     try {
         forward(m, x_bf16, T, y_bf16, stream);
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
+int stbl_moe_forward_block(stbl_moe *m, const float *x_pre, const float *norm_w, float eps, const float *res,
+                           const float *post, const float *comb, int hc, int T, float *h_out, cudaStream_t stream) {
+    try {
+        if (!x_pre || !norm_w || !res || !post || !comb || !h_out) throw std::runtime_error("null argument");
+        if (hc < 1 || hc > 16) throw std::runtime_error("hc must be in 1..16");
+        if (m->ep_n > 1) throw std::runtime_error("the fused block is single-GPU");
+        for (const void *ptr : {(const void *)x_pre, (const void *)norm_w, (const void *)res, (const void *)h_out})
+            if ((uintptr_t)ptr & 15) throw std::runtime_error("x_pre, norm_w, res and h_out must be 16-byte aligned");
+        const BlockIO io{x_pre, norm_w, eps, res, post, comb, hc, h_out};
+        forward(m, nullptr, T, nullptr, stream, nullptr, &io);
         return 0;
     } catch (const std::exception &e) {
         m->err = e.what();

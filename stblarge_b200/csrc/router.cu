@@ -42,16 +42,58 @@ __device__ __forceinline__ void top2_merge(uint32_t &a1, uint32_t &a2, uint32_t 
     a2 = max(lo, max(a2, b2));
 }
 
+// ---- fused RMSNorm (RouterParams::x_pre) ---------------------------------------------------------------
+
+// the reference's warp_sum (stbl/kernels.cu:15-18): xor butterfly, lane 0's sum is the one used
+__device__ __forceinline__ float warp_sum_xor(float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// The normalized input value: bf16(w * (x * r)), the two products rounded as written (k_rms_norm's
+// output, stbl/kernels.cu:235), returned as the float of the bf16.
+__device__ __forceinline__ float rms_value(float x, float w, float r) { return bf16r(w * (x * r)); }
+
+// r = rsqrt(mean(x^2) + eps) of one token row, by all 256 threads of the CTA in the order of the
+// reference's k_rms_norm with 256 threads (stbl/kernels.cu:217-234, launched by stbl_rms_norm with 256
+// threads, kernels.cu:594-596): thread i sums x[i], x[i + 256], ... in index order, each warp's 32
+// sums are added by the xor butterfly, then the 8 warp sums by the same butterfly in warp 0.  The
+// result goes to *out (thread 0).  red: 8 floats of shared memory.
+__device__ void rms_rsqrt(const float *xr, int H, float eps, float *red, float *out) {
+    static_assert(kLgThreads == 256, "the reduction order is the reference's 256-thread one");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float s = 0.f;
+    for (int i = tid; i < H; i += kLgThreads) s += xr[i] * xr[i];
+    s = warp_sum_xor(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < kLgThreads / 32 ? red[lane] : 0.f;
+        v = warp_sum_xor(v);
+        if (lane == 0) *out = rsqrtf(v / H + eps);
+    }
+    __syncthreads();
+}
+
 // act_quant (ref/kernel.py:35-45) of 128 consecutive values of one token: lane l takes 4 of them.
 // blk 128: fp32 scale amax/448; blk 32: power-of-two scale per 32 (pow2 selects the rounding).
 // xe8 (optional): the scales as e8m0 bytes (per-32 power-of-two rule), laid out as the MXFP4 experts'
 // tensor-core kernel copies them: [H/128][xe8_rows][16 B], row t's bytes 0..3 for the 128-K block.
+// With the fused RMSNorm (nrm non-null) the values are normalized from x_pre first (rms_value).
 __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq, float *xs, int blk, int pow2, int lane,
-                            uint8_t *xe8, int xe8_rows) {
+                            uint8_t *xe8, int xe8_rows, const RouterParams *nrm = nullptr, float r = 0.f) {
     const int k = 128 * g + 4 * lane;
-    const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)t * H + k));
-    const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
-                        __uint_as_float(xv.y & 0xffff0000u)};
+    float v[4];
+    if (nrm) {
+        const float4 xv = __ldg(reinterpret_cast<const float4 *>(nrm->x_pre + (size_t)t * H + k));
+        const float4 wv = __ldg(reinterpret_cast<const float4 *>(nrm->norm_w + k));
+        v[0] = rms_value(xv.x, wv.x, r), v[1] = rms_value(xv.y, wv.y, r), v[2] = rms_value(xv.z, wv.z, r),
+        v[3] = rms_value(xv.w, wv.w, r);
+    } else {
+        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + (size_t)t * H + k));
+        v[0] = __uint_as_float(xv.x << 16), v[1] = __uint_as_float(xv.x & 0xffff0000u), v[2] = __uint_as_float(xv.y << 16),
+        v[3] = __uint_as_float(xv.y & 0xffff0000u);
+    }
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     for (int o = blk / 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     amax = fmaxf(amax, 1e-4f);
@@ -132,6 +174,9 @@ __device__ __forceinline__ void logits_tile(const float *w, const uint16_t *x, i
 __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int abort_flag;
+    // fused RMSNorm: r of the tokens this CTA reduces (t = its cluster rank mod ksplit), then of all
+    __shared__ float r_own[kRouterMaxTokens], r_all[kRouterMaxTokens], red[kLgThreads / 32];
+    const bool fused = p.x_pre != nullptr;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     cg::cluster_group cluster = cg::this_cluster();
     const int ks = (int)cluster.block_rank();
@@ -159,7 +204,30 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
         if (lane < ne) bulk_g2s(w_s + lane * slice, p.W + (size_t)(e0 + lane) * p.H + (size_t)ks * slice, slice * 4, bar_w);
     }
     pdl_wait();  // x may come from the kernel before this one
+    if (fused) {
+        // the cluster's CTAs split the tokens' norms and share them through distributed shared memory
+        for (int t = ks; t < p.T; t += p.ksplit) rms_rsqrt(p.x_pre + (size_t)t * p.H, p.H, p.norm_eps, red, &r_own[t]);
+        cluster.sync();
+        for (int t = tid; t < p.T; t += kLgThreads) r_all[t] = cluster.map_shared_rank(r_own, t % p.ksplit)[t];
+        __syncthreads();
+    }
     auto stage_x = [&](int r0, int nr) {
+        if (fused) {
+            // normalized rows of the slice, written by the threads (the round's barrier publishes them)
+            const int base = ks * slice, q4 = slice / 4;
+            for (int i = tid; i < nr * q4; i += kLgThreads) {
+                const int t = i / q4, k = base + 4 * (i % q4);
+                const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x_pre + (size_t)(r0 + t) * p.H + k));
+                const float4 wv = __ldg(reinterpret_cast<const float4 *>(p.norm_w + k));
+                const float r = r_all[r0 + t];
+                const uint32_t lo = (uint32_t)f32_to_bf16_bits(rms_value(xv.x, wv.x, r)) |
+                                    ((uint32_t)f32_to_bf16_bits(rms_value(xv.y, wv.y, r)) << 16);
+                const uint32_t hi = (uint32_t)f32_to_bf16_bits(rms_value(xv.z, wv.z, r)) |
+                                    ((uint32_t)f32_to_bf16_bits(rms_value(xv.w, wv.w, r)) << 16);
+                *reinterpret_cast<uint2 *>(x_s + (size_t)t * slice + (k - base)) = make_uint2(lo, hi);
+            }
+            return;
+        }
         if (warp == 0) {
             if (lane == 0) mbar_arrive_expect_tx(bar_x, (uint32_t)(nr * slice * 2));
             __syncwarp();
@@ -181,10 +249,11 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
         const int nwarps_grid = gridDim.x * (kLgThreads / 32), gwarp = blockIdx.x * (kLgThreads / 32) + warp;
         const int groups = p.T * (p.H / 128);
         for (int u = gwarp; u < groups; u += nwarps_grid) {
-            quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane, p.xe8_a,
-                        p.xe8_rows);
-            if (p.xq_b != p.xq_a)
-                quant_group(p.x, p.H, u / (p.H / 128), u % (p.H / 128), p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane, nullptr, 0);
+            const int t = u / (p.H / 128), g = u % (p.H / 128);
+            const RouterParams *nrm = fused ? &p : nullptr;
+            const float r = fused ? r_all[t] : 0.f;
+            quant_group(p.x, p.H, t, g, p.xq_a, p.xs_a, p.blk_a, p.pow2_a, lane, p.xe8_a, p.xe8_rows, nrm, r);
+            if (p.xq_b != p.xq_a) quant_group(p.x, p.H, t, g, p.xq_b, p.xs_b, p.blk_b, p.pow2_b, lane, nullptr, 0, nrm, r);
         }
     }
 
@@ -198,7 +267,7 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
             stage_x(r0, nr);
             last_round = round;
         }
-        ok = mbar_wait(bar_x, round & 1, &abort_flag) && ok;
+        if (!fused) ok = mbar_wait(bar_x, round & 1, &abort_flag) && ok;
         ok = __syncthreads_and(ok ? 1 : 0) != 0;  // uniform: every warp stops if one gave up
         if (!ok) break;
         // work split of the round by its token count: (experts, tokens) per warp
@@ -244,7 +313,8 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
     // a CTA that gave up waits (bounded) for its own copies before its shared memory is released
     if (abort_flag && tid == 0) {
         int dummy = 0;
-        if (!mbar_wait(bar_w, 0, &dummy) || !mbar_wait(bar_x, last_round & 1, &dummy)) atomicOr(p.status, kErrCopyTimeout);
+        if (!mbar_wait(bar_w, 0, &dummy) || (!fused && !mbar_wait(bar_x, last_round & 1, &dummy)))
+            atomicOr(p.status, kErrCopyTimeout);
     }
 }
 

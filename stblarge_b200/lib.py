@@ -55,6 +55,7 @@ SIGNATURES = {
     "stbl_moe_last_scores": (I, [P, P]),
     "stbl_moe_set_expert": (I, [P, I, P, P, P]),
     "stbl_moe_forward_routed": (I, [P, P, I, P, P, P]),
+    "stbl_moe_forward_block": (I, [P, P, P, F, P, P, P, I, I, P, P]),
     "stbl_cache_create": (I, [ctypes.POINTER(CacheDesc), ctypes.POINTER(P), ctypes.c_char_p, I]),
     "stbl_cache_layer_desc": (I, [P, ctypes.POINTER(MoEDesc)]),
     "stbl_moe_attach_cache": (I, [P, P, I]),

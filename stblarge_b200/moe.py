@@ -107,6 +107,25 @@ class MoELayer:
                                                      ctypes.c_void_p(st.cuda_stream)), "stbl_moe_forward_routed")
         return out
 
+    def forward_block(self, x_pre, norm_w, eps, res, post, comb, out=None, stream=None):
+        """The layer inside its block (stbl_moe_forward_block; stbl/model.cu:803-805): RMSNorm of x_pre
+        (cuda float32 [T, hidden]) with norm_w (float32 [hidden]) and eps before it, the hyper-connection
+        post after it: res float32 [T, hc, hidden], post [T, hc], comb [T, hc, hc] -> float32 [T, hc, hidden]."""
+        T, H = x_pre.shape
+        hc = res.shape[1]
+        assert H == self.cfg.hidden and tuple(res.shape) == (T, hc, H) and tuple(post.shape) == (T, hc)
+        assert tuple(comb.shape) == (T, hc, hc) and tuple(norm_w.shape) == (H,)
+        ts = [t.contiguous() for t in (x_pre, norm_w, res, post, comb)]
+        assert all(t.is_cuda and t.dtype == torch.float32 for t in ts)
+        if out is None:
+            out = torch.empty(T, hc, H, dtype=torch.float32, device=x_pre.device)
+        st = stream if stream is not None else torch.cuda.current_stream(x_pre.device)
+        x_pre, norm_w, res, post, comb = ts
+        self._check(self.lib.stbl_moe_forward_block(self.handle, _ptr(x_pre), _ptr(norm_w), ctypes.c_float(eps), _ptr(res),
+                                                    _ptr(post), _ptr(comb), hc, T, _ptr(out), ctypes.c_void_p(st.cuda_stream)),
+                    "stbl_moe_forward_block")
+        return out
+
     def forward_host(self, x_bits, y_bits=None, stream=None):
         """End to end with host buffers: x_bits uint16 [T, hidden] (numpy or pinned torch)."""
         if isinstance(x_bits, np.ndarray):
