@@ -156,6 +156,23 @@ int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint
 int stbl_cache_state(const stbl_cache *c, int *map, int *owner);
 void stbl_cache_destroy(stbl_cache *c);
 
+/* Prefetch into the cache, the reference's shadow next-layer guesses (stbl/model.cu:432-475 predict,
+ * 555-586 issue, 347-373 take_slot): of the first `consider` distinct ids (device [n], guessed experts of
+ * layer `layer` in priority order) the ones not cached take a never-used slot or the least recently used
+ * one and become the most recent; cached ones are not touched.  Planned on `stream` (after what is queued
+ * there), copied on `copy_stream`; the cache's next call waits for that copy, so the guesses have landed
+ * when a layer is routed (the reference's prefetch reads that finished in time).  A slot the last call
+ * used is never taken: the prefetch stops there.  Counters: experts prefetched, prefetched experts a
+ * later call routed to, bytes prefetched. */
+int stbl_cache_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, cudaStream_t stream,
+                        cudaStream_t copy_stream);
+int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_t *used, uint64_t *bytes);
+/* Each call of layer m (attached to a cache) then also runs `next`'s router on m's input and prefetches
+ * its top n_predict experts per token (first `consider` distinct ones, stbl_cache_prefetch) for `next`,
+ * copied on copy_stream beside m's expert kernels.  next: a layer attached to the same cache, or NULL
+ * to stop.  Single-GPU; n_predict <= 16. */
+int stbl_moe_attach_prefetch(stbl_moe *m, const stbl_moe *next, int n_predict, int consider, cudaStream_t copy_stream);
+
 /* The reference engine's MXFP4 storage, GGUF blocks of 17 bytes per 32 values (the e8m0 scale, then 16
  * bytes holding values 0..15 in the low nibbles and 16..31 in the high nibbles; stbl/kernels.cu:134-141,
  * tools/convert_official.py:187-201), into the layer's STBL_FMT_MXFP4 layout: codes [rows][k/2] (even

@@ -346,7 +346,7 @@ def ref_hc_post(y, res, post, comb):
 # ---- expert cache bookkeeping ---------------------------------------------------------------------
 
 class LruExpertCache:
-    """The reference's expert cache decisions without prefetch (stbl/model.cu:99-106 ExpertCache,
+    """The reference's expert cache decisions (stbl/model.cu:99-106 ExpertCache,
     371-393 take_slot, 397-422 expert(), 503-520 the touch order in moe()): an LRU list of (layer,
     expert) keys, most recent first.  A call first moves its cached experts to the front in order, then
     walks its experts in order: a hit moves to the front again, a miss takes the next never-used slot
@@ -360,6 +360,9 @@ class LruExpertCache:
         self.lru = []        # keys, most recent first
         self.next_slot = 0
         self.hits = self.misses = 0
+        self.last = set()    # keys of the last call (still being read while a prefetch is planned)
+        self.pf_keys = set() # prefetched keys no call has routed to yet
+        self.prefetched = self.pf_used = 0
 
     def _front(self, key):
         self.lru.remove(key)
@@ -370,7 +373,30 @@ class LruExpertCache:
             self.next_slot += 1
             return self.next_slot - 1
         key = self.lru.pop()
+        self.pf_keys.discard(key)
         return self.where.pop(key)
+
+    def prefetch(self, layer, ids, consider):
+        """The reference's prefetch issue (stbl/model.cu:555-569) when every earlier prefetch has landed
+        before the next routing: of the first `consider` distinct ids, the ones not cached take a slot
+        (take_slot: never used first, else the list's last key) and go to the front; cached ones are
+        not touched.  A slot of the last call's experts is never taken (they may still be read): the
+        prefetch stops there.  Returns the placed (slot, expert)."""
+        order = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))[:consider]
+        placed = []
+        for e in order:
+            key = (layer, e)
+            if key in self.where:
+                continue
+            if self.next_slot >= self.slots and self.lru[-1] in self.last:
+                break
+            s = self._take_slot()
+            self.where[key] = s
+            self.lru.insert(0, key)
+            self.pf_keys.add(key)
+            self.prefetched += 1
+            placed.append((s, e))
+        return placed
 
     def call(self, layer, ids):
         """ids: the call's routed expert ids, token-major.  Returns the misses as (slot, expert) in
@@ -385,12 +411,16 @@ class LruExpertCache:
             if key in self.where:
                 self._front(key)
                 self.hits += 1
+                if key in self.pf_keys:
+                    self.pf_keys.discard(key)
+                    self.pf_used += 1
             else:
                 self.misses += 1
                 s = self._take_slot()
                 self.where[key] = s
                 self.lru.insert(0, key)
                 placed.append((s, e))
+        self.last = {(layer, e) for e in order}
         return placed
 
     def state(self, n_layers, n_experts):

@@ -78,6 +78,13 @@ class ExpertCache:
             raise RuntimeError("stbl_cache_stats failed")
         return {"hits": h.value, "misses": m.value, "bytes": b.value}
 
+    def prefetch_stats(self):
+        """Experts prefetched, prefetched experts a later call routed to, bytes prefetched."""
+        p, u, b = L.U64(), L.U64(), L.U64()
+        if self.lib.stbl_cache_prefetch_stats(self.handle, ctypes.byref(p), ctypes.byref(u), ctypes.byref(b)) != 0:
+            raise RuntimeError("stbl_cache_prefetch_stats failed")
+        return {"prefetched": p.value, "used": u.value, "bytes": b.value}
+
     def state(self):
         mp = np.empty((self.n_layers, self.cfg.n_experts), np.int32)
         owner = np.empty(self.slots, np.int32)

@@ -11,6 +11,15 @@
 // Missing experts are then copied by a grid of CTAs reading the pinned host store directly
 // (device-visible host memory, 16-byte loads, many in flight): the copy, like everything else in
 // the call, is ordered on the layer's stream and needs no host thread.
+//
+// Prefetch (the reference's shadow next-layer guesses, stbl/model.cu:432-475, 555-586): the planner's
+// second mode places guessed experts of a coming layer call without touching cached ones (its
+// issue(), each new guess takes a never-used slot or the least recently used one and goes to the
+// front), and the copy runs on a second stream, beside the current call's expert kernels (the copy
+// kernel keeps no shared memory and few registers, so its CTAs fit next to theirs).  A prefetch never
+// takes a slot the last demand call used (those experts may still be read), and the next demand call
+// waits for the prefetch copy before planning: the guesses have always landed by then, which is the
+// reference's case of reads that finished in time (it also cancels guesses not yet started).
 #include "../../include/stbl_moe.h"
 #include "cache.cuh"
 #include "layer.cuh"
@@ -42,6 +51,10 @@ struct CachePlanParams {
     int *n_jobs;
     long long expert_bytes;
     uint32_t *status;
+    // prefetch mode: consider the first `consider` distinct ids; pf_flag [S]: filled by a prefetch and
+    // not yet routed to (counted as used at its first hit)
+    int prefetch, consider;
+    unsigned char *pf_flag;
 };
 
 struct CacheCopyParams {
@@ -52,7 +65,7 @@ struct CacheCopyParams {
     long long piece_bytes[6], piece_off[6], host_stride[6];
     long long host_rows;
     const uint8_t *host[6];
-    int chunks[6];  // work items of each piece: kCopyChunk bytes, or (blocked scales) one 128-row tile
+    int chunks[6];  // work items of each piece: kCopyChunk bytes, or (blocked scales) 8 row groups of a 128-row tile
     // MXFP4 caches: the scale pieces (3..5) are written in the expert kernel's scale-block layout
     // (per 128 rows x 128 K a 512-byte block, byte l*16 + c*4 + j = scale of row 32c + l, 32-block j)
     int blocked;
@@ -127,19 +140,25 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
     int *row = p.map + (size_t)p.layer * p.E;
     // the call's cached experts are touched first (in order), so no miss of this call evicts one;
     // then each hit is touched again in order (the reference moves it to the front twice)
-    int hits = 0;
-    for (int i = tid; i < nu; i += kPlanThreads) {
+    // prefetch mode: cached guesses are not touched, and only the first `consider` guesses count
+    const int nw = p.prefetch ? min(nu, p.consider) : nu;
+    const unsigned long long guard = p.prefetch ? p.ctr[4] : base;  // slots with a later use are off limits
+    int hits = 0, used = 0;
+    for (int i = tid; i < nu && !p.prefetch; i += kPlanThreads) {
         const int s = row[ulist[i]];
-        if (s >= 0) p.ts[s] = base + 1 + nu + i, hits++;
+        if (s >= 0) {
+            p.ts[s] = base + 1 + nu + i, hits++;
+            if (p.pf_flag[s]) p.pf_flag[s] = 0, used++;
+        }
     }
     // misses, in order: each takes the least recently used slot (every slot this call touched is newer)
-    for (int o = 16; o > 0; o >>= 1) hits += __shfl_xor_sync(0xffffffffu, hits, o);
-    if (lane == 0) wsum[warp] = hits;
+    for (int o = 16; o > 0; o >>= 1) hits += __shfl_xor_sync(0xffffffffu, hits, o), used += __shfl_xor_sync(0xffffffffu, used, o);
+    if (lane == 0) wsum[warp] = hits | (used << 16);
     __syncthreads();
-    int n_hits = 0;
-    for (int w = 0; w < kPlanThreads / 32; w++) n_hits += wsum[w];
+    int n_hits = 0, n_used = 0;
+    for (int w = 0; w < kPlanThreads / 32; w++) n_hits += wsum[w] & 0xFFFF, n_used += wsum[w] >> 16;
     int j = 0;
-    for (int i = 0; i < nu; i++) {
+    for (int i = 0; i < nw; i++) {
         const int e = ulist[i];
         if (row[e] >= 0) continue;  // uniform: row[] changes only below, after a barrier
         unsigned long long best = ~0ull;
@@ -155,14 +174,17 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
             v = min_u64_warp(v);
             if (lane == 0) {
                 const int s = (int)(v & 0xFFFFF);
-                if ((v >> 20) > base) {
-                    s_bad = 1;  // every slot is in use by this call: too few slots (checked at attach)
+                if ((v >> 20) > guard) {
+                    // demand: every slot is in use by this call, too few slots (checked at attach);
+                    // prefetch: the rest would evict experts of the last call: the prefetch stops
+                    s_bad = p.prefetch ? 2 : 1;
                 } else {
                     const int old = p.owner[s];
                     if (old >= 0) p.map[old] = -1;
                     p.owner[s] = p.layer * p.E + e;
                     row[e] = s;
-                    p.ts[s] = base + 1 + nu + i;
+                    p.ts[s] = p.prefetch ? base + 1 + i : base + 1 + nu + i;
+                    p.pf_flag[s] = p.prefetch ? 1 : 0;
                     p.jobs[j] = make_int2(s, p.layer * p.E + e);
                 }
             }
@@ -172,12 +194,20 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
         j++;
     }
     if (tid == 0) {
-        p.ctr[0] = base + 1 + 2ull * nu;
-        p.ctr[1] += n_hits;
-        p.ctr[2] += j;
-        p.ctr[3] += (unsigned long long)j * p.expert_bytes;
+        if (p.prefetch) {
+            p.ctr[0] = base + 1 + (unsigned long long)nw;
+            p.ctr[5] += j;
+            p.ctr[7] += (unsigned long long)j * p.expert_bytes;
+        } else {
+            p.ctr[0] = base + 1 + 2ull * nu;
+            p.ctr[1] += n_hits;
+            p.ctr[2] += j;
+            p.ctr[3] += (unsigned long long)j * p.expert_bytes;
+            p.ctr[4] = base;
+            p.ctr[6] += n_used;
+        }
         *p.n_jobs = j;
-        if (s_bad) atomicOr(p.status, kErrBadTable);
+        if (s_bad == 1) atomicOr(p.status, kErrBadTable);
     }
 }
 
@@ -195,23 +225,23 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
         while (q < 5 && r >= p.chunks[q]) r -= p.chunks[q++];
         const int2 job = p.jobs[jb];
         if (p.blocked && q >= 3) {
-            // one 128-row tile of natural [rows][K/32] scales through shared memory into its blocks
-            extern __shared__ uint4 tile_s[];
+            // natural [rows][K/32] scales into their blocks, without shared memory: item r = (128-row
+            // tile r / 4, group of 8 row groups l); warp w takes row group l = 8 (r % 4) + w, i.e. rows
+            // 32 c + l of the tile (c < 4); lane j loads 16 bytes (the 4 words of blocks 4j..4j+3) of each
+            // of the 4 rows and writes the 16-byte word (l, kb) of each of its blocks kb
             const int mt = q - 3, kw = p.K[mt] / 32, nkb = p.K[mt] / 128;
+            const int tile = r >> 2, l = 8 * (r & 3) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
             const long long hrow = (long long)job.y % p.host_rows;
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + (size_t)r * 128 * kw);
-            const int words = 128 * kw / 16;
-            __syncthreads();  // the previous item's reads of tile_s are done
-            for (int w = threadIdx.x; w < words; w += kCopyThreads) tile_s[w] = src[w];
-            __syncthreads();
-            const uint8_t *ts = reinterpret_cast<const uint8_t *>(tile_s);
-            uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + (size_t)r * nkb * 512);
-            for (int w = threadIdx.x; w < nkb * 32; w += kCopyThreads) {  // 16 bytes = row group l of block kb
-                const int kb = w >> 5, l = w & 31;
-                uint32_t v[4];
+            const uint8_t *src = p.host[q] + (size_t)hrow * p.host_stride[q] + (size_t)tile * 128 * kw;
+            uint8_t *dst = p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + (size_t)tile * nkb * 512;
+            for (int jc = lane; jc < kw / 16; jc += 32) {
+                uint4 v[4];
 #pragma unroll
-                for (int c = 0; c < 4; c++) v[c] = *reinterpret_cast<const uint32_t *>(ts + (size_t)(32 * c + l) * kw + kb * 4);
-                dst[w] = make_uint4(v[0], v[1], v[2], v[3]);
+                for (int c = 0; c < 4; c++) v[c] = *reinterpret_cast<const uint4 *>(src + (size_t)(32 * c + l) * kw + 16 * jc);
+                const uint32_t *w0 = &v[0].x, *w1 = &v[1].x, *w2 = &v[2].x, *w3 = &v[3].x;
+#pragma unroll
+                for (int b = 0; b < 4; b++)
+                    *reinterpret_cast<uint4 *>(dst + (size_t)(4 * jc + b) * 512 + l * 16) = make_uint4(w0[b], w1[b], w2[b], w3[b]);
             }
             continue;
         }
@@ -249,29 +279,55 @@ void launch_pdl_k(const void *fn, dim3 grid, dim3 block, void **args, size_t sme
     CK(cudaLaunchKernelExC(&cfg, fn, args));
 }
 
-void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *status, cudaStream_t st) {
-    if (n < 1 || n > kPlanMaxIds) throw std::runtime_error("routed ids per call out of range for the cache planner");
-    CachePlanParams pp{idx, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->jobs, c->n_jobs, c->expert_bytes, status};
-    void *a1[] = {&pp};
-    launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
+// the copy of the jobs a planner wrote (jobs / n_jobs), on stream st
+void launch_copy(stbl_cache *c, const int2 *jobs, const int *n_jobs, cudaStream_t st, bool pdl) {
     CacheCopyParams cp{};
-    cp.jobs = c->jobs, cp.n_jobs = c->n_jobs, cp.pool = c->pool, cp.slot_bytes = c->slot_bytes;
+    cp.jobs = jobs, cp.n_jobs = n_jobs, cp.pool = c->pool, cp.slot_bytes = c->slot_bytes;
     cp.host_rows = c->host_rows;
     cp.blocked = c->fmt == STBL_FMT_MXFP4;
     const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
-    int smem = 0;
     for (int q = 0; q < 6; q++) {
         cp.piece_bytes[q] = c->piece_bytes[q], cp.piece_off[q] = c->piece_off[q], cp.host_stride[q] = c->host_stride[q];
         cp.host[q] = c->host[q];
         cp.chunks[q] = (int)((c->piece_bytes[q] + kCopyChunk - 1) / kCopyChunk);
         if (cp.blocked && q >= 3) {
             cp.rows[q - 3] = rows[q - 3], cp.K[q - 3] = ks[q - 3];
-            cp.chunks[q] = rows[q - 3] / 128;
-            smem = std::max(smem, 128 * (ks[q - 3] / 32));
+            cp.chunks[q] = rows[q - 3] / 128 * 4;
         }
     }
     void *a2[] = {&cp};
-    launch_pdl_k((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, smem, st);
+    if (pdl) {
+        launch_pdl_k((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, 0, st);
+    } else {
+        CK(cudaLaunchKernel((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, 0, st));
+    }
+}
+
+void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *status, cudaStream_t st) {
+    if (n < 1 || n > kPlanMaxIds) throw std::runtime_error("routed ids per call out of range for the cache planner");
+    // a prefetch copy still running may be filling slots this call reads or evicts
+    if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
+    CachePlanParams pp{idx, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->jobs, c->n_jobs, c->expert_bytes, status,
+                       0, 0, c->pf_flag};
+    void *a1[] = {&pp};
+    launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
+    launch_copy(c, c->jobs, c->n_jobs, st, true);
+}
+
+void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, uint32_t *status, cudaStream_t st,
+                     cudaStream_t copy_st) {
+    if (n < 1 || n > kPlanMaxIds) throw std::runtime_error("prefetch ids out of range for the cache planner");
+    // the previous prefetch's jobs list and slots are reused: its copy must be done
+    if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
+    CachePlanParams pp{ids, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->pf_jobs, c->pf_n_jobs, c->expert_bytes,
+                       status, 1, consider, c->pf_flag};
+    void *a1[] = {&pp};
+    launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
+    CK(cudaEventRecord(c->pf_planned, st));
+    CK(cudaStreamWaitEvent(copy_st, c->pf_planned, 0));
+    launch_copy(c, c->pf_jobs, c->pf_n_jobs, copy_st, false);
+    CK(cudaEventRecord(c->pf_done, copy_st));
+    c->pf_pending = true;
 }
 
 }  // namespace stbl
@@ -357,11 +413,20 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
         CK(cudaMemset(c->owner, 0xFF, sizeof(int) * c->S));
         CK(cudaMalloc(&c->ts, sizeof(unsigned long long) * c->S));
         CK(cudaMemset(c->ts, 0, sizeof(unsigned long long) * c->S));
-        CK(cudaMalloc(&c->ctr, sizeof(unsigned long long) * 4));
-        CK(cudaMemset(c->ctr, 0, sizeof(unsigned long long) * 4));
+        CK(cudaMalloc(&c->ctr, sizeof(unsigned long long) * 8));
+        CK(cudaMemset(c->ctr, 0, sizeof(unsigned long long) * 8));
         CK(cudaMalloc(&c->jobs, sizeof(int2) * c->S));
         CK(cudaMalloc(&c->n_jobs, sizeof(int)));
         CK(cudaMemset(c->n_jobs, 0, sizeof(int)));
+        CK(cudaMalloc(&c->pf_jobs, sizeof(int2) * c->S));
+        CK(cudaMalloc(&c->pf_n_jobs, sizeof(int)));
+        CK(cudaMemset(c->pf_n_jobs, 0, sizeof(int)));
+        CK(cudaMalloc(&c->pf_flag, c->S));
+        CK(cudaMemset(c->pf_flag, 0, c->S));
+        CK(cudaEventCreateWithFlags(&c->pf_done, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&c->pf_planned, cudaEventDisableTiming));
+        CK(cudaMalloc(&c->status, sizeof(uint32_t)));
+        CK(cudaMemset(c->status, 0, sizeof(uint32_t)));
         CK(cudaDeviceSynchronize());
         *out = c;
         return 0;
@@ -402,6 +467,30 @@ int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint
     return 0;
 }
 
+int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_t *used, uint64_t *bytes) {
+    if (!c) return -1;
+    unsigned long long v[8];
+    if (cudaMemcpy(v, c->ctr, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (prefetched) *prefetched = v[5];
+    if (used) *used = v[6];
+    if (bytes) *bytes = v[7];
+    return 0;
+}
+
+int stbl_cache_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, cudaStream_t stream,
+                        cudaStream_t copy_stream) {
+    try {
+        if (!c || !ids) throw std::runtime_error("null argument");
+        if (layer < 0 || layer >= c->L) throw std::runtime_error("layer out of the cache's range");
+        if (consider < 1) throw std::runtime_error("consider must be >= 1");
+        launch_prefetch(c, layer, ids, n, consider, c->status, stream, copy_stream);
+        return 0;
+    } catch (const std::exception &e) {
+        c->err = e.what();
+        return -1;
+    }
+}
+
 int stbl_cache_state(const stbl_cache *c, int *map, int *owner) {
     if (!c) return -1;
     if (map && cudaMemcpy(map, c->map, sizeof(int) * (size_t)c->L * c->E, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
@@ -419,6 +508,12 @@ void stbl_cache_destroy(stbl_cache *c) {
     cudaFree(c->ctr);
     cudaFree(c->jobs);
     cudaFree(c->n_jobs);
+    cudaFree(c->pf_jobs);
+    cudaFree(c->pf_n_jobs);
+    cudaFree(c->pf_flag);
+    cudaFree(c->status);
+    if (c->pf_done) cudaEventDestroy(c->pf_done);
+    if (c->pf_planned) cudaEventDestroy(c->pf_planned);
     delete c;
 }
 

@@ -18,10 +18,20 @@ struct stbl_cache {
     int *map = nullptr;               // [L][E] slot of (layer, expert), -1 when not resident
     int *owner = nullptr;             // [S] l * E + e held by the slot, -1 when free
     unsigned long long *ts = nullptr; // [S] last use (a logical clock), 0 never used
-    unsigned long long *ctr = nullptr;// [0] clock, [1] hits, [2] misses, [3] bytes copied
+    // [0] clock, [1] hits, [2] misses, [3] bytes copied, [4] clock before the last demand call,
+    // [5] experts prefetched, [6] prefetched experts routed to later, [7] bytes prefetched
+    unsigned long long *ctr = nullptr;
     int2 *jobs = nullptr;             // [S] (slot, l * E + e) to fill in the current call
     int *n_jobs = nullptr;
     int copy_ctas = 0;
+    // prefetch (stbl_cache_prefetch): its own jobs list, per-slot "prefetched, not yet routed to"
+    // flags, the event after its copy (the next planner waits for it) and status bits
+    int2 *pf_jobs = nullptr;
+    int *pf_n_jobs = nullptr;
+    unsigned char *pf_flag = nullptr;
+    cudaEvent_t pf_done = nullptr, pf_planned = nullptr;
+    bool pf_pending = false;
+    uint32_t *status = nullptr;
     std::string err;
 };
 
@@ -30,4 +40,8 @@ namespace stbl {
 // = map row `layer`) and the copy of the missing experts from the host store into their slots.
 // idx: device [n] routed expert ids of the call (token-major, top-k order).
 void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *status, cudaStream_t st);
+// Enqueues a prefetch for layer `layer`: the planner (prefetch mode) on st, the copy on copy_st.
+// ids: device [n] guessed expert ids in priority order; the first `consider` distinct ones count.
+void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, uint32_t *status, cudaStream_t st,
+                     cudaStream_t copy_st);
 }  // namespace stbl

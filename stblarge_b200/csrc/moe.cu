@@ -97,6 +97,13 @@ struct stbl_moe {
     bool slots_moved = false;         // some expert reads a slot other than its own id
     stbl_cache *cache = nullptr;      // attached expert cache (stbl_moe_attach_cache), layer cache_layer
     int cache_layer = 0;
+    // shadow next-layer prefetch (stbl_moe_attach_prefetch): the next layer's router on this layer's
+    // input, its top pf_predict experts per token prefetched into the cache (pf_consider counted)
+    const stbl_moe *pf_next = nullptr;
+    int pf_predict = 0, pf_consider = 0;
+    cudaStream_t pf_stream = nullptr;
+    void *pf_ws = nullptr;
+    RouterParams pf_r{};              // the shadow router's buffers (inputs and routing set per call)
     long long w_stride[3] = {0, 0, 0}, s_stride[3] = {0, 0, 0};  // bytes between slots
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
@@ -687,6 +694,20 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         // bring the call's routed experts into the cache: plan (hits, LRU victims), copy the misses
         launch_cache(m->cache, m->cache_layer, m->idx, T * m->K, m->status, st);
         launches += 2;
+        if (m->pf_next) {
+            // the next layer's router on this layer's input (stbl/model.cu:432-436), then its guesses
+            // into the cache: planned here, copied on the prefetch stream beside this call's experts
+            const stbl_moe *nx = m->pf_next;
+            RouterParams sr = m->pf_r;
+            sr.x = r.x, sr.x_pre = r.x_pre, sr.norm_w = r.norm_w, sr.norm_eps = r.norm_eps;
+            sr.W = nx->d.router_w, sr.bias = nx->d.router_bias;
+            sr.T = T, sr.E = nx->E, sr.H = nx->H, sr.topk = m->pf_predict, sr.n_groups = nx->d.n_groups;
+            sr.topk_groups = nx->d.topk_groups, sr.score_fn = nx->d.score_fn, sr.route_scale = nx->d.route_scale;
+            sr.ksplit = nx->ksplit;
+            CK(launch_router(sr, st, true));
+            launch_prefetch(m->cache, nx->cache_layer, sr.idx, T * m->pf_predict, m->pf_consider, m->status, st, m->pf_stream);
+            launches += 4;
+        }
     }
     if (m->timing) CK(cudaEventRecord(tc.ev[1], st));
 
@@ -904,6 +925,55 @@ int stbl_moe_forward_routed(stbl_moe *m, const void *x_bf16, int T, const int *i
     }
 }
 
+int stbl_moe_attach_prefetch(stbl_moe *m, const stbl_moe *next, int n_predict, int consider, cudaStream_t copy_stream) {
+    try {
+        if (m->pf_ws) {
+            CK(cudaDeviceSynchronize());
+            CK(cudaFree(m->pf_ws));
+            m->pf_ws = nullptr;
+        }
+        m->pf_next = nullptr;
+        if (!next) return 0;
+        if (!m->cache || next->cache != m->cache) throw std::runtime_error("both layers must be attached to the same expert cache");
+        if (next->E != m->E || next->H != m->H) throw std::runtime_error("the next layer's shape differs");
+        if (n_predict < 1 || n_predict > 16 || n_predict > next->E) throw std::runtime_error("n_predict must be in 1..16 and <= n_experts");
+        if (consider < 1) throw std::runtime_error("consider must be >= 1");
+        if (next->d.n_groups > 1 && next->d.topk_groups < next->d.n_groups &&
+            next->d.topk_groups * (next->E / next->d.n_groups) < n_predict)
+            throw std::runtime_error("the next layer's kept groups hold fewer than n_predict experts");
+        const int T = m->Tmax, E = m->E, H = m->H, K = n_predict;
+        const size_t bytes = ((size_t)T * E * 4 + 255) + 2 * ((size_t)T * K * 4 + 255) + 2 * ((size_t)(E + 1) * 4 + 255) +
+                             ((size_t)T * K * 4 + 255) + ((size_t)T * (K + 1) * sizeof(Chunk) + 255) + 2 * 256 +
+                             ((size_t)T * H + 255) + ((size_t)T * (H / 32) * 4 + 255) + ((size_t)E * 4 + 255) +
+                             ((size_t)E * ((T + 31) / 32) * 4 + 255) + 4096;
+        CK(cudaMalloc(&m->pf_ws, bytes));
+        char *p = static_cast<char *>(m->pf_ws);
+        RouterParams &r = m->pf_r;
+        r = RouterParams{};
+        r.scores = carve<float>(p, (size_t)T * E);
+        r.idx = carve<int>(p, (size_t)T * K);
+        r.wts = carve<float>(p, (size_t)T * K);
+        r.counts = carve<int>(p, E + 1);
+        r.offsets = carve<int>(p, E + 1);
+        r.perm = carve<int>(p, (size_t)T * K);
+        r.chunks = carve<Chunk>(p, (size_t)T * (K + 1));
+        r.n_chunks = carve<int>(p, 4);
+        r.status = m->status;
+        r.xq_a = r.xq_b = carve<uint8_t>(p, (size_t)T * H);
+        r.xs_a = r.xs_b = carve<float>(p, (size_t)T * (H / 32));
+        r.blk_a = r.blk_b = 128, r.pow2_a = r.pow2_b = 0;
+        r.sel_cnt = carve<int>(p, E);
+        r.sel_bm = carve<uint32_t>(p, (size_t)E * ((T + 31) / 32));
+        r.sel_ticket = carve<unsigned int>(p, 4);
+        r.has_shared = 0, r.nt_routed = 16, r.nt_shared = 16;
+        m->pf_next = next, m->pf_predict = n_predict, m->pf_consider = consider, m->pf_stream = copy_stream;
+        return 0;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
 int stbl_moe_attach_cache(stbl_moe *m, stbl_cache *c, int layer) {
     try {
         if (!c) throw std::runtime_error("null cache");
@@ -1054,6 +1124,7 @@ void stbl_moe_destroy(stbl_moe *m) {
     for (auto &t : m->event_pool)
         for (auto e : t.ev) cudaEventDestroy(e);
     if (m->ws) cudaFree(m->ws);
+    if (m->pf_ws) cudaFree(m->pf_ws);
     if (m->sf_own) cudaFree(m->sf_own);
     if (m->sf_shared) cudaFree(m->sf_shared);
     for (int d = 0; d < m->ep_n; d++)

@@ -63,6 +63,9 @@ SIGNATURES = {
     "stbl_cache_info": (I, [P, ctypes.POINTER(I), ctypes.POINTER(U64)]),
     "stbl_cache_state": (I, [P, P, P]),
     "stbl_cache_destroy": (None, [P]),
+    "stbl_cache_prefetch": (I, [P, I, P, I, I, P, P]),
+    "stbl_cache_prefetch_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "stbl_moe_attach_prefetch": (I, [P, P, I, I, P]),
     "stbl_mxfp4_from_gguf": (I, [P, I, I, P, P, P]),
     "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),
     "stbl_moe_set_timing": (I, [P, I]),

@@ -107,6 +107,17 @@ class MoELayer:
                                                      ctypes.c_void_p(st.cuda_stream)), "stbl_moe_forward_routed")
         return out
 
+    def attach_prefetch(self, next_layer, n_predict, consider, copy_stream):
+        """Each call also runs next_layer's router on this call's input and prefetches its top n_predict
+        experts per token (the first `consider` distinct ones) into the shared expert cache, copied on
+        copy_stream (a torch.cuda.Stream) beside this call's experts (stbl_moe_attach_prefetch).
+        next_layer None stops it."""
+        self._pf = (next_layer, copy_stream)  # keep both alive while attached
+        self._check(self.lib.stbl_moe_attach_prefetch(self.handle, next_layer.handle if next_layer is not None else None,
+                                                      n_predict, consider,
+                                                      ctypes.c_void_p(copy_stream.cuda_stream if copy_stream is not None else 0)),
+                    "stbl_moe_attach_prefetch")
+
     def forward_block(self, x_pre, norm_w, eps, res, post, comb, out=None, stream=None):
         """The layer inside its block (stbl_moe_forward_block; stbl/model.cu:803-805): RMSNorm of x_pre
         (cuda float32 [T, hidden]) with norm_w (float32 [hidden]) and eps before it, the hyper-connection

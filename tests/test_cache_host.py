@@ -23,8 +23,19 @@ class ClockPlanner:
         self.map = np.full((n_layers, n_experts), -1, np.int64)
         self.owner = np.full(slots, -1, np.int64)
         self.ts = np.zeros(slots, np.int64)
-        self.clock = 0
-        self.hits = self.misses = 0
+        self.pf = np.zeros(slots, bool)
+        self.clock = self.last_base = 0
+        self.hits = self.misses = self.prefetched = self.pf_used = 0
+
+    def _place(self, layer, e, t):
+        key = self.ts * (1 << 20) + np.arange(self.S)
+        s = int(np.argmin(key))
+        if self.owner[s] >= 0:
+            self.map.reshape(-1)[self.owner[s]] = -1
+        self.owner[s] = layer * self.E + e
+        self.map[layer, e] = s
+        self.ts[s] = t
+        return s
 
     def call(self, layer, ids):
         u = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))
@@ -34,19 +45,32 @@ class ClockPlanner:
             if row[e] >= 0:
                 self.ts[row[e]] = base + 1 + nu + i
                 self.hits += 1
+                if self.pf[row[e]]:
+                    self.pf[row[e]] = False
+                    self.pf_used += 1
         for i, e in enumerate(u):
             if row[e] >= 0:
                 continue
-            key = self.ts * (1 << 20) + np.arange(self.S)
-            s = int(np.argmin(key))
-            assert self.ts[s] <= base, "every slot is in use by this call"
-            if self.owner[s] >= 0:
-                self.map.reshape(-1)[self.owner[s]] = -1
-            self.owner[s] = layer * self.E + e
-            row[e] = s
-            self.ts[s] = base + 1 + nu + i
+            assert self.ts.min() <= base, "every slot is in use by this call"
+            s = self._place(layer, e, base + 1 + nu + i)
+            self.pf[s] = False
             self.misses += 1
         self.clock = base + 1 + 2 * nu
+        self.last_base = base
+
+    def prefetch(self, layer, ids, consider):
+        """the planner's prefetch mode: cached guesses untouched, no slot newer than the last call's start"""
+        u = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))[:consider]
+        base = self.clock
+        for i, e in enumerate(u):
+            if self.map[layer, e] >= 0:
+                continue
+            if self.ts.min() > self.last_base:
+                break
+            s = self._place(layer, e, base + 1 + i)
+            self.pf[s] = True
+            self.prefetched += 1
+        self.clock = base + 1 + len(u)
 
 
 @pytest.mark.parametrize("slots,T", [(8, 1), (12, 2), (40, 4), (64, 1)])
@@ -66,6 +90,34 @@ def test_clock_planner_equals_reference_lru(slots, T):
         assert np.array_equal(owner, dev.owner), f"call {call}: slot owners differ"
         assert (ref.hits, ref.misses) == (dev.hits, dev.misses)
     assert ref.hits > 0 and ref.misses > slots
+
+
+@pytest.mark.parametrize("slots,T,consider", [(8, 1, 3), (12, 2, 4), (40, 4, 8), (6, 1, 8)])
+def test_clock_planner_with_prefetch_equals_reference_lru(slots, T, consider):
+    # the shadow next-layer prefetch between calls: guesses for the next layer, some right, some wrong
+    L, E, K = 4, 32, 4
+    rng = np.random.default_rng(slots * 7 + T + consider)
+    ref, dev = O.LruExpertCache(slots), ClockPlanner(L, E, slots)
+    p = np.linspace(2.0, 0.2, E)
+    p /= p.sum()
+    nxt = None
+    for call in range(400):
+        layer = call % L
+        if nxt is not None and rng.random() < 0.7:
+            ids = nxt  # the guess was right (the first tokens' experts)
+        else:
+            ids = np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(T)])
+        ref.call(layer, ids)
+        dev.call(layer, ids)
+        nxt = np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(T)])
+        guess = np.concatenate([nxt.reshape(-1), rng.choice(E, 3)])
+        ref.prefetch((layer + 1) % L, guess, consider)
+        dev.prefetch((layer + 1) % L, guess, consider)
+        m, owner = ref.state(L, E)
+        assert np.array_equal(m, dev.map), f"call {call}: residency differs"
+        assert np.array_equal(owner, dev.owner), f"call {call}: slot owners differ"
+        assert (ref.hits, ref.misses, ref.prefetched, ref.pf_used) == (dev.hits, dev.misses, dev.prefetched, dev.pf_used)
+    assert ref.prefetched > 0 and ref.pf_used > 0
 
 
 def test_reference_lru_fills_slots_in_order_then_evicts_least_recent():

@@ -67,3 +67,55 @@ def test_fused_block_equals_the_reference_sequence(cfg):
         # the routes of the fused call are those of the unfused call's layer input
         assert layer.status() == 0
     layer.close()
+
+
+@pytest.mark.skipif(not os.path.exists(REF_SO), reason="the unfused sequence uses the reference's kernels (oracle/_ref)")
+@pytest.mark.parametrize("T", [1, 16])
+def test_fused_block_saves_the_separate_launches(T, capsys):
+    """Device time per block call, L2 flushed: the fused call against the reference's sequence of separate
+    launches around this layer (k_rms_norm, the bf16 conversion the layer's interface takes, the layer,
+    the fp32 conversion, k_hc_post per token), on a full-shape FP8 layer with 16 experts."""
+    import dataclasses
+
+    from stblarge_b200.config import CFG2
+    cfg = dataclasses.replace(CFG2, n_experts=16, n_groups=4, topk_groups=2)
+    layer = MoELayer(cfg, synth.device_layer(cfg), max_tokens=16)
+    ref = ctypes.CDLL(REF_SO)
+    hc, eps = 4, 1e-6
+    x_pre, norm_w, res, post, comb = block_inputs(cfg, T, hc, 7)
+    xn, h = torch.empty_like(x_pre), torch.empty(T, hc, cfg.hidden, device="cuda")
+    xb = torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty_like(xb)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    st = P(torch.cuda.current_stream().cuda_stream)
+
+    def unfused():
+        ref.stbl_rms_norm(P(xn.data_ptr()), P(x_pre.data_ptr()), P(norm_w.data_ptr()), I(T), I(cfg.hidden), F(eps), st)
+        xb.copy_(xn)
+        layer(xb, y)
+        yf = y.float()
+        for t in range(T):
+            ref.stbl_hc_post(P(h[t].data_ptr()), P(yf[t].data_ptr()), P(res[t].data_ptr()), P(post[t].data_ptr()),
+                             P(comb[t].data_ptr()), I(hc), I(cfg.hidden), st)
+
+    def fused():
+        layer.forward_block(x_pre, norm_w, eps, res, post, comb, out=h)
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in ev:
+            flush.zero_()
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return float(np.mean([a.elapsed_time(b) for a, b in ev])) * 1e3
+
+    t_unfused, t_fused = timed(unfused), timed(fused)
+    with capsys.disabled():
+        print(f"\nblock call, FP8 16 experts, T={T}: unfused {t_unfused:.1f} us, fused {t_fused:.1f} us")
+    assert t_fused < t_unfused
+    assert layer.status() == 0
+    layer.close()

@@ -135,3 +135,45 @@ def test_cached_layer_with_forced_routes(cfg):
         assert layer.status() == 0
         layer.close()
     cache.close()
+
+
+@pytest.mark.parametrize("cfg,S", [(CFG1, 12), (CFG1_FP4, 12), (CFG1_FP4, 8)], ids=["fp8", "mxfp4", "mxfp4_small"])
+def test_shadow_prefetch_matches_resident_layers_and_reference_lru(cfg, S):
+    # layer l runs layer l+1's router on its own input and prefetches the top guesses for l+1, copied on
+    # a second stream beside l's experts (stbl_moe_attach_prefetch); the next call waits for that copy
+    L, E, T, n_predict, consider = 3, cfg.n_experts, 2, 4, 3
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, S, store)
+    resident = [synth.device_layer(cfg, seed_base=1000 + l * E) for l in range(L)]
+    plain = [MoELayer(cfg, resident[l], max_tokens=T) for l in range(L)]
+    cached = [MoELayer(cfg, resident[l], max_tokens=T, cache=(cache, l)) for l in range(L)]
+    side = torch.cuda.Stream()
+    for l in range(L - 1):
+        cached[l].attach_prefetch(cached[l + 1], n_predict, consider, side)
+    lru = O.LruExpertCache(S)
+    for step in range(6):
+        x_bits = synth.make_x(cfg.hidden, T, seed=900 + step)
+        x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+        for l in range(L):  # the same input for every layer: the next layer's guesses are its routes
+            y_plain, y = plain[l](x), cached[l](x)
+            torch.cuda.synchronize()
+            assert torch.equal(y.view(torch.int16), y_plain.view(torch.int16)), f"step {step} layer {l}"
+            lru.call(l, cached[l].last_route()["idx"])
+            if l + 1 < L:
+                nw = resident[l + 1]
+                lg = O.router_logits(nw["router_w"].cpu().numpy(), x_bits)
+                _, guess, _ = O.router_select(lg, nw["router_bias"].cpu().numpy(), n_predict, cfg.n_groups, cfg.topk_groups,
+                                              cfg.score_fn, cfg.route_scale)
+                lru.prefetch(l + 1, guess, consider)
+            mp, owner = cache.state()
+            emp, eowner = lru.state(L, E)
+            assert np.array_equal(mp, emp), f"step {step} layer {l}: residency map differs"
+            assert np.array_equal(owner, eowner), f"step {step} layer {l}: slot owners differ"
+            st, pf = cache.stats(), cache.prefetch_stats()
+            assert (st["hits"], st["misses"]) == (lru.hits, lru.misses)
+            assert (pf["prefetched"], pf["used"]) == (lru.prefetched, lru.pf_used)
+    assert lru.prefetched > 0 and lru.pf_used > 0
+    for layer in cached + plain:
+        assert layer.status() == 0
+        layer.close()
+    cache.close()
