@@ -8,8 +8,11 @@
 // accumulator once.  The numerics equal the reference's fp32 sum of dequantized products up to
 // summation order (ref/kernel.py:94-102 fp4_gemm).
 //
-// Items are 128 output rows x one chunk of up to 16 token columns; for the up product an item holds
-// 128 gate rows AND the matching 128 up rows (two accumulators), so SwiGLU reads both from TMEM.
+// Items are two 128-row weight tiles x one chunk of up to 16 token columns, two accumulators: for the
+// up product 128 gate rows AND the matching 128 up rows, so SwiGLU reads both from TMEM; for the down
+// product 256 consecutive rows of W2.  Two independent accumulators per K step keep the tensor pipe
+// busy: measured on one SM, a 128-K block of two matrices (3 scale copies + 8 MMAs) takes about as
+// long as a block of one (2 copies + 4 MMAs).
 // Stream-K over (item, 256-K unit) pairs, one persistent CTA per SM.  A pipeline stage is one
 // 256-K unit: each weight matrix arrives as ONE 4-D TMA box of 128 rows x 2 K blocks (128 contiguous
 // bytes of packed codes per row and op; single-K-block boxes read 64-byte row pieces, which streams
@@ -45,11 +48,11 @@ constexpr int kT4PartialCols = 32;   // floats per row in the stream-K partial b
 
 template <bool UP>
 struct T4 {
-    static constexpr int nA = UP ? 2 : 1;                  // weight matrices per item
+    static constexpr int nA = 2;                           // weight tiles per item (up: gate, up; down: 2 x 128 rows)
     static constexpr int A = nA * kT4Kb * kT4ATile;        // [m][kb][128 rows][128 B]
     static constexpr int B = kT4Kb * kT4BTile;             // [kb][16 rows][128 B]
     static constexpr int SF = (nA + 1) * kT4Kb * 512;      // [m | B][kb][512 B]
-    static constexpr int stage = A + B + SF;               // up 71 KB, down 38 KB
+    static constexpr int stage = A + B + SF;               // 71 KB
     static constexpr int NV = nA * kTcN;                   // accumulator columns per item
 };
 static_assert(T4<true>::stage % 1024 == 0 && T4<false>::stage % 1024 == 0, "stages must keep 1 KB alignment");
@@ -89,9 +92,12 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;     // reduction length
-    const int rows = UP ? p.I : p.H;  // output rows per matrix
+    const int rows = UP ? p.I : p.H;  // output rows per matrix (down: H / 256 items of 2 tiles)
     const int nu = K / 256;               // 256-K units per item
-    const int tiles = rows / 128;
+    const int tiles = UP ? rows / 128 : rows / 256;
+    // 128-row weight tile of matrix slot m of item tile t: up, gate (m 0) and up (m 1) rows of tile t;
+    // down, the two halves of W2 rows [256 t, 256 t + 256)
+    auto tile_row = [&](int t, int m) { return UP ? t : 2 * t + m; };
     unsigned char *stages = smem;                                                   // [nst][A | B | SF]
     int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][16] by column
     float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);                  // [2][16]
@@ -175,8 +181,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * kTcN * 16);
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
-                        tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile * 128, kT4Kb * u, z,
-                                    &full[s]);
+                        tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile_row(tile, m) * 128,
+                                    kT4Kb * u, z, &full[s]);
                     tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
                     // scales: the unit's two 512-byte weight-scale blocks per matrix are adjacent; the
                     // activation scales are the chunk's 16 rows of 16 bytes per K block
@@ -184,7 +190,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     for (int m = 0; m < S::nA; m++)
                         bulk_g2s(sf + m * kT4Kb * 512,
                                  (shared ? p.sf_s[m] : p.sf_a[m] + (size_t)z * p.sf_a_stride) +
-                                     ((size_t)tile * nkb + kT4Kb * u) * 512,
+                                     ((size_t)tile_row(tile, m) * nkb + kT4Kb * u) * 512,
                                  kT4Kb * 512,
                                  &full[s]);
 #pragma unroll
@@ -313,7 +319,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
             if (ok) {
                 tc_fence_after();
                 tmem_ld16(tl + (uint32_t)(acc_i * S::NV), va);
-                if (UP) tmem_ld16(tl + (uint32_t)(acc_i * S::NV + kTcN), vb);
+                tmem_ld16(tl + (uint32_t)(acc_i * S::NV + kTcN), vb);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc_i]);
             }
@@ -330,10 +336,9 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 float4 *dst = reinterpret_cast<float4 *>(prow);
 #pragma unroll
                 for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]);
-                if (UP)
 #pragma unroll
-                    for (int j = 0; j < kTcN / 4; j++)
-                        dst[kTcN / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
+                for (int j = 0; j < kTcN / 4; j++)
+                    dst[kTcN / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
                 if (et == 0) flag_release(p.flags + cta, p.seq);
@@ -353,12 +358,11 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     const float4 v = __ldcg(src + j);
                     va[4 * j] += v.x, va[4 * j + 1] += v.y, va[4 * j + 2] += v.z, va[4 * j + 3] += v.w;
                 }
-                if (UP)
 #pragma unroll
-                    for (int j = 0; j < kTcN / 4; j++) {
-                        const float4 v = __ldcg(src + kTcN / 4 + j);
-                        vb[4 * j] += v.x, vb[4 * j + 1] += v.y, vb[4 * j + 2] += v.z, vb[4 * j + 3] += v.w;
-                    }
+                for (int j = 0; j < kTcN / 4; j++) {
+                    const float4 v = __ldcg(src + kTcN / 4 + j);
+                    vb[4 * j] += v.x, vb[4 * j + 1] += v.y, vb[4 * j + 2] += v.z, vb[4 * j + 3] += v.w;
+                }
             }
             if (!got) {
                 abort_flag = 1;
@@ -391,9 +395,15 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     if (lane == 0) p.he8[((size_t)tile * p.he8_rows + dst) * 16 + (warp & 3)] = (uint8_t)(__float_as_uint(s) >> 23);
                 }
             } else {
+                // rows 256 tile + row (va) and 256 tile + 128 + row (vb) of W2's output
+                const int r0 = tile * 256 + row;
 #pragma unroll
                 for (int j = 0; j < kTcN; j++)
-                    if (j < ch.n) (ch.e == p.E ? p.sh : p.eo)[(size_t)cdst[j] * p.H + r] = f32_to_bf16_bits(va[j]);
+                    if (j < ch.n) {
+                        uint16_t *o = (ch.e == p.E ? p.sh : p.eo) + (size_t)cdst[j] * p.H;
+                        o[r0] = f32_to_bf16_bits(va[j]);
+                        o[r0 + 128] = f32_to_bf16_bits(vb[j]);
+                    }
             }
             if (it + 1 < hi) park(buf ^ 1);
         }
@@ -438,7 +448,7 @@ const void *expert_tc4_kernel_ptr(bool up) {
 
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
 int expert_tc4_smem_bytes(bool up, int nst) {
-    const int stage = up ? T4<true>::stage : T4<false>::stage;
+    const int stage = up ? T4<true>::stage : T4<false>::stage;  // equal: two 128-row tiles per item
     return nst * stage + 4 * (4 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
 }
 
