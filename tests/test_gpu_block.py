@@ -119,3 +119,30 @@ def test_fused_block_saves_the_separate_launches(T, capsys):
     assert t_fused < t_unfused
     assert layer.status() == 0
     layer.close()
+
+
+def test_fused_block_on_cached_layers_with_prefetch():
+    # the block form on layers whose experts live in a cache fed from a host store, with the shadow
+    # next-layer prefetch attached: the same bits as the block form on resident layers
+    from stblarge_b200.cache import ExpertCache, host_store
+    cfg, L, S, T, hc, eps = CFG1_REF, 2, 10, 2, 4, 1e-6
+    E = cfg.n_experts
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, S, store)
+    resident = [synth.device_layer(cfg, seed_base=1000 + l * E) for l in range(L)]
+    plain = [MoELayer(cfg, resident[l], max_tokens=T) for l in range(L)]
+    cached = [MoELayer(cfg, resident[l], max_tokens=T, cache=(cache, l)) for l in range(L)]
+    side = torch.cuda.Stream()
+    cached[0].attach_prefetch(cached[1], 4, 3, side)
+    for step in range(4):
+        x_pre, norm_w, res, post, comb = block_inputs(cfg, T, hc, 50 + step)
+        for l in range(L):
+            want = plain[l].forward_block(x_pre, norm_w, eps, res, post, comb)
+            got = cached[l].forward_block(x_pre, norm_w, eps, res, post, comb)
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int32), want.view(torch.int32)), f"step {step} layer {l}"
+    assert cache.prefetch_stats()["prefetched"] > 0
+    for layer in cached + plain:
+        assert layer.status() == 0
+        layer.close()
+    cache.close()
