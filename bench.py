@@ -70,6 +70,72 @@ def up_bytes(cfg, n_distinct):
     return 2 * (n_distinct * mat(cfg.routed_fmt) + mat(cfg.shared_fmt))
 
 
+class NvmlClockSampler:
+    """SM clock and clock-event (throttle) reasons of the GPU, read through NVML from a thread every
+    `period` seconds while the timed region runs (the region can be a few tens of milliseconds, shorter
+    than nvidia-smi's start-up).  Reads only; nothing on the GPU is changed.  start() returns once the
+    first sample is taken."""
+
+    def __init__(self, cuda_index, period=0.002):
+        import threading
+
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        # the CUDA device's NVML handle (CUDA_VISIBLE_DEVICES may renumber): by UUID, else by index
+        self.h = None
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+        except Exception:
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+        self.period = period
+        self.samples, self.reasons = [], 0
+        self.stop_ev, self.first = threading.Event(), threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            self.first.set()
+            time.sleep(self.period)
+
+    def start(self):
+        self.thread.start()
+        self.first.wait(timeout=5)
+
+    def stop(self):
+        self.stop_ev.set()
+        self.thread.join(timeout=5)
+        nv = self.nv
+        try:
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+        except Exception:
+            mx = None
+        names = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted(n for n, bit in names.items() if self.reasons & bit)
+        sm = [float(v) for v in self.samples]
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": reasons, "source": "nvml"}
+
+
+def clock_sampler(cuda_index):
+    """NVML sampling in-process when the bindings load, else the nvidia-smi subprocess."""
+    try:
+        return NvmlClockSampler(cuda_index)
+    except Exception:
+        return ClockSampler(cuda_index)
+
+
 class ClockSampler:
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
@@ -162,11 +228,16 @@ def run_streamed(args, rank, world):
     if rank != 0:
         return
     from stblarge_b200 import streamed
-    clocks = ClockSampler(0)
-    clocks.start()
+    clocks = clock_sampler(0)
+    ck = {}
+
+    def on_timed(begin):  # sample the clocks over the timed steps only (the store build leaves the GPU idle)
+        if begin:
+            clocks.start()
+        else:
+            ck.update(clocks.stop())
     r = streamed.run(layers=58, cache_gb=40.0, store_experts=1024, steps=args.steps, warmup=args.warmup,
-                     log=lambda m: print(m, file=sys.stderr, flush=True))
-    ck = clocks.stop()
+                     log=lambda m: print(m, file=sys.stderr, flush=True), on_timed=on_timed)
     line = {
         "metric": "streamed decode tokens/s (58 MXFP4 layers, host-streamed experts, 40 GB GPU expert cache)",
         "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -267,7 +338,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
+    sampler = clock_sampler(local)
     sampler.start()
     layer.timing()
     layer.set_timing(True)

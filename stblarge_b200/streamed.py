@@ -46,7 +46,9 @@ def route_trace(E, K, L, steps, reuse=0.6, zipf_s=1.0, seed=5):
     return out
 
 
-def run(layers=58, cache_gb=40.0, store_experts=1024, steps=64, warmup=3, seed=5, log=print):
+def run(layers=58, cache_gb=40.0, store_experts=1024, steps=64, warmup=3, seed=5, log=print, on_timed=None):
+    """on_timed(True / False): called right before the timed steps are enqueued and after they finished
+    (a clock sampler's start and stop)."""
     import torch
 
     from .cache import ExpertCache, host_store
@@ -80,11 +82,15 @@ def run(layers=58, cache_gb=40.0, store_experts=1024, steps=64, warmup=3, seed=5
     torch.cuda.synchronize()
     s0 = cache.stats()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if on_timed:
+        on_timed(True)
     for i in range(steps):
         ev[i][0].record()
         token(warmup + i)
         ev[i][1].record()
     torch.cuda.synchronize()
+    if on_timed:
+        on_timed(False)
     s1 = cache.stats()
     ms = [a.elapsed_time(b) for a, b in ev]
     total_s = sum(ms) / 1e3
