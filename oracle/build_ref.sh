@@ -7,8 +7,8 @@
 # Needs the reference tree (present where the repository is developed, absent on GPU boxes, which use
 # the prebuilt files).
 set -euo pipefail
-REF=${STBL_REFERENCE:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+REF=${STBL_REFERENCE:-$HERE/../../reference}   # default: the reference tree next to the repository
 if [ ! -f "$REF/stbl/kernels.cu" ]; then
     echo "reference tree not found at $REF; keeping the prebuilt _ref/ (if any)" >&2
     exit 0

@@ -9,7 +9,7 @@ tools/stbl_gguf.py helpers (pack_string, kv_*, tensor_header, align, qtype_nbyte
 reference tree; the content is seeded numpy and is rebuilt by `content()` without the reference,
 which is what the tests compare the file with.
 
-    python tests/golden/make_gguf_file.py        (needs the reference tree at /root/reference)
+    python tests/golden/make_gguf_file.py        (needs the reference tree: STBL_REFERENCE, else ../reference)
 """
 
 import importlib.util
@@ -54,7 +54,7 @@ def content():
 
 
 def main():
-    ref = os.environ.get("STBL_REFERENCE", "/root/reference")
+    ref = os.environ.get("STBL_REFERENCE", os.path.join(HERE, "..", "..", "..", "reference"))
     spec = importlib.util.spec_from_file_location("stbl_gguf", os.path.join(ref, "tools", "stbl_gguf.py"))
     G = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(G)

@@ -2,7 +2,7 @@
 
 Run where the reference tree is present:
 
-    python tests/golden/make_gguf_golden.py [--reference /root/reference]
+    python tests/golden/make_gguf_golden.py [--reference <reference tree>]   (default: STBL_REFERENCE, else ../reference)
 
 Quantizes seeded weights to MXFP4 in the official layout with the reference's ref/kernel.py
 (fp4_act_quant, E8M0 scales), then packs them into the reference engine's 17-byte GGUF blocks with
@@ -35,7 +35,7 @@ class _Db:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("STBL_REFERENCE", os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "..", "reference")))
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.reference, "ref"))
     sys.path.insert(0, os.path.join(a.reference, "tools"))

@@ -3,7 +3,7 @@
 Run where the reference tree is present (it imports ref/kernel.py, the reference's own torch
 stand-ins for its quantizers and GEMMs):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference tree>]   (default: STBL_REFERENCE, else ../reference)
 
 Writes small .npz fixtures next to this file.  The tests read only the fixtures; nothing at test
 time touches the reference tree.  Layer weights are not stored: they are regenerated from fixed
@@ -187,7 +187,7 @@ def layer_case(K, cfg, T, seed_x):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("STBL_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("STBL_REFERENCE", os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "..", "reference")))
     args = ap.parse_args()
     K = load_reference(args.reference)
     torch.set_num_threads(1)  # reproducible summation inside the torch GEMMs
