@@ -4,10 +4,10 @@
 
 namespace stbl {
 
-template <bool UP>
+template <bool UP, bool T2>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p,
                                                                   int nst) {
-    tc8_body<UP>(maps, p, nst, blockIdx.x, gridDim.x);
+    tc8_body<UP, T2>(maps, p, nst, blockIdx.x, gridDim.x);
 }
 
 // x codes and scales of every position (routed assignments in dispatch order, then the shared
@@ -69,19 +69,22 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
 
 const void *hquant_kernel_ptr() { return (const void *)hquant_kernel; }
 
-template __global__ void expert_tc_kernel<true>(const __grid_constant__ TcMaps, TcParams, int);
-template __global__ void expert_tc_kernel<false>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<true, false>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<false, false>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<false, true>(const __grid_constant__ TcMaps, TcParams, int);
 
-const void *expert_tc_kernel_ptr(bool up) {
-    return up ? (const void *)expert_tc_kernel<true> : (const void *)expert_tc_kernel<false>;
+// two: the down product with items of two 128-row tiles (not with expert parallelism)
+const void *expert_tc_kernel_ptr(bool up, bool two) {
+    if (up) return (const void *)expert_tc_kernel<true, false>;
+    return two ? (const void *)expert_tc_kernel<false, true> : (const void *)expert_tc_kernel<false, false>;
 }
 
 const void *gather_kernel_ptr() { return (const void *)gather_kernel; }
 
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
-int expert_tc_smem_bytes(bool up, int H, int I, int nst) {
+int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two) {
     const int K = up ? H : I, nkb = K / 128;
-    return nst * kStage + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 6 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
+    return nst * (two && !up ? kStage2 : kStage) + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 6 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
            8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
 }
 

@@ -20,7 +20,7 @@
 
 namespace stbl {
 const void *combine_kernel_ptr();                 // combine.cu
-const void *expert_tc_kernel_ptr(bool up);        // experts_tc.cu
+const void *expert_tc_kernel_ptr(bool up, bool two);  // experts_tc.cu
 const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
 int expert_tc4_smem_bytes(bool up, int nst);
 int expert_tc4_partial_cols();
@@ -28,7 +28,7 @@ cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *
                              int z0, int nz, int rps, cudaStream_t st);
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
-int expert_tc_smem_bytes(bool up, int H, int I, int nst);
+int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two);
 }  // namespace stbl
 
 using namespace stbl;
@@ -86,7 +86,7 @@ struct stbl_moe {
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     uint32_t *status = nullptr;
-    float *tc_partial = nullptr;      // split-item partial sums: FP8 body [sms][128][16], then MXFP4 [sms][128][32]
+    float *tc_partial = nullptr;      // split-item partial sums: FP8 body [sms][128][16 or 32 (two-tile down)], then MXFP4 [sms][128][32]
     unsigned int *tc_flags = nullptr; // [2][sms] launch number whose partial a CTA slot holds (FP8, MXFP4 bodies)
     unsigned int tc_seq = 0;
     // expert slots: routed expert e reads slot slot[e] of the strided weight arrays (an expert cache
@@ -108,6 +108,7 @@ struct stbl_moe {
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
+    int tc_nst_down2 = 0, tc_smem_down2 = 0;  // the down kernel with two-tile items (single GPU, T >= 4)
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_bs = false;           // routed experts MXFP4 or FP8-e8m0: the block-scaled tensor-core kernels
     bool shared_bs = false;           // shared expert FP8-e8m0: handled by the block-scaled kernels too
@@ -363,7 +364,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
-        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 48);
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 64);
         m->tc_flags = carve<unsigned int>(p, 2 * m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
@@ -469,19 +470,22 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->bmap4_xa = act_map2(m->xq_a, H, Tpad);
         m->bmap4_xpos = act_map2(m->xq_pos, H, npos + 16);
         m->bmap4_hq = act_map2(m->hq, I, npos + 16);
-        auto pick = [&](bool up, int &nst, int &smem) {
+        // stages: at least kTcBatch (4: the producer requests K blocks four at a time and first waits
+        // for four free stages), at most 8 of one tile (more outstanding requests only lengthen the
+        // DRAM queues, measured) or 6 of two
+        auto pick = [&](bool up, bool two, int &nst, int &smem) {
             cudaFuncAttributes fa{};
-            CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up)));
-            // at most 8 stages (two batches of 4 K blocks in flight): measured best on B200, more
-            // outstanding requests only lengthen the DRAM queues
-            for (nst = 8; nst >= 4; nst--)
-                if (expert_tc_smem_bytes(up, H, I, nst) + (int)fa.sharedSizeBytes <= max_smem) break;
-            if (nst < 4) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
-            smem = expert_tc_smem_bytes(up, H, I, nst);
-            CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up, two)));
+            const int nmax = two ? 6 : 8, nmin = 4;
+            for (nst = nmax; nst >= nmin; nst--)
+                if (expert_tc_smem_bytes(up, H, I, nst, two) + (int)fa.sharedSizeBytes <= max_smem) break;
+            if (nst < nmin) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
+            smem = expert_tc_smem_bytes(up, H, I, nst, two);
+            CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up, two), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         };
-        pick(true, m->tc_nst_up, m->tc_smem_up);
-        pick(false, m->tc_nst_down, m->tc_smem_down);
+        pick(true, false, m->tc_nst_up, m->tc_smem_up);
+        pick(false, false, m->tc_nst_down, m->tc_smem_down);
+        if (m->ep_n == 1) pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
         if (m->routed_bs) {
             // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
             // fit; a MXFP4 stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
@@ -489,11 +493,13 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
                 cudaFuncAttributes fa{};
                 CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
                 const int room = max_smem - (int)fa.sharedSizeBytes;
-                int n4 = 6, n8 = 8;
+                // the FP8 body's down part takes two-tile items here (34 KB stages, 4 to 6)
+                int n4 = 6, n8 = up ? 8 : 6;
+                const int n8min = 4;
                 while (n4 >= 2 && expert_tc4_smem_bytes(up, n4) > room) n4--;
-                while (n8 >= 4 && expert_tc_smem_bytes(up, H, I, n8) > room) n8--;
-                if (n4 < 2 || n8 < 4) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8));
+                while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, !up) > room) n8--;
+                if (n4 < 2 || n8 < n8min) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
+                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8, !up));
                 CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
                 (up ? m->tc4_nst_up : m->tc4_nst_down) = n4;
                 (up ? m->tc4_nst8_up : m->tc4_nst8_down) = n8;
@@ -599,8 +605,12 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     TcMaps maps = up ? m->tc_up : m->tc_down;
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
-    void *args[] = {&maps, &p, up ? &m->tc_nst_up : &m->tc_nst_down};
-    launch_pdl(expert_tc_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc_smem_up : m->tc_smem_down, st);
+    // down items of two 128-row tiles from T = 4 on (measured at 256 experts, down kernel: T=16 218 ->
+    // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us); not under expert parallelism
+    const bool two = !up && m->ep_n == 1 && p.T >= 4;
+    void *args[] = {&maps, &p, up ? &m->tc_nst_up : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
+    launch_pdl(expert_tc_kernel_ptr(up, two), dim3(m->sms), dim3(192), args,
+               up ? m->tc_smem_up : (two ? m->tc_smem_down2 : m->tc_smem_down), st);
 }
 
 // the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range)
@@ -610,7 +620,7 @@ void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st)
     TcMaps maps4 = up ? m->tc4_up : m->tc4_down;
     maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
     p4.flags = m->tc_flags + m->sms;
-    p4.partial = m->tc_partial + (size_t)m->sms * 128 * 16;
+    p4.partial = m->tc_partial + (size_t)m->sms * 128 * 32;
     int *n8 = up ? &m->tc4_nst8_up : &m->tc4_nst8_down, *n4 = up ? &m->tc4_nst_up : &m->tc4_nst_down;
     void *args[] = {&maps8, &p8, n8, &maps4, &p4, n4};
     launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc4_smem_up : m->tc4_smem_down, st);

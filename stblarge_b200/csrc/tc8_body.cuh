@@ -17,7 +17,10 @@
 //              ref/kernel.py:85-91) and accumulate in registers; then write the outputs.
 // up: the tile is [64 gate rows; 64 up rows]; h = bf16(silu(bf16 g) * bf16 u * w) (stbl/kernels.cu:
 //   445-459).  hquant_kernel then re-quantizes h (act_quant per 128, ref/kernel.py:35-45).
-// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); combine_kernel (combine.cu) adds them.
+// down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); combine_kernel (combine.cu) adds them.  With
+//   T2 an item takes two such tiles (256 rows, two boxes per stage, two accumulator sets in TMEM) and
+//   the MMA issuer alternates between them: a 128-K block of two tiles costs the tensor pipe about as
+//   long as one of one tile (measured on one SM), so the stages are released sooner.
 // Every wait is bounded; a CTA that gives up raises a status bit, drains its copies and MMAs, frees
 // its TMEM and returns.
 #pragma once
@@ -37,22 +40,27 @@ constexpr int kTcTmemCols = kTcGroups * kTcG * kTcN;
 constexpr int kATile = 128 * 128;
 constexpr int kBTile = kTcN * 128;
 constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
+constexpr int kStage2 = 2 * kATile + kBTile;  // T2 (two down tiles): 34 KB
 constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
 constexpr int kTcChunks = 192;    // chunk entries [chunk_begin, +192) kept in shared memory (one per thread)
 constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
 
 // One CTA's share of an FP8 expert launch: CTA `cta` of the `ncta` that run this body (in a mixed
 // launch these number themselves 0..ncta-1).
-template <bool UP>
+template <bool UP, bool T2 = false>
 __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
+    static_assert(!(UP && T2), "two-tile items are a down-product option");
+    constexpr int NT = T2 ? 2 : 1;                       // weight tiles per item
+    constexpr int STAGE = T2 ? kStage2 : kStage;
+    constexpr int TMEM_COLS = NT * kTcTmemCols;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;            // reduction length
     const int rows = UP ? p.I : p.H;         // output rows per matrix
     const int nkb = K / 128;
-    const int tiles = UP ? rows / 64 : rows / 128;
-    unsigned char *stages = smem;                                         // [nst][A tile | B tile]
-    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * kStage);  // [2][16][nkb] activation scales
+    const int tiles = UP ? rows / 64 : rows / (128 * NT);
+    unsigned char *stages = smem;                                         // [nst][A tile(s) | B tile]
+    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * STAGE);  // [2][16][nkb] activation scales
     float *sw = sx + 2 * kTcN * nkb;                                      // [2][2][nkb] weight scales
     float *xacc = sw + 4 * nkb;                                           // [128][17] item sums
     float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
@@ -80,7 +88,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(&tmem_base, kTcTmemCols);
+    if (warp == 1) tmem_alloc(&tmem_base, TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -150,15 +158,18 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                   }
                   for (int u = 0; u < nb && !stop; u++, q++) {
                     const int s = q % nst, kb = kb0 + u;
-                    unsigned char *a = stages + (size_t)s * kStage;
-                    mbar_arrive_expect_tx(&full[s], kStage);
+                    unsigned char *a = stages + (size_t)s * STAGE;
+                    mbar_arrive_expect_tx(&full[s], STAGE);
                     if (UP) {
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 64, z, &full[s]);
                         tma_load_3d(a + kATile / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
                     } else {
-                        tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 128, z, &full[s]);
+#pragma unroll
+                        for (int m = 0; m < NT; m++)
+                            tma_load_3d(a + m * kATile, shared ? &maps.s[0] : &maps.w[0], kb * 128, (NT * tile + m) * 128, z,
+                                        &full[s]);
                     }
-                    tma_load_2d(a + kATile, &maps.b, kb * 128, brow, &full[s]);
+                    tma_load_2d(a + NT * kATile, &maps.b, kb * 128, brow, &full[s]);
                   }
                 }
             }
@@ -195,11 +206,15 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                             break;
                         }
                         tc_fence_after();
-                        const unsigned char *a = stages + (size_t)s * kStage;
-                        const uint32_t d = tmem + (uint32_t)((g * kTcG + u) * kTcN);
+                        const unsigned char *a = stages + (size_t)s * STAGE;
+                        // accumulator of (group g, K block u, tile m): columns ((g NT + m) kTcG + u) kTcN
 #pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            umma_f8(d, sw128_desc(a + 32 * k), sw128_desc(a + kATile + 32 * k), idesc, k > 0);
+                        for (int m = 0; m < NT; m++) {
+                            const uint32_t d = tmem + (uint32_t)(((g * NT + m) * kTcG + u) * kTcN);
+#pragma unroll
+                            for (int k = 0; k < 4; k++)
+                                umma_f8(d, sw128_desc(a + m * kATile + 32 * k), sw128_desc(a + NT * kATile + 32 * k), idesc, k > 0);
+                        }
                         umma_commit(&empty[s]);
                     }
                     if (!stop) umma_commit(&acc_full[g]);
@@ -226,7 +241,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         const int et = tid - 64;                   // 0..127
         const int row = 32 * (warp & 3) + lane;    // TMEM lane = tile row
         const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        const int nsw = (UP ? 2 : 1) * nkb;
+        const int nsw = (UP ? 2 : NT) * nkb;
         float px[kTcPre];
         float pw = 0.f;
         int pcol = 0, pdst = 0;
@@ -246,9 +261,11 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 px[k] = (u < kTcN * nkb && j < bvalid) ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
             }
             if (et < nsw) {
+                // up: the gate (m 0) and up (m 1) scales of the tile's 128-row block; down: tile m's block
                 const int m = et / nkb, kb = et % nkb;
-                const int rblk = UP ? (tile * 64) / 128 : tile;
-                const float *base = shared ? p.s_scale[m] : p.w_scale[m] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
+                const int rblk = UP ? (tile * 64) / 128 : NT * tile + m;
+                const int mat = UP ? m : 0;
+                const float *base = shared ? p.s_scale[mat] : p.w_scale[mat] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
                 pw = __ldg(base + (size_t)rblk * nkb + kb);
             }
             if (et < kTcN) {
@@ -296,9 +313,12 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             if (it + 1 < hi) prefetch(it + 1);
             const float *sxb = sx + buf * kTcN * nkb, *swb = sw + buf * 2 * nkb;
             const int mrow = UP ? (row >> 6) : 0;  // up: rows 64..127 are the up matrix
-            float acc[kTcN];
+            float acc2[NT][kTcN];                  // the item's sums, per weight tile
 #pragma unroll
-            for (int j = 0; j < kTcN; j++) acc[j] = 0.f;
+            for (int m = 0; m < NT; m++)
+#pragma unroll
+                for (int j = 0; j < kTcN; j++) acc2[m][j] = 0.f;
+            float *acc = acc2[0];
             bool ok = true;
             int ka, kz;
             k_range(it, ka, kz);
@@ -309,17 +329,22 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     break;
                 }
                 tc_fence_after();
-                float d[kTcG * kTcN];
-                tmem_ld64(tl + (uint32_t)(g * kTcG * kTcN), d);
-                tc_fence_before();
-                mbar_arrive(&acc_empty[g]);
 #pragma unroll
-                for (int u = 0; u < kTcG; u++) {
-                    const int kb = kb0 + u;
-                    if (kb < kz) {
-                        const float wsc = swb[mrow * nkb + kb];
+                for (int m = 0; m < NT; m++) {
+                    float d[kTcG * kTcN];
+                    tmem_ld64(tl + (uint32_t)((g * NT + m) * kTcG * kTcN), d);
+                    if (m == NT - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&acc_empty[g]);
+                    }
 #pragma unroll
-                        for (int j = 0; j < kTcN; j++) acc[j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc[j]);
+                    for (int u = 0; u < kTcG; u++) {
+                        const int kb = kb0 + u;
+                        if (kb < kz) {
+                            const float wsc = swb[(UP ? mrow : m) * nkb + kb];
+#pragma unroll
+                            for (int j = 0; j < kTcN; j++) acc2[m][j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc2[m][j]);
+                        }
                     }
                 }
             }
@@ -332,9 +357,12 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             }
             if (ka > 0) {
                 // the range starts inside this item: publish the partial sums for the CTA that finishes it
-                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)cta * 128 + row) * kTcN);
+                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)cta * 128 + row) * (NT * kTcN));
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+                for (int m = 0; m < NT; m++)
+#pragma unroll
+                    for (int j = 0; j < kTcN / 4; j++)
+                        dst[m * (kTcN / 4) + j] = make_float4(acc2[m][4 * j], acc2[m][4 * j + 1], acc2[m][4 * j + 2], acc2[m][4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
                 if (et == 0) flag_release(p.flags + cta, p.seq);
@@ -351,12 +379,14 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 if (n_units * (c + 1) / ncta == uc) continue;  // empty range
                 if (et == 0) got = flag_wait(p.flags + c, p.seq, &abort_flag) && got;
                 bar_sync(2, 128);
-                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * kTcN);
+                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * (NT * kTcN));
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) {
-                    const float4 v = __ldcg(src + j);
-                    acc[4 * j] += v.x, acc[4 * j + 1] += v.y, acc[4 * j + 2] += v.z, acc[4 * j + 3] += v.w;
-                }
+                for (int m = 0; m < NT; m++)
+#pragma unroll
+                    for (int j = 0; j < kTcN / 4; j++) {
+                        const float4 v = __ldcg(src + m * (kTcN / 4) + j);
+                        acc2[m][4 * j] += v.x, acc2[m][4 * j + 1] += v.y, acc2[m][4 * j + 2] += v.z, acc2[m][4 * j + 3] += v.w;
+                    }
             }
             if (!got) {
                 abort_flag = 1;
@@ -381,25 +411,28 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
                 }
             } else {
-                const int r = tile * 128 + row;
-                if (ch.e < p.E && p.pos_w) {
-                    // expert parallelism: straight into the source rank's eo row, over NVLink
 #pragma unroll
-                    for (int j = 0; j < kTcN; j++)
-                        if (j < ch.n) {
-                            const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
-                            if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
-                                if (row == 0) atomicOr(p.status, kErrBadTable);
-                                continue;
+                for (int m = 0; m < NT; m++) {
+                    const int r = (NT * tile + m) * 128 + row;
+                    if (ch.e < p.E && p.pos_w) {
+                        // expert parallelism: straight into the source rank's eo row, over NVLink
+#pragma unroll
+                        for (int j = 0; j < kTcN; j++)
+                            if (j < ch.n) {
+                                const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
+                                if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
+                                    if (row == 0) atomicOr(p.status, kErrBadTable);
+                                    continue;
+                                }
+                                uint16_t *out = reinterpret_cast<uint16_t *>(p.ep.region[src] + p.ep.L.eo);
+                                out[(size_t)a * p.H + r] = f32_to_bf16_bits(acc2[m][j]);
                             }
-                            uint16_t *out = reinterpret_cast<uint16_t *>(p.ep.region[src] + p.ep.L.eo);
-                            out[(size_t)a * p.H + r] = f32_to_bf16_bits(acc[j]);
-                        }
-                } else {
-                    uint16_t *out = ch.e < p.E ? p.eo : p.sh;
+                    } else {
+                        uint16_t *out = ch.e < p.E ? p.eo : p.sh;
 #pragma unroll
-                    for (int j = 0; j < kTcN; j++)
-                        if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc[j]);
+                        for (int j = 0; j < kTcN; j++)
+                            if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc2[m][j]);
+                    }
                 }
             }
             if (it + 1 < hi) park(buf ^ 1);
@@ -410,7 +443,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTcTmemCols);
+        tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
