@@ -156,6 +156,40 @@ int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint
 int stbl_cache_state(const stbl_cache *c, int *map, int *owner);
 void stbl_cache_destroy(stbl_cache *c);
 
+/* File-backed cache: the reference's expert streaming from the checkpoint (stbl/model.cu:269-308 reads,
+ * 940-949 experts kept as file offsets, 978-987 readers and O_DIRECT).  Instead of a host store the
+ * routed experts stay in the GGUF file as MXFP4 blocks (type 39, ffn_{gate,up,down}_exps.weight, dims
+ * (k, rows, n_experts), 17 bytes per 32 values); desc->host_* and host_rows are ignored and desc->fmt
+ * must be STBL_FMT_MXFP4.  Each call's missing experts are read by `readers` host threads (pread in
+ * 2 MiB pieces, O_DIRECT where the file system takes it; include/stbl_io.h) into page-locked staging of
+ * `stage_experts` experts, from a host step the call enqueues on its stream after the planner
+ * (cudaLaunchHostFunc), then converted into the slot layout by the copy kernel; more missing experts than
+ * the staging holds are read in rounds.  The stream waits for the reads; the caller does not (a
+ * prefetch reads on its copy stream, beside the current call's kernels).  A failed read raises status
+ * bit 8 in the layer (stbl_moe_status; that call's output is not valid), is counted, and its message
+ * is kept (stbl_cache_error); the experts it was reading leave the cache at the next call, so a later
+ * call routed to them reads them again. */
+typedef struct stbl_cache_file_desc {
+    const char *path;         /* the GGUF checkpoint */
+    const uint64_t *offset;   /* [n_layers][3] absolute file offset of cache layer l's gate / up / down
+                                 expert tensor (multiples of 16); expert e's matrix q starts at
+                                 offset[3 l + q] + e * rows_q * (k_q / 32) * 17 */
+    int readers;              /* reader threads, 0: 4 (the reference's default), at most 64 */
+    int direct;               /* 1: O_DIRECT where the file system takes it, 0: buffered reads */
+    int stage_experts;        /* experts per staging round (page-locked), 0: 8 */
+} stbl_cache_file_desc;
+int stbl_cache_create_file(const stbl_cache_desc *desc, const stbl_cache_file_desc *file, stbl_cache **out, char *err,
+                           int errlen);
+/* File-backed caches: pieces read, bytes read, seconds the read steps took, *direct = 1 while reads go
+ * through O_DIRECT, and read rounds that failed.  -1 for a cache over a host store. */
+int stbl_cache_file_stats(const stbl_cache *c, uint64_t *pieces, uint64_t *bytes, double *seconds, int *direct,
+                          uint64_t *failed_rounds);
+/* Host-side fault injection for tests (file-backed caches): counting from this call, read number `after`
+ * and every later one fail with errno err_no (0 switches it off); see stbl_reader_inject_error. */
+int stbl_cache_inject_read_error(stbl_cache *c, int64_t after, int err_no);
+/* The message of the cache's last error ("" when none). */
+const char *stbl_cache_error(const stbl_cache *c);
+
 /* Prefetch into the cache, the reference's shadow next-layer guesses (stbl/model.cu:432-475 predict,
  * 555-586 issue, 347-373 take_slot): of the first `consider` distinct ids (device [n], guessed experts of
  * layer `layer` in priority order) the ones not cached take a never-used slot or the least recently used
@@ -196,7 +230,8 @@ int stbl_moe_forward_block(stbl_moe *m, const float *x_pre, const float *norm_w,
 
 /* Device status bits raised by kernels since the last call of this function (waits for the
  * device): 1 a wait timed out, 2 a dispatch entry was out of range, 4 copies were still in flight
- * when a CTA gave up.  0 when every call so far ran cleanly. */
+ * when a CTA gave up, 8 an expert read from the checkpoint failed (file-backed cache).  0 when every
+ * call so far ran cleanly. */
 int stbl_moe_status(stbl_moe *m, uint32_t *status);
 
 /* Per-kernel device timing, the counterpart of the reference's STBL_TIMING / stbl_timing

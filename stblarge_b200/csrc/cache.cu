@@ -20,13 +20,29 @@
 // takes a slot the last demand call used (those experts may still be read), and the next demand call
 // waits for the prefetch copy before planning: the guesses have always landed by then, which is the
 // reference's case of reads that finished in time (it also cancels guesses not yet started).
+//
+// File-backed store (stbl_cache_create_file; the reference's expert tensors kept as file offsets and
+// read on a miss, stbl/model.cu:269-308, 940-949, 978-987): the planner writes its jobs into mapped
+// page-locked memory, a host step enqueued on the copying stream (cudaLaunchHostFunc) reads the listed
+// experts' GGUF MXFP4 blocks with the reader threads into page-locked staging, and the copy kernel
+// converts the staged 17-byte blocks into the slot layout (codes and block-layout scales) while it
+// copies them into device memory.  The stream waits for the reads in order, so a call still needs no
+// host synchronisation; a prefetch's reads run on its own stream beside the current call's kernels.
+// A failed read raises status bit 8 (that call's output is not valid) and marks its slots; the next
+// planner drops them from the cache, so a later call that routes to those experts reads them again.
 #include "../../include/stbl_moe.h"
 #include "cache.cuh"
 #include "layer.cuh"
+#include "reader.cuh"
+
+#include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #define CK(x)                                                                                        \
     do {                                                                                             \
@@ -55,6 +71,10 @@ struct CachePlanParams {
     // not yet routed to (counted as used at its first hit)
     int prefetch, consider;
     unsigned char *pf_flag;
+    // file-backed store: slots whose read failed (mapped host memory written by the read step) and a
+    // flag that any are marked; null otherwise
+    unsigned char *bad;
+    int *n_bad;
 };
 
 struct CacheCopyParams {
@@ -94,6 +114,24 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
     pdl_wait();
     pdl_launch_dependents();
     if (tid == 0) s_bad = 0;
+    if (p.n_bad) {
+        // slots a failed read left behind become free (never used) before anything is planned
+        __shared__ int s_any;
+        if (tid == 0) s_any = *(volatile int *)p.n_bad;
+        __syncthreads();
+        if (s_any) {
+            volatile unsigned char *bad = p.bad;
+            for (int s = tid; s < p.S; s += kPlanThreads)
+                if (bad[s]) {
+                    const int old = p.owner[s];
+                    if (old >= 0) p.map[old] = -1;
+                    p.owner[s] = -1, p.ts[s] = 0, p.pf_flag[s] = 0;
+                    bad[s] = 0;
+                }
+            __syncthreads();
+            if (tid == 0) *(volatile int *)p.n_bad = 0;
+        }
+    }
     for (int e = tid; e < p.E; e += kPlanThreads) first[e] = INT_MAX;
     __syncthreads();
     for (int a = tid; a < p.n; a += kPlanThreads) {
@@ -265,6 +303,171 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
     }
 }
 
+// ---- file-backed store ---------------------------------------------------------------------------
+
+struct FileStore;
+
+struct FileRound {  // the argument of one read step: round `round` of the demand (0) or prefetch (1) jobs
+    stbl_cache *c;
+    int round, which;
+};
+
+struct FileStore {
+    ExpertReader *reader = nullptr;
+    std::vector<uint64_t> offset;       // [L][3] file offset of expert 0's gate / up / down blocks
+    uint64_t gbytes[3] = {};            // bytes of one expert's matrix in the file (17 per 32 values)
+    long long region_off[3] = {}, row_bytes = 0;  // one staged expert: three aligned read regions
+    int cap = 0;                        // experts staged per round
+    uint8_t *stage = nullptr, *stage_d = nullptr;       // page-locked [cap][row_bytes] (host, device view)
+    const uint8_t **src = nullptr, **src_d = nullptr;   // [cap][3] device address of each staged matrix
+    uint32_t *fstat = nullptr, *fstat_d = nullptr;      // 1: the current round's reads failed
+    unsigned char *bad = nullptr, *bad_d = nullptr;     // [S] slots whose read failed
+    int *n_bad = nullptr, *n_bad_d = nullptr;
+    int2 *jobs_h[2] = {};               // host views of the demand / prefetch jobs lists
+    int *n_jobs_h[2] = {};
+    std::vector<FileRound> rounds[2];
+    std::atomic<uint64_t> failed_rounds{0};
+    std::mutex mu;
+    std::string err;
+};
+
+struct FileCopyParams {
+    const int2 *jobs;
+    const int *n_jobs;
+    int begin, cap;                // this round's jobs: [begin, min(n_jobs, begin + cap))
+    const uint8_t *const *src;     // [cap][3]
+    const uint32_t *fstat;
+    uint32_t *status;
+    uint8_t *pool;
+    long long slot_bytes, piece_off[6];
+    int K[3], tiles[3];            // gate, up: K = hidden, I / 128 tiles; down: K = inter, H / 128 tiles
+};
+
+// 16 GGUF MXFP4 blocks (272 bytes: per block the e8m0 scale, then values i and 16 + i in the low and
+// high nibble of byte i) -> 256 bytes of codes (values 2j, 2j + 1 in byte j, low nibble first) and the
+// 16 scales as four words of the scale-block layout (word kk of the group goes 512 bytes after word kk-1)
+__device__ __forceinline__ void convert_group(const uint8_t *src, uint8_t *codes, uint8_t *sdst) {
+    uint32_t w[69];
+#pragma unroll
+    for (int i = 0; i < 17; i++) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+        w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+    }
+    w[68] = 0;
+    uint32_t sw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int b = 0; b < 16; b++) {
+        const int o = 17 * b;
+        sw[b >> 2] |= ((w[o >> 2] >> (8 * (o & 3))) & 0xFFu) << (8 * (b & 3));
+        uint32_t q[4];
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const int ob = o + 1 + 4 * m;
+            q[m] = (ob & 3) ? __funnelshift_r(w[ob >> 2], w[(ob >> 2) + 1], 8 * (ob & 3)) : w[ob >> 2];
+        }
+        // a | a >> 4 puts the nibble pairs (2j, 2j + 1) into bytes 0 and 2; the permute keeps those
+        auto pack = [](uint32_t a, uint32_t c) { return __byte_perm(a | (a >> 4), c | (c >> 4), 0x6420); };
+        const uint32_t l0 = q[0] & 0x0F0F0F0Fu, l1 = q[1] & 0x0F0F0F0Fu, l2 = q[2] & 0x0F0F0F0Fu, l3 = q[3] & 0x0F0F0F0Fu;
+        const uint32_t h0 = (q[0] >> 4) & 0x0F0F0F0Fu, h1 = (q[1] >> 4) & 0x0F0F0F0Fu, h2 = (q[2] >> 4) & 0x0F0F0F0Fu,
+                       h3 = (q[3] >> 4) & 0x0F0F0F0Fu;
+        reinterpret_cast<uint4 *>(codes)[b] = make_uint4(pack(l0, l1), pack(l2, l3), pack(h0, h1), pack(h2, h3));
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) *reinterpret_cast<uint32_t *>(sdst + kk * 512) = sw[kk];
+}
+
+// One CTA per 128-row tile of one matrix of one staged expert; thread t takes (row t / G, group t % G)
+// with G = K / 512 groups of 16 blocks per row, so a warp reads consecutive 272-byte runs.
+__global__ void __launch_bounds__(kCopyThreads) cache_file_copy_kernel(FileCopyParams p) {
+    const int nj = *(volatile const int *)p.n_jobs;
+    const int n = min(nj - p.begin, p.cap);
+    if (n <= 0) return;
+    if (*(volatile const uint32_t *)p.fstat) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.status, kErrRead);
+        return;
+    }
+    const int per_job = p.tiles[0] + p.tiles[1] + p.tiles[2];
+    for (long long it = blockIdx.x; it < (long long)n * per_job; it += gridDim.x) {
+        const int j = (int)(it / per_job);
+        int tile = (int)(it % per_job), q = 0;
+        while (q < 2 && tile >= p.tiles[q]) tile -= p.tiles[q++];
+        const int2 job = p.jobs[p.begin + j];
+        const int K = p.K[q], G = K / 512, rowb = K / 32 * 17;
+        const uint8_t *src = p.src[j * 3 + q] + (size_t)tile * 128 * rowb;
+        uint8_t *codes = p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + (size_t)tile * 128 * (K / 2);
+        uint8_t *scales = p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[3 + q] + (size_t)tile * (K / 128) * 512;
+        for (int t = threadIdx.x; t < 128 * G; t += kCopyThreads) {
+            const int r = t / G, g = t % G;
+            convert_group(src + (size_t)r * rowb + (size_t)g * 272, codes + (size_t)r * (K / 2) + (size_t)g * 256,
+                          scales + (size_t)(4 * g) * 512 + (r & 31) * 16 + (r >> 5) * 4);
+        }
+    }
+}
+
+// The read step of one round, run by the CUDA runtime in stream order (no CUDA calls here): reads the
+// round's experts into the staging rows and publishes where each matrix's data starts.
+void CUDART_CB file_round_host(void *arg) {
+    const FileRound *fr = static_cast<const FileRound *>(arg);
+    stbl_cache *c = fr->c;
+    FileStore *f = c->file;
+    volatile uint32_t *fstat = f->fstat;
+    *fstat = 0;
+    const int nj = *(volatile const int *)f->n_jobs_h[fr->which];
+    const int begin = fr->round * f->cap, n = std::min(nj, begin + f->cap) - begin;
+    if (n <= 0) return;
+    std::vector<uint64_t> off(3 * n), bytes(3 * n), at(3 * n);
+    std::vector<uint8_t *> region(3 * n);
+    const volatile int2 *jobs = f->jobs_h[fr->which];
+    for (int j = 0; j < n; j++) {
+        const int key = jobs[begin + j].y, l = key / c->E, e = key % c->E;
+        for (int q = 0; q < 3; q++) {
+            off[3 * j + q] = f->offset[3 * l + q] + (uint64_t)e * f->gbytes[q];
+            bytes[3 * j + q] = f->gbytes[q];
+            region[3 * j + q] = f->stage + (size_t)j * f->row_bytes + f->region_off[q];
+        }
+    }
+    if (!f->reader->read(3 * n, off.data(), bytes.data(), region.data(), at.data())) {
+        volatile unsigned char *bad = f->bad;
+        for (int j = 0; j < n; j++) bad[jobs[begin + j].x] = 1;
+        *(volatile int *)f->n_bad = 1;
+        *fstat = 1;
+        f->failed_rounds++;
+        std::lock_guard<std::mutex> lk(f->mu);
+        f->err = "expert read failed: " + f->reader->error();
+        std::atomic_thread_fence(std::memory_order_seq_cst);
+        return;
+    }
+    for (int i = 0; i < 3 * n; i++) f->src[i] = f->stage_d + (region[i] - f->stage) + at[i];
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+}
+
+void launch_file_copy(stbl_cache *c, int which, int round, uint32_t *status, cudaStream_t st) {
+    FileStore *f = c->file;
+    FileCopyParams fp{};
+    fp.jobs = which ? c->pf_jobs : c->jobs;
+    fp.n_jobs = which ? c->pf_n_jobs : c->n_jobs;
+    fp.begin = round * f->cap, fp.cap = f->cap;
+    fp.src = f->src_d, fp.fstat = f->fstat_d, fp.status = status;
+    fp.pool = c->pool, fp.slot_bytes = c->slot_bytes;
+    for (int q = 0; q < 6; q++) fp.piece_off[q] = c->piece_off[q];
+    const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
+    for (int q = 0; q < 3; q++) fp.K[q] = ks[q], fp.tiles[q] = rows[q] / 128;
+    cache_file_copy_kernel<<<c->copy_ctas, kCopyThreads, 0, st>>>(fp);
+    CK(cudaGetLastError());
+}
+
+// `jobs` experts at most in the jobs list: rounds of read step + copy; a failed read raises kErrRead in
+// `status` (the calling layer's status word)
+void launch_file_rounds(stbl_cache *c, int which, int jobs, uint32_t *status, cudaStream_t st) {
+    FileStore *f = c->file;
+    const int rounds = (jobs + f->cap - 1) / f->cap;
+    if (rounds > (int)f->rounds[which].size()) throw std::runtime_error("too many experts per call for the staging rounds");
+    for (int r = 0; r < rounds; r++) {
+        CK(cudaLaunchHostFunc(st, file_round_host, &f->rounds[which][r]));
+        launch_file_copy(c, which, r, status, st);
+    }
+}
+
 void launch_pdl_k(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
@@ -308,10 +511,11 @@ void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *sta
     // a prefetch copy still running may be filling slots this call reads or evicts
     if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
     CachePlanParams pp{idx, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->jobs, c->n_jobs, c->expert_bytes, status,
-                       0, 0, c->pf_flag};
+                       0, 0, c->pf_flag, c->file ? c->file->bad_d : nullptr, c->file ? c->file->n_bad_d : nullptr};
     void *a1[] = {&pp};
     launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
-    launch_copy(c, c->jobs, c->n_jobs, st, true);
+    if (c->file) launch_file_rounds(c, 0, std::min(n, c->S), status, st);
+    else launch_copy(c, c->jobs, c->n_jobs, st, true);
 }
 
 void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, uint32_t *status, cudaStream_t st,
@@ -320,12 +524,13 @@ void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consid
     // the previous prefetch's jobs list and slots are reused: its copy must be done
     if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
     CachePlanParams pp{ids, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->pf_jobs, c->pf_n_jobs, c->expert_bytes,
-                       status, 1, consider, c->pf_flag};
+                       status, 1, consider, c->pf_flag, c->file ? c->file->bad_d : nullptr, c->file ? c->file->n_bad_d : nullptr};
     void *a1[] = {&pp};
     launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
     CK(cudaEventRecord(c->pf_planned, st));
     CK(cudaStreamWaitEvent(copy_st, c->pf_planned, 0));
-    launch_copy(c, c->pf_jobs, c->pf_n_jobs, copy_st, false);
+    if (c->file) launch_file_rounds(c, 1, std::min({n, consider, c->S}), status, copy_st);
+    else launch_copy(c, c->pf_jobs, c->pf_n_jobs, copy_st, false);
     CK(cudaEventRecord(c->pf_done, copy_st));
     c->pf_pending = true;
 }
@@ -351,24 +556,80 @@ int fail(char *err, int errlen, const std::string &m) {
     return -1;
 }
 
+// page-locked host memory, mapped: (host view, device view)
+template <class T>
+void host_mapped(T **h, T **d, size_t bytes) {
+    CK(cudaHostAlloc((void **)h, bytes, cudaHostAllocMapped));
+    memset((void *)*h, 0, bytes);
+    CK(cudaHostGetDevicePointer((void **)d, (void *)*h, 0));
+}
+
+void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
+    if (!fd->path || !fd->offset) throw std::runtime_error("file desc: path and offset are required");
+    if (fd->readers < 0 || fd->stage_experts < 0) throw std::runtime_error("file desc: readers and stage_experts must be >= 0");
+    FileStore *f = new FileStore();
+    c->file = f;
+    const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
+    for (int q = 0; q < 3; q++) f->gbytes[q] = (uint64_t)rows[q] * (ks[q] / 32) * 17;
+    f->offset.assign(fd->offset, fd->offset + 3 * (size_t)c->L);
+    for (uint64_t o : f->offset)
+        if (o % 16) throw std::runtime_error("expert tensor offsets must be multiples of 16 (GGUF alignment >= 16)");
+    long long off = 0;
+    for (int q = 0; q < 3; q++) f->region_off[q] = off, off += (long long)read_region_bytes(f->gbytes[q]);
+    f->row_bytes = off;
+    f->cap = std::min(fd->stage_experts ? fd->stage_experts : 8, c->S);
+    f->reader = new ExpertReader(fd->path, fd->readers, fd->direct != 0);
+    host_mapped(&f->stage, &f->stage_d, (size_t)f->cap * f->row_bytes);
+    if ((uintptr_t)f->stage % kReadAlign) throw std::runtime_error("staging is not page aligned");
+    host_mapped(&f->src, &f->src_d, sizeof(uint8_t *) * 3 * f->cap);
+    host_mapped(&f->fstat, &f->fstat_d, sizeof(uint32_t));
+    host_mapped(&f->bad, &f->bad_d, (size_t)c->S);
+    host_mapped(&f->n_bad, &f->n_bad_d, sizeof(int));
+    for (int w = 0; w < 2; w++) {
+        host_mapped(&f->jobs_h[w], w ? &c->pf_jobs : &c->jobs, sizeof(int2) * c->S);
+        host_mapped(&f->n_jobs_h[w], w ? &c->pf_n_jobs : &c->n_jobs, sizeof(int));
+        const int most = std::min(c->S, kPlanMaxIds);
+        for (int r = 0; r < (most + f->cap - 1) / f->cap; r++) f->rounds[w].push_back(FileRound{c, r, w});
+    }
+}
+
+void file_store_free(stbl_cache *c) {
+    FileStore *f = c->file;
+    if (!f) return;
+    delete f->reader;
+    cudaFreeHost(f->stage);
+    cudaFreeHost(f->src);
+    cudaFreeHost(f->fstat);
+    cudaFreeHost(f->bad);
+    cudaFreeHost(f->n_bad);
+    for (int w = 0; w < 2; w++) cudaFreeHost(f->jobs_h[w]), cudaFreeHost(f->n_jobs_h[w]);
+    c->jobs = c->pf_jobs = nullptr;
+    c->n_jobs = c->pf_n_jobs = nullptr;
+    delete f;
+    c->file = nullptr;
+}
+
 }  // namespace
 
 extern "C" {
 
-int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int errlen) {
+// the cache of desc d over the pinned host store d->host_* (f null) or over the checkpoint file f
+static stbl_cache *cache_new(const stbl_cache_desc *d, const stbl_cache_file_desc *f) {
     stbl_cache *c = nullptr;
     try {
-        if (!d || !out) throw std::runtime_error("null argument");
+        if (!d) throw std::runtime_error("null argument");
         if (d->n_layers < 1 || d->n_experts < 1 || d->n_experts > 512) throw std::runtime_error("n_layers >= 1, n_experts in 1..512");
         if (d->slots < 0 || d->slots > (1 << 20) - 1) throw std::runtime_error("slots must be in 0..2^20-1");
         if (d->fmt != STBL_FMT_FP8_B128 && d->fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad fmt");
+        if (f && d->fmt != STBL_FMT_MXFP4) throw std::runtime_error("a file-backed cache holds MXFP4 experts (GGUF type 39)");
         if (d->hidden <= 0 || d->inter <= 0 || d->hidden % 512 || d->inter % 512)
             throw std::runtime_error("hidden and inter must be multiples of 512");
         if ((long long)d->n_layers * d->n_experts >= (1LL << 31)) throw std::runtime_error("store too large");
         c = new stbl_cache();
         c->L = d->n_layers, c->E = d->n_experts, c->S = d->slots, c->fmt = d->fmt, c->H = d->hidden, c->I = d->inter;
-        if (d->host_rows < 0 || d->host_rows > (long long)c->L * c->E) throw std::runtime_error("host_rows must be in 0..n_layers*n_experts");
-        c->host_rows = d->host_rows ? d->host_rows : (long long)c->L * c->E;
+        if (!f && (d->host_rows < 0 || d->host_rows > (long long)c->L * c->E))
+            throw std::runtime_error("host_rows must be in 0..n_layers*n_experts");
+        c->host_rows = !f && d->host_rows ? d->host_rows : (long long)c->L * c->E;
         CK(cudaGetDevice(&c->dev));
         const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
         long long off = 0;
@@ -378,6 +639,7 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
             c->piece_off[q] = off;
             off += (c->piece_bytes[q] + 1023) & ~1023LL;
             c->expert_bytes += c->piece_bytes[q];
+            if (f) continue;  // no host store
             const void *h = q < 3 ? d->host_w[q] : d->host_s[q - 3];
             const long long hs = q < 3 ? d->host_w_stride[q] : d->host_s_stride[q - 3];
             c->host_stride[q] = hs ? hs : c->piece_bytes[q];
@@ -415,12 +677,16 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
         CK(cudaMemset(c->ts, 0, sizeof(unsigned long long) * c->S));
         CK(cudaMalloc(&c->ctr, sizeof(unsigned long long) * 8));
         CK(cudaMemset(c->ctr, 0, sizeof(unsigned long long) * 8));
-        CK(cudaMalloc(&c->jobs, sizeof(int2) * c->S));
-        CK(cudaMalloc(&c->n_jobs, sizeof(int)));
-        CK(cudaMemset(c->n_jobs, 0, sizeof(int)));
-        CK(cudaMalloc(&c->pf_jobs, sizeof(int2) * c->S));
-        CK(cudaMalloc(&c->pf_n_jobs, sizeof(int)));
-        CK(cudaMemset(c->pf_n_jobs, 0, sizeof(int)));
+        if (f) {
+            file_store_new(c, f);
+        } else {
+            CK(cudaMalloc(&c->jobs, sizeof(int2) * c->S));
+            CK(cudaMalloc(&c->n_jobs, sizeof(int)));
+            CK(cudaMemset(c->n_jobs, 0, sizeof(int)));
+            CK(cudaMalloc(&c->pf_jobs, sizeof(int2) * c->S));
+            CK(cudaMalloc(&c->pf_n_jobs, sizeof(int)));
+            CK(cudaMemset(c->pf_n_jobs, 0, sizeof(int)));
+        }
         CK(cudaMalloc(&c->pf_flag, c->S));
         CK(cudaMemset(c->pf_flag, 0, c->S));
         CK(cudaEventCreateWithFlags(&c->pf_done, cudaEventDisableTiming));
@@ -428,12 +694,58 @@ int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int
         CK(cudaMalloc(&c->status, sizeof(uint32_t)));
         CK(cudaMemset(c->status, 0, sizeof(uint32_t)));
         CK(cudaDeviceSynchronize());
-        *out = c;
+        return c;
+    } catch (...) {
+        if (c) stbl_cache_destroy(c);
+        throw;
+    }
+}
+
+int stbl_cache_create(const stbl_cache_desc *d, stbl_cache **out, char *err, int errlen) {
+    try {
+        if (!out) throw std::runtime_error("null argument");
+        *out = cache_new(d, nullptr);
         return 0;
     } catch (const std::exception &e) {
-        if (c) stbl_cache_destroy(c);
         return fail(err, errlen, e.what());
     }
+}
+
+int stbl_cache_create_file(const stbl_cache_desc *d, const stbl_cache_file_desc *f, stbl_cache **out, char *err, int errlen) {
+    try {
+        if (!out || !f) throw std::runtime_error("null argument");
+        *out = cache_new(d, f);
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(err, errlen, e.what());
+    }
+}
+
+int stbl_cache_file_stats(const stbl_cache *c, uint64_t *pieces, uint64_t *bytes, double *seconds, int *direct,
+                          uint64_t *failed_rounds) {
+    if (!c || !c->file) return -1;
+    c->file->reader->stats(pieces, bytes, seconds, direct);
+    if (failed_rounds) *failed_rounds = c->file->failed_rounds.load();
+    return 0;
+}
+
+int stbl_cache_inject_read_error(stbl_cache *c, int64_t after, int err_no) {
+    if (!c || !c->file || after < 0 || err_no < 0) return -1;
+    c->file->reader->inject_error(after, err_no);
+    return 0;
+}
+
+const char *stbl_cache_error(const stbl_cache *c) {
+    if (!c) return "null cache";
+    if (c->file) {
+        std::lock_guard<std::mutex> lk(c->file->mu);
+        if (!c->file->err.empty()) {
+            thread_local std::string msg;
+            msg = c->file->err;
+            return msg.c_str();
+        }
+    }
+    return c->err.c_str();
 }
 
 int stbl_cache_layer_desc(const stbl_cache *c, stbl_moe_desc *d) {
@@ -506,6 +818,7 @@ void stbl_cache_destroy(stbl_cache *c) {
     cudaFree(c->owner);
     cudaFree(c->ts);
     cudaFree(c->ctr);
+    file_store_free(c);  // mapped jobs lists
     cudaFree(c->jobs);
     cudaFree(c->n_jobs);
     cudaFree(c->pf_jobs);

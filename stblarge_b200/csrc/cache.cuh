@@ -6,6 +6,10 @@
 
 #include <string>
 
+namespace stbl {
+struct FileStore;
+}
+
 struct stbl_cache {
     int L = 0, E = 0, S = 0, fmt = 0, H = 0, I = 0, dev = 0;
     // one expert = six pieces: codes of gate, up, down, then their scales; slot s holds piece p at
@@ -33,6 +37,9 @@ struct stbl_cache {
     bool pf_pending = false;
     uint32_t *status = nullptr;
     std::string err;
+    // file-backed store (stbl_cache_create_file): the jobs lists above live in mapped page-locked memory
+    // and the missing experts are read from the checkpoint by a host step on the copying stream
+    stbl::FileStore *file = nullptr;
 };
 
 namespace stbl {

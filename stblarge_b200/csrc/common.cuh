@@ -16,6 +16,7 @@ enum : uint32_t {
     kErrWaitTimeout = 1u,   // an mbarrier wait ran out of time
     kErrBadTable = 2u,      // a dispatch table entry was out of range
     kErrCopyTimeout = 4u,   // copies still in flight when a CTA gave up
+    kErrRead = 8u,          // an expert read from the checkpoint file failed (file-backed expert cache)
 };
 
 // one second: far above any legal wait (a whole layer takes well under a millisecond)

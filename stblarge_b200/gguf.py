@@ -231,9 +231,42 @@ def moe_config(g, layer=0, prefix=PREFIX):
                      routed_fmt=FMT_MXFP4, shared_fmt=FMT_FP8_E8M0 if shared is not None else FMT_NONE)
 
 
-def load_moe_layer(g, layer, prefix=PREFIX, device="cuda"):
+def expert_offsets(g, layers):
+    """[[gate, up, down] file offsets] of the MXFP4 expert tensors of `layers` (ffn_*_exps.weight): where
+    a file-backed expert cache reads them (the reference keeps the same file pointers,
+    stbl/model.cu:940-949)."""
+    out = []
+    for layer in layers:
+        row = []
+        for part in ("gate", "up", "down"):
+            t = g.tensor(f"blk.{layer}.ffn_{part}_exps.weight")
+            if t is None:
+                raise KeyError(f"missing tensor blk.{layer}.ffn_{part}_exps.weight")
+            if t["type"] != T_MXFP4:
+                raise ValueError(f"blk.{layer}.ffn_{part}_exps.weight has type {t['type']}, not MXFP4")
+            row.append(t["offset"])
+        out.append(row)
+    return out
+
+
+def file_cache(path, layers, slots, readers=0, direct=1, stage_experts=0, prefix=PREFIX):
+    """An ExpertCache whose cache layer i streams model layer layers[i]'s routed experts from the GGUF
+    file at `path` (read on demand, converted on the device).  Layers attached to it are loaded with
+    load_moe_layer(g, layer, routed=False)."""
+    from .cache import ExpertCache
+
+    with GgufFile(path) as g:
+        cfg = moe_config(g, layers[0], prefix)
+        offsets = expert_offsets(g, layers)
+    return ExpertCache(cfg, len(layers), slots, file={"path": str(path), "offsets": offsets, "readers": readers,
+                                                       "direct": direct, "stage_experts": stage_experts})
+
+
+def load_moe_layer(g, layer, prefix=PREFIX, device="cuda", routed=True):
     """(MoEConfig, device tensors in the layout MoELayer takes) for layer `layer` of an open GgufFile.
-    The MXFP4 expert blocks are copied to the device and converted there (stbl_mxfp4_from_gguf)."""
+    The MXFP4 expert blocks are copied to the device and converted there (stbl_mxfp4_from_gguf).
+    routed=False leaves the routed experts out (routed_w / routed_s empty): a layer attached to a
+    file-backed expert cache reads them from the file."""
     import torch
 
     cfg = moe_config(g, layer, prefix)
@@ -255,6 +288,8 @@ def load_moe_layer(g, layer, prefix=PREFIX, device="cuda"):
     lib = L.load()
     stream = torch.cuda.current_stream(device)
     for m, part in enumerate(("gate", "up", "down")):
+        if not routed:
+            break
         rows, k = shapes[m]
         blocks = need(b + f"ffn_{part}_exps.weight", T_MXFP4, (k, rows, E))
         codes = torch.empty(E, rows, k // 2, dtype=torch.uint8, device=device)

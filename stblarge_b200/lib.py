@@ -1,4 +1,5 @@
-"""ctypes binding of libstbl_moe.so (include/stbl_moe.h, include/stbl_kernels.h, include/stbl_gguf.h).
+"""ctypes binding of libstbl_moe.so (include/stbl_moe.h, include/stbl_kernels.h, include/stbl_gguf.h,
+include/stbl_io.h).
 
 The reference drives its engine from Python through ctypes (stbl/run.py:37-47, stbl/test_kernels.py:25);
 this module does the same for the B200 library.  There is no fallback: if the library is missing
@@ -42,6 +43,10 @@ class CacheDesc(ctypes.Structure):
     ]
 
 
+class CacheFileDesc(ctypes.Structure):
+    _fields_ = [("path", ctypes.c_char_p), ("offset", P), ("readers", I), ("direct", I), ("stage_experts", I)]
+
+
 # every symbol the headers declare, with its C signature
 SIGNATURES = {
     # include/stbl_moe.h
@@ -66,6 +71,12 @@ SIGNATURES = {
     "stbl_cache_prefetch": (I, [P, I, P, I, I, P, P]),
     "stbl_cache_prefetch_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
     "stbl_moe_attach_prefetch": (I, [P, P, I, I, P]),
+    "stbl_cache_create_file": (I, [ctypes.POINTER(CacheDesc), ctypes.POINTER(CacheFileDesc), ctypes.POINTER(P),
+                                   ctypes.c_char_p, I]),
+    "stbl_cache_file_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(I), ctypes.POINTER(U64)]),
+    "stbl_cache_inject_read_error": (I, [P, ctypes.c_int64, I]),
+    "stbl_cache_error": (ctypes.c_char_p, [P]),
     "stbl_mxfp4_from_gguf": (I, [P, I, I, P, P, P]),
     "stbl_moe_status": (I, [P, ctypes.POINTER(U32)]),
     "stbl_moe_set_timing": (I, [P, I]),
@@ -85,6 +96,15 @@ SIGNATURES = {
     "stbl_gguf_f32": (I, [P, ctypes.c_char_p, ctypes.POINTER(F)]),
     "stbl_gguf_uints": (ctypes.c_int64, [P, ctypes.c_char_p, ctypes.POINTER(U64), ctypes.c_int64]),
     "stbl_gguf_str": (ctypes.c_int64, [P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int64]),
+    # include/stbl_io.h
+    "stbl_reader_open": (I, [ctypes.c_char_p, I, I, ctypes.POINTER(P), ctypes.c_char_p, I]),
+    "stbl_reader_region_bytes": (U64, [U64]),
+    "stbl_reader_read": (I, [P, I, P, P, P, P]),
+    "stbl_reader_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(ctypes.c_double),
+                              ctypes.POINTER(I)]),
+    "stbl_reader_inject_error": (I, [P, ctypes.c_int64, I]),
+    "stbl_reader_error": (ctypes.c_char_p, [P]),
+    "stbl_reader_close": (None, [P]),
     # include/stbl_kernels.h
     "stbl_act_quant_fp8": (None, [P, I, P]),
     "stbl_round_bf16": (None, [P, I, P]),
