@@ -318,7 +318,9 @@ struct FileStore {
     uint64_t gbytes[3] = {};            // bytes of one expert's matrix in the file (17 per 32 values)
     long long region_off[3] = {}, row_bytes = 0;  // one staged expert: three aligned read regions
     int cap = 0;                        // experts staged per round
-    uint8_t *stage = nullptr, *stage_d = nullptr;       // page-locked [cap][row_bytes] (host, device view)
+    uint8_t *stage_alloc = nullptr;     // page-locked allocation holding the staging (small ones need not
+                                        // start on a page)
+    uint8_t *stage = nullptr, *stage_d = nullptr;       // [cap][row_bytes], 4096-aligned (host, device view)
     const uint8_t **src = nullptr, **src_d = nullptr;   // [cap][3] device address of each staged matrix
     uint32_t *fstat = nullptr, *fstat_d = nullptr;      // 1: the current round's reads failed
     unsigned char *bad = nullptr, *bad_d = nullptr;     // [S] slots whose read failed
@@ -579,8 +581,10 @@ void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
     f->row_bytes = off;
     f->cap = std::min(fd->stage_experts ? fd->stage_experts : 8, c->S);
     f->reader = new ExpertReader(fd->path, fd->readers, fd->direct != 0);
-    host_mapped(&f->stage, &f->stage_d, (size_t)f->cap * f->row_bytes);
-    if ((uintptr_t)f->stage % kReadAlign) throw std::runtime_error("staging is not page aligned");
+    uint8_t *alloc_d = nullptr;
+    host_mapped(&f->stage_alloc, &alloc_d, (size_t)f->cap * f->row_bytes + kReadAlign);
+    const size_t pad = (kReadAlign - (uintptr_t)f->stage_alloc % kReadAlign) % kReadAlign;  // O_DIRECT buffers
+    f->stage = f->stage_alloc + pad, f->stage_d = alloc_d + pad;
     host_mapped(&f->src, &f->src_d, sizeof(uint8_t *) * 3 * f->cap);
     host_mapped(&f->fstat, &f->fstat_d, sizeof(uint32_t));
     host_mapped(&f->bad, &f->bad_d, (size_t)c->S);
@@ -597,7 +601,7 @@ void file_store_free(stbl_cache *c) {
     FileStore *f = c->file;
     if (!f) return;
     delete f->reader;
-    cudaFreeHost(f->stage);
+    cudaFreeHost(f->stage_alloc);
     cudaFreeHost(f->src);
     cudaFreeHost(f->fstat);
     cudaFreeHost(f->bad);
