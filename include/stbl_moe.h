@@ -162,9 +162,9 @@ void stbl_cache_destroy(stbl_cache *c);
  * (k, rows, n_experts), 17 bytes per 32 values); desc->host_* and host_rows are ignored and desc->fmt
  * must be STBL_FMT_MXFP4.  Each call's missing experts are read by `readers` host threads (pread in
  * 2 MiB pieces, O_DIRECT where the file system takes it; include/stbl_io.h) into page-locked staging of
- * `stage_experts` experts, from a host step the call enqueues on its stream after the planner
- * (cudaLaunchHostFunc), then converted into the slot layout by the copy kernel; more missing experts than
- * the staging holds are read in rounds.  The stream waits for the reads; the caller does not (a
+ * `stage_experts` experts, from host steps (cudaLaunchHostFunc) on a reader stream that the call's
+ * stream waits for through events, then converted into the slot layout by the copy kernel; the missing
+ * experts are read in rounds of stage_experts, double-buffered.  The stream waits for the reads; the caller does not (a
  * prefetch reads on its copy stream, beside the current call's kernels).  A failed read raises status
  * bit 8 in the layer (stbl_moe_status; that call's output is not valid), is counted, and its message
  * is kept (stbl_cache_error); the experts it was reading leave the cache at the next call, so a later
@@ -176,7 +176,8 @@ typedef struct stbl_cache_file_desc {
                                  offset[3 l + q] + e * rows_q * (k_q / 32) * 17 */
     int readers;              /* reader threads, 0: 4 (the reference's default), at most 64 */
     int direct;               /* 1: O_DIRECT where the file system takes it, 0: buffered reads */
-    int stage_experts;        /* experts per staging round (page-locked), 0: 8 */
+    int stage_experts;        /* experts per staging round, 0: 2 (two buffers of it, page-locked; round r + 1 is
+                                 read while round r is converted, so small rounds hide the conversion) */
 } stbl_cache_file_desc;
 int stbl_cache_create_file(const stbl_cache_desc *desc, const stbl_cache_file_desc *file, stbl_cache **out, char *err,
                            int errlen);

@@ -23,10 +23,11 @@
 //
 // File-backed store (stbl_cache_create_file; the reference's expert tensors kept as file offsets and
 // read on a miss, stbl/model.cu:269-308, 940-949, 978-987): the planner writes its jobs into mapped
-// page-locked memory, a host step enqueued on the copying stream (cudaLaunchHostFunc) reads the listed
-// experts' GGUF MXFP4 blocks with the reader threads into page-locked staging, and the copy kernel
-// converts the staged 17-byte blocks into the slot layout (codes and block-layout scales) while it
-// copies them into device memory.  The stream waits for the reads in order, so a call still needs no
+// page-locked memory, a host step (cudaLaunchHostFunc, on a reader stream joined to the copying stream
+// by events) reads the listed experts' GGUF MXFP4 blocks with the reader threads into page-locked
+// staging, and the copy kernel converts the staged 17-byte blocks into the slot layout (codes and
+// block-layout scales) while it copies them into device memory.  The staging has two buffers, so the
+// reads of one round overlap the copy of the one before.  The stream waits for the reads in order, so a call still needs no
 // host synchronisation; a prefetch's reads run on its own stream beside the current call's kernels.
 // A failed read raises status bit 8 (that call's output is not valid) and marks its slots; the next
 // planner drops them from the cache, so a later call that routes to those experts reads them again.
@@ -318,11 +319,15 @@ struct FileStore {
     uint64_t gbytes[3] = {};            // bytes of one expert's matrix in the file (17 per 32 values)
     long long region_off[3] = {}, row_bytes = 0;  // one staged expert: three aligned read regions
     int cap = 0;                        // experts staged per round
+    // two staging buffers: round r reads into buffer r % 2 while the copy of round r - 1 converts the other
     uint8_t *stage_alloc = nullptr;     // page-locked allocation holding the staging (small ones need not
                                         // start on a page)
-    uint8_t *stage = nullptr, *stage_d = nullptr;       // [cap][row_bytes], 4096-aligned (host, device view)
-    const uint8_t **src = nullptr, **src_d = nullptr;   // [cap][3] device address of each staged matrix
-    uint32_t *fstat = nullptr, *fstat_d = nullptr;      // 1: the current round's reads failed
+    uint8_t *stage = nullptr, *stage_d = nullptr;       // [2][cap][row_bytes], 4096-aligned (host, device view)
+    const uint8_t **src = nullptr, **src_d = nullptr;   // [2][cap][3] device address of each staged matrix
+    uint32_t *fstat = nullptr, *fstat_d = nullptr;      // [2] 1: the buffer's last round of reads failed
+    cudaStream_t rstream = nullptr;     // the read steps run here, ahead of the copies on the caller's stream
+    cudaEvent_t ev_plan = nullptr;      // the planner has written the jobs list
+    std::vector<cudaEvent_t> ev_read, ev_copy;  // per round: its reads / its copy are done
     unsigned char *bad = nullptr, *bad_d = nullptr;     // [S] slots whose read failed
     int *n_bad = nullptr, *n_bad_d = nullptr;
     int2 *jobs_h[2] = {};               // host views of the demand / prefetch jobs lists
@@ -412,7 +417,8 @@ void CUDART_CB file_round_host(void *arg) {
     const FileRound *fr = static_cast<const FileRound *>(arg);
     stbl_cache *c = fr->c;
     FileStore *f = c->file;
-    volatile uint32_t *fstat = f->fstat;
+    const int buf = fr->round & 1;
+    volatile uint32_t *fstat = f->fstat + buf;
     *fstat = 0;
     const int nj = *(volatile const int *)f->n_jobs_h[fr->which];
     const int begin = fr->round * f->cap, n = std::min(nj, begin + f->cap) - begin;
@@ -425,7 +431,7 @@ void CUDART_CB file_round_host(void *arg) {
         for (int q = 0; q < 3; q++) {
             off[3 * j + q] = f->offset[3 * l + q] + (uint64_t)e * f->gbytes[q];
             bytes[3 * j + q] = f->gbytes[q];
-            region[3 * j + q] = f->stage + (size_t)j * f->row_bytes + f->region_off[q];
+            region[3 * j + q] = f->stage + ((size_t)buf * f->cap + j) * f->row_bytes + f->region_off[q];
         }
     }
     if (!f->reader->read(3 * n, off.data(), bytes.data(), region.data(), at.data())) {
@@ -439,7 +445,7 @@ void CUDART_CB file_round_host(void *arg) {
         std::atomic_thread_fence(std::memory_order_seq_cst);
         return;
     }
-    for (int i = 0; i < 3 * n; i++) f->src[i] = f->stage_d + (region[i] - f->stage) + at[i];
+    for (int i = 0; i < 3 * n; i++) f->src[(size_t)buf * f->cap * 3 + i] = f->stage_d + (region[i] - f->stage) + at[i];
     std::atomic_thread_fence(std::memory_order_seq_cst);
 }
 
@@ -449,7 +455,7 @@ void launch_file_copy(stbl_cache *c, int which, int round, uint32_t *status, cud
     fp.jobs = which ? c->pf_jobs : c->jobs;
     fp.n_jobs = which ? c->pf_n_jobs : c->n_jobs;
     fp.begin = round * f->cap, fp.cap = f->cap;
-    fp.src = f->src_d, fp.fstat = f->fstat_d, fp.status = status;
+    fp.src = f->src_d + (size_t)(round & 1) * f->cap * 3, fp.fstat = f->fstat_d + (round & 1), fp.status = status;
     fp.pool = c->pool, fp.slot_bytes = c->slot_bytes;
     for (int q = 0; q < 6; q++) fp.piece_off[q] = c->piece_off[q];
     const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
@@ -458,15 +464,23 @@ void launch_file_copy(stbl_cache *c, int which, int round, uint32_t *status, cud
     CK(cudaGetLastError());
 }
 
-// `jobs` experts at most in the jobs list: rounds of read step + copy; a failed read raises kErrRead in
-// `status` (the calling layer's status word)
+// `jobs` experts at most in the jobs list: rounds of read step (on the reader stream) + copy (on st); a
+// failed read raises kErrRead in `status` (the calling layer's status word).  Round r + 1's reads run
+// while round r's copy converts; round r + 2 reuses round r's buffer after its copy.  Every event is
+// recorded before anything here waits for it, so no wait can see a recording of an earlier call.
 void launch_file_rounds(stbl_cache *c, int which, int jobs, uint32_t *status, cudaStream_t st) {
     FileStore *f = c->file;
     const int rounds = (jobs + f->cap - 1) / f->cap;
     if (rounds > (int)f->rounds[which].size()) throw std::runtime_error("too many experts per call for the staging rounds");
+    CK(cudaEventRecord(f->ev_plan, st));
+    CK(cudaStreamWaitEvent(f->rstream, f->ev_plan, 0));
     for (int r = 0; r < rounds; r++) {
-        CK(cudaLaunchHostFunc(st, file_round_host, &f->rounds[which][r]));
+        if (r >= 2) CK(cudaStreamWaitEvent(f->rstream, f->ev_copy[r - 2], 0));
+        CK(cudaLaunchHostFunc(f->rstream, file_round_host, &f->rounds[which][r]));
+        CK(cudaEventRecord(f->ev_read[r], f->rstream));
+        CK(cudaStreamWaitEvent(st, f->ev_read[r], 0));
         launch_file_copy(c, which, r, status, st);
+        CK(cudaEventRecord(f->ev_copy[r], st));
     }
 }
 
@@ -579,14 +593,16 @@ void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
     long long off = 0;
     for (int q = 0; q < 3; q++) f->region_off[q] = off, off += (long long)read_region_bytes(f->gbytes[q]);
     f->row_bytes = off;
-    f->cap = std::min(fd->stage_experts ? fd->stage_experts : 8, c->S);
+    f->cap = std::min(fd->stage_experts ? fd->stage_experts : 2, c->S);  // small rounds overlap best
     f->reader = new ExpertReader(fd->path, fd->readers, fd->direct != 0);
     uint8_t *alloc_d = nullptr;
-    host_mapped(&f->stage_alloc, &alloc_d, (size_t)f->cap * f->row_bytes + kReadAlign);
+    host_mapped(&f->stage_alloc, &alloc_d, 2 * (size_t)f->cap * f->row_bytes + kReadAlign);
     const size_t pad = (kReadAlign - (uintptr_t)f->stage_alloc % kReadAlign) % kReadAlign;  // O_DIRECT buffers
     f->stage = f->stage_alloc + pad, f->stage_d = alloc_d + pad;
-    host_mapped(&f->src, &f->src_d, sizeof(uint8_t *) * 3 * f->cap);
-    host_mapped(&f->fstat, &f->fstat_d, sizeof(uint32_t));
+    host_mapped(&f->src, &f->src_d, sizeof(uint8_t *) * 2 * 3 * f->cap);
+    host_mapped(&f->fstat, &f->fstat_d, 2 * sizeof(uint32_t));
+    CK(cudaStreamCreateWithFlags(&f->rstream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&f->ev_plan, cudaEventDisableTiming));
     host_mapped(&f->bad, &f->bad_d, (size_t)c->S);
     host_mapped(&f->n_bad, &f->n_bad_d, sizeof(int));
     for (int w = 0; w < 2; w++) {
@@ -595,12 +611,23 @@ void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
         const int most = std::min(c->S, kPlanMaxIds);
         for (int r = 0; r < (most + f->cap - 1) / f->cap; r++) f->rounds[w].push_back(FileRound{c, r, w});
     }
+    for (size_t r = 0; r < f->rounds[0].size(); r++) {
+        f->ev_read.push_back(nullptr), f->ev_copy.push_back(nullptr);
+        CK(cudaEventCreateWithFlags(&f->ev_read.back(), cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&f->ev_copy.back(), cudaEventDisableTiming));
+    }
 }
 
 void file_store_free(stbl_cache *c) {
     FileStore *f = c->file;
     if (!f) return;
     delete f->reader;
+    for (cudaEvent_t e : f->ev_read)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : f->ev_copy)
+        if (e) cudaEventDestroy(e);
+    if (f->ev_plan) cudaEventDestroy(f->ev_plan);
+    if (f->rstream) cudaStreamDestroy(f->rstream);
     cudaFreeHost(f->stage_alloc);
     cudaFreeHost(f->src);
     cudaFreeHost(f->fstat);

@@ -163,25 +163,57 @@ def kv(key, vtype, value):
     return _str(key) + struct.pack("<I", vtype) + _value(vtype, value)
 
 
+class Repeated:
+    """Tensor data given as `chunk` repeated `count` times (large synthetic checkpoints written without
+    holding them in memory)."""
+
+    def __init__(self, chunk, count):
+        self.chunk, self.count = bytes(chunk), int(count)
+
+    def __len__(self):
+        return len(self.chunk) * self.count
+
+
 def write_gguf(path, records, tensors, alignment=32):
-    """records: metadata records (kv(...) bytes); tensors: (name, type, dims innermost first, bytes).
-    The data offsets follow the tensors' order, each padded to the alignment."""
+    """records: metadata records (kv(...) bytes); tensors: (name, type, dims innermost first, bytes or
+    Repeated).  The data offsets follow the tensors' order, each padded to the alignment."""
     infos, offset, payload = [], 0, []
     for name, ttype, dims, data in tensors:
-        data = bytes(data)
+        if not isinstance(data, Repeated):
+            data = bytes(data)
         if len(data) != tensor_nbytes(ttype, dims):
             raise ValueError(f"{name}: {len(data)} bytes for a {ttype} tensor of dims {dims}")
         infos.append(_str(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}Q", *dims)
                      + struct.pack("<IQ", ttype, offset))
         pad = (-len(data)) % alignment
-        payload.append(data + bytes(pad))
+        payload.append((data, pad))
         offset += len(data) + pad
     header = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(records)) + b"".join(records) + b"".join(infos)
     header += bytes((-len(header)) % alignment)
     with open(path, "wb") as f:
         f.write(header)
-        for p in payload:
-            f.write(p)
+        for data, pad in payload:
+            if isinstance(data, Repeated):
+                for _ in range(data.count):
+                    f.write(data.chunk)
+            else:
+                f.write(data)
+            f.write(bytes(pad))
+
+
+def mxfp4_to_blocks(codes, scales):
+    """The layer's MXFP4 layout (codes [rows][k/2], values 2j and 2j+1 in byte j, low nibble first; e8m0
+    scales [rows][k/32]) -> GGUF blocks [rows][k/32 * 17] (per 32 values the scale, then values i and
+    16 + i in the low and high nibble of byte i; the reference converter's layout,
+    tools/convert_official.py:187-201); the inverse of stbl_mxfp4_from_gguf."""
+    codes, scales = np.asarray(codes, np.uint8), np.asarray(scales, np.uint8)
+    rows, nb = scales.shape
+    c = codes.reshape(rows, nb, 16)
+    v = np.stack([c & 15, c >> 4], -1).reshape(rows, nb, 32)  # values in order
+    out = np.empty((rows, nb, 17), np.uint8)
+    out[..., 0] = scales
+    out[..., 1:] = v[..., :16] | (v[..., 16:] << 4)
+    return out.reshape(rows, nb * 17)
 
 
 def moe_layer_tensors(layer, router_w, router_bias, shared, experts):

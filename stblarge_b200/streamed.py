@@ -10,6 +10,15 @@ Zipf(1.0) popularity (a seeded permutation of ranks per layer) without replaceme
 token through every layer; tokens/s = steps / device time, hit rate = cache hits / routed experts.
 
     python -m stblarge_b200.streamed [--layers 58] [--cache-gb 40] [--store-experts 1024] [--steps 64]
+
+With --source file the experts are streamed from a GGUF checkpoint instead (the reference's reads from
+the file, stbl/model.cu:269-308; stbl_cache_create_file): a file of --file-experts full-size MXFP4
+experts (the same expert repeated; every layer reads the same tensors) is written to --file-dir, and
+each token's missing experts are read from it by the cache's reader threads (O_DIRECT where the file
+system takes it) and converted on the device.  Reported besides tokens/s: bytes read per second of
+read time and whether O_DIRECT was in use.
+
+    python -m stblarge_b200.streamed --source file [--layers 8] [--file-experts 32] [--slots 16] [--steps 12]
 """
 
 import argparse
@@ -109,15 +118,103 @@ def run(layers=58, cache_gb=40.0, store_experts=1024, steps=64, warmup=3, seed=5
     return res
 
 
+def run_file(layers=8, file_experts=32, slots=16, steps=12, warmup=3, readers=8, direct=1, stage_experts=2,
+             file_dir=None, seed=5, log=print):
+    import dataclasses
+    import os
+    import tempfile
+
+    import torch
+
+    from . import gguf as G
+    from .moe import MoELayer
+
+    cfg = dataclasses.replace(CFG3, name="cfg3_file", n_experts=file_experts, n_groups=1, topk_groups=1)
+    E, K, H, I = cfg.n_experts, cfg.topk, cfg.hidden, cfg.inter
+    fd, path = tempfile.mkstemp(suffix=".gguf", dir=file_dir)
+    os.close(fd)
+    try:
+        t0 = time.time()
+        w, s = synth.routed_expert(cfg, 1000)
+        tensors = []
+        for m, part in enumerate(("gate", "up", "down")):
+            rows, k = (I, H) if m < 2 else (H, I)
+            blocks = G.mxfp4_to_blocks(w[m].cpu().numpy(), s[m].cpu().numpy())
+            tensors.append((f"blk.0.ffn_{part}_exps.weight", G.T_MXFP4, (k, rows, E), G.Repeated(blocks.tobytes(), E)))
+        G.write_gguf(path, [], tensors)
+        file_gb = os.path.getsize(path) / 1e9
+        with G.GgufFile(path) as g:
+            offsets = G.expert_offsets(g, [0]) * layers  # every layer reads the same expert tensors
+        t_write = time.time() - t0
+        from .cache import ExpertCache
+        cache = ExpertCache(cfg, layers, slots, file={"path": path, "offsets": offsets, "readers": readers,
+                                                        "direct": direct, "stage_experts": stage_experts})
+        stack = []
+        for l in range(layers):
+            wl = synth.device_layer(cfg, experts=range(0))
+            stack.append(MoELayer(cfg, wl, max_tokens=1, cache=(cache, l)))
+        trace = route_trace(E, K, layers, warmup + steps, seed=seed)
+        idx = torch.from_numpy(trace).cuda().view(warmup + steps, layers, 1, K)
+        xs = [torch.from_numpy(synth.make_x(H, 1, seed=4 + t).view(np.int16)).cuda() for t in range(warmup + steps)]
+        log(f"file {file_gb:.2f} GB written in {t_write:.1f} s; cache {slots} slots")
+
+        def token(t):
+            x = xs[t]
+            for l in range(layers):
+                x = stack[l].forward_routed(x, idx[t, l])
+            return x
+
+        for t in range(warmup):
+            token(t)
+        torch.cuda.synchronize()
+        s0, f0 = cache.stats(), cache.file_stats()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            ev[i][0].record()
+            token(warmup + i)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        s1, f1 = cache.stats(), cache.file_stats()
+        total_s = sum(a.elapsed_time(b) for a, b in ev) / 1e3
+        hits, misses = s1["hits"] - s0["hits"], s1["misses"] - s0["misses"]
+        read_b, read_s = f1["bytes"] - f0["bytes"], f1["seconds"] - f0["seconds"]
+        res = {
+            "tokens_per_s": steps / total_s, "ms_per_token": 1e3 * total_s / steps,
+            "hit_rate": hits / max(hits + misses, 1), "misses_per_token": misses / steps,
+            "read_gbs": read_b / max(read_s, 1e-9) / 1e9, "read_share_of_time": read_s / total_s,
+            "bytes_read_per_token": read_b / steps, "direct": f1["direct"], "failed_rounds": f1["failed_rounds"],
+            "layers": layers, "slots": slots, "file_experts": E, "file_gb": file_gb, "readers": readers,
+            "stage_experts": stage_experts, "steps": steps, "warmup": warmup,
+            "device_status": max(layer.status() for layer in stack),
+        }
+        for layer in stack:
+            layer.close()
+        cache.close()
+        return res
+    finally:
+        os.unlink(path)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--source", choices=("host", "file"), default="host")
+    ap.add_argument("--file-experts", type=int, default=32)
+    ap.add_argument("--slots", type=int, default=16)
+    ap.add_argument("--readers", type=int, default=8)
+    ap.add_argument("--direct", type=int, default=1)
+    ap.add_argument("--stage-experts", type=int, default=2)
+    ap.add_argument("--file-dir", default=None)
     ap.add_argument("--layers", type=int, default=58)
     ap.add_argument("--cache-gb", type=float, default=40.0)
     ap.add_argument("--store-experts", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
-    print(json.dumps(run(a.layers, a.cache_gb, a.store_experts, a.steps, a.warmup)), flush=True)
+    if a.source == "file":
+        print(json.dumps(run_file(a.layers, a.file_experts, a.slots, a.steps, a.warmup, a.readers, a.direct,
+                                  a.stage_experts, a.file_dir)), flush=True)
+    else:
+        print(json.dumps(run(a.layers, a.cache_gb, a.store_experts, a.steps, a.warmup)), flush=True)
 
 
 if __name__ == "__main__":

@@ -215,3 +215,40 @@ def test_malformed_files_are_refused(tmp_path):
     p.write_bytes(b"GGUF" + struct.pack("<IQQ", 3, 0, 1) + G.kv("general.alignment", G.U32, 0))
     assert "alignment" in _open_error(p)
     assert "cannot open" in _open_error(tmp_path / "missing.gguf")
+
+
+def test_mxfp4_blocks_writer_matches_the_oracle_converter():
+    # the product's writer-side conversion (gguf.mxfp4_to_blocks) against the oracle's restatement of
+    # the reference converter (tools/convert_official.py:187-201), itself pinned to golden vectors
+    from oracle import oracle as O
+    rng = np.random.default_rng(9)
+    for rows, k in ((1, 32), (7, 64), (128, 1024)):
+        codes = rng.integers(0, 256, (rows, k // 2), dtype=np.uint8)
+        scales = rng.integers(0, 256, (rows, k // 32), dtype=np.uint8)
+        assert np.array_equal(G.mxfp4_to_blocks(codes, scales), O.mxfp4_to_gguf(codes, scales).reshape(rows, -1))
+
+
+def test_repeated_tensor_data_and_expert_offsets(tmp_path):
+    # a checkpoint written from repeated chunks (no copy in memory) reads back chunk by chunk, and the
+    # expert tensors' offsets are where a file-backed cache reads them
+    H, I, E = 64, 32, 3
+    rng = np.random.default_rng(4)
+    chunk = {m: rng.integers(0, 256, (r * (k // 32) * 17,), dtype=np.uint8).tobytes()
+             for m, (r, k) in enumerate(((I, H), (I, H), (H, I)))}
+    tensors = [("blk.0.ffn_gate_inp.weight", G.T_F32, (H, E), bytes(H * E * 4))]
+    for m, part in enumerate(("gate", "up", "down")):
+        r, k = ((I, H), (I, H), (H, I))[m]
+        tensors.append((f"blk.0.ffn_{part}_exps.weight", G.T_MXFP4, (k, r, E), G.Repeated(chunk[m], E)))
+    path = tmp_path / "rep.gguf"
+    G.write_gguf(path, [], tensors)
+    raw = open(path, "rb").read()
+    with G.GgufFile(path) as g:
+        offs = G.expert_offsets(g, [0])[0]
+        for m, part in enumerate(("gate", "up", "down")):
+            t = g.tensor(f"blk.0.ffn_{part}_exps.weight")
+            assert t["offset"] == offs[m] and t["offset"] % 32 == 0 and t["nbytes"] == E * len(chunk[m])
+            for e in range(E):
+                o = offs[m] + e * len(chunk[m])
+                assert raw[o:o + len(chunk[m])] == chunk[m]
+        with pytest.raises(KeyError):
+            G.expert_offsets(g, [1])  # no such layer
