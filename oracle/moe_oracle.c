@@ -710,3 +710,41 @@ void orc_ref_hc_post(float *out, const float *x, const float *res, const float *
             out[(size_t)j * dim + d] = orc_bf16_round(post[j] * x[d] + s);
         }
 }
+
+/* ---- Q8 activation variant ---------------------------------------------------------------------- */
+
+void orc_q8_codes(const float *x, int n_blocks, int8_t *q, float *d) {
+    for (int b = 0; b < n_blocks; b++) {
+        const float *xb = x + (size_t)b * 32;
+        float amax = 0.f;
+        for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(xb[i]));
+        const float db = amax / 127.0f;
+        const float div = db > 0.f ? db : 1.0f;
+        for (int i = 0; i < 32; i++) {
+            float v = nearbyintf(xb[i] / div); /* round half to even (default rounding mode) */
+            v = fminf(fmaxf(v, -128.f), 127.f);
+            q[(size_t)b * 32 + i] = (int8_t)v;
+        }
+        d[b] = db;
+    }
+}
+
+void orc_gemv_mxfp4_q8(const uint8_t *w, const uint8_t *ws, int rows, int k, const int8_t *q, const float *d, int n_tok,
+                       float *y) {
+    const int nb = k / 32;
+    for (int t = 0; t < n_tok; t++)
+        for (int r = 0; r < rows; r++) {
+            double acc = 0.0;
+            for (int b = 0; b < nb; b++) {
+                /* twice the e2m1 values are integers: the block's sum is exact in integers */
+                long long s = 0;
+                for (int i = 0; i < 32; i++) {
+                    const uint8_t byte = w[(size_t)r * (k / 2) + b * 16 + i / 2];
+                    const int nib = (i & 1) ? byte >> 4 : byte & 15;
+                    s += (long long)q[(size_t)t * k + b * 32 + i] * (long long)(2.0f * kFp4[nib]);
+                }
+                acc += (double)s * 0.5 * (double)d[(size_t)t * nb + b] * ldexp(1.0, (int)ws[(size_t)r * nb + b] - 127);
+            }
+            y[(size_t)t * rows + r] = (float)acc;
+        }
+}

@@ -112,6 +112,18 @@ void orc_ref_rms_norm(float *out, const float *x, const float *w, int rows, int 
 void orc_ref_hc_post(float *out, const float *x, const float *res, const float *post, const float *comb, int hc,
                      int dim);                                                            /* :328-338 */
 
+/* ---- Q8 activation variant (ref/emulate_ds4.py: q8_codes :23-30, the FP4 branch of linear :69-77) --------
+ * Activations quantized per 32 values to int8 with scale d = amax / 127 (fp32, no fp16 rounding for
+ * activations), codes round-half-even(x / d) clamped to [-128, 127] (d = 0: divided by 1).  The FP4
+ * expert linear takes them instead of FP8 activations:
+ *   y[t][r] = sum_b d[t][b] * 2^(s[r][b] - 127) * sum_i q[t][b][i] * e2m1(w[r][b][i])
+ * with exact integer sums per block, the blocks added in double precision and the total rounded once
+ * to fp32 (the emulation's fp32 matmul differs from it only by its own summation's rounding).  Codes in the layer's layout (values 2j, 2j + 1 in byte j, low nibble
+ * first), e8m0 scales [rows][k/32] taken as 2^(s - 127). */
+void orc_q8_codes(const float *x, int n_blocks, int8_t *q, float *d);
+void orc_gemv_mxfp4_q8(const uint8_t *w, const uint8_t *ws, int rows, int k, const int8_t *q, const float *d, int n_tok,
+                       float *y);
+
 #ifdef __cplusplus
 }
 #endif

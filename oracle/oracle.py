@@ -181,6 +181,28 @@ def gemv_mxfp4(w, ws, xc, xs, act_block):
 
 # ---- router / dispatch ----------------------------------------------------------------------------
 
+def q8_codes(x):
+    """int8 codes and fp32 scales per 32 along the last axis (ref/emulate_ds4.py:23-30, activations)."""
+    x = np.ascontiguousarray(x, np.float32)
+    nb = x.size // 32
+    q = np.empty(x.shape, np.int8)
+    d = np.empty(x.shape[:-1] + (x.shape[-1] // 32,), np.float32)
+    lib().orc_q8_codes(ptr(x), I(nb), ptr(q), ptr(d))
+    return q, d
+
+
+def gemv_mxfp4_q8(w, ws, q, d):
+    """FP4 expert linear with Q8 activations (ref/emulate_ds4.py:69-77): w codes [rows][k/2], ws e8m0
+    [rows][k/32], q int8 [T][k], d fp32 [T][k/32] -> fp32 [T][rows]."""
+    w, ws = np.ascontiguousarray(w, np.uint8), np.ascontiguousarray(ws, np.uint8)
+    q, d = np.ascontiguousarray(q, np.int8), np.ascontiguousarray(d, np.float32)
+    rows, k = w.shape[0], w.shape[1] * 2
+    T = q.shape[0]
+    y = np.empty((T, rows), np.float32)
+    lib().orc_gemv_mxfp4_q8(ptr(w), ptr(ws), I(rows), I(k), ptr(q), ptr(d), I(T), ptr(y))
+    return y
+
+
 def router_logits(W, x_bits):
     W = _f32(W)
     x_bits = np.ascontiguousarray(x_bits, np.uint16)
