@@ -54,7 +54,7 @@ std::string ExpertReader::error() const {
 void ExpertReader::stats(uint64_t *pieces, uint64_t *bytes, double *seconds, int *direct) const {
     if (pieces) *pieces = pieces_.load();
     if (bytes) *bytes = bytes_.load();
-    if (seconds) *seconds = seconds_;
+    if (seconds) *seconds = 1e-9 * (double)ns_.load();
     if (direct) *direct = direct_on_.load() ? 1 : 0;
 }
 
@@ -151,7 +151,7 @@ bool ExpertReader::read(int n, const uint64_t *off, const uint64_t *bytes, uint8
         std::unique_lock<std::mutex> lk(mu_);
         cv_done_.wait(lk, [&] { return active_ == 0; });
     }
-    seconds_ += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    ns_ += (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
     return ok_.load();
 }
 

@@ -59,7 +59,7 @@ class ExpertReader {
     std::atomic<size_t> next_{0};
     std::atomic<bool> ok_{true};
     std::atomic<uint64_t> pieces_{0}, bytes_{0};
-    double seconds_ = 0;
+    std::atomic<uint64_t> ns_{0};  // time spent in read(); stats() may run during a read
     std::atomic<int64_t> inject_left_{-1};
     std::atomic<int> inject_errno_{0};
     mutable std::mutex err_mu_;
