@@ -202,6 +202,12 @@ const char *stbl_cache_error(const stbl_cache *c);
 int stbl_cache_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, cudaStream_t stream,
                         cudaStream_t copy_stream);
 int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_t *used, uint64_t *bytes);
+/* The same counters in the layout of the reference's stbl_prefetch (stbl/stbl.h:23-24, printed by
+ * stbl/run.py:100): out[0] guesses issued, out[1] guesses routed to after they landed, out[2] guesses
+ * routed to while still being read, out[3] guesses cancelled.  A demand call here waits for the whole
+ * prefetch copy before it plans, so every routed guess has landed (out[2] = 0) and none is cancelled
+ * (out[3] = 0).  Waits for the device. */
+int stbl_cache_prefetch_counters(const stbl_cache *c, uint64_t *out);
 /* Each call of layer m (attached to a cache) then also runs `next`'s router on m's input and prefetches
  * its top n_predict experts per token (first `consider` distinct ones, stbl_cache_prefetch) for `next`,
  * copied on copy_stream beside m's expert kernels.  next: a layer attached to the same cache, or NULL

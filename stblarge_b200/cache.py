@@ -106,6 +106,14 @@ class ExpertCache:
             raise RuntimeError("stbl_cache_prefetch_stats failed")
         return {"prefetched": p.value, "used": u.value, "bytes": b.value}
 
+    def prefetch_counters(self):
+        """The reference's stbl_prefetch layout: issued, routed after landing, routed while reading,
+        cancelled."""
+        out = (L.U64 * 4)()
+        if self.lib.stbl_cache_prefetch_counters(self.handle, out) != 0:
+            raise RuntimeError("stbl_cache_prefetch_counters failed")
+        return [int(v) for v in out]
+
     def file_stats(self):
         """File-backed caches: pieces and bytes read, seconds the read steps took, whether reads go
         through O_DIRECT, read rounds that failed."""

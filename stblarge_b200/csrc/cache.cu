@@ -820,6 +820,14 @@ int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_
     return 0;
 }
 
+int stbl_cache_prefetch_counters(const stbl_cache *c, uint64_t *out) {
+    if (!out) return -1;
+    uint64_t issued = 0, used = 0;
+    if (stbl_cache_prefetch_stats(c, &issued, &used, nullptr) != 0) return -1;
+    out[0] = issued, out[1] = used, out[2] = 0, out[3] = 0;
+    return 0;
+}
+
 int stbl_cache_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, cudaStream_t stream,
                         cudaStream_t copy_stream) {
     try {

@@ -71,6 +71,7 @@ SIGNATURES = {
     "stbl_cache_prefetch": (I, [P, I, P, I, I, P, P]),
     "stbl_cache_prefetch_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
     "stbl_moe_attach_prefetch": (I, [P, P, I, I, P]),
+    "stbl_cache_prefetch_counters": (I, [P, ctypes.POINTER(U64)]),
     "stbl_cache_create_file": (I, [ctypes.POINTER(CacheDesc), ctypes.POINTER(CacheFileDesc), ctypes.POINTER(P),
                                    ctypes.c_char_p, I]),
     "stbl_cache_file_stats": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(ctypes.c_double),

@@ -173,6 +173,7 @@ def test_shadow_prefetch_matches_resident_layers_and_reference_lru(cfg, S):
             assert (st["hits"], st["misses"]) == (lru.hits, lru.misses)
             assert (pf["prefetched"], pf["used"]) == (lru.prefetched, lru.pf_used)
     assert lru.prefetched > 0 and lru.pf_used > 0
+    assert cache.prefetch_counters() == [lru.prefetched, lru.pf_used, 0, 0]
     for layer in cached + plain:
         assert layer.status() == 0
         layer.close()
