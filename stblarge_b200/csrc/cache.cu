@@ -411,10 +411,38 @@ __global__ void __launch_bounds__(kCopyThreads) cache_file_copy_kernel(FileCopyP
     }
 }
 
-// The read step of one round, run by the CUDA runtime in stream order (no CUDA calls here): reads the
-// round's experts into the staging rows and publishes where each matrix's data starts.
+// marks round fr's jobs as failed: status for its copy, slots for the next planner, the message
+void file_round_failed(const FileRound *fr, int begin, int n, const std::string &why) {
+    FileStore *f = fr->c->file;
+    const volatile int2 *jobs = f->jobs_h[fr->which];
+    volatile unsigned char *bad = f->bad;
+    for (int j = 0; j < n; j++) bad[jobs[begin + j].x] = 1;
+    *(volatile int *)f->n_bad = 1;
+    ((volatile uint32_t *)f->fstat)[fr->round & 1] = 1;
+    f->failed_rounds++;
+    std::lock_guard<std::mutex> lk(f->mu);
+    f->err = "expert read failed: " + why;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+}
+
+void file_round_read(const FileRound *fr);
+
+// The read step of one round, run by the CUDA runtime in stream order (no CUDA calls here).  Nothing
+// may escape a runtime callback: an exception counts as a failed read.
 void CUDART_CB file_round_host(void *arg) {
     const FileRound *fr = static_cast<const FileRound *>(arg);
+    try {
+        file_round_read(fr);
+    } catch (const std::exception &e) {
+        FileStore *f = fr->c->file;
+        const int nj = *(volatile const int *)f->n_jobs_h[fr->which];
+        const int begin = fr->round * f->cap, n = std::max(0, std::min(nj, begin + f->cap) - begin);
+        file_round_failed(fr, begin, n, e.what());
+    }
+}
+
+// reads the round's experts into the staging rows and publishes where each matrix's data starts
+void file_round_read(const FileRound *fr) {
     stbl_cache *c = fr->c;
     FileStore *f = c->file;
     const int buf = fr->round & 1;
@@ -435,14 +463,7 @@ void CUDART_CB file_round_host(void *arg) {
         }
     }
     if (!f->reader->read(3 * n, off.data(), bytes.data(), region.data(), at.data())) {
-        volatile unsigned char *bad = f->bad;
-        for (int j = 0; j < n; j++) bad[jobs[begin + j].x] = 1;
-        *(volatile int *)f->n_bad = 1;
-        *fstat = 1;
-        f->failed_rounds++;
-        std::lock_guard<std::mutex> lk(f->mu);
-        f->err = "expert read failed: " + f->reader->error();
-        std::atomic_thread_fence(std::memory_order_seq_cst);
+        file_round_failed(fr, begin, n, f->reader->error());
         return;
     }
     for (int i = 0; i < 3 * n; i++) f->src[(size_t)buf * f->cap * 3 + i] = f->stage_d + (region[i] - f->stage) + at[i];
