@@ -601,16 +601,19 @@ void host_mapped(T **h, T **d, size_t bytes) {
     CK(cudaHostGetDevicePointer((void **)d, (void *)*h, 0));
 }
 
-void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
+void file_desc_check(const stbl_cache_desc *d, const stbl_cache_file_desc *fd) {
     if (!fd->path || !fd->offset) throw std::runtime_error("file desc: path and offset are required");
     if (fd->readers < 0 || fd->stage_experts < 0) throw std::runtime_error("file desc: readers and stage_experts must be >= 0");
+    for (long long i = 0; i < 3LL * d->n_layers; i++)
+        if (fd->offset[i] % 16) throw std::runtime_error("expert tensor offsets must be multiples of 16 (GGUF alignment >= 16)");
+}
+
+void file_store_new(stbl_cache *c, const stbl_cache_file_desc *fd) {
     FileStore *f = new FileStore();
     c->file = f;
     const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
     for (int q = 0; q < 3; q++) f->gbytes[q] = (uint64_t)rows[q] * (ks[q] / 32) * 17;
     f->offset.assign(fd->offset, fd->offset + 3 * (size_t)c->L);
-    for (uint64_t o : f->offset)
-        if (o % 16) throw std::runtime_error("expert tensor offsets must be multiples of 16 (GGUF alignment >= 16)");
     long long off = 0;
     for (int q = 0; q < 3; q++) f->region_off[q] = off, off += (long long)read_region_bytes(f->gbytes[q]);
     f->row_bytes = off;
@@ -674,6 +677,7 @@ static stbl_cache *cache_new(const stbl_cache_desc *d, const stbl_cache_file_des
         if (d->slots < 0 || d->slots > (1 << 20) - 1) throw std::runtime_error("slots must be in 0..2^20-1");
         if (d->fmt != STBL_FMT_FP8_B128 && d->fmt != STBL_FMT_MXFP4) throw std::runtime_error("bad fmt");
         if (f && d->fmt != STBL_FMT_MXFP4) throw std::runtime_error("a file-backed cache holds MXFP4 experts (GGUF type 39)");
+        if (f) file_desc_check(d, f);  // before any device call
         if (d->hidden <= 0 || d->inter <= 0 || d->hidden % 512 || d->inter % 512)
             throw std::runtime_error("hidden and inter must be multiples of 512");
         if ((long long)d->n_layers * d->n_experts >= (1LL << 31)) throw std::runtime_error("store too large");
