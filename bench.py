@@ -1,23 +1,27 @@
 """MoE-layer decode benchmark (BASELINE.json metric: decode tokens/s and achieved HBM GB/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl b200|reference] [--workload ...]
 
-A step is one call of the full-size DeepSeek-V3-shaped MoE layer (configs[1]: hidden 7168,
-moe_intermediate 2048, 256 routed experts + 1 shared, top-8 of 8 groups keeping 4, FP8 128x128
-block-scaled weights) on T decode tokens (default 16), with weights resident in HBM.  Every step
+A step is one call of a full-size DeepSeek-V3-shaped MoE layer (hidden 7168, moe_intermediate 2048,
+256 routed experts + 1 shared, top-8 of 8 groups keeping 4), weights resident in HBM.  Every step
 gets fresh tokens (different routing), and L2 is flushed before each step; each step is timed with
 CUDA events on the launching stream.  `e2e` is the same metric through the host-buffer entry point
 (stbl_moe_forward_host: H2D of x, layer, D2H of y, inside the timed region).
 
-N > 1: one process per GPU, expert parallelism: rank r holds routed experts [r 256/N, (r+1) 256/N)
-(the router and the shared expert are replicated); every rank routes its own tokens, and the
-layer's kernels dispatch them to the owning ranks and bring the outputs back through NVLink peer
-memory.  --workload cfg2 (default): T tokens per rank (weak scaling, the N=1 line is configs[1]);
---workload cfg4: configs[3], 256 tokens in all split over the ranks (strong scaling), uniform
-routing (bias 0) or Zipf(1.2) with --zipf.  Time = max over ranks of the device time.
+Default workload:
+  * one GPU: configs[1] (cfg2, FP8 128x128 weights) at T = 16 decode tokens, the headline; the line
+    also carries `sweep` (configs[1] at T = 1, 4, 16), `cfg3_sweep` (configs[2]: MXFP4 routed experts,
+    FP8 shared, Zipf(1.0) bias, T = 1, 4, 16, 64) and `cfg4_n1` (configs[3]'s 256 tokens on this one
+    GPU: the N = 1 point of the strong-scaling curve);
+  * N > 1 GPUs: configs[3] (cfg4), 256 tokens in all split over the ranks (strong scaling), expert
+    parallelism: rank r holds routed experts [r 256/N, (r+1) 256/N) (router and shared expert
+    replicated), every rank routes its own tokens and the layer's kernels dispatch them to the owning
+    ranks and bring the outputs back through NVLink peer memory.  The line also carries `weak_cfg2`
+    (configs[1] with 16 tokens per rank).  Time = max over ranks of the device time.
+--workload cfg2|cfg3|cfg3ref|cfg4|cfg5 picks one explicitly (--zipf: Zipf(1.2) routing for cfg4).
 
 --impl reference: the reference's CPU path (the CPU oracle restating stbl/model.cu:426-594 on the
-numerics of ref/kernel.py) on the host cores, same workload and metric; rank 0 only.
+numerics of ref/kernel.py) on the host cores, the same workload, config and metric; rank 0 only.
 """
 
 import argparse
@@ -183,40 +187,87 @@ def cpu_oracle_layer(cfg, W_host, x_bits, nthreads):
     return time.perf_counter() - t0
 
 
-def run_reference(args, rank):
-    """The reference's CPU path on this host's cores, on the b200 arm's workload."""
+def workload_of(args, world):
+    """(name, cfg, tokens per rank).  Default: configs[1] (cfg2, T tokens) on one GPU; configs[3]
+    (cfg4, 256 tokens split over the ranks, expert parallelism) on more than one."""
+    import dataclasses
+    wl = args.workload or ("cfg2" if world == 1 else "cfg4")
+    if wl == "cfg4":
+        if 256 % world:
+            raise SystemExit("cfg4 splits 256 tokens over the ranks: --gpus must divide 256")
+        return wl, dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=1.2 if args.zipf else 0.0), 256 // world
+    if wl == "cfg3":
+        return wl, CFG3, args.tokens
+    if wl == "cfg3ref":
+        return wl, CFG3_REF, args.tokens
+    return wl, CFG2, args.tokens
+
+
+def config_of(args, wl, T, world):
+    """The `config` object of the JSON line: the same for the b200 arm and the reference arm."""
+    E_loc = 256 // world
+    return {"workload": (f"cfg4 expert-parallel full-size FP8 MoE layer, 256 tokens split over {world} GPU(s), "
+                         f"{'Zipf(1.2)' if args.zipf else 'uniform'} routing"
+                         if wl == "cfg4" else
+                         "cfg3 full-size layer, MXFP4 routed experts (FP8 shared), Zipf(1.0) routing"
+                         if wl == "cfg3" else
+                         "cfg3ref full-size layer in the reference engine's formats and routing: MXFP4 routed "
+                         "experts, FP8 shared expert with e8m0 32x32 block scales, sqrt(softplus) top-8 of 256"
+                         if wl == "cfg3ref" else
+                         "cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4)")
+                        + f", T={T} decode tokens per rank", "tokens_per_rank": T,
+            "parallelism": "single GPU" if world == 1 else
+            f"ep{world}: expert parallelism, {E_loc} routed experts per GPU, dispatch/combine through NVLink peer memory",
+            "l2": "flushed (256 MB write) before every timed step; fresh tokens each step"}
+
+
+def step_tokens(cfg, T, world, step):
+    """The tokens of one step of the whole job (every rank's, rank-major), bf16 bits [world * T, H]."""
+    return np.concatenate([synth.make_x(cfg.hidden, T, seed=1_000_000 * (r + 1) + step) for r in range(world)])
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU path (the oracle restating stbl/model.cu:426-594 on the numerics of
+    ref/kernel.py) on this host's cores, on the b200 arm's workload and config: each step is one layer
+    call on the whole job's tokens of that step (every rank's), rank 0 only."""
     if rank != 0:
         return
     import torch
-    from oracle import oracle as O
-    cfg, T = CFG2, args.tokens
+    wl, cfg, T = workload_of(args, world)
+    if cfg.routed_fmt != CFG2.routed_fmt:
+        raise SystemExit("the reference arm times the FP8 workloads (cfg2, cfg4)")
     cores = os.cpu_count()
     torch.set_num_threads(cores)
-    # routing uses the real router; expert weights come from a pool of 8 generated experts aliased
-    # behind the 256 ids (the oracle's work does not depend on the weight values)
+    # 8 generated experts; each of the 256 ids holds its own copy of one of them with every code row
+    # rotated by a per-id amount, so the oracle streams 256 distinct experts' bytes (the real working
+    # set) with the value distribution of the generated weights
     g = torch.Generator().manual_seed(1000)
     pool = []
     for _ in range(8):
         ws = []
         for (r, k) in synth.mat_shapes(cfg):
-            c, s = synth.quant_fp8_b128(torch.randn(r, k, generator=g) * cfg.weight_std)
-            ws.append((c.numpy(), s.numpy()))
+            c, s_ = synth.quant_fp8_b128(torch.randn(r, k, generator=g) * cfg.weight_std)
+            ws.append((c.numpy(), s_.numpy()))
         pool.append(ws)
-    W = {"router_w": synth.router_w(cfg), "router_bias": synth.router_bias(cfg),
-         "routed": [[pool[e % 8][m] for e in range(cfg.n_experts)] for m in range(3)], "shared": pool[0]}
-    xs = [synth.make_x(cfg.hidden, T, seed=10_000 + i) for i in range(args.warmup + args.steps)]
+    routed = [[(np.roll(pool[e % 8][m][0], 1 + e // 8, axis=1), pool[e % 8][m][1]) for e in range(cfg.n_experts)]
+              for m in range(3)]
+    W = {"router_w": synth.router_w(cfg), "router_bias": synth.router_bias(cfg), "routed": routed, "shared": pool[0]}
+    Tj = T * world
     for i in range(args.warmup):
-        cpu_oracle_layer(cfg, W, xs[i], cores)
+        cpu_oracle_layer(cfg, W, step_tokens(cfg, T, world, i), cores)
     total = 0.0
     for i in range(args.steps):
-        total += cpu_oracle_layer(cfg, W, xs[args.warmup + i], cores)
-    value = T * args.steps / total
-    sample = f"{args.steps} full layer calls of the T={T} workload on the CPU oracle, {cores} threads"
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        total += cpu_oracle_layer(cfg, W, step_tokens(cfg, T, world, args.warmup + i), cores)
+    value = Tj * args.steps / total
+    sample = (f"{args.steps} full layer calls of {Tj} tokens each (the whole job's tokens of a step) on the CPU "
+              f"oracle with {cores} threads; the 256 experts are distinct in memory (8 generated experts, "
+              f"code rows rotated per id)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 x fp32-accumulate",
-            "data": "synthetic", "config": {"workload": f"cfg2 full-size FP8 MoE layer, T={T} decode tokens",
-                                            "tokens": T, "l2": "n/a (CPU)"},
+            "higher_is_better": True, "scaling": "strong" if wl == "cfg4" else "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 weights and activations, fp32 accumulate, bf16 io",
+            "data": "synthetic (seeded ~N(0,0.02) weights quantized to FP8 128x128; bf16 ~N(0,1) tokens)",
+            "config": config_of(args, wl, T, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -252,15 +303,46 @@ def run_streamed(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def sweep_layer(layer, cfg, token_counts, distinct_of, timed_steps, peak, seed0):
+    """Device time per call and per kernel at each decode batch size in token_counts (20 timed calls
+    each, L2 flushed before every call, fresh tokens), with the HBM fraction of the layer and of its
+    up kernel."""
+    import torch
+    out = []
+    dev = torch.device("cuda", torch.cuda.current_device())
+    for Ts in token_counts:
+        xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=seed0 + 100 * Ts + i).view(np.int16)).to(dev)
+               for i in range(23)]
+        for i in range(3):
+            layer(xs2[i])
+        torch.cuda.synchronize()
+        base = layer.timing()
+        layer.set_timing(True)
+        ms = timed_steps(layer, xs2[3:])
+        layer.set_timing(False)
+        k2 = layer.timing()
+        n2 = max(k2["calls"] - base["calls"], 1)
+        dd = [distinct_of(layer, x) for x in xs2[3:]]
+        mean_ms = float(np.mean(ms))
+        gbs = np.mean([layer_bytes(cfg, d, Ts) for d in dd]) / (mean_ms / 1e3) / 1e9
+        kms = {k: (k2[k] - base[k]) / n2 * 1e3 for k in ("router", "up", "down")}
+        up_gbs = np.mean([up_bytes(cfg, d) for d in dd]) / (kms["up"] / 1e3) / 1e9
+        out.append({"tokens": Ts, "tokens_per_s": Ts / (mean_ms / 1e3), "ms_per_call": mean_ms,
+                    "distinct_experts": float(np.mean(dd)), "hbm_gbs": float(gbs), "hbm_frac_of_measured": float(gbs / peak),
+                    "kernel_ms": kms, "up_gbs": float(up_gbs), "up_frac_of_measured": float(up_gbs / peak)})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg3ref", "cfg4", "cfg5"])
+    ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg3ref", "cfg4", "cfg5"],
+                    help="default: cfg2 on one GPU, cfg4 on more")
     ap.add_argument("--zipf", action="store_true", help="cfg4: Zipf(1.2) expert popularity instead of uniform")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -270,11 +352,13 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if args.workload == "cfg5":
         run_streamed(args, rank, world)
         return
+
+    import dataclasses
 
     import torch
     import torch.distributed as dist
@@ -286,33 +370,22 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    import dataclasses
-    if args.workload == "cfg4":
-        cfg = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=1.2 if args.zipf else 0.0)
-        if 256 % world:
-            raise SystemExit("cfg4 splits 256 tokens over the ranks: --gpus must divide 256")
-        T = 256 // world
-    elif args.workload == "cfg3":
-        cfg, T = CFG3, args.tokens
-    elif args.workload == "cfg3ref":
-        cfg, T = CFG3_REF, args.tokens
-    else:
-        cfg, T = CFG2, args.tokens
+    wl, cfg, T = workload_of(args, world)
     E_loc = cfg.n_experts // world
     shard = range(rank * E_loc, (rank + 1) * E_loc)
     weights = synth.device_layer(cfg, device=dev, experts=shard)
-    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if args.workload in ("cfg3", "cfg3ref") else 16),
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if wl in ("cfg3", "cfg3ref") else 16),
                      ep=(rank, world, None) if world > 1 else None)
     n_steps = args.warmup + args.steps
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
                       for i in range(n_steps)]).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
 
-    def distinct_of(x):
+    def distinct_of(lay, x):
         """Distinct routed experts of this rank's shard that the step streams: the experts that any
         rank's tokens are routed to (untimed pass, every rank in step; routes read back)."""
-        layer(x)
-        ids = layer.last_route()["idx"]
+        lay(x)
+        ids = lay.last_route()["idx"]
         if world > 1:
             allids = [None] * world
             dist.all_gather_object(allids, ids)
@@ -320,17 +393,23 @@ def main():
         ids = np.unique(ids)
         return int(np.sum((ids >= shard.start) & (ids < shard.stop)))
 
-    def timed_steps(inputs):
+    def timed_steps(lay, inputs):
         """Device time of each call, L2 flushed before each; nothing synchronises inside the loop, so
         the host runs ahead and the GPU executes flush, layer, flush, layer ... back to back."""
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in inputs]
         for x, (a, b) in zip(inputs, evs):
             flush.zero_()
             a.record()
-            layer(x)
+            lay(x)
             b.record()
         torch.cuda.synchronize()
         return [a.elapsed_time(b) for a, b in evs]
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     for i in range(args.warmup):
         layer(xs[i])
@@ -342,19 +421,16 @@ def main():
     sampler.start()
     layer.timing()
     layer.set_timing(True)
-    step_ms = timed_steps([xs[args.warmup + i] for i in range(args.steps)])
+    step_ms = timed_steps(layer, [xs[args.warmup + i] for i in range(args.steps)])
     layer.set_timing(False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
     kt = layer.timing()
-    distinct = [distinct_of(xs[args.warmup + i]) for i in range(args.steps)]
+    distinct = [distinct_of(layer, xs[args.warmup + i]) for i in range(args.steps)]
     total_s = sum(step_ms) / 1e3
-    t = torch.tensor([total_s], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_max = float(t.item())
+    total_max = max_over_ranks(total_s)
     value = world * T * args.steps / total_max
     bytes_steps = [layer_bytes(cfg, d, T) for d in distinct]
     hbm_gbs = sum(bytes_steps) / total_s / 1e9
@@ -378,33 +454,14 @@ def main():
         e2e_ev[i][1].record(stream)
     torch.cuda.synchronize()
     e2e_s = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
-    t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * T * args.steps / float(t.item())
+    e2e_value = world * T * args.steps / max_over_ranks(e2e_s)
 
-    # batch-size sweep of configs[1] (1, 4, 16 tokens): device time per call and per kernel
+    extra = {}
     sweep = []
-    if not args.no_sweep and world == 1 and args.workload in ("cfg2", "cfg3", "cfg3ref"):
-        for Ts in ((1, 4, 16) if args.workload == "cfg2" else (1, 4, 16, 64)):
-            xs2 = [torch.from_numpy(synth.make_x(cfg.hidden, Ts, seed=7_000_000 + 100 * Ts + i).view(np.int16)).to(dev)
-                   for i in range(23)]
-            for i in range(3):
-                layer(xs2[i])
-            torch.cuda.synchronize()
-            layer.timing()
-            base = layer.timing()
-            layer.set_timing(True)
-            ms = timed_steps(xs2[3:])
-            layer.set_timing(False)
-            k2 = layer.timing()
-            n2 = max(k2["calls"] - base["calls"], 1)
-            dd = [distinct_of(x) for x in xs2[3:]]
-            mean_ms = float(np.mean(ms))
-            gbs = np.mean([layer_bytes(cfg, d, Ts) for d in dd]) / (mean_ms / 1e3) / 1e9
-            sweep.append({"tokens": Ts, "tokens_per_s": Ts / (mean_ms / 1e3), "ms_per_call": mean_ms,
-                          "distinct_experts": float(np.mean(dd)), "hbm_gbs": gbs, "hbm_frac_of_measured": gbs / peak,
-                          "kernel_ms": {k: (k2[k] - base[k]) / n2 * 1e3 for k in ("router", "up", "down")}})
+    if not args.no_sweep and world == 1 and wl in ("cfg2", "cfg3", "cfg3ref"):
+        # batch sizes of the workload's config: configs[1] 1, 4, 16; configs[2] 1, 4, 16, 64
+        sweep = sweep_layer(layer, cfg, (1, 4, 16) if wl == "cfg2" else (1, 4, 16, 64), distinct_of, timed_steps,
+                            peak, 7_000_000)
     status = layer.status()
 
     cpu = None
@@ -424,30 +481,64 @@ def main():
         cpu = {"value": T / dt, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"1 layer call of the T={T} workload (the first timed step's tokens) on the CPU oracle"}
 
+    if not args.no_sweep and world == 1 and wl == "cfg2":
+        # configs[3] on this one GPU (256 tokens, the same FP8 experts with bias 0): the N = 1 point of
+        # the strong-scaling curve that `--gpus N` (default workload cfg4) measures at N > 1
+        cfg4 = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=0.0)
+        w4 = dict(weights)
+        w4["router_bias"] = torch.from_numpy(synth.router_bias(cfg4)).to(dev)
+        l4 = MoELayer(cfg4, w4, max_tokens=256)
+        x4 = [torch.from_numpy(synth.make_x(cfg4.hidden, 256, seed=1_000_000 + i).view(np.int16)).to(dev)
+              for i in range(args.warmup + 20)]
+        for i in range(args.warmup):
+            l4(x4[i])
+        ms4 = timed_steps(l4, x4[args.warmup:])
+        extra["cfg4_n1"] = {"workload": "cfg4 (configs[3]) on one GPU: 256 tokens, uniform routing, full-size FP8",
+                            "tokens_per_s": 256 * len(ms4) / (sum(ms4) / 1e3), "ms_per_step": float(np.mean(ms4)),
+                            "steps": len(ms4), "device_status": l4.status()}
+        l4.close()
+        del w4, l4
+        # configs[2] (MXFP4 routed experts, FP8 shared, Zipf(1.0)) at T = 1, 4, 16, 64 on this GPU
+        layer.close()
+        del weights, layer
+        torch.cuda.empty_cache()
+        w3 = synth.device_layer(CFG3, device=dev)
+        l3 = MoELayer(CFG3, w3, max_tokens=64)
+        extra["cfg3_sweep"] = sweep_layer(l3, CFG3, (1, 4, 16, 64), distinct_of, timed_steps, peak, 8_000_000)
+        extra["cfg3_device_status"] = l3.status()
+        l3.close()
+        layer = None
+
+    if world > 1 and not args.no_sweep and wl == "cfg4":
+        # weak scaling beside it: configs[1] with 16 tokens per rank (the same shard, configs[1]'s bias)
+        w2 = dict(weights)
+        w2["router_bias"] = torch.from_numpy(synth.router_bias(CFG2)).to(dev)
+        l2 = MoELayer(CFG2, w2, max_tokens=16, ep=(rank, world, None))
+        x2 = [torch.from_numpy(synth.make_x(CFG2.hidden, 16, seed=2_000_000 * (rank + 1) + i).view(np.int16)).to(dev)
+              for i in range(args.warmup + 20)]
+        for i in range(args.warmup):
+            l2(x2[i])
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms2 = timed_steps(l2, x2[args.warmup:])
+        t2 = max_over_ranks(sum(ms2) / 1e3)
+        extra["weak_cfg2"] = {"workload": "cfg2 (configs[1]) with 16 tokens per rank, expert parallelism",
+                              "tokens_per_s": world * 16 * len(ms2) / t2, "ms_per_step": 1e3 * t2 / len(ms2),
+                              "steps": len(ms2), "device_status": l2.status()}
+        l2.close()
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
-            "scaling": "strong" if args.workload == "cfg4" else "weak", "vs_baseline": None,
+            "scaling": "strong" if wl == "cfg4" else "weak", "vs_baseline": None,
             "dtype": ("fp8-e4m3 weights and activations, fp32 accumulate, bf16 io" if cfg.routed_fmt != FMT_MXFP4 else
                       "e2m1 routed / e4m3 shared weights, e4m3 activations, fp32 accumulate, bf16 io"),
             "data": ("synthetic (seeded ~N(0,0.02) weights quantized to "
                      + {"cfg3": "MXFP4 routed / FP8 128x128 shared",
-                        "cfg3ref": "MXFP4 routed / FP8 e8m0-32x32 shared"}.get(args.workload, "FP8 128x128")
+                        "cfg3ref": "MXFP4 routed / FP8 e8m0-32x32 shared"}.get(wl, "FP8 128x128")
                      + "; bf16 ~N(0,1) tokens)"),
-            "config": {"workload": (f"cfg4 expert-parallel full-size FP8 MoE layer, 256 tokens split over {world} GPU(s), "
-                                    f"{'Zipf(1.2)' if args.zipf else 'uniform'} routing"
-                                    if args.workload == "cfg4" else
-                                    "cfg3 full-size layer, MXFP4 routed experts (FP8 shared), Zipf(1.0) routing"
-                                    if args.workload == "cfg3" else
-                                    "cfg3ref full-size layer in the reference engine's formats and routing: MXFP4 routed "
-                                    "experts, FP8 shared expert with e8m0 32x32 block scales, sqrt(softplus) top-8 of 256"
-                                    if args.workload == "cfg3ref" else
-                                    "cfg2 full-size FP8 MoE layer (7168/2048, 256+1 experts, top-8, 8 groups keep 4)")
-                                   + f", T={T} decode tokens per rank", "tokens_per_rank": T,
-                       "parallelism": "single GPU" if world == 1 else
-                       f"ep{world}: expert parallelism, {E_loc} routed experts per GPU, dispatch/combine through NVLink peer memory",
-                       "l2": "flushed (256 MB write) before every timed step; fresh tokens each step"},
+            "config": config_of(args, wl, T, world),
             "hbm_gbs": hbm_gbs, "hbm_frac_of_measured": hbm_gbs / peak, "hbm_frac_of_8tbs": hbm_gbs / HBM_NOMINAL_GBS,
             "hbm_note": "per GPU (rank 0): its shard's distinct routed experts + shared expert + router + x/y, over its device time",
             "distinct_experts_per_step": float(np.mean(distinct)),
@@ -468,9 +559,11 @@ def main():
             "gpu_launches": launches * args.steps,
             "clocks": clocks, "sweep": sweep, "device_status": status,
             "cpu_baseline": cpu,
+            **extra,
         }
         print(json.dumps(line), flush=True)
-    layer.close()
+    if layer is not None:
+        layer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

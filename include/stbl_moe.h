@@ -1,7 +1,7 @@
 /* B200-native MoE decode layer: layer-level C ABI (libstbl_moe.so).
  *
  * Drop-in for the reference's MoE layer, stbl/model.cu:426-594 (moe(), the body of
- * stbl_block_test stage 4, stbl/stbl.h:75-81), in the reference's C-ABI style: plain pointers and
+ * stbl_block_test stage 4, stbl/stbl.h:25-31), in the reference's C-ABI style: plain pointers and
  * sizes, int status (0 ok, -1 error, message from stbl_moe_error), caller-owned device buffers,
  * work ordered on the caller's cudaStream_t.  Routing, dispatch, the expert products and the
  * combine all stay on the GPU: there is no device->host copy inside a layer call.
@@ -89,13 +89,31 @@ int stbl_moe_forward(stbl_moe *m, const void *x_bf16, int T, void *y_bf16, cudaS
 int stbl_moe_forward_host(stbl_moe *m, const void *x_bf16_host, int T, void *y_bf16_host, cudaStream_t stream);
 
 /* Routing of the last call, copied to host (waits for the stream): idx [T][topk] in selection order
- * (stbl_last_route, stbl/stbl.h:85-86), weights [T][topk], counts [E], offsets [E+1] and the
+ * (stbl_last_route, stbl/stbl.h:35-36), weights [T][topk], counts [E], offsets [E+1] and the
  * bucketed dispatch permutation perm [T*topk] (perm[p] = token * topk + slot, expert-major, token
  * order inside an expert).  Any pointer may be NULL.  Returns T of that call, or -1. */
 int stbl_moe_last_route(stbl_moe *m, int *idx, float *weights, int *counts, int *offsets, int *perm);
 
 /* Router scores of the last call (fp32 [T][E]), for parity checks.  Returns T, or -1. */
 int stbl_moe_last_scores(stbl_moe *m, float *scores);
+
+/* The quantized activations of the last call as the expert kernels read them, copied to host (waits
+ * for the device), for bit-exact checks of the layer's own act_quant steps against the reference's
+ * rule (ref/kernel.py:35-45; stbl/kernels.cu:56-63; the reference tests them at tolerance 0,
+ * stbl/test_kernels.py:63-69).  `which`:
+ *   STBL_ACTS_X_ROUTED  x as the routed experts read it: rows T, width hidden
+ *   STBL_ACTS_X_SHARED  x as the shared expert reads it: rows T, width hidden
+ *   STBL_ACTS_H_ROUTED  h of the routed assignments by dispatch position (perm): rows T*topk, width inter
+ *   STBL_ACTS_H_SHARED  h of the shared expert by token: rows T, width inter
+ * h_bf16 (h rows only; may be NULL): the bf16 values that were quantized, [rows][width]; codes: e4m3
+ * [rows][width]; scales: fp32 [rows][width / blk], blk 128 (fp32 scale amax/448) for FP8 128x128
+ * weights, 32 (power-of-two scale, stored as e8m0) for MXFP4 and FP8-e8m0 weights.  Any output
+ * pointer may be NULL.  Single-GPU layers.  Returns the row count, or -1. */
+#define STBL_ACTS_X_ROUTED 0
+#define STBL_ACTS_X_SHARED 1
+#define STBL_ACTS_H_ROUTED 2
+#define STBL_ACTS_H_SHARED 3
+int stbl_moe_last_acts(stbl_moe *m, int which, void *h_bf16, void *codes, float *scales);
 
 /* Point routed expert e at another slot of the layer's expert arrays (an expert cache: the arrays
  * passed in the description are the slot pool, slot j at routed_w[m] + j * routed_w_stride[m]).  w and
@@ -242,7 +260,7 @@ int stbl_moe_forward_block(stbl_moe *m, const float *x_pre, const float *norm_w,
 int stbl_moe_status(stbl_moe *m, uint32_t *status);
 
 /* Per-kernel device timing, the counterpart of the reference's STBL_TIMING / stbl_timing
- * (stbl/model.cu:13-15, 250-258; stbl/stbl.h:82-84), without its stream synchronisations: while
+ * (stbl/model.cu:13-15, 250-258; stbl/stbl.h:32-34), without its stream synchronisations: while
  * enabled, every call records CUDA events on its stream around the router, expert-up and
  * expert-down launches.  stbl_moe_timing waits for the recorded events, adds their durations to
  * per-section totals in seconds (order: router, expert up, expert down; sec[3] = number of calls
@@ -278,8 +296,8 @@ int stbl_moe_ep_connect(stbl_moe *m, const void *handles /* n_ranks x STBL_EP_HA
  * engines that own a fixed memory pool and allow no allocation outside it, embedded runtimes without
  * an allocator.  It runs the layer's router (logits, scores, group-limited top-k, routing weights,
  * bucketed dispatch; the same kernels and results as stbl_moe_forward's routing) for T tokens with
- * all of its working memory in one fixed array inside the library (about 660 KB, held by every GPU
- * that loads the library until the process exits).  Limits: T <= 64, n_experts <= 256, hidden a
+ * all of its working memory in one fixed array inside the library (86,784 bytes, held by every GPU
+ * that loads the library until the process exits; x is not quantized for expert kernels here).  Limits: T <= 64, n_experts <= 256, hidden a
  * multiple of 128 up to 8192 (up to 2048 when it is not a multiple of 512), topk <= 16; larger sizes
  * are rejected with a message in err.  router_w and x must be 16-byte aligned.  Inputs and outputs
  * are device buffers owned by the caller: idx, weights [T][topk], counts [E], offsets [E+1],
@@ -290,6 +308,13 @@ int stbl_route_noalloc(const float *router_w, const float *router_bias, const vo
                        int hidden, int topk, int n_groups, int topk_groups, int score_fn, float route_scale, int *idx,
                        float *weights, int *counts, int *offsets, int *perm, cudaStream_t stream, char *err,
                        int errlen);
+
+/* Status bits the router kernels raised during the stbl_route_noalloc calls on the current device
+ * since the last read (waits for the device, then clears them; bits as stbl_moe_status: 1 a bounded
+ * wait ran out, 2 a table entry was out of range).  Each stbl_route_noalloc call clears the word on
+ * its stream before its kernels run, so a read right after a call covers that call.  Non-zero: the
+ * outputs of those calls are not valid.  Returns 0, or -1 if the device could not be read. */
+int stbl_route_noalloc_status(uint32_t *status);
 
 #ifdef __cplusplus
 }

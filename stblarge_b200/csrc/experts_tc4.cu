@@ -386,6 +386,9 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                         uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
                     }
                     const float hv = bf16r(gv / (1.f + expf(-gv)) * uv * cw[j]);
+                    // the bf16 h itself too (0.2 % of the launch's bytes at T=16): the layer's
+                    // activation readback checks the quantization below against the reference rule
+                    p.h[(size_t)dst * p.I + r] = f32_to_bf16_bits(hv);
                     float amax = fabsf(hv);
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));

@@ -52,7 +52,7 @@ struct RouterParams {
     Chunk *chunks;           // [T * topk + T]
     int *n_chunks;           // [0] total, [1] shared chunks
     // activation quantization of x for the routed (a) and shared (b) experts' formats; scale rows
-    // hold H / 32 floats whatever the block
+    // hold H / 32 floats whatever the block (xq_a null: no quantization, routing only)
     uint8_t *xq_a;
     float *xs_a;
     int blk_a, pow2_a;

@@ -1052,6 +1052,61 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores) {
     }
 }
 
+int stbl_moe_last_acts(stbl_moe *m, int which, void *h_bf16, void *codes, float *scales) {
+    try {
+        if (m->ep_n > 1) throw std::runtime_error("activation readback is for single-GPU layers");
+        if (which < STBL_ACTS_X_ROUTED || which > STBL_ACTS_H_SHARED) throw std::runtime_error("bad `which`");
+        const int T = m->last_T;
+        if (T < 1) throw std::runtime_error("no call yet");
+        const bool x = which == STBL_ACTS_X_ROUTED || which == STBL_ACTS_X_SHARED;
+        const bool shared = which == STBL_ACTS_X_SHARED || which == STBL_ACTS_H_SHARED;
+        if (shared && !m->has_shared) throw std::runtime_error("the layer has no shared expert");
+        const int fr = m->d.routed_fmt, fmt = shared ? m->d.shared_fmt : fr;
+        const int blk = act_blk_of(fmt);
+        const int width = x ? m->H : m->I;
+        const int rows = x ? T : (shared ? T : T * m->K);
+        const int pos0 = x ? 0 : (shared ? T * m->K : 0);  // first position of the h rows
+        CK(cudaDeviceSynchronize());
+        // x: the routed format's buffer, or the shared expert's own when its rule differs (forward())
+        const bool own_b = x && shared && !(act_blk_of(fmt) == act_blk_of(fr) && act_pow2_of(fmt) == act_pow2_of(fr));
+        const uint8_t *src_codes = x ? (own_b ? m->xq_b : m->xq_a) : m->hq + (size_t)pos0 * width;
+        if (codes) CK(cudaMemcpy(codes, src_codes, (size_t)rows * width, cudaMemcpyDeviceToHost));
+        if (h_bf16 && !x) CK(cudaMemcpy(h_bf16, m->h + (size_t)pos0 * width, (size_t)rows * width * 2, cudaMemcpyDeviceToHost));
+        if (scales) {
+            const int ns = width / blk;
+            std::vector<float> out((size_t)rows * ns);
+            if (blk == 128) {
+                // fp32 scales: x rows hold H / 32 floats (the first H / 128 used), h rows I / 128
+                const float *src = x ? (own_b ? m->xs_b : m->xs_a) : m->hs + (size_t)pos0 * (width / 128);
+                const int stride = x ? m->H / 32 : width / 128;
+                std::vector<float> buf((size_t)rows * stride);
+                CK(cudaMemcpy(buf.data(), src, buf.size() * 4, cudaMemcpyDeviceToHost));
+                for (int r = 0; r < rows; r++)
+                    for (int j = 0; j < ns; j++) out[(size_t)r * ns + j] = buf[(size_t)r * stride + j];
+            } else {
+                // e8m0 bytes in the tensor cores' activation-scale layout [width/128][rows_of_layout][16 B]
+                const uint8_t *src = x ? m->xe8_a : m->he8;
+                const int lrows = x ? m->Tpad : m->pos_rows;
+                std::vector<uint8_t> buf((size_t)(width / 128) * lrows * 16);
+                CK(cudaMemcpy(buf.data(), src, buf.size(), cudaMemcpyDeviceToHost));
+                for (int r = 0; r < rows; r++)
+                    for (int j = 0; j < ns; j++) {
+                        const uint8_t b = buf[((size_t)(j / 4) * lrows + pos0 + r) * 16 + (j % 4)];
+                        uint32_t bits = (uint32_t)b << 23;
+                        float f;
+                        memcpy(&f, &bits, 4);
+                        out[(size_t)r * ns + j] = f;
+                    }
+            }
+            memcpy(scales, out.data(), out.size() * 4);
+        }
+        return rows;
+    } catch (const std::exception &e) {
+        m->err = e.what();
+        return -1;
+    }
+}
+
 int stbl_moe_set_expert(stbl_moe *m, int e, const void *const w[3], const void *const s[3], cudaStream_t stream) {
     try {
         if (e < 0 || e >= m->E_loc) throw std::runtime_error("expert id out of range (local experts of this rank)");

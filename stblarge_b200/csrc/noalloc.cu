@@ -9,10 +9,14 @@
 //
 // Limits: T <= kNaMaxTokens tokens, E <= kNaMaxExperts experts, H <= kNaMaxHidden (and at most
 // 2048 when H is not a multiple of 512: the router's hidden slice), topk <= 16.
-// The array (about 660 KB) is part of the library image: every GPU that loads the library holds it
-// until the process exits.  All calls share it, so calls that overlap on the GPU (two streams, two
-// threads) race; serialise them.  The first call on each device looks up the array's device
-// address (cudaGetSymbolAddress); make that first call before any stream capture.
+// The array (kNaBytes = 86,784 bytes) is part of the library image: every GPU that loads the library
+// holds it until the process exits.  All calls share it, so calls that overlap on the GPU (two
+// streams, two threads) race; serialise them.  The first call on each device looks up the array's
+// device address (cudaGetSymbolAddress); make that first call before any stream capture.
+// The router kernels raise status bits in the array (a bounded wait that ran out, a bad table
+// entry); each call clears the word on its stream before the kernels run (a memset: no allocation),
+// and stbl_route_noalloc_status reads and clears it.  A non-zero status means the outputs of the
+// calls since the last read are not valid.
 #include <mutex>
 #include <stdio.h>
 
@@ -28,17 +32,16 @@ constexpr int kNaMaxExperts = 256;
 constexpr int kNaMaxHidden = 8192;
 constexpr int kNaMaxTopk = 16;
 
-// byte layout of the scratch array
+// byte layout of the scratch array (routing only: x is not quantized for expert kernels here)
 constexpr size_t kNaScores = 0;                                                        // f32 [T][E]
-constexpr size_t kNaXq = kNaScores + sizeof(float) * kNaMaxTokens * kNaMaxExperts;     // u8 [T][H]
-constexpr size_t kNaXs = kNaXq + (size_t)kNaMaxTokens * kNaMaxHidden;                   // f32 [T][H / 32]
-constexpr size_t kNaChunks = kNaXs + sizeof(float) * kNaMaxTokens * (kNaMaxHidden / 32);  // Chunk [T * (topk + 1)]
+constexpr size_t kNaChunks = kNaScores + sizeof(float) * kNaMaxTokens * kNaMaxExperts;  // Chunk [T * (topk + 1)]
 constexpr size_t kNaNChunks = kNaChunks + sizeof(Chunk) * kNaMaxTokens * (kNaMaxTopk + 1);  // int [4]
 constexpr size_t kNaStatus = kNaNChunks + 256;                                         // u32 status
 constexpr size_t kNaSelCnt = kNaStatus + 256;                                          // int [E]
 constexpr size_t kNaSelBm = kNaSelCnt + sizeof(int) * kNaMaxExperts;                  // u32 [E][T / 32]
 constexpr size_t kNaSelTicket = kNaSelBm + sizeof(uint32_t) * kNaMaxExperts * (kNaMaxTokens / 32);  // u32
 constexpr size_t kNaBytes = kNaSelTicket + 256;
+static_assert(kNaBytes == 86784, "the array size stated in stbl_moe.h and this file's header");
 
 static __device__ __align__(256) unsigned char g_route_scratch[kNaBytes];
 
@@ -106,17 +109,40 @@ extern "C" int stbl_route_noalloc(const float *router_w, const float *router_bia
     r.idx = idx, r.wts = weights, r.counts = counts, r.offsets = offsets, r.perm = perm;
     r.chunks = reinterpret_cast<Chunk *>(base + kNaChunks);
     r.n_chunks = reinterpret_cast<int *>(base + kNaNChunks);
-    r.xq_a = r.xq_b = base + kNaXq;
-    r.xs_a = r.xs_b = reinterpret_cast<float *>(base + kNaXs);
+    r.xq_a = r.xq_b = nullptr;  // no expert kernels follow: skip the activation quantization
+    r.xs_a = r.xs_b = nullptr;
     r.blk_a = r.blk_b = 128, r.pow2_a = r.pow2_b = 0;
     r.status = reinterpret_cast<uint32_t *>(base + kNaStatus);
     r.sel_cnt = reinterpret_cast<int *>(base + kNaSelCnt);
     r.sel_bm = reinterpret_cast<uint32_t *>(base + kNaSelBm);
     r.sel_ticket = reinterpret_cast<unsigned int *>(base + kNaSelTicket);
-    const cudaError_t e = launch_router(r, stream, false);
+    // this call's status starts clear (stream-ordered, so a later read covers this call only)
+    cudaError_t e = cudaMemsetAsync(base + kNaStatus, 0, sizeof(uint32_t), stream);
+    if (e == cudaSuccess) e = launch_router(r, stream, false);
     if (e != cudaSuccess) {
         if (err && errlen > 0) snprintf(err, errlen, "stbl_route_noalloc: %s", cudaGetErrorString(e));
         return -1;
     }
+    return 0;
+}
+
+extern "C" int stbl_route_noalloc_status(uint32_t *status) {
+    if (!status) return -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNaMaxDevices) return -1;
+    unsigned char *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_na_mu);
+        base = g_na_addr[dev];
+    }
+    if (!base) {  // no call on this device yet: nothing can have been raised
+        *status = 0;
+        return 0;
+    }
+    uint32_t s = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    if (cudaMemcpy(&s, base + kNaStatus, sizeof s, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (cudaMemset(base + kNaStatus, 0, sizeof s) != cudaSuccess) return -1;
+    *status = s;
     return 0;
 }

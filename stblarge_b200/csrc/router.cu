@@ -244,8 +244,9 @@ __global__ void __launch_bounds__(kLgThreads) router_logits_kernel(RouterParams 
         if (tid == 0) *p.sel_ticket = 0;
     }
 
-    // activation quantization of x for the expert kernels, spread over every warp of the grid
-    {
+    // activation quantization of x for the expert kernels, spread over every warp of the grid (none
+    // when the caller routes only: xq_a null)
+    if (p.xq_a) {
         const int nwarps_grid = gridDim.x * (kLgThreads / 32), gwarp = blockIdx.x * (kLgThreads / 32) + warp;
         const int groups = p.T * (p.H / 128);
         for (int u = gwarp; u < groups; u += nwarps_grid) {

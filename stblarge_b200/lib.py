@@ -58,6 +58,7 @@ SIGNATURES = {
     "stbl_moe_forward_host": (I, [P, P, I, P, P]),
     "stbl_moe_last_route": (I, [P, P, P, P, P, P]),
     "stbl_moe_last_scores": (I, [P, P]),
+    "stbl_moe_last_acts": (I, [P, I, P, P, P]),
     "stbl_moe_set_expert": (I, [P, I, P, P, P]),
     "stbl_moe_forward_routed": (I, [P, P, I, P, P, P]),
     "stbl_moe_forward_block": (I, [P, P, P, F, P, P, P, I, I, P, P]),
@@ -86,6 +87,7 @@ SIGNATURES = {
     "stbl_moe_error": (ctypes.c_char_p, [P]),
     "stbl_moe_destroy": (None, [P]),
     "stbl_route_noalloc": (I, [P, P, P, I, I, I, I, I, I, I, F, P, P, P, P, P, P, ctypes.c_char_p, I]),
+    "stbl_route_noalloc_status": (I, [ctypes.POINTER(U32)]),
     # include/stbl_gguf.h
     "stbl_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P), ctypes.c_char_p, I]),
     "stbl_gguf_close": (None, [P]),

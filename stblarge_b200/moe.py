@@ -15,7 +15,7 @@ import numpy as np
 import torch
 
 from . import lib as L
-from .config import FMT_NONE, MoEConfig
+from .config import FMT_FP8_B128, FMT_NONE, MoEConfig
 
 
 def _ptr(t):
@@ -164,6 +164,31 @@ class MoELayer:
         T = self._check(self.lib.stbl_moe_last_route(self.handle, idx.ctypes.data, w.ctypes.data, counts.ctypes.data,
                                                      offsets.ctypes.data, perm.ctypes.data), "stbl_moe_last_route")
         return {"idx": idx[:T], "weights": w[:T], "counts": counts, "offsets": offsets, "perm": perm[:T * cfg.topk]}
+
+    ACTS_X_ROUTED, ACTS_X_SHARED, ACTS_H_ROUTED, ACTS_H_SHARED = 0, 1, 2, 3
+
+    def last_acts(self, which):
+        """Quantized activations of the last call as the expert kernels read them
+        (stbl_moe_last_acts): {'codes': uint8 [rows, width], 'scales': float32 [rows, width / blk],
+        'blk': blk, 'h': bf16 bits uint16 [rows, width] for the h rows}.  x rows are tokens; h rows
+        are dispatch positions (routed) or tokens (shared)."""
+        cfg = self.cfg
+        T = self.max_tokens
+        x = which in (self.ACTS_X_ROUTED, self.ACTS_X_SHARED)
+        shared = which in (self.ACTS_X_SHARED, self.ACTS_H_SHARED)
+        fmt = cfg.shared_fmt if shared else cfg.routed_fmt
+        blk = 128 if fmt == FMT_FP8_B128 else 32
+        width = cfg.hidden if x else cfg.inter
+        rows_max = T if (x or shared) else T * cfg.topk
+        codes = np.empty((rows_max, width), np.uint8)
+        scales = np.empty((rows_max, width // blk), np.float32)
+        h = None if x else np.empty((rows_max, width), np.uint16)
+        rows = self._check(self.lib.stbl_moe_last_acts(self.handle, which, h.ctypes.data if h is not None else None,
+                                                       codes.ctypes.data, scales.ctypes.data), "stbl_moe_last_acts")
+        out = {"codes": codes[:rows], "scales": scales[:rows], "blk": blk}
+        if h is not None:
+            out["h"] = h[:rows]
+        return out
 
     def last_scores(self):
         s = np.empty((self.max_tokens, self.cfg.n_experts), np.float32)

@@ -29,6 +29,11 @@ def test_reference_arm_prints_the_contract_line():
     assert d["value"] > 0 and d["higher_is_better"] is True and d["n_gpus"] == 1
     assert d["steps"] == 1 and d["warmup"] >= 3
     assert "workload" in d["config"]
+    # the same config object the b200 arm prints for this workload (the driver compares the two)
+    import argparse
+
+    import bench
+    assert d["config"] == bench.config_of(argparse.Namespace(zipf=False), "cfg2", 16, 1)
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]

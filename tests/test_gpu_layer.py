@@ -1,9 +1,15 @@
 """Parity of the B200 MoE layer (libstbl_moe.so through its C ABI) with the CPU oracle.
 
 Bar: router logits, scores, expert ids, routing weights and the dispatch permutation bit-exact;
-layer output within max-abs 1e-2 of max |reference| in bf16 (BASELINE tolerance), reported in bf16
-ulps as well.  Small layers run the oracle on every expert; full-size layers hand the oracle only
-the experts the GPU chose (it fails if it would route elsewhere)."""
+the layer's own activation quantizations (x per token, h per dispatch position and per shared-expert
+token, as the expert kernels read them) bit-exact against the reference's act_quant rule (tolerance
+0, as stbl/test_kernels.py:63-69); layer output within max-abs 1e-2 of max |reference| in bf16
+(BASELINE tolerance), reported in bf16 ulps as well.  Small layers run the oracle on every expert;
+full-size layers hand the oracle only the experts the GPU chose (it fails if it would route
+elsewhere).  Full-size routes are also compared with the reference-style torch composition of the
+router (tests/golden/route_cfg2.npz), every mismatch reported with its selection margin."""
+
+import dataclasses
 
 import numpy as np
 import pytest
@@ -11,7 +17,7 @@ import torch
 
 from oracle import oracle as O
 from stblarge_b200 import synth
-from stblarge_b200.config import CFG1, CFG1_FP4, CFG2, CFG3, FMT_NONE
+from stblarge_b200.config import CFG1, CFG1_FP4, CFG2, CFG3, FMT_FP8_B128, FMT_NONE, SCORE_SQRT_SOFTPLUS
 from stblarge_b200.moe import MoELayer, host_weights_to_device
 
 pytestmark = pytest.mark.gpu
@@ -62,8 +68,32 @@ def run_and_check(cfg, layer, dev_w, host_W, x_bits):
     assert np.array_equal(idx2, idx_ref)
     rel, same, ulps = compare_y(y_bits, y_ref)
     assert rel <= TOL, f"max-abs-rel {rel:.3e} (bit-identical fraction {same:.4f}, max {ulps:.1f} bf16 ulps)"
+    check_quantizers(cfg, layer, x_bits)
     assert layer.status() == 0
     return rel, same
+
+
+def check_quantizers(cfg, layer, x_bits):
+    """The layer's act_quant steps, read back as the expert kernels consume them, equal the oracle's
+    act_quant (pinned bit-exact to ref/kernel.py by tests/test_oracle_golden.py) applied to the same
+    input: x per token for the routed and the shared experts; h (the bf16 values the up kernels
+    produced, read back too) per dispatch position and per shared-expert token.  Codes and scales
+    bit for bit: per-128 fp32 amax/448 for FP8 128x128 weights, per-32 power-of-two for MXFP4 and
+    FP8-e8m0 weights."""
+    xf = O.bf16_bits_to_f32(x_bits)
+    kinds = [(MoELayer.ACTS_X_ROUTED, cfg.routed_fmt), (MoELayer.ACTS_H_ROUTED, cfg.routed_fmt)]
+    if cfg.shared_fmt != FMT_NONE:
+        kinds += [(MoELayer.ACTS_X_SHARED, cfg.shared_fmt), (MoELayer.ACTS_H_SHARED, cfg.shared_fmt)]
+    for which, fmt in kinds:
+        a = layer.last_acts(which)
+        if "h" in a:
+            src = O.bf16_bits_to_f32(a["h"])
+            assert np.any(a["h"] != 0), f"acts {which}: h was not written"
+        else:
+            src = xf
+        codes, scales = O.act_quant(src, a["blk"], fmt != FMT_FP8_B128)
+        assert np.array_equal(a["codes"], codes), f"acts {which}: codes differ at {np.argwhere(a['codes'] != codes)[:4]}"
+        assert np.array_equal(a["scales"].view(np.uint32), scales.view(np.uint32)), f"acts {which}: scales differ"
 
 
 @pytest.fixture(scope="module")
@@ -140,7 +170,7 @@ def test_planted_router_ties(small_layers):
 @pytest.fixture(scope="module")
 def cfg2_layer():
     dev = synth.device_layer(CFG2)
-    layer = MoELayer(CFG2, dev, max_tokens=64)
+    layer = MoELayer(CFG2, dev, max_tokens=256)
     yield dev, layer
     layer.close()
     del dev
@@ -151,6 +181,58 @@ def cfg2_layer():
 def test_full_size_fp8_layer(cfg2_layer, T):
     dev, layer = cfg2_layer
     run_and_check(CFG2, layer, dev, None, synth.make_x(CFG2.hidden, T, seed=200 + T))
+
+
+@pytest.mark.parametrize("zipf", [0.0, 1.2])
+def test_full_size_cfg4_single_gpu(cfg2_layer, zipf):
+    """configs[3] on one GPU: the full-size FP8 layer at T = 256 (gathered activations; under
+    Zipf(1.2) popular experts hold many 16-token chunks), uniform routing (bias 0) and Zipf(1.2)."""
+    dev, _ = cfg2_layer
+    cfg = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=zipf)
+    dev4 = dict(dev)
+    dev4["router_bias"] = torch.from_numpy(synth.router_bias(cfg)).cuda()
+    layer = MoELayer(cfg, dev4, max_tokens=256)
+    run_and_check(cfg, layer, dev4, None, synth.make_x(cfg.hidden, 256, seed=400 + int(10 * zipf)))
+    layer.close()
+
+
+def route_report(got_idx, want_idx, margin):
+    """Route mismatches as stbl/test_layers.py:105 reports them: (token, reference margin, ids in one
+    route but not the other), compared as sets of ids."""
+    flips = []
+    for t in range(want_idx.shape[0]):
+        a, b = set(got_idx[t].tolist()), set(want_idx[t].tolist())
+        if a != b:
+            flips.append((t, float(margin[t]), sorted(a ^ b)))
+    return flips
+
+
+@pytest.mark.parametrize("rule", ["v3", "sp"])
+def test_full_size_routes_match_reference_composition(cfg2_layer, golden, rule):
+    """The full-size router against the routes of the torch composition the reference's harness uses
+    (fp32 x @ W^T, score, + bias, top-k; tests/golden/make_route_golden.py), 256 tokens: v3 = the
+    group-limited sigmoid gate, sp = the reference engine's sqrt(softplus) flat top-8.  A mismatch is
+    allowed only where the reference's own selection margin is below what fp32 summation order can
+    move (1e-5); the report lists every mismatch with its margin."""
+    dev, _ = cfg2_layer
+    g = golden("route_cfg2")
+    cfg = CFG2 if rule == "v3" else dataclasses.replace(CFG2, name="cfg2_sp", score_fn=SCORE_SQRT_SOFTPLUS,
+                                                         n_groups=1, topk_groups=1)
+    T = int(g["T"])
+    xb = synth.make_x(cfg.hidden, T, seed=int(g["x_seed"]))
+    layer = MoELayer(cfg, dev, max_tokens=T) if rule == "sp" else cfg2_layer[1]
+    layer(torch.from_numpy(xb.view(np.int16)).cuda())
+    route = layer.last_route()
+    want, margin = g["idx_" + rule], g["margin_" + rule]
+    flips = route_report(route["idx"], want, margin)
+    print(f"\n{rule}: route mismatches {len(flips)}/{T} (token, ref margin, differing ids): {flips}")
+    assert all(m < 1e-5 for _, m, _ in flips), flips
+    same = [t for t in range(T) if set(route["idx"][t].tolist()) == set(want[t].tolist())]
+    assert np.array_equal(route["idx"][same], want[same]), "same experts in a different order"
+    np.testing.assert_allclose(route["weights"][same], g["w_" + rule][same], rtol=1e-5)
+    assert layer.status() == 0
+    if rule == "sp":
+        layer.close()
 
 
 def test_full_size_fp8_device_quantization_matches_oracle(cfg2_layer):
@@ -174,7 +256,7 @@ def cfg3_layer():
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("T", [1, 16, 64])
+@pytest.mark.parametrize("T", [1, 4, 16, 64])
 def test_full_size_fp4_layer(cfg3_layer, T):
     dev, layer = cfg3_layer
     run_and_check(CFG3, layer, dev, None, synth.make_x(CFG3.hidden, T, seed=300 + T))

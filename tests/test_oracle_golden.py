@@ -3,7 +3,10 @@
 match within fp32 summation-order noise; the whole small layer matches the reference composition
 (expert ids exactly, output within the 1e-2 bf16 tolerance, in practice at most one bf16 ulp)."""
 
+import dataclasses
 import hashlib
+import os
+import sys
 
 import numpy as np
 import pytest
@@ -126,3 +129,30 @@ def test_layer_matches_reference_composition(golden, cfg, name):
     # in practice the oracle and the reference composition differ by at most one bf16 ulp
     ulp = np.abs(ref) * 2.0 ** -7 + 1e-30
     assert np.all(np.abs(yf - ref) <= ulp * 1.01)
+
+
+@pytest.mark.parametrize("rule", ["v3", "sp"])
+def test_oracle_full_size_routes_match_reference_composition(golden, rule):
+    """The oracle's router (it restates the GPU's exact logits order, so the GPU equals it bit for bit)
+    against the reference-style torch composition of the full-size router on 256 tokens
+    (tests/golden/route_cfg2.npz): v3 group-limited sigmoid top-8 and the reference engine's
+    sqrt(softplus) flat top-8.  Every mismatch is reported with the reference's selection margin (as
+    stbl/test_layers.py:105 does) and allowed only below 1e-5, what fp32 summation order can move."""
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from make_route_golden import inputs
+
+    from stblarge_b200.config import CFG2, SCORE_SQRT_SOFTPLUS
+    g = golden("route_cfg2")
+    W, b, x, digest = inputs()
+    assert digest == str(g["inputs_sha256"]), "synth no longer regenerates the fixture's inputs"
+    cfg = CFG2 if rule == "v3" else dataclasses.replace(CFG2, score_fn=SCORE_SQRT_SOFTPLUS, n_groups=1, topk_groups=1)
+    lg = O.router_logits(W, x)
+    _, idx, w = O.router_select(lg, b, cfg.topk, cfg.n_groups, cfg.topk_groups, cfg.score_fn, cfg.route_scale)
+    want, margin = g["idx_" + rule], g["margin_" + rule]
+    flips = [(t, float(margin[t]), sorted(set(idx[t].tolist()) ^ set(want[t].tolist())))
+             for t in range(len(want)) if set(idx[t].tolist()) != set(want[t].tolist())]
+    print(f"\n{rule}: route mismatches {len(flips)}/{len(want)} (token, ref margin, differing ids): {flips}")
+    assert all(m < 1e-5 for _, m, _ in flips), flips
+    same = [t for t in range(len(want)) if set(idx[t].tolist()) == set(want[t].tolist())]
+    assert np.array_equal(idx[same], want[same])
+    np.testing.assert_allclose(w[same], g["w_" + rule][same], rtol=1e-5)

@@ -3,9 +3,11 @@ captured, an engine with its own fixed memory pool, a runtime without an allocat
 memory is a fixed array inside the library; this test calls it through the C ABI and checks, on two
 calls in a row, that it returns exactly the routing of the regular layer entry point
 (stbl_moe_forward + stbl_moe_last_route): expert ids, weights, counts, offsets and the dispatch
-permutation, bit for bit, which is the tolerance the routing tests use.  It also checks that sizes
-beyond the array's limit are refused.  Collected last so that a failure here leaves every other
-test already run; it needs nothing from the other test files."""
+permutation, bit for bit, which is the tolerance the routing tests use; that the status word the
+router kernels raise reads 0 after each call (stbl_route_noalloc_status); that the full-size router
+(256 experts, hidden 7168) at the array's token limit (64) equals the CPU oracle bit for bit; and
+that sizes beyond the array's limit are refused.  Collected last so that a failure here leaves every
+other test already run; it needs nothing from the other test files."""
 
 import ctypes
 
@@ -15,7 +17,8 @@ import torch
 
 from stblarge_b200 import lib as L
 from stblarge_b200 import synth
-from stblarge_b200.config import CFG1
+from oracle import oracle as O
+from stblarge_b200.config import CFG1, CFG2
 from stblarge_b200.moe import MoELayer, host_weights_to_device
 
 pytestmark = pytest.mark.gpu
@@ -35,7 +38,9 @@ def route_noalloc(lib, cfg, dev, x):
                                 cfg.route_scale, idx.data_ptr(), w.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
                                 perm.data_ptr(), st, err, 256)
     assert rc == 0, err.value.decode()
-    torch.cuda.synchronize()
+    status = ctypes.c_uint32(123)
+    assert lib.stbl_route_noalloc_status(ctypes.byref(status)) == 0
+    assert status.value == 0, f"router status bits {status.value:#x}"
     return {"idx": idx.cpu().numpy(), "weights": w.cpu().numpy(), "counts": counts.cpu().numpy(),
             "offsets": offsets.cpu().numpy(), "perm": perm.cpu().numpy()}
 
@@ -54,6 +59,27 @@ def test_noalloc_routing_matches_layer_on_two_calls():
             assert np.array_equal(got[k], want[k]), (call, k)
         assert np.array_equal(got["weights"].view(np.uint32), want["weights"].view(np.uint32)), call
     layer.close()
+
+
+def test_noalloc_full_size_at_its_token_limit_matches_oracle():
+    """The full-size router (configs[1]: 256 experts, hidden 7168, top-8 of 8 groups keeping 4) at
+    T = 64, the array's limit, on two calls in a row, against the CPU oracle's restatement of the
+    router (logits order, scores, selection, weights, dispatch) bit for bit."""
+    lib = L.load()
+    cfg = CFG2
+    dev = {"router_w": torch.from_numpy(synth.router_w(cfg)).cuda(),
+           "router_bias": torch.from_numpy(synth.router_bias(cfg)).cuda()}
+    for call, seed in enumerate((611, 612)):
+        xb = synth.make_x(cfg.hidden, 64, seed=seed)
+        got = route_noalloc(lib, cfg, dev, torch.from_numpy(xb.view(np.int16)).cuda())
+        lg = O.router_logits(synth.router_w(cfg), xb)
+        _, idx, w = O.router_select(lg, synth.router_bias(cfg), cfg.topk, cfg.n_groups, cfg.topk_groups,
+                                    cfg.score_fn, cfg.route_scale)
+        counts, offsets, perm = O.dispatch(idx, cfg.n_experts)
+        assert np.array_equal(got["idx"], idx), call
+        assert np.array_equal(got["weights"].view(np.uint32), w.view(np.uint32)), call
+        assert np.array_equal(got["counts"], counts) and np.array_equal(got["offsets"], offsets), call
+        assert np.array_equal(got["perm"], perm), call
 
 
 def test_noalloc_rejects_sizes_beyond_its_array():
