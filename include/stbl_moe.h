@@ -74,6 +74,13 @@ typedef struct stbl_moe_desc {
        [rows][k/32] layout; the layer then keeps its own copy in the block layout, made at create for
        every slot and again for a slot when stbl_moe_set_expert points an expert at it. */
     int routed_s_blocked;
+    /* 1: the routed MXFP4 experts take Q8 activations instead of FP8: x and h quantized per 32 values
+       to int8 with an fp32 scale amax / 127, round-half-even (ref/emulate_ds4.py:23-30, 69-77; the
+       reference's ds4 numerics), products on the CUDA cores with exact integer block sums.  Needs
+       routed_fmt STBL_FMT_MXFP4 with natural scales (routed_s_blocked 0), a shared expert in
+       STBL_FMT_FP8_B128 (it keeps its FP8 rule) or none, hidden <= 8192, inter <= 4096, one GPU, no
+       expert cache.  0: the FP8 rule of the weight format. */
+    int act_q8;
 } stbl_moe_desc;
 
 /* Validate the description, allocate the layer's workspace on the current device and build its
@@ -107,7 +114,8 @@ int stbl_moe_last_scores(stbl_moe *m, float *scores);
  *   STBL_ACTS_H_SHARED  h of the shared expert by token: rows T, width inter
  * h_bf16 (h rows only; may be NULL): the bf16 values that were quantized, [rows][width]; codes: e4m3
  * [rows][width]; scales: fp32 [rows][width / blk], blk 128 (fp32 scale amax/448) for FP8 128x128
- * weights, 32 (power-of-two scale, stored as e8m0) for MXFP4 and FP8-e8m0 weights.  Any output
+ * weights, 32 (power-of-two scale, stored as e8m0) for MXFP4 and FP8-e8m0 weights; for the routed
+ * rows of an act_q8 layer, int8 codes and fp32 scales amax/127 per 32.  Any output
  * pointer may be NULL.  Single-GPU layers.  Returns the row count, or -1. */
 #define STBL_ACTS_X_ROUTED 0
 #define STBL_ACTS_X_SHARED 1
@@ -308,6 +316,17 @@ int stbl_route_noalloc(const float *router_w, const float *router_bias, const vo
                        int hidden, int topk, int n_groups, int topk_groups, int score_fn, float route_scale, int *idx,
                        float *weights, int *counts, int *offsets, int *perm, cudaStream_t stream, char *err,
                        int errlen);
+
+/* The Q8 linear of the act_q8 layers alone: y[t][r] = sum over K of dequantized w[r] times
+ * dequantized q[t], for MXFP4 weights (codes [rows][k/2], value 2j in the low nibble of byte j; e8m0
+ * scales [rows][k/32]) and Q8 activations (int8 codes q [n_tok][k], fp32 scales d [n_tok][k/32], the
+ * rule of ref/emulate_ds4.py:23-30).  The FP4 branch of the reference's emulated linear
+ * (ref/emulate_ds4.py:69-77), which the reference's kernels.h has no launcher for: per 32-value
+ * block an exact integer dot product (twice every e2m1 value is an integer), scaled in fp32.  Device
+ * buffers, w and q 16-byte aligned, k a multiple of 32; fp32 out [n_tok][rows], not rounded.
+ * Enqueued on `stream`.  Returns 0, or -1 for a bad argument or launch. */
+int stbl_gemv_mxfp4_q8(float *y, const void *w, const void *scales, const int8_t *q, const float *d, int rows, int k,
+                       int n_tok, cudaStream_t stream);
 
 /* Status bits the router kernels raised during the stbl_route_noalloc calls on the current device
  * since the last read (waits for the device, then clears them; bits as stbl_moe_status: 1 a bounded

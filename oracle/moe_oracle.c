@@ -454,6 +454,34 @@ static void expert_ffn(const orc_moe_desc *d, int fmt, const uint8_t *const w[3]
     free(xc), free(xs), free(g), free(u);
 }
 
+/* One routed MXFP4 expert with Q8 activations (ref/emulate_ds4.py:23-30, 69-77), composed as
+ * expert_ffn: g, u = bf16(W1 q8(x)), bf16(W3 q8(x)); h = bf16(silu(g) * u * w) (clamps as above);
+ * out = bf16(W2 q8(h)). */
+static void expert_ffn_q8(const orc_moe_desc *d, const uint8_t *const w[3], const void *const s[3], const float *xin,
+                          const float *wt, int n_tok, float *out) {
+    const int H = d->hidden, I = d->inter, KM = H > I ? H : I;
+    int8_t *q = (int8_t *)malloc((size_t)n_tok * KM);
+    float *dq = (float *)malloc(sizeof(float) * (size_t)n_tok * (KM / 32));
+    float *g = (float *)malloc(sizeof(float) * (size_t)n_tok * I), *u = (float *)malloc(sizeof(float) * (size_t)n_tok * I);
+    orc_q8_codes(xin, n_tok * (H / 32), q, dq);
+    orc_gemv_mxfp4_q8(w[0], (const uint8_t *)s[0], I, H, q, dq, n_tok, g);
+    orc_gemv_mxfp4_q8(w[1], (const uint8_t *)s[1], I, H, q, dq, n_tok, u);
+    const float L = d->swiglu_limit;
+    for (int t = 0; t < n_tok; t++)
+        for (int j = 0; j < I; j++) {
+            float gv = orc_bf16_round(g[(size_t)t * I + j]), uv = orc_bf16_round(u[(size_t)t * I + j]);
+            if (L > 0) {
+                uv = fminf(fmaxf(uv, -L), L);
+                gv = fminf(gv, L);
+            }
+            g[(size_t)t * I + j] = orc_bf16_round(gv / (1.f + expf(-gv)) * uv * wt[t]);
+        }
+    orc_q8_codes(g, n_tok * (I / 32), q, dq);
+    orc_gemv_mxfp4_q8(w[2], (const uint8_t *)s[2], H, I, q, dq, n_tok, out);
+    for (size_t i = 0; i < (size_t)n_tok * H; i++) out[i] = orc_bf16_round(out[i]);
+    free(q), free(dq), free(g), free(u);
+}
+
 /* The layer with the routed experts given (forced routes): forced [T][topk], weights = unbiased
  * scores of the given experts normalised in the given order, times route_scale (the selection's
  * weight rule, model.cu:450-451, 527-530).  forced == NULL: the router selects. */
@@ -535,7 +563,10 @@ static int moe_forward_impl(const orc_moe_desc *d, const uint16_t *x, int T, con
             if (!w[m] || !sp[m]) rc = -1;
         }
         if (rc) break;
-        expert_ffn(d, d->routed_fmt, w, sp, xin, wt, n, out);
+        if (d->act_q8 && d->routed_fmt == ORC_FMT_MXFP4)
+            expert_ffn_q8(d, w, sp, xin, wt, n, out);
+        else
+            expert_ffn(d, d->routed_fmt, w, sp, xin, wt, n, out);
         for (int i = 0; i < n; i++) memcpy(eo + (size_t)slot[i] * H, out + (size_t)i * H, sizeof(float) * H);
     }
     float *sh = (float *)calloc((size_t)T * H, sizeof(float));
@@ -733,6 +764,7 @@ void orc_gemv_mxfp4_q8(const uint8_t *w, const uint8_t *ws, int rows, int k, con
                        float *y) {
     const int nb = k / 32;
     for (int t = 0; t < n_tok; t++)
+#pragma omp parallel for schedule(static)
         for (int r = 0; r < rows; r++) {
             double acc = 0.0;
             for (int b = 0; b < nb; b++) {

@@ -88,6 +88,9 @@ typedef struct orc_moe_desc {
     const void *const *routed_s;    /* [3 * n_experts] */
     const uint8_t *shared_w[3];
     const void *shared_s[3];
+    /* 1: routed MXFP4 experts take Q8 activations (int8 per 32, scale amax / 127) instead of FP8
+     * (ref/emulate_ds4.py:23-30, 69-77); the shared expert keeps its FP8 rule */
+    int act_q8;
 } orc_moe_desc;
 
 /* y = bf16(sum over top-k slots in order of the routed outputs, then + shared output).  Writes

@@ -243,7 +243,7 @@ class _Desc(ctypes.Structure):
         ("hidden", I), ("inter", I), ("n_experts", I), ("topk", I), ("n_groups", I), ("topk_groups", I),
         ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
         ("router_w", P), ("router_bias", P), ("routed_w", P), ("routed_s", P),
-        ("shared_w", P * 3), ("shared_s", P * 3),
+        ("shared_w", P * 3), ("shared_s", P * 3), ("act_q8", I),
     ]
 
 
@@ -276,6 +276,7 @@ def moe_forward(cfg, weights, x_bits, nthreads=0, forced=None):
     d.n_groups, d.topk_groups, d.score_fn = cfg["n_groups"], cfg["topk_groups"], cfg["score_fn"]
     d.route_scale, d.swiglu_limit = cfg["route_scale"], cfg["swiglu_limit"]
     d.routed_fmt, d.shared_fmt = cfg["routed_fmt"], cfg["shared_fmt"]
+    d.act_q8 = int(cfg.get("act_q8", 0))
     d.router_w = p(_f32(weights["router_w"]))
     d.router_bias = p(_f32(weights["router_bias"]))
     d.routed_w = ctypes.cast(rw, P)

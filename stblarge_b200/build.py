@@ -20,7 +20,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libstbl_moe.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["router.cu", "combine.cu", "experts_tc.cu", "experts_tc4.cu", "moe.cu", "compat.cu", "noalloc.cu", "ep.cu", "cache.cu", "formats.cu", "gguf.cu", "reader.cu"]
+SOURCES = ["router.cu", "combine.cu", "experts_tc.cu", "experts_tc4.cu", "experts_q8.cu", "moe.cu", "compat.cu", "noalloc.cu", "ep.cu", "cache.cu", "formats.cu", "gguf.cu", "reader.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
          "-I" + INCLUDE]

@@ -38,6 +38,7 @@ class MoEConfig:
     bias_std: float = 0.1
     zipf_s: float = 0.0         # > 0: correction bias skews expert popularity as Zipf(s)
     zipf_c: float = 0.5         # bias = zipf_c * (ln p_e - mean ln p)
+    act_q8: int = 0             # 1: routed MXFP4 experts take Q8 activations (int8 per 32, scale amax/127)
 
     def as_dict(self):
         return asdict(self)
@@ -72,4 +73,9 @@ CFG1_E8 = replace(CFG1, name="cfg1_e8", routed_fmt=FMT_FP8_E8M0, shared_fmt=FMT_
 CFG3_REF = replace(CFG2, name="cfg3_ref", routed_fmt=FMT_MXFP4, shared_fmt=FMT_FP8_E8M0, score_fn=SCORE_SQRT_SOFTPLUS,
                    n_groups=1, topk_groups=1)
 
-PRESETS = {c.name: c for c in (CFG1, CFG1_FP4, CFG2, CFG3, CFG1_REF, CFG1_E8, CFG3_REF)}
+# the Q8 activation variant of the MXFP4 layers (ref/emulate_ds4.py: routed MXFP4 experts take int8
+# activations per 32 instead of FP8; the shared expert keeps FP8)
+CFG1_Q8 = replace(CFG1_FP4, name="cfg1_q8", act_q8=1)
+CFG3_Q8 = replace(CFG3, name="cfg3_q8", act_q8=1)
+
+PRESETS = {c.name: c for c in (CFG1, CFG1_FP4, CFG2, CFG3, CFG1_REF, CFG1_E8, CFG3_REF, CFG1_Q8, CFG3_Q8)}

@@ -29,6 +29,7 @@ cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
 int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two);
+cudaError_t launch_q8(bool up, const Q8Params &p, int sms, cudaStream_t st);  // experts_q8.cu
 }  // namespace stbl
 
 using namespace stbl;
@@ -124,6 +125,8 @@ struct stbl_moe {
     long long sf_own_stride = 0, sf_own_off[3] = {0, 0, 0};
     uint8_t *hq = nullptr, *xq_pos = nullptr;
     float *hs = nullptr, *xs_pos = nullptr;
+    bool act_q8 = false;              // routed MXFP4 experts with Q8 activations (CUDA-core kernels)
+    float *hd8 = nullptr;             // Q8 scales of h by position [pos][I / 32]
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
     CUtensorMap bmap4_xa{}, bmap4_xpos{}, bmap4_hq{};         // the same, two K blocks per box (MXFP4 kernels)
 
@@ -294,6 +297,15 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
     if (d->routed_fmt == STBL_FMT_FP8_B128 && d->shared_fmt == STBL_FMT_FP8_E8M0)
         throw std::runtime_error("an FP8-e8m0 shared expert needs block-scaled routed experts (MXFP4 or FP8-e8m0)");
     if (d->max_tokens < 1 || d->max_tokens > kRouterMaxTokens) throw std::runtime_error("max_tokens must be in 1..256");
+    if (d->act_q8 != 0 && d->act_q8 != 1) throw std::runtime_error("act_q8 must be 0 or 1");
+    if (d->act_q8) {
+        if (d->routed_fmt != STBL_FMT_MXFP4) throw std::runtime_error("act_q8 needs MXFP4 routed experts");
+        if (d->shared_fmt != STBL_FMT_FP8_B128 && d->shared_fmt != STBL_FMT_NONE)
+            throw std::runtime_error("act_q8 needs an FP8 128x128 shared expert or none");
+        if (d->routed_s_blocked) throw std::runtime_error("act_q8 reads the natural MXFP4 scale layout (routed_s_blocked 0)");
+        if (ep_n > 1) throw std::runtime_error("act_q8 layers are single-GPU");
+        if (d->inter > 4096) throw std::runtime_error("act_q8 needs inter <= 4096");
+    }
     if (H / router_ksplit(H) > kLgMaxSlice) throw std::runtime_error("hidden must be at most 8192");
     if (!d->router_w || !d->router_bias) throw std::runtime_error("router weights missing");
     if ((uintptr_t)d->router_w & 15) throw std::runtime_error("router weights must be 16-byte aligned");
@@ -359,6 +371,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->h = carve<uint16_t>(p, (size_t)npos * I);
         m->hq = carve<uint8_t>(p, (size_t)(npos + 16) * I);
         m->hs = carve<float>(p, (size_t)(npos + 16) * (I / 128));
+        m->hd8 = d->act_q8 ? carve<float>(p, (size_t)(npos + 16) * (I / 32)) : nullptr;
         m->eo = ep_n > 1 ? nullptr : carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
@@ -387,11 +400,12 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
 
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
+    m->act_q8 = d->act_q8 != 0;
     m->routed_bs = !m->routed_tc;
     m->shared_bs = d->shared_fmt == STBL_FMT_FP8_E8M0;
     if (H % 128 || I % 128 || H > 8192 || I > 8192)
         throw std::runtime_error("experts need hidden and inter multiples of 128, at most 8192");
-    if (m->routed_bs) {
+    if (m->routed_bs && !m->act_q8) {
         const bool e8 = d->routed_fmt == STBL_FMT_FP8_E8M0;
         const long long wst4[3] = {m->w_stride[0], m->w_stride[1], m->w_stride[2]};
         const int ns = m->n_slots, rps = scale_rows_of(d->routed_fmt);
@@ -591,6 +605,31 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
     return p;
 }
 
+// the Q8 routed products' parameters (act_q8 layers): up reads x codes by token, down h codes by
+// position; weights and natural e8m0 scales of the routed slots
+Q8Params q8_params(stbl_moe *m, int T, bool up) {
+    Q8Params q{};
+    q.slot = m->slots_moved ? m->slot : nullptr;
+    q.chunks = m->chunks, q.n_chunks = m->n_chunks;
+    q.T = T, q.topk = m->K, q.E = m->E_loc, q.H = m->H, q.I = m->I;
+    q.perm = m->perm, q.wts = m->wts;
+    const int mats[2] = {up ? 0 : 2, up ? 1 : 2};
+    for (int i = 0; i < 2; i++) {
+        q.w[i] = static_cast<const uint8_t *>(m->d.routed_w[mats[i]]);
+        q.w_stride[i] = m->w_stride[mats[i]];
+        q.s[i] = static_cast<const uint8_t *>(m->d.routed_s[mats[i]]);
+        q.s_stride[i] = m->s_stride[mats[i]];
+    }
+    q.xq = reinterpret_cast<const int8_t *>(up ? m->xq_a : m->hq);
+    q.xd = up ? m->xs_a : m->hd8;
+    q.xd_stride = up ? m->H / 32 : m->I / 32;
+    q.hq = reinterpret_cast<int8_t *>(m->hq), q.hd = m->hd8, q.h = m->h;
+    q.swiglu_limit = m->d.swiglu_limit;
+    q.eo = m->eo;
+    q.status = m->status;
+    return q;
+}
+
 // act_quant of h for the positions of [pos_begin, pos_end) (the down kernel's B operand)
 void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
     if (pos_end <= pos_begin) return;
@@ -687,13 +726,15 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     r.scores = m->scores, r.idx = m->idx, r.wts = m->wts;
     r.counts = m->counts, r.offsets = m->offsets, r.perm = m->perm, r.chunks = m->chunks, r.n_chunks = m->n_chunks;
     const int fr = m->d.routed_fmt, fs = m->has_shared ? m->d.shared_fmt : fr;
-    r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = act_pow2_of(fr);
-    if (act_blk_of(fs) == act_blk_of(fr) && act_pow2_of(fs) == act_pow2_of(fr))  // one quantization serves both
+    // the routed experts' rule: the weight format's FP8 rule, or Q8 (int8 per 32) for an act_q8 layer
+    const int rule_a = m->act_q8 ? kActQ8 : act_pow2_of(fr);
+    r.xq_a = m->xq_a, r.xs_a = m->xs_a, r.blk_a = act_blk_of(fr), r.pow2_a = rule_a;
+    if (act_blk_of(fs) == act_blk_of(fr) && act_pow2_of(fs) == rule_a)  // one quantization serves both
         r.xq_b = m->xq_a, r.xs_b = m->xs_a, r.blk_b = r.blk_a, r.pow2_b = r.pow2_a;
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
-    r.xe8_a = m->routed_bs ? m->xe8_a : nullptr;
+    r.xe8_a = m->routed_bs && !m->act_q8 ? m->xe8_a : nullptr;
     r.xe8_rows = m->Tpad;
-    r.nt_routed = 16;
+    r.nt_routed = m->act_q8 ? kQ8ChunkTokens : 16;
     r.nt_shared = 16;
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
@@ -749,6 +790,30 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         launch_pdl(hquant_kernel_ptr(), dim3(m->sms), dim3(256), hargs, 0, st);
         launch_tc(m, false, pd, st);
         launches += 5;
+    } else if (m->act_q8) {
+        // routed MXFP4 experts x Q8 activations on the CUDA cores (chunks of <= 8 tokens); the FP8
+        // shared expert on the tensor cores (its chunks, first in the table, read x by token):
+        // [shared up] -> routed up (+ SwiGLU, Q8 of h) -> [hquant of the shared rows] -> [shared down]
+        // -> routed down -> combine
+        const int ns = m->has_shared ? (T + 15) / 16 : 0;
+        if (ns) {
+            TcParams su = tc_params(m, T, true, true);
+            su.chunk_begin = 0, su.chunk_end = ns;
+            launch_tc(m, true, su, st);
+            launches++;
+        }
+        CK(launch_q8(true, q8_params(m, T, true), m->sms, st));
+        if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
+        launches++;
+        if (ns) {
+            launch_hquant(m, T * m->K, npos, st);
+            TcParams sd = tc_params(m, T, false);
+            sd.chunk_begin = 0, sd.chunk_end = ns;
+            launch_tc(m, false, sd, st);
+            launches += 2;
+        }
+        CK(launch_q8(false, q8_params(m, T, false), m->sms, st));
+        launches++;
     } else if (m->routed_tc) {
         // every expert on the tensor cores: [gather] -> up -> hquant -> down -> combine
         const bool direct = T <= 16;
@@ -988,6 +1053,7 @@ int stbl_moe_attach_cache(stbl_moe *m, stbl_cache *c, int layer) {
     try {
         if (!c) throw std::runtime_error("null cache");
         if (m->ep_n > 1) throw std::runtime_error("the expert cache is single-GPU");
+        if (m->act_q8) throw std::runtime_error("act_q8 layers read the natural MXFP4 scales; the expert cache holds the block layout");
         if (layer < 0 || layer >= c->L) throw std::runtime_error("layer out of the cache's range");
         int dev = 0;
         CK(cudaGetDevice(&dev));
@@ -1075,7 +1141,11 @@ int stbl_moe_last_acts(stbl_moe *m, int which, void *h_bf16, void *codes, float 
         if (scales) {
             const int ns = width / blk;
             std::vector<float> out((size_t)rows * ns);
-            if (blk == 128) {
+            if (m->act_q8 && !shared) {
+                // Q8: fp32 scales per 32, x rows H / 32 floats, h rows I / 32
+                const float *src = x ? m->xs_a : m->hd8 + (size_t)pos0 * (width / 32);
+                CK(cudaMemcpy(out.data(), src, out.size() * 4, cudaMemcpyDeviceToHost));
+            } else if (blk == 128) {
                 // fp32 scales: x rows hold H / 32 floats (the first H / 128 used), h rows I / 128
                 const float *src = x ? (own_b ? m->xs_b : m->xs_a) : m->hs + (size_t)pos0 * (width / 128);
                 const int stride = x ? m->H / 32 : width / 128;

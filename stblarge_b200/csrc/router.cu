@@ -76,7 +76,8 @@ __device__ void rms_rsqrt(const float *xr, int H, float eps, float *red, float *
 }
 
 // act_quant (ref/kernel.py:35-45) of 128 consecutive values of one token: lane l takes 4 of them.
-// blk 128: fp32 scale amax/448; blk 32: power-of-two scale per 32 (pow2 selects the rounding).
+// blk 128: fp32 scale amax/448; blk 32: power-of-two scale per 32 (pow2 selects the rounding);
+// pow2 == kActQ8 (blk 32): the Q8 rule instead, int8 codes with an fp32 scale amax/127.
 // xe8 (optional): the scales as e8m0 bytes (per-32 power-of-two rule), laid out as the MXFP4 experts'
 // tensor-core kernel copies them: [H/128][xe8_rows][16 B], row t's bytes 0..3 for the 128-K block.
 // With the fused RMSNorm (nrm non-null) the values are normalized from x_pre first (rms_value).
@@ -96,6 +97,21 @@ __device__ void quant_group(const uint16_t *x, int H, int t, int g, uint8_t *xq,
     }
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     for (int o = blk / 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (pow2 == kActQ8) {
+        // Q8 (ref/emulate_ds4.py:23-30): int8 codes round-half-even(x / d), d = amax / 127 (no floor;
+        // d = 0 divides by 1), clamped to [-128, 127]; d kept as fp32 per 32 values
+        const float d = amax / 127.0f;
+        const float div = d > 0.f ? d : 1.0f;
+        uint32_t codes = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int q = (int)fminf(fmaxf(rintf(v[j] / div), -128.f), 127.f);
+            codes |= ((uint32_t)q & 0xffu) << (8 * j);
+        }
+        *reinterpret_cast<uint32_t *>(xq + (size_t)t * H + k) = codes;
+        if ((k % 32) == 0) xs[(size_t)t * (H / 32) + k / 32] = d;
+        return;
+    }
     amax = fmaxf(amax, 1e-4f);
     const float tq = amax * (1.0f / 448.0f);
     const float s = pow2 ? pow2_ceil(tq) : tq;

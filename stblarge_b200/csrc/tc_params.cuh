@@ -98,4 +98,27 @@ struct GatherParams {
     int xe8_rows, xe8_pos_rows;
 };
 
+// the Q8 routed expert products (experts_q8.cu): routed MXFP4 experts x int8 activations per 32
+struct Q8Params {
+    const int *slot;          // [E] storage slot of each routed expert (null: e)
+    const Chunk *chunks;
+    const int *n_chunks;      // [0] total chunks, [1] the shared expert's (first); routed chunks follow
+    int T, topk, E, H, I;
+    const int *perm;
+    const float *wts;
+    const uint8_t *w[2];      // up: gate, up codes; down: down codes ([rows][K / 2] per slot)
+    long long w_stride[2];    // bytes between slots
+    const uint8_t *s[2];      // e8m0 scales [rows][K / 32] per slot
+    long long s_stride[2];
+    const int8_t *xq;         // activation codes: up, x by token [.][H]; down, h by position [.][I]
+    const float *xd;          // their per-32 scales, xd_stride floats per row
+    int xd_stride;
+    int8_t *hq;               // up out: Q8 codes of h by position [pos][I]
+    float *hd;                // up out: their scales [pos][I / 32]
+    uint16_t *h;              // up out: h (bf16) by position [pos][I]
+    float swiglu_limit;
+    uint16_t *eo;             // down out: [T * topk][H] by assignment
+    uint32_t *status;
+};
+
 }  // namespace stbl

@@ -26,7 +26,7 @@ class MoEDesc(ctypes.Structure):
         ("score_fn", I), ("route_scale", F), ("swiglu_limit", F), ("routed_fmt", I), ("shared_fmt", I),
         ("max_tokens", I), ("router_w", P), ("router_bias", P), ("routed_w", P * 3), ("routed_s", P * 3),
         ("routed_w_stride", LL * 3), ("routed_s_stride", LL * 3), ("shared_w", P * 3), ("shared_s", P * 3),
-        ("n_slots", I), ("routed_s_blocked", I),
+        ("n_slots", I), ("routed_s_blocked", I), ("act_q8", I),
     ]
 
 
@@ -88,6 +88,7 @@ SIGNATURES = {
     "stbl_moe_destroy": (None, [P]),
     "stbl_route_noalloc": (I, [P, P, P, I, I, I, I, I, I, I, F, P, P, P, P, P, P, ctypes.c_char_p, I]),
     "stbl_route_noalloc_status": (I, [ctypes.POINTER(U32)]),
+    "stbl_gemv_mxfp4_q8": (I, [P, P, P, P, P, I, I, I, P]),
     # include/stbl_gguf.h
     "stbl_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P), ctypes.c_char_p, I]),
     "stbl_gguf_close": (None, [P]),

@@ -43,6 +43,7 @@ class MoELayer:
         d.n_groups, d.topk_groups, d.score_fn = cfg.n_groups, cfg.topk_groups, cfg.score_fn
         d.route_scale, d.swiglu_limit = cfg.route_scale, cfg.swiglu_limit
         d.routed_fmt, d.shared_fmt, d.max_tokens = cfg.routed_fmt, cfg.shared_fmt, max_tokens
+        d.act_q8 = cfg.act_q8
         d.router_w = weights["router_w"].data_ptr()
         d.router_bias = weights["router_bias"].data_ptr()
         if cache is not None:
@@ -185,7 +186,8 @@ class MoELayer:
         h = None if x else np.empty((rows_max, width), np.uint16)
         rows = self._check(self.lib.stbl_moe_last_acts(self.handle, which, h.ctypes.data if h is not None else None,
                                                        codes.ctypes.data, scales.ctypes.data), "stbl_moe_last_acts")
-        out = {"codes": codes[:rows], "scales": scales[:rows], "blk": blk}
+        out = {"codes": codes[:rows], "scales": scales[:rows], "blk": blk,
+               "rule": "q8" if (cfg.act_q8 and not shared) else ("fp32" if blk == 128 else "pow2")}
         if h is not None:
             out["h"] = h[:rows]
         return out

@@ -53,3 +53,11 @@ def test_kernels_are_sm100a_only(built):
     out = subprocess.run(["cuobjdump", "--list-elf", built], capture_output=True, text=True).stdout
     assert "sm_100a" in out
     assert "sm_90" not in out and "sm_80" not in out
+
+
+def test_library_leaves_none_of_its_own_symbols_undefined(built):
+    """Every translation unit is linked in: no function of the library's namespace or C ABI is left
+    for the dynamic loader to find (a source missing from the build would show up here)."""
+    out = subprocess.run(["nm", "-D", "--undefined-only", "-C", built], check=True, capture_output=True, text=True).stdout
+    own = [l for l in out.splitlines() if "stbl" in l]
+    assert not own, own

@@ -17,7 +17,7 @@ import torch
 
 from oracle import oracle as O
 from stblarge_b200 import synth
-from stblarge_b200.config import CFG1, CFG1_FP4, CFG2, CFG3, FMT_FP8_B128, FMT_NONE, SCORE_SQRT_SOFTPLUS
+from stblarge_b200.config import CFG1, CFG1_FP4, CFG2, CFG3, CFG3_Q8, FMT_FP8_B128, FMT_NONE, SCORE_SQRT_SOFTPLUS
 from stblarge_b200.moe import MoELayer, host_weights_to_device
 
 pytestmark = pytest.mark.gpu
@@ -91,7 +91,12 @@ def check_quantizers(cfg, layer, x_bits):
             assert np.any(a["h"] != 0), f"acts {which}: h was not written"
         else:
             src = xf
-        codes, scales = O.act_quant(src, a["blk"], fmt != FMT_FP8_B128)
+        if a["rule"] == "q8":
+            # the Q8 rule (ref/emulate_ds4.py:23-30): int8 codes, fp32 scale amax / 127 per 32
+            q, scales = O.q8_codes(src)
+            codes = q.view(np.uint8)
+        else:
+            codes, scales = O.act_quant(src, a["blk"], fmt != FMT_FP8_B128)
         assert np.array_equal(a["codes"], codes), f"acts {which}: codes differ at {np.argwhere(a['codes'] != codes)[:4]}"
         assert np.array_equal(a["scales"].view(np.uint32), scales.view(np.uint32)), f"acts {which}: scales differ"
 
@@ -260,6 +265,16 @@ def cfg3_layer():
 def test_full_size_fp4_layer(cfg3_layer, T):
     dev, layer = cfg3_layer
     run_and_check(CFG3, layer, dev, None, synth.make_x(CFG3.hidden, T, seed=300 + T))
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_full_size_fp4_layer_q8_activations(cfg3_layer, T):
+    """configs[2]'s layer (the same MXFP4 experts) with Q8 activations for the routed experts
+    (ref/emulate_ds4.py: int8 per 32, scale amax/127; CUDA-core kernels), FP8 shared expert."""
+    dev, _ = cfg3_layer
+    layer = MoELayer(CFG3_Q8, dev, max_tokens=64)
+    run_and_check(CFG3_Q8, layer, dev, None, synth.make_x(CFG3_Q8.hidden, T, seed=500 + T))
+    layer.close()
 
 
 @pytest.mark.parametrize("name", ["cfg1", "cfg1_fp4"])
