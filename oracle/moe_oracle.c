@@ -232,13 +232,17 @@ void orc_gemv_fp8_e8m0(const uint8_t *w, const uint8_t *ws, int rows, int k, con
     for (int r = 0; r < rows; r++) {
         const uint8_t *wr = w + (size_t)r * k;
         const uint8_t *sr = ws + (size_t)(r / 32) * (k / 32);
+        /* tokens in groups of 64 (each token's sum is independent of the grouping) */
+        for (int t0 = 0; t0 < n_tok; t0 += 64) {
+        const int nt = n_tok - t0 < 64 ? n_tok - t0 : 64;
         float acc[64];
-        for (int t = 0; t < n_tok; t++) acc[t] = 0.f;
+        for (int t = 0; t < nt; t++) acc[t] = 0.f;
         for (int c = 0; c < k; c++) {
             const float B = g_e4m3[wr[c]] * u2f((uint32_t)sr[c / 32] << 23);
-            for (int t = 0; t < n_tok; t++) acc[t] = acc[t] + A[(size_t)t * k + c] * B;
+            for (int t = 0; t < nt; t++) acc[t] = acc[t] + A[(size_t)(t0 + t) * k + c] * B;
         }
-        for (int t = 0; t < n_tok; t++) y[(size_t)t * rows + r] = acc[t];
+        for (int t = 0; t < nt; t++) y[(size_t)(t0 + t) * rows + r] = acc[t];
+        }
     }
     free(A);
 }
@@ -256,13 +260,17 @@ void orc_gemv_fp8_b128(const uint8_t *w, const float *ws, int rows, int k, const
     for (int r = 0; r < rows; r++) {
         const uint8_t *wr = w + (size_t)r * k;
         const float *sr = ws + (size_t)(r / 128) * kb;
+        /* tokens in groups of 64 (each token's sum is independent of the grouping) */
+        for (int t0 = 0; t0 < n_tok; t0 += 64) {
+        const int nt = n_tok - t0 < 64 ? n_tok - t0 : 64;
         float acc[64];
-        for (int t = 0; t < n_tok; t++) acc[t] = 0.f;
+        for (int t = 0; t < nt; t++) acc[t] = 0.f;
         for (int c = 0; c < k; c++) {
             const float B = g_e4m3[wr[c]] * sr[c / 128];
-            for (int t = 0; t < n_tok; t++) acc[t] = acc[t] + A[(size_t)t * k + c] * B;
+            for (int t = 0; t < nt; t++) acc[t] = acc[t] + A[(size_t)(t0 + t) * k + c] * B;
         }
-        for (int t = 0; t < n_tok; t++) y[(size_t)t * rows + r] = acc[t];
+        for (int t = 0; t < nt; t++) y[(size_t)(t0 + t) * rows + r] = acc[t];
+        }
     }
     free(A);
 }
@@ -279,14 +287,18 @@ void orc_gemv_mxfp4(const uint8_t *w, const uint8_t *ws, int rows, int k, const 
     for (int r = 0; r < rows; r++) {
         const uint8_t *wr = w + (size_t)r * (k / 2);
         const uint8_t *sr = ws + (size_t)r * (k / 32);
+        /* tokens in groups of 64 (each token's sum is independent of the grouping) */
+        for (int t0 = 0; t0 < n_tok; t0 += 64) {
+        const int nt = n_tok - t0 < 64 ? n_tok - t0 : 64;
         float acc[64];
-        for (int t = 0; t < n_tok; t++) acc[t] = 0.f;
+        for (int t = 0; t < nt; t++) acc[t] = 0.f;
         for (int c = 0; c < k; c++) {
             const uint8_t byte = wr[c / 2];
             const float B = kFp4[(c & 1) ? (byte >> 4) : (byte & 15)] * u2f((uint32_t)sr[c / 32] << 23);
-            for (int t = 0; t < n_tok; t++) acc[t] = acc[t] + A[(size_t)t * k + c] * B;
+            for (int t = 0; t < nt; t++) acc[t] = acc[t] + A[(size_t)(t0 + t) * k + c] * B;
         }
-        for (int t = 0; t < n_tok; t++) y[(size_t)t * rows + r] = acc[t];
+        for (int t = 0; t < nt; t++) y[(size_t)(t0 + t) * rows + r] = acc[t];
+        }
     }
     free(A);
 }
