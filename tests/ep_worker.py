@@ -54,6 +54,65 @@ def parity(rank, n, port, q):
         q.put((rank, None, traceback.format_exc()))
 
 
+def _parity_full(rank, n, port, q, zipf):
+    """the full-size FP8 layer (256 experts, hidden 7168) sharded over n ranks, 256 tokens
+    in all (256 / n per rank, the strong-scaling split), uniform routing (bias 0) or Zipf(1.2).  Each
+    rank checks its routes and outputs against the single-device oracle layer, whose weights it
+    regenerates from the same seeds (synth builds expert e from seed 1000 + e on any device)."""
+    try:
+        import dataclasses
+
+        from stblarge_b200.config import CFG2
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=n,
+                                timeout=datetime.timedelta(seconds=600))
+        cfg = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=zipf)
+        E_loc = cfg.n_experts // n
+        dev = synth.device_layer(cfg, experts=range(rank * E_loc, (rank + 1) * E_loc))
+        T = 256 // n
+        layer = MoELayer(cfg, dev, max_tokens=T, ep=(rank, n, None))
+        report = []
+        for call in range(2):
+            x_bits = synth.make_x(cfg.hidden, T, seed=900 + 10 * call + rank)
+            y = layer(torch.from_numpy(x_bits.view(np.int16)).cuda())
+            torch.cuda.synchronize()
+            report.append({"y": y.view(torch.int16).cpu().numpy().view(np.uint16), "x": x_bits,
+                           "route": layer.last_route(), "status": layer.status()})
+        dist.barrier()
+        layer.close()
+        del dev
+        torch.cuda.empty_cache()
+        dist.barrier()
+        dist.destroy_process_group()
+        # the oracle over the whole layer: every expert this rank's tokens chose, rebuilt from its seed
+        out = []
+        shared = synth.device_layer(cfg, experts=range(0))  # the shared expert and router only
+        shared = [(shared["shared_w"][m].cpu().numpy(), shared["shared_s"][m].cpu().numpy()) for m in range(3)]
+        for r in report:
+            idx = r["route"]["idx"]
+            W = {"router_w": synth.router_w(cfg), "router_bias": synth.router_bias(cfg),
+                 "routed": [[None] * cfg.n_experts for _ in range(3)], "shared": shared}
+            for e in np.unique(idx):
+                ws, ss = synth.routed_expert(cfg, 1000 + int(e), device="cuda")
+                for m in range(3):
+                    W["routed"][m][int(e)] = (ws[m].cpu().numpy(), ss[m].cpu().numpy())
+            y_ref, idx_ref, w_ref = O.moe_forward(cfg.as_dict(), W, r["x"])
+            out.append({"T": T, "idx": bool(np.array_equal(idx, idx_ref)),
+                        "w": bool(np.array_equal(r["route"]["weights"].view(np.uint32), w_ref.view(np.uint32))),
+                        "rel": _rel(r["y"], y_ref), "status": r["status"], "distinct": int(len(np.unique(idx)))})
+        q.put((rank, out, None))
+    except Exception:
+        q.put((rank, None, traceback.format_exc()))
+
+
+def parity_full_uniform(rank, n, port, q):
+    _parity_full(rank, n, port, q, 0.0)
+
+
+def parity_full_zipf(rank, n, port, q):
+    _parity_full(rank, n, port, q, 1.2)
+
+
 def skipped_call(rank, n, port, q):
     """Rank 1 skips one call: rank 0's waits on it run out (about 1 s each) and its status reports a
     timed-out wait; nothing faults.  Both ranks then meet at a host barrier before freeing anything."""

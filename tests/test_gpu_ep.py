@@ -15,6 +15,9 @@ from tests import ep_worker
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
 
+# full-size runs: every rank on its own GPU, as many ranks as there are GPUs (2, 4 or 8)
+N_FULL = max(n for n in (2, 4, 8) if n <= max(torch.cuda.device_count(), 2))
+
 
 def _port():
     with socket.socket() as s:
@@ -22,7 +25,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(fn, n):
+def _run(fn, n, timeout=300):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -31,7 +34,7 @@ def _run(fn, n):
         p.start()
     res = {}
     for _ in ps:
-        rank, out, err = q.get(timeout=300)
+        rank, out, err = q.get(timeout=timeout)
         res[rank] = (out, err)
     for p in ps:
         p.join(timeout=120)
@@ -43,6 +46,19 @@ def test_ep_two_ranks_match_oracle():
     for rank, (out, err) in sorted(res.items()):
         assert err is None, f"rank {rank}:\n{err}"
         for r in out:
+            assert r["idx"] and r["w"], (rank, r)
+            assert r["rel"] <= ep_worker.TOL, (rank, r)
+            assert r["status"] == 0, (rank, r)
+
+
+@pytest.mark.parametrize("fn", [ep_worker.parity_full_uniform, ep_worker.parity_full_zipf], ids=["uniform", "zipf1.2"])
+def test_ep_full_size_cfg4_matches_oracle(fn):
+    """configs[3] at full size over all GPUs of the box (256 tokens split over the ranks)."""
+    res = _run(fn, N_FULL, timeout=900)
+    for rank, (out, err) in sorted(res.items()):
+        assert err is None, f"rank {rank}:\n{err}"
+        for r in out:
+            print(f"rank {rank}/{N_FULL}: T={r['T']} distinct {r['distinct']} rel {r['rel']:.2e}")
             assert r["idx"] and r["w"], (rank, r)
             assert r["rel"] <= ep_worker.TOL, (rank, r)
             assert r["status"] == 0, (rank, r)
