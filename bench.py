@@ -11,14 +11,15 @@ CUDA events on the launching stream.  `e2e` is the same metric through the host-
 Default workload:
   * one GPU: configs[1] (cfg2, FP8 128x128 weights) at T = 16 decode tokens, the headline; the line
     also carries `sweep` (configs[1] at T = 1, 4, 16), `cfg3_sweep` (configs[2]: MXFP4 routed experts,
-    FP8 shared, Zipf(1.0) bias, T = 1, 4, 16, 64) and `cfg4_n1` (configs[3]'s 256 tokens on this one
+    FP8 shared, Zipf(1.0) bias, T = 1, 4, 16, 64), `cfg3q8_sweep` (the same layer with Q8 activations
+    for the routed experts, the reference's ds4 numerics) and `cfg4_n1` (configs[3]'s 256 tokens on this one
     GPU: the N = 1 point of the strong-scaling curve);
   * N > 1 GPUs: configs[3] (cfg4), 256 tokens in all split over the ranks (strong scaling), expert
     parallelism: rank r holds routed experts [r 256/N, (r+1) 256/N) (router and shared expert
     replicated), every rank routes its own tokens and the layer's kernels dispatch them to the owning
     ranks and bring the outputs back through NVLink peer memory.  The line also carries `weak_cfg2`
     (configs[1] with 16 tokens per rank).  Time = max over ranks of the device time.
---workload cfg2|cfg3|cfg3ref|cfg4|cfg5 picks one explicitly (--zipf: Zipf(1.2) routing for cfg4).
+--workload cfg2|cfg3|cfg3ref|cfg3q8|cfg4|cfg5 picks one explicitly (--zipf: Zipf(1.2) routing for cfg4).
 
 --impl reference: the reference's CPU path (the CPU oracle restating stbl/model.cu:426-594 on the
 numerics of ref/kernel.py) on the host cores, the same workload, config and metric; rank 0 only.
@@ -37,7 +38,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from stblarge_b200 import synth  # noqa: E402
-from stblarge_b200.config import CFG2, CFG3, CFG3_REF, FMT_FP8_E8M0, FMT_MXFP4  # noqa: E402
+from stblarge_b200.config import CFG2, CFG3, CFG3_Q8, CFG3_REF, FMT_FP8_E8M0, FMT_MXFP4  # noqa: E402
 
 METRIC = "MoE-layer decode tokens/s (full-size FP8 layer)"
 UNIT = "tokens/s"
@@ -200,6 +201,8 @@ def workload_of(args, world):
         return wl, CFG3, args.tokens
     if wl == "cfg3ref":
         return wl, CFG3_REF, args.tokens
+    if wl == "cfg3q8":
+        return wl, CFG3_Q8, args.tokens
     return wl, CFG2, args.tokens
 
 
@@ -211,6 +214,9 @@ def config_of(args, wl, T, world):
                          if wl == "cfg4" else
                          "cfg3 full-size layer, MXFP4 routed experts (FP8 shared), Zipf(1.0) routing"
                          if wl == "cfg3" else
+                         "cfg3q8 full-size layer, MXFP4 routed experts with Q8 activations (int8 per 32), FP8 shared, "
+                         "Zipf(1.0) routing"
+                         if wl == "cfg3q8" else
                          "cfg3ref full-size layer in the reference engine's formats and routing: MXFP4 routed "
                          "experts, FP8 shared expert with e8m0 32x32 block scales, sqrt(softplus) top-8 of 256"
                          if wl == "cfg3ref" else
@@ -341,7 +347,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg3ref", "cfg4", "cfg5"],
+    ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg3ref", "cfg3q8", "cfg4", "cfg5"],
                     help="default: cfg2 on one GPU, cfg4 on more")
     ap.add_argument("--zipf", action="store_true", help="cfg4: Zipf(1.2) expert popularity instead of uniform")
     ap.add_argument("--no-cpu", action="store_true")
@@ -374,7 +380,7 @@ def main():
     E_loc = cfg.n_experts // world
     shard = range(rank * E_loc, (rank + 1) * E_loc)
     weights = synth.device_layer(cfg, device=dev, experts=shard)
-    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if wl in ("cfg3", "cfg3ref") else 16),
+    layer = MoELayer(cfg, weights, max_tokens=max(T, 64 if wl in ("cfg3", "cfg3ref", "cfg3q8") else 16),
                      ep=(rank, world, None) if world > 1 else None)
     n_steps = args.warmup + args.steps
     xs = torch.stack([torch.from_numpy(synth.make_x(cfg.hidden, T, seed=1_000_000 * (rank + 1) + i).view(np.int16))
@@ -458,7 +464,7 @@ def main():
 
     extra = {}
     sweep = []
-    if not args.no_sweep and world == 1 and wl in ("cfg2", "cfg3", "cfg3ref"):
+    if not args.no_sweep and world == 1 and wl in ("cfg2", "cfg3", "cfg3ref", "cfg3q8"):
         # batch sizes of the workload's config: configs[1] 1, 4, 16; configs[2] 1, 4, 16, 64
         sweep = sweep_layer(layer, cfg, (1, 4, 16) if wl == "cfg2" else (1, 4, 16, 64), distinct_of, timed_steps,
                             peak, 7_000_000)
@@ -507,6 +513,11 @@ def main():
         extra["cfg3_sweep"] = sweep_layer(l3, CFG3, (1, 4, 16, 64), distinct_of, timed_steps, peak, 8_000_000)
         extra["cfg3_device_status"] = l3.status()
         l3.close()
+        # the same experts with Q8 activations for the routed experts (CUDA-core kernels)
+        lq = MoELayer(CFG3_Q8, w3, max_tokens=64)
+        extra["cfg3q8_sweep"] = sweep_layer(lq, CFG3_Q8, (1, 4, 16, 64), distinct_of, timed_steps, peak, 8_000_000)
+        extra["cfg3q8_device_status"] = lq.status()
+        lq.close()
         layer = None
 
     if world > 1 and not args.no_sweep and wl == "cfg4":
@@ -533,9 +544,11 @@ def main():
             "warmup": args.warmup, "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if wl == "cfg4" else "weak", "vs_baseline": None,
             "dtype": ("fp8-e4m3 weights and activations, fp32 accumulate, bf16 io" if cfg.routed_fmt != FMT_MXFP4 else
+                      "e2m1 routed / e4m3 shared weights, int8 routed / e4m3 shared activations, exact integer "
+                      "block sums + fp32 accumulate, bf16 io" if cfg.act_q8 else
                       "e2m1 routed / e4m3 shared weights, e4m3 activations, fp32 accumulate, bf16 io"),
             "data": ("synthetic (seeded ~N(0,0.02) weights quantized to "
-                     + {"cfg3": "MXFP4 routed / FP8 128x128 shared",
+                     + {"cfg3": "MXFP4 routed / FP8 128x128 shared", "cfg3q8": "MXFP4 routed / FP8 128x128 shared",
                         "cfg3ref": "MXFP4 routed / FP8 e8m0-32x32 shared"}.get(wl, "FP8 128x128")
                      + "; bf16 ~N(0,1) tokens)"),
             "config": config_of(args, wl, T, world),
@@ -544,7 +557,9 @@ def main():
             "distinct_experts_per_step": float(np.mean(distinct)),
             "kernel_ms_per_step": {"router": kt["router"] / max(kt["calls"], 1) * 1e3, "up": up_ms,
                                    "down": kt["down"] / max(kt["calls"], 1) * 1e3},
-            "roofline": {"bound": "hbm", "kernel": ("expert_tc4_kernel<up> (tcgen05 MXFP4 routed + FP8 shared gate+up, SwiGLU)"
+            "roofline": {"bound": "hbm", "kernel": ("expert_q8_kernel<up> (CUDA-core MXFP4 x Q8 routed gate+up, SwiGLU) "
+                                                    "after expert_tc_kernel<up> (FP8 shared)" if cfg.act_q8 else
+                                                    "expert_tc4_kernel<up> (tcgen05 MXFP4 routed + FP8 shared gate+up, SwiGLU)"
                                                     if cfg.routed_fmt == FMT_MXFP4 else
                                                     "expert_tc_kernel<up> (tcgen05 FP8 gate+up, SwiGLU)"),
                          "achieved": up_gbs, "peak": peak, "unit": "GB/s", "frac": up_gbs / peak, "peak_kind": peak_kind,

@@ -37,7 +37,7 @@ namespace stbl {
 
 constexpr int kT4Threads = 192;
 constexpr int kT4Acc = 4;            // item accumulators in TMEM (32 columns each for up, 16 for down)
-constexpr int kT4Kb = 2;             // K blocks per stage (one 256-K unit)
+constexpr int kT4Kb = kT4StageKb;    // K blocks per stage (one unit of stream-K)
 constexpr int kT4ATile = 128 * 128;  // one K block of one weight matrix in shared memory (unpacked codes)
 constexpr int kT4BTile = kTcN * 128; // one K block of activations
 constexpr int kT4SfSlots = 4;        // scale-factor slots in TMEM, 16 columns each (A0, A1, B)
@@ -52,7 +52,7 @@ struct T4 {
     static constexpr int A = nA * kT4Kb * kT4ATile;        // [m][kb][128 rows][128 B]
     static constexpr int B = kT4Kb * kT4BTile;             // [kb][16 rows][128 B]
     static constexpr int SF = (nA + 1) * kT4Kb * 512;      // [m | B][kb][512 B]
-    static constexpr int stage = A + B + SF;               // 71 KB
+    static constexpr int stage = (A + B + SF + 1023) / 1024 * 1024;  // 71 KB at two K blocks
     static constexpr int NV = nA * kTcN;                   // accumulator columns per item
 };
 static_assert(T4<true>::stage % 1024 == 0 && T4<false>::stage % 1024 == 0, "stages must keep 1 KB alignment");
@@ -93,7 +93,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;     // reduction length
     const int rows = UP ? p.I : p.H;  // output rows per matrix (down: H / 256 items of 2 tiles)
-    const int nu = K / 256;               // 256-K units per item
+    const int nu = K / (128 * kT4Kb);     // units (stages) per item
     const int tiles = UP ? rows / 128 : rows / 256;
     // 128-row weight tile of matrix slot m of item tile t: up, gate (m 0) and up (m 1) rows of tile t;
     // down, the two halves of W2 rows [256 t, 256 t + 256)

@@ -109,7 +109,7 @@ struct stbl_moe {
     // tensor-core kernels (FP8 experts): tensor maps, launch shape
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
-    int tc_nst_down2 = 0, tc_smem_down2 = 0;  // the down kernel with two-tile items (single GPU, T >= 4)
+    int tc_nst_down2 = 0, tc_smem_down2 = 0;  // the down kernel with two-tile items (T >= 4)
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_bs = false;           // routed experts MXFP4 or FP8-e8m0: the block-scaled tensor-core kernels
     bool shared_bs = false;           // shared expert FP8-e8m0: handled by the block-scaled kernels too
@@ -194,7 +194,7 @@ CUtensorMap weight_map8x2(const void *base, int K, int rows, int experts, long l
         throw std::runtime_error("FP8 expert weights must be 16-byte aligned (base, row and expert strides)");
     const cuuint64_t dims[4] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128), (cuuint64_t)experts};
     const cuuint64_t strides[3] = {(cuuint64_t)K, 128, (cuuint64_t)(estride ? estride : (long long)rows * K)};
-    const cuuint32_t box[4] = {128, 128, 2, 1};
+    const cuuint32_t box[4] = {128, 128, (cuuint32_t)kT4StageKb, 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, es,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -209,7 +209,7 @@ CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long lon
         throw std::runtime_error("MXFP4 expert weights must be 32-byte aligned (base, row and expert strides)");
     const cuuint64_t dims[4] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128), (cuuint64_t)experts};
     const cuuint64_t strides[3] = {(cuuint64_t)(K / 2), 64, (cuuint64_t)estride};
-    const cuuint32_t box[4] = {128, 128, 2, 1};
+    const cuuint32_t box[4] = {128, 128, (cuuint32_t)kT4StageKb, 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, const_cast<void *>(base), dims, strides, box,
                                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -226,7 +226,7 @@ CUtensorMap act_map2(const void *base, int K, int rows) {
     CUtensorMap m;
     const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128)};
     const cuuint64_t strides[2] = {(cuuint64_t)K, 128};
-    const cuuint32_t box[3] = {128, 16, 2};
+    const cuuint32_t box[3] = {128, 16, (cuuint32_t)kT4StageKb};
     const cuuint32_t es[3] = {1, 1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -499,7 +499,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         };
         pick(true, false, m->tc_nst_up, m->tc_smem_up);
         pick(false, false, m->tc_nst_down, m->tc_smem_down);
-        if (m->ep_n == 1) pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
+        pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
         if (m->routed_bs) {
             // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
             // fit; a MXFP4 stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
@@ -645,8 +645,9 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
     // down items of two 128-row tiles from T = 4 on (measured at 256 experts, down kernel: T=16 218 ->
-    // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us); not under expert parallelism
-    const bool two = !up && m->ep_n == 1 && p.T >= 4;
+    // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us); under expert parallelism
+    // too (the epilogue stores each tile's rows into the source ranks' eo rows)
+    const bool two = !up && p.T >= 4;
     void *args[] = {&maps, &p, up ? &m->tc_nst_up : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
     launch_pdl(expert_tc_kernel_ptr(up, two), dim3(m->sms), dim3(192), args,
                up ? m->tc_smem_up : (two ? m->tc_smem_down2 : m->tc_smem_down), st);

@@ -7,6 +7,10 @@
 
 namespace stbl {
 
+// K blocks of 128 per pipeline stage of the block-scaled (MXFP4 / FP8-e8m0) expert kernels; the
+// weight and activation tensor maps' boxes span this many K blocks
+constexpr int kT4StageKb = 2;
+
 struct TcMaps {
     CUtensorMap w[2];  // up: routed gate, routed up; down: routed down (twice)
     CUtensorMap s[2];  // up: shared gate, shared up; down: shared down (twice)
