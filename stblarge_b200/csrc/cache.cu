@@ -351,17 +351,18 @@ struct FileCopyParams {
 };
 
 // 16 GGUF MXFP4 blocks (272 bytes: per block the e8m0 scale, then values i and 16 + i in the low and
-// high nibble of byte i) -> 256 bytes of codes (values 2j, 2j + 1 in byte j, low nibble first) and the
-// 16 scales as four words of the scale-block layout (word kk of the group goes 512 bytes after word kk-1)
-__device__ __forceinline__ void convert_group(const uint8_t *src, uint8_t *codes, uint8_t *sdst) {
+// high nibble of byte i, as 17 uint4 words) -> 256 bytes of codes (values 2j, 2j + 1 in byte j, low
+// nibble first) in codes[16] and the 16 scales as four words of the scale-block layout in sw[4]
+__device__ __forceinline__ void convert_group(const uint4 *src, uint4 (&codes)[16], uint32_t (&sw)[4]) {
     uint32_t w[69];
 #pragma unroll
     for (int i = 0; i < 17; i++) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+        const uint4 v = src[i];
         w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
     }
     w[68] = 0;
-    uint32_t sw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 4; i++) sw[i] = 0u;
 #pragma unroll
     for (int b = 0; b < 16; b++) {
         const int o = 17 * b;
@@ -377,15 +378,24 @@ __device__ __forceinline__ void convert_group(const uint8_t *src, uint8_t *codes
         const uint32_t l0 = q[0] & 0x0F0F0F0Fu, l1 = q[1] & 0x0F0F0F0Fu, l2 = q[2] & 0x0F0F0F0Fu, l3 = q[3] & 0x0F0F0F0Fu;
         const uint32_t h0 = (q[0] >> 4) & 0x0F0F0F0Fu, h1 = (q[1] >> 4) & 0x0F0F0F0Fu, h2 = (q[2] >> 4) & 0x0F0F0F0Fu,
                        h3 = (q[3] >> 4) & 0x0F0F0F0Fu;
-        reinterpret_cast<uint4 *>(codes)[b] = make_uint4(pack(l0, l1), pack(l2, l3), pack(h0, h1), pack(h2, h3));
+        codes[b] = make_uint4(pack(l0, l1), pack(l2, l3), pack(h0, h1), pack(h2, h3));
     }
-#pragma unroll
-    for (int kk = 0; kk < 4; kk++) *reinterpret_cast<uint32_t *>(sdst + kk * 512) = sw[kk];
 }
 
-// One CTA per 128-row tile of one matrix of one staged expert; thread t takes (row t / G, group t % G)
-// with G = K / 512 groups of 16 blocks per row, so a warp reads consecutive 272-byte runs.
-__global__ void __launch_bounds__(kCopyThreads) cache_file_copy_kernel(FileCopyParams p) {
+constexpr int kFileWarps = 2;                        // warps per CTA of the conversion
+constexpr int kFileGroupBytes = 272;                 // 16 GGUF blocks: 512 values of one row
+constexpr int kFileRunBytes = 32 * kFileGroupBytes;  // the 32 consecutive groups a warp converts at a time
+
+// The staged GGUF rows of one matrix are one contiguous array of 272-byte groups (group u = row
+// u / G, groups g = u % G of K / 512 per row), and the slot's codes of that matrix one contiguous
+// array of 256-byte groups in the same order.  A warp takes 32 consecutive groups (8,704 bytes): it
+// reads them from page-locked host memory with coalesced 512-byte loads (lane l the 16 bytes at
+// 16 l of each), parks them in its shared-memory buffer, converts group `lane` from there, parks the
+// 8 KB of codes back (rotated by lane so the 16-byte stores hit distinct banks) and writes them to the
+// slot with coalesced 512-byte stores; the four scale words of each group go to the scale-block
+// layout directly.  Host memory sees only whole 512-byte requests.
+__global__ void __launch_bounds__(kFileWarps * 32) cache_file_copy_kernel(FileCopyParams p) {
+    extern __shared__ uint4 fsm[];
     const int nj = *(volatile const int *)p.n_jobs;
     const int n = min(nj - p.begin, p.cap);
     if (n <= 0) return;
@@ -393,21 +403,45 @@ __global__ void __launch_bounds__(kCopyThreads) cache_file_copy_kernel(FileCopyP
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.status, kErrRead);
         return;
     }
-    const int per_job = p.tiles[0] + p.tiles[1] + p.tiles[2];
-    for (long long it = blockIdx.x; it < (long long)n * per_job; it += gridDim.x) {
-        const int j = (int)(it / per_job);
-        int tile = (int)(it % per_job), q = 0;
-        while (q < 2 && tile >= p.tiles[q]) tile -= p.tiles[q++];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint4 *buf = fsm + (size_t)warp * (kFileRunBytes / 16);
+    int runs[3];
+#pragma unroll
+    for (int q = 0; q < 3; q++) runs[q] = p.tiles[q] * 128 * (p.K[q] / 512) / 32;
+    const int per_job = runs[0] + runs[1] + runs[2];
+    const long long total = (long long)n * per_job;
+    for (long long wj = (long long)blockIdx.x * kFileWarps + warp; wj < total; wj += (long long)gridDim.x * kFileWarps) {
+        const int j = (int)(wj / per_job);
+        int run = (int)(wj % per_job), q = 0;
+        while (q < 2 && run >= runs[q]) run -= runs[q++];
         const int2 job = p.jobs[p.begin + j];
-        const int K = p.K[q], G = K / 512, rowb = K / 32 * 17;
-        const uint8_t *src = p.src[j * 3 + q] + (size_t)tile * 128 * rowb;
-        uint8_t *codes = p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + (size_t)tile * 128 * (K / 2);
-        uint8_t *scales = p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[3 + q] + (size_t)tile * (K / 128) * 512;
-        for (int t = threadIdx.x; t < 128 * G; t += kCopyThreads) {
-            const int r = t / G, g = t % G;
-            convert_group(src + (size_t)r * rowb + (size_t)g * 272, codes + (size_t)r * (K / 2) + (size_t)g * 256,
-                          scales + (size_t)(4 * g) * 512 + (r & 31) * 16 + (r >> 5) * 4);
+        const int K = p.K[q], G = K / 512;
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.src[j * 3 + q] + (size_t)run * kFileRunBytes);
+#pragma unroll
+        for (int k = 0; k < 17; k++) buf[k * 32 + lane] = __ldg(src + k * 32 + lane);
+        __syncwarp();
+        uint4 codes[16];
+        uint32_t sw[4];
+        convert_group(buf + lane * 17, codes, sw);
+        __syncwarp();
+        // codes of group `lane` into the buffer, 16-byte unit b at lane * 16 + ((b + lane) & 15)
+#pragma unroll
+        for (int b = 0; b < 16; b++) buf[lane * 16 + ((b + lane) & 15)] = codes[b];
+        __syncwarp();
+        uint8_t *slot = p.pool + (size_t)job.x * p.slot_bytes;
+        uint4 *dst = reinterpret_cast<uint4 *>(slot + p.piece_off[q] + (size_t)run * (32 * 256));
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int U = k * 32 + lane, gl = U >> 4, b = U & 15;  // unit b of the run's group gl
+            dst[U] = buf[gl * 16 + ((b + gl) & 15)];
         }
+        // the group's 16 scales: four words of the scale-block layout of its row's 128-row tile
+        const int u = run * 32 + lane, r = u / G, g = u % G;
+        uint8_t *sdst = slot + p.piece_off[3 + q] + (size_t)(r >> 7) * (K / 128) * 512 + (size_t)(4 * g) * 512 +
+                        (r & 31) * 16 + ((r & 127) >> 5) * 4;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) *reinterpret_cast<uint32_t *>(sdst + kk * 512) = sw[kk];
+        __syncwarp();  // the buffer is reused by the next run
     }
 }
 
@@ -481,7 +515,7 @@ void launch_file_copy(stbl_cache *c, int which, int round, uint32_t *status, cud
     for (int q = 0; q < 6; q++) fp.piece_off[q] = c->piece_off[q];
     const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
     for (int q = 0; q < 3; q++) fp.K[q] = ks[q], fp.tiles[q] = rows[q] / 128;
-    cache_file_copy_kernel<<<c->copy_ctas, kCopyThreads, 0, st>>>(fp);
+    cache_file_copy_kernel<<<2 * c->copy_ctas, kFileWarps * 32, kFileWarps * kFileRunBytes, st>>>(fp);
     CK(cudaGetLastError());
 }
 
