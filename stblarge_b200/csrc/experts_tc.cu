@@ -70,12 +70,13 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
 const void *hquant_kernel_ptr() { return (const void *)hquant_kernel; }
 
 template __global__ void expert_tc_kernel<true, false>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<true, true>(const __grid_constant__ TcMaps, TcParams, int);
 template __global__ void expert_tc_kernel<false, false>(const __grid_constant__ TcMaps, TcParams, int);
 template __global__ void expert_tc_kernel<false, true>(const __grid_constant__ TcMaps, TcParams, int);
 
-// two: the down product with items of two 128-row tiles (not with expert parallelism)
+// two: items of two 128-row tiles (up: 128 gate + 128 up rows; down: 256 rows of W2)
 const void *expert_tc_kernel_ptr(bool up, bool two) {
-    if (up) return (const void *)expert_tc_kernel<true, false>;
+    if (up) return two ? (const void *)expert_tc_kernel<true, true> : (const void *)expert_tc_kernel<true, false>;
     return two ? (const void *)expert_tc_kernel<false, true> : (const void *)expert_tc_kernel<false, false>;
 }
 
@@ -84,7 +85,7 @@ const void *gather_kernel_ptr() { return (const void *)gather_kernel; }
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
 int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two) {
     const int K = up ? H : I, nkb = K / 128;
-    return nst * (two && !up ? kStage2 : kStage) + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 6 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
+    return nst * (two ? kStage2 : kStage) + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 10 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
            8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
 }
 

@@ -110,6 +110,8 @@ struct stbl_moe {
     TcMaps tc_up{}, tc_down{};
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
     int tc_nst_down2 = 0, tc_smem_down2 = 0;  // the down kernel with two-tile items (T >= 4)
+    int tc_nst_up2 = 0, tc_smem_up2 = 0;      // the up kernel with two-tile items (128 gate + 128 up rows)
+    TcMaps tc_up2{};                          // its maps: 128-row boxes of the gate and up matrices
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_bs = false;           // routed experts MXFP4 or FP8-e8m0: the block-scaled tensor-core kernels
     bool shared_bs = false;           // shared expert FP8-e8m0: handled by the block-scaled kernels too
@@ -463,20 +465,28 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         if (m->routed_tc) {
             m->tc_up.w[0] = weight_map(d->routed_w[0], H, I, m->n_slots, wst[0], 64);
             m->tc_up.w[1] = weight_map(d->routed_w[1], H, I, m->n_slots, wst[1], 64);
+            m->tc_up2.w[0] = weight_map(d->routed_w[0], H, I, m->n_slots, wst[0], 128);
+            m->tc_up2.w[1] = weight_map(d->routed_w[1], H, I, m->n_slots, wst[1], 128);
             m->tc_down.w[0] = weight_map(d->routed_w[2], I, H, m->n_slots, wst[2], 128);
             m->tc_down.w[1] = m->tc_down.w[0];
         }
         if (m->has_shared && !m->shared_bs) {
             m->tc_up.s[0] = weight_map(d->shared_w[0], H, I, 1, (long long)I * H, 64);
             m->tc_up.s[1] = weight_map(d->shared_w[1], H, I, 1, (long long)I * H, 64);
+            m->tc_up2.s[0] = weight_map(d->shared_w[0], H, I, 1, (long long)I * H, 128);
+            m->tc_up2.s[1] = weight_map(d->shared_w[1], H, I, 1, (long long)I * H, 128);
             m->tc_down.s[0] = weight_map(d->shared_w[2], I, H, 1, (long long)H * I, 128);
             m->tc_down.s[1] = m->tc_down.s[0];
         }
-        if (!m->routed_tc && m->has_shared && !m->shared_bs)
+        if (!m->routed_tc && m->has_shared && !m->shared_bs) {
             m->tc_up.w[0] = m->tc_up.w[1] = m->tc_up.s[0], m->tc_down.w[0] = m->tc_down.w[1] = m->tc_down.s[0];
-        if (!m->has_shared && m->routed_tc)
+            m->tc_up2.w[0] = m->tc_up2.w[1] = m->tc_up2.s[0];
+        }
+        if (!m->has_shared && m->routed_tc) {
             m->tc_up.s[0] = m->tc_up.s[1] = m->tc_up.w[0], m->tc_down.s[0] = m->tc_down.s[1] = m->tc_down.w[0];
-        if (!m->routed_tc && (!m->has_shared || m->shared_bs)) m->tc_up = m->tc4_up, m->tc_down = m->tc4_down;  // unused, valid
+            m->tc_up2.s[0] = m->tc_up2.s[1] = m->tc_up2.w[0];
+        }
+        if (!m->routed_tc && (!m->has_shared || m->shared_bs)) m->tc_up = m->tc_up2 = m->tc4_up, m->tc_down = m->tc4_down;  // unused, valid
         m->bmap_xa = act_map(m->xq_a, H, Tpad);
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
         m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
@@ -498,6 +508,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
             CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up, two), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         };
         pick(true, false, m->tc_nst_up, m->tc_smem_up);
+        pick(true, true, m->tc_nst_up2, m->tc_smem_up2);
         pick(false, false, m->tc_nst_down, m->tc_smem_down);
         pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
         if (m->routed_bs) {
@@ -640,17 +651,21 @@ void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
     launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
 }
 
+// up items of 128 gate + 128 up rows from this many tokens on (the up kernel's two-tile form)
+constexpr int kUpTwoMinT = 4;
+
 void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
-    TcMaps maps = up ? m->tc_up : m->tc_down;
+    const bool up2 = up && p.T >= kUpTwoMinT;
+    TcMaps maps = up ? (up2 ? m->tc_up2 : m->tc_up) : m->tc_down;
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
     // down items of two 128-row tiles from T = 4 on (measured at 256 experts, down kernel: T=16 218 ->
     // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us); under expert parallelism
     // too (the epilogue stores each tile's rows into the source ranks' eo rows)
-    const bool two = !up && p.T >= 4;
-    void *args[] = {&maps, &p, up ? &m->tc_nst_up : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
+    const bool two = up ? up2 : p.T >= 4;
+    void *args[] = {&maps, &p, up ? (two ? &m->tc_nst_up2 : &m->tc_nst_up) : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
     launch_pdl(expert_tc_kernel_ptr(up, two), dim3(m->sms), dim3(192), args,
-               up ? m->tc_smem_up : (two ? m->tc_smem_down2 : m->tc_smem_down), st);
+               up ? (two ? m->tc_smem_up2 : m->tc_smem_up) : (two ? m->tc_smem_down2 : m->tc_smem_down), st);
 }
 
 // the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range)

@@ -16,7 +16,9 @@
 //              fp32 block scales (weight block x activation block: the promotion of
 //              ref/kernel.py:85-91) and accumulate in registers; then write the outputs.
 // up: the tile is [64 gate rows; 64 up rows]; h = bf16(silu(bf16 g) * bf16 u * w) (stbl/kernels.cu:
-//   445-459).  hquant_kernel then re-quantizes h (act_quant per 128, ref/kernel.py:35-45).
+//   445-459).  hquant_kernel then re-quantizes h (act_quant per 128, ref/kernel.py:35-45).  With T2 an
+//   up item is 128 gate rows and the matching 128 up rows (two boxes per stage, two accumulator sets),
+//   so each epilogue thread holds a row's gate and up sums and applies SwiGLU directly.
 // down: the tile is 128 rows of W2; eo = bf16(W2 q(h)); combine_kernel (combine.cu) adds them.  With
 //   T2 an item takes two such tiles (256 rows, two boxes per stage, two accumulator sets in TMEM) and
 //   the MMA issuer alternates between them: a 128-K block of two tiles costs the tensor pipe about as
@@ -49,7 +51,6 @@ constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contig
 // launch these number themselves 0..ncta-1).
 template <bool UP, bool T2 = false>
 __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
-    static_assert(!(UP && T2), "two-tile items are a down-product option");
     constexpr int NT = T2 ? 2 : 1;                       // weight tiles per item
     constexpr int STAGE = T2 ? kStage2 : kStage;
     constexpr int TMEM_COLS = NT * kTcTmemCols;
@@ -58,7 +59,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     const int K = UP ? p.H : p.I;            // reduction length
     const int rows = UP ? p.I : p.H;         // output rows per matrix
     const int nkb = K / 128;
-    const int tiles = UP ? rows / 64 : rows / (128 * NT);
+    const int tiles = UP ? (T2 ? rows / 128 : rows / 64) : rows / (128 * NT);
     unsigned char *stages = smem;                                         // [nst][A tile(s) | B tile]
     float *sx = reinterpret_cast<float *>(stages + (size_t)nst * STAGE);  // [2][16][nkb] activation scales
     float *sw = sx + 2 * kTcN * nkb;                                      // [2][2][nkb] weight scales
@@ -66,7 +67,9 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
     int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);           // [2][16] B column of a slot
     int *slot_dst = slot_col + 2 * kTcN;                                  // [2][16] output row of a slot
-    Chunk *ctab = reinterpret_cast<Chunk *>(slot_dst + 2 * kTcN);         // [kTcChunks] from chunk_begin
+    int *col_dst = slot_dst + 2 * kTcN;                                   // [2][16] up T2: h row of a column (-1: none)
+    float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);         // [2][16] up T2: routing weight of a column
+    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);            // [kTcChunks] from chunk_begin
     uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kTcChunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
@@ -160,9 +163,14 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     const int s = q % nst, kb = kb0 + u;
                     unsigned char *a = stages + (size_t)s * STAGE;
                     mbar_arrive_expect_tx(&full[s], STAGE);
-                    if (UP) {
+                    if (UP && !T2) {
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 64, z, &full[s]);
                         tma_load_3d(a + kATile / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
+                    } else if (UP) {
+                        // 128 gate rows, then the matching 128 up rows (maps of 128-row boxes)
+#pragma unroll
+                        for (int m = 0; m < 2; m++)
+                            tma_load_3d(a + m * kATile, shared ? &maps.s[m] : &maps.w[m], kb * 128, tile * 128, z, &full[s]);
                     } else {
 #pragma unroll
                         for (int m = 0; m < NT; m++)
@@ -246,6 +254,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         float pw = 0.f;
         int pcol = 0, pdst = 0;
         float pwt = 0.f;
+        bool pval = false;
         // loads of item `it` into registers (thread et takes sx entries et, et + 128, ..., one weight scale
         // and, for et < 16, slot et's column, output row and routing weight)
         auto prefetch = [&](int it) {
@@ -263,7 +272,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             if (et < nsw) {
                 // up: the gate (m 0) and up (m 1) scales of the tile's 128-row block; down: tile m's block
                 const int m = et / nkb, kb = et % nkb;
-                const int rblk = UP ? (tile * 64) / 128 : NT * tile + m;
+                const int rblk = UP ? (T2 ? tile : (tile * 64) / 128) : NT * tile + m;
                 const int mat = UP ? m : 0;
                 const float *base = shared ? p.s_scale[mat] : p.w_scale[mat] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
                 pw = __ldg(base + (size_t)rblk * nkb + kb);
@@ -271,6 +280,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             if (et < kTcN) {
                 const int pos = ch.pos0 + et;
                 pcol = et, pdst = pos, pwt = 1.f;
+                pval = et < ch.n;
                 if (et < ch.n) {
                     if (!shared && p.pos_w) {
                         // expert parallelism: weight and origin of the receive row
@@ -298,6 +308,12 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             }
             if (et < nsw) sw[buf * 2 * nkb + et] = pw;
             if (et < kTcN) slot_col[buf * kTcN + et] = pcol, slot_dst[buf * kTcN + et] = pdst, slot_w[buf * kTcN + et] = pwt;
+            if (UP && T2) {
+                // the same by column (every column at most once: a token meets an expert at most once)
+                if (et < kTcN) col_dst[buf * kTcN + et] = -1;
+                bar_sync(2, 128);
+                if (et < kTcN && pval) col_dst[buf * kTcN + pcol] = pdst, col_w[buf * kTcN + pcol] = pwt;
+            }
         };
         int gq = 0;
         if (lo < hi) {
@@ -341,7 +357,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     for (int u = 0; u < kTcG; u++) {
                         const int kb = kb0 + u;
                         if (kb < kz) {
-                            const float wsc = swb[(UP ? mrow : m) * nkb + kb];
+                            const float wsc = swb[(UP && !T2 ? mrow : m) * nkb + kb];
 #pragma unroll
                             for (int j = 0; j < kTcN; j++) acc2[m][j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc2[m][j]);
                         }
@@ -394,7 +410,24 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             }
             const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
             const float *swt = slot_w + buf * kTcN;
-            if (UP) {
+            if (UP && T2) {
+                // this thread holds row r's gate sums (tile 0) and up sums (tile 1) for every column
+                const int *cd = col_dst + buf * kTcN;
+                const float *cw = col_w + buf * kTcN;
+                const int r = tile * 128 + row;
+#pragma unroll
+                for (int j = 0; j < kTcN; j++) {
+                    const int dst = cd[j];
+                    if (dst < 0) continue;
+                    float gv = bf16r(acc2[0][j]), uv = bf16r(acc2[NT - 1][j]);
+                    if (p.swiglu_limit > 0.f) {
+                        gv = fminf(gv, p.swiglu_limit);
+                        uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
+                    }
+                    const float hv = gv / (1.f + expf(-gv)) * uv * cw[j];
+                    p.h[(size_t)dst * p.I + r] = f32_to_bf16_bits(hv);
+                }
+            } else if (UP) {
                 // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
 #pragma unroll
                 for (int j = 0; j < kTcN; j++) xacc[row * 17 + j] = acc[j];
