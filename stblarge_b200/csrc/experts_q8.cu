@@ -64,42 +64,65 @@ __device__ __forceinline__ float e8m0_half(uint8_t s) {
     return __uint_as_float((uint32_t)s << 23) * 0.5f;
 }
 
-// R rows of one weight matrix (rows r0 .. r0 + R - 1 of slot z) against the chunk's n tokens: lane
-// l takes blocks l + 32 i (i < NBL); every weight load of the R rows is issued before any compute.
-// acc[j][t] gets row j's sums for token t (lane partials, reduced by the caller).
+// Signed bytes 2 w of one code word (8 values as nibbles 0..7, sign in each nibble's bit 3): lo gets
+// values 0..3, hi values 4..7.  Two table lookups per half (magnitude and negated magnitude, prmt on
+// the nibble's three index bits) and a third prmt picking between them by the sign bit.
+__device__ __forceinline__ void expand_word(uint32_t wd, uint32_t &lo, uint32_t &hi) {
+    constexpr uint32_t kNegLo = 0xFDFEFF00u, kNegHi = 0xF4F8FAFCu;  // 0, -1, -2, -3 | -4, -6, -8, -12
+    const uint32_t idx = wd & 0x77777777u, sgn = wd & 0x88888888u;
+    lo = prmt(prmt(kMagLo, kMagHi, idx), prmt(kNegLo, kNegHi, idx), (sgn >> 1) | 0x3210u);
+    hi = prmt(prmt(kMagLo, kMagHi, idx >> 16), prmt(kNegLo, kNegHi, idx >> 16), (sgn >> 17) | 0x3210u);
+}
+
+// R weight rows (wr[j], their e8m0 scales sr[j]) against the chunk's n tokens: lane l takes the K
+// blocks l + 32 i.  Per block each row's 16 code bytes become 32 signed bytes once; each token's 32
+// codes are loaded once and meet all R rows (8 dp4a per row).  The next block's weights are loaded
+// while this one is computed.  acc[j][t]: row j's lane partial for token t (reduced by the caller).
 template <int NBL, int R>
-__device__ __forceinline__ void q8_rows(const uint8_t *wrow, const uint8_t *srow, int K, int nb, int n, const int *xrow,
-                                        const Q8Params &p, int lane, float (&acc)[R][kQ8Tok]) {
-    uint4 wv[R][NBL];
-    float sc[R][NBL];
-#pragma unroll
-    for (int j = 0; j < R; j++)
-#pragma unroll
-        for (int i = 0; i < NBL; i++) {
-            const int b = lane + 32 * i;
-            if (b < nb) {
-                wv[j][i] = __ldg(reinterpret_cast<const uint4 *>(wrow + (size_t)j * (K / 2) + (size_t)b * 16));
-                sc[j][i] = e8m0_half(__ldg(srow + (size_t)j * nb + b));
-            }
-        }
+__device__ __forceinline__ void q8_rows(const uint8_t *const (&wr)[R], const uint8_t *const (&sr)[R], int K, int nb, int n,
+                                        const int *xrow, const Q8Params &p, int lane, float (&acc)[R][kQ8Tok]) {
 #pragma unroll
     for (int j = 0; j < R; j++)
 #pragma unroll
         for (int t = 0; t < kQ8Tok; t++) acc[j][t] = 0.f;
+    uint4 wv[R];
+    float sc[R];
+    auto load = [&](int b) {
 #pragma unroll
-    for (int t = 0; t < kQ8Tok; t++) {
-        if (t >= n) break;
-        const int8_t *xr = p.xq + (size_t)xrow[t] * K;
-        const float *dr = p.xd + (size_t)xrow[t] * p.xd_stride;
+        for (int j = 0; j < R; j++) {
+            wv[j] = __ldg(reinterpret_cast<const uint4 *>(wr[j] + (size_t)b * 16));
+            sc[j] = e8m0_half(__ldg(sr[j] + b));
+        }
+    };
+    if (lane < nb) load(lane);
+#pragma unroll 1
+    for (int i = 0; i < NBL; i++) {
+        const int b = lane + 32 * i;
+        if (b >= nb) break;  // a lane's blocks run out at its own count (nb need not be a multiple of 32)
+        uint32_t sv[R][8];
+        float s[R];
 #pragma unroll
-        for (int i = 0; i < NBL; i++) {
-            const int b = lane + 32 * i;
-            if (b < nb) {
-                const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(xr + (size_t)b * 32));
-                const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(xr + (size_t)b * 32 + 16));
-                const float dx = __ldg(dr + b);
+        for (int j = 0; j < R; j++) {
+            const uint32_t wd[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
-                for (int j = 0; j < R; j++) acc[j][t] = fmaf((float)block_dot(wv[j][i], qa, qb), sc[j][i] * dx, acc[j][t]);
+            for (int k = 0; k < 4; k++) expand_word(wd[k], sv[j][2 * k], sv[j][2 * k + 1]);
+            s[j] = sc[j];
+        }
+        if (b + 32 < nb) load(b + 32);
+#pragma unroll
+        for (int t = 0; t < kQ8Tok; t++) {
+            if (t >= n) break;
+            const int8_t *xr = p.xq + (size_t)xrow[t] * K + (size_t)b * 32;
+            const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(xr));
+            const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(xr + 16));
+            const float dx = __ldg(p.xd + (size_t)xrow[t] * p.xd_stride + b);
+            const uint32_t qd[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int j = 0; j < R; j++) {
+                int dot = 0;
+#pragma unroll
+                for (int k = 0; k < 8; k++) dot = __dp4a((int)sv[j][k], (int)qd[k], dot);
+                acc[j][t] = fmaf((float)dot, s[j] * dx, acc[j][t]);
             }
         }
     }
@@ -137,29 +160,34 @@ __global__ void __launch_bounds__(kQ8Threads, 2) expert_q8_kernel(Q8Params p) {
         __syncthreads();
         const int r0 = tile * 32 + warp * kQ8RowsPerWarp;
         if (UP) {
-            // per output row: its gate row and its up row, then SwiGLU
+            // two output rows at a time: their gate rows and their up rows, then SwiGLU
 #pragma unroll 1
-            for (int j = 0; j < kQ8RowsPerWarp; j++) {
-                const int r = r0 + j;
-                float g[1][kQ8Tok], u[1][kQ8Tok];
-                q8_rows<NBL, 1>(p.w[0] + (size_t)z * p.w_stride[0] + (size_t)r * (K / 2), p.s[0] + (size_t)z * p.s_stride[0] + (size_t)r * nb,
-                                K, nb, ch.n, xrow, p, lane, g);
-                q8_rows<NBL, 1>(p.w[1] + (size_t)z * p.w_stride[1] + (size_t)r * (K / 2), p.s[1] + (size_t)z * p.s_stride[1] + (size_t)r * nb,
-                                K, nb, ch.n, xrow, p, lane, u);
+            for (int j0 = 0; j0 < kQ8RowsPerWarp; j0 += 2) {
+                const int r = r0 + j0;
+                const uint8_t *g0 = p.w[0] + (size_t)z * p.w_stride[0] + (size_t)r * (K / 2);
+                const uint8_t *u0 = p.w[1] + (size_t)z * p.w_stride[1] + (size_t)r * (K / 2);
+                const uint8_t *gs = p.s[0] + (size_t)z * p.s_stride[0] + (size_t)r * nb;
+                const uint8_t *us = p.s[1] + (size_t)z * p.s_stride[1] + (size_t)r * nb;
+                const uint8_t *const wr[4] = {g0, u0, g0 + K / 2, u0 + K / 2};
+                const uint8_t *const sr[4] = {gs, us, gs + nb, us + nb};
+                float acc[4][kQ8Tok];
+                q8_rows<NBL, 4>(wr, sr, K, nb, ch.n, xrow, p, lane, acc);
 #pragma unroll
-                for (int t = 0; t < kQ8Tok; t++) {
-                    if (t >= ch.n) break;
-                    float gv = bf16r(warp_sum(g[0][t])), uv = bf16r(warp_sum(u[0][t]));
-                    if (p.swiglu_limit > 0.f) {
-                        gv = fminf(gv, p.swiglu_limit);
-                        uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
+                for (int jj = 0; jj < 2; jj++)
+#pragma unroll
+                    for (int t = 0; t < kQ8Tok; t++) {
+                        if (t >= ch.n) break;
+                        float gv = bf16r(warp_sum(acc[2 * jj][t])), uv = bf16r(warp_sum(acc[2 * jj + 1][t]));
+                        if (p.swiglu_limit > 0.f) {
+                            gv = fminf(gv, p.swiglu_limit);
+                            uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
+                        }
+                        const float hv = bf16r(gv / (1.f + expf(-gv)) * uv * wt[t]);
+                        if (lane == 0) {
+                            hs[t][warp * kQ8RowsPerWarp + j0 + jj] = hv;
+                            p.h[(size_t)dst[t] * p.I + r + jj] = f32_to_bf16_bits(hv);
+                        }
                     }
-                    const float hv = bf16r(gv / (1.f + expf(-gv)) * uv * wt[t]);
-                    if (lane == 0) {
-                        hs[t][warp * kQ8RowsPerWarp + j] = hv;
-                        p.h[(size_t)dst[t] * p.I + r] = f32_to_bf16_bits(hv);
-                    }
-                }
             }
             __syncthreads();
             // Q8 of h for the down product: the 32 rows of this item are one block; warp t: token t
@@ -179,9 +207,13 @@ __global__ void __launch_bounds__(kQ8Threads, 2) expert_q8_kernel(Q8Params p) {
 #pragma unroll 1
             for (int j0 = 0; j0 < kQ8RowsPerWarp; j0 += R) {
                 const int r = r0 + j0;
+                const uint8_t *w0 = p.w[0] + (size_t)z * p.w_stride[0] + (size_t)r * (K / 2);
+                const uint8_t *s0 = p.s[0] + (size_t)z * p.s_stride[0] + (size_t)r * nb;
+                uint8_t const *wr[R], *sr[R];
+#pragma unroll
+                for (int j = 0; j < R; j++) wr[j] = w0 + (size_t)j * (K / 2), sr[j] = s0 + (size_t)j * nb;
                 float acc[R][kQ8Tok];
-                q8_rows<NBL, R>(p.w[0] + (size_t)z * p.w_stride[0] + (size_t)r * (K / 2), p.s[0] + (size_t)z * p.s_stride[0] + (size_t)r * nb,
-                                K, nb, ch.n, xrow, p, lane, acc);
+                q8_rows<NBL, R>(wr, sr, K, nb, ch.n, xrow, p, lane, acc);
 #pragma unroll
                 for (int j = 0; j < R; j++) {
                     // lane t stores token t's output of row r + j
@@ -201,10 +233,8 @@ __global__ void __launch_bounds__(kQ8Threads, 2) expert_q8_kernel(Q8Params p) {
     }
 }
 
-template __global__ void expert_q8_kernel<true, 7, 1>(Q8Params);
-template __global__ void expert_q8_kernel<true, 8, 1>(Q8Params);
-template __global__ void expert_q8_kernel<false, 2, 4>(Q8Params);
-template __global__ void expert_q8_kernel<false, 4, 2>(Q8Params);
+template __global__ void expert_q8_kernel<true, 8, 4>(Q8Params);
+template __global__ void expert_q8_kernel<false, 4, 4>(Q8Params);
 
 }  // namespace stbl
 
@@ -213,16 +243,14 @@ namespace stbl {
 // The two launches of the Q8 routed products (chunks [n_chunks[1], n_chunks[0]) of the router's
 // table, chunks of <= 8 tokens): grid of two CTAs per SM, programmatic dependent launch.
 cudaError_t launch_q8(bool up, const Q8Params &p, int sms, cudaStream_t st) {
+    // blocks per lane: up K = hidden <= 8192 (8 x 32 blocks), down K = inter <= 4096 (4 x 32 blocks)
     const void *fn;
     if (up) {
         if (p.H > 32 * 32 * 8 || p.H % 32) return cudaErrorInvalidValue;
-        fn = p.H <= 32 * 32 * 7 ? (const void *)expert_q8_kernel<true, 7, 1> : (const void *)expert_q8_kernel<true, 8, 1>;
-    } else if (p.I <= 32 * 32 * 2) {
-        fn = (const void *)expert_q8_kernel<false, 2, 4>;
-    } else if (p.I <= 32 * 32 * 4) {
-        fn = (const void *)expert_q8_kernel<false, 4, 2>;
+        fn = (const void *)expert_q8_kernel<true, 8, 4>;
     } else {
-        return cudaErrorInvalidValue;
+        if (p.I > 32 * 32 * 4 || p.I % 32) return cudaErrorInvalidValue;
+        fn = (const void *)expert_q8_kernel<false, 4, 4>;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * sms);
