@@ -322,9 +322,12 @@ def sweep_layer(layer, cfg, token_counts, distinct_of, timed_steps, peak, seed0)
         for i in range(3):
             layer(xs2[i])
         torch.cuda.synchronize()
+        # the call time without the library's per-kernel events (an event between two chained kernels
+        # keeps the second from starting while the first drains), then the per-kernel times with them
+        ms = timed_steps(layer, xs2[3:])
         base = layer.timing()
         layer.set_timing(True)
-        ms = timed_steps(layer, xs2[3:])
+        timed_steps(layer, xs2[3:])
         layer.set_timing(False)
         k2 = layer.timing()
         n2 = max(k2["calls"] - base["calls"], 1)
@@ -425,14 +428,21 @@ def main():
     torch.cuda.synchronize()
     sampler = clock_sampler(local)
     sampler.start()
-    layer.timing()
-    layer.set_timing(True)
     step_ms = timed_steps(layer, [xs[args.warmup + i] for i in range(args.steps)])
-    layer.set_timing(False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
+    # per-kernel device times (router, up, down) from a second pass over the same steps with the
+    # library's timing events on; the headline pass above runs without them (an event between two
+    # chained kernels keeps the second from starting while the first drains)
+    layer.timing()
+    layer.set_timing(True)
+    timed_steps(layer, [xs[args.warmup + i] for i in range(args.steps)])
+    layer.set_timing(False)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     kt = layer.timing()
     distinct = [distinct_of(layer, xs[args.warmup + i]) for i in range(args.steps)]
     total_s = sum(step_ms) / 1e3
