@@ -433,10 +433,13 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     // streamed bytes: MXFP4 up 128 x 2 rows x K/2, down 128 x K/2 per tile; FP8 128 x K per tile
     const double b4 = (double)n4c * (UP ? p4.I / 128 : p4.H / 128) * (UP ? 256.0 : 128.0) * (UP ? p4.H : p4.I) / 2;
     const double b8 = (double)n8c * (UP ? p8.I / 64 : p8.H / 128) * 128.0 * (UP ? p8.H : p8.I);
+    // a CTA streams FP8 tiles about kRate8 times as fast as MXFP4 ones (measured on the full-size layer:
+    // up 5.9 against 3.2-3.4 TB/s, down 5.5 against 3.0), so the split follows bytes / rate
+    constexpr double kRate8 = 1.7;
     const int ncta = gridDim.x;
     int c8 = 0;
-    if (n8c > 0) c8 = n4c > 0 ? min(ncta - 1, max(1, (int)(ncta * b8 / (b8 + b4) + 0.5))) : ncta;
-    if ((int)blockIdx.x < c8) tc8_body<UP, !UP>(maps8, p8, nst8, blockIdx.x, c8);  // down: two-tile items
+    if (n8c > 0) c8 = n4c > 0 ? min(ncta - 1, max(1, (int)(ncta * (b8 / kRate8) / (b8 / kRate8 + b4) + 0.5))) : ncta;
+    if ((int)blockIdx.x < c8) tc8_body<UP, true>(maps8, p8, nst8, blockIdx.x, c8);  // two-tile items
     else tc4_body<UP>(maps4, p4, nst4, blockIdx.x - c8, ncta - c8);
 }
 

@@ -518,13 +518,13 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
                 cudaFuncAttributes fa{};
                 CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
                 const int room = max_smem - (int)fa.sharedSizeBytes;
-                // the FP8 body's down part takes two-tile items here (34 KB stages, 4 to 6)
-                int n4 = 6, n8 = up ? 8 : 6;
+                // the FP8 body takes two-tile items here (34 KB stages, 4 to 6)
+                int n4 = 6, n8 = 6;
                 const int n8min = 4;
                 while (n4 >= 2 && expert_tc4_smem_bytes(up, n4) > room) n4--;
-                while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, !up) > room) n8--;
+                while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, true) > room) n8--;
                 if (n4 < 2 || n8 < n8min) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8, !up));
+                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8, true));
                 CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
                 (up ? m->tc4_nst_up : m->tc4_nst_down) = n4;
                 (up ? m->tc4_nst8_up : m->tc4_nst8_down) = n8;
@@ -674,7 +674,7 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
 
 // the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range)
 void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st) {
-    TcMaps maps8 = up ? m->tc_up : m->tc_down;
+    TcMaps maps8 = up ? m->tc_up2 : m->tc_down;  // the FP8 body's two-tile items (128-row boxes)
     maps8.b = up ? m->bmap_xb : m->bmap_hq;
     TcMaps maps4 = up ? m->tc4_up : m->tc4_down;
     maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
