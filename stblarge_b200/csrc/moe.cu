@@ -653,13 +653,12 @@ void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
 
 // up items of 128 gate + 128 up rows from this many tokens on (the up kernel's two-tile form).
 // Measured on one GPU: cfg2 T=16 up 407 -> 351 us, cfg4 T=256 layer 2.29 -> 2.07 ms; at T=1 the
-// single-tile form stays (73 against 76 us).  Under expert parallelism the two-tile up form was slower
-// (2 GPUs, cfg4: up phase 0.81 -> 0.99 ms), so expert-parallel layers keep the single-tile up items;
-// their down product takes two-tile items (0.445 -> 0.422 ms).
+// single-tile form stays (73 against 76 us).  Under expert parallelism (2 GPUs, cfg4): 1.282 ->
+// 1.198 ms per step.
 constexpr int kUpTwoMinT = 4;
 
 void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
-    const bool up2 = up && p.T >= kUpTwoMinT && m->ep_n == 1;
+    const bool up2 = up && p.T >= kUpTwoMinT;
     TcMaps maps = up ? (up2 ? m->tc_up2 : m->tc_up) : m->tc_down;
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
