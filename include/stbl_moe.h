@@ -219,20 +219,24 @@ const char *stbl_cache_error(const stbl_cache *c);
 
 /* Prefetch into the cache, the reference's shadow next-layer guesses (stbl/model.cu:432-475 predict,
  * 555-586 issue, 347-373 take_slot): of the first `consider` distinct ids (device [n], guessed experts of
- * layer `layer` in priority order) the ones not cached take a never-used slot or the least recently used
- * one and become the most recent; cached ones are not touched.  Planned on `stream` (after what is queued
- * there), copied on `copy_stream`; the cache's next call waits for that copy, so the guesses have landed
- * when a layer is routed (the reference's prefetch reads that finished in time).  A slot the last call
- * used is never taken: the prefetch stops there.  Counters: experts prefetched, prefetched experts a
- * later call routed to, bytes prefetched. */
+ * layer `layer` in priority order) the ones not cached take a freed slot, a never-used one or the least
+ * recently used one and become the most recent; cached ones are not touched.  Planned on `stream` (after
+ * what is queued there), copied on `copy_stream`.  A slot the last call used is never taken: the prefetch
+ * stops there.  The cache's next call plans beside that copy (the reference's PfJob states,
+ * stbl/model.cu:92-97, 397-414, 478-494): a guess of its layer not yet claimed by the copy is cancelled
+ * when the call does not route to it (its slot is freed) and taken over when it does (the call copies
+ * it; a miss); guesses being copied or landed are hits, and the call's expert kernels wait for the copy.
+ * Landed guesses of earlier layers are forgotten (no longer counted as prefetched).  File-backed caches
+ * read whole prefetches: their next call waits for the prefetch before planning, so nothing is
+ * cancelled.  Counters: experts prefetched, prefetched experts a later call routed to (landed or being
+ * copied), bytes the prefetch copies wrote. */
 int stbl_cache_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, cudaStream_t stream,
                         cudaStream_t copy_stream);
 int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_t *used, uint64_t *bytes);
 /* The same counters in the layout of the reference's stbl_prefetch (stbl/stbl.h:23-24, printed by
  * stbl/run.py:100): out[0] guesses issued, out[1] guesses routed to after they landed, out[2] guesses
- * routed to while still being read, out[3] guesses cancelled.  A demand call here waits for the whole
- * prefetch copy before it plans, so every routed guess has landed (out[2] = 0) and none is cancelled
- * (out[3] = 0).  Waits for the device. */
+ * routed to while still being copied, out[3] guesses cancelled (guesses a call took over count as its
+ * misses, as in the reference).  Waits for the device. */
 int stbl_cache_prefetch_counters(const stbl_cache *c, uint64_t *out);
 /* Each call of layer m (attached to a cache) then also runs `next`'s router on m's input and prefetches
  * its top n_predict experts per token (first `consider` distinct ones, stbl_cache_prefetch) for `next`,

@@ -370,73 +370,119 @@ def ref_hc_post(y, res, post, comb):
 
 class LruExpertCache:
     """The reference's expert cache decisions (stbl/model.cu:99-106 ExpertCache,
-    371-393 take_slot, 397-422 expert(), 503-520 the touch order in moe()): an LRU list of (layer,
-    expert) keys, most recent first.  A call first moves its cached experts to the front in order, then
-    walks its experts in order: a hit moves to the front again, a miss takes the next never-used slot
-    (slots are used in order) or else the slot of the list's last key, and goes to the front.  A call
+    347-372 take_slot, 386-422 expert(), 478-494 the cancel pass and 503-520 the touch order in moe()):
+    an LRU list of (layer, expert) keys, most recent first.  A call first moves its cached experts to
+    the front in order, then walks its experts in order: a hit moves to the front again, a miss takes a
+    slot freed by a cancelled prefetch, else the next never-used slot (slots are used in order), else
+    the slot of the list's last key that no prefetch is still filling, and goes to the front.  A call
     with several tokens walks its distinct experts in order of first appearance (token-major, top-k
-    order), the single-token rule applied to the token batch.  Test infrastructure only."""
+    order), the single-token rule applied to the token batch.
+
+    Prefetch jobs (stbl/model.cu:92-97 PfJob) are "queued" or "landed" when a call plans (`pending`
+    says which, for all of them: the copy has not started, or it has finished).  A call cancels its own
+    layer's queued guesses it does not route to (their slots are freed), takes over the queued ones it
+    routes to (a miss, copied into the same slot) and forgets landed guesses of earlier layers.  The
+    reference's freed-slot stack is kept in ascending slot order (its cancel pass walks a hash map,
+    whose order is unspecified).  Test infrastructure only."""
 
     def __init__(self, slots):
         self.slots = slots
         self.where = {}      # (layer, expert) -> slot
         self.lru = []        # keys, most recent first
         self.next_slot = 0
+        self.free = []       # slots freed by cancelled prefetches
         self.hits = self.misses = 0
         self.last = set()    # keys of the last call (still being read while a prefetch is planned)
-        self.pf_keys = set() # prefetched keys no call has routed to yet
-        self.prefetched = self.pf_used = 0
+        self.jobs = {}       # prefetched keys no call has routed to yet -> "queued" | "landed"
+        self.prefetched = self.pf_landed = self.pf_reading = self.cancelled = self.taken = 0
+
+    @property
+    def pf_used(self):
+        return self.pf_landed + self.pf_reading
 
     def _front(self, key):
         self.lru.remove(key)
         self.lru.insert(0, key)
 
+    def _victim(self):
+        """The key take_slot would evict (the list's last key no prefetch is still filling)."""
+        for key in reversed(self.lru):
+            if self.jobs.get(key) != "queued":
+                return key
+        raise RuntimeError("every expert cache slot is being filled")
+
     def _take_slot(self):
+        if self.free:
+            s = min(self.free)
+            self.free.remove(s)
+            return s
         if self.next_slot < self.slots:
             self.next_slot += 1
             return self.next_slot - 1
-        key = self.lru.pop()
-        self.pf_keys.discard(key)
+        key = self._victim()
+        self.lru.remove(key)
+        self.jobs.pop(key, None)
         return self.where.pop(key)
 
     def prefetch(self, layer, ids, consider):
-        """The reference's prefetch issue (stbl/model.cu:555-569) when every earlier prefetch has landed
-        before the next routing: of the first `consider` distinct ids, the ones not cached take a slot
-        (take_slot: never used first, else the list's last key) and go to the front; cached ones are
-        not touched.  A slot of the last call's experts is never taken (they may still be read): the
-        prefetch stops there.  Returns the placed (slot, expert)."""
+        """The reference's prefetch issue (stbl/model.cu:555-569): of the first `consider` distinct ids,
+        the ones not cached take a slot (take_slot) and go to the front as queued jobs; cached ones are
+        not touched.  Every earlier prefetch copy has ended when a prefetch plans (its jobs that no call
+        cancelled or took over have landed).  A slot of the last call's experts is never taken (they may
+        still be read): the prefetch stops there.  Returns the placed (slot, expert)."""
+        for k in self.jobs:
+            self.jobs[k] = "landed"
         order = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))[:consider]
         placed = []
         for e in order:
             key = (layer, e)
             if key in self.where:
                 continue
-            if self.next_slot >= self.slots and self.lru[-1] in self.last:
+            if not self.free and self.next_slot >= self.slots and self._victim() in self.last:
                 break
             s = self._take_slot()
             self.where[key] = s
             self.lru.insert(0, key)
-            self.pf_keys.add(key)
+            self.jobs[key] = "queued"
             self.prefetched += 1
             placed.append((s, e))
         return placed
 
-    def call(self, layer, ids):
-        """ids: the call's routed expert ids, token-major.  Returns the misses as (slot, expert) in
-        the order they were placed."""
+    def call(self, layer, ids, pending="landed"):
+        """ids: the call's routed expert ids, token-major.  pending: the state of the prefetch jobs when
+        the call plans, "landed" (copied) or "queued" (not started).  Returns the copies of the call
+        as (slot, expert): guesses taken over, then misses, each in order."""
+        assert pending in ("landed", "queued")
         order = list(dict.fromkeys(int(e) for e in np.asarray(ids).reshape(-1)))
+        if pending == "landed":
+            for k in self.jobs:
+                self.jobs[k] = "landed"
+        routed = set(order)
+        for key, st in list(self.jobs.items()):
+            if key[0] == layer and key[1] not in routed and st == "queued":
+                self.free.append(self.where.pop(key))
+                self.lru.remove(key)
+                del self.jobs[key]
+                self.cancelled += 1
+            elif key[0] < layer and st == "landed":
+                del self.jobs[key]
         for e in order:
             if (layer, e) in self.where:
                 self._front((layer, e))
-        placed = []
+        taken, placed = [], []
         for e in order:
             key = (layer, e)
             if key in self.where:
                 self._front(key)
+                st = self.jobs.pop(key, None)
+                if st == "queued":
+                    self.misses += 1
+                    self.taken += 1
+                    taken.append((self.where[key], e))
+                    continue
                 self.hits += 1
-                if key in self.pf_keys:
-                    self.pf_keys.discard(key)
-                    self.pf_used += 1
+                if st == "landed":
+                    self.pf_landed += 1
             else:
                 self.misses += 1
                 s = self._take_slot()
@@ -444,7 +490,7 @@ class LruExpertCache:
                 self.lru.insert(0, key)
                 placed.append((s, e))
         self.last = {(layer, e) for e in order}
-        return placed
+        return taken + placed
 
     def state(self, n_layers, n_experts):
         """(map [n_layers][n_experts] slot or -1, owner [slots] layer * n_experts + expert or -1)"""

@@ -100,15 +100,16 @@ class ExpertCache:
         return {"hits": h.value, "misses": m.value, "bytes": b.value}
 
     def prefetch_stats(self):
-        """Experts prefetched, prefetched experts a later call routed to, bytes prefetched."""
+        """Experts prefetched, prefetched experts a later call routed to (landed or being copied), bytes
+        the prefetch copies wrote (cancelled and taken-over guesses are not copied by them)."""
         p, u, b = L.U64(), L.U64(), L.U64()
         if self.lib.stbl_cache_prefetch_stats(self.handle, ctypes.byref(p), ctypes.byref(u), ctypes.byref(b)) != 0:
             raise RuntimeError("stbl_cache_prefetch_stats failed")
         return {"prefetched": p.value, "used": u.value, "bytes": b.value}
 
     def prefetch_counters(self):
-        """The reference's stbl_prefetch layout: issued, routed after landing, routed while reading,
-        cancelled."""
+        """The reference's stbl_prefetch layout: issued, routed after landing, routed while being
+        copied, cancelled."""
         out = (L.U64 * 4)()
         if self.lib.stbl_cache_prefetch_counters(self.handle, out) != 0:
             raise RuntimeError("stbl_cache_prefetch_counters failed")

@@ -14,12 +14,19 @@
 //
 // Prefetch (the reference's shadow next-layer guesses, stbl/model.cu:432-475, 555-586): the planner's
 // second mode places guessed experts of a coming layer call without touching cached ones (its
-// issue(), each new guess takes a never-used slot or the least recently used one and goes to the
-// front), and the copy runs on a second stream, beside the current call's expert kernels (the copy
-// kernel keeps no shared memory and few registers, so its CTAs fit next to theirs).  A prefetch never
-// takes a slot the last demand call used (those experts may still be read), and the next demand call
-// waits for the prefetch copy before planning: the guesses have always landed by then, which is the
-// reference's case of reads that finished in time (it also cancels guesses not yet started).
+// issue(), each new guess takes a freed slot, a never-used one or the least recently used one and goes
+// to the front), and the copy runs on a second stream, beside the current call's expert kernels (the
+// copy kernel keeps no shared memory and few registers, so its CTAs fit next to theirs).  A prefetch
+// never takes a slot the last demand call used (those experts may still be read).
+// Cancellation (the reference's PfJob states, stbl/model.cu:92-97, 319-345, 397-414, 478-494): each
+// prefetched slot carries a claim word in device memory, queued -> copying -> landed.  The copy kernel
+// claims a job (queued -> copying) before it writes any of its bytes and marks it landed after the last
+// one; the next demand planner runs without waiting for that copy and, for the guesses of its own layer
+// still queued, cancels the ones it did not route to (the slot is freed and taken first by later
+// misses) and takes over the ones it did (queued -> its own copy job, counted as a miss).  Guesses it
+// routes to that are being copied or have landed are hits; the call's expert kernels wait for the
+// prefetch copy.  Victims skip slots still queued or being copied.  Claims are atomic, so a job is
+// either copied whole by the prefetch or not touched by it.
 //
 // File-backed store (stbl_cache_create_file; the reference's expert tensors kept as file offsets and
 // read on a miss, stbl/model.cu:269-308, 940-949, 978-987): the planner writes its jobs into mapped
@@ -68,10 +75,13 @@ struct CachePlanParams {
     int *n_jobs;
     long long expert_bytes;
     uint32_t *status;
-    // prefetch mode: consider the first `consider` distinct ids; pf_flag [S]: filled by a prefetch and
-    // not yet routed to (counted as used at its first hit)
+    // prefetch mode: consider the first `consider` distinct ids; pf_flag [S]: 1 = filled by a prefetch
+    // and not yet routed to (counted at its first hit), 2 = freed by a cancelled prefetch
     int prefetch, consider;
     unsigned char *pf_flag;
+    // claim words [S] (kPfLanded / kPfQueued / kPfCopying) and landed work items [S] of the prefetch
+    // jobs; null for file-backed stores, whose demand calls wait for the prefetch before planning
+    unsigned int *pf_state, *pf_items;
     // file-backed store: slots whose read failed (mapped host memory written by the read step) and a
     // flag that any are marked; null otherwise
     unsigned char *bad;
@@ -91,7 +101,14 @@ struct CacheCopyParams {
     // (per 128 rows x 128 K a 512-byte block, byte l*16 + c*4 + j = scale of row 32c + l, 32-block j)
     int blocked;
     int rows[3], K[3];
+    // prefetch copies: the jobs' claim words and landed-item counters (cache_plan_kernel); null for
+    // demand copies, which own their slots
+    unsigned int *state, *items;
 };
+
+// prefetch job claim words (the reference's PfJob::state 0 queued, 1 reading, 2 landed; cancelled and
+// taken-on-demand jobs go straight back to kPfLanded, the word of a slot with no job in flight)
+constexpr unsigned int kPfLanded = 0, kPfQueued = 1, kPfCopying = 2;
 
 __device__ __forceinline__ unsigned long long min_u64_warp(unsigned long long v) {
 #pragma unroll
@@ -104,7 +121,7 @@ __device__ __forceinline__ unsigned long long min_u64_warp(unsigned long long v)
 
 // One CTA.  Keys pack (last use, slot): the smallest key is the least recently used slot, ties (never
 // used, clock 0) to the lower slot - the reference's sequential fill of fresh slots.
-__global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParams p) {
+__global__ void __launch_bounds__(kPlanThreads, 1) cache_plan_kernel(CachePlanParams p) {
     extern __shared__ int sm[];
     int *first = sm;                 // [E] first position of each expert in the call
     int *ulist = first + p.E;        // [n] distinct experts in order of first appearance
@@ -177,32 +194,80 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
     const int nu = s_nu;
     const unsigned long long base = p.ctr[0];
     int *row = p.map + (size_t)p.layer * p.E;
+    __shared__ int s_taken;
+    if (tid == 0) s_taken = 0;
+    // demand mode, before anything is touched (stbl/model.cu:478-494): guesses of this layer still
+    // queued and not routed to are cancelled (their slots freed); landed guesses of earlier layers are
+    // forgotten (a later hit on them is a plain hit)
+    int cancelled = 0;
+    if (!p.prefetch) {
+        for (int s = tid; s < p.S; s += kPlanThreads) {
+            if (p.pf_flag[s] != 1) continue;
+            const int key = p.owner[s], l = key / p.E, e = key - l * p.E;
+            if (l == p.layer && first[e] == INT_MAX) {
+                if (p.pf_state && atomicCAS(p.pf_state + s, kPfQueued, kPfLanded) == kPfQueued) {
+                    row[e] = -1;
+                    p.owner[s] = -1, p.ts[s] = 0, p.pf_flag[s] = 2;
+                    cancelled++;
+                }
+            } else if (l < p.layer && (!p.pf_state || atomicAdd(p.pf_state + s, 0) == kPfLanded)) {
+                p.pf_flag[s] = 0;
+            }
+        }
+    }
+    __syncthreads();
     // the call's cached experts are touched first (in order), so no miss of this call evicts one;
-    // then each hit is touched again in order (the reference moves it to the front twice)
+    // then each hit is touched again in order (the reference moves it to the front twice).  A guess
+    // still queued is taken over (stbl/model.cu:404-408): its slot gets this call's copy, a miss.
     // prefetch mode: cached guesses are not touched, and only the first `consider` guesses count
     const int nw = p.prefetch ? min(nu, p.consider) : nu;
     const unsigned long long guard = p.prefetch ? p.ctr[4] : base;  // slots with a later use are off limits
-    int hits = 0, used = 0;
+    int hits = 0, landed = 0, reading = 0;
     for (int i = tid; i < nu && !p.prefetch; i += kPlanThreads) {
-        const int s = row[ulist[i]];
-        if (s >= 0) {
-            p.ts[s] = base + 1 + nu + i, hits++;
-            if (p.pf_flag[s]) p.pf_flag[s] = 0, used++;
+        const int e = ulist[i], s = row[e];
+        if (s < 0) continue;
+        p.ts[s] = base + 1 + nu + i;
+        if (p.pf_flag[s] != 1) {
+            hits++;
+            continue;
+        }
+        p.pf_flag[s] = 0;
+        const unsigned int st = p.pf_state ? atomicCAS(p.pf_state + s, kPfQueued, kPfLanded) : kPfLanded;
+        if (st == kPfQueued) {
+            p.jobs[atomicAdd(&s_taken, 1)] = make_int2(s, p.layer * p.E + e);
+        } else {
+            hits++;
+            if (st == kPfCopying) reading++;
+            else landed++;
         }
     }
-    // misses, in order: each takes the least recently used slot (every slot this call touched is newer)
-    for (int o = 16; o > 0; o >>= 1) hits += __shfl_xor_sync(0xffffffffu, hits, o), used += __shfl_xor_sync(0xffffffffu, used, o);
-    if (lane == 0) wsum[warp] = hits | (used << 16);
+    for (int o = 16; o > 0; o >>= 1) {
+        hits += __shfl_xor_sync(0xffffffffu, hits, o), landed += __shfl_xor_sync(0xffffffffu, landed, o);
+        reading += __shfl_xor_sync(0xffffffffu, reading, o), cancelled += __shfl_xor_sync(0xffffffffu, cancelled, o);
+    }
+    if (lane == 0) wsum[warp] = hits | (landed << 16), wmin[warp] = (unsigned long long)reading | ((unsigned long long)cancelled << 32);
     __syncthreads();
-    int n_hits = 0, n_used = 0;
-    for (int w = 0; w < kPlanThreads / 32; w++) n_hits += wsum[w] & 0xFFFF, n_used += wsum[w] >> 16;
-    int j = 0;
+    int n_hits = 0, n_landed = 0, n_reading = 0, n_cancelled = 0;
+    for (int w = 0; w < kPlanThreads / 32; w++) {
+        n_hits += wsum[w] & 0xFFFF, n_landed += wsum[w] >> 16;
+        n_reading += (int)(wmin[w] & 0xFFFFFFFFu), n_cancelled += (int)(wmin[w] >> 32);
+    }
+    const int n_taken = s_taken;
+    __syncthreads();  // wsum / wmin are reused below
+    // misses, in order: each takes a freed slot, else a never-used one (in slot order), else the least
+    // recently used one (every slot this call touched is newer); slots a prefetch is still filling are
+    // skipped (stbl/model.cu:347-372).  Key = (class, slot): freed 0, never used 1, else last use + 1.
+    int j = n_taken;
     for (int i = 0; i < nw; i++) {
         const int e = ulist[i];
         if (row[e] >= 0) continue;  // uniform: row[] changes only below, after a barrier
         unsigned long long best = ~0ull;
         for (int s = tid; s < p.S; s += kPlanThreads) {
-            const unsigned long long k = (p.ts[s] << 20) | (unsigned long long)s;
+            const unsigned char fl = p.pf_flag[s];
+            unsigned long long k;
+            if (fl == 1 && p.pf_state && atomicAdd(p.pf_state + s, 0) != kPfLanded) k = ~0ull;
+            else if (fl == 2) k = (unsigned long long)s;
+            else k = ((p.ts[s] + 1) << 20) | (unsigned long long)s;
             best = k < best ? k : best;
         }
         best = min_u64_warp(best);
@@ -213,8 +278,8 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
             v = min_u64_warp(v);
             if (lane == 0) {
                 const int s = (int)(v & 0xFFFFF);
-                if ((v >> 20) > guard) {
-                    // demand: every slot is in use by this call, too few slots (checked at attach);
+                if ((v >> 20) > guard + 1) {
+                    // demand: every slot is in use by this call or being filled (too few slots);
                     // prefetch: the rest would evict experts of the last call: the prefetch stops
                     s_bad = p.prefetch ? 2 : 1;
                 } else {
@@ -224,6 +289,7 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
                     row[e] = s;
                     p.ts[s] = p.prefetch ? base + 1 + i : base + 1 + nu + i;
                     p.pf_flag[s] = p.prefetch ? 1 : 0;
+                    if (p.prefetch && p.pf_state) p.pf_state[s] = kPfQueued, p.pf_items[s] = 0;
                     p.jobs[j] = make_int2(s, p.layer * p.E + e);
                 }
             }
@@ -243,16 +309,24 @@ __global__ void __launch_bounds__(kPlanThreads) cache_plan_kernel(CachePlanParam
             p.ctr[2] += j;
             p.ctr[3] += (unsigned long long)j * p.expert_bytes;
             p.ctr[4] = base;
-            p.ctr[6] += n_used;
+            p.ctr[6] += n_landed;
+            // jobs the prefetch copy will not write: bytes prefetched counts what it copied
+            p.ctr[7] -= (unsigned long long)(n_cancelled + n_taken) * p.expert_bytes;
+            p.ctr[8] += n_reading;
+            p.ctr[9] += n_cancelled;
+            p.ctr[10] += n_taken;
         }
         *p.n_jobs = j;
         if (s_bad == 1) atomicOr(p.status, kErrBadTable);
     }
 }
 
+// A prefetch job's item claims it first (queued -> copying; a job already copying goes on, a cancelled
+// or taken-over one is skipped); the item that completes the job marks it landed.
 __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParams p) {
     pdl_wait();
     pdl_launch_dependents();
+    __shared__ unsigned int s_go;
     const int nj = *(volatile const int *)p.n_jobs;
     int per_job = 0;
 #pragma unroll
@@ -263,6 +337,15 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
         int r = (int)(it % per_job), q = 0;
         while (q < 5 && r >= p.chunks[q]) r -= p.chunks[q++];
         const int2 job = p.jobs[jb];
+        if (p.state) {
+            __syncthreads();  // s_go of the previous item has been read
+            if (threadIdx.x == 0) {
+                const unsigned int st = atomicCAS(p.state + job.x, kPfQueued, kPfCopying);
+                s_go = st == kPfQueued || st == kPfCopying;
+            }
+            __syncthreads();
+            if (!s_go) continue;
+        }
         if (p.blocked && q >= 3) {
             // natural [rows][K/32] scales into their blocks, without shared memory: item r = (128-row
             // tile r / 4, group of 8 row groups l); warp w takes row group l = 8 (r % 4) + w, i.e. rows
@@ -282,24 +365,32 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
                 for (int b = 0; b < 4; b++)
                     *reinterpret_cast<uint4 *>(dst + (size_t)(4 * jc + b) * 512 + l * 16) = make_uint4(w0[b], w1[b], w2[b], w3[b]);
             }
-            continue;
-        }
-        const long long off = (long long)r * kCopyChunk;
-        const long long bytes = min((long long)kCopyChunk, p.piece_bytes[q] - off);
-        const long long hrow = (long long)job.y % p.host_rows;
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + off);
-        uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + off);
-        const int words = (int)(bytes >> 4);
-        uint4 v[kCopyUnroll];
+        } else {
+            const long long off = (long long)r * kCopyChunk;
+            const long long bytes = min((long long)kCopyChunk, p.piece_bytes[q] - off);
+            const long long hrow = (long long)job.y % p.host_rows;
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + off);
+            uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + off);
+            const int words = (int)(bytes >> 4);
+            uint4 v[kCopyUnroll];
 #pragma unroll
-        for (int u = 0; u < kCopyUnroll; u++) {
-            const int w = threadIdx.x + u * kCopyThreads;
-            if (w < words) v[u] = src[w];
-        }
+            for (int u = 0; u < kCopyUnroll; u++) {
+                const int w = threadIdx.x + u * kCopyThreads;
+                if (w < words) v[u] = src[w];
+            }
 #pragma unroll
-        for (int u = 0; u < kCopyUnroll; u++) {
-            const int w = threadIdx.x + u * kCopyThreads;
-            if (w < words) dst[w] = v[u];
+            for (int u = 0; u < kCopyUnroll; u++) {
+                const int w = threadIdx.x + u * kCopyThreads;
+                if (w < words) dst[w] = v[u];
+            }
+        }
+        if (p.state) {
+            __threadfence();  // this item's bytes before the count that may mark the job landed
+            __syncthreads();
+            if (threadIdx.x == 0 && atomicAdd(p.items + job.x, 1u) == (unsigned int)per_job - 1) {
+                __threadfence();
+                atomicExch(p.state + job.x, kPfLanded);
+            }
         }
     }
 }
@@ -577,9 +668,10 @@ void launch_pdl_k(const void *fn, dim3 grid, dim3 block, void **args, size_t sme
 }
 
 // the copy of the jobs a planner wrote (jobs / n_jobs), on stream st
-void launch_copy(stbl_cache *c, const int2 *jobs, const int *n_jobs, cudaStream_t st, bool pdl) {
+void launch_copy(stbl_cache *c, const int2 *jobs, const int *n_jobs, cudaStream_t st, bool pdl, bool prefetch) {
     CacheCopyParams cp{};
     cp.jobs = jobs, cp.n_jobs = n_jobs, cp.pool = c->pool, cp.slot_bytes = c->slot_bytes;
+    if (prefetch) cp.state = c->pf_state, cp.items = c->pf_items;
     cp.host_rows = c->host_rows;
     cp.blocked = c->fmt == STBL_FMT_MXFP4;
     const int rows[3] = {c->I, c->I, c->H}, ks[3] = {c->H, c->H, c->I};
@@ -602,14 +694,21 @@ void launch_copy(stbl_cache *c, const int2 *jobs, const int *n_jobs, cudaStream_
 
 void launch_cache(stbl_cache *c, int layer, const int *idx, int n, uint32_t *status, cudaStream_t st) {
     if (n < 1 || n > kPlanMaxIds) throw std::runtime_error("routed ids per call out of range for the cache planner");
-    // a prefetch copy still running may be filling slots this call reads or evicts
-    if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
+    // host store: the planner runs beside a prefetch copy still in flight (claim words decide which of
+    // its jobs it cancels or takes over) and the call's expert kernels, enqueued after this, wait for
+    // that copy; file-backed store (no claims): the planner waits for the prefetch's reads and copy
+    if (c->pf_pending && c->file) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
     CachePlanParams pp{idx, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->jobs, c->n_jobs, c->expert_bytes, status,
-                       0, 0, c->pf_flag, c->file ? c->file->bad_d : nullptr, c->file ? c->file->n_bad_d : nullptr};
+                       0, 0, c->pf_flag, c->pf_state, c->pf_items, c->file ? c->file->bad_d : nullptr,
+                       c->file ? c->file->n_bad_d : nullptr};
     void *a1[] = {&pp};
     launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
-    if (c->file) launch_file_rounds(c, 0, std::min(n, c->S), status, st);
-    else launch_copy(c, c->jobs, c->n_jobs, st, true);
+    if (c->file) {
+        launch_file_rounds(c, 0, std::min(n, c->S), status, st);
+    } else {
+        launch_copy(c, c->jobs, c->n_jobs, st, true, false);
+        if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
+    }
 }
 
 void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consider, uint32_t *status, cudaStream_t st,
@@ -618,13 +717,14 @@ void launch_prefetch(stbl_cache *c, int layer, const int *ids, int n, int consid
     // the previous prefetch's jobs list and slots are reused: its copy must be done
     if (c->pf_pending) CK(cudaStreamWaitEvent(st, c->pf_done, 0));
     CachePlanParams pp{ids, n, layer, c->E, c->S, c->map, c->owner, c->ts, c->ctr, c->pf_jobs, c->pf_n_jobs, c->expert_bytes,
-                       status, 1, consider, c->pf_flag, c->file ? c->file->bad_d : nullptr, c->file ? c->file->n_bad_d : nullptr};
+                       status, 1, consider, c->pf_flag, c->pf_state, c->pf_items, c->file ? c->file->bad_d : nullptr,
+                       c->file ? c->file->n_bad_d : nullptr};
     void *a1[] = {&pp};
     launch_pdl_k((const void *)cache_plan_kernel, dim3(1), dim3(kPlanThreads), a1, sizeof(int) * (c->E + n), st);
     CK(cudaEventRecord(c->pf_planned, st));
     CK(cudaStreamWaitEvent(copy_st, c->pf_planned, 0));
     if (c->file) launch_file_rounds(c, 1, std::min({n, consider, c->S}), status, copy_st);
-    else launch_copy(c, c->pf_jobs, c->pf_n_jobs, copy_st, false);
+    else launch_copy(c, c->pf_jobs, c->pf_n_jobs, copy_st, false, true);
     CK(cudaEventRecord(c->pf_done, copy_st));
     c->pf_pending = true;
 }
@@ -790,8 +890,8 @@ static stbl_cache *cache_new(const stbl_cache_desc *d, const stbl_cache_file_des
         CK(cudaMemset(c->owner, 0xFF, sizeof(int) * c->S));
         CK(cudaMalloc(&c->ts, sizeof(unsigned long long) * c->S));
         CK(cudaMemset(c->ts, 0, sizeof(unsigned long long) * c->S));
-        CK(cudaMalloc(&c->ctr, sizeof(unsigned long long) * 8));
-        CK(cudaMemset(c->ctr, 0, sizeof(unsigned long long) * 8));
+        CK(cudaMalloc(&c->ctr, sizeof(unsigned long long) * kCtrWords));
+        CK(cudaMemset(c->ctr, 0, sizeof(unsigned long long) * kCtrWords));
         if (f) {
             file_store_new(c, f);
         } else {
@@ -801,6 +901,10 @@ static stbl_cache *cache_new(const stbl_cache_desc *d, const stbl_cache_file_des
             CK(cudaMalloc(&c->pf_jobs, sizeof(int2) * c->S));
             CK(cudaMalloc(&c->pf_n_jobs, sizeof(int)));
             CK(cudaMemset(c->pf_n_jobs, 0, sizeof(int)));
+            CK(cudaMalloc(&c->pf_state, sizeof(unsigned int) * c->S));
+            CK(cudaMemset(c->pf_state, 0, sizeof(unsigned int) * c->S));
+            CK(cudaMalloc(&c->pf_items, sizeof(unsigned int) * c->S));
+            CK(cudaMemset(c->pf_items, 0, sizeof(unsigned int) * c->S));
         }
         CK(cudaMalloc(&c->pf_flag, c->S));
         CK(cudaMemset(c->pf_flag, 0, c->S));
@@ -896,19 +1000,19 @@ int stbl_cache_stats(const stbl_cache *c, uint64_t *hits, uint64_t *misses, uint
 
 int stbl_cache_prefetch_stats(const stbl_cache *c, uint64_t *prefetched, uint64_t *used, uint64_t *bytes) {
     if (!c) return -1;
-    unsigned long long v[8];
+    unsigned long long v[kCtrWords];
     if (cudaMemcpy(v, c->ctr, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
     if (prefetched) *prefetched = v[5];
-    if (used) *used = v[6];
+    if (used) *used = v[6] + v[8];
     if (bytes) *bytes = v[7];
     return 0;
 }
 
 int stbl_cache_prefetch_counters(const stbl_cache *c, uint64_t *out) {
-    if (!out) return -1;
-    uint64_t issued = 0, used = 0;
-    if (stbl_cache_prefetch_stats(c, &issued, &used, nullptr) != 0) return -1;
-    out[0] = issued, out[1] = used, out[2] = 0, out[3] = 0;
+    if (!c || !out) return -1;
+    unsigned long long v[kCtrWords];
+    if (cudaMemcpy(v, c->ctr, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    out[0] = v[5], out[1] = v[6], out[2] = v[8], out[3] = v[9];
     return 0;
 }
 
@@ -947,6 +1051,8 @@ void stbl_cache_destroy(stbl_cache *c) {
     cudaFree(c->pf_jobs);
     cudaFree(c->pf_n_jobs);
     cudaFree(c->pf_flag);
+    cudaFree(c->pf_state);
+    cudaFree(c->pf_items);
     cudaFree(c->status);
     if (c->pf_done) cudaEventDestroy(c->pf_done);
     if (c->pf_planned) cudaEventDestroy(c->pf_planned);

@@ -8,6 +8,7 @@
 
 namespace stbl {
 struct FileStore;
+constexpr int kCtrWords = 16;  // stbl_cache::ctr
 }
 
 struct stbl_cache {
@@ -23,16 +24,19 @@ struct stbl_cache {
     int *owner = nullptr;             // [S] l * E + e held by the slot, -1 when free
     unsigned long long *ts = nullptr; // [S] last use (a logical clock), 0 never used
     // [0] clock, [1] hits, [2] misses, [3] bytes copied, [4] clock before the last demand call,
-    // [5] experts prefetched, [6] prefetched experts routed to later, [7] bytes prefetched
+    // [5] experts prefetched (issued), [6] prefetched experts routed to after they landed, [7] bytes the
+    // prefetch copies wrote, [8] prefetched experts routed to while being copied, [9] prefetches
+    // cancelled, [10] prefetches taken over by a demand call (copied by it, counted as misses)
     unsigned long long *ctr = nullptr;
     int2 *jobs = nullptr;             // [S] (slot, l * E + e) to fill in the current call
     int *n_jobs = nullptr;
     int copy_ctas = 0;
     // prefetch (stbl_cache_prefetch): its own jobs list, per-slot "prefetched, not yet routed to"
-    // flags, the event after its copy (the next planner waits for it) and status bits
+    // flags, the event after its copy (the next call's expert kernels wait for it) and status bits
     int2 *pf_jobs = nullptr;
     int *pf_n_jobs = nullptr;
     unsigned char *pf_flag = nullptr;
+    unsigned int *pf_state = nullptr, *pf_items = nullptr;  // host store: claim words, landed items [S]
     cudaEvent_t pf_done = nullptr, pf_planned = nullptr;
     bool pf_pending = false;
     uint32_t *status = nullptr;

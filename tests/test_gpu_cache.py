@@ -6,6 +6,10 @@ which expert, hits, misses) must equal the reference's LRU bookkeeping restated 
 (oracle.LruExpertCache, stbl/model.cu:347-422, 503-520) after every call.  Forced routes are checked
 against the oracle layer with the same routes."""
 
+import ctypes
+import threading
+import time
+
 import numpy as np
 import pytest
 import torch
@@ -173,8 +177,121 @@ def test_shadow_prefetch_matches_resident_layers_and_reference_lru(cfg, S):
             assert (st["hits"], st["misses"]) == (lru.hits, lru.misses)
             assert (pf["prefetched"], pf["used"]) == (lru.prefetched, lru.pf_used)
     assert lru.prefetched > 0 and lru.pf_used > 0
-    assert cache.prefetch_counters() == [lru.prefetched, lru.pf_used, 0, 0]
+    # every call plans after the prefetch copy has landed: nothing is read late or cancelled
+    assert cache.prefetch_counters() == [lru.prefetched, lru.pf_landed, 0, 0]
     for layer in cached + plain:
         assert layer.status() == 0
         layer.close()
     cache.close()
+
+
+def _cu():
+    cu = ctypes.CDLL("libcuda.so.1")
+    cu.cuLaunchHostFunc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    cu.cuStreamCreate.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_uint]
+    cu.cuStreamDestroy_v2.argtypes = [ctypes.c_void_p]
+    return cu
+
+
+def _nonblocking_stream():
+    """A stream that does not synchronise with the legacy default stream (CU_STREAM_NON_BLOCKING), so
+    the cache's counters can be read with cudaMemcpy while work on it waits."""
+    h = ctypes.c_void_p()
+    assert _cu().cuStreamCreate(ctypes.byref(h), 1) == 0
+    return torch.cuda.ExternalStream(h.value), h
+
+
+class _StreamGate:
+    """Holds a stream at a host function until open() is called (or 60 s pass): the work queued on
+    the stream behind it does not start before then."""
+    _CB = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
+
+    def __init__(self, stream):
+        self._ev = threading.Event()
+        self._cb = self._CB(lambda _: self._ev.wait(60))
+        assert _cu().cuLaunchHostFunc(ctypes.c_void_p(stream.cuda_stream), ctypes.cast(self._cb, ctypes.c_void_p), None) == 0
+
+    def open(self):
+        self._ev.set()
+
+
+@pytest.mark.parametrize("cfg", [CFG1, CFG1_FP4], ids=["fp8", "mxfp4"])
+def test_prefetch_cancelled_and_taken_over_before_its_copy_starts(cfg):
+    # the reference's cancellation (stbl/model.cu:397-414, 478-494): a call that plans before the
+    # prefetch copy for its layer has started cancels the guesses it does not route to and takes over
+    # the ones it does.  The copy stream is held by a host function until the call's planner has run
+    # (its hit/miss counts moved); every third step lets the copy land first.  Routes are forced, one
+    # token routed to one guess of the prefetch, so both cases occur; outputs must equal resident layers,
+    # decisions and counters the reference's bookkeeping (oracle.LruExpertCache with the job states).
+    L, S, T, E, K, n_predict, consider = 3, 12, 2, cfg.n_experts, cfg.topk, 4, 4
+    torch.cuda.init()
+    store = host_store(cfg, L)
+    cache = ExpertCache(cfg, L, S, store)
+    resident = [synth.device_layer(cfg, seed_base=1000 + l * E) for l in range(L)]
+    plain = [MoELayer(cfg, resident[l], max_tokens=T) for l in range(L)]
+    cached = [MoELayer(cfg, resident[l], max_tokens=T, cache=(cache, l)) for l in range(L)]
+    main, hm = _nonblocking_stream()
+    side, hs = _nonblocking_stream()
+    for l in range(L - 1):
+        cached[l].attach_prefetch(cached[l + 1], n_predict, consider, side)
+    lru = O.LruExpertCache(S)
+    rng = np.random.default_rng(5)
+    gates = []
+    try:
+        with torch.cuda.stream(main):
+            for step in range(6):
+                gated = step % 3 != 2
+                placed, held = [], None
+                for l in range(L):
+                    x_bits = synth.make_x(cfg.hidden, T, seed=1200 + 10 * step + l)
+                    guessed = [e for _, e in placed]
+                    keep = guessed[:1]
+                    others = [int(e) for e in rng.permutation(E) if e not in guessed]
+                    rows = np.array([keep + others[:K - len(keep)], others[K - len(keep):2 * K - len(keep)]], np.int32)
+                    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+                    idx = torch.from_numpy(rows).cuda()
+                    y_plain = plain[l].forward_routed(x, idx)
+                    nxt = _StreamGate(side) if gated and l + 1 < L else None  # holds this call's prefetch copy
+                    if nxt is not None:
+                        gates.append(nxt)
+                    st0 = cache.stats()
+                    y = cached[l].forward_routed(x, idx)
+                    if held is not None:
+                        t0 = time.time()
+                        while sum(cache.stats()[k] for k in ("hits", "misses")) == st0["hits"] + st0["misses"]:
+                            assert time.time() - t0 < 30, "the call's planner did not run"
+                            time.sleep(0.002)
+                        held.open()
+                    main.synchronize()
+                    if nxt is None:
+                        torch.cuda.synchronize()  # the prefetch copy (if any) lands before the next call
+                    assert torch.equal(y.view(torch.int16), y_plain.view(torch.int16)), f"step {step} layer {l}"
+                    lru.call(l, rows, pending="queued" if held is not None else "landed")
+                    held, placed = nxt, []
+                    if l + 1 < L:
+                        nw = resident[l + 1]
+                        lg = O.router_logits(nw["router_w"].cpu().numpy(), x_bits)
+                        _, guess, _ = O.router_select(lg, nw["router_bias"].cpu().numpy(), n_predict, cfg.n_groups,
+                                                      cfg.topk_groups, cfg.score_fn, cfg.route_scale)
+                        placed = lru.prefetch(l + 1, guess, consider)
+                    mp, owner = cache.state()
+                    emp, eowner = lru.state(L, E)
+                    assert np.array_equal(mp, emp), f"step {step} layer {l}: residency map differs"
+                    assert np.array_equal(owner, eowner), f"step {step} layer {l}: slot owners differ"
+                    st = cache.stats()
+                    assert (st["hits"], st["misses"]) == (lru.hits, lru.misses), f"step {step} layer {l}"
+                    assert cache.prefetch_counters() == [lru.prefetched, lru.pf_landed, 0, lru.cancelled]
+        torch.cuda.synchronize()
+    finally:
+        for g in gates:
+            g.open()
+    assert lru.cancelled > 0 and lru.taken > 0 and lru.pf_landed > 0
+    st, pf = cache.stats(), cache.prefetch_stats()
+    # bytes: the demand copies (misses, taken-over guesses included) and the prefetch copies that ran
+    assert pf["bytes"] * lru.misses == st["bytes"] * (lru.prefetched - lru.cancelled - lru.taken)
+    for layer in cached + plain:
+        assert layer.status() == 0
+        layer.close()
+    cache.close()
+    _cu().cuStreamDestroy_v2(hm)
+    _cu().cuStreamDestroy_v2(hs)
