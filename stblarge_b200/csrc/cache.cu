@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) cache_plan_kernel(CachePlanPa
 
 // A prefetch job's item claims it first (queued -> copying; a job already copying goes on, a cancelled
 // or taken-over one is skipped); the item that completes the job marks it landed.
-__global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParams p) {
+__global__ void __launch_bounds__(kCopyThreads, 4) cache_copy_kernel(const __grid_constant__ CacheCopyParams p) {
     pdl_wait();
     pdl_launch_dependents();
     __shared__ unsigned int s_go;
@@ -372,16 +372,21 @@ __global__ void __launch_bounds__(kCopyThreads) cache_copy_kernel(CacheCopyParam
             const uint4 *src = reinterpret_cast<const uint4 *>(p.host[q] + (size_t)hrow * p.host_stride[q] + off);
             uint4 *dst = reinterpret_cast<uint4 *>(p.pool + (size_t)job.x * p.slot_bytes + p.piece_off[q] + off);
             const int words = (int)(bytes >> 4);
-            uint4 v[kCopyUnroll];
+            // two halves of 16 KB per CTA in flight: the kernel stays within 64 registers, so a CTA of it
+            // fits beside an expert kernel's CTA on the same SM
+#pragma unroll 1
+            for (int h = 0; h < 2; h++) {
+                uint4 v[kCopyUnroll / 2];
 #pragma unroll
-            for (int u = 0; u < kCopyUnroll; u++) {
-                const int w = threadIdx.x + u * kCopyThreads;
-                if (w < words) v[u] = src[w];
-            }
+                for (int u = 0; u < kCopyUnroll / 2; u++) {
+                    const int w = threadIdx.x + (h * kCopyUnroll / 2 + u) * kCopyThreads;
+                    if (w < words) v[u] = src[w];
+                }
 #pragma unroll
-            for (int u = 0; u < kCopyUnroll; u++) {
-                const int w = threadIdx.x + u * kCopyThreads;
-                if (w < words) dst[w] = v[u];
+                for (int u = 0; u < kCopyUnroll / 2; u++) {
+                    const int w = threadIdx.x + (h * kCopyUnroll / 2 + u) * kCopyThreads;
+                    if (w < words) dst[w] = v[u];
+                }
             }
         }
         if (p.state) {
@@ -685,10 +690,14 @@ void launch_copy(stbl_cache *c, const int2 *jobs, const int *n_jobs, cudaStream_
         }
     }
     void *a2[] = {&cp};
+    // a demand copy has the GPU to itself (the call's expert kernels wait for it): two CTAs per SM; a
+    // prefetch copy runs beside the expert kernels, whose persistent CTAs leave room on each SM for
+    // one CTA of it (64 registers x 256 threads, no dynamic shared memory): one per SM
+    const int grid = prefetch ? std::max(1, c->copy_ctas / 2) : c->copy_ctas;
     if (pdl) {
-        launch_pdl_k((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, 0, st);
+        launch_pdl_k((const void *)cache_copy_kernel, dim3(grid), dim3(kCopyThreads), a2, 0, st);
     } else {
-        CK(cudaLaunchKernel((const void *)cache_copy_kernel, dim3(c->copy_ctas), dim3(kCopyThreads), a2, 0, st));
+        CK(cudaLaunchKernel((const void *)cache_copy_kernel, dim3(grid), dim3(kCopyThreads), a2, 0, st));
     }
 }
 
