@@ -15,8 +15,8 @@
 // Prefetch (the reference's shadow next-layer guesses, stbl/model.cu:432-475, 555-586): the planner's
 // second mode places guessed experts of a coming layer call without touching cached ones (its
 // issue(), each new guess takes a freed slot, a never-used one or the least recently used one and goes
-// to the front), and the copy runs on a second stream, beside the current call's expert kernels (the
-// copy kernel keeps no shared memory and few registers, so its CTAs fit next to theirs).  A prefetch
+// to the front), and the copy runs on a second stream, beside the current call's expert kernels (one
+// CTA per SM of at most 64 registers and no dynamic shared memory fits next to theirs).  A prefetch
 // never takes a slot the last demand call used (those experts may still be read).
 // Cancellation (the reference's PfJob states, stbl/model.cu:92-97, 319-345, 397-414, 478-494): each
 // prefetched slot carries a claim word in device memory, queued -> copying -> landed.  The copy kernel
