@@ -8,15 +8,16 @@
 // accumulator once.  The numerics equal the reference's fp32 sum of dequantized products up to
 // summation order (ref/kernel.py:94-102 fp4_gemm).
 //
-// Items are two 128-row weight tiles x one chunk of up to 16 token columns, two accumulators: for the
-// up product 128 gate rows AND the matching 128 up rows, so SwiGLU reads both from TMEM; for the down
-// product 256 consecutive rows of W2.  Two independent accumulators per K step keep the tensor pipe
+// Items are two 128-row weight tiles x one chunk of up to NTOK token columns (16, or 32 when a call
+// has more than 16 tokens: an expert routed to by 17-32 of them then streams its weights once instead
+// of twice), two accumulators: for the up product 128 gate rows AND the matching 128 up rows, so
+// SwiGLU reads both from TMEM; for the down product 256 consecutive rows of W2.  Two independent accumulators per K step keep the tensor pipe
 // busy: measured on one SM, a 128-K block of two matrices (3 scale copies + 8 MMAs) takes about as
 // long as a block of one (2 copies + 4 MMAs).
 // Stream-K over (item, 256-K unit) pairs, one persistent CTA per SM.  A pipeline stage is one
 // 256-K unit: each weight matrix arrives as ONE 4-D TMA box of 128 rows x 2 K blocks (128 contiguous
 // bytes of packed codes per row and op; single-K-block boxes read 64-byte row pieces, which streams
-// about a third slower from HBM), the activations as one 16-row x 2-K-block box.  Six warps:
+// about a third slower from HBM), the activations as one NTOK-row x 2-K-block box.  Six warps:
 //   warp 0     producer: lane 0 issues every copy of a stage on the copy engine: the TMA boxes (the
 //              packed codes land in the 128-byte swizzled layout the MMA reads, each 16 codes padded
 //              to 16 bytes: tensor-map type 16U4_ALIGN16B) and bulk copies of the scales, which are
@@ -36,26 +37,31 @@
 namespace stbl {
 
 constexpr int kT4Threads = 192;
-constexpr int kT4Acc = 4;            // item accumulators in TMEM (32 columns each for up, 16 for down)
+constexpr int kT4Acc = 4;            // item accumulators in TMEM (2 x NTOK columns each)
 constexpr int kT4Kb = kT4StageKb;    // K blocks per stage (one unit of stream-K)
 constexpr int kT4ATile = 128 * 128;  // one K block of one weight matrix in shared memory (unpacked codes)
-constexpr int kT4BTile = kTcN * 128; // one K block of activations
 constexpr int kT4SfSlots = 4;        // scale-factor slots in TMEM, 16 columns each (A0, A1, B)
-constexpr int kT4SfBase = 128;       // first TMEM column of the scale slots
-constexpr int kT4TmemCols = 256;
-constexpr int kT4Chunks = 192;       // chunk entries [chunk_begin, +192) kept in shared memory
-constexpr int kT4PartialCols = 32;   // floats per row in the stream-K partial buffer
+constexpr int kT4PartialCols = 64;   // floats per row in the stream-K partial buffer (2 x up to 32 columns)
 
-template <bool UP>
+template <bool UP, int NTOK>
 struct T4 {
+    static_assert(NTOK == 16 || NTOK == 32, "token columns per item: 16 or 32");
     static constexpr int nA = 2;                           // weight tiles per item (up: gate, up; down: 2 x 128 rows)
+    static constexpr int BTile = NTOK * 128;               // one K block of activations
     static constexpr int A = nA * kT4Kb * kT4ATile;        // [m][kb][128 rows][128 B]
-    static constexpr int B = kT4Kb * kT4BTile;             // [kb][16 rows][128 B]
-    static constexpr int SF = (nA + 1) * kT4Kb * 512;      // [m | B][kb][512 B]
-    static constexpr int stage = (A + B + SF + 1023) / 1024 * 1024;  // 71 KB at two K blocks
-    static constexpr int NV = nA * kTcN;                   // accumulator columns per item
+    static constexpr int B = kT4Kb * BTile;                // [kb][NTOK rows][128 B]
+    // scales: [m | B][kb][512 B]; the activations' 512 bytes are the chunk's rows of 16 bytes (32 rows:
+    // the tcgen05.cp 32x128b block, scale of token t at lane t, column 0)
+    static constexpr int SF = (nA + 1) * kT4Kb * 512;
+    static constexpr int stage = (A + B + SF + 1023) / 1024 * 1024;  // 71 KB (16 tokens), 75 KB (32)
+    static constexpr int NV = nA * NTOK;                   // accumulator columns per item
+    static constexpr int SfBase = kT4Acc * NV;             // first TMEM column of the scale slots
+    static constexpr int TmemCols = SfBase + kT4SfSlots * 16 <= 256 ? 256 : 512;
+    // chunk entries [chunk_begin, +Chunks) kept in shared memory (three 75 KB stages leave room for 16)
+    static constexpr int Chunks = NTOK == 16 ? 192 : 16;
 };
-static_assert(T4<true>::stage % 1024 == 0 && T4<false>::stage % 1024 == 0, "stages must keep 1 KB alignment");
+static_assert(T4<true, 16>::stage % 1024 == 0 && T4<false, 16>::stage % 1024 == 0 && T4<true, 32>::stage % 1024 == 0,
+              "stages must keep 1 KB alignment");
 
 __device__ __forceinline__ uint64_t plain_desc_32x16(const void *p) {
     // K-major, no swizzle: 8-row core matrices of 16-byte rows, 128 bytes apart (SBO), one along K
@@ -66,8 +72,9 @@ __device__ __forceinline__ uint64_t plain_desc_32x16(const void *p) {
 // Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (7-9 = 5) or e4m3 (0), B e4m3 (10-12 =
 // 0), K-major, N >> 3 at 17-22, scale type ue8m0 (bit 23), M >> 4 at 24-28; the scale byte of the K/32
 // sub-block j for B at bits 4-5 and for A at bits 29-30.
+template <int NTOK>
 __device__ __forceinline__ uint32_t idesc_mx(int j, bool a8) {
-    return ((uint32_t)j << 4) | ((a8 ? 0u : 5u) << 7) | ((uint32_t)(kTcN >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+    return ((uint32_t)j << 4) | ((a8 ? 0u : 5u) << 7) | ((uint32_t)(NTOK >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
            ((uint32_t)j << 29);
 }
 
@@ -86,9 +93,9 @@ __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, const void *smem) {
 }
 
 // One CTA's share of the MXFP4 products: CTA `cta` of the `ncta` that run this body.
-template <bool UP>
+template <bool UP, int NTOK>
 __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
-    using S = T4<UP>;
+    using S = T4<UP, NTOK>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;     // reduction length
@@ -99,10 +106,10 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     // down, the two halves of W2 rows [256 t, 256 t + 256)
     auto tile_row = [&](int t, int m) { return UP ? t : 2 * t + m; };
     unsigned char *stages = smem;                                                   // [nst][A | B | SF]
-    int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][16] by column
-    float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);                  // [2][16]
-    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);                      // [kT4Chunks] from chunk_begin
-    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kT4Chunks);
+    int *col_dst = reinterpret_cast<int *>(stages + (size_t)nst * S::stage);        // [2][NTOK] by column
+    float *col_w = reinterpret_cast<float *>(col_dst + 2 * NTOK);                  // [2][NTOK]
+    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * NTOK);                      // [S::Chunks] from chunk_begin
+    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + S::Chunks);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
     uint64_t *acc_empty = acc_full + kT4Acc;
@@ -124,7 +131,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(&tmem_base, kT4TmemCols);
+    if (warp == 1) tmem_alloc(&tmem_base, S::TmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -134,7 +141,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     pdl_launch_dependents();
     // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
     if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
-    if (p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    if (tid < S::Chunks && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
     __syncthreads();
     const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
@@ -146,8 +153,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
         uz = (int)min(u_hi - (long long)it * nu, (long long)nu);
     };
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - p.chunk_begin < kT4Chunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
-        return tc_check(p, ch);
+        const Chunk ch = (c - p.chunk_begin < S::Chunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
+        return tc_check(p, ch, NTOK);
     };
 
     if (warp == 0) {
@@ -178,14 +185,14 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     }
                     unsigned char *a = stages + (size_t)s * S::stage;
                     unsigned char *sf = a + S::A + S::B;
-                    mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * kTcN * 16);
+                    mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * NTOK * 16);
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
                         tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile_row(tile, m) * 128,
                                     kT4Kb * u, z, &full[s]);
                     tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
                     // scales: the unit's two 512-byte weight-scale blocks per matrix are adjacent; the
-                    // activation scales are the chunk's 16 rows of 16 bytes per K block
+                    // activation scales are the chunk's NTOK rows of 16 bytes per K block
 #pragma unroll
                     for (int m = 0; m < S::nA; m++)
                         bulk_g2s(sf + m * kT4Kb * 512,
@@ -196,7 +203,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
 #pragma unroll
                     for (int g = 0; g < kT4Kb; g++)
                         bulk_g2s(sf + (S::nA * kT4Kb + g) * 512,
-                                 p.act_e8 + ((size_t)(kT4Kb * u + g) * p.act_e8_rows + brow) * 16, kTcN * 16, &full[s]);
+                                 p.act_e8 + ((size_t)(kT4Kb * u + g) * p.act_e8_rows + brow) * 16, NTOK * 16, &full[s]);
                 }
             }
             // drain: every issued copy must land before the CTA may exit
@@ -236,7 +243,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     const unsigned char *sfs = a + S::A + S::B;
 #pragma unroll
                     for (int g = 0; g < kT4Kb; g++) {
-                        const uint32_t sf = tmem + (uint32_t)(kT4SfBase + ((kT4Kb * q + g) % kT4SfSlots) * 16);
+                        const uint32_t sf = tmem + (uint32_t)(S::SfBase + ((kT4Kb * q + g) % kT4SfSlots) * 16);
 #pragma unroll
                         for (int m = 0; m < S::nA; m++) tmem_cp_sf(sf + 4 * m, sfs + (m * kT4Kb + g) * 512);
                         tmem_cp_sf(sf + 8, sfs + (S::nA * kT4Kb + g) * 512);
@@ -244,8 +251,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                         for (int m = 0; m < S::nA; m++)
 #pragma unroll
                             for (int j = 0; j < 4; j++)
-                                umma_mx(d + m * kTcN, sw128_desc(a + (m * kT4Kb + g) * kT4ATile + 32 * j),
-                                        sw128_desc(a + S::A + g * kT4BTile + 32 * j), idesc_mx(j, a8), (u > ua || g > 0 || j > 0),
+                                umma_mx(d + m * NTOK, sw128_desc(a + (m * kT4Kb + g) * kT4ATile + 32 * j),
+                                        sw128_desc(a + S::A + g * S::BTile + 32 * j), idesc_mx<NTOK>(j, a8), (u > ua || g > 0 || j > 0),
                                         sf + 4 * m, sf + 8);
                     }
                     umma_commit(&empty[s]);
@@ -295,9 +302,9 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
         };
         // scatter into the column table of buffer buf (all 128 threads; two barriers)
         auto park = [&](int buf) {
-            if (et < kTcN) col_dst[buf * kTcN + et] = -1;
+            if (et < NTOK) col_dst[buf * NTOK + et] = -1;
             bar_sync(2, 128);
-            if (pval) col_dst[buf * kTcN + pcol] = pdst, col_w[buf * kTcN + pcol] = pwt;
+            if (pval) col_dst[buf * NTOK + pcol] = pdst, col_w[buf * NTOK + pcol] = pwt;
             bar_sync(2, 128);
         };
         if (lo < hi) {
@@ -315,11 +322,19 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
             int ua, uz;
             u_range(it, ua, uz);
             bool ok = mbar_wait(&acc_full[acc_i], (ia / kT4Acc) & 1, &abort_flag);
-            float va[kTcN], vb[kTcN];
+            float va[NTOK], vb[NTOK];
             if (ok) {
                 tc_fence_after();
-                tmem_ld16(tl + (uint32_t)(acc_i * S::NV), va);
-                tmem_ld16(tl + (uint32_t)(acc_i * S::NV + kTcN), vb);
+#pragma unroll
+                for (int h = 0; h < NTOK / 16; h++) {
+                    float t[16];
+                    tmem_ld16(tl + (uint32_t)(acc_i * S::NV + 16 * h), t);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) va[16 * h + i] = t[i];
+                    tmem_ld16(tl + (uint32_t)(acc_i * S::NV + NTOK + 16 * h), t);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) vb[16 * h + i] = t[i];
+                }
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc_i]);
             }
@@ -335,10 +350,10 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 // the range starts inside this item: publish the partial sums for the CTA that finishes it
                 float4 *dst = reinterpret_cast<float4 *>(prow);
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) dst[j] = make_float4(va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]);
+                for (int j = 0; j < NTOK / 4; j++) dst[j] = make_float4(va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]);
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++)
-                    dst[kTcN / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
+                for (int j = 0; j < NTOK / 4; j++)
+                    dst[NTOK / 4 + j] = make_float4(vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
                 if (et == 0) flag_release(p.flags + cta, p.seq);
@@ -354,13 +369,13 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 bar_sync(2, 128);
                 const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)cb * 128 + row) * kT4PartialCols);
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) {
+                for (int j = 0; j < NTOK / 4; j++) {
                     const float4 v = __ldcg(src + j);
                     va[4 * j] += v.x, va[4 * j + 1] += v.y, va[4 * j + 2] += v.z, va[4 * j + 3] += v.w;
                 }
 #pragma unroll
-                for (int j = 0; j < kTcN / 4; j++) {
-                    const float4 v = __ldcg(src + kTcN / 4 + j);
+                for (int j = 0; j < NTOK / 4; j++) {
+                    const float4 v = __ldcg(src + NTOK / 4 + j);
                     vb[4 * j] += v.x, vb[4 * j + 1] += v.y, vb[4 * j + 2] += v.z, vb[4 * j + 3] += v.w;
                 }
             }
@@ -368,8 +383,8 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 abort_flag = 1;
                 atomicOr(p.status, kErrWaitTimeout);
             }
-            const int *cdst = col_dst + buf * kTcN;
-            const float *cw = col_w + buf * kTcN;
+            const int *cdst = col_dst + buf * NTOK;
+            const float *cw = col_w + buf * NTOK;
             const int r = tile * 128 + row;
             if (UP) {
                 // SwiGLU per column straight from the two accumulators (gate: va, up: vb); h is bf16
@@ -377,7 +392,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 // power-of-two scale (stbl/kernels.cu:56-63): the 32 rows of this warp are one block,
                 // so the block's amax is a warp reduction and h never leaves the SM unquantized
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) {
+                for (int j = 0; j < NTOK; j++) {
                     const int dst = cdst[j];
                     if (dst < 0) continue;  // the same for every thread of the warpgroup
                     float gv = bf16r(va[j]), uv = bf16r(vb[j]);
@@ -401,7 +416,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 // rows 256 tile + row (va) and 256 tile + 128 + row (vb) of W2's output
                 const int r0 = tile * 256 + row;
 #pragma unroll
-                for (int j = 0; j < kTcN; j++)
+                for (int j = 0; j < NTOK; j++)
                     if (j < ch.n) {
                         uint16_t *o = (ch.e == p.E ? p.sh : p.eo) + (size_t)cdst[j] * p.H;
                         o[r0] = f32_to_bf16_bits(va[j]);
@@ -415,7 +430,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kT4TmemCols);
+        tmem_dealloc(tmem, S::TmemCols);
     }
 }
 
@@ -423,7 +438,7 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
 // expert's (tc8_body), in one persistent grid, so the shared expert's 44 MB stream alongside the
 // routed weights instead of in launches of their own.  The split follows the bytes each side streams
 // (known only on the device: the routed chunk count comes from the router); p8 may hold no chunks.
-template <bool UP>
+template <bool UP, int NTOK>
 __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_constant__ TcMaps maps8, TcParams p8,
                                                                    int nst8, const __grid_constant__ TcMaps maps4,
                                                                    TcParams p4, int nst4) {
@@ -440,22 +455,35 @@ __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_
     int c8 = 0;
     if (n8c > 0) c8 = n4c > 0 ? min(ncta - 1, max(1, (int)(ncta * (b8 / kRate8) / (b8 / kRate8 + b4) + 0.5))) : ncta;
     if ((int)blockIdx.x < c8) tc8_body<UP, true>(maps8, p8, nst8, blockIdx.x, c8);  // two-tile items
-    else tc4_body<UP>(maps4, p4, nst4, blockIdx.x - c8, ncta - c8);
+    else tc4_body<UP, NTOK>(maps4, p4, nst4, blockIdx.x - c8, ncta - c8);
 }
 
-template __global__ void expert_tc4_kernel<true>(const __grid_constant__ TcMaps, TcParams, int, const __grid_constant__ TcMaps,
-                                                 TcParams, int);
-template __global__ void expert_tc4_kernel<false>(const __grid_constant__ TcMaps, TcParams, int, const __grid_constant__ TcMaps,
-                                                  TcParams, int);
+template __global__ void expert_tc4_kernel<true, 16>(const __grid_constant__ TcMaps, TcParams, int,
+                                                     const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc4_kernel<false, 16>(const __grid_constant__ TcMaps, TcParams, int,
+                                                      const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc4_kernel<true, 32>(const __grid_constant__ TcMaps, TcParams, int,
+                                                     const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc4_kernel<false, 32>(const __grid_constant__ TcMaps, TcParams, int,
+                                                      const __grid_constant__ TcMaps, TcParams, int);
 
-const void *expert_tc4_kernel_ptr(bool up) {
-    return up ? (const void *)expert_tc4_kernel<true> : (const void *)expert_tc4_kernel<false>;
+// wide: items of up to 32 token columns (calls of more than 16 tokens), else 16
+const void *expert_tc4_kernel_ptr(bool up, bool wide) {
+    if (wide) return up ? (const void *)expert_tc4_kernel<true, 32> : (const void *)expert_tc4_kernel<false, 32>;
+    return up ? (const void *)expert_tc4_kernel<true, 16> : (const void *)expert_tc4_kernel<false, 16>;
 }
 
-// dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
-int expert_tc4_smem_bytes(bool up, int nst) {
-    const int stage = up ? T4<true>::stage : T4<false>::stage;  // equal: two 128-row tiles per item
-    return nst * stage + 4 * (4 * kTcN) + (int)sizeof(Chunk) * kT4Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
+// dynamic shared-memory bytes of one launch (1 KB of it aligns the stages); up and down stages are
+// equal (two 128-row tiles per item)
+template <int NTOK>
+int tc4_smem_bytes(int nst) {
+    using S = T4<true, NTOK>;
+    return nst * S::stage + 4 * (4 * NTOK) + (int)sizeof(Chunk) * S::Chunks + 8 * (2 * nst + 2 * kT4Acc + 1) + 1024;
+}
+
+int expert_tc4_smem_bytes(bool up, int nst, bool wide) {
+    (void)up;
+    return wide ? tc4_smem_bytes<32>(nst) : tc4_smem_bytes<16>(nst);
 }
 
 // e8m0 weight scales of slots [z0, z0 + nz) (slot z at src + z * src_stride) into the scale-block

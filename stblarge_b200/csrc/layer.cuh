@@ -13,6 +13,9 @@ enum : int { kScoreSigmoid = 0, kScoreSqrtSoftplus = 1 };
 // activation quantization rules (RouterParams::pow2_a / pow2_b): 0 fp32 scale amax/448, 1 power-of-two
 // scale, kActQ8 int8 codes with an fp32 scale amax/127 per 32 (ref/emulate_ds4.py:23-30)
 constexpr int kActQ8 = 2;
+// rows after the position-ordered activation buffers (x by position, h): a chunk's TMA box and the
+// bulk copy of its scales read whole 16- or 32-row blocks from its first position
+constexpr int kPosPad = 32;
 constexpr int kQ8ChunkTokens = 8;   // tokens per routed chunk of an act_q8 layer (experts_q8.cu)
 
 constexpr int kMaxExperts = 512;    // router: a lane holds experts l, l+32, ... (16 per lane)

@@ -21,8 +21,8 @@
 namespace stbl {
 const void *combine_kernel_ptr();                 // combine.cu
 const void *expert_tc_kernel_ptr(bool up, bool two);  // experts_tc.cu
-const void *expert_tc4_kernel_ptr(bool up);       // experts_tc4.cu
-int expert_tc4_smem_bytes(bool up, int nst);
+const void *expert_tc4_kernel_ptr(bool up, bool wide);  // experts_tc4.cu
+int expert_tc4_smem_bytes(bool up, int nst, bool wide);
 int expert_tc4_partial_cols();
 cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *dst, long long dst_stride, int rows, int K,
                              int z0, int nz, int rps, cudaStream_t st);
@@ -118,7 +118,7 @@ struct stbl_moe {
     uint8_t *sf_shared = nullptr;     // the shared expert's scales in the scale-block layout (3 matrices)
     long long sf_shared_off[3] = {0, 0, 0};
     TcMaps tc4_up{}, tc4_down{};      // MXFP4 weight maps (16 codes padded to 16 bytes in shared memory)
-    int tc4_nst_up = 0, tc4_nst_down = 0, tc4_nst8_up = 0, tc4_nst8_down = 0, tc4_smem_up = 0, tc4_smem_down = 0;
+    int tc4_nst[2][2] = {}, tc4_nst8[2][2] = {}, tc4_smem[2][2] = {};  // [up][wide]: stages of both bodies, bytes
     uint8_t *xe8_a = nullptr, *xe8_pos = nullptr, *he8 = nullptr;  // e8m0 activation scales (per 32), [K/128][rows][16 B]
     int Tpad = 0, pos_rows = 0;       // rows of the token-ordered and position-ordered activation buffers
     // MXFP4 weight scales in the scale-block layout: the layer's own copy (natural scales given), slot z
@@ -131,6 +131,7 @@ struct stbl_moe {
     float *hd8 = nullptr;             // Q8 scales of h by position [pos][I / 32]
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
     CUtensorMap bmap4_xa{}, bmap4_xpos{}, bmap4_hq{};         // the same, two K blocks per box (MXFP4 kernels)
+    CUtensorMap bmap4w_xpos{}, bmap4w_hq{};                   // 32-row boxes (MXFP4 items of up to 32 tokens)
 
     int last_T = 0;
     uint64_t calls = 0, tokens = 0;
@@ -222,13 +223,14 @@ CUtensorMap weight_map4(const void *base, int K, int rows, int experts, long lon
 
 void launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t st);
 
-// 3-D view {128 codes, rows, K blocks} of [rows][K] e4m3 activation codes: one box is 16 rows x 2 K
-// blocks, landing as two [16 rows][128 B] tiles (128B swizzle); the MXFP4 kernels' B operand
-CUtensorMap act_map2(const void *base, int K, int rows) {
+// 3-D view {128 codes, rows, K blocks} of [rows][K] e4m3 activation codes: one box is box_rows (16 or
+// 32) rows x 2 K blocks, landing as two [box_rows][128 B] tiles (128B swizzle); the MXFP4 kernels' B
+// operand
+CUtensorMap act_map2(const void *base, int K, int rows, int box_rows = 16) {
     CUtensorMap m;
     const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(K / 128)};
     const cuuint64_t strides[2] = {(cuuint64_t)K, 128};
-    const cuuint32_t box[3] = {128, 16, (cuuint32_t)kT4StageKb};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)kT4StageKb};
     const cuuint32_t es[3] = {1, 1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -264,8 +266,8 @@ EpLayout ep_layout(int E, int n, int routed_cap, int Tmax, int K, int H) {
     L.cnt_flag = take(4LL * kEpMaxRanks);
     L.pay_flag = take(4LL * kEpMaxRanks);
     L.done_flag = take(4LL * kEpMaxRanks);
-    L.xq_pos = take((long long)(routed_cap + Tmax + 16) * H);
-    L.xs_pos = take(4LL * (routed_cap + Tmax + 16) * (H / 128));
+    L.xq_pos = take((long long)(routed_cap + Tmax + kPosPad) * H);
+    L.xs_pos = take(4LL * (routed_cap + Tmax + kPosPad) * (H / 128));
     L.pos_meta = take(4LL * routed_cap);
     L.pos_w = take(4LL * routed_cap);
     L.eo = take(2LL * Tmax * K * H);
@@ -366,20 +368,20 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xq_b = carve<uint8_t>(p, (size_t)Tpad * H);
         m->xs_b = carve<float>(p, (size_t)Tpad * (H / 32));
         m->xe8_a = carve<uint8_t>(p, (size_t)(H / 128) * Tpad * 16);
-        m->xe8_pos = carve<uint8_t>(p, (size_t)(H / 128) * (npos + 16) * 16);
-        m->he8 = carve<uint8_t>(p, (size_t)(I / 128) * (npos + 16) * 16);
-        m->xq_pos = ep_n > 1 ? nullptr : carve<uint8_t>(p, (size_t)(npos + 16) * H);
-        m->xs_pos = ep_n > 1 ? nullptr : carve<float>(p, (size_t)(npos + 16) * (H / 128));
+        m->xe8_pos = carve<uint8_t>(p, (size_t)(H / 128) * (npos + kPosPad) * 16);
+        m->he8 = carve<uint8_t>(p, (size_t)(I / 128) * (npos + kPosPad) * 16);
+        m->xq_pos = ep_n > 1 ? nullptr : carve<uint8_t>(p, (size_t)(npos + kPosPad) * H);
+        m->xs_pos = ep_n > 1 ? nullptr : carve<float>(p, (size_t)(npos + kPosPad) * (H / 128));
         m->h = carve<uint16_t>(p, (size_t)npos * I);
-        m->hq = carve<uint8_t>(p, (size_t)(npos + 16) * I);
-        m->hs = carve<float>(p, (size_t)(npos + 16) * (I / 128));
-        m->hd8 = d->act_q8 ? carve<float>(p, (size_t)(npos + 16) * (I / 32)) : nullptr;
+        m->hq = carve<uint8_t>(p, (size_t)(npos + kPosPad) * I);
+        m->hs = carve<float>(p, (size_t)(npos + kPosPad) * (I / 128));
+        m->hd8 = d->act_q8 ? carve<float>(p, (size_t)(npos + kPosPad) * (I / 32)) : nullptr;
         m->eo = ep_n > 1 ? nullptr : carve<uint16_t>(p, (size_t)T * K * H);
         m->sh = carve<uint16_t>(p, (size_t)T * H);
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
-        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * 64);
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * (32 + 64));
         m->tc_flags = carve<unsigned int>(p, 2 * m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
@@ -398,7 +400,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->eo = reinterpret_cast<uint16_t *>(m->ep_region + m->ep_L.eo);
     }
     CK(cudaMemcpy(m->slot, m->host_slot.data(), sizeof(int) * E, cudaMemcpyHostToDevice));
-    m->Tpad = Tpad, m->pos_rows = npos + 16;
+    m->Tpad = Tpad, m->pos_rows = npos + kPosPad;
 
     CK(router_setup());
     m->routed_tc = d->routed_fmt == STBL_FMT_FP8_B128;
@@ -489,11 +491,13 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         if (!m->routed_tc && (!m->has_shared || m->shared_bs)) m->tc_up = m->tc_up2 = m->tc4_up, m->tc_down = m->tc4_down;  // unused, valid
         m->bmap_xa = act_map(m->xq_a, H, Tpad);
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
-        m->bmap_xpos = act_map(m->xq_pos, H, npos + 16);
-        m->bmap_hq = act_map(m->hq, I, npos + 16);
+        m->bmap_xpos = act_map(m->xq_pos, H, npos + kPosPad);
+        m->bmap_hq = act_map(m->hq, I, npos + kPosPad);
         m->bmap4_xa = act_map2(m->xq_a, H, Tpad);
-        m->bmap4_xpos = act_map2(m->xq_pos, H, npos + 16);
-        m->bmap4_hq = act_map2(m->hq, I, npos + 16);
+        m->bmap4_xpos = act_map2(m->xq_pos, H, npos + kPosPad);
+        m->bmap4_hq = act_map2(m->hq, I, npos + kPosPad);
+        m->bmap4w_xpos = act_map2(m->xq_pos, H, npos + kPosPad, 32);
+        m->bmap4w_hq = act_map2(m->hq, I, npos + kPosPad, 32);
         // stages: at least kTcBatch (4: the producer requests K blocks four at a time and first waits
         // for four free stages), at most 8 of one tile (more outstanding requests only lengthen the
         // DRAM queues, measured) or 6 of two
@@ -513,23 +517,23 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
         if (m->routed_bs) {
             // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
-            // fit; a MXFP4 stage is one 256-K unit (up: 71 KB, gate + up; down: 38 KB)
-            for (int up = 1; up >= 0; up--) {
-                cudaFuncAttributes fa{};
-                CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up)));
-                const int room = max_smem - (int)fa.sharedSizeBytes;
-                // the FP8 body takes two-tile items here (34 KB stages, 4 to 6)
-                int n4 = 6, n8 = 6;
-                const int n8min = 4;
-                while (n4 >= 2 && expert_tc4_smem_bytes(up, n4) > room) n4--;
-                while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, true) > room) n8--;
-                if (n4 < 2 || n8 < n8min) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-                const int smem = std::max(expert_tc4_smem_bytes(up, n4), expert_tc_smem_bytes(up, H, I, n8, true));
-                CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-                (up ? m->tc4_nst_up : m->tc4_nst_down) = n4;
-                (up ? m->tc4_nst8_up : m->tc4_nst8_down) = n8;
-                (up ? m->tc4_smem_up : m->tc4_smem_down) = smem;
-            }
+            // fit; a MXFP4 stage is one 256-K unit of two 128-row tiles (71 KB with 16-token items, 75
+            // KB with 32-token ones)
+            for (int up = 1; up >= 0; up--)
+                for (int wide = 0; wide < 2; wide++) {
+                    cudaFuncAttributes fa{};
+                    CK(cudaFuncGetAttributes(&fa, expert_tc4_kernel_ptr(up, wide)));
+                    const int room = max_smem - (int)fa.sharedSizeBytes;
+                    // the FP8 body takes two-tile items here (34 KB stages, 4 to 6)
+                    int n4 = 6, n8 = 6;
+                    const int n8min = 4;
+                    while (n4 >= 2 && expert_tc4_smem_bytes(up, n4, wide) > room) n4--;
+                    while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, true) > room) n8--;
+                    if (n4 < 2 || n8 < n8min) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
+                    const int smem = std::max(expert_tc4_smem_bytes(up, n4, wide), expert_tc_smem_bytes(up, H, I, n8, true));
+                    CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up, wide), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+                    m->tc4_nst[up][wide] = n4, m->tc4_nst8[up][wide] = n8, m->tc4_smem[up][wide] = smem;
+                }
         }
     }
 }
@@ -651,6 +655,11 @@ void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
     launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
 }
 
+// Block-scaled (MXFP4 / FP8-e8m0) routed experts take items of up to 32 tokens in calls of more than
+// 16 tokens (their chunks are read by position then): an expert routed to by 17-32 of the call's tokens
+// streams its weights once, not twice.  The router builds its chunks to match.
+bool tc4_wide(const stbl_moe *m, int T) { return m->routed_bs && !m->act_q8 && T > 16; }
+
 // up items of 128 gate + 128 up rows from this many tokens on (the up kernel's two-tile form).
 // Measured on one GPU: cfg2 T=16 up 407 -> 351 us, cfg4 T=256 layer 2.29 -> 2.07 ms; at T=1 the
 // single-tile form stays (73 against 76 us).  Under expert parallelism (2 GPUs, cfg4): 1.282 ->
@@ -671,17 +680,19 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
                up ? (two ? m->tc_smem_up2 : m->tc_smem_up) : (two ? m->tc_smem_down2 : m->tc_smem_down), st);
 }
 
-// the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range)
-void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, cudaStream_t st) {
+// the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range).
+// wide: the call's block-scaled chunks hold up to 32 tokens (tc4_wide), read by position
+void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, bool wide, cudaStream_t st) {
     TcMaps maps8 = up ? m->tc_up2 : m->tc_down;  // the FP8 body's two-tile items (128-row boxes)
     maps8.b = up ? m->bmap_xb : m->bmap_hq;
     TcMaps maps4 = up ? m->tc4_up : m->tc4_down;
-    maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
+    if (wide) maps4.b = up ? m->bmap4w_xpos : m->bmap4w_hq;
+    else maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
     p4.flags = m->tc_flags + m->sms;
     p4.partial = m->tc_partial + (size_t)m->sms * 128 * 32;
-    int *n8 = up ? &m->tc4_nst8_up : &m->tc4_nst8_down, *n4 = up ? &m->tc4_nst_up : &m->tc4_nst_down;
+    int *n8 = &m->tc4_nst8[up][wide], *n4 = &m->tc4_nst[up][wide];
     void *args[] = {&maps8, &p8, n8, &maps4, &p4, n4};
-    launch_pdl(expert_tc4_kernel_ptr(up), dim3(m->sms), dim3(192), args, up ? m->tc4_smem_up : m->tc4_smem_down, st);
+    launch_pdl(expert_tc4_kernel_ptr(up, wide), dim3(m->sms), dim3(192), args, m->tc4_smem[up][wide], st);
 }
 
 void launch_gather(stbl_moe *m, int T, cudaStream_t st) {
@@ -753,8 +764,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
     r.xe8_a = m->routed_bs && !m->act_q8 ? m->xe8_a : nullptr;
     r.xe8_rows = m->Tpad;
-    r.nt_routed = m->act_q8 ? kQ8ChunkTokens : 16;
-    r.nt_shared = 16;
+    r.nt_routed = m->act_q8 ? kQ8ChunkTokens : tc4_wide(m, T) ? 32 : 16;
+    r.nt_shared = tc4_wide(m, T) && m->shared_bs ? 32 : 16;  // an FP8 128x128 shared expert keeps 16
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
     r.forced_idx = forced;
@@ -864,7 +875,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         TcParams su = tc_params(m, T, true, true), pu = tc_params(m, T, true, direct);
         su.chunk_begin = 0, su.chunk_end = n8;
         pu.chunk_begin = n8, pu.chunk_end = -1;
-        launch_tc4(m, true, su, pu, st);
+        launch_tc4(m, true, su, pu, tc4_wide(m, T), st);
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         launches += 1;
         if (n8) {
@@ -874,7 +885,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         TcParams sd = tc_params(m, T, false), pd = tc_params(m, T, false);
         sd.chunk_begin = 0, sd.chunk_end = n8;
         pd.chunk_begin = n8, pd.chunk_end = -1;
-        launch_tc4(m, false, sd, pd, st);
+        launch_tc4(m, false, sd, pd, tc4_wide(m, T), st);
         launches += 1;
     }
     CombineParams cp{m->eo, m->sh, io ? nullptr : static_cast<uint16_t *>(y), T, m->K, m->H, m->has_shared, ep_view(m), m->status};

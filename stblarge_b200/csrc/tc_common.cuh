@@ -11,11 +11,12 @@ struct TcChunk {
     int e, pos0, n, ok;
 };
 
-__device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch) {
+// a chunk entry checked against the launch (max_n: token columns per item)
+__device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch, int max_n = kTcN) {
     TcChunk r{ch.e, ch.pos0, ch.n, 1};
     const int nrouted = p.n_routed;
     const bool shared = ch.e == p.E;
-    const bool bad = ch.e < 0 || ch.e > p.E || (shared && !p.has_shared) || ch.n < 1 || ch.n > kTcN ||
+    const bool bad = ch.e < 0 || ch.e > p.E || (shared && !p.has_shared) || ch.n < 1 || ch.n > max_n ||
                      (shared ? (ch.pos0 < nrouted || ch.pos0 + ch.n > nrouted + p.T)
                              : (ch.pos0 < 0 || ch.pos0 + ch.n > nrouted));
     if (bad) r = TcChunk{0, 0, 0, 0};

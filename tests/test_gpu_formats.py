@@ -41,7 +41,7 @@ def ref_layers():
 
 
 @pytest.mark.parametrize("name", list(CFGS))
-@pytest.mark.parametrize("T", [1, 4, 16, 64])
+@pytest.mark.parametrize("T", [1, 4, 16, 17, 40, 64])  # > 16: chunks of up to 32 tokens, shared expert's too
 def test_reference_format_layer_parity(ref_layers, name, T):
     W, dev, layer = ref_layers[name]
     run_and_check(CFGS[name], layer, dev, W, synth.make_x(CFGS[name].hidden, T, seed=600 + T))

@@ -112,7 +112,7 @@ def small_layers():
 
 
 @pytest.mark.parametrize("name", ["cfg1", "cfg1_fp4"])
-@pytest.mark.parametrize("T", [1, 4, 5, 16, 64])
+@pytest.mark.parametrize("T", [1, 4, 5, 16, 17, 40, 64])  # 17, 40: ragged 32-token chunks (MXFP4)
 def test_small_layer_parity(small_layers, name, T):
     W, dev, layer = small_layers[name]
     cfg = layer.cfg
