@@ -1,7 +1,7 @@
 // Ordered combine of the MoE layer: y = bf16(((0 + eo_0) + ... + eo_{k-1}) + shared), the sums in fp32
 // in top-k order (stbl/model.cu:589-592, the reference's k_axpy chain + k_round_bf16), one thread per
 // 8 outputs.  Under expert parallelism the routed rows were written by the owning GPUs; the kernel
-// first raises this rank's done flag everywhere and waits for every rank's.  With the fused
+// first waits for every rank's done flag (raised by the last CTA of that rank's down kernel).  With the fused
 // hyper-connection post (CombineParams::hout) each thread also writes its 8 outputs of every stream j
 // of the block's residual update (stbl/model.cu:805, k_hc_post, stbl/kernels.cu:328-338).
 #include "layer.cuh"
@@ -12,11 +12,10 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineParams p) {
     pdl_launch_dependents();  // the next kernel may start its prologue; it waits for this one's end
     pdl_wait();
     if (p.ep.n_ranks > 1) {
-        // expert parallelism: this rank's down kernel (before this one) has finished writing into
-        // every source rank's eo rows: say so everywhere, then wait until every rank has said so
+        // expert parallelism: every rank's down kernel has written its rows into this rank's eo rows
+        // once that rank's done flag carries this call
         __shared__ int ok;
         if (threadIdx.x == 0) {
-            if (blockIdx.x == 0) signal_all(p.ep, p.ep.L.done_flag);
             ok = wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.done_flag),
                                 p.ep.n_ranks, p.ep.epoch);
             if (!ok) atomicOr(p.status, kErrWaitTimeout);

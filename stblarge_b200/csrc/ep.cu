@@ -40,33 +40,48 @@ constexpr int kEpCountThreads = 512;  // one thread per expert (E <= kMaxExperts
 __global__ void __launch_bounds__(kEpCountThreads) ep_counts_kernel(EpCountsParams p) {
     __shared__ int warp_tot[kEpCountThreads / 32];
     __shared__ int dst_off[kMaxExperts];
-    __shared__ int ok_all;
+    __shared__ int cnt[kEpMaxRanks * kMaxExperts];  // [source rank][expert] counts of this call
+    __shared__ int timed_out;
     const int tid = threadIdx.x;
     const EpView &v = p.ep;
     pdl_wait();  // the router's counts, offsets and permutation
     pdl_launch_dependents();
+    if (tid == 0) timed_out = 0, *p.done_ctr = 0;
+    const unsigned int tag = v.epoch % 0xffffu + 1u;  // 1..65535, never the zeroed region's 0
 
-    // 1. this rank's counts into every rank's inbox row [rank]
+    // 1. this rank's counts, tagged with the call, into every rank's inbox row [rank]
     for (int d = 0; d < v.n_ranks; d++) {
-        int *inbox = reinterpret_cast<int *>(v.region[d] + v.L.inbox) + (size_t)v.rank * p.E;
-        for (int e = tid; e < p.E; e += kEpCountThreads) inbox[e] = p.counts[e];
+        unsigned int *inbox = reinterpret_cast<unsigned int *>(v.region[d] + v.L.inbox) + (size_t)v.rank * p.E;
+        for (int e = tid; e < p.E; e += kEpCountThreads) inbox[e] = tag << 16 | (unsigned int)p.counts[e];
     }
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0) {
-        signal_all(v, v.L.cnt_flag);
-        ok_all = wait_flags_sys(reinterpret_cast<const unsigned int *>(v.region[v.rank] + v.L.cnt_flag), v.n_ranks, v.epoch);
-        if (!ok_all) atomicOr(p.status, kErrWaitTimeout);
+    // 2. every rank's row of this rank's inbox, once it carries this call's tag (bounded wait).  A rank
+    //    writes its row of call c + 1 only after its combine of call c, so the tag also says that every
+    //    rank is done with the buffers of call c that this call's payload and outputs overwrite.
+    const unsigned int *own = reinterpret_cast<const unsigned int *>(v.region[v.rank] + v.L.inbox);
+    if (tid < p.E) {
+        const uint64_t t0 = global_ns();
+        for (int s = 0; s < v.n_ranks; s++) {
+            unsigned int x;
+            for (;;) {
+                asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(x) : "l"(own + (size_t)s * p.E + tid) : "memory");
+                if ((x >> 16) == tag) break;
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    timed_out = 1;
+                    break;
+                }
+            }
+            cnt[s * kMaxExperts + tid] = (int)(x & 0xffffu);
+        }
     }
     __syncthreads();
+    if (tid == 0 && timed_out) atomicOr(p.status, kErrWaitTimeout);
 
-    // 2. every expert's total and this rank's place among its sources
-    const int *inbox = reinterpret_cast<const int *>(v.region[v.rank] + v.L.inbox);
+    // every expert's total and this rank's place among its sources
     const int e = tid;
     int tot = 0, below = 0;
     if (e < p.E)
         for (int s = 0; s < v.n_ranks; s++) {
-            const int c = __ldcg(inbox + (size_t)s * p.E + e);
+            const int c = cnt[s * kMaxExperts + e];
             tot += c;
             if (s < v.rank) below += c;
         }
@@ -91,7 +106,7 @@ __global__ void __launch_bounds__(kEpCountThreads) ep_counts_kernel(EpCountsPara
     const int el = tid;
     int my_tot = 0;
     if (el < p.E_loc)
-        for (int s = 0; s < v.n_ranks; s++) my_tot += __ldcg(inbox + (size_t)s * p.E + v.rank * p.E_loc + el);
+        for (int s = 0; s < v.n_ranks; s++) my_tot += cnt[s * kMaxExperts + v.rank * p.E_loc + el];
     int rows_total;
     const int base = block_scan_excl<kEpCountThreads>(el < p.E_loc ? my_tot : 0, warp_tot, rows_total);
     const int nch = el < p.E_loc ? (my_tot + p.nt_routed - 1) / p.nt_routed : 0;

@@ -16,6 +16,7 @@ struct EpCountsParams {
     Chunk *chunks;       // out: this rank's compute chunks (shared expert first; e = local expert)
     int *n_chunks;       // out: [0] all, [1] shared
     int *n_rows;         // out: [0] routed rows received
+    unsigned int *done_ctr;  // the down kernel's CTA ticket (zeroed here, before that kernel runs)
     uint32_t *status;
 };
 

@@ -98,24 +98,26 @@ cudaError_t launch_router(RouterParams r, cudaStream_t st, bool pdl_first);
 // Rank r of n holds routed experts [r E/n, (r+1) E/n).  Every rank owns one exchange region, mapped
 // into every other rank's address space (CUDA IPC over NVLink); the regions have the same layout on
 // every rank.  Per layer call (epoch = the call's number, the same on every rank):
-//   counts  each rank writes its per-expert assignment counts into every rank's inbox[r] and raises
-//           cnt_flag[r] there; every rank waits for all n cnt_flags, then knows where each of its
-//           assignments lands in its owner's receive rows (expert-major, then source rank, then the
-//           source's token order)
+//   counts  each rank writes its per-expert assignment counts into every rank's inbox[r], each word
+//           tagged with the call (tag << 16 | count, the tag cycling over 1..65535); every rank waits
+//           until all n rows of its inbox carry this call's tag (a word is written whole, so no fence
+//           or flag is needed), then knows where each of its assignments lands in its owner's receive
+//           rows (expert-major, then source rank, then the source's token order)
 //   payload each rank writes the FP8 codes + scales of each assignment's token, its routing weight
 //           and (source rank, assignment) into the owner's receive rows; the owner's up kernel, once
 //           the payload kernel before it has finished, raises pay_flag[r] on every rank and waits for
 //           all n pay_flags
 //   outputs the owner's down kernel stores each assignment's bf16 output row straight into the source
-//           rank's eo rows; the combine kernel raises done_flag[r] on every rank and waits for all n
+//           rank's eo rows; each of its CTAs fences its stores and the last one to finish raises
+//           done_flag[r] on every rank; the combine kernel waits for all n
 // Every wait is bounded.  A rank never waits for a later step of another rank, so the waits cannot
 // form a cycle; the count exchange of call c+1 cannot start on any rank before every rank has
 // finished call c's combine, which protects every buffer that peers write.
 constexpr int kEpMaxRanks = 8;
 
 struct EpLayout {            // byte offsets inside an exchange region
-    long long inbox;         // int [n][E]: assignment counts per expert, by source rank
-    long long cnt_flag;      // u32 [n]
+    long long inbox;         // u32 [n][E]: call tag << 16 | assignment count per expert, by source rank
+    long long cnt_flag;      // u32 [n] (unused: the inbox words carry the call)
     long long pay_flag;      // u32 [n]
     long long done_flag;     // u32 [n]
     long long xq_pos;        // u8 [rows][H]: receive rows (routed, capacity n Tmax topk), then the shared rows

@@ -76,6 +76,7 @@ struct stbl_moe {
     bool ep_connected = false;
     unsigned int ep_epoch = 0;
     int *a_dst = nullptr, *n_rows = nullptr;
+    unsigned int *ep_done_ctr = nullptr;  // expert parallelism: the down kernel's CTA ticket (ep.cu zeroes it per call)
     int *sel_cnt = nullptr;
     uint32_t *sel_bm = nullptr;
     unsigned int *sel_ticket = nullptr;
@@ -385,6 +386,7 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->tc_flags = carve<unsigned int>(p, 2 * m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
+        m->ep_done_ctr = carve<unsigned int>(p, 1);
         m->sel_cnt = carve<int>(p, Eg);
         m->sel_bm = carve<uint32_t>(p, (size_t)Eg * ((T + 31) / 32));
         m->sel_ticket = carve<unsigned int>(p, 4);
@@ -563,6 +565,7 @@ TcParams tc_params(stbl_moe *m, int T, bool up, bool direct = true) {
         p.pos_w = reinterpret_cast<const float *>(m->ep_region + m->ep_L.pos_w);
         p.pos_meta = reinterpret_cast<const int *>(m->ep_region + m->ep_L.pos_meta);
         p.T_max_assign = m->Tmax * m->K;
+        p.ep_done_ctr = m->ep_done_ctr;
     } else {
         p.n_routed = T * m->K;
     }
@@ -802,6 +805,7 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         cpp.T = T, cpp.topk = m->K, cpp.E = m->E, cpp.E_loc = m->E_loc;
         cpp.nt_routed = 16, cpp.nt_shared = 16, cpp.has_shared = m->has_shared, cpp.routed_cap = m->routed_cap;
         cpp.a_dst = m->a_dst, cpp.chunks = m->chunks, cpp.n_chunks = m->n_chunks, cpp.n_rows = m->n_rows;
+        cpp.done_ctr = m->ep_done_ctr;
         cpp.status = m->status;
         EpPayloadParams ppp{};
         ppp.ep = cpp.ep;

@@ -471,9 +471,13 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             if (it + 1 < hi) park(buf ^ 1);
             bar_sync(2, 128);
         }
+        // expert parallelism: this CTA's output rows went into the source ranks' eo rows
+        if (!UP && p.ep.n_ranks > 1) __threadfence_system();
     }
     tc_fence_before();
     __syncthreads();
+    if (!UP && p.ep.n_ranks > 1 && tid == 0 && atomicAdd(p.ep_done_ctr, 1u) == (unsigned int)ncta - 1)
+        signal_all(p.ep, p.ep.L.done_flag);  // every CTA's rows are visible: the combines may read them
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);

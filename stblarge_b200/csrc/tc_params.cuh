@@ -69,6 +69,7 @@ struct TcParams {
     float *partial;
     unsigned int *flags;
     unsigned int seq;          // this launch's number, never 0
+    unsigned int *ep_done_ctr; // expert parallelism, down: CTA ticket; the last CTA raises done_flag
     uint32_t *status;
 };
 
