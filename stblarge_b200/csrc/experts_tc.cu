@@ -42,11 +42,27 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
     // rows: [0, n_pos), or under expert parallelism [0, routed rows received) and the shared rows
     const int n_head = p.n_routed_dev ? min(*p.n_routed_dev, p.n_pos) : p.n_pos;
     const int rows = n_head + (p.n_routed_dev ? p.n_tail : 0);
-    for (int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w < rows * per_row; w += nw) {
+    const int items = rows * per_row;
+    // two blocks per iteration, their loads issued together (a warp may have several blocks to do
+    // when the grid is sized for the SMs rather than the rows, as under expert parallelism)
+    for (int w0 = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w0 < items; w0 += 2 * nw) {
+      uint2 xin[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int w = w0 + k * nw;
+        if (w >= items) continue;
+        int pos = w / per_row;
+        if (pos >= n_head) pos = p.n_pos + (pos - n_head);
+        xin[k] = __ldg(reinterpret_cast<const uint2 *>(p.h + (size_t)pos * p.I + (w % per_row) * 128 + 4 * lane));
+      }
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int w = w0 + k * nw;
+        if (w >= items) continue;
         int pos = w / per_row;
         const int g = w % per_row;
         if (pos >= n_head) pos = p.n_pos + (pos - n_head);
-        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(p.h + (size_t)pos * p.I + g * 128 + 4 * lane));
+        const uint2 xv = xin[k];
         const float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u), __uint_as_float(xv.y << 16),
                             __uint_as_float(xv.y & 0xffff0000u)};
         float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -64,6 +80,7 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
         } else if (lane == 0) {
             p.hs[(size_t)pos * per_row + g] = s;
         }
+      }
     }
 }
 

@@ -821,7 +821,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         HquantParams hp{m->h, m->hq, m->hs, m->routed_cap, m->I, m->n_rows, m->has_shared ? T : 0};
         void *hargs[] = {&hp};
-        launch_pdl(hquant_kernel_ptr(), dim3(m->sms), dim3(256), hargs, 0, st);
+        // two CTAs per SM: they fit beside the down kernel's CTAs, which start early (programmatic launch)
+        launch_pdl(hquant_kernel_ptr(), dim3(2 * m->sms), dim3(256), hargs, 0, st);
         launch_tc(m, false, pd, st);
         launches += 5;
     } else if (m->act_q8) {

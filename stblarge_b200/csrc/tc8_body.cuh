@@ -99,20 +99,14 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
 
     pdl_wait();
     pdl_launch_dependents();
-    if (UP && p.ep.n_ranks > 1) {
-        // every rank's payload rows must have landed in this rank's receive rows: the payload
-        // kernel before this one has finished, so raise this rank's flag everywhere, then wait for all
-        if (cta == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
-        if (tid == 0) {
-            if (!wait_flags_sys(reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.pay_flag),
-                                p.ep.n_ranks, p.ep.epoch)) {
-                abort_flag = 1;
-                atomicOr(p.status, kErrWaitTimeout);
-            }
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // the rows are read by TMA
-        }
-        __syncthreads();
-    }
+    // expert parallelism: every rank's payload rows must have landed in this rank's receive rows
+    // before they are read.  The payload kernel before this one has finished, so this rank's flag is
+    // raised everywhere now; the producer waits for all of them after it has prefetched its first
+    // weight tiles into L2 (weights do not depend on the payload), the epilogue before it reads the
+    // rows' weights and origins.
+    const bool ep_up = UP && p.ep.n_ranks > 1;
+    const unsigned int *pay_flags = ep_up ? reinterpret_cast<const unsigned int *>(p.ep.region[p.ep.rank] + p.ep.L.pay_flag) : nullptr;
+    if (ep_up && cta == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
     // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
     if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
     if (p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
@@ -138,6 +132,28 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         if (lane == 0) {
             int q = 0;  // running stage counter
             bool stop = false;
+            if (ep_up) {
+                // the weight tiles of the first stages into L2 while the other ranks' payload arrives
+                int n_pf = 0;
+                for (int it = lo; it < hi && n_pf < 2 * nst; it++) {
+                    const int c = p.chunk_begin + it / tiles, tile = it % tiles;
+                    const TcChunk ch = chunk_of(c);
+                    const bool shared = ch.e == p.E;
+                    const int z = shared ? 0 : expert_slot(p, ch.e);
+                    int ka, kz;
+                    k_range(it, ka, kz);
+                    for (int kb = ka; kb < kz && n_pf < 2 * nst; kb++, n_pf++)
+#pragma unroll
+                        for (int m = 0; m < 2; m++)
+                            tma_prefetch_l2_3d(shared ? &maps.s[m] : &maps.w[m], kb * 128, T2 ? tile * 128 : tile * 64, z);
+                }
+                if (!wait_flags_sys(pay_flags, p.ep.n_ranks, p.ep.epoch)) {
+                    abort_flag = 1;
+                    atomicOr(p.status, kErrWaitTimeout);
+                    stop = true;
+                }
+                asm volatile("fence.proxy.async.global;" ::: "memory");  // the rows are read by TMA
+            }
             for (int it = lo; it < hi && !stop; it++) {
                 const int c = p.chunk_begin + it / tiles, tile = it % tiles;
                 const TcChunk ch = chunk_of(c);
@@ -316,6 +332,14 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             }
         };
         int gq = 0;
+        if (ep_up) {
+            // pos_w / pos_meta of the receive rows come from the other ranks' payload kernels
+            if (et == 0 && !wait_flags_sys(pay_flags, p.ep.n_ranks, p.ep.epoch)) {
+                abort_flag = 1;
+                atomicOr(p.status, kErrWaitTimeout);
+            }
+            bar_sync(2, 128);
+        }
         if (lo < hi) {
             prefetch(lo);
             park(0);

@@ -32,6 +32,13 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// a tile into L2 only (no shared memory, no barrier): cp.async.bulk.prefetch.tensor
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
