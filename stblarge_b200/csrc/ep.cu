@@ -109,16 +109,27 @@ __global__ void __launch_bounds__(kEpCountThreads) ep_counts_kernel(EpCountsPara
         for (int s = 0; s < v.n_ranks; s++) my_tot += cnt[s * kMaxExperts + v.rank * p.E_loc + el];
     int rows_total;
     const int base = block_scan_excl<kEpCountThreads>(el < p.E_loc ? my_tot : 0, warp_tot, rows_total);
-    const int nch = el < p.E_loc ? (my_tot + p.nt_routed - 1) / p.nt_routed : 0;
+    int nt_r = p.nt_routed, nt_s = p.nt_shared;
+    if (p.adaptive_wide) {
+        // 32-token chunks when they save more than a quarter of the 16-token ones (this rank's experts)
+        int c16, c32;
+        block_scan_excl<kEpCountThreads>(el < p.E_loc ? (my_tot + 15) / 16 : 0, warp_tot, c16);
+        block_scan_excl<kEpCountThreads>(el < p.E_loc ? (my_tot + 31) / 32 : 0, warp_tot, c32);
+        if (p.has_shared) c16 += (p.T + 15) / 16, c32 += (p.T + 31) / 32;
+        const bool wide = 4 * c32 < 3 * c16;
+        if (wide) nt_r = nt_s = 32;
+        if (tid == 0) *p.wide_sel = wide;
+    }
+    const int nch = el < p.E_loc ? (my_tot + nt_r - 1) / nt_r : 0;
     int nch_total;
     const int ch0 = block_scan_excl<kEpCountThreads>(nch, warp_tot, nch_total);
-    const int ns = p.has_shared ? (p.T + p.nt_shared - 1) / p.nt_shared : 0;
+    const int ns = p.has_shared ? (p.T + nt_s - 1) / nt_s : 0;
     const bool fits = rows_total <= p.routed_cap;  // always, unless a count exchange went wrong
     if (el < p.E_loc && fits)
         for (int c = 0; c < nch; c++)
-            p.chunks[ns + ch0 + c] = Chunk{el, base + c * p.nt_routed, min(p.nt_routed, my_tot - c * p.nt_routed), 0};
+            p.chunks[ns + ch0 + c] = Chunk{el, base + c * nt_r, min(nt_r, my_tot - c * nt_r), 0};
     for (int i = tid; i < ns; i += kEpCountThreads)
-        p.chunks[i] = Chunk{p.E_loc, p.routed_cap + i * p.nt_shared, min(p.nt_shared, p.T - i * p.nt_shared), 0};
+        p.chunks[i] = Chunk{p.E_loc, p.routed_cap + i * nt_s, min(nt_s, p.T - i * nt_s), 0};
     if (tid == 0) {
         p.n_chunks[0] = ns + (fits ? nch_total : 0);
         p.n_chunks[1] = ns;

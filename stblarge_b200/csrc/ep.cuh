@@ -17,6 +17,8 @@ struct EpCountsParams {
     int *n_chunks;       // out: [0] all, [1] shared
     int *n_rows;         // out: [0] routed rows received
     unsigned int *done_ctr;  // the down kernel's CTA ticket (zeroed here, before that kernel runs)
+    int adaptive_wide;   // chunks of 32 tokens when that saves more than a quarter of the chunks
+    int *wide_sel;       // out (adaptive_wide): 1 when the chunks are of 32 tokens
     uint32_t *status;
 };
 

@@ -4,10 +4,10 @@
 
 namespace stbl {
 
-template <bool UP, bool T2>
+template <bool UP, bool T2, int NTOK>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const __grid_constant__ TcMaps maps, TcParams p,
                                                                   int nst) {
-    tc8_body<UP, T2>(maps, p, nst, blockIdx.x, gridDim.x);
+    tc8_body<UP, T2, NTOK>(maps, p, nst, blockIdx.x, gridDim.x);
 }
 
 // x codes and scales of every position (routed assignments in dispatch order, then the shared
@@ -86,24 +86,29 @@ __global__ void __launch_bounds__(256) hquant_kernel(HquantParams p) {
 
 const void *hquant_kernel_ptr() { return (const void *)hquant_kernel; }
 
-template __global__ void expert_tc_kernel<true, false>(const __grid_constant__ TcMaps, TcParams, int);
-template __global__ void expert_tc_kernel<true, true>(const __grid_constant__ TcMaps, TcParams, int);
-template __global__ void expert_tc_kernel<false, false>(const __grid_constant__ TcMaps, TcParams, int);
-template __global__ void expert_tc_kernel<false, true>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<true, false, 16>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<true, true, 16>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<false, false, 16>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<false, true, 16>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<true, true, 32>(const __grid_constant__ TcMaps, TcParams, int);
+template __global__ void expert_tc_kernel<false, true, 32>(const __grid_constant__ TcMaps, TcParams, int);
 
-// two: items of two 128-row tiles (up: 128 gate + 128 up rows; down: 256 rows of W2)
-const void *expert_tc_kernel_ptr(bool up, bool two) {
-    if (up) return two ? (const void *)expert_tc_kernel<true, true> : (const void *)expert_tc_kernel<true, false>;
-    return two ? (const void *)expert_tc_kernel<false, true> : (const void *)expert_tc_kernel<false, false>;
+// two: items of two 128-row tiles (up: 128 gate + 128 up rows; down: 256 rows of W2); wide: items of
+// up to 32 tokens (two-tile forms only)
+const void *expert_tc_kernel_ptr(bool up, bool two, bool wide) {
+    if (wide) return up ? (const void *)expert_tc_kernel<true, true, 32> : (const void *)expert_tc_kernel<false, true, 32>;
+    if (up) return two ? (const void *)expert_tc_kernel<true, true, 16> : (const void *)expert_tc_kernel<true, false, 16>;
+    return two ? (const void *)expert_tc_kernel<false, true, 16> : (const void *)expert_tc_kernel<false, false, 16>;
 }
 
 const void *gather_kernel_ptr() { return (const void *)gather_kernel; }
 
 // dynamic shared-memory bytes of one launch (1 KB of it aligns the stages)
-int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two) {
-    const int K = up ? H : I, nkb = K / 128;
-    return nst * (two ? kStage2 : kStage) + 4 * (2 * kTcN * nkb + 4 * nkb + 128 * 17 + 10 * kTcN) + (int)sizeof(Chunk) * kTcChunks +
-           8 * (2 * nst + 2 * kTcAcc + 1) + 1024;
+int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two, bool wide) {
+    const int nkb = (up ? H : I) / 128;
+    // the layout depends on the tile count and width only (up and down differ in nkb)
+    if (wide) return Tc8<true, true, 32>::smem_bytes(nkb, nst);
+    return two ? Tc8<true, true, 16>::smem_bytes(nkb, nst) : Tc8<true, false, 16>::smem_bytes(nkb, nst);
 }
 
 }  // namespace stbl

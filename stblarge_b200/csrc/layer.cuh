@@ -50,6 +50,11 @@ struct RouterParams {
     int ksplit;
     int has_shared;
     int nt_routed, nt_shared;  // tokens per chunk of a routed / the shared expert
+    // adaptive chunking (FP8 layers, calls of more than 16 tokens): chunks of 32 tokens instead of
+    // nt_routed / nt_shared (16) when that saves more than a quarter of the chunks; the choice goes to
+    // *wide_sel (1: 32-token chunks), which the expert launches of both widths read
+    int adaptive_wide;
+    int *wide_sel;
     float *scores;           // [T][E]
     int *idx;                // [T][topk]
     float *wts;              // [T][topk]

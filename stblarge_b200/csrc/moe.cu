@@ -20,7 +20,7 @@
 
 namespace stbl {
 const void *combine_kernel_ptr();                 // combine.cu
-const void *expert_tc_kernel_ptr(bool up, bool two);  // experts_tc.cu
+const void *expert_tc_kernel_ptr(bool up, bool two, bool wide);  // experts_tc.cu
 const void *expert_tc4_kernel_ptr(bool up, bool wide);  // experts_tc4.cu
 int expert_tc4_smem_bytes(bool up, int nst, bool wide);
 int expert_tc4_partial_cols();
@@ -28,7 +28,7 @@ cudaError_t launch_sf_repack(const uint8_t *src, long long src_stride, uint8_t *
                              int z0, int nz, int rps, cudaStream_t st);
 const void *gather_kernel_ptr();                  // experts_tc.cu
 const void *hquant_kernel_ptr();                  // experts_tc.cu
-int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two);
+int expert_tc_smem_bytes(bool up, int H, int I, int nst, bool two, bool wide);
 cudaError_t launch_q8(bool up, const Q8Params &p, int sms, cudaStream_t st);  // experts_q8.cu
 }  // namespace stbl
 
@@ -76,7 +76,8 @@ struct stbl_moe {
     bool ep_connected = false;
     unsigned int ep_epoch = 0;
     int *a_dst = nullptr, *n_rows = nullptr;
-    unsigned int *ep_done_ctr = nullptr;  // expert parallelism: the down kernel's CTA ticket (ep.cu zeroes it per call)
+    unsigned int *ep_done_ctr = nullptr;
+    int *wide_sel = nullptr;  // the call's chunk width choice (1: 32 tokens), written by the router / count exchange  // expert parallelism: the down kernel's CTA ticket (ep.cu zeroes it per call)
     int *sel_cnt = nullptr;
     uint32_t *sel_bm = nullptr;
     unsigned int *sel_ticket = nullptr;
@@ -88,7 +89,7 @@ struct stbl_moe {
     uint8_t *xq_a = nullptr, *xq_b = nullptr;
     uint16_t *h = nullptr, *eo = nullptr, *sh = nullptr, *xin = nullptr, *yout = nullptr;
     uint32_t *status = nullptr;
-    float *tc_partial = nullptr;      // split-item partial sums: FP8 body [sms][128][16 or 32 (two-tile down)], then MXFP4 [sms][128][32]
+    float *tc_partial = nullptr;      // split-item partial sums: FP8 body [sms][128][<= 64], then MXFP4 [sms][128][64]
     unsigned int *tc_flags = nullptr; // [2][sms] launch number whose partial a CTA slot holds (FP8, MXFP4 bodies)
     unsigned int tc_seq = 0;
     // expert slots: routed expert e reads slot slot[e] of the strided weight arrays (an expert cache
@@ -112,6 +113,7 @@ struct stbl_moe {
     int tc_nst_up = 0, tc_nst_down = 0, tc_smem_up = 0, tc_smem_down = 0;
     int tc_nst_down2 = 0, tc_smem_down2 = 0;  // the down kernel with two-tile items (T >= 4)
     int tc_nst_up2 = 0, tc_smem_up2 = 0;      // the up kernel with two-tile items (128 gate + 128 up rows)
+    int tc_nst_upw = 0, tc_smem_upw = 0, tc_nst_downw = 0, tc_smem_downw = 0;  // two-tile items of up to 32 tokens
     TcMaps tc_up2{};                          // its maps: 128-row boxes of the gate and up matrices
     bool routed_tc = false;           // routed experts on the FP8 tensor-core kernels
     bool routed_bs = false;           // routed experts MXFP4 or FP8-e8m0: the block-scaled tensor-core kernels
@@ -131,6 +133,7 @@ struct stbl_moe {
     bool act_q8 = false;              // routed MXFP4 experts with Q8 activations (CUDA-core kernels)
     float *hd8 = nullptr;             // Q8 scales of h by position [pos][I / 32]
     CUtensorMap bmap_xa{}, bmap_xb{}, bmap_xpos{}, bmap_hq{};  // activation tiles for the tensor-core kernels
+    CUtensorMap bmap_xa32{}, bmap_xb32{}, bmap_xpos32{}, bmap_hq32{};  // the same in 32-row tiles (32-token items)
     CUtensorMap bmap4_xa{}, bmap4_xpos{}, bmap4_hq{};         // the same, two K blocks per box (MXFP4 kernels)
     CUtensorMap bmap4w_xpos{}, bmap4w_hq{};                   // 32-row boxes (MXFP4 items of up to 32 tokens)
 
@@ -241,11 +244,11 @@ CUtensorMap act_map2(const void *base, int K, int rows, int box_rows = 16) {
 }
 
 // 2-D tensor map over [rows][K] e4m3 activation codes, read in 16-row x 128-byte tiles (128B swizzle)
-CUtensorMap act_map(const void *base, int K, int rows) {
+CUtensorMap act_map(const void *base, int K, int rows, int box_rows = 16) {
     CUtensorMap m;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)K};
-    const cuuint32_t box[2] = {128, 16};
+    const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -382,11 +385,12 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->xin = carve<uint16_t>(p, (size_t)T * H);
         m->yout = carve<uint16_t>(p, (size_t)T * H);
         m->status = carve<uint32_t>(p, 4);
-        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * (32 + 64));
+        m->tc_partial = carve<float>(p, (size_t)m->sms * 128 * (64 + 64));
         m->tc_flags = carve<unsigned int>(p, 2 * m->sms);
         m->a_dst = carve<int>(p, (size_t)T * K);
         m->n_rows = carve<int>(p, 4);
         m->ep_done_ctr = carve<unsigned int>(p, 1);
+        m->wide_sel = carve<int>(p, 1);
         m->sel_cnt = carve<int>(p, Eg);
         m->sel_bm = carve<uint32_t>(p, (size_t)Eg * ((T + 31) / 32));
         m->sel_ticket = carve<unsigned int>(p, 4);
@@ -495,6 +499,10 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         m->bmap_xb = act_map(m->xq_b, H, Tpad);
         m->bmap_xpos = act_map(m->xq_pos, H, npos + kPosPad);
         m->bmap_hq = act_map(m->hq, I, npos + kPosPad);
+        m->bmap_xa32 = act_map(m->xq_a, H, Tpad, 32);
+        m->bmap_xb32 = act_map(m->xq_b, H, Tpad, 32);
+        m->bmap_xpos32 = act_map(m->xq_pos, H, npos + kPosPad, 32);
+        m->bmap_hq32 = act_map(m->hq, I, npos + kPosPad, 32);
         m->bmap4_xa = act_map2(m->xq_a, H, Tpad);
         m->bmap4_xpos = act_map2(m->xq_pos, H, npos + kPosPad);
         m->bmap4_hq = act_map2(m->hq, I, npos + kPosPad);
@@ -503,20 +511,22 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
         // stages: at least kTcBatch (4: the producer requests K blocks four at a time and first waits
         // for four free stages), at most 8 of one tile (more outstanding requests only lengthen the
         // DRAM queues, measured) or 6 of two
-        auto pick = [&](bool up, bool two, int &nst, int &smem) {
+        auto pick = [&](bool up, bool two, bool wide, int &nst, int &smem) {
             cudaFuncAttributes fa{};
-            CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up, two)));
+            CK(cudaFuncGetAttributes(&fa, expert_tc_kernel_ptr(up, two, wide)));
             const int nmax = two ? 6 : 8, nmin = 4;
             for (nst = nmax; nst >= nmin; nst--)
-                if (expert_tc_smem_bytes(up, H, I, nst, two) + (int)fa.sharedSizeBytes <= max_smem) break;
+                if (expert_tc_smem_bytes(up, H, I, nst, two, wide) + (int)fa.sharedSizeBytes <= max_smem) break;
             if (nst < nmin) throw std::runtime_error("tensor-core expert kernel does not fit in shared memory");
-            smem = expert_tc_smem_bytes(up, H, I, nst, two);
-            CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up, two), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            smem = expert_tc_smem_bytes(up, H, I, nst, two, wide);
+            CK(cudaFuncSetAttribute(expert_tc_kernel_ptr(up, two, wide), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         };
-        pick(true, false, m->tc_nst_up, m->tc_smem_up);
-        pick(true, true, m->tc_nst_up2, m->tc_smem_up2);
-        pick(false, false, m->tc_nst_down, m->tc_smem_down);
-        pick(false, true, m->tc_nst_down2, m->tc_smem_down2);
+        pick(true, false, false, m->tc_nst_up, m->tc_smem_up);
+        pick(true, true, false, m->tc_nst_up2, m->tc_smem_up2);
+        pick(false, false, false, m->tc_nst_down, m->tc_smem_down);
+        pick(false, true, false, m->tc_nst_down2, m->tc_smem_down2);
+        pick(true, true, true, m->tc_nst_upw, m->tc_smem_upw);
+        pick(false, true, true, m->tc_nst_downw, m->tc_smem_downw);
         if (m->routed_bs) {
             // the MXFP4 launch runs both bodies (MXFP4 routed, FP8 shared): as many stages of each as
             // fit; a MXFP4 stage is one 256-K unit of two 128-row tiles (71 KB with 16-token items, 75
@@ -530,9 +540,9 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
                     int n4 = 6, n8 = 6;
                     const int n8min = 4;
                     while (n4 >= 2 && expert_tc4_smem_bytes(up, n4, wide) > room) n4--;
-                    while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, true) > room) n8--;
+                    while (n8 >= n8min && expert_tc_smem_bytes(up, H, I, n8, true, false) > room) n8--;
                     if (n4 < 2 || n8 < n8min) throw std::runtime_error("MXFP4 tensor-core expert kernel does not fit in shared memory");
-                    const int smem = std::max(expert_tc4_smem_bytes(up, n4, wide), expert_tc_smem_bytes(up, H, I, n8, true));
+                    const int smem = std::max(expert_tc4_smem_bytes(up, n4, wide), expert_tc_smem_bytes(up, H, I, n8, true, false));
                     CK(cudaFuncSetAttribute(expert_tc4_kernel_ptr(up, wide), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
                     m->tc4_nst[up][wide] = n4, m->tc4_nst8[up][wide] = n8, m->tc4_smem[up][wide] = smem;
                 }
@@ -658,10 +668,22 @@ void launch_hquant(stbl_moe *m, int pos_begin, int pos_end, cudaStream_t st) {
     launch_pdl(hquant_kernel_ptr(), dim3((warps + 7) / 8), dim3(256), args, 0, st);
 }
 
-// Block-scaled (MXFP4 / FP8-e8m0) routed experts take items of up to 32 tokens in calls of more than
-// 16 tokens (their chunks are read by position then): an expert routed to by 17-32 of the call's tokens
-// streams its weights once, not twice.  The router builds its chunks to match.
-bool tc4_wide(const stbl_moe *m, int T) { return m->routed_bs && !m->act_q8 && T > 16; }
+// Chunk widths of calls of more than 16 tokens (their chunks are read by position then).
+//  * Block-scaled (MXFP4 / FP8-e8m0) routed experts, and a block-scaled shared expert, always take
+//    items of up to 32 tokens: an expert routed to by 17-32 of the call's tokens streams its weights
+//    once, not twice.
+//  * FP8 layers choose on the device, per call (the router, or under expert parallelism the count
+//    exchange): 32-token chunks when they save more than a quarter of the 16-token ones (experts with
+//    many tokens, e.g. skewed routing), else 16 (the 16-token launch is faster when experts have few
+//    tokens: its TMEM holds twice as many K blocks ahead of the epilogue).  Both launches of each
+//    product are enqueued; the one not chosen takes no items.
+//  * An FP8 shared expert inside the MXFP4 launch, and the shared expert of a Q8 layer, keep 16.
+//  * Q8 routed experts keep their own 8-token chunks.
+bool wide_call(int T) { return T > 16; }
+bool tc4_wide(const stbl_moe *m, int T) { return m->routed_bs && !m->act_q8 && wide_call(T); }
+bool fp8_adaptive(const stbl_moe *m, int T) { return m->routed_tc && wide_call(T); }
+int routed_chunk_tokens(const stbl_moe *m, int T) { return m->act_q8 ? kQ8ChunkTokens : tc4_wide(m, T) ? 32 : 16; }
+int shared_chunk_tokens(const stbl_moe *m, int T) { return tc4_wide(m, T) && m->shared_bs ? 32 : 16; }
 
 // up items of 128 gate + 128 up rows from this many tokens on (the up kernel's two-tile form).
 // Measured on one GPU: cfg2 T=16 up 407 -> 351 us, cfg4 T=256 layer 2.29 -> 2.07 ms; at T=1 the
@@ -669,9 +691,24 @@ bool tc4_wide(const stbl_moe *m, int T) { return m->routed_bs && !m->act_q8 && T
 // 1.198 ms per step.
 constexpr int kUpTwoMinT = 4;
 
-void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
+// adaptive (fp8_adaptive): enqueue the 16-token launch and the 32-token one; each runs only if the
+// device chose its width for this call (TcParams::sel).  Returns the launches enqueued.
+int launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st, bool adaptive = false) {
     const bool up2 = up && p.T >= kUpTwoMinT;
     TcMaps maps = up ? (up2 ? m->tc_up2 : m->tc_up) : m->tc_down;
+    if (adaptive) {
+        // the 32-token form (two-tile items; T > 16 implies them), after the 16-token one below
+        TcMaps mw = maps;
+        if (up) mw.b = p.b_direct ? (m->routed_tc ? m->bmap_xa32 : m->bmap_xb32) : m->bmap_xpos32;
+        else mw.b = m->bmap_hq32;
+        TcParams pw = p;
+        p.sel = pw.sel = m->wide_sel;
+        p.sel_val = 0, pw.sel_val = 1;
+        launch_tc(m, up, p, st);
+        void *args[] = {&mw, &pw, up ? &m->tc_nst_upw : &m->tc_nst_downw};
+        launch_pdl(expert_tc_kernel_ptr(up, true, true), dim3(m->sms), dim3(192), args, up ? m->tc_smem_upw : m->tc_smem_downw, st);
+        return 2;
+    }
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
     // down items of two 128-row tiles from T = 4 on (measured at 256 experts, down kernel: T=16 218 ->
@@ -679,8 +716,9 @@ void launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st) {
     // too (the epilogue stores each tile's rows into the source ranks' eo rows)
     const bool two = up ? up2 : p.T >= 4;
     void *args[] = {&maps, &p, up ? (two ? &m->tc_nst_up2 : &m->tc_nst_up) : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
-    launch_pdl(expert_tc_kernel_ptr(up, two), dim3(m->sms), dim3(192), args,
+    launch_pdl(expert_tc_kernel_ptr(up, two, false), dim3(m->sms), dim3(192), args,
                up ? (two ? m->tc_smem_up2 : m->tc_smem_up) : (two ? m->tc_smem_down2 : m->tc_smem_down), st);
+    return 1;
 }
 
 // the MXFP4 launch: p4 the routed MXFP4 chunks, p8 the FP8 shared expert's chunks (none: an empty range).
@@ -692,7 +730,7 @@ void launch_tc4(stbl_moe *m, bool up, TcParams p8, TcParams p4, bool wide, cudaS
     if (wide) maps4.b = up ? m->bmap4w_xpos : m->bmap4w_hq;
     else maps4.b = up ? (p4.b_direct ? m->bmap4_xa : m->bmap4_xpos) : m->bmap4_hq;
     p4.flags = m->tc_flags + m->sms;
-    p4.partial = m->tc_partial + (size_t)m->sms * 128 * 32;
+    p4.partial = m->tc_partial + (size_t)m->sms * 128 * 64;
     int *n8 = &m->tc4_nst8[up][wide], *n4 = &m->tc4_nst[up][wide];
     void *args[] = {&maps8, &p8, n8, &maps4, &p4, n4};
     launch_pdl(expert_tc4_kernel_ptr(up, wide), dim3(m->sms), dim3(192), args, m->tc4_smem[up][wide], st);
@@ -767,8 +805,10 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
     else r.xq_b = m->xq_b, r.xs_b = m->xs_b, r.blk_b = act_blk_of(fs), r.pow2_b = act_pow2_of(fs);
     r.xe8_a = m->routed_bs && !m->act_q8 ? m->xe8_a : nullptr;
     r.xe8_rows = m->Tpad;
-    r.nt_routed = m->act_q8 ? kQ8ChunkTokens : tc4_wide(m, T) ? 32 : 16;
-    r.nt_shared = tc4_wide(m, T) && m->shared_bs ? 32 : 16;  // an FP8 128x128 shared expert keeps 16
+    r.nt_routed = routed_chunk_tokens(m, T);
+    r.nt_shared = shared_chunk_tokens(m, T);
+    r.adaptive_wide = fp8_adaptive(m, T);
+    r.wide_sel = m->wide_sel;
     r.sel_cnt = m->sel_cnt, r.sel_bm = m->sel_bm, r.sel_ticket = m->sel_ticket;
     r.status = m->status;
     r.forced_idx = forced;
@@ -803,7 +843,9 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         cpp.ep = ep_view(m);
         cpp.counts = m->counts, cpp.offsets = m->offsets, cpp.perm = m->perm, cpp.idx = m->idx;
         cpp.T = T, cpp.topk = m->K, cpp.E = m->E, cpp.E_loc = m->E_loc;
-        cpp.nt_routed = 16, cpp.nt_shared = 16, cpp.has_shared = m->has_shared, cpp.routed_cap = m->routed_cap;
+        cpp.nt_routed = routed_chunk_tokens(m, T), cpp.nt_shared = shared_chunk_tokens(m, T);
+        cpp.adaptive_wide = fp8_adaptive(m, T), cpp.wide_sel = m->wide_sel;
+        cpp.has_shared = m->has_shared, cpp.routed_cap = m->routed_cap;
         cpp.a_dst = m->a_dst, cpp.chunks = m->chunks, cpp.n_chunks = m->n_chunks, cpp.n_rows = m->n_rows;
         cpp.done_ctr = m->ep_done_ctr;
         cpp.status = m->status;
@@ -817,20 +859,20 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         TcParams pu = tc_params(m, T, true, false), pd = tc_params(m, T, false);
         pu.chunk_begin = pd.chunk_begin = 0;
         pu.chunk_end = pd.chunk_end = -1;
-        launch_tc(m, true, pu, st);
+        launches += launch_tc(m, true, pu, st, fp8_adaptive(m, T));
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         HquantParams hp{m->h, m->hq, m->hs, m->routed_cap, m->I, m->n_rows, m->has_shared ? T : 0};
         void *hargs[] = {&hp};
         // two CTAs per SM: they fit beside the down kernel's CTAs, which start early (programmatic launch)
         launch_pdl(hquant_kernel_ptr(), dim3(2 * m->sms), dim3(256), hargs, 0, st);
-        launch_tc(m, false, pd, st);
-        launches += 5;
+        launches += launch_tc(m, false, pd, st, fp8_adaptive(m, T));
+        launches += 3;
     } else if (m->act_q8) {
         // routed MXFP4 experts x Q8 activations on the CUDA cores (chunks of <= 8 tokens); the FP8
         // shared expert on the tensor cores (its chunks, first in the table, read x by token):
         // [shared up] -> routed up (+ SwiGLU, Q8 of h) -> [hquant of the shared rows] -> [shared down]
         // -> routed down -> combine
-        const int ns = m->has_shared ? (T + 15) / 16 : 0;
+        const int ns = m->has_shared ? (T + shared_chunk_tokens(m, T) - 1) / shared_chunk_tokens(m, T) : 0;
         if (ns) {
             TcParams su = tc_params(m, T, true, true);
             su.chunk_begin = 0, su.chunk_end = ns;
@@ -850,7 +892,8 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         CK(launch_q8(false, q8_params(m, T, false), m->sms, st));
         launches++;
     } else if (m->routed_tc) {
-        // every expert on the tensor cores: [gather] -> up -> hquant -> down -> combine
+        // every expert on the tensor cores: [gather] -> up (16- and 32-token launches when the
+        // width is chosen on the device) -> hquant -> down (likewise) -> combine
         const bool direct = T <= 16;
         if (!direct) {
             launch_gather(m, T, st);
@@ -859,19 +902,19 @@ void forward(stbl_moe *m, const void *x, int T, void *y, cudaStream_t st, const 
         TcParams pu = tc_params(m, T, true, direct), pd = tc_params(m, T, false);
         pu.chunk_begin = pd.chunk_begin = 0;
         pu.chunk_end = pd.chunk_end = -1;
-        launch_tc(m, true, pu, st);
+        launches += launch_tc(m, true, pu, st, fp8_adaptive(m, T));
         if (m->timing) CK(cudaEventRecord(tc.ev[2], st));
         launch_hquant(m, 0, npos, st);
-        launch_tc(m, false, pd, st);
-        launches += 3;
+        launches += launch_tc(m, false, pd, st, fp8_adaptive(m, T));
+        launches += 1;
     } else {
         // routed experts MXFP4 or FP8-e8m0 on the block-scaled tensor cores.  An FP8 128x128 shared
-        // expert (its chunks read x by token, as 16 consecutive tokens, at any T) runs on a share of the
+        // expert (its chunks read x by token, as 16 or 32 consecutive tokens, at any T) runs on a share of the
         // same launches' CTAs; an FP8-e8m0 shared expert is one more set of chunks of the block-scaled
         // body.  [gather] -> up (h quantized per 32 in its epilogue for every block-scaled row) ->
         // [hquant per 128 of the FP8 128x128 shared rows] -> down -> combine
         const bool direct = T <= 16;
-        const int ns = m->has_shared ? (T + 15) / 16 : 0;
+        const int ns = m->has_shared ? (T + shared_chunk_tokens(m, T) - 1) / shared_chunk_tokens(m, T) : 0;
         const int n8 = m->shared_bs ? 0 : ns;  // chunks of the FP8 128x128 body (the shared expert's, first)
         if (!direct) {
             launch_gather(m, T, st);

@@ -508,7 +508,8 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
     __shared__ int is_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = p.E, T = p.T, K = p.topk;
-    const int sh_r = __ffs(p.nt_routed) - 1, sh_s = __ffs(p.nt_shared) - 1;  // chunk sizes: powers of two
+    int sh_r = __ffs(p.nt_routed) - 1, sh_s = __ffs(p.nt_shared) - 1;  // chunk sizes: powers of two
+    __shared__ int s_wide;
     const int t0 = blockIdx.x * kSelTokensPerCta, n_own = min(kSelTokensPerCta, T - t0);
     int *s_idx = reinterpret_cast<int *>(smem);        // [16][K] (first pass)
     int *s_cnt = s_idx + kSelTokensPerCta * K;         // [E] (first pass)
@@ -573,6 +574,24 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
         // the expert's tokens (the expert's token bitmap).
         const int n = live ? T : n_own;
         const int *sel = live ? p.idx : s_idx;
+        if (live && p.adaptive_wide) {
+            // 32-token chunks when they save more than a quarter of the 16-token ones (one item then
+            // streams an expert's weights for up to 32 tokens; with few tokens per expert the 16-token
+            // launch is faster)
+            if (warp == 0) {
+                int c16 = 0, c32 = 0;
+                for (int e = lane; e < E; e += 32) c16 += (cnt[e] + 15) >> 4, c32 += (cnt[e] + 31) >> 5;
+                if (p.has_shared) c16 += lane == 0 ? (T + 15) >> 4 : 0, c32 += lane == 0 ? (T + 31) >> 5 : 0;
+                for (int o = 16; o > 0; o >>= 1) c16 += __shfl_xor_sync(0xffffffffu, c16, o), c32 += __shfl_xor_sync(0xffffffffu, c32, o);
+                if (lane == 0) {
+                    s_wide = 4 * c32 < 3 * c16;
+                    *p.wide_sel = s_wide;
+                }
+            }
+            __syncthreads();
+            if (s_wide) sh_r = 5, sh_s = 5;
+        }
+        const int nt_r = 1 << sh_r, nt_s = 1 << sh_s;
         if (warp == 0) {
             const int epl = (E + 31) / 32, e0 = lane * epl;
             int run = 0;
@@ -580,7 +599,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
                 const int e = e0 + i;
                 if (e < E) {
                     const int c = cnt[e];
-                    run += c | (((c + p.nt_routed - 1) >> sh_r) << 16);
+                    run += c | (((c + nt_r - 1) >> sh_r) << 16);
                 }
             }
             int incl = run;
@@ -595,7 +614,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
                 if (e < E) {
                     pk[e] = acc;
                     const int c = cnt[e];
-                    acc += c | (((c + p.nt_routed - 1) >> sh_r) << 16);
+                    acc += c | (((c + nt_r - 1) >> sh_r) << 16);
                 }
             }
         }
@@ -607,19 +626,19 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterParams
             for (int w = 0; w < (t >> 5); w++) rank += __popc(row[w]);
             if (live) p.perm[(pk[e] & 0xffff) + rank] = a;
         }
-        const int ns = p.has_shared ? (T + p.nt_shared - 1) >> sh_s : 0;
+        const int ns = p.has_shared ? (T + nt_s - 1) >> sh_s : 0;
         if (live) {
             for (int i = tid; i < ns; i += kSelThreads)
-                p.chunks[i] = Chunk{E, T * K + (i << sh_s), min(p.nt_shared, T - (i << sh_s)), 0};
+                p.chunks[i] = Chunk{E, T * K + (i << sh_s), min(nt_s, T - (i << sh_s)), 0};
             for (int e = tid; e < E; e += kSelThreads) {
                 const int c_e = cnt[e], off = pk[e] & 0xffff, ch = pk[e] >> 16;
                 p.counts[e] = c_e;
                 p.offsets[e] = off;
                 for (int c = 0; (c << sh_r) < c_e; c++)
-                    p.chunks[ns + ch + c] = Chunk{e, off + (c << sh_r), min(p.nt_routed, c_e - (c << sh_r)), 0};
+                    p.chunks[ns + ch + c] = Chunk{e, off + (c << sh_r), min(nt_r, c_e - (c << sh_r)), 0};
                 if (e == E - 1) {
                     p.offsets[E] = T * K;
-                    p.n_chunks[0] = ns + ch + ((c_e + p.nt_routed - 1) >> sh_r);
+                    p.n_chunks[0] = ns + ch + ((c_e + nt_r - 1) >> sh_r);
                     p.n_chunks[1] = ns;
                 }
             }

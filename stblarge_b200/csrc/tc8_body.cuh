@@ -1,7 +1,10 @@
 // FP8 128x128-block expert products on the 5th-generation tensor cores: the per-CTA body shared by
 // the FP8 expert kernel (experts_tc.cu) and the mixed MXFP4 + FP8 kernel (experts_tc4.cu).
 //
-// Work item: (chunk of <= 16 tokens of one expert, output tile), nkb = K / 128 blocks of K each.
+// Work item: (chunk of <= NTOK tokens of one expert, output tile), nkb = K / 128 blocks of K each;
+// NTOK = 16, or 32 in calls of more than 16 tokens (two-tile items only: an expert routed to by 17-32
+// tokens then streams its weights once; its TMEM holds two accumulator groups instead of four, and
+// its activation scales are parked in one buffer so that six stages still fit).
 // One persistent CTA per SM takes an equal contiguous range of the (item, K block) units, so no SM
 // idles while others finish a last item.  An item cut by a range boundary is finished by the CTA
 // holding its first K block (which reaches it last, at the end of its range): the CTAs whose ranges
@@ -36,24 +39,44 @@ namespace stbl {
 
 constexpr int kTcThreads = 192;
 constexpr int kTcG = 4;           // 128-K blocks per accumulator group (one TMEM read per group)
-constexpr int kTcGroups = 4;      // accumulator groups in TMEM (4 x 4 x 16 columns)
-constexpr int kTcAcc = kTcGroups;
-constexpr int kTcTmemCols = kTcGroups * kTcG * kTcN;
-constexpr int kATile = 128 * 128;
-constexpr int kBTile = kTcN * 128;
-constexpr int kStage = kATile + kBTile;  // 18 KB, a multiple of the 1 KB swizzle atom
-constexpr int kStage2 = 2 * kATile + kBTile;  // T2 (two down tiles): 34 KB
-constexpr int kTcPre = 8;         // activation scales prefetched per epilogue thread (16 x nkb <= 1024)
+constexpr int kTcGroups = 4;      // accumulator groups in TMEM with 16-token items (4 x 4 x 16 columns per tile)
+constexpr int kATile = 128 * 128; // one 128-row x 128-byte weight tile (a multiple of the 1 KB swizzle atom)
 constexpr int kTcChunks = 192;    // chunk entries [chunk_begin, +192) kept in shared memory (one per thread)
 constexpr int kTcBatch = 4;       // K blocks requested back to back (512 contiguous bytes of a weight row)
 
+// Shapes and shared-memory layout of one body instance (T2: two weight tiles per item; NTOK: token
+// columns per item).  The 16-token layout is the one the single-width body always had.
+template <bool UP, bool T2, int NTOK>
+struct Tc8 {
+    static_assert(NTOK == 16 || (NTOK == 32 && T2), "32-token items exist in the two-tile forms only");
+    static constexpr bool WIDE = NTOK > 16;
+    static constexpr int NT = T2 ? 2 : 1;                    // weight tiles per item
+    static constexpr int GROUPS = WIDE ? 2 : kTcGroups;      // accumulator groups in TMEM
+    static constexpr int BTILE = NTOK * 128;                 // one K block of activations
+    static constexpr int STAGE = NT * kATile + BTILE;        // 18 / 34 / 36 KB
+    static constexpr int TMEM_COLS = NT * GROUPS * kTcG * NTOK;
+    static constexpr int SXB = WIDE ? 1 : 2;                 // buffers of parked activation scales
+    static constexpr int XACC = WIDE ? 0 : 128 * 17;         // item sums (single-tile up items)
+    static constexpr int CHUNKS = WIDE ? 16 : kTcChunks;     // chunk entries kept in shared memory
+    static constexpr int PRE = NTOK * 64 / 128;              // activation scales a thread prefetches (nkb <= 64)
+    // dynamic shared-memory bytes (1 KB of it aligns the stages)
+    __host__ __device__ static constexpr int smem_bytes(int nkb, int nst) {
+        return nst * STAGE + 4 * (SXB * NTOK * nkb + 4 * nkb + XACC + 10 * NTOK) + (int)sizeof(Chunk) * CHUNKS +
+               8 * (2 * nst + 2 * GROUPS + 1) + 1024;
+    }
+};
+static_assert(Tc8<true, true, 16>::TMEM_COLS == 512 && Tc8<true, true, 32>::TMEM_COLS == 512 &&
+              Tc8<true, false, 16>::TMEM_COLS == 256, "TMEM allocations");
+
 // One CTA's share of an FP8 expert launch: CTA `cta` of the `ncta` that run this body (in a mixed
 // launch these number themselves 0..ncta-1).
-template <bool UP, bool T2 = false>
+template <bool UP, bool T2 = false, int NTOK = 16>
 __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, int nst, int cta, int ncta) {
-    constexpr int NT = T2 ? 2 : 1;                       // weight tiles per item
-    constexpr int STAGE = T2 ? kStage2 : kStage;
-    constexpr int TMEM_COLS = NT * kTcTmemCols;
+    using L = Tc8<UP, T2, NTOK>;
+    constexpr int NT = L::NT;                            // weight tiles per item
+    constexpr int STAGE = L::STAGE;
+    constexpr int TMEM_COLS = L::TMEM_COLS;
+    constexpr int GROUPS = L::GROUPS;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int K = UP ? p.H : p.I;            // reduction length
@@ -61,24 +84,30 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     const int nkb = K / 128;
     const int tiles = UP ? (T2 ? rows / 128 : rows / 64) : rows / (128 * NT);
     unsigned char *stages = smem;                                         // [nst][A tile(s) | B tile]
-    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * STAGE);  // [2][16][nkb] activation scales
-    float *sw = sx + 2 * kTcN * nkb;                                      // [2][2][nkb] weight scales
-    float *xacc = sw + 4 * nkb;                                           // [128][17] item sums
-    float *slot_w = xacc + 128 * 17;                                      // [2][16] routing weights
-    int *slot_col = reinterpret_cast<int *>(slot_w + 2 * kTcN);           // [2][16] B column of a slot
-    int *slot_dst = slot_col + 2 * kTcN;                                  // [2][16] output row of a slot
-    int *col_dst = slot_dst + 2 * kTcN;                                   // [2][16] up T2: h row of a column (-1: none)
-    float *col_w = reinterpret_cast<float *>(col_dst + 2 * kTcN);         // [2][16] up T2: routing weight of a column
-    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * kTcN);            // [kTcChunks] from chunk_begin
-    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + kTcChunks);
+    float *sx = reinterpret_cast<float *>(stages + (size_t)nst * STAGE);  // [SXB][NTOK][nkb] activation scales
+    float *sw = sx + L::SXB * NTOK * nkb;                                 // [2][2][nkb] weight scales
+    float *xacc = sw + 4 * nkb;                                           // [128][17] item sums (XACC)
+    float *slot_w = xacc + L::XACC;                                       // [2][NTOK] routing weights
+    int *slot_col = reinterpret_cast<int *>(slot_w + 2 * NTOK);           // [2][NTOK] B column of a slot
+    int *slot_dst = slot_col + 2 * NTOK;                                  // [2][NTOK] output row of a slot
+    int *col_dst = slot_dst + 2 * NTOK;                                   // [2][NTOK] up T2: h row of a column (-1: none)
+    float *col_w = reinterpret_cast<float *>(col_dst + 2 * NTOK);         // [2][NTOK] up T2: routing weight of a column
+    Chunk *ctab = reinterpret_cast<Chunk *>(col_w + 2 * NTOK);            // [CHUNKS] from chunk_begin
+    uint64_t *full = reinterpret_cast<uint64_t *>(ctab + L::CHUNKS);
     uint64_t *empty = full + nst;
     uint64_t *acc_full = empty + nst;
-    uint64_t *acc_empty = acc_full + kTcAcc;
-    uint64_t *mma_done = acc_empty + kTcAcc;
+    uint64_t *acc_empty = acc_full + GROUPS;
+    uint64_t *mma_done = acc_empty + GROUPS;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag, s_chunk_end;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (p.sel) {
+        // one of two launches of different widths: the one the device did not choose for this call
+        // returns before it allocates anything (the chosen one then sets up after the wait)
+        pdl_wait();
+        if (*(volatile const int *)p.sel != p.sel_val) return;
+    }
     if (tid == 32) {
         // the tensor maps are kernel parameters: fetch their descriptors while the previous kernel drains
         for (int m = 0; m < 2; m++) tma_prefetch_map(&maps.w[m]), tma_prefetch_map(&maps.s[m]);
@@ -87,7 +116,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     if (tid == 0) {
         abort_flag = 0;
         for (int s = 0; s < nst; s++) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
-        for (int a = 0; a < kTcAcc; a++) mbar_init(&acc_full[a], 1), mbar_init(&acc_empty[a], 128);
+        for (int a = 0; a < GROUPS; a++) mbar_init(&acc_full[a], 1), mbar_init(&acc_empty[a], 128);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -109,7 +138,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     if (ep_up && cta == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
     // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
     if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
-    if (p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    if (tid < L::CHUNKS && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
     __syncthreads();
     const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
@@ -123,8 +152,8 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     };
     // chunks beyond the shared-memory table are read from global memory
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - p.chunk_begin < kTcChunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
-        return tc_check(p, ch);
+        const Chunk ch = (c - p.chunk_begin < L::CHUNKS) ? ctab[c - p.chunk_begin] : p.chunks[c];
+        return tc_check(p, ch, NTOK);
     };
 
     if (warp == 0) {
@@ -210,15 +239,19 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f8_f32(128, kTcN);
             int q = 0, gq = 0;
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {
                 int ka, kz;
                 k_range(it, ka, kz);
+                // 32-token items: a chunk of at most 16 tokens takes N = 16 MMAs, its K blocks packed 16
+                // columns apart (the 16-token layout), so the epilogue reads and scales 16 columns
+                const bool half = L::WIDE && chunk_of(p.chunk_begin + it / tiles).n <= 16;
+                const uint32_t idesc = idesc_f8_f32(128, half ? 16 : NTOK);
+                const int bcols = half ? 16 : NTOK;  // TMEM columns between K blocks
                 for (int kb0 = ka; kb0 < kz && !stop; kb0 += kTcG, gq++) {
-                    const int g = gq % kTcGroups;
-                    if (!mbar_wait(&acc_empty[g], ((gq / kTcGroups) & 1) ^ 1, &abort_flag)) {
+                    const int g = gq % GROUPS;
+                    if (!mbar_wait(&acc_empty[g], ((gq / GROUPS) & 1) ^ 1, &abort_flag)) {
                         stop = true;
                         break;
                     }
@@ -231,10 +264,10 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                         }
                         tc_fence_after();
                         const unsigned char *a = stages + (size_t)s * STAGE;
-                        // accumulator of (group g, K block u, tile m): columns ((g NT + m) kTcG + u) kTcN
+                        // accumulator of (group g, K block u, tile m): columns (g NT + m) kTcG NTOK + u bcols
 #pragma unroll
                         for (int m = 0; m < NT; m++) {
-                            const uint32_t d = tmem + (uint32_t)(((g * NT + m) * kTcG + u) * kTcN);
+                            const uint32_t d = tmem + (uint32_t)((g * NT + m) * kTcG * NTOK + u * bcols);
 #pragma unroll
                             for (int k = 0; k < 4; k++)
                                 umma_f8(d, sw128_desc(a + m * kATile + 32 * k), sw128_desc(a + NT * kATile + 32 * k), idesc, k > 0);
@@ -266,7 +299,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
         const int row = 32 * (warp & 3) + lane;    // TMEM lane = tile row
         const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         const int nsw = (UP ? 2 : NT) * nkb;
-        float px[kTcPre];
+        float px[L::PRE];
         float pw = 0.f;
         int pcol = 0, pdst = 0;
         float pwt = 0.f;
@@ -280,10 +313,10 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             const int brow = b_row(p, ch);
             const int bvalid = p.b_direct && !shared ? p.T : ch.n;
 #pragma unroll
-            for (int k = 0; k < kTcPre; k++) {
+            for (int k = 0; k < L::PRE; k++) {
                 const int u = et + 128 * k;
                 const int j = u / nkb, kb = u % nkb;
-                px[k] = (u < kTcN * nkb && j < bvalid) ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
+                px[k] = (u < NTOK * nkb && j < bvalid) ? __ldg(p.act_s + (size_t)(brow + j) * p.act_s_stride + kb) : 0.f;
             }
             if (et < nsw) {
                 // up: the gate (m 0) and up (m 1) scales of the tile's 128-row block; down: tile m's block
@@ -293,7 +326,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 const float *base = shared ? p.s_scale[mat] : p.w_scale[mat] + (size_t)expert_slot(p, ch.e) * p.w_scale_stride;
                 pw = __ldg(base + (size_t)rblk * nkb + kb);
             }
-            if (et < kTcN) {
+            if (et < NTOK) {
                 const int pos = ch.pos0 + et;
                 pcol = et, pdst = pos, pwt = 1.f;
                 pval = et < ch.n;
@@ -316,19 +349,22 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 }
             }
         };
+        // (one buffer of activation scales with 32-token items: every thread has finished reading the
+        // current item's when park runs, after the accumulation's closing barrier)
         auto park = [&](int buf) {
+            const int bx = L::SXB > 1 ? buf : 0;
 #pragma unroll
-            for (int k = 0; k < kTcPre; k++) {
+            for (int k = 0; k < L::PRE; k++) {
                 const int u = et + 128 * k;
-                if (u < kTcN * nkb) sx[buf * kTcN * nkb + u] = px[k];
+                if (u < NTOK * nkb) sx[bx * NTOK * nkb + u] = px[k];
             }
             if (et < nsw) sw[buf * 2 * nkb + et] = pw;
-            if (et < kTcN) slot_col[buf * kTcN + et] = pcol, slot_dst[buf * kTcN + et] = pdst, slot_w[buf * kTcN + et] = pwt;
+            if (et < NTOK) slot_col[buf * NTOK + et] = pcol, slot_dst[buf * NTOK + et] = pdst, slot_w[buf * NTOK + et] = pwt;
             if (UP && T2) {
                 // the same by column (every column at most once: a token meets an expert at most once)
-                if (et < kTcN) col_dst[buf * kTcN + et] = -1;
+                if (et < NTOK) col_dst[buf * NTOK + et] = -1;
                 bar_sync(2, 128);
-                if (et < kTcN && pval) col_dst[buf * kTcN + pcol] = pdst, col_w[buf * kTcN + pcol] = pwt;
+                if (et < NTOK && pval) col_dst[buf * NTOK + pcol] = pdst, col_w[buf * NTOK + pcol] = pwt;
             }
         };
         int gq = 0;
@@ -350,40 +386,75 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             const int c = p.chunk_begin + it / tiles, tile = it % tiles;
             const TcChunk ch = chunk_of(c);
             if (!ch.ok && et == 0) atomicOr(p.status, kErrBadTable);
+            const bool half = L::WIDE && ch.n <= 16;  // the MMA issuer's choice for this item
             if (it + 1 < hi) prefetch(it + 1);
-            const float *sxb = sx + buf * kTcN * nkb, *swb = sw + buf * 2 * nkb;
+            const float *sxb = sx + (L::SXB > 1 ? buf : 0) * NTOK * nkb, *swb = sw + buf * 2 * nkb;
             const int mrow = UP ? (row >> 6) : 0;  // up: rows 64..127 are the up matrix
-            float acc2[NT][kTcN];                  // the item's sums, per weight tile
+            float acc2[NT][NTOK];                  // the item's sums, per weight tile
 #pragma unroll
             for (int m = 0; m < NT; m++)
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) acc2[m][j] = 0.f;
+                for (int j = 0; j < NTOK; j++) acc2[m][j] = 0.f;
             float *acc = acc2[0];
             bool ok = true;
             int ka, kz;
             k_range(it, ka, kz);
             for (int kb0 = ka; kb0 < kz; kb0 += kTcG, gq++) {
-                const int g = gq % kTcGroups;
-                if (!mbar_wait(&acc_full[g], (gq / kTcGroups) & 1, &abort_flag)) {
+                const int g = gq % GROUPS;
+                if (!mbar_wait(&acc_full[g], (gq / GROUPS) & 1, &abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                if (L::WIDE && half) {
+                    // a chunk of at most 16 tokens in a 32-token launch: four blocks of 16 columns per
+                    // tile, two per 32-column read
+#pragma unroll
+                    for (int m = 0; m < NT; m++) {
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            float d[32];
+                            tmem_ld32(tl + (uint32_t)((g * NT + m) * kTcG * NTOK + 32 * h), d);
+                            if (m == NT - 1 && h == 1) {
+                                tc_fence_before();
+                                mbar_arrive(&acc_empty[g]);
+                            }
+#pragma unroll
+                            for (int uu = 0; uu < 2; uu++) {
+                                const int kb = kb0 + 2 * h + uu;
+                                if (kb < kz) {
+                                    const float wsc = swb[m * nkb + kb];
+#pragma unroll
+                                    for (int j = 0; j < 16; j++) acc2[m][j] = fmaf(d[uu * 16 + j], wsc * sxb[j * nkb + kb], acc2[m][j]);
+                                }
+                            }
+                        }
+                    }
+                    continue;
+                }
+                // a group's kTcG blocks of NTOK columns per tile: four blocks in one 64-column read with
+                // 16-token items, one block per 32-column read with 32-token items (registers)
+                constexpr int W = NTOK == 16 ? 64 : 32;                // columns per read
+                constexpr int LD = kTcG * NTOK / W, BPL = W / NTOK;    // reads per tile, blocks per read
 #pragma unroll
                 for (int m = 0; m < NT; m++) {
-                    float d[kTcG * kTcN];
-                    tmem_ld64(tl + (uint32_t)((g * NT + m) * kTcG * kTcN), d);
-                    if (m == NT - 1) {
-                        tc_fence_before();
-                        mbar_arrive(&acc_empty[g]);
-                    }
 #pragma unroll
-                    for (int u = 0; u < kTcG; u++) {
-                        const int kb = kb0 + u;
-                        if (kb < kz) {
-                            const float wsc = swb[(UP && !T2 ? mrow : m) * nkb + kb];
+                    for (int h = 0; h < LD; h++) {
+                        float d[W];
+                        if constexpr (W == 64) tmem_ld64(tl + (uint32_t)((g * NT + m) * kTcG * NTOK + W * h), d);
+                        else tmem_ld32(tl + (uint32_t)((g * NT + m) * kTcG * NTOK + W * h), d);
+                        if (m == NT - 1 && h == LD - 1) {
+                            tc_fence_before();
+                            mbar_arrive(&acc_empty[g]);
+                        }
 #pragma unroll
-                            for (int j = 0; j < kTcN; j++) acc2[m][j] = fmaf(d[u * kTcN + j], wsc * sxb[j * nkb + kb], acc2[m][j]);
+                        for (int uu = 0; uu < BPL; uu++) {
+                            const int kb = kb0 + h * BPL + uu;
+                            if (kb < kz) {
+                                const float wsc = swb[(UP && !T2 ? mrow : m) * nkb + kb];
+#pragma unroll
+                                for (int j = 0; j < NTOK; j++) acc2[m][j] = fmaf(d[uu * NTOK + j], wsc * sxb[j * nkb + kb], acc2[m][j]);
+                            }
                         }
                     }
                 }
@@ -397,12 +468,12 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             }
             if (ka > 0) {
                 // the range starts inside this item: publish the partial sums for the CTA that finishes it
-                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)cta * 128 + row) * (NT * kTcN));
+                float4 *dst = reinterpret_cast<float4 *>(p.partial + ((size_t)cta * 128 + row) * (NT * NTOK));
 #pragma unroll
                 for (int m = 0; m < NT; m++)
 #pragma unroll
-                    for (int j = 0; j < kTcN / 4; j++)
-                        dst[m * (kTcN / 4) + j] = make_float4(acc2[m][4 * j], acc2[m][4 * j + 1], acc2[m][4 * j + 2], acc2[m][4 * j + 3]);
+                    for (int j = 0; j < NTOK / 4; j++)
+                        dst[m * (NTOK / 4) + j] = make_float4(acc2[m][4 * j], acc2[m][4 * j + 1], acc2[m][4 * j + 2], acc2[m][4 * j + 3]);
                 __threadfence();
                 bar_sync(2, 128);
                 if (et == 0) flag_release(p.flags + cta, p.seq);
@@ -419,12 +490,12 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 if (n_units * (c + 1) / ncta == uc) continue;  // empty range
                 if (et == 0) got = flag_wait(p.flags + c, p.seq, &abort_flag) && got;
                 bar_sync(2, 128);
-                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * (NT * kTcN));
+                const float4 *src = reinterpret_cast<const float4 *>(p.partial + ((size_t)c * 128 + row) * (NT * NTOK));
 #pragma unroll
                 for (int m = 0; m < NT; m++)
 #pragma unroll
-                    for (int j = 0; j < kTcN / 4; j++) {
-                        const float4 v = __ldcg(src + m * (kTcN / 4) + j);
+                    for (int j = 0; j < NTOK / 4; j++) {
+                        const float4 v = __ldcg(src + m * (NTOK / 4) + j);
                         acc2[m][4 * j] += v.x, acc2[m][4 * j + 1] += v.y, acc2[m][4 * j + 2] += v.z, acc2[m][4 * j + 3] += v.w;
                     }
             }
@@ -432,15 +503,15 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                 abort_flag = 1;
                 atomicOr(p.status, kErrWaitTimeout);
             }
-            const int *scol = slot_col + buf * kTcN, *sdst = slot_dst + buf * kTcN;
-            const float *swt = slot_w + buf * kTcN;
+            const int *scol = slot_col + buf * NTOK, *sdst = slot_dst + buf * NTOK;
+            const float *swt = slot_w + buf * NTOK;
             if (UP && T2) {
                 // this thread holds row r's gate sums (tile 0) and up sums (tile 1) for every column
-                const int *cd = col_dst + buf * kTcN;
-                const float *cw = col_w + buf * kTcN;
+                const int *cd = col_dst + buf * NTOK;
+                const float *cw = col_w + buf * NTOK;
                 const int r = tile * 128 + row;
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) {
+                for (int j = 0; j < NTOK; j++) {
                     const int dst = cd[j];
                     if (dst < 0) continue;
                     float gv = bf16r(acc2[0][j]), uv = bf16r(acc2[NT - 1][j]);
@@ -454,7 +525,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
             } else if (UP) {
                 // every row's column sums to shared memory; a thread per (gate row, slot) applies SwiGLU
 #pragma unroll
-                for (int j = 0; j < kTcN; j++) xacc[row * 17 + j] = acc[j];
+                for (int j = 0; j < NTOK; j++) xacc[row * 17 + j] = acc[j];
                 bar_sync(2, 128);
                 const int i = et & 63, r = tile * 64 + i;
                 for (int j = et >> 6; j < ch.n; j += 2) {
@@ -474,7 +545,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     if (ch.e < p.E && p.pos_w) {
                         // expert parallelism: straight into the source rank's eo row, over NVLink
 #pragma unroll
-                        for (int j = 0; j < kTcN; j++)
+                        for (int j = 0; j < NTOK; j++)
                             if (j < ch.n) {
                                 const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
                                 if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
@@ -487,7 +558,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     } else {
                         uint16_t *out = ch.e < p.E ? p.eo : p.sh;
 #pragma unroll
-                        for (int j = 0; j < kTcN; j++)
+                        for (int j = 0; j < NTOK; j++)
                             if (j < ch.n) out[(size_t)sdst[j] * p.H + r] = f32_to_bf16_bits(acc2[m][j]);
                     }
                 }

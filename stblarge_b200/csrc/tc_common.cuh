@@ -24,7 +24,7 @@ __device__ __forceinline__ TcChunk tc_check(const TcParams &p, const Chunk ch, i
 }
 
 // first row of the chunk's B tiles: b_direct (x by token): routed chunks (T <= 16) read tokens 0..15
-// and use column = token; shared chunks read their own 16 consecutive tokens, column = slot.
+// and use column = token; shared chunks read their own 16 or 32 consecutive tokens, column = slot.
 // Otherwise (rows by position) the chunk's first position, column = slot.
 __device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
     if (!p.b_direct) return ch.pos0;

@@ -70,6 +70,10 @@ struct TcParams {
     unsigned int *flags;
     unsigned int seq;          // this launch's number, never 0
     unsigned int *ep_done_ctr; // expert parallelism, down: CTA ticket; the last CTA raises done_flag
+    // adaptive chunk width: the launch runs only when *sel == sel_val (the router's or count exchange's
+    // choice, read after the programmatic-launch wait); otherwise it returns at once.  sel null: always
+    const int *sel;
+    int sel_val;
     uint32_t *status;
 };
 
