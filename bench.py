@@ -12,8 +12,8 @@ Default workload:
   * one GPU: configs[1] (cfg2, FP8 128x128 weights) at T = 16 decode tokens, the headline; the line
     also carries `sweep` (configs[1] at T = 1, 4, 16), `cfg3_sweep` (configs[2]: MXFP4 routed experts,
     FP8 shared, Zipf(1.0) bias, T = 1, 4, 16, 64), `cfg3q8_sweep` (the same layer with Q8 activations
-    for the routed experts, the reference's ds4 numerics) and `cfg4_n1` (configs[3]'s 256 tokens on this one
-    GPU: the N = 1 point of the strong-scaling curve);
+    for the routed experts, the reference's ds4 numerics), `cfg4_n1` (configs[3]'s 256 tokens on this one
+    GPU: the N = 1 point of the strong-scaling curve) and `cfg4_n1_zipf` (the same with Zipf(1.2) routing);
   * N > 1 GPUs: configs[3] (cfg4), 256 tokens in all split over the ranks (strong scaling), expert
     parallelism: rank r holds routed experts [r 256/N, (r+1) 256/N) (router and shared expert
     replicated), every rank routes its own tokens and the layer's kernels dispatch them to the owning
@@ -512,6 +512,17 @@ def main():
         extra["cfg4_n1"] = {"workload": "cfg4 (configs[3]) on one GPU: 256 tokens, uniform routing, full-size FP8",
                             "tokens_per_s": 256 * len(ms4) / (sum(ms4) / 1e3), "ms_per_step": float(np.mean(ms4)),
                             "steps": len(ms4), "device_status": l4.status()}
+        l4.close()
+        # the same with configs[3]'s Zipf(1.2) routing (hot experts: the 32-token items)
+        cfg4z = dataclasses.replace(CFG2, name="cfg4", bias_std=0.0, zipf_s=1.2)
+        w4["router_bias"] = torch.from_numpy(synth.router_bias(cfg4z)).to(dev)
+        l4 = MoELayer(cfg4z, w4, max_tokens=256)
+        for i in range(args.warmup):
+            l4(x4[i])
+        ms4 = timed_steps(l4, x4[args.warmup:])
+        extra["cfg4_n1_zipf"] = {"workload": "cfg4 (configs[3]) on one GPU: 256 tokens, Zipf(1.2) routing, full-size FP8",
+                                 "tokens_per_s": 256 * len(ms4) / (sum(ms4) / 1e3), "ms_per_step": float(np.mean(ms4)),
+                                 "steps": len(ms4), "device_status": l4.status()}
         l4.close()
         del w4, l4
         # configs[2] (MXFP4 routed experts, FP8 shared, Zipf(1.0)) at T = 1, 4, 16, 64 on this GPU
