@@ -36,10 +36,10 @@ def block_inputs(cfg, T, hc, seed):
 @pytest.mark.parametrize("cfg", [CFG1_REF, CFG1], ids=["mxfp4_e8m0", "fp8"])
 def test_fused_block_equals_the_reference_sequence(cfg):
     dev = synth.device_layer(cfg)
-    layer = MoELayer(cfg, dev, max_tokens=16)
+    layer = MoELayer(cfg, dev, max_tokens=64)
     eps, hc = 1e-6, 4
     ref = ctypes.CDLL(REF_SO) if os.path.exists(REF_SO) else None
-    for T, seed in ((1, 1), (5, 2), (16, 3)):
+    for T, seed in ((1, 1), (5, 2), (16, 3), (40, 4)):  # 40: the router stages its normalized rows in two rounds
         x_pre, norm_w, res, post, comb = block_inputs(cfg, T, hc, seed)
         h = layer.forward_block(x_pre, norm_w, eps, res, post, comb)
         torch.cuda.synchronize()
