@@ -538,6 +538,37 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                     const float hv = gv / (1.f + expf(-gv)) * uv * swt[j];
                     p.h[(size_t)sdst[j] * p.I + r] = f32_to_bf16_bits(hv);
                 }
+            } else if constexpr (!L::WIDE) {
+                // the item's bf16 outputs [tile m][column j][128 rows] through shared memory (xacc is
+                // free in the down product), then 16-byte stores of 8 rows of one column: an eighth of
+                // the store instructions, and whole 16-byte pieces over NVLink under expert parallelism
+                uint16_t *ob = reinterpret_cast<uint16_t *>(xacc);
+                static_assert(NT * 16 * 128 * 2 <= 128 * 17 * 4, "staging fits the item-sum buffer");
+#pragma unroll
+                for (int m = 0; m < NT; m++)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) ob[(m * 16 + j) * 128 + row] = f32_to_bf16_bits(acc2[m][j]);
+                bar_sync(2, 128);
+                const bool remote = ch.e < p.E && p.pos_w;
+                for (int c = et; c < NT * 16 * 16; c += 128) {
+                    const int m = c >> 8, j = (c >> 4) & 15, q = c & 15;  // tile, column, 8-row piece
+                    if (j >= ch.n) continue;
+                    const uint4 v = *reinterpret_cast<const uint4 *>(ob + (m * 16 + j) * 128 + q * 8);
+                    const int r = (NT * tile + m) * 128 + q * 8;
+                    if (remote) {
+                        // expert parallelism: straight into the source rank's eo row, over NVLink
+                        const int meta = sdst[j], src = meta >> 16, a = meta & 0xffff;
+                        if (src < 0 || src >= p.ep.n_ranks || a >= p.T_max_assign) {
+                            atomicOr(p.status, kErrBadTable);
+                            continue;
+                        }
+                        uint16_t *out = reinterpret_cast<uint16_t *>(p.ep.region[src] + p.ep.L.eo);
+                        *reinterpret_cast<uint4 *>(out + (size_t)a * p.H + r) = v;
+                    } else {
+                        uint16_t *out = ch.e < p.E ? p.eo : p.sh;
+                        *reinterpret_cast<uint4 *>(out + (size_t)sdst[j] * p.H + r) = v;
+                    }
+                }
             } else {
 #pragma unroll
                 for (int m = 0; m < NT; m++) {
