@@ -137,11 +137,18 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
     tc_fence_after();
     const uint32_t tmem = tmem_base;
 
-    pdl_wait();
-    pdl_launch_dependents();
+    // The down product's chunk table, weights and weight scales do not depend on the kernel before it
+    // (the up product, or the h quantizer): the router wrote the table, and it had finished before this
+    // launch began.  So the table is read, and the weights of the first stages requested, before the
+    // programmatic wait; the activation tiles and their scales wait for it.
+    constexpr bool early = !UP;
+    if (!early) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
     // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
     if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
-    if (tid < S::Chunks && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    if (tid < S::Chunks && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = load_chunk(p.chunks + p.chunk_begin + tid);
     __syncthreads();
     const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
@@ -153,14 +160,47 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
         uz = (int)min(u_hi - (long long)it * nu, (long long)nu);
     };
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - p.chunk_begin < S::Chunks) ? ctab[c - p.chunk_begin] : p.chunks[c];
+        const Chunk ch = (c - p.chunk_begin < S::Chunks) ? ctab[c - p.chunk_begin] : load_chunk(p.chunks + c);
         return tc_check(p, ch, NTOK);
     };
+    const int nkb = K / 128;
+    // a unit's copies: the weight boxes and their scale blocks (`early` part), then the activation box
+    // and its scales, all on the stage's barrier, which expects their bytes
+    auto copy_weights = [&](int s, int tile, int u, bool shared, int z, bool a8) {
+        unsigned char *a = stages + (size_t)s * S::stage;
+        unsigned char *sf = a + S::A + S::B;
+        const uint32_t a_bytes = S::nA * kT4Kb * 128 * (a8 ? 128 : 64);
+        mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * NTOK * 16);
+#pragma unroll
+        for (int m = 0; m < S::nA; m++)
+            tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile_row(tile, m) * 128, kT4Kb * u, z,
+                        &full[s]);
+        // the unit's two 512-byte weight-scale blocks per matrix are adjacent
+#pragma unroll
+        for (int m = 0; m < S::nA; m++)
+            bulk_g2s(sf + m * kT4Kb * 512,
+                     (shared ? p.sf_s[m] : p.sf_a[m] + (size_t)z * p.sf_a_stride) + ((size_t)tile_row(tile, m) * nkb + kT4Kb * u) * 512,
+                     kT4Kb * 512, &full[s]);
+    };
+    int n_early = 0;  // producer: stages whose weights were requested before the programmatic wait
+    if (early) {
+        if (tid == 0) {
+            for (int it = lo; it < hi && n_early < nst; it++) {
+                const TcChunk ch = chunk_of(p.chunk_begin + it / tiles);
+                const bool shared = ch.e == p.E;
+                int ua, uz;
+                u_range(it, ua, uz);
+                for (int u = ua; u < uz && n_early < nst; u++, n_early++)
+                    copy_weights(n_early, it % tiles, u, shared, shared ? 0 : expert_slot(p, ch.e), shared ? p.s_a8 : p.w_a8);
+            }
+        }
+        pdl_wait();
+        pdl_launch_dependents();
+    }
 
     if (warp == 0) {
         // ---------------- producer (lane 0: every copy of a stage, on the copy engine) ----------------
         if (lane == 0) {
-            const int nkb = K / 128;
             int q = 0;
             bool stop = false;
             for (int it = lo; it < hi && !stop; it++) {
@@ -172,7 +212,6 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                 const bool shared = ch.e == p.E;
                 const int z = shared ? 0 : expert_slot(p, ch.e);
                 const bool a8 = shared ? p.s_a8 : p.w_a8;
-                const uint32_t a_bytes = S::nA * kT4Kb * 128 * (a8 ? 128 : 64);
                 int ua, uz;
                 u_range(it, ua, uz);
                 for (int u = ua; u < uz; u++, q++) {
@@ -185,21 +224,9 @@ __device__ __forceinline__ void tc4_body(const TcMaps &maps, const TcParams &p, 
                     }
                     unsigned char *a = stages + (size_t)s * S::stage;
                     unsigned char *sf = a + S::A + S::B;
-                    mbar_arrive_expect_tx(&full[s], a_bytes + S::B + S::nA * kT4Kb * 512 + kT4Kb * NTOK * 16);
-#pragma unroll
-                    for (int m = 0; m < S::nA; m++)
-                        tma_load_4d(a + m * kT4Kb * kT4ATile, shared ? &maps.s[m] : &maps.w[m], 0, tile_row(tile, m) * 128,
-                                    kT4Kb * u, z, &full[s]);
+                    if (q >= n_early) copy_weights(s, tile, u, shared, z, a8);
                     tma_load_3d(a + S::A, &maps.b, 0, brow, kT4Kb * u, &full[s]);
-                    // scales: the unit's two 512-byte weight-scale blocks per matrix are adjacent; the
-                    // activation scales are the chunk's NTOK rows of 16 bytes per K block
-#pragma unroll
-                    for (int m = 0; m < S::nA; m++)
-                        bulk_g2s(sf + m * kT4Kb * 512,
-                                 (shared ? p.sf_s[m] : p.sf_a[m] + (size_t)z * p.sf_a_stride) +
-                                     ((size_t)tile_row(tile, m) * nkb + kT4Kb * u) * 512,
-                                 kT4Kb * 512,
-                                 &full[s]);
+                    // the activation scales: the chunk's NTOK rows of 16 bytes per K block
 #pragma unroll
                     for (int g = 0; g < kT4Kb; g++)
                         bulk_g2s(sf + (S::nA * kT4Kb + g) * 512,
@@ -442,7 +469,9 @@ template <bool UP, int NTOK>
 __global__ void __launch_bounds__(kT4Threads, 1) expert_tc4_kernel(const __grid_constant__ TcMaps maps8, TcParams p8,
                                                                    int nst8, const __grid_constant__ TcMaps maps4,
                                                                    TcParams p4, int nst4) {
-    pdl_wait();
+    // the down launch reads the router's chunk count before the programmatic wait: the router had
+    // finished before this launch began (each body waits before it reads the kernel before's output)
+    if (UP) pdl_wait();
     const int n4c = max(0, (p4.chunk_end >= 0 ? p4.chunk_end : *(volatile const int *)p4.n_chunks) - p4.chunk_begin);
     const int n8c = max(0, p8.chunk_end - p8.chunk_begin);
     // streamed bytes: MXFP4 up 128 x 2 rows x K/2, down 128 x K/2 per tile; FP8 128 x K per tile

@@ -126,8 +126,15 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     tc_fence_after();
     const uint32_t tmem = tmem_base;
 
-    pdl_wait();
-    pdl_launch_dependents();
+    // The down product's chunk table and weights do not depend on the kernel before it (the h
+    // quantizer): the router wrote the table, and it had finished before this launch began.  So on one
+    // GPU the table is read, and the weight tiles of the first stages requested, before the
+    // programmatic wait; only the activation tiles wait for it.
+    const bool early = !UP && !p.sel && p.ep.n_ranks <= 1;
+    if (!early) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
     // expert parallelism: every rank's payload rows must have landed in this rank's receive rows
     // before they are read.  The payload kernel before this one has finished, so this rank's flag is
     // raised everywhere now; the producer waits for all of them after it has prefetched its first
@@ -138,7 +145,7 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     if (ep_up && cta == 0 && tid == 0) signal_all(p.ep, p.ep.L.pay_flag);
     // one round trip: the chunk count and the chunk table (each thread one entry, read concurrently)
     if (tid == 0) s_chunk_end = p.chunk_end >= 0 ? p.chunk_end : *(volatile const int *)p.n_chunks;
-    if (tid < L::CHUNKS && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = p.chunks[p.chunk_begin + tid];
+    if (tid < L::CHUNKS && p.chunk_begin + tid < p.chunk_cap) ctab[tid] = load_chunk(p.chunks + p.chunk_begin + tid);
     __syncthreads();
     const int chunk_end = s_chunk_end;
     const long long n_items = (long long)max(0, chunk_end - p.chunk_begin) * tiles;
@@ -152,9 +159,34 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
     };
     // chunks beyond the shared-memory table are read from global memory
     auto chunk_of = [&](int c) -> TcChunk {
-        const Chunk ch = (c - p.chunk_begin < L::CHUNKS) ? ctab[c - p.chunk_begin] : p.chunks[c];
+        const Chunk ch = (c - p.chunk_begin < L::CHUNKS) ? ctab[c - p.chunk_begin] : load_chunk(p.chunks + c);
         return tc_check(p, ch, NTOK);
     };
+    int n_early = 0;  // producer: stages whose weight tiles were requested before the programmatic wait
+    if (early) {
+        if (tid == 0) {
+            // the first stages in the producer loop's order (each stage's barrier expects the weight
+            // and activation bytes; the loop below adds only the activation tile for these)
+            for (int it = lo; it < hi && n_early < nst; it++) {
+                const int c = p.chunk_begin + it / tiles, tile = it % tiles;
+                const TcChunk ch = chunk_of(c);
+                const bool shared = ch.e == p.E;
+                const int z = shared ? 0 : expert_slot(p, ch.e);
+                int ka, kz;
+                k_range(it, ka, kz);
+                for (int kb = ka; kb < kz && n_early < nst; kb++, n_early++) {
+                    unsigned char *a = stages + (size_t)n_early * STAGE;
+                    mbar_arrive_expect_tx(&full[n_early], STAGE);
+#pragma unroll
+                    for (int m = 0; m < NT; m++)
+                        tma_load_3d(a + m * kATile, shared ? &maps.s[0] : &maps.w[0], kb * 128, (NT * tile + m) * 128, z,
+                                    &full[n_early]);
+                }
+            }
+        }
+        pdl_wait();
+        pdl_launch_dependents();
+    }
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -207,8 +239,10 @@ __device__ __forceinline__ void tc8_body(const TcMaps &maps, const TcParams &p, 
                   for (int u = 0; u < nb && !stop; u++, q++) {
                     const int s = q % nst, kb = kb0 + u;
                     unsigned char *a = stages + (size_t)s * STAGE;
-                    mbar_arrive_expect_tx(&full[s], STAGE);
-                    if (UP && !T2) {
+                    // (the first n_early stages have their weights requested already)
+                    if (q >= n_early) mbar_arrive_expect_tx(&full[s], STAGE);
+                    if (q < n_early) {
+                    } else if (UP && !T2) {
                         tma_load_3d(a, shared ? &maps.s[0] : &maps.w[0], kb * 128, tile * 64, z, &full[s]);
                         tma_load_3d(a + kATile / 2, shared ? &maps.s[1] : &maps.w[1], kb * 128, tile * 64, z, &full[s]);
                     } else if (UP) {

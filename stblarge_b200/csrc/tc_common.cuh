@@ -31,8 +31,17 @@ __device__ __forceinline__ int b_row(const TcParams &p, const TcChunk &ch) {
     return ch.e == p.E ? ch.pos0 - p.n_routed : 0;
 }
 
-// storage slot of a routed expert in the strided weight arrays (the expert cache re-points experts)
-__device__ __forceinline__ int expert_slot(const TcParams &p, int e) { return p.slot ? __ldg(p.slot + e) : e; }
+// storage slot of a routed expert in the strided weight arrays (the expert cache re-points experts).
+// Read at L2 (the cache planner rewrites the table between calls; the down kernels read it before
+// their programmatic wait).
+__device__ __forceinline__ int expert_slot(const TcParams &p, int e) { return p.slot ? __ldcg(p.slot + e) : e; }
+
+// a chunk-table entry, read at L2 (written by the router of this call; the down kernels read the
+// table before their programmatic wait)
+__device__ __forceinline__ Chunk load_chunk(const Chunk *c) {
+    const int4 v = __ldcg(reinterpret_cast<const int4 *>(c));
+    return Chunk{v.x, v.y, v.z, v.w};
+}
 
 __device__ __forceinline__ void flag_release(unsigned int *f, unsigned int v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
