@@ -291,3 +291,32 @@ def test_expert_slots_repoint_experts(small_layers, name):
     W2["routed"] = [[W["routed"][m][E - 1 - e] for e in range(E)] for m in range(3)]
     run_and_check(cfg, layer, dev, W2, synth.make_x(cfg.hidden, 16, seed=77))
     layer.close()
+
+
+def test_layer_rejects_bad_calls(small_layers):
+    """Calls outside the layer's limits (no tokens, more than max_tokens, unaligned x, no output)
+    return -1 with a message and launch nothing; the layer then still computes the same bits as
+    before them, with a clean status word."""
+    import ctypes
+
+    W, dev, layer = small_layers["cfg1"]
+    x = torch.from_numpy(synth.make_x(1024, 16, seed=31).view(np.int16)).cuda()
+    y0 = layer(x).clone()
+    torch.cuda.synchronize()
+    lib, h = layer.lib, layer.handle
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    y = torch.empty_like(y0)
+    xp, yp = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr())
+    cases = [
+        (xp, 0, yp, b"max_tokens"),                               # no tokens
+        (xp, 65, yp, b"max_tokens"),                              # beyond the layer's sizing (64)
+        (ctypes.c_void_p(x.data_ptr() + 2), 4, yp, b"aligned"),  # x not on a 16-byte boundary
+        (xp, 4, ctypes.c_void_p(0), b"null"),                     # no output
+    ]
+    for xa, T, ya, msg in cases:
+        assert lib.stbl_moe_forward(h, xa, T, ya, st) == -1, (T, msg)
+        assert msg in lib.stbl_moe_error(h), lib.stbl_moe_error(h)
+    y1 = layer(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+    assert layer.status() == 0
