@@ -465,7 +465,8 @@ void create(stbl_moe *m, const stbl_moe_desc *d, int ep_rank = 0, int ep_n = 1) 
                 throw std::runtime_error("block-scaled expert scales must be 16-byte aligned (base and expert stride)");
     }
     {
-        // tensor maps: up tiles are 64 gate rows + 64 up rows, down tiles 128 rows
+        // tensor maps: up boxes of 64 rows (T < 4: 64 gate + 64 up rows per item) and of 128 rows (128
+        // gate + 128 up rows), down boxes of 128 rows (one or two per item)
         const long long wst[3] = {
             d->routed_w_stride[0] ? d->routed_w_stride[0] : (long long)I * H,
             d->routed_w_stride[1] ? d->routed_w_stride[1] : (long long)I * H,

@@ -10,10 +10,12 @@
 // holding its first K block (which reaches it last, at the end of its range): the CTAs whose ranges
 // start inside the item publish their partial sums first thing and raise a flag; the finishing CTA
 // adds them in CTA order.  Publishers never wait, so the waits cannot form a cycle.  Six warps:
-//   warp 0     TMA producer: per 128-K block one stage = a 128-row x 128-byte weight tile and a
-//              16-row x 128-byte activation tile, both in the 128-byte swizzle layout;
-//   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 token columns,
-//              K = 32 per instruction, four per 128-K block, each block into its own 16 TMEM columns;
+//   warp 0     TMA producer: per 128-K block one stage = the item's 128-row x 128-byte weight
+//              tile(s) and an NTOK-row x 128-byte activation tile, all in the 128-byte swizzle layout
+//              (down: the first stages' weight tiles are requested before the programmatic wait);
+//   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = NTOK token columns
+//              (16 for a chunk of at most 16 in a 32-token launch), K = 32 per instruction, four per
+//              128-K block, each block into its own TMEM columns;
 //              blocks are grouped by four (one completion signal per group), four groups in flight;
 //   warps 2-5  epilogue: read a group's four blocks of partials from TMEM in one load, apply the
 //              fp32 block scales (weight block x activation block: the promotion of
