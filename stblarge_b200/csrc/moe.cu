@@ -713,7 +713,8 @@ int launch_tc(stbl_moe *m, bool up, TcParams p, cudaStream_t st, bool adaptive =
     if (up) maps.b = p.b_direct ? (m->routed_tc ? m->bmap_xa : m->bmap_xb) : m->bmap_xpos;
     else maps.b = m->bmap_hq;
     // down items of two 128-row tiles from T = 4 on (measured at 256 experts, down kernel: T=16 218 ->
-    // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us); under expert parallelism
+    // 185 us; at T=1 a single-tile item's shorter ramp wins, 46 against 50 us, and still with the first
+    // stages' weights requested before the programmatic wait: layer call 141.3 against 144.4 us); under expert parallelism
     // too (the epilogue stores each tile's rows into the source ranks' eo rows)
     const bool two = up ? up2 : p.T >= 4;
     void *args[] = {&maps, &p, up ? (two ? &m->tc_nst_up2 : &m->tc_nst_up) : (two ? &m->tc_nst_down2 : &m->tc_nst_down)};
