@@ -304,9 +304,8 @@ int stbl_moe_ep_handle(stbl_moe *m, void *handle /* STBL_EP_HANDLE_BYTES */);
 int stbl_moe_ep_connect(stbl_moe *m, const void *handles /* n_ranks x STBL_EP_HANDLE_BYTES, rank order */);
 
 /* Routing without allocating.  This entry point has no counterpart in the reference; it exists for
- * callers that cannot allocate device memory: code running while a CUDA graph is being captured,
- * engines that own a fixed memory pool and allow no allocation outside it, embedded runtimes without
- * an allocator.  It runs the layer's router (logits, scores, group-limited top-k, routing weights,
+ * callers that cannot allocate device memory: engines that own a fixed memory pool and allow no
+ * allocation outside it, embedded runtimes without an allocator.  It runs the layer's router (logits, scores, group-limited top-k, routing weights,
  * bucketed dispatch; the same kernels and results as stbl_moe_forward's routing) for T tokens with
  * all of its working memory in one fixed array inside the library (86,784 bytes, held by every GPU
  * that loads the library until the process exits; x is not quantized for expert kernels here).  Limits: T <= 64, n_experts <= 256, hidden a

@@ -1,8 +1,7 @@
 // Allocation-free routing entry point (stbl_route_noalloc, include/stbl_moe.h).
 //
-// Some callers cannot allocate device memory: code that runs while a CUDA graph is being captured
-// (cudaMalloc is not capturable), engines that own a fixed memory pool and forbid allocations outside
-// it, and embedded runtimes that never link an allocator.  For them this entry point runs the router
+// Some callers cannot allocate device memory: engines that own a fixed memory pool and forbid
+// allocations outside it, and embedded runtimes that never link an allocator.  For them this entry point runs the router
 // kernels (router.cu, the same launches as the layer's) with all of their working memory in one
 // fixed-size array that the library declares at file scope; the caller passes only its inputs and
 // output buffers.

@@ -1,5 +1,5 @@
-"""stbl_route_noalloc: routing for callers that cannot allocate device memory (a CUDA graph being
-captured, an engine with its own fixed memory pool, a runtime without an allocator).  Its working
+"""stbl_route_noalloc: routing for callers that cannot allocate device memory (an engine with its
+own fixed memory pool, a runtime without an allocator).  Its working
 memory is a fixed array inside the library; this test calls it through the C ABI and checks, on two
 calls in a row, that it returns exactly the routing of the regular layer entry point
 (stbl_moe_forward + stbl_moe_last_route): expert ids, weights, counts, offsets and the dispatch
