@@ -320,3 +320,17 @@ def test_layer_rejects_bad_calls(small_layers):
     torch.cuda.synchronize()
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
     assert layer.status() == 0
+
+
+@pytest.mark.parametrize("base", ["cfg1", "cfg1_fp4"])
+@pytest.mark.parametrize("T", [1, 16, 40])  # 40: 32-token chunks (MXFP4) / the width chosen on the device (FP8)
+def test_layer_without_shared_expert(base, T):
+    """A layer with no shared expert (shared format none): no shared chunks, the routed experts alone
+    in the expert launches, and a combine of the routed rows only, against the oracle's layer."""
+    cfg = dataclasses.replace(CFG1 if base == "cfg1" else CFG1_FP4, name=base + "_noshared", shared_fmt=FMT_NONE)
+    W = synth.host_layer(cfg)
+    dev = host_weights_to_device(cfg, W)
+    layer = MoELayer(cfg, dev, max_tokens=64)
+    run_and_check(cfg, layer, dev, W, synth.make_x(cfg.hidden, T, seed=300 + T))
+    assert layer.status() == 0
+    layer.close()
